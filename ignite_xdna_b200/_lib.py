@@ -1,0 +1,125 @@
+"""ctypes binding of libixb200.so (include/ixb200.h).
+
+The structures mirror the header field for field; ``load()`` checks their sizes against the
+library's own ``ixb_abi_sizes`` before anything is called. There is no fallback: without the
+compiled library every GPU entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_NAME = "libixb200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+IXB_OK = 0
+ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
+IXB_ERR_TIMEOUT = -3
+MAX_SEGS = 4
+API_VERSION = 1
+MODE_WINDOW, MODE_GATHER, MODE_STEM = 0, 1, 2
+IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH = 1, 2, 4, 8
+OP_CONV, OP_POOL = 0, 1
+
+
+class Segment(C.Structure):
+    _fields_ = [("offset", C.c_uint64), ("pitch", C.c_int32), ("ch_offset", C.c_int32),
+                ("channels", C.c_int32), ("height", C.c_int32), ("width", C.c_int32), ("up2", C.c_int32)]
+
+
+class ConvDesc(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("k", C.c_int32), ("stride", C.c_int32),
+                ("in_h", C.c_int32), ("in_w", C.c_int32), ("out_h", C.c_int32), ("out_w", C.c_int32),
+                ("cin", C.c_int32), ("cout", C.c_int32), ("n_tile", C.c_int32), ("cp", C.c_int32),
+                ("nseg", C.c_int32), ("seg", Segment * MAX_SEGS),
+                ("w_offset", C.c_uint64), ("w_bytes", C.c_uint64), ("bias_offset", C.c_uint64),
+                ("lut_offset", C.c_uint64), ("shift", C.c_int32), ("has_residual", C.c_int32),
+                ("residual", Segment), ("res_lsh_main", C.c_int32), ("res_lsh_res", C.c_int32),
+                ("res_shift", C.c_int32), ("out_nchw", C.c_int32), ("out", Segment),
+                ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64)]
+
+
+class PoolDesc(C.Structure):
+    _fields_ = [("inp", Segment), ("out", Segment * 3)]
+
+
+class Op(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("index", C.c_int32)]
+
+
+class Plan(C.Structure):
+    _fields_ = [("api_version", C.c_int32), ("max_batch", C.c_int32), ("img_h", C.c_int32), ("img_w", C.c_int32),
+                ("n_convs", C.c_int32), ("n_pools", C.c_int32), ("n_ops", C.c_int32),
+                ("convs", C.POINTER(ConvDesc)), ("pools", C.POINTER(PoolDesc)), ("ops", C.POINTER(Op)),
+                ("images_offset", C.c_uint64), ("input_lut_offset", C.c_uint64), ("input", Segment),
+                ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64), ("arena_bytes", C.c_uint64)]
+
+
+class IxbError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ixb error {code} ({ERRORS.get(code, '?')}): {msg}")
+        self.code = code
+
+
+_lib = None
+
+_SIGS = {
+    "ixb_last_error": (C.c_char_p, []),
+    "ixb_version": (C.c_int, []),
+    "ixb_abi_sizes": (C.c_int, [C.POINTER(C.c_uint64), C.c_int]),
+    "ixb_device_error": (C.c_int, [C.POINTER(C.c_int)]),
+    "ixb_session_create": (C.c_int, [C.POINTER(Plan), C.c_int, C.c_void_p, C.c_uint64, C.POINTER(C.c_void_p)]),
+    "ixb_session_destroy": (C.c_int, [C.c_void_p]),
+    "ixb_session_arena": (C.c_void_p, [C.c_void_p]),
+    "ixb_session_stream": (C.c_void_p, [C.c_void_p]),
+    "ixb_session_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
+    "ixb_session_wait": (C.c_int, [C.c_void_p, C.c_int]),
+    "ixb_session_last_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
+    "ixb_session_launches": (C.c_int, [C.c_void_p, C.c_int]),
+    "ixb_session_profile": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "ixb_conv_layer": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
+    "ixb_pool_layer": (C.c_int, [C.POINTER(PoolDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
+    "ixb_quantize_images": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "ixb_i8gemm_srs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                 C.c_int, C.c_void_p]),
+    "ixb_i8gemm_i32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ixb_w4a8_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                C.c_int, C.c_void_p]),
+    "ixb_w4a8_gemv": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                C.c_void_p]),
+}
+
+
+def exported_symbols():
+    return sorted(_SIGS)
+
+
+def load():
+    """The loaded library; raises if it was not built (``python -c 'import __graft_entry__; __graft_entry__.build()'``)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("IXB_LIB", LIB_PATH))
+    if not path.exists():
+        raise ImportError(f"{path} is missing: build the CUDA extension first (ignite_xdna_b200.build)")
+    lib = C.CDLL(str(path))
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    sizes = (C.c_uint64 * 4)()
+    lib.ixb_abi_sizes(sizes, 4)
+    want = [C.sizeof(Segment), C.sizeof(ConvDesc), C.sizeof(PoolDesc), C.sizeof(Plan)]
+    if list(sizes) != want:
+        raise ImportError(f"ABI mismatch between {path} and this binding: {list(sizes)} vs {want}")
+    if lib.ixb_version() != API_VERSION:
+        raise ImportError("libixb200 API version mismatch")
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> int:
+    if rc < 0:
+        raise IxbError(rc, load().ixb_last_error().decode(errors="replace"))
+    return rc

@@ -1,0 +1,657 @@
+// libixb200.so: the C ABI of include/ixb200.h over the sm_100a kernels.
+//
+// The host side checks every descriptor before anything launches: each view a kernel reads
+// or writes must lie inside the arena for the batch size used, with the alignment the
+// 16-byte copies and stores need. A session replays one captured CUDA graph per batch size
+// (input staging -> image ingress -> every layer -> head egress) on its own stream.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/ixb200.h"
+#include "ixb_conv.cuh"
+#include "ixb_gemm.cuh"
+#include "ixb_misc.cuh"
+#include "ixb_ptx.cuh"
+
+using namespace ixb;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(IXB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define IXB_CUDA(call)                                      \
+  do {                                                      \
+    cudaError_t e_ = (call);                                \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);     \
+  } while (0)
+
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kSmemTwoCta = 100 * 1024;
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// The bytes a view can touch for `batch` images: from its offset to the end of the last image.
+int check_seg(const ixb_segment& s, int batch, uint64_t arena_bytes, bool image, const char* what,
+              std::string& err) {
+  char buf[256];
+  const int need_pitch = image ? 4 : 16;
+  if (s.height < 1 || s.width < 1 || s.channels < 1 || s.pitch < 1 || s.ch_offset < 0) {
+    snprintf(buf, sizeof buf, "%s: empty or negative view", what);
+    err = buf;
+    return -1;
+  }
+  if (s.offset % 16 || s.pitch % need_pitch || s.ch_offset % 16 || s.ch_offset + s.channels > s.pitch) {
+    snprintf(buf, sizeof buf, "%s: misaligned view (offset %llu pitch %d ch_offset %d channels %d)", what,
+             (unsigned long long)s.offset, s.pitch, s.ch_offset, s.channels);
+    err = buf;
+    return -1;
+  }
+  if (!image && s.channels % 16) {
+    snprintf(buf, sizeof buf, "%s: %d channels is not a multiple of 16", what, s.channels);
+    err = buf;
+    return -1;
+  }
+  const unsigned long long bytes =
+      (unsigned long long)batch * (s.height + 2) * (unsigned long long)(s.width + 2) * s.pitch;
+  if (s.offset + bytes > arena_bytes) {
+    snprintf(buf, sizeof buf, "%s: view ends at %llu, past the %llu-byte arena", what,
+             (unsigned long long)(s.offset + bytes), (unsigned long long)arena_bytes);
+    err = buf;
+    return -1;
+  }
+  return 0;
+}
+
+SegDev seg_dev(const ixb_segment& s, uint8_t* arena, int chunk_begin) {
+  SegDev d;
+  d.base = reinterpret_cast<const int8_t*>(arena + s.offset);
+  d.img_stride = (long long)(s.height + 2) * (s.width + 2) * s.pitch;
+  d.pitch = s.pitch;
+  d.ch_off = s.ch_offset;
+  d.chunk_begin = chunk_begin;
+  d.chunks = (s.channels + 15) / 16;
+  d.H = s.height;
+  d.W = s.width;
+  d.up2 = s.up2;
+  return d;
+}
+
+struct ConvLaunch {
+  ConvParams p;
+  dim3 grid;
+  int smem;
+  int mode, stages;
+};
+
+int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, ConvLaunch& L,
+               std::string& err) {
+  char buf[256];
+  auto bad = [&](const char* m) {
+    err = m;
+    return -1;
+  };
+  if (batch < 1) return bad("batch < 1");
+  if (d.mode < IXB_MODE_WINDOW || d.mode > IXB_MODE_STEM) return bad("unknown conv mode");
+  if (!(d.k == 1 || d.k == 3) || !(d.stride == 1 || d.stride == 2)) return bad("k must be 1 or 3, stride 1 or 2");
+  if (d.nseg < 1 || d.nseg > IXB_MAX_SEGS) return bad("1..4 input segments");
+  const int pad = d.k / 2;
+  if (d.out_h != (d.in_h + 2 * pad - d.k) / d.stride + 1 || d.out_w != (d.in_w + 2 * pad - d.k) / d.stride + 1)
+    return bad("output size does not follow from input size, k and stride");
+  if (d.cout % 16 || d.n_tile % 16 || d.n_tile < 16 || d.n_tile > 256 || d.cout % d.n_tile)
+    return bad("cout and n_tile must be multiples of 16, n_tile <= 256 dividing cout");
+  if (!(d.cp == 1 || d.cp == 2 || d.cp == 4)) return bad("cp must be 1, 2 or 4");
+  if (d.shift < 0 || d.shift > 16) return bad("shift outside [0, 16]");
+  ConvParams& p = L.p;
+  memset(&p, 0, sizeof p);
+  p.mode = d.mode;
+  p.k = d.k;
+  p.stride = d.stride;
+  p.pad = pad;
+  p.H = d.in_h;
+  p.W = d.in_w;
+  p.Ho = d.out_h;
+  p.Wo = d.out_w;
+  p.batch = batch;
+  p.cp = d.cp;
+  p.n_tile = d.n_tile;
+  p.cout = d.cout;
+  p.nseg = d.nseg;
+  int cin = 0;
+  int chunk = 0;
+  for (int i = 0; i < d.nseg; ++i) {
+    const ixb_segment& s = d.seg[i];
+    const bool image = d.mode == IXB_MODE_STEM;
+    if (check_seg(s, batch, arena_bytes, image, "conv input", err)) return -1;
+    const int sh = s.up2 ? 2 * s.height : s.height, sw = s.up2 ? 2 * s.width : s.width;
+    if (sh != d.in_h || sw != d.in_w) return bad("input segment size differs from the conv input size");
+    if (s.up2 && (d.mode != IXB_MODE_GATHER || d.k != 1 || d.stride != 1))
+      return bad("an up2 input needs GATHER mode and a 1x1 stride-1 conv");
+    if (d.mode == IXB_MODE_WINDOW && s.up2) return bad("WINDOW mode reads no up2 input");
+    p.seg[i] = seg_dev(s, arena, chunk);
+    chunk += p.seg[i].chunks;
+    cin += s.channels;
+  }
+  if (cin != d.cin) return bad("segment channels do not add up to cin");
+  if (d.mode == IXB_MODE_STEM) {
+    if (d.k != 3 || d.stride != 2 || d.nseg != 1 || d.cin != 3 || d.seg[0].pitch != 4 || d.cp != 2)
+      return bad("STEM mode is a 3x3 stride-2 conv of the 3-channel 4-byte-pixel image with cp = 2");
+    if (d.in_h % 2 || d.in_w % 2) return bad("STEM needs an even input size");
+  }
+  if (d.mode == IXB_MODE_WINDOW && d.stride != 1) return bad("WINDOW mode is stride 1");
+  p.cin_chunks = chunk;
+  const int pairs = (chunk + 1) / 2;
+  int b_block;
+  if (d.mode == IXB_MODE_WINDOW) {
+    p.kblocks = (pairs + d.cp - 1) / d.cp;
+    p.taps_per_block = d.k * d.k;
+    p.pair_groups = p.kblocks;
+    p.win_origin = pad * (d.in_w + 2) + pad;
+    p.rowsA = kTileM + 2 * p.win_origin;
+    b_block = d.cp * d.k * d.k * d.n_tile * 32;
+    p.m_total = (long long)batch * (d.in_h + 2) * (d.in_w + 2);
+  } else if (d.mode == IXB_MODE_GATHER) {
+    p.pair_groups = (pairs + d.cp - 1) / d.cp;
+    p.kblocks = d.k * d.k * p.pair_groups;
+    p.taps_per_block = 1;
+    p.rowsA = kTileM;
+    b_block = d.cp * d.n_tile * 32;
+    p.m_total = (long long)batch * d.out_h * d.out_w;
+  } else {
+    p.kblocks = 1;
+    p.pair_groups = 1;
+    p.taps_per_block = 1;
+    p.rowsA = kTileM;
+    b_block = 2 * d.n_tile * 32;
+    p.m_total = (long long)batch * d.out_h * d.out_w;
+  }
+  const long long ntiles = d.cout / d.n_tile;
+  if ((unsigned long long)ntiles * p.kblocks * b_block != d.w_bytes) {
+    snprintf(buf, sizeof buf, "packed weights are %llu bytes, the tiling needs %llu",
+             (unsigned long long)d.w_bytes, (unsigned long long)(ntiles * p.kblocks * b_block));
+    err = buf;
+    return -1;
+  }
+  if (d.w_offset % 16 || d.w_offset + d.w_bytes > arena_bytes) return bad("weights outside the arena or misaligned");
+  if (d.bias_offset % 16 || d.bias_offset + 4ull * d.cout > arena_bytes) return bad("bias outside the arena");
+  if (d.lut_offset + 256 > arena_bytes) return bad("activation table outside the arena");
+  p.a_stage_bytes = 2 * d.cp * p.rowsA * 16;
+  p.b_stage_bytes = b_block;
+  p.stage_bytes = round_up(p.a_stage_bytes + b_block, 128);
+  const int extra = 512 + 1024;
+  int S = 4;
+  while (S > 2 && S * p.stage_bytes + extra > kSmemTwoCta) --S;
+  if (S * p.stage_bytes + extra > kSmemLimit) return bad("a pipeline stage does not fit shared memory");
+  p.stages = S;
+  p.w_ntile_stride = (long long)p.kblocks * b_block;
+  p.wpack = arena + d.w_offset;
+  p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
+  p.lut = reinterpret_cast<const int8_t*>(arena + d.lut_offset);
+  p.shift = d.shift;
+  int cols = 32;
+  while (cols < d.n_tile) cols *= 2;
+  p.tmem_cols = cols;
+  p.idesc = umma_idesc_s8(kTileM, d.n_tile);
+  p.has_res = d.has_residual;
+  if (d.has_residual) {
+    if (d.mode != IXB_MODE_WINDOW) return bad("a residual needs WINDOW mode");
+    if (check_seg(d.residual, batch, arena_bytes, false, "residual", err)) return -1;
+    if (d.residual.height != d.out_h || d.residual.width != d.out_w || d.residual.channels != d.cout ||
+        d.residual.up2)
+      return bad("residual view must match the output");
+    if (d.res_lsh_main < 0 || d.res_lsh_main > 16 || d.res_lsh_res < 0 || d.res_lsh_res > 16 ||
+        d.res_shift < 0 || d.res_shift > 16)
+      return bad("residual shifts outside [0, 16]");
+    p.res = seg_dev(d.residual, arena, 0);
+    p.res_lsh_m = d.res_lsh_main;
+    p.res_lsh_r = d.res_lsh_res;
+    p.res_shift = d.res_shift;
+  }
+  p.out_nchw = d.out_nchw;
+  if (!d.out_nchw) {
+    if (check_seg(d.out, batch, arena_bytes, false, "conv output", err)) return -1;
+    if (d.out.height != d.out_h || d.out.width != d.out_w || d.out.channels != d.cout || d.out.up2)
+      return bad("output view must be out_h x out_w x cout");
+    p.out = seg_dev(d.out, arena, 0);
+  } else {
+    const unsigned long long plane = (unsigned long long)d.out_h * d.out_w;
+    if (d.egress_image_bytes < plane * d.cout ||
+        d.egress_offset + (unsigned long long)(batch - 1) * d.egress_image_bytes + plane * d.cout > arena_bytes)
+      return bad("head egress outside the arena");
+    p.egress = reinterpret_cast<int8_t*>(arena + d.egress_offset);
+    p.egress_img = (long long)d.egress_image_bytes;
+  }
+  if (d.mode == IXB_MODE_WINDOW) {
+    // every view shares the padded geometry the flattened pixel index walks
+    auto same = [&](const ixb_segment& s) { return s.height == d.in_h && s.width == d.in_w; };
+    for (int i = 0; i < d.nseg; ++i)
+      if (!same(d.seg[i])) return bad("WINDOW views must share the input geometry");
+    if (!d.out_nchw && !same(d.out)) return bad("WINDOW output must share the input geometry");
+  }
+  const long long mt = (p.m_total + kTileM - 1) / kTileM;
+  if (mt > 0x7fffffffLL) return bad("too many tiles");
+  L.grid = dim3((unsigned)mt, (unsigned)ntiles, 1);
+  L.smem = S * p.stage_bytes + extra;
+  L.mode = d.mode;
+  L.stages = S;
+  return 0;
+}
+
+template <int MODE, int S>
+int launch_conv_t(const ConvLaunch& L, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    configured = true;
+  }
+  conv_kernel<MODE, S><<<L.grid, kConvThreads, L.smem, st>>>(L.p);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
+template <int MODE>
+int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
+  switch (L.stages) {
+    case 2: return launch_conv_t<MODE, 2>(L, st);
+    case 3: return launch_conv_t<MODE, 3>(L, st);
+    default: return launch_conv_t<MODE, 4>(L, st);
+  }
+}
+
+int launch_conv(const ConvLaunch& L, cudaStream_t st) {
+  switch (L.mode) {
+    case IXB_MODE_WINDOW: return launch_conv_m<IXB_MODE_WINDOW>(L, st);
+    case IXB_MODE_GATHER: return launch_conv_m<IXB_MODE_GATHER>(L, st);
+    default: return launch_conv_m<IXB_MODE_STEM>(L, st);
+  }
+}
+
+struct PoolLaunch {
+  PoolParams p;
+  dim3 grid;
+  int smem;
+};
+
+int build_pool(const ixb_pool_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, PoolLaunch& L,
+               std::string& err) {
+  if (check_seg(d.in, batch, arena_bytes, false, "pool input", err)) return -1;
+  if (d.in.up2) {
+    err = "pool input cannot be an up2 view";
+    return -1;
+  }
+  for (int k = 0; k < 3; ++k) {
+    if (check_seg(d.out[k], batch, arena_bytes, false, "pool output", err)) return -1;
+    if (d.out[k].height != d.in.height || d.out[k].width != d.in.width || d.out[k].channels != d.in.channels ||
+        d.out[k].up2) {
+      err = "pool outputs must match the input";
+      return -1;
+    }
+  }
+  const int n = d.in.height * d.in.width;
+  L.smem = 3 * n * 16;
+  if (L.smem > kSmemLimit) {
+    err = "pool plane does not fit shared memory";
+    return -1;
+  }
+  L.p.in = seg_dev(d.in, arena, 0);
+  for (int k = 0; k < 3; ++k) L.p.out[k] = seg_dev(d.out[k], arena, 0);
+  L.p.H = d.in.height;
+  L.p.W = d.in.width;
+  L.p.chunks = d.in.channels / 16;
+  L.grid = dim3(L.p.chunks, batch, 1);
+  return 0;
+}
+
+int launch_pool(const PoolLaunch& L, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    IXB_CUDA(cudaFuncSetAttribute(sppf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    configured = true;
+  }
+  sppf_kernel<<<L.grid, 256, L.smem, st>>>(L.p);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int launch_quantize(const uint8_t* images, const int8_t* lut, int batch, int h, int w, int8_t* out,
+                    cudaStream_t st) {
+  if (w % 4) return fail(IXB_ERR_INVALID, "image width must be a multiple of 4");
+  const long long items = (long long)batch * h * (w / 4);
+  const int blocks = (int)std::min<long long>((items + 255) / 256, 148LL * 16);
+  quantize_images_kernel<<<blocks, 256, 0, st>>>(images, lut, batch, h, w, out);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int read_device_error() {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_dev_error, sizeof v);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error flag");
+  if (v) {
+    unsigned int z = 0;
+    cudaMemcpyToSymbol(g_dev_error, &z, sizeof z);
+    return fail(IXB_ERR_DEVICE, "a kernel's bounded wait gave up (device error flag " + std::to_string(v) + ")");
+  }
+  return 0;
+}
+
+}  // namespace
+
+struct ixb_session {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint8_t* arena = nullptr;
+  uint64_t arena_bytes = 0;
+  bool own_arena = false;
+  ixb_plan plan{};
+  std::vector<ixb_conv_desc> convs;
+  std::vector<ixb_pool_desc> pools;
+  std::vector<ixb_op> ops;
+  std::map<int, std::vector<ConvLaunch>> conv_launch;
+  std::map<int, std::vector<PoolLaunch>> pool_launch;
+  std::map<int, cudaGraphExec_t> graphs;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev_done = nullptr;
+  bool pending = false;
+  float last_ms = 0.f;
+
+  int prepare(int batch) {
+    if (conv_launch.count(batch)) return 0;
+    std::vector<ConvLaunch> cl(convs.size());
+    std::vector<PoolLaunch> pl(pools.size());
+    std::string err;
+    for (size_t i = 0; i < convs.size(); ++i)
+      if (build_conv(convs[i], arena, arena_bytes, batch, cl[i], err))
+        return fail(IXB_ERR_INVALID, "conv " + std::to_string(i) + ": " + err);
+    for (size_t i = 0; i < pools.size(); ++i)
+      if (build_pool(pools[i], arena, arena_bytes, batch, pl[i], err))
+        return fail(IXB_ERR_INVALID, "pool " + std::to_string(i) + ": " + err);
+    conv_launch[batch] = std::move(cl);
+    pool_launch[batch] = std::move(pl);
+    return 0;
+  }
+
+  int enqueue_op(int batch, int i) {
+    const ixb_op& op = ops[i];
+    if (op.kind == IXB_OP_CONV) return launch_conv(conv_launch[batch][op.index], stream);
+    return launch_pool(pool_launch[batch][op.index], stream);
+  }
+
+  int enqueue_ingress(int batch) {
+    return launch_quantize(arena + plan.images_offset, reinterpret_cast<const int8_t*>(arena + plan.input_lut_offset),
+                           batch, plan.img_h, plan.img_w, reinterpret_cast<int8_t*>(arena + plan.input.offset),
+                           stream);
+  }
+
+  int enqueue(int batch) {
+    if (int r = enqueue_ingress(batch)) return r;
+    for (size_t i = 0; i < ops.size(); ++i)
+      if (int r = enqueue_op(batch, (int)i)) return r;
+    return 0;
+  }
+
+  int graph_for(int batch, cudaGraphExec_t* out) {
+    auto it = graphs.find(batch);
+    if (it != graphs.end()) {
+      *out = it->second;
+      return 0;
+    }
+    cudaGraph_t g = nullptr;
+    IXB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    int r = enqueue(batch);
+    cudaError_t e = cudaStreamEndCapture(stream, &g);
+    if (r) {
+      if (g) cudaGraphDestroy(g);
+      return r;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    graphs[batch] = exec;
+    *out = exec;
+    return 0;
+  }
+};
+
+extern "C" {
+
+const char* ixb_last_error(void) { return g_last_error.c_str(); }
+
+int ixb_abi_sizes(uint64_t* sizes, int n) {
+  const uint64_t v[4] = {sizeof(ixb_segment), sizeof(ixb_conv_desc), sizeof(ixb_pool_desc), sizeof(ixb_plan)};
+  for (int i = 0; i < n && i < 4; ++i) sizes[i] = v[i];
+  return 0;
+}
+int ixb_version(void) { return IXB_API_VERSION; }
+
+int ixb_device_error(int* flag) {
+  unsigned int v = 0;
+  IXB_CUDA(cudaMemcpyFromSymbol(&v, g_dev_error, sizeof v));
+  unsigned int z = 0;
+  IXB_CUDA(cudaMemcpyToSymbol(g_dev_error, &z, sizeof z));
+  if (flag) *flag = (int)v;
+  return 0;
+}
+
+int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t arena_bytes, ixb_session** out) {
+  if (!plan || !out) return fail(IXB_ERR_INVALID, "null plan or output pointer");
+  *out = nullptr;
+  if (plan->api_version != IXB_API_VERSION) return fail(IXB_ERR_INVALID, "plan api_version mismatch");
+  if (plan->max_batch < 1 || plan->n_ops < 1 || plan->n_convs < 1) return fail(IXB_ERR_INVALID, "empty plan");
+  if (plan->arena_bytes > arena_bytes && arena) return fail(IXB_ERR_INVALID, "arena smaller than the plan");
+  IXB_CUDA(cudaSetDevice(device));
+  auto* s = new ixb_session();
+  s->device = device;
+  s->plan = *plan;
+  s->convs.assign(plan->convs, plan->convs + plan->n_convs);
+  s->pools.assign(plan->pools, plan->pools + plan->n_pools);
+  s->ops.assign(plan->ops, plan->ops + plan->n_ops);
+  s->plan.convs = nullptr;
+  s->plan.pools = nullptr;
+  s->plan.ops = nullptr;
+  for (const ixb_op& op : s->ops) {
+    if ((op.kind == IXB_OP_CONV && (op.index < 0 || op.index >= plan->n_convs)) ||
+        (op.kind == IXB_OP_POOL && (op.index < 0 || op.index >= plan->n_pools)) ||
+        (op.kind != IXB_OP_CONV && op.kind != IXB_OP_POOL)) {
+      delete s;
+      return fail(IXB_ERR_INVALID, "op list names a missing layer");
+    }
+  }
+  s->arena_bytes = arena ? arena_bytes : plan->arena_bytes;
+  if (arena) {
+    s->arena = static_cast<uint8_t*>(arena);
+  } else {
+    cudaError_t e = cudaMalloc(&s->arena, s->arena_bytes);
+    if (e == cudaSuccess) e = cudaMemset(s->arena, 0, s->arena_bytes);
+    if (e != cudaSuccess) {
+      delete s;
+      return cuda_fail(e, "arena allocation");
+    }
+    s->own_arena = true;
+  }
+  // image staging, input lookup table, stem input and egress must lie in the arena
+  std::string err;
+  const int B = plan->max_batch;
+  const unsigned long long img_bytes = (unsigned long long)B * 3 * plan->img_h * plan->img_w;
+  int bad = 0;
+  if (plan->img_w % 4 || plan->img_h < 1) bad = fail(IXB_ERR_INVALID, "image width must be a multiple of 4");
+  else if (plan->images_offset % 16 || plan->images_offset + img_bytes > s->arena_bytes)
+    bad = fail(IXB_ERR_INVALID, "image staging outside the arena");
+  else if (plan->input_lut_offset + 256 > s->arena_bytes) bad = fail(IXB_ERR_INVALID, "input table outside the arena");
+  else if (check_seg(plan->input, B, s->arena_bytes, true, "stem input", err)) bad = fail(IXB_ERR_INVALID, err);
+  else if (plan->input.height != plan->img_h || plan->input.width != plan->img_w || plan->input.pitch != 4)
+    bad = fail(IXB_ERR_INVALID, "stem input view must be img_h x img_w x 4 bytes");
+  else if (plan->egress_offset + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes)
+    bad = fail(IXB_ERR_INVALID, "egress outside the arena");
+  if (!bad) bad = s->prepare(B);
+  if (bad) {
+    if (s->own_arena) cudaFree(s->arena);
+    delete s;
+    return bad;
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
+  if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->ev_done, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    int r = cuda_fail(e, "stream/event creation");
+    ixb_session_destroy(s);
+    return r;
+  }
+  *out = s;
+  return 0;
+}
+
+int ixb_session_destroy(ixb_session* s) {
+  if (!s) return 0;
+  cudaSetDevice(s->device);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  if (s->ev0) cudaEventDestroy(s->ev0);
+  if (s->ev1) cudaEventDestroy(s->ev1);
+  if (s->ev_done) cudaEventDestroy(s->ev_done);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  if (s->own_arena && s->arena) cudaFree(s->arena);
+  delete s;
+  return 0;
+}
+
+void* ixb_session_arena(ixb_session* s) { return s ? s->arena : nullptr; }
+void* ixb_session_stream(ixb_session* s) { return s ? (void*)s->stream : nullptr; }
+
+int ixb_session_launches(ixb_session* s, int batch) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  (void)batch;
+  return 1 + (int)s->ops.size();
+}
+
+int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, int flags) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
+  if (s->pending) return fail(IXB_ERR_INVALID, "the previous asynchronous run was not waited for");
+  if (!(flags & IXB_IN_DEVICE) && !images) return fail(IXB_ERR_INVALID, "null images");
+  if (!(flags & IXB_OUT_DEVICE) && !egress) return fail(IXB_ERR_INVALID, "null egress");
+  const bool copy_in = images != nullptr, copy_out = egress != nullptr;
+  IXB_CUDA(cudaSetDevice(s->device));
+  if (int r = s->prepare(batch)) return r;
+  const size_t in_bytes = (size_t)batch * 3 * s->plan.img_h * s->plan.img_w;
+  if (copy_in)
+    IXB_CUDA(cudaMemcpyAsync(s->arena + s->plan.images_offset, images, in_bytes,
+                             (flags & IXB_IN_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                             s->stream));
+  IXB_CUDA(cudaEventRecord(s->ev0, s->stream));
+  if (flags & IXB_NO_GRAPH) {
+    if (int r = s->enqueue(batch)) return r;
+  } else {
+    cudaGraphExec_t exec;
+    if (int r = s->graph_for(batch, &exec)) return r;
+    IXB_CUDA(cudaGraphLaunch(exec, s->stream));
+  }
+  IXB_CUDA(cudaEventRecord(s->ev1, s->stream));
+  if (copy_out)
+    IXB_CUDA(cudaMemcpyAsync(egress, s->arena + s->plan.egress_offset, (size_t)batch * s->plan.egress_image_bytes,
+                             (flags & IXB_OUT_DEVICE) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                             s->stream));
+  IXB_CUDA(cudaEventRecord(s->ev_done, s->stream));
+  s->pending = true;
+  if (flags & IXB_ASYNC) return 0;
+  return ixb_session_wait(s, 60000);
+}
+
+int ixb_session_wait(ixb_session* s, int timeout_ms) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (!s->pending) return 0;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(s->ev_done);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      s->pending = false;
+      return cuda_fail(e, "run");
+    }
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (ms.count() >= timeout_ms) return fail(IXB_ERR_TIMEOUT, "run did not finish within the timeout");
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  s->pending = false;
+  cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1);
+  return read_device_error();
+}
+
+int ixb_session_last_ms(ixb_session* s, float* ms) {
+  if (!s || !ms) return fail(IXB_ERR_INVALID, "null argument");
+  *ms = s->last_ms;
+  return 0;
+}
+
+int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms) {
+  if (!s || !ms || iters < 1) return fail(IXB_ERR_INVALID, "bad profile arguments");
+  if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
+  if (s->pending) return fail(IXB_ERR_INVALID, "a run is pending");
+  IXB_CUDA(cudaSetDevice(s->device));
+  if (int r = s->prepare(batch)) return r;
+  const size_t n = s->ops.size();
+  std::vector<cudaEvent_t> ev(n + 1);
+  for (auto& e : ev) IXB_CUDA(cudaEventCreate(&e));
+  std::vector<double> acc(n, 0.0);
+  int rc = 0;
+  for (int it = 0; it < iters && !rc; ++it) {
+    rc = s->enqueue_ingress(batch);
+    if (!rc) rc = cudaEventRecord(ev[0], s->stream) == cudaSuccess ? 0 : fail(IXB_ERR_CUDA, "event record");
+    for (size_t i = 0; i < n && !rc; ++i) {
+      rc = s->enqueue_op(batch, (int)i);
+      if (!rc && cudaEventRecord(ev[i + 1], s->stream) != cudaSuccess) rc = fail(IXB_ERR_CUDA, "event record");
+    }
+    if (!rc && cudaEventSynchronize(ev[n]) != cudaSuccess) rc = fail(IXB_ERR_CUDA, "event synchronize");
+    for (size_t i = 0; i < n && !rc; ++i) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+      acc[i] += t;
+    }
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  if (rc) return rc;
+  for (size_t i = 0; i < n; ++i) ms[i] = (float)(acc[i] / iters);
+  return read_device_error();
+}
+
+int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream) {
+  if (!d || !arena) return fail(IXB_ERR_INVALID, "null argument");
+  ConvLaunch L;
+  std::string err;
+  if (build_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
+  return launch_conv(L, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream) {
+  if (!d || !arena) return fail(IXB_ERR_INVALID, "null argument");
+  PoolLaunch L;
+  std::string err;
+  if (build_pool(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
+  return launch_pool(L, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w, int8_t* padded_nhwc4,
+                        void* stream) {
+  if (!images || !lut || !padded_nhwc4 || batch < 1 || h < 1 || w < 4) return fail(IXB_ERR_INVALID, "bad arguments");
+  return launch_quantize(images, lut, batch, h, w, padded_nhwc4, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

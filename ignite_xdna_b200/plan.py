@@ -1,0 +1,395 @@
+"""Lower a layer IR to the device plan: storage, packed weights and per-layer descriptors.
+
+HBM layout (one arena per GPU, sized for ``max_batch`` images):
+
+* image staging, uint8 [B][3][H][W], and the pixel -> int8 input table;
+* the stem input, int8 [B][H+2][W+2][4] (3 channels + 1 zero, zero halo ring);
+* activation buffers, int8 [B][h+2][w+2][pitch] with a one-pixel zero halo. Tensors read
+  together as one concat (a C2f's cv1/m outputs, SPPF's cv1 and pools, the PAN concats at
+  one resolution) share a buffer as consecutive channel ranges, so the concat is free and
+  every producer writes straight into its slice. Stored values are t = q - 128;
+* the egress, int8 [B][egress bytes]: the six heads as NCHW, back to back in head order, the
+  head convs write it directly (read_heads' int8 NCHW egress, graph_session.py:903-930);
+* constants: weights packed per (n-tile, K-block) in the UMMA core-matrix layout, int32
+  biases, the int8 activation tables.
+
+The packing here and the K-block walk in ``csrc/ixb_conv.cuh`` are two sides of one contract:
+``conv_kblocks`` is the single definition of the K order.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+
+from . import _lib as L
+from .graph import ConvLayer, GraphIR, PoolLayer, Segment
+from .yolov8 import HEAD_NAMES
+
+ALIGN = 256
+TILE_M = 128
+
+
+def _align(x: int, a: int = ALIGN) -> int:
+    return (x + a - 1) // a * a
+
+
+@dataclass
+class Store:
+    """Where one tensor lives: buffer offset, pitch, channel offset."""
+    offset: int
+    pitch: int
+    ch_offset: int
+    channels: int
+    height: int
+    width: int
+
+
+@dataclass
+class ConvPlan:
+    layer: ConvLayer
+    mode: int
+    n_tile: int
+    cp: int
+    w_packed: np.ndarray
+    desc: Optional[object] = None
+
+
+@dataclass
+class DevicePlan:
+    ir: GraphIR
+    max_batch: int
+    img_h: int
+    img_w: int
+    arena_bytes: int
+    images_offset: int
+    input_lut_offset: int
+    input_store: Store
+    egress_offset: int
+    egress_image_bytes: int
+    head_offsets: Dict[str, int]
+    stores: Dict[str, Store]
+    convs: List[ConvPlan]
+    pools: List[Tuple[PoolLayer, object]]
+    ops: List[Tuple[int, int]]
+    const_offset: int
+    const_blob: np.ndarray
+    c_plan: object = None
+    keep: list = field(default_factory=list)
+
+    def tensor_bytes(self, name: str, batch: int) -> int:
+        s = self.stores[name]
+        return batch * (s.height + 2) * (s.width + 2) * s.pitch
+
+
+def input_lut_t(scale: float) -> np.ndarray:
+    """int8 table pixel -> t = clip(round(p/255/s) + 128, 0, 255) - 128 (graph_session.py:144-149)."""
+    pixel = np.arange(256, dtype=np.float64) / 255.0
+    q = np.clip(np.round(pixel / scale).astype(np.int64) + 128, 0, 255)
+    return (q - 128).astype(np.int8)
+
+
+def conv_mode(layer: ConvLayer, ir: GraphIR) -> int:
+    if layer.inputs[0].tensor == ir.input:
+        return L.MODE_STEM
+    if layer.stride == 1 and not any(s.up2 for s in layer.inputs):
+        return L.MODE_WINDOW
+    return L.MODE_GATHER
+
+
+def choose_n_tile(cout: int) -> int:
+    if cout <= 256:
+        return cout
+    for n in range(256, 15, -16):
+        if cout % n == 0:
+            return n
+    raise ValueError(f"no n-tile for {cout} output channels")
+
+
+def choose_cp(mode: int, k: int, cin: int) -> int:
+    if mode == L.MODE_STEM:
+        return 2
+    pairs = (cin + 31) // 32
+    if mode == L.MODE_WINDOW and k == 3:
+        return 1
+    return 4 if pairs >= 4 else (2 if pairs >= 2 else 1)
+
+
+def conv_kblocks(mode: int, k: int, cin: int, cp: int) -> List[List[Tuple[int, int]]]:
+    """K order: per K-block, per MMA, the (tap, 32-channel pair) it multiplies.
+
+    WINDOW: K-block = cp pairs x all taps (pair-major); GATHER: K-block = one tap x cp pairs,
+    blocks tap-major; STEM: one block of two 32-byte halves of the 64-byte image K row."""
+    pairs = (cin + 31) // 32
+    taps = k * k
+    if mode == L.MODE_STEM:
+        return [[(0, 0), (0, 1)]]
+    groups = (pairs + cp - 1) // cp
+    blocks = []
+    if mode == L.MODE_WINDOW:
+        for g in range(groups):
+            blocks.append([(t, g * cp + p) for p in range(cp) for t in range(taps)])
+    else:
+        for t in range(taps):
+            for g in range(groups):
+                blocks.append([(t, g * cp + p) for p in range(cp)])
+    return blocks
+
+
+def _core_layout(b: np.ndarray) -> np.ndarray:
+    """[n, 32] K-major bytes -> UMMA no-swizzle core matrices [n/8][2][8][16]."""
+    n = b.shape[0]
+    return b.reshape(n // 8, 8, 2, 16).transpose(0, 2, 1, 3).reshape(-1)
+
+
+def pack_weights(layer: ConvLayer, mode: int, n_tile: int, cp: int) -> np.ndarray:
+    w = layer.weights.astype(np.int8)       # [cout][cin][k][k]
+    cout, cin, k, _ = w.shape
+    if mode == L.MODE_STEM:
+        # K byte 16*ky + 4*j + ci holds w[n][ci][ky][j] (j = kx); row ky = 3 and pixel j = 3 are zero
+        kk = np.zeros((cout, 64), dtype=np.int8)
+        for ky in range(3):
+            for j in range(3):
+                for ci in range(3):
+                    kk[:, 16 * ky + 4 * j + ci] = w[:, ci, ky, j]
+        mats = [kk[:, 0:32], kk[:, 32:64]]
+        blocks = [[0, 1]]
+        out = []
+        for nt in range(cout // n_tile):
+            sl = slice(nt * n_tile, (nt + 1) * n_tile)
+            out.append(np.concatenate([_core_layout(np.ascontiguousarray(mats[i][sl])) for i in blocks[0]]))
+        return np.concatenate(out).view(np.uint8)
+    pairs = (cin + 31) // 32
+    wp = np.zeros((cout, pairs * 32, k * k), dtype=np.int8)
+    wp[:, :cin, :] = w.reshape(cout, cin, k * k)
+    out = []
+    for nt in range(cout // n_tile):
+        sl = slice(nt * n_tile, (nt + 1) * n_tile)
+        for block in conv_kblocks(mode, k, cin, cp):
+            for tap, pair in block:
+                if pair >= pairs:
+                    out.append(np.zeros(n_tile * 32, dtype=np.int8))
+                else:
+                    out.append(_core_layout(np.ascontiguousarray(wp[sl, pair * 32:(pair + 1) * 32, tap])))
+    return np.concatenate(out).view(np.uint8)
+
+
+def _storage_groups(ir: GraphIR, heads: set) -> List[List[str]]:
+    """Tensors read together as a concat at one resolution, in channel order."""
+    grouped: Dict[str, int] = {}
+    groups: List[List[str]] = []
+    for layer in ir.conv_layers():
+        run: List[str] = []
+
+        def flush():
+            if len(run) >= 2 and not any(t in grouped for t in run):
+                for t in run:
+                    grouped[t] = len(groups)
+                groups.append(list(run))
+            run.clear()
+
+        for s in layer.inputs:
+            t = ir.tensors[s.tensor]
+            whole = s.block_offset == 0 and s.blocks * 8 == t.channels
+            if s.up2 or not whole or s.tensor == ir.input or s.tensor in run:
+                flush()
+                continue
+            run.append(s.tensor)
+        flush()
+    for name in ir.tensors:
+        if name not in grouped and name != ir.input and name not in heads:
+            groups.append([name])
+    return groups
+
+
+def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
+    if max_batch < 1:
+        raise ValueError("max_batch must be >= 1")
+    timg = ir.tensors[ir.input]
+    H, W = timg.height, timg.width
+    head_tensor = dict(ir.outputs)
+    heads = set(head_tensor.values())
+    off = 0
+
+    def alloc(nbytes: int) -> int:
+        nonlocal off
+        o = off
+        off = _align(off + nbytes)
+        return o
+
+    images_offset = alloc(max_batch * 3 * H * W)
+    input_lut_offset = alloc(256)
+    input_store = Store(alloc(max_batch * (H + 2) * (W + 2) * 4), 4, 0, 3, H, W)
+    stores: Dict[str, Store] = {}
+    for grp in _storage_groups(ir, heads):
+        infos = [ir.tensors[t] for t in grp]
+        for t in infos:
+            if t.channels % 16:
+                raise ValueError(f"{t.name}: {t.channels} channels is not a multiple of 16")
+        pitch = sum(t.channels for t in infos)
+        h, w = infos[0].height, infos[0].width
+        base = alloc(max_batch * (h + 2) * (w + 2) * pitch)
+        ch = 0
+        for t in infos:
+            stores[t.name] = Store(base, pitch, ch, t.channels, h, w)
+            ch += t.channels
+    head_offsets: Dict[str, int] = {}
+    eb = 0
+    for name in HEAD_NAMES:
+        t = ir.tensors[head_tensor[name]]
+        head_offsets[name] = eb
+        eb += t.channels * t.height * t.width
+    egress_image_bytes = eb
+    egress_offset = alloc(max_batch * egress_image_bytes)
+
+    # constants
+    const_parts: List[Tuple[int, np.ndarray]] = []
+    coff = 0
+
+    def cput(a: np.ndarray) -> int:
+        nonlocal coff
+        o = coff
+        const_parts.append((o, np.ascontiguousarray(a).view(np.uint8).reshape(-1)))
+        coff = _align(coff + a.nbytes)
+        return o
+
+    convs: List[ConvPlan] = []
+    for layer in ir.conv_layers():
+        mode = conv_mode(layer, ir)
+        n_tile = choose_n_tile(layer.cout)
+        cp = choose_cp(mode, layer.k, layer.cin)
+        wp = pack_weights(layer, mode, n_tile, cp)
+        cpl = ConvPlan(layer, mode, n_tile, cp, wp)
+        cpl.w_rel = cput(wp)
+        cpl.bias_rel = cput(layer.bias_int8_domain().astype(np.int32))
+        cpl.lut_rel = cput(layer.lut_t())
+        convs.append(cpl)
+    ilut_rel = cput(input_lut_t(timg.scale))
+    const_offset = alloc(coff)
+    blob = np.zeros(coff, dtype=np.uint8)
+    for o, a in const_parts:
+        blob[o:o + a.size] = a
+    arena_bytes = _align(off, 1 << 20)
+
+    def seg_of(s: Segment) -> L.Segment:
+        if s.tensor == ir.input:
+            st = input_store
+            return L.Segment(st.offset, 4, 0, 3, st.height, st.width, 0)
+        st = stores[s.tensor]
+        return L.Segment(st.offset, st.pitch, st.ch_offset + s.block_offset * 8, s.blocks * 8, st.height,
+                         st.width, int(s.up2))
+
+    def whole(name: str) -> L.Segment:
+        st = stores[name]
+        return L.Segment(st.offset, st.pitch, st.ch_offset, st.channels, st.height, st.width, 0)
+
+    plan_convs = []
+    index_of = {}
+    for i, cpl in enumerate(convs):
+        layer = cpl.layer
+        t_out = ir.tensors[layer.output]
+        src = ir.tensors[layer.inputs[0].tensor]
+        up = 2 if layer.inputs[0].up2 else 1
+        d = L.ConvDesc()
+        d.mode = cpl.mode
+        d.k, d.stride = layer.k, layer.stride
+        d.in_h, d.in_w = src.height * up, src.width * up
+        d.out_h, d.out_w = t_out.height, t_out.width
+        d.cin, d.cout = layer.cin, layer.cout
+        d.n_tile, d.cp = cpl.n_tile, cpl.cp
+        segs = _merge_segments([seg_of(s) for s in layer.inputs])
+        if len(segs) > L.MAX_SEGS:
+            raise ValueError(f"{layer.name}: more than {L.MAX_SEGS} input segments")
+        d.nseg = len(segs)
+        for j, s in enumerate(segs):
+            d.seg[j] = s
+        d.w_offset = const_offset + cpl.w_rel
+        d.w_bytes = cpl.w_packed.size
+        d.bias_offset = const_offset + cpl.bias_rel
+        d.lut_offset = const_offset + cpl.lut_rel
+        d.shift = layer.shift_out
+        if layer.residual is not None:
+            d.has_residual = 1
+            d.residual = seg_of(layer.residual)
+            d.res_lsh_main = layer.residual_lsh_main
+            d.res_lsh_res = layer.residual_lsh_res if layer.residual_lsh_res is not None else layer.residual_shift
+            d.res_shift = layer.residual_shift
+        if layer.output in heads:
+            name = [n for n, t in ir.outputs if t == layer.output][0]
+            d.out_nchw = 1
+            d.egress_offset = egress_offset + head_offsets[name]
+            d.egress_image_bytes = egress_image_bytes
+        else:
+            d.out = whole(layer.output)
+        cpl.desc = d
+        plan_convs.append(d)
+        index_of[layer.name] = i
+    pools = []
+    ops: List[Tuple[int, int]] = []
+    pool_layers = ir.pool_layers()
+    done_pools = set()
+    for layer in ir.layers:
+        if isinstance(layer, ConvLayer):
+            ops.append((L.OP_CONV, index_of[layer.name]))
+            continue
+        if layer.name in done_pools:
+            continue
+        # SPPF: three chained pools run as one kernel
+        chain = [layer]
+        while len(chain) < 3:
+            nxt = [p for p in pool_layers if p.input.tensor == chain[-1].output]
+            if len(nxt) != 1:
+                raise ValueError(f"{layer.name}: expected a chain of three 5x5 pools")
+            chain.append(nxt[0])
+        pd = L.PoolDesc()
+        pd.inp = seg_of(layer.input)
+        for k, p in enumerate(chain):
+            pd.out[k] = whole(p.output)
+            done_pools.add(p.name)
+        pools.append((chain, pd))
+        ops.append((L.OP_POOL, len(pools) - 1))
+    return DevicePlan(ir=ir, max_batch=max_batch, img_h=H, img_w=W, arena_bytes=arena_bytes,
+                      images_offset=images_offset, input_lut_offset=const_offset + ilut_rel,
+                      input_store=input_store, egress_offset=egress_offset, egress_image_bytes=egress_image_bytes,
+                      head_offsets=head_offsets, stores=stores, convs=convs, pools=pools, ops=ops,
+                      const_offset=const_offset, const_blob=blob)
+
+
+def _merge_segments(segs: List[L.Segment]) -> List[L.Segment]:
+    """Adjacent views of one buffer (same offset, consecutive channels) become one view."""
+    out: List[L.Segment] = []
+    for s in segs:
+        if out:
+            p = out[-1]
+            if (p.offset == s.offset and p.pitch == s.pitch and not p.up2 and not s.up2
+                    and p.ch_offset + p.channels == s.ch_offset):
+                p.channels += s.channels
+                continue
+        out.append(L.Segment(s.offset, s.pitch, s.ch_offset, s.channels, s.height, s.width, s.up2))
+    return out
+
+
+def c_plan(dp: DevicePlan) -> L.Plan:
+    """The ixb_plan struct (arrays kept alive on the DevicePlan)."""
+    convs = (L.ConvDesc * len(dp.convs))(*[c.desc for c in dp.convs])
+    pools = (L.PoolDesc * max(1, len(dp.pools)))(*[p for _, p in dp.pools])
+    ops = (L.Op * len(dp.ops))(*[L.Op(k, i) for k, i in dp.ops])
+    p = L.Plan()
+    p.api_version = L.API_VERSION
+    p.max_batch = dp.max_batch
+    p.img_h, p.img_w = dp.img_h, dp.img_w
+    p.n_convs, p.n_pools, p.n_ops = len(dp.convs), len(dp.pools), len(dp.ops)
+    p.convs = convs
+    p.pools = pools
+    p.ops = ops
+    p.images_offset = dp.images_offset
+    p.input_lut_offset = dp.input_lut_offset
+    s = dp.input_store
+    p.input = L.Segment(s.offset, 4, 0, 3, s.height, s.width, 0)
+    p.egress_offset = dp.egress_offset
+    p.egress_image_bytes = dp.egress_image_bytes
+    p.arena_bytes = dp.arena_bytes
+    dp.keep = [convs, pools, ops]
+    dp.c_plan = p
+    return p

@@ -1,0 +1,322 @@
+"""Inference sessions: the reference's runtime surface over the B200 engine.
+
+``GraphSession`` keeps the method names, arguments and return dictionaries of the
+reference's ``src/ignite_xdna/runtime/graph_session.py`` ``GraphSession`` (``stage_input``
+:891-901, ``dispatch`` :628-651, ``read_heads`` :903-930, ``run_yolo_monolithic`` :932-989,
+``run`` :991-992, ``head_status`` :855, ``close``/context manager :764-770, :995) and
+``InferenceSession.decode_yolo_predictions`` (``runtime/session.py`` :1223-1278), with a
+leading batch dimension: the reference runs one image per dispatch, this engine a batch per
+CUDA-graph launch.
+
+PyTorch provides device memory (the arena) and pinned host buffers only; every kernel is
+launched by libixb200.so on the session's own stream. There is no CPU path: without the
+library or a GPU the session refuses to open.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import time
+import warnings
+from pathlib import Path
+from typing import Any, Dict, Optional, Union
+
+import numpy as np
+
+from . import _lib as L
+from .graph import GraphIR
+from .heads import HEAD_NAMES, HeadStatus, layout_from_plan
+from .plan import DevicePlan, build_plan, c_plan
+
+
+def _torch():
+    import torch
+    return torch
+
+
+class GraphSession:
+    """Whole-network XINT8 YOLOv8 on one B200: persistent arena, one CUDA graph per batch size."""
+
+    def __init__(self, ir: GraphIR, device_index: int = 0, max_batch: int = 64):
+        torch = _torch()
+        if not torch.cuda.is_available():
+            raise RuntimeError("GraphSession needs a CUDA device; this engine has no CPU path")
+        self.lib = L.load()
+        self.ir = ir
+        self.device_index = int(device_index)
+        self.device = torch.device("cuda", self.device_index)
+        self.max_batch = int(max_batch)
+        self.plan: DevicePlan = build_plan(ir, self.max_batch)
+        self.arena = torch.zeros(self.plan.arena_bytes, dtype=torch.uint8, device=self.device)
+        blob = torch.from_numpy(self.plan.const_blob)
+        self.arena[self.plan.const_offset:self.plan.const_offset + blob.numel()].copy_(blob.to(self.device))
+        torch.cuda.synchronize(self.device)
+        self._cplan = c_plan(self.plan)
+        h = C.c_void_p()
+        L.check(self.lib.ixb_session_create(C.byref(self._cplan), self.device_index,
+                                            C.c_void_p(self.arena.data_ptr()), self.plan.arena_bytes, C.byref(h)))
+        self._h = h
+        self.layout = layout_from_plan(self.plan)
+        self.head_names = HEAD_NAMES
+        self.in_image_bytes = 3 * self.plan.img_h * self.plan.img_w
+        self.out_bytes = self.plan.egress_image_bytes
+        self._egress = np.zeros((self.max_batch, self.out_bytes), dtype=np.int8)
+        self._staged = 0
+        self.last_dispatch_ms = 0.0
+        self.last_host_ms = 0.0
+
+    # ------------------------------------------------------------------ status
+    @property
+    def head_status(self) -> HeadStatus:
+        return HeadStatus(True, f"{len(HEAD_NAMES)} heads in the plan's egress, {self.out_bytes} bytes per image",
+                          self.layout)
+
+    @property
+    def stream_handle(self) -> int:
+        return int(self.lib.ixb_session_stream(self._h) or 0)
+
+    def launches(self, batch: int) -> int:
+        return L.check(self.lib.ixb_session_launches(self._h, int(batch)))
+
+    # ------------------------------------------------------------------ frame
+    def _as_pixels(self, x: Any):
+        """uint8 pixels [B,3,H,W]; an int8 tensor is the preprocessor's (pixel - 128) convention."""
+        torch = _torch()
+        if isinstance(x, torch.Tensor):
+            if x.dtype == torch.int8:
+                x = (x.view(torch.uint8) ^ 0x80)
+            elif x.dtype != torch.uint8:
+                raise TypeError(f"images must be uint8 pixels or int8 (pixel - 128), got {x.dtype}")
+            if x.dim() == 3:
+                x = x.unsqueeze(0)
+            return x.contiguous()
+        a = np.asarray(x)
+        if a.dtype == np.int8:
+            a = a.view(np.uint8) ^ np.uint8(0x80)
+        elif a.dtype != np.uint8:
+            raise TypeError(f"images must be uint8 pixels or int8 (pixel - 128), got {a.dtype}")
+        if a.ndim == 3:
+            a = a[None]
+        return np.ascontiguousarray(a)
+
+    def _check_shape(self, shape) -> int:
+        if len(shape) != 4 or tuple(shape[1:]) != (3, self.plan.img_h, self.plan.img_w):
+            raise ValueError(f"expected images [B, 3, {self.plan.img_h}, {self.plan.img_w}], got {tuple(shape)}")
+        b = int(shape[0])
+        if not 1 <= b <= self.max_batch:
+            raise ValueError(f"batch {b} outside [1, {self.max_batch}]")
+        return b
+
+    def stage_input(self, input_tensor: Any) -> None:
+        """Copy a batch of images into the device staging buffer (no compute)."""
+        torch = _torch()
+        x = self._as_pixels(input_tensor)
+        b = self._check_shape(x.shape)
+        n = b * self.in_image_bytes
+        dst = self.arena[self.plan.images_offset:self.plan.images_offset + n]
+        if isinstance(x, torch.Tensor):
+            dst.copy_(x.reshape(-1).to(self.device))
+        else:
+            dst.copy_(torch.from_numpy(x.reshape(-1)).to(self.device))
+        torch.cuda.synchronize(self.device)
+        self._staged = b
+
+    def dispatch(self, timeout_ms: int = 10000, batch: Optional[int] = None) -> None:
+        """Run the network on the staged images; heads stay in the device egress."""
+        b = int(batch or self._staged)
+        if b < 1:
+            raise RuntimeError("no staged input")
+        L.check(self.lib.ixb_session_run(self._h, None, b, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
+        self._wait(timeout_ms)
+        self._last_batch = b
+
+    def _wait(self, timeout_ms: int) -> None:
+        rc = self.lib.ixb_session_wait(self._h, int(timeout_ms))
+        if rc == L.IXB_ERR_TIMEOUT:
+            raise TimeoutError(f"GPU dispatch did not complete within {timeout_ms} ms")
+        L.check(rc)
+        ms = C.c_float()
+        self.lib.ixb_session_last_ms(self._h, C.byref(ms))
+        self.last_dispatch_ms = float(ms.value)
+
+    def read_heads(self, unswizzle: bool = True, batch: Optional[int] = None) -> np.ndarray:
+        """Copy the int8 NCHW egress [B, bytes] back to the host."""
+        torch = _torch()
+        b = int(batch or getattr(self, "_last_batch", self._staged) or 1)
+        src = self.arena[self.plan.egress_offset:self.plan.egress_offset + b * self.out_bytes]
+        out = src.cpu().numpy().view(np.int8).reshape(b, self.out_bytes)
+        self._egress[:b] = out
+        return self._egress[:b]
+
+    def run_yolo_monolithic(self, input_tensor: Any, unswizzle: bool = True, timeout_ms: int = 10000,
+                            return_timestamps: bool = False, max_segments: Optional[int] = None):
+        """Whole-network forward pass of a batch; the reference's head dictionary with a batch dimension.
+
+        ``input_tensor`` is uint8 pixels [B,3,H,W] (or [3,H,W]) or the int8 (pixel - 128) tensor of the
+        reference's preprocessor, host or CUDA memory; ``None`` runs the images staged by ``stage_input``.
+        ``unswizzle`` and ``max_segments`` are accepted for compatibility: the heads are always NCHW
+        and the network is one segment."""
+        torch = _torch()
+        t0 = time.perf_counter()
+        if input_tensor is None:
+            b = self._staged
+            if b < 1:
+                raise RuntimeError("no staged input")
+            L.check(self.lib.ixb_session_run(self._h, None, b, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
+        else:
+            x = self._as_pixels(input_tensor)
+            b = self._check_shape(x.shape)
+            if isinstance(x, torch.Tensor) and x.is_cuda:
+                torch.cuda.current_stream(x.device).synchronize()
+                L.check(self.lib.ixb_session_run(self._h, C.c_void_p(x.data_ptr()), b,
+                                                 self._egress.ctypes.data_as(C.c_void_p), L.IN_DEVICE | L.ASYNC))
+            else:
+                if isinstance(x, torch.Tensor):
+                    x = x.numpy()
+                L.check(self.lib.ixb_session_run(self._h, x.ctypes.data_as(C.c_void_p), b,
+                                                 self._egress.ctypes.data_as(C.c_void_p), L.ASYNC))
+        t1 = time.perf_counter()
+        self._wait(timeout_ms)
+        t2 = time.perf_counter()
+        self._last_batch = b
+        egress = self.read_heads(batch=b) if input_tensor is None else self._egress[:b]
+        t3 = time.perf_counter()
+        out: Dict[str, Any] = dict(self.layout.unpack(egress))
+        out["scales"] = self.layout.scales()
+        out["heads_present"] = True
+        out["head_status"] = self.head_status.reason
+        out["raw_output"] = egress
+        out["raw_heads"] = egress
+        out["unswizzled"] = True
+        if return_timestamps:
+            ts = {"stage_ms": (t1 - t0) * 1e3, "npu_ms": self.last_dispatch_ms, "gpu_ms": self.last_dispatch_ms,
+                  "host_ms": 0.0, "readback_ms": (t3 - t2) * 1e3, "wall_ms": (t3 - t0) * 1e3}
+            return out, ts
+        return out
+
+    def run(self, input_tensor: Any, **kwargs) -> np.ndarray:
+        return self.run_yolo_monolithic(input_tensor, **kwargs)["raw_output"]
+
+    # ------------------------------------------------------------------ parity helpers
+    def read_tensor(self, name: str, batch: Optional[int] = None) -> np.ndarray:
+        """A stored activation as the reference holds it: uint8 (zero point 128) [B, C, H, W]."""
+        b = int(batch or getattr(self, "_last_batch", 1))
+        if name in dict((t, n) for n, t in self.ir.outputs):
+            head = [n for n, t in self.ir.outputs if t == name][0]
+            h = self.layout.unpack(self.read_heads(batch=b))[head]
+            return (h.astype(np.int16) + 128).astype(np.uint8)
+        if name == self.ir.input:
+            st = self.plan.input_store
+            raw = self.arena[st.offset:st.offset + b * (st.height + 2) * (st.width + 2) * 4].cpu().numpy()
+            v = raw.view(np.int8).reshape(b, st.height + 2, st.width + 2, 4)[:, 1:-1, 1:-1, :3]
+            return (v.astype(np.int16) + 128).astype(np.uint8).transpose(0, 3, 1, 2)
+        st = self.plan.stores[name]
+        n = b * (st.height + 2) * (st.width + 2) * st.pitch
+        raw = self.arena[st.offset:st.offset + n].cpu().numpy().view(np.int8)
+        v = raw.reshape(b, st.height + 2, st.width + 2, st.pitch)[:, 1:-1, 1:-1, st.ch_offset:st.ch_offset + st.channels]
+        return (v.astype(np.int16) + 128).astype(np.uint8).transpose(0, 3, 1, 2)
+
+    def profile(self, batch: int, iters: int = 3):
+        """Mean device milliseconds per op (layer-by-layer launches with events)."""
+        ms = (C.c_float * len(self.plan.ops))()
+        L.check(self.lib.ixb_session_profile(self._h, int(batch), int(iters), ms))
+        return list(ms)
+
+    # ------------------------------------------------------------------ lifetime
+    def close(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            self.lib.ixb_session_destroy(h)
+            self._h = C.c_void_p()
+        self.arena = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        self.close()
+        return False
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def decode_yolo_predictions(head_outputs: Dict[str, np.ndarray], strides=(8, 16, 32)) -> np.ndarray:
+        return InferenceSession.decode_yolo_predictions(head_outputs, strides)
+
+
+class InferenceSession:
+    """Entry points of the reference's ``ignite_xdna.InferenceSession`` that serve this path."""
+
+    @classmethod
+    def from_spec(cls, model: str = "yolov8n", seed: int = 0, imgsz: int = 640, device_index: int = 0,
+                  max_batch: int = 64, **kw) -> GraphSession:
+        """Open a session on the seeded synthetic XINT8 graph ``model`` in {yolov8n, yolov8s, yolov8m}."""
+        from .yolov8 import build_yolov8
+        variant = model.replace("yolov8", "")
+        return GraphSession(build_yolov8(variant, imgsz=imgsz, seed=seed, **kw), device_index=device_index,
+                            max_batch=max_batch)
+
+    @classmethod
+    def from_file(cls, path: Union[str, Path], device_index: int = 0, max_batch: int = 64, **kwargs) -> GraphSession:
+        """Open a pickled ``GraphIR`` (as ``save_graph`` writes) or a ``yolov8{n,s,m}[_<imgsz>]`` spec name."""
+        p = Path(path)
+        if p.exists():
+            import pickle
+            with open(p, "rb") as f:
+                ir = pickle.load(f)
+            if not isinstance(ir, GraphIR):
+                raise ValueError(f"{p} does not hold a GraphIR")
+            return GraphSession(ir, device_index=device_index, max_batch=max_batch)
+        name = p.name
+        if name.startswith("yolov8"):
+            parts = name.split("_")
+            imgsz = int(parts[1]) if len(parts) > 1 else 640
+            return cls.from_spec(parts[0], imgsz=imgsz, device_index=device_index, max_batch=max_batch, **kwargs)
+        raise FileNotFoundError(path)
+
+    @staticmethod
+    def decode_yolo_predictions(head_outputs: Dict[str, np.ndarray], strides=(8, 16, 32)) -> np.ndarray:
+        """Heads -> [B, 84, anchors]: DFL softmax + integral over 16 bins, dist2bbox xywh, class sigmoid
+        (runtime/session.py:1223-1278), in float32 numpy."""
+        scales = head_outputs.get("scales")
+
+        def as_float(name):
+            t = head_outputs.get(name)
+            if t is None:
+                return None
+            if t.dtype == np.int8:
+                s, zp = scales[name]
+                return (t.astype(np.float32) - np.float32(zp)) * np.float32(s)
+            return t
+
+        preds = []
+        bins = np.arange(16, dtype=np.float32)
+        for lvl, stride in zip((3, 4, 5), strides):
+            box, cls = as_float(f"p{lvl}_box"), as_float(f"p{lvl}_cls")
+            if box is None or cls is None:
+                continue
+            if box.ndim == 3:
+                box, cls = box[None], cls[None]
+            b, _, h, w = box.shape
+            bf = box.reshape(b, 4, 16, h * w)
+            e = np.exp(bf - bf.max(axis=2, keepdims=True))
+            dist = (e / e.sum(axis=2, keepdims=True) * bins[None, None, :, None]).sum(axis=2)
+            yv, xv = np.meshgrid(np.arange(h, dtype=np.float32), np.arange(w, dtype=np.float32), indexing="ij")
+            gx, gy = xv.reshape(-1), yv.reshape(-1)
+            x1 = (gx - dist[:, 0]) * stride
+            y1 = (gy - dist[:, 1]) * stride
+            x2 = (gx + dist[:, 2]) * stride
+            y2 = (gy + dist[:, 3]) * stride
+            xywh = np.stack([(x1 + x2) / 2, (y1 + y2) / 2, x2 - x1, y2 - y1], axis=1)
+            prob = 1.0 / (1.0 + np.exp(-cls.reshape(b, cls.shape[1], h * w)))
+            preds.append(np.concatenate([xywh, prob], axis=1))
+        return np.concatenate(preds, axis=2) if preds else np.zeros((1, 84, 8400), dtype=np.float32)
+
+
+def save_graph(ir: GraphIR, path: Union[str, Path]) -> None:
+    import pickle
+    with open(path, "wb") as f:
+        pickle.dump(ir, f)

@@ -1,0 +1,177 @@
+/*
+ * ixb200.h - C ABI of the B200 (sm_100a) XINT8 YOLOv8 / W4A8 engine, libixb200.so.
+ *
+ * Plain C: pointers, sizes and POD descriptors only. Every entry point returns 0 or a
+ * negative IXB_ERR_* code and never aborts; ixb_last_error() gives a thread-local message
+ * (as the reference's ignite_get_last_error, src/ignite_xdna/c_api/ignite.h:157-160 and
+ * ignite.cpp:60-64).
+ *
+ * Which reference interface each entry point replaces:
+ *   ixb_session_create   ignite_load (c_api/ignite.h:66-67) and GraphSession.__init__
+ *                        (runtime/graph_session.py:775-853): device buffers and weights are
+ *                        placed once; here the graph arrives as a plan instead of a container.
+ *   ixb_session_run      ignite_run / ignite_run_async (c_api/ignite.h:81-110) and
+ *                        GraphSession.run_yolo_monolithic (runtime/graph_session.py:932-989):
+ *                        stage_input + dispatch + read_heads for a whole batch.
+ *   ixb_session_wait     ignite_wait (c_api/ignite.h:121-126) and RunHandle.wait
+ *                        (runtime/session.py:65-84): a timeout is reported, not fatal.
+ *   ixb_session_destroy  ignite_free (c_api/ignite.h:133).
+ *   ixb_conv_layer, ixb_pool_layer
+ *                        one layer of the graph on device buffers, for per-layer parity
+ *                        (the reference checks every layer against run_direct,
+ *                        results/aie/graph_engine_yolov8n_phoenix_20260913T2210Z.log:12-98).
+ *   ixb_i8gemm_srs       int8 x int8 -> int32 GEMM (kernels/int8_matmul_sweep) with the pow2
+ *                        SRS epilogue of compiler/engine_emulator.py:149-162 in the int8 domain.
+ *   ixb_w4a8_gemm / ixb_w4a8_gemv
+ *                        int8 x packed int4 -> int32 (kernels/w4a8_probe/w4a8_kernels.cc:288-305,
+ *                        mm_i8i4_native) plus a group-aligned pow2 SRS epilogue.
+ */
+#ifndef IXB200_H
+#define IXB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IXB_OK 0
+#define IXB_ERR_INVALID -1    /* bad argument or descriptor */
+#define IXB_ERR_CUDA -2       /* a CUDA runtime call failed */
+#define IXB_ERR_TIMEOUT -3    /* the host wait ran out */
+#define IXB_ERR_DEVICE -4     /* a kernel's bounded wait gave up (device error flag set) */
+#define IXB_ERR_UNSUPPORTED -5
+
+#define IXB_MAX_SEGS 4
+#define IXB_API_VERSION 1
+
+/* Conv A-operand modes. */
+#define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one padded pixel window per K-block */
+#define IXB_MODE_GATHER 1   /* stride 2 or an up2 input: per-pixel gather per tap */
+#define IXB_MODE_STEM 2     /* 3x3 stride-2 conv over the 4-byte-pixel image tensor */
+
+/* ixb_session_run flags */
+#define IXB_IN_DEVICE 1     /* images is a device pointer; NULL: the images already sit in the staging buffer */
+#define IXB_OUT_DEVICE 2    /* egress is a device pointer; NULL: leave the heads in the session's egress buffer */
+#define IXB_ASYNC 4         /* return after enqueueing; ixb_session_wait completes the call */
+#define IXB_NO_GRAPH 8      /* launch layer by layer instead of replaying the captured graph */
+
+/* One stored activation tensor viewed as [batch][H+2][W+2][pitch] int8 (t = q - 128) with a
+ * zero halo ring, or a channel range of it. */
+typedef struct ixb_segment {
+  uint64_t offset;     /* arena byte offset of padded pixel (0,0) of image 0 */
+  int32_t pitch;       /* bytes per stored pixel; multiple of 16 (4 for the image tensor) */
+  int32_t ch_offset;   /* first channel of the view; multiple of 16 */
+  int32_t channels;    /* channels of the view; multiple of 16 (3 for the image tensor) */
+  int32_t height;      /* stored height (unpadded) */
+  int32_t width;       /* stored width (unpadded) */
+  int32_t up2;         /* 1: read as its nearest-2x upsampling */
+} ixb_segment;
+
+typedef struct ixb_conv_desc {
+  int32_t mode;        /* IXB_MODE_* */
+  int32_t k, stride;   /* 1 or 3; 1 or 2 */
+  int32_t in_h, in_w;  /* logical input size (after any up2) */
+  int32_t out_h, out_w;
+  int32_t cin, cout;   /* logical channels; cout multiple of 16 */
+  int32_t n_tile;      /* output channels per CTA (multiple of 16, <= 256, divides cout) */
+  int32_t cp;          /* 32-channel pairs of input per K-block */
+  int32_t nseg;
+  ixb_segment seg[IXB_MAX_SEGS];
+  uint64_t w_offset;   /* packed weights: [cout/n_tile][kblocks][block bytes] */
+  uint64_t w_bytes;
+  uint64_t bias_offset;/* int32[cout]: bias_q << e */
+  uint64_t lut_offset; /* int8[256]: activation over t1 + 128 */
+  int32_t shift;       /* SRS shift, 0..16 */
+  int32_t has_residual;
+  ixb_segment residual;
+  int32_t res_lsh_main, res_lsh_res, res_shift;
+  int32_t out_nchw;    /* 0: write out (NHWC view); 1: write int8 NCHW into the egress */
+  ixb_segment out;     /* NHWC destination view (out_nchw == 0) */
+  uint64_t egress_offset;       /* arena offset of this head inside image 0's egress */
+  uint64_t egress_image_bytes;  /* egress bytes per image */
+} ixb_conv_desc;
+
+typedef struct ixb_pool_desc {  /* SPPF: out_k = pool5^k(in), k = 1..3, pad -128 */
+  ixb_segment in;
+  ixb_segment out[3];
+} ixb_pool_desc;
+
+#define IXB_OP_CONV 0
+#define IXB_OP_POOL 1
+typedef struct ixb_op { int32_t kind, index; } ixb_op;
+
+typedef struct ixb_plan {
+  int32_t api_version;
+  int32_t max_batch;
+  int32_t img_h, img_w;
+  int32_t n_convs, n_pools, n_ops;
+  const ixb_conv_desc* convs;
+  const ixb_pool_desc* pools;
+  const ixb_op* ops;
+  uint64_t images_offset;       /* uint8 [max_batch][3][H][W] staging */
+  uint64_t input_lut_offset;    /* int8[256]: pixel -> t */
+  ixb_segment input;            /* padded NHWC4 image tensor the stem reads */
+  uint64_t egress_offset;       /* int8 [max_batch][egress_image_bytes] */
+  uint64_t egress_image_bytes;
+  uint64_t arena_bytes;
+} ixb_plan;
+
+typedef struct ixb_session ixb_session;
+
+const char* ixb_last_error(void);
+int ixb_version(void);
+
+/* Validates every descriptor against the arena (no access outside it) and takes the
+ * arena pointer (device memory of arena_bytes, zero-initialised halos, weights in place).
+ * arena == NULL: the session allocates and zeroes its own arena. */
+int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t arena_bytes, ixb_session** out);
+int ixb_session_destroy(ixb_session* s);
+void* ixb_session_arena(ixb_session* s);
+void* ixb_session_stream(ixb_session* s);    /* the cudaStream_t every launch goes to */
+/* Runs the whole network on `batch` images: uint8 [batch][3][H][W] pixels (host memory, or
+ * device memory with IXB_IN_DEVICE) -> int8 heads [batch][egress_image_bytes] (host memory,
+ * or device memory with IXB_OUT_DEVICE). Copies are issued on the session stream. */
+int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, int flags);
+int ixb_session_wait(ixb_session* s, int timeout_ms);
+/* Device milliseconds of the last completed run (CUDA events around the graph launch). */
+int ixb_session_last_ms(ixb_session* s, float* ms);
+/* Number of kernels one run of `batch` images launches. */
+int ixb_session_launches(ixb_session* s, int batch);
+/* Runs the network `iters` times layer by layer with an event pair around each launch;
+ * writes the mean milliseconds of op i to ms[i] (n_ops entries). */
+int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms);
+
+/* One layer on caller-owned device memory: arena is the base every offset refers to. */
+int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);
+int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);
+int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w,
+                        int8_t* padded_nhwc4, void* stream);
+
+/* int8 GEMM + pow2 SRS: out[m][n] = clamp(rne((sum_k a[m][k] * b[n][k] + bias[n]) >> shift), -128, 127).
+ * a: int8 [M][K] row-major, b: int8 [N][K] (K-major), bias int32 [N]; M % 128 == 0,
+ * N % 16 == 0, K % 32 == 0. All pointers device memory. */
+int ixb_i8gemm_srs(const int8_t* a, const int8_t* b, const int32_t* bias, int8_t* out,
+                   int M, int N, int K, int shift, void* stream);
+/* Same product without the epilogue: int32 out [M][N]. */
+int ixb_i8gemm_i32(const int8_t* a, const int8_t* b, int32_t* out, int M, int N, int K, void* stream);
+
+/* W4A8: a int8 [M][K]; w uint8 [N][K/2] (two int4 per byte along K, even k in the low nibble);
+ * gpos int8 [N][K/128] group positions; shift int32 [N]; out int8 [M][N]:
+ * out = clamp(rne((sum_g (a_g . w_g) << (pmax_n - gpos[n][g])) >> shift[n]), -128, 127). */
+int ixb_w4a8_gemm(const int8_t* a, const uint8_t* w, const int8_t* gpos, const int32_t* shift,
+                  int8_t* out, int M, int N, int K, void* stream);
+int ixb_w4a8_gemv(const int8_t* a, const uint8_t* w, const int8_t* gpos, const int32_t* shift,
+                  int8_t* out, int N, int K, void* stream);
+
+/* sizeof of ixb_segment, ixb_conv_desc, ixb_pool_desc, ixb_plan (for binding checks). */
+int ixb_abi_sizes(uint64_t* sizes, int n);
+
+/* Device error flag (bounded waits that gave up); reading clears it. */
+int ixb_device_error(int* flag);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* IXB200_H */

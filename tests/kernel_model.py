@@ -1,0 +1,214 @@
+"""CPU model of the conv/SPPF kernels' address arithmetic, for offline checks of the plan.
+
+It walks a DevicePlan the way ``csrc/ixb_conv.cuh`` does: the same K-blocks, the same
+shared-memory images of A (window / gather / stem loads) and B (the packed weights), UMMA
+operands read back through the no-swizzle K-major descriptor layout
+(element (r, k) at start + (r // 8) * SBO + (r % 8) * 16 + (k // 16) * LBO + k % 16), and the
+same integer epilogue. It checks the host-side packing and descriptors against the oracle
+without a GPU; it says nothing about the hardware beyond that layout contract.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from ignite_xdna_b200 import _lib as L
+from ignite_xdna_b200.plan import DevicePlan
+
+TILE_M = 128
+
+
+def _rne(x: np.ndarray, s: int) -> np.ndarray:
+    if s <= 0:
+        return x << (-s)
+    q = x >> s
+    r = x - (q << s)
+    h = 1 << (s - 1)
+    return q + ((r > h) | ((r == h) & ((q & 1) == 1))).astype(np.int64)
+
+
+def _operand(smem: np.ndarray, start: int, lbo: int, sbo: int, rows: int) -> np.ndarray:
+    r = np.arange(rows)[:, None]
+    k = np.arange(32)[None, :]
+    idx = start + (r // 8) * sbo + (r % 8) * 16 + (k // 16) * lbo + (k % 16)
+    return smem[idx].view(np.int8).astype(np.int64)
+
+
+def _seg_params(d, s, chunk_begin):
+    return dict(off=int(s.offset), pitch=int(s.pitch), ch_off=int(s.ch_offset), chunk_begin=chunk_begin,
+                chunks=(int(s.channels) + 15) // 16, H=int(s.height), W=int(s.width), up2=int(s.up2),
+                img=(int(s.height) + 2) * (int(s.width) + 2) * int(s.pitch))
+
+
+def run_conv(arena: np.ndarray, d, batch: int) -> None:
+    mode, k, stride = d.mode, d.k, d.stride
+    pad = k // 2
+    H, W, Ho, Wo = d.in_h, d.in_w, d.out_h, d.out_w
+    cp, n_tile = d.cp, d.n_tile
+    segs, chunk = [], 0
+    for i in range(d.nseg):
+        sp = _seg_params(d, d.seg[i], chunk)
+        chunk += sp["chunks"]
+        segs.append(sp)
+    cin_chunks = chunk
+    pairs = (cin_chunks + 1) // 2
+    if mode == L.MODE_WINDOW:
+        kblocks = (pairs + cp - 1) // cp
+        taps_pb, groups = k * k, kblocks
+        win_origin = pad * (W + 2) + pad
+        rowsA = TILE_M + 2 * win_origin
+        b_block = cp * k * k * n_tile * 32
+        m_total = batch * (H + 2) * (W + 2)
+    elif mode == L.MODE_GATHER:
+        groups = (pairs + cp - 1) // cp
+        kblocks, taps_pb, rowsA, win_origin = k * k * groups, 1, TILE_M, 0
+        b_block = cp * n_tile * 32
+        m_total = batch * Ho * Wo
+    else:
+        kblocks, taps_pb, groups, rowsA, win_origin = 1, 1, 1, TILE_M, 0
+        b_block = 2 * n_tile * 32
+        m_total = batch * Ho * Wo
+    assert (d.cout // n_tile) * kblocks * b_block == d.w_bytes
+    a_bytes = 2 * cp * rowsA * 16
+    bias = arena[d.bias_offset:d.bias_offset + 4 * d.cout].view(np.int32).astype(np.int64)
+    lut = arena[d.lut_offset:d.lut_offset + 256].view(np.int8).astype(np.int64)
+    nch = 2 * cp
+    for mt in range((m_total + TILE_M - 1) // TILE_M):
+        m0 = mt * TILE_M
+        for nt in range(d.cout // n_tile):
+            acc = np.zeros((TILE_M, n_tile), dtype=np.int64)
+            for kb in range(kblocks):
+                smem = np.zeros(a_bytes + b_block, dtype=np.uint8)
+                # ---- A
+                for c in range(nch):
+                    dst0 = c * rowsA * 16
+                    if mode == L.MODE_STEM:
+                        r = np.arange(TILE_M)
+                        m = m0 + r
+                        ok = (c < 3) & (m < m_total)
+                        s = segs[0]
+                        img = m // (Ho * Wo)
+                        rem = m - img * Ho * Wo
+                        y, x = rem // Wo, rem % Wo
+                        src = s["off"] + img * s["img"] + ((2 * y + c) * (s["W"] + 2) + 2 * x) * s["pitch"]
+                        for rr in np.nonzero(ok)[0]:
+                            smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[src[rr]:src[rr] + 16]
+                        continue
+                    if mode == L.MODE_WINDOW:
+                        gc = kb * nch + c
+                        tap = 0
+                    else:
+                        tap = kb // groups
+                        gc = (kb - tap * groups) * nch + c
+                    si = [i for i, s in enumerate(segs) if s["chunk_begin"] <= gc < s["chunk_begin"] + s["chunks"]]
+                    if not si:
+                        continue
+                    s = segs[si[-1]]
+                    cbase = s["off"] + s["ch_off"] + (gc - s["chunk_begin"]) * 16
+                    if mode == L.MODE_WINDOW:
+                        px = np.arange(rowsA)
+                        m = m0 - win_origin + px
+                        ok = (m >= 0) & (m < m_total)
+                        src = cbase + m * s["pitch"]
+                        rows = px
+                    else:
+                        r = np.arange(TILE_M)
+                        m = m0 + r
+                        ok = m < m_total
+                        img = m // (Ho * Wo)
+                        rem = m - img * Ho * Wo
+                        y, x = rem // Wo, rem % Wo
+                        ky, kx = tap // k, tap % k
+                        iy, ix = y * stride + ky - pad, x * stride + kx - pad
+                        if s["up2"]:
+                            iy, ix = iy >> 1, ix >> 1
+                        src = cbase + img * s["img"] + ((iy + 1) * (s["W"] + 2) + ix + 1) * s["pitch"]
+                        rows = r
+                    for rr, sa in zip(rows[ok], src[ok]):
+                        smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[sa:sa + 16]
+                # ---- B (one bulk copy)
+                wsrc = d.w_offset + nt * kblocks * b_block + kb * b_block
+                smem[a_bytes:a_bytes + b_block] = arena[wsrc:wsrc + b_block]
+                # ---- MMAs
+                lbo_a = rowsA * 16
+                for pp in range(cp):
+                    for t in range(taps_pb):
+                        shift_px = (t // k) * (W + 2) + (t % k) if mode == L.MODE_WINDOW else 0
+                        A = _operand(smem, pp * 2 * lbo_a + shift_px * 16, lbo_a, 128, TILE_M)
+                        B = _operand(smem, a_bytes + (pp * taps_pb + t) * n_tile * 32, 128, 256, n_tile)
+                        acc += A @ B.T
+            # ---- epilogue
+            m = m0 + np.arange(TILE_M)
+            valid = m < m_total
+            if mode == L.MODE_WINDOW:
+                P = (H + 2) * (W + 2)
+                img = m // P
+                rem = m - img * P
+                yp, xp = rem // (W + 2), rem % (W + 2)
+                valid &= (yp >= 1) & (yp <= H) & (xp >= 1) & (xp <= W)
+                opix, oy, ox = m, yp - 1, xp - 1
+            else:
+                img = m // (Ho * Wo)
+                rem = m - img * Ho * Wo
+                oy, ox = rem // Wo, rem % Wo
+                opix = img * (Ho + 2) * (Wo + 2) + (oy + 1) * (Wo + 2) + ox + 1
+            co = nt * n_tile + np.arange(n_tile)
+            a = acc + bias[co][None, :]
+            t1 = np.clip(_rne(a, d.shift), -128, 127)
+            t2 = lut[t1 + 128]
+            if d.has_residual:
+                r = d.residual
+                ra = (r.offset + opix[:, None] * r.pitch + r.ch_offset + co[None, :])
+                rv = arena[np.where(valid[:, None], ra, 0)].view(np.int8).astype(np.int64)
+                t2 = np.clip(_rne((t2 << d.res_lsh_main) + (rv << d.res_lsh_res), d.res_shift), -128, 127)
+            out = t2.astype(np.int8).view(np.uint8)
+            for rr in np.nonzero(valid)[0]:
+                if not d.out_nchw:
+                    base = d.out.offset + opix[rr] * d.out.pitch + d.out.ch_offset + nt * n_tile
+                    arena[base:base + n_tile] = out[rr]
+                else:
+                    plane = Ho * Wo
+                    e = d.egress_offset + img[rr] * d.egress_image_bytes + oy[rr] * Wo + ox[rr]
+                    arena[e + co * plane] = out[rr]
+
+
+def run_pool(arena: np.ndarray, pd, batch: int) -> None:
+    s = pd.inp
+    H, W, C = s.height, s.width, s.channels
+    img_b = (H + 2) * (W + 2) * s.pitch
+    for b in range(batch):
+        base = s.offset + b * img_b
+        v = arena[base:base + img_b].view(np.int8).reshape(H + 2, W + 2, s.pitch)
+        cur = v[1:-1, 1:-1, s.ch_offset:s.ch_offset + C].astype(np.int64)
+        for kk in range(3):
+            p = np.full((H + 4, W + 4, C), -128, dtype=np.int64)
+            p[2:-2, 2:-2] = cur
+            nxt = np.full((H, W, C), -128, dtype=np.int64)
+            for dy in range(5):
+                for dx in range(5):
+                    nxt = np.maximum(nxt, p[dy:dy + H, dx:dx + W])
+            o = pd.out[kk]
+            ob = o.offset + b * (o.height + 2) * (o.width + 2) * o.pitch
+            ov = arena[ob:ob + img_b].view(np.int8).reshape(H + 2, W + 2, o.pitch)
+            ov[1:-1, 1:-1, o.ch_offset:o.ch_offset + C] = nxt.astype(np.int8)
+            cur = nxt
+
+
+def run_network(dp: DevicePlan, images: np.ndarray) -> np.ndarray:
+    """uint8 images [B,3,H,W] -> int8 egress [B, bytes], through the modelled kernels."""
+    batch = images.shape[0]
+    arena = np.zeros(dp.arena_bytes, dtype=np.uint8)
+    arena[dp.const_offset:dp.const_offset + dp.const_blob.size] = dp.const_blob
+    lut = arena[dp.input_lut_offset:dp.input_lut_offset + 256].view(np.int8)
+    s = dp.input_store
+    for b in range(batch):
+        base = s.offset + b * (s.height + 2) * (s.width + 2) * 4
+        v = arena[base:base + (s.height + 2) * (s.width + 2) * 4].view(np.int8).reshape(s.height + 2, s.width + 2, 4)
+        v[1:-1, 1:-1, :3] = lut[images[b].transpose(1, 2, 0)]
+    convs = [c.desc for c in dp.convs]
+    for kind, idx in dp.ops:
+        if kind == L.OP_CONV:
+            run_conv(arena, convs[idx], batch)
+        else:
+            run_pool(arena, dp.pools[idx][1], batch)
+    e = arena[dp.egress_offset:dp.egress_offset + batch * dp.egress_image_bytes]
+    return e.view(np.int8).reshape(batch, dp.egress_image_bytes).copy()

@@ -1,0 +1,121 @@
+"""Whole-network parity on a B200 through the C ABI: every int8 activation and head tensor
+must equal the oracle (and, at 640x640, the reference's own run_direct hashes) byte for byte."""
+import hashlib
+import json
+
+import numpy as np
+import pytest
+
+import ixb_oracle as O
+from ignite_xdna_b200 import InferenceSession, build_yolov8, random_images
+from ignite_xdna_b200 import _lib as L
+
+pytestmark = pytest.mark.gpu
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+@pytest.fixture(scope="module")
+def hashes(golden_dir):
+    return json.loads((golden_dir / "graph_hashes.json").read_text())
+
+
+@pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 3), (128, 1)])
+def test_small_graph_every_tensor(imgsz, batch):
+    sess = InferenceSession.from_spec("yolov8n", imgsz=imgsz, max_batch=batch)
+    imgs = random_images(batch, imgsz, seed=21 + imgsz)
+    out = sess.run_yolo_monolithic(imgs)
+    for b in range(batch):
+        ref = O.run_image(sess.ir, imgs[b])
+        for name in ref:
+            got = sess.read_tensor(name, batch=batch)[b]
+            assert np.array_equal(got, ref[name]), f"image {b} tensor {name}"
+        assert np.array_equal(out["raw_output"][b], O.egress_int8(sess.ir, ref))
+    sess.close()
+
+
+def test_yolov8n_640_matches_reference_hashes(hashes):
+    h = hashes["yolov8n"]
+    sess = InferenceSession.from_spec("yolov8n", imgsz=640, max_batch=2)
+    imgs = np.concatenate([random_images(1, 640, seed=h["image_seed"]), random_images(1, 640, seed=99)])
+    out = sess.run_yolo_monolithic(imgs)
+    for name, v in h["tensors"].items():
+        got = sess.read_tensor(name, batch=2)[0]
+        assert sha(got) == v, name
+    for name, v in h["heads"].items():
+        assert sha(out[name][0]) == v, name
+    ref1 = O.run_batch_egress(sess.ir, imgs[1:2])
+    assert np.array_equal(out["raw_output"][1:2], ref1)
+    sess.close()
+
+
+@pytest.mark.parametrize("variant", ["s", "m"])
+def test_yolov8sm_640_heads_match_reference_hashes(hashes, variant):
+    h = hashes[f"yolov8{variant}"]
+    sess = InferenceSession.from_spec(f"yolov8{variant}", imgsz=640, max_batch=1)
+    out = sess.run_yolo_monolithic(random_images(1, 640, seed=h["image_seed"]))
+    for name, v in h["heads"].items():
+        assert sha(out[name][0]) == v, name
+    for name, v in h["tensors"].items():
+        assert sha(sess.read_tensor(name, batch=1)[0]) == v, name
+    sess.close()
+
+
+def test_batch64_rows_are_independent_and_exact():
+    """Each image's heads in a batch of 64 equal a separate run of that image, and the oracle."""
+    sess = InferenceSession.from_spec("yolov8n", imgsz=640, max_batch=64)
+    imgs = random_images(64, 640, seed=5)
+    full = np.array(sess.run_yolo_monolithic(imgs)["raw_output"])
+    for j in (0, 17, 63):
+        one = np.array(sess.run_yolo_monolithic(imgs[j:j + 1])["raw_output"])
+        assert np.array_equal(full[j], one[0]), j
+    part = np.array(sess.run_yolo_monolithic(imgs[20:27])["raw_output"])
+    assert np.array_equal(full[20:27], part)
+    assert np.array_equal(full[63:64], O.run_batch_egress(sess.ir, imgs[63:64]))
+    sess.close()
+
+
+def test_graph_replay_equals_layer_by_layer_launches():
+    import ctypes as C
+    sess = InferenceSession.from_spec("yolov8n", imgsz=96, max_batch=4)
+    imgs = random_images(4, 96, seed=8)
+    a = np.array(sess.run_yolo_monolithic(imgs)["raw_output"])
+    sess.stage_input(imgs)
+    L.check(sess.lib.ixb_session_run(sess._h, None, 4, None, L.IN_DEVICE | L.OUT_DEVICE | L.NO_GRAPH))
+    b = sess.read_heads(batch=4)
+    assert np.array_equal(a, b)
+    sess.close()
+
+
+def test_int8_preprocessor_input_equals_uint8_pixels():
+    sess = InferenceSession.from_spec("yolov8n", imgsz=64, max_batch=2)
+    imgs = random_images(2, 64, seed=4)
+    a = np.array(sess.run(imgs))
+    b = np.array(sess.run((imgs.astype(np.int16) - 128).astype(np.int8)))
+    assert np.array_equal(a, b)
+    sess.close()
+
+
+def test_device_input_and_staged_dispatch_paths():
+    import torch
+    sess = InferenceSession.from_spec("yolov8n", imgsz=64, max_batch=2)
+    imgs = random_images(2, 64, seed=6)
+    ref = O.run_batch_egress(sess.ir, imgs)
+    dev = torch.from_numpy(imgs).cuda()
+    assert np.array_equal(np.array(sess.run(dev)), ref)
+    sess.stage_input(imgs)
+    sess.dispatch()
+    assert np.array_equal(sess.read_heads(batch=2), ref)
+    out = sess.run_yolo_monolithic(None)
+    assert np.array_equal(out["raw_output"], ref)
+    sess.close()
+
+
+def test_profile_reports_every_op():
+    sess = InferenceSession.from_spec("yolov8n", imgsz=128, max_batch=2)
+    ms = sess.profile(2, iters=2)
+    assert len(ms) == len(sess.plan.ops) and all(v > 0 for v in ms)
+    assert sess.launches(2) == 1 + len(sess.plan.ops)
+    sess.close()

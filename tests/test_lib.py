@@ -1,0 +1,70 @@
+"""The C ABI library: it loads, exports every declared entry point, and its host-side checks
+refuse descriptors that would reach outside the arena (no GPU needed: validation runs first)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from ignite_xdna_b200 import _lib as L
+from ignite_xdna_b200 import build_yolov8
+from ignite_xdna_b200.plan import build_plan
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ixb200.h"
+
+
+def declared():
+    txt = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(ixb_\w+)\(", txt, re.M)))
+
+
+def test_header_declares_what_binding_binds():
+    assert declared() == L.exported_symbols()
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = L.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert lib.ixb_version() == L.API_VERSION
+
+
+def _desc():
+    ir = build_yolov8("n", imgsz=64)
+    dp = build_plan(ir, 2)
+    return dp, [c.desc for c in dp.convs]
+
+
+def test_valid_descriptor_passes_checks_until_launch():
+    dp, descs = _desc()
+    lib = L.load()
+    # arena pointer is a dummy: validation runs on the host before any CUDA call
+    rc = lib.ixb_conv_layer(C.byref(descs[3]), C.c_void_p(0x10000), dp.arena_bytes, 2, None)
+    # either launched (GPU present) or failed in CUDA, never rejected as invalid
+    assert rc != -1 or "arena" not in lib.ixb_last_error().decode()
+
+
+@pytest.mark.parametrize("mutate,needle", [
+    (lambda d, n: setattr(d.out, "offset", n), "arena"),
+    (lambda d, n: setattr(d.seg[0], "offset", n - 64), "arena"),
+    (lambda d, n: setattr(d, "w_offset", n), "weights"),
+    (lambda d, n: setattr(d, "shift", 17), "shift"),
+    (lambda d, n: setattr(d.seg[0], "ch_offset", 8), "misaligned"),
+    (lambda d, n: setattr(d, "n_tile", 24), "n_tile"),
+    (lambda d, n: setattr(d, "cin", d.cin + 16), "cin"),
+])
+def test_host_checks_refuse_out_of_bounds_descriptors(mutate, needle):
+    dp, descs = _desc()
+    lib = L.load()
+    d = L.ConvDesc.from_buffer_copy(descs[5])
+    mutate(d, dp.arena_bytes)
+    rc = lib.ixb_conv_layer(C.byref(d), C.c_void_p(0x10000), dp.arena_bytes, 2, None)
+    assert rc == -1
+    assert needle in lib.ixb_last_error().decode()
+
+
+def test_batch_beyond_plan_is_refused():
+    dp, descs = _desc()
+    lib = L.load()
+    rc = lib.ixb_conv_layer(C.byref(descs[5]), C.c_void_p(0x10000), dp.arena_bytes, 100000, None)
+    assert rc == -1 and "arena" in lib.ixb_last_error().decode()

@@ -1,0 +1,52 @@
+"""Host-side plan: packed weights, descriptors and storage, checked through the CPU kernel model."""
+import numpy as np
+import pytest
+
+import ixb_oracle as O
+import kernel_model as KM
+from ignite_xdna_b200 import _lib as L
+from ignite_xdna_b200 import build_yolov8, random_images
+from ignite_xdna_b200.plan import build_plan, conv_kblocks, input_lut_t
+
+
+@pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 1)])
+def test_kernel_model_matches_oracle(imgsz, batch):
+    ir = build_yolov8("n", imgsz=imgsz)
+    dp = build_plan(ir, batch)
+    imgs = random_images(batch, imgsz, seed=11)
+    assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
+
+
+def test_input_table_is_reference_lut():
+    lut = input_lut_t(2.0 ** -7)
+    ref = O.input_lut(2.0 ** -7).astype(np.int16) - 128
+    assert np.array_equal(lut.astype(np.int16), ref)
+    assert lut.min() == 0 and lut.max() == 127
+
+
+@pytest.mark.parametrize("variant", ["n", "s", "m"])
+def test_plan_storage_is_disjoint_and_aligned(variant):
+    ir = build_yolov8(variant)
+    dp = build_plan(ir, 64)
+    spans = {}
+    for name, st in dp.stores.items():
+        n = 64 * (st.height + 2) * (st.width + 2) * st.pitch
+        spans.setdefault(st.offset, n)
+        assert st.offset % 256 == 0 and st.pitch % 16 == 0 and st.ch_offset % 16 == 0
+    spans[dp.images_offset] = 64 * 3 * dp.img_h * dp.img_w
+    spans[dp.input_store.offset] = 64 * (dp.img_h + 2) * (dp.img_w + 2) * 4
+    spans[dp.egress_offset] = 64 * dp.egress_image_bytes
+    spans[dp.const_offset] = dp.const_blob.size
+    iv = sorted(spans.items())
+    for (a, n), (b, _) in zip(iv, iv[1:]):
+        assert a + n <= b
+    assert iv[-1][0] + iv[-1][1] <= dp.arena_bytes
+    assert dp.egress_image_bytes == 1_209_600
+
+
+def test_k_order_covers_every_tap_and_pair_once():
+    for mode in (L.MODE_WINDOW, L.MODE_GATHER):
+        for k, cin, cp in ((3, 80, 1), (1, 384, 4), (3, 576, 2), (1, 48, 2)):
+            blocks = conv_kblocks(mode, k, cin, cp)
+            seen = [x for b in blocks for x in b if x[1] < (cin + 31) // 32]
+            assert sorted(seen) == sorted({(t, p) for t in range(k * k) for p in range((cin + 31) // 32)})
