@@ -586,9 +586,11 @@ int ixb_session_wait(ixb_session* s, int timeout_ms) {
       s->pending = false;
       return cuda_fail(e, "run");
     }
-    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
-    if (ms.count() >= timeout_ms) return fail(IXB_ERR_TIMEOUT, "run did not finish within the timeout");
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    const auto us = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0);
+    if (us.count() >= 1000LL * timeout_ms) return fail(IXB_ERR_TIMEOUT, "run did not finish within the timeout");
+    // spin briefly (a step takes milliseconds), then back off
+    if (us.count() < 5000) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
   s->pending = false;
   cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1);
