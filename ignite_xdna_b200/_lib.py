@@ -79,6 +79,7 @@ _SIGS = {
     "ixb_session_launches": (C.c_int, [C.c_void_p, C.c_int]),
     "ixb_session_profile": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "ixb_conv_layer": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
+    "ixb_conv_launch_info": (C.c_int, [C.POINTER(ConvDesc), C.c_uint64, C.c_int, C.POINTER(C.c_int32), C.c_int]),
     "ixb_pool_layer": (C.c_int, [C.POINTER(PoolDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
     "ixb_quantize_images": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "ixb_i8gemm_srs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
@@ -117,6 +118,16 @@ def load():
         raise ImportError("libixb200 API version mismatch")
     _lib = lib
     return lib
+
+
+LAUNCH_FIELDS = ("mt", "tile_rows", "m_tiles", "stages", "b_resident", "grid_x", "grid_y", "smem", "tmem_cols",
+                 "kblocks", "rows_a", "cp")
+
+
+def conv_launch_info(desc, arena_bytes: int, batch: int) -> dict:
+    info = (C.c_int32 * len(LAUNCH_FIELDS))()
+    check(load().ixb_conv_launch_info(C.byref(desc), arena_bytes, batch, info, len(LAUNCH_FIELDS)))
+    return dict(zip(LAUNCH_FIELDS, list(info)))
 
 
 def check(rc: int) -> int:

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -43,9 +44,33 @@ int cuda_fail(cudaError_t e, const char* what) {
   } while (0)
 
 constexpr int kSmemLimit = 227 * 1024;
-constexpr int kSmemTwoCta = 100 * 1024;
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// SMs the launch planner spreads tiles over: the current device's count (148 on B200), 148
+// when no device answers (host-side checks run without a GPU), or IXB_SM_COUNT when set
+// (tests use it to force the multi-block tiles on small inputs).
+int sm_count() {
+  if (const char* env = getenv("IXB_SM_COUNT")) {
+    const int v = atoi(env);
+    if (v > 0) return v;
+  }
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
 
 // The bytes a view can touch for `batch` images: from its offset to the end of the last image.
 int check_seg(const ixb_segment& s, int batch, uint64_t arena_bytes, bool image, const char* what,
@@ -163,21 +188,18 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.taps_per_block = d.k * d.k;
     p.pair_groups = p.kblocks;
     p.win_origin = pad * (d.in_w + 2) + pad;
-    p.rowsA = kTileM + 2 * p.win_origin;
     b_block = d.cp * d.k * d.k * d.n_tile * 32;
     p.m_total = (long long)batch * (d.in_h + 2) * (d.in_w + 2);
   } else if (d.mode == IXB_MODE_GATHER) {
     p.pair_groups = (pairs + d.cp - 1) / d.cp;
     p.kblocks = d.k * d.k * p.pair_groups;
     p.taps_per_block = 1;
-    p.rowsA = kTileM;
     b_block = d.cp * d.n_tile * 32;
     p.m_total = (long long)batch * d.out_h * d.out_w;
   } else {
     p.kblocks = 1;
     p.pair_groups = 1;
     p.taps_per_block = 1;
-    p.rowsA = kTileM;
     b_block = 2 * d.n_tile * 32;
     p.m_total = (long long)batch * d.out_h * d.out_w;
   }
@@ -191,23 +213,52 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   if (d.w_offset % 16 || d.w_offset + d.w_bytes > arena_bytes) return bad("weights outside the arena or misaligned");
   if (d.bias_offset % 16 || d.bias_offset + 4ull * d.cout > arena_bytes) return bad("bias outside the arena");
   if (d.lut_offset + 256 > arena_bytes) return bad("activation table outside the arena");
-  p.a_stage_bytes = 2 * d.cp * p.rowsA * 16;
-  p.b_stage_bytes = b_block;
-  p.stage_bytes = round_up(p.a_stage_bytes + b_block, 128);
-  const int extra = 512 + 1024;
-  int S = 4;
-  while (S > 2 && S * p.stage_bytes + extra > kSmemTwoCta) --S;
-  if (S * p.stage_bytes + extra > kSmemLimit) return bad("a pipeline stage does not fit shared memory");
-  p.stages = S;
+  // Tile of MT blocks of 128 pixels: the largest MT that keeps two accumulators within TMEM
+  // (2 * MT * n_tile <= 512 columns) and still leaves two tiles per SM to spread.
+  const int sms = sm_count();
+  int mt = 1;
+  for (int cand : {4, 2}) {
+    const long long tiles = (p.m_total + 128LL * cand - 1) / (128LL * cand);
+    if (cand * d.n_tile <= 256 && tiles * ntiles >= 2LL * sms) {
+      mt = cand;
+      break;
+    }
+  }
+  p.b_block_bytes = b_block;
+  const int b_total = p.kblocks * b_block;
+  const int extra = 512 + 256 + 1024;   // barriers, activation table, bias
+  const int budget = kSmemLimit - 1024 - extra;
+  for (;; mt /= 2) {
+    p.mt = mt;
+    p.tile_rows = 128 * mt;
+    p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + 2 * p.win_origin : p.tile_rows;
+    p.a_stage_bytes = 2 * d.cp * p.rowsA * 16;
+    p.b_resident = b_total <= budget / 2 ? 1 : 0;
+    const int res_bytes = p.b_resident ? round_up(b_total, 1024) : 0;
+    p.stage_bytes = round_up(p.a_stage_bytes + (p.b_resident ? 0 : b_block), 1024);
+    const int S = std::min(6, (budget - res_bytes) / p.stage_bytes);
+    if (S >= 2) {
+      p.stages = S;
+      p.a_off = res_bytes;
+      break;
+    }
+    if (mt == 1) return bad("a pipeline stage does not fit shared memory");
+  }
+  p.m_tiles = (int)((p.m_total + p.tile_rows - 1) / p.tile_rows);
+  p.bar_off = p.a_off + p.stages * p.stage_bytes;
+  p.lut_off = p.bar_off + 512;
+  p.bias_off = p.lut_off + 256;
+  if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
   p.w_ntile_stride = (long long)p.kblocks * b_block;
   p.wpack = arena + d.w_offset;
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
   p.lut = reinterpret_cast<const int8_t*>(arena + d.lut_offset);
   p.shift = d.shift;
+  p.acc_cols = p.mt * d.n_tile;
   int cols = 32;
-  while (cols < d.n_tile) cols *= 2;
+  while (cols < 2 * p.acc_cols) cols *= 2;
   p.tmem_cols = cols;
-  p.idesc = umma_idesc_s8(kTileM, d.n_tile);
+  p.idesc = umma_idesc_s8(kBlockM, d.n_tile);
   p.has_res = d.has_residual;
   if (d.has_residual) {
     if (d.mode != IXB_MODE_WINDOW) return bad("a residual needs WINDOW mode");
@@ -244,34 +295,27 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
       if (!same(d.seg[i])) return bad("WINDOW views must share the input geometry");
     if (!d.out_nchw && !same(d.out)) return bad("WINDOW output must share the input geometry");
   }
-  const long long mt = (p.m_total + kTileM - 1) / kTileM;
-  if (mt > 0x7fffffffLL) return bad("too many tiles");
-  L.grid = dim3((unsigned)mt, (unsigned)ntiles, 1);
-  L.smem = S * p.stage_bytes + extra;
+  const int smem = p.bias_off + 4 * d.n_tile + 1024;
+  const int per_sm = (p.tmem_cols <= 256 && 2 * smem <= 228 * 1024) ? 2 : 1;
+  const long long gm =
+      std::max<long long>(1, std::min<long long>(p.m_tiles, ((long long)sms * per_sm + ntiles - 1) / ntiles));
+  L.grid = dim3((unsigned)gm, (unsigned)ntiles, 1);
+  L.smem = smem;
   L.mode = d.mode;
-  L.stages = S;
-  return 0;
-}
-
-template <int MODE, int S>
-int launch_conv_t(const ConvLaunch& L, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-    configured = true;
-  }
-  conv_kernel<MODE, S><<<L.grid, kConvThreads, L.smem, st>>>(L.p);
-  IXB_CUDA(cudaGetLastError());
+  L.stages = p.stages;
   return 0;
 }
 
 template <int MODE>
 int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
-  switch (L.stages) {
-    case 2: return launch_conv_t<MODE, 2>(L, st);
-    case 3: return launch_conv_t<MODE, 3>(L, st);
-    default: return launch_conv_t<MODE, 4>(L, st);
+  static bool configured = false;
+  if (!configured) {
+    IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    configured = true;
   }
+  conv_kernel<MODE><<<L.grid, kConvThreads, L.smem, st>>>(L.p);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
 }
 
 int launch_conv(const ConvLaunch& L, cudaStream_t st) {
@@ -640,6 +684,18 @@ int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, in
   std::string err;
   if (build_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
   return launch_conv(L, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_conv_launch_info(const ixb_conv_desc* d, uint64_t arena_bytes, int batch, int32_t* info, int n) {
+  if (!d || !info) return fail(IXB_ERR_INVALID, "null argument");
+  ConvLaunch L;
+  std::string err;
+  // offsets are checked against arena_bytes; a null base only feeds pointer arithmetic
+  if (build_conv(*d, nullptr, arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
+  const int32_t v[12] = {L.p.mt, L.p.tile_rows, L.p.m_tiles, L.p.stages, L.p.b_resident, (int32_t)L.grid.x,
+                         (int32_t)L.grid.y, L.smem, L.p.tmem_cols, L.p.kblocks, L.p.rowsA, L.p.cp};
+  for (int i = 0; i < n && i < 12; ++i) info[i] = v[i];
+  return 0;
 }
 
 int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream) {

@@ -9,21 +9,30 @@
 // Because 128 << shift is a multiple of 2^shift, this equals the reference's uint8 rule
 // sat_u8(rne(bias_acc + sum w * q)) - 128 exactly.
 //
-// GEMM view: M = output pixels (128 per CTA, one TMEM lane each), N = output channels
-// (n_tile per CTA, one TMEM column each), K = input channels x taps in 32-byte steps.
-// Activations are int8 NHWC with a one-pixel zero halo, so:
-//  * WINDOW (stride 1, same resolution): the CTA computes 128 consecutive pixels of the
+// GEMM view: M = output pixels, N = output channels (n_tile per CTA, one TMEM column each),
+// K = input channels x taps in 32-byte steps. A tile is MT blocks of 128 pixels; block b
+// accumulates into TMEM columns [b * n_tile, (b+1) * n_tile). Activations are int8 NHWC with a
+// one-pixel zero halo, so:
+//  * WINDOW (stride 1, same resolution): the tile is 128*MT consecutive pixels of the
 //    flattened padded image; tap (ky, kx) of output pixel m reads padded pixel
-//    m + (ky-1)(W+2) + (kx-1), so ONE window of 128 + 2((W+2)+1) pixels per 32 input channels
+//    m + (ky-1)(W+2) + (kx-1), so ONE window of 128*MT + 2((W+2)+1) pixels per 32 input channels
 //    feeds all nine taps: each tap is the same smem window seen through a descriptor whose
 //    start address moves by 16 bytes per pixel of shift. Halo outputs are computed and dropped.
-//  * GATHER (stride 2, or an input read through a nearest-2x upsample): the CTA computes 128
-//    interior output pixels and gathers each tap's rows with 16-byte cp.async.
+//  * GATHER (stride 2, or an input read through a nearest-2x upsample): the tile is 128*MT
+//    interior output pixels; each tap's rows are gathered with 16-byte cp.async.
 //  * STEM: the 3-channel image stored as 4-byte pixels; one 16-byte K-chunk is 4 pixels x
 //    4 channels of one input row, so K = 3 rows x 16 bytes (+16 zero) covers the 3x3 window.
 // Shared-memory operands use the K-major no-swizzle core-matrix layout: A as
 // [chunk][pixel][16 B] (SBO 128 B, LBO = rows x 16 B), B as [n/8][chunk][8][16 B]
 // (SBO 256 B, LBO 128 B), prepacked on the host so one bulk copy lands a K-block.
+//
+// The kernel is persistent and warp-specialised (288 threads):
+//   warps 0-3  epilogue: TMEM -> registers -> integer epilogue -> global (TMEM lane quarter = warp)
+//   warps 4-7  producers: cp.async A loads into a ring of stages, completion tracked by the
+//              stage's mbarrier (cp.async.mbarrier.arrive); producer 0 also bulk-copies B
+//   warp 8     one thread issues tcgen05.mma and commits stages / accumulators
+// Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next. When a
+// CTA's weights fit, they are loaded once and stay resident in shared memory.
 #pragma once
 #include <cstdint>
 #include "ixb_ptx.cuh"
@@ -44,9 +53,11 @@ struct ConvParams {
   int H, W, Ho, Wo, batch;
   long long m_total;
   int cin_chunks, cp, kblocks, taps_per_block, pair_groups;
+  int mt, tile_rows, m_tiles;
   int rowsA, win_origin;
-  int a_stage_bytes, b_stage_bytes, stage_bytes, stages;
-  int n_tile, tmem_cols;
+  int a_stage_bytes, b_block_bytes, stage_bytes, stages;
+  int b_resident, a_off, bar_off, lut_off, bias_off;
+  int n_tile, acc_cols, tmem_cols;
   uint32_t idesc;
   int nseg;
   SegDev seg[IXB_MAX_SEGS];
@@ -65,23 +76,24 @@ struct ConvParams {
   int cout;
 };
 
-constexpr int kConvThreads = 128;
-constexpr int kTileM = 128;
+constexpr int kProducerThreads = 128;
+constexpr int kConvThreads = 288;
+constexpr int kBlockM = 128;
 
 template <int MODE>
 __device__ __forceinline__ void conv_load_a(const ConvParams& p, uint8_t* As, int kb, long long m0, int tid) {
   const int nch = 2 * p.cp;
   const int c = tid % nch;  // 128 is a multiple of nch, so each thread keeps one chunk
-  const int step = kConvThreads / nch;
+  const int step = kProducerThreads / nch;
   uint8_t* dst = As + c * p.rowsA * 16;
   if (MODE == IXB_MODE_STEM) {
     const SegDev& s = p.seg[0];
-    for (int r = tid / nch; r < kTileM; r += step) {
+    const long long hw = (long long)p.Ho * p.Wo;
+    for (int r = tid / nch; r < p.tile_rows; r += step) {
       const long long m = m0 + r;
       const bool ok = c < 3 && m < p.m_total;
       const int8_t* src = s.base;
       if (ok) {
-        const long long hw = (long long)p.Ho * p.Wo;
         const long long img = m / hw;
         const int rem = (int)(m - img * hw);
         const int y = rem / p.Wo, x = rem - (rem / p.Wo) * p.Wo;
@@ -117,7 +129,7 @@ __device__ __forceinline__ void conv_load_a(const ConvParams& p, uint8_t* As, in
   } else {
     const int ky = tap / p.k, kx = tap - (tap / p.k) * p.k;
     const long long hw = (long long)p.Ho * p.Wo;
-    for (int r = tid / nch; r < kTileM; r += step) {
+    for (int r = tid / nch; r < p.tile_rows; r += step) {
       const long long m = m0 + r;
       const bool ok = cvalid && m < p.m_total;
       const int8_t* src = s.base;
@@ -134,17 +146,79 @@ __device__ __forceinline__ void conv_load_a(const ConvParams& p, uint8_t* As, in
   }
 }
 
-template <int MODE, int S>
-__global__ void __launch_bounds__(kConvThreads) conv_kernel(const __grid_constant__ ConvParams p) {
+template <int MODE>
+__device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, long long m0, int ntile,
+                                                   int warp, int lane, const int8_t* lut_s, const int* bias_s) {
+  for (int b = 0; b < p.mt; ++b) {
+    const int row = b * kBlockM + warp * 32 + lane;
+    const long long m = m0 + row;
+    bool valid = m < p.m_total;
+    long long opix = 0, img = 0;
+    int oy = 0, ox = 0;
+    if (MODE == IXB_MODE_WINDOW) {
+      const long long P = (long long)(p.H + 2) * (p.W + 2);
+      img = m / P;
+      const int rem = (int)(m - img * P);
+      const int yp = rem / (p.W + 2), xp = rem - (rem / (p.W + 2)) * (p.W + 2);
+      valid = valid && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
+      opix = m;
+      oy = yp - 1;
+      ox = xp - 1;
+    } else {
+      const long long hw = (long long)p.Ho * p.Wo;
+      img = m / hw;
+      const int rem = (int)(m - img * hw);
+      oy = rem / p.Wo;
+      ox = rem - oy * p.Wo;
+      opix = img * (long long)(p.Ho + 2) * (p.Wo + 2) + (long long)(oy + 1) * (p.Wo + 2) + (ox + 1);
+    }
+    const uint32_t tl = tacc + b * p.n_tile + ((uint32_t)(warp * 32) << 16);
+    for (int j = 0; j < p.n_tile / 16; ++j) {
+      uint32_t v[16];
+      tmem_ld16(tl + j * 16, v);
+      tmem_ld_wait();
+      if (!valid) continue;
+      const int cl = j * 16;                 // channel within the n-tile
+      const int co = ntile * p.n_tile + cl;  // output channel
+      int8_t rv[16];
+      if (p.has_res)
+        *reinterpret_cast<uint4*>(rv) =
+            *reinterpret_cast<const uint4*>(p.res.base + opix * p.res.pitch + p.res.ch_off + co);
+      alignas(16) int8_t ov[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int a = (int)v[i] + bias_s[cl + i];
+        int t = lut_s[clamp_i8(rne_shift(a, p.shift)) + 128];
+        if (p.has_res) t = clamp_i8(rne_shift((t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r), p.res_shift));
+        ov[i] = (int8_t)t;
+      }
+      if (!p.out_nchw) {
+        *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + opix * p.out.pitch + p.out.ch_off + co) =
+            *reinterpret_cast<const uint4*>(ov);
+      } else {
+        int8_t* e = p.egress + img * p.egress_img + (long long)oy * p.Wo + ox;
+        const long long plane = (long long)p.Ho * p.Wo;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) e[(co + i) * plane] = ov[i];
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_constant__ ConvParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint64_t* bfull = reinterpret_cast<uint64_t*>(smem + S * p.stage_bytes);
-  uint64_t* mdone = bfull + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + S);
-  int8_t* lut_s = reinterpret_cast<int8_t*>(smem + S * p.stage_bytes + 256);
-
-  const long long m0 = (long long)blockIdx.x * kTileM;
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* bres_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
+  int8_t* lut_s = reinterpret_cast<int8_t*>(smem + p.lut_off);
+  int* bias_s = reinterpret_cast<int*>(smem + p.bias_off);
   const int ntile = blockIdx.y;
   const int KB = p.kblocks;
 
@@ -152,140 +226,113 @@ __global__ void __launch_bounds__(kConvThreads) conv_kernel(const __grid_constan
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
-  if (tid == 0) {
+  if (tid == kConvThreads - 32) {
+    const uint32_t fcount = kProducerThreads + (p.b_resident ? 0 : 1);
     for (int s = 0; s < S; ++s) {
-      mbar_init(&bfull[s], 1);
-      mbar_init(&mdone[s], 1);
+      mbar_init(&full[s], fcount);
+      mbar_init(&empty[s], 1);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(bres_bar, 1);
     fence_mbar_init();
   }
   for (int i = tid; i < 256; i += kConvThreads) lut_s[i] = p.lut[i];
+  for (int i = tid; i < p.n_tile; i += kConvThreads) bias_s[i] = p.bias[ntile * p.n_tile + i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto load_stage = [&](int kb) {
-    const int st = kb % S;
-    uint8_t* As = smem + st * p.stage_bytes;
-    uint8_t* Bs = As + p.a_stage_bytes;
-    conv_load_a<MODE>(p, As, kb, m0, tid);
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&bfull[st], p.b_stage_bytes);
-      bulk_g2s(Bs, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_stage_bytes, p.b_stage_bytes,
-               &bfull[st]);
+  if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ producers
+    const int ptid = tid - 128;
+    if (p.b_resident && ptid == 0) {
+      mbar_arrive_expect_tx(bres_bar, (uint32_t)(KB * p.b_block_bytes));
+      for (int kb = 0; kb < KB; ++kb)
+        bulk_g2s(smem + kb * p.b_block_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
+                 p.b_block_bytes, bres_bar);
     }
-  };
-
-  // L K-blocks of loads run ahead of the MMAs; S - L K-blocks of MMAs may be in flight.
-  constexpr int L = (S >= 4) ? S - 2 : S - 1;
-#pragma unroll
-  for (int s = 0; s < L; ++s) {
-    if (s < KB) load_stage(s);
-    cp_async_commit();
-  }
-
-  for (int kb = 0; kb < KB; ++kb) {
-    const int st = kb % S;
-    const int nk = kb + L;
-    if (nk < KB) {
-      const int prev = nk - S;  // the K-block that last used stage nk % S
-      if (prev >= 0) mbar_wait(&mdone[prev % S], (prev / S) & 1);
-      load_stage(nk);
-    }
-    cp_async_commit();
-    cp_async_wait<L>();
-    fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      mbar_wait(&bfull[st], (kb / S) & 1);
-      tc_fence_after();
-      const uint32_t a0 = smem_u32(smem + st * p.stage_bytes);
-      const uint32_t b0 = a0 + p.a_stage_bytes;
-      const uint32_t lbo_a = p.rowsA * 16;
-      int i = 0;
-      for (int pp = 0; pp < p.cp; ++pp) {
-        for (int t = 0; t < p.taps_per_block; ++t) {
-          uint32_t shift_px = 0;
-          if (MODE == IXB_MODE_WINDOW) shift_px = (t / p.k) * (p.W + 2) + (t - (t / p.k) * p.k);
-          const uint64_t ad = umma_desc(a0 + pp * 2 * lbo_a + shift_px * 16, lbo_a, 128);
-          const uint64_t bd = umma_desc(b0 + (pp * p.taps_per_block + t) * p.n_tile * 32, 128, 256);
-          umma_s8(tmem, ad, bd, p.idesc, (kb > 0 || i > 0) ? 1u : 0u);
-          ++i;
+    int stage = 0;
+    uint32_t ph = 0;
+    for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+      const long long m0 = (long long)t * p.tile_rows;
+      for (int kb = 0; kb < KB; ++kb) {
+        mbar_wait(&empty[stage], ph ^ 1);
+        uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
+        conv_load_a<MODE>(p, As, kb, m0, ptid);
+        cp_async_mbar_arrive(&full[stage]);
+        if (!p.b_resident && ptid == 0) {
+          mbar_arrive_expect_tx(&full[stage], p.b_block_bytes);
+          bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
+                   p.b_block_bytes, &full[stage]);
+        }
+        if (++stage == S) {
+          stage = 0;
+          ph ^= 1;
         }
       }
-      umma_commit(&mdone[st]);
     }
-  }
-  if (KB > 0) mbar_wait(&mdone[(KB - 1) % S], ((KB - 1) / S) & 1);
-  tc_fence_after();
-
-  // ---------------------------------------------------------------- epilogue
-  const int row = warp * 32 + lane;
-  const long long m = m0 + row;
-  bool valid = m < p.m_total;
-  long long opix = 0;
-  long long img = 0;
-  int oy = 0, ox = 0;
-  if (MODE == IXB_MODE_WINDOW) {
-    const long long P = (long long)(p.H + 2) * (p.W + 2);
-    img = m / P;
-    const int rem = (int)(m - img * P);
-    const int yp = rem / (p.W + 2), xp = rem - (rem / (p.W + 2)) * (p.W + 2);
-    valid = valid && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
-    opix = m;
-    oy = yp - 1;
-    ox = xp - 1;
-  } else {
-    const long long hw = (long long)p.Ho * p.Wo;
-    img = m / hw;
-    const int rem = (int)(m - img * hw);
-    oy = rem / p.Wo;
-    ox = rem - oy * p.Wo;
-    opix = img * (long long)(p.Ho + 2) * (p.Wo + 2) + (long long)(oy + 1) * (p.Wo + 2) + (ox + 1);
-  }
-  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-  for (int j = 0; j < p.n_tile / 16; ++j) {
-    uint32_t v[16];
-    tmem_ld16(tl + j * 16, v);
-    tmem_ld_wait();
-    if (!valid) continue;
-    const int co = ntile * p.n_tile + j * 16;
-    int bias[16];
-    {
-      const int4* bp = reinterpret_cast<const int4*>(p.bias + co);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int4 b4 = __ldg(bp + q);
-        bias[4 * q] = b4.x; bias[4 * q + 1] = b4.y; bias[4 * q + 2] = b4.z; bias[4 * q + 3] = b4.w;
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      if (p.b_resident) mbar_wait(bres_bar, 0);
+      const uint32_t lbo_a = p.rowsA * 16;
+      int stage = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+        mbar_wait(&acc_empty[acc], aph ^ 1);
+        tc_fence_after();
+        const uint32_t d0 = tmem + acc * p.acc_cols;
+        for (int kb = 0; kb < KB; ++kb) {
+          mbar_wait(&full[stage], ph);
+          fence_proxy_async_smem();
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes);
+          const uint32_t b0 = p.b_resident ? smem_u32(smem) + kb * p.b_block_bytes : a0 + p.a_stage_bytes;
+          for (int pp = 0; pp < p.cp; ++pp) {
+            for (int tap = 0; tap < p.taps_per_block; ++tap) {
+              uint32_t shift_px = 0;
+              if (MODE == IXB_MODE_WINDOW) shift_px = (tap / p.k) * (p.W + 2) + (tap - (tap / p.k) * p.k);
+              const uint64_t bd = umma_desc(b0 + (pp * p.taps_per_block + tap) * p.n_tile * 32, 128, 256);
+              const uint32_t accum = (kb > 0 || pp > 0 || tap > 0) ? 1u : 0u;
+              for (int b = 0; b < p.mt; ++b) {
+                const uint64_t ad = umma_desc(a0 + pp * 2 * lbo_a + (b * kBlockM + shift_px) * 16, lbo_a, 128);
+                umma_s8(d0 + b * p.n_tile, ad, bd, p.idesc, accum);
+              }
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            ph ^= 1;
+          }
+        }
+        umma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
       }
     }
-    int8_t rv[16];
-    if (p.has_res) {
-      const uint4 r4 = *reinterpret_cast<const uint4*>(p.res.base + opix * p.res.pitch + p.res.ch_off + co);
-      *reinterpret_cast<uint4*>(rv) = r4;
-    }
-    alignas(16) int8_t ov[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int a = (int)v[i] + bias[i];
-      int t = lut_s[clamp_i8(rne_shift(a, p.shift)) + 128];
-      if (p.has_res)
-        t = clamp_i8(rne_shift((t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r), p.res_shift));
-      ov[i] = (int8_t)t;
-    }
-    if (!p.out_nchw) {
-      *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + opix * p.out.pitch + p.out.ch_off + co) =
-          *reinterpret_cast<const uint4*>(ov);
-    } else {
-      int8_t* e = p.egress + img * p.egress_img + (long long)oy * p.Wo + ox;
-      const long long plane = (long long)p.Ho * p.Wo;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) e[(co + i) * plane] = ov[i];
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 0-3)
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+      mbar_wait(&acc_full[acc], aph);
+      tc_fence_after();
+      conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, (long long)t * p.tile_rows, ntile, warp, lane, lut_s,
+                               bias_s);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
     }
   }
   tc_fence_before();
   __syncthreads();
+  tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, p.tmem_cols);
 }
 

@@ -146,6 +146,10 @@ int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms);
 /* One layer on caller-owned device memory: arena is the base every offset refers to. */
 int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);
 int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);
+/* The launch a conv descriptor gets for `batch` images (host-side decision, no GPU needed):
+ * info = {blocks of 128 pixels per tile, tile rows, tiles, pipeline stages, weights resident,
+ *         grid.x, grid.y, shared bytes, TMEM columns, K-blocks, A rows per stage, pairs per K-block}. */
+int ixb_conv_launch_info(const ixb_conv_desc* d, uint64_t arena_bytes, int batch, int32_t* info, int n);
 int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w,
                         int8_t* padded_nhwc4, void* stream);
 

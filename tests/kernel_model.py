@@ -39,7 +39,10 @@ def _seg_params(d, s, chunk_begin):
                 img=(int(s.height) + 2) * (int(s.width) + 2) * int(s.pitch))
 
 
-def run_conv(arena: np.ndarray, d, batch: int) -> None:
+def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
+    info = L.conv_launch_info(d, arena_bytes, batch)
+    MT = info["mt"]
+    TM = 128 * MT
     mode, k, stride = d.mode, d.k, d.stride
     pad = k // 2
     H, W, Ho, Wo = d.in_h, d.in_w, d.out_h, d.out_w
@@ -55,34 +58,35 @@ def run_conv(arena: np.ndarray, d, batch: int) -> None:
         kblocks = (pairs + cp - 1) // cp
         taps_pb, groups = k * k, kblocks
         win_origin = pad * (W + 2) + pad
-        rowsA = TILE_M + 2 * win_origin
+        rowsA = TM + 2 * win_origin
         b_block = cp * k * k * n_tile * 32
         m_total = batch * (H + 2) * (W + 2)
     elif mode == L.MODE_GATHER:
         groups = (pairs + cp - 1) // cp
-        kblocks, taps_pb, rowsA, win_origin = k * k * groups, 1, TILE_M, 0
+        kblocks, taps_pb, rowsA, win_origin = k * k * groups, 1, TM, 0
         b_block = cp * n_tile * 32
         m_total = batch * Ho * Wo
     else:
-        kblocks, taps_pb, groups, rowsA, win_origin = 1, 1, 1, TILE_M, 0
+        kblocks, taps_pb, groups, rowsA, win_origin = 1, 1, 1, TM, 0
         b_block = 2 * n_tile * 32
         m_total = batch * Ho * Wo
     assert (d.cout // n_tile) * kblocks * b_block == d.w_bytes
+    assert info["kblocks"] == kblocks and info["rows_a"] == rowsA
     a_bytes = 2 * cp * rowsA * 16
     bias = arena[d.bias_offset:d.bias_offset + 4 * d.cout].view(np.int32).astype(np.int64)
     lut = arena[d.lut_offset:d.lut_offset + 256].view(np.int8).astype(np.int64)
     nch = 2 * cp
-    for mt in range((m_total + TILE_M - 1) // TILE_M):
-        m0 = mt * TILE_M
+    for mt in range((m_total + TM - 1) // TM):
+        m0 = mt * TM
         for nt in range(d.cout // n_tile):
-            acc = np.zeros((TILE_M, n_tile), dtype=np.int64)
+            acc = np.zeros((TM, n_tile), dtype=np.int64)
             for kb in range(kblocks):
                 smem = np.zeros(a_bytes + b_block, dtype=np.uint8)
                 # ---- A
                 for c in range(nch):
                     dst0 = c * rowsA * 16
                     if mode == L.MODE_STEM:
-                        r = np.arange(TILE_M)
+                        r = np.arange(TM)
                         m = m0 + r
                         ok = (c < 3) & (m < m_total)
                         s = segs[0]
@@ -111,7 +115,7 @@ def run_conv(arena: np.ndarray, d, batch: int) -> None:
                         src = cbase + m * s["pitch"]
                         rows = px
                     else:
-                        r = np.arange(TILE_M)
+                        r = np.arange(TM)
                         m = m0 + r
                         ok = m < m_total
                         img = m // (Ho * Wo)
@@ -133,11 +137,12 @@ def run_conv(arena: np.ndarray, d, batch: int) -> None:
                 for pp in range(cp):
                     for t in range(taps_pb):
                         shift_px = (t // k) * (W + 2) + (t % k) if mode == L.MODE_WINDOW else 0
-                        A = _operand(smem, pp * 2 * lbo_a + shift_px * 16, lbo_a, 128, TILE_M)
                         B = _operand(smem, a_bytes + (pp * taps_pb + t) * n_tile * 32, 128, 256, n_tile)
-                        acc += A @ B.T
+                        for blk in range(MT):
+                            A = _operand(smem, pp * 2 * lbo_a + (blk * 128 + shift_px) * 16, lbo_a, 128, 128)
+                            acc[blk * 128:(blk + 1) * 128] += A @ B.T
             # ---- epilogue
-            m = m0 + np.arange(TILE_M)
+            m = m0 + np.arange(TM)
             valid = m < m_total
             if mode == L.MODE_WINDOW:
                 P = (H + 2) * (W + 2)
@@ -207,7 +212,7 @@ def run_network(dp: DevicePlan, images: np.ndarray) -> np.ndarray:
     convs = [c.desc for c in dp.convs]
     for kind, idx in dp.ops:
         if kind == L.OP_CONV:
-            run_conv(arena, convs[idx], batch)
+            run_conv(arena, convs[idx], batch, dp.arena_bytes)
         else:
             run_pool(arena, dp.pools[idx][1], batch)
     e = arena[dp.egress_offset:dp.egress_offset + batch * dp.egress_image_bytes]

@@ -22,8 +22,12 @@ def hashes(golden_dir):
     return json.loads((golden_dir / "graph_hashes.json").read_text())
 
 
-@pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 3), (128, 1)])
-def test_small_graph_every_tensor(imgsz, batch):
+@pytest.mark.parametrize("imgsz,batch,sms", [(64, 2, None), (96, 3, None), (128, 1, None), (64, 2, "1"),
+                                            (96, 3, "2"), (128, 2, "4")])
+def test_small_graph_every_tensor(imgsz, batch, sms, monkeypatch):
+    """sms forces the launch planner's SM count, so small inputs also run 256/512-row tiles."""
+    if sms:
+        monkeypatch.setenv("IXB_SM_COUNT", sms)
     sess = InferenceSession.from_spec("yolov8n", imgsz=imgsz, max_batch=batch)
     imgs = random_images(batch, imgsz, seed=21 + imgsz)
     out = sess.run_yolo_monolithic(imgs)

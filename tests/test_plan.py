@@ -9,8 +9,11 @@ from ignite_xdna_b200 import build_yolov8, random_images
 from ignite_xdna_b200.plan import build_plan, conv_kblocks, input_lut_t
 
 
-@pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 1)])
-def test_kernel_model_matches_oracle(imgsz, batch):
+@pytest.mark.parametrize("imgsz,batch,sms", [(64, 2, None), (96, 1, None), (64, 2, "1"), (96, 1, "2")])
+def test_kernel_model_matches_oracle(imgsz, batch, sms, monkeypatch):
+    """sms forces the launch planner's SM count, so small inputs take the 256/512-row tiles."""
+    if sms:
+        monkeypatch.setenv("IXB_SM_COUNT", sms)
     ir = build_yolov8("n", imgsz=imgsz)
     dp = build_plan(ir, batch)
     imgs = random_images(batch, imgsz, seed=11)
