@@ -17,15 +17,16 @@ IXB_OK = 0
 ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
 IXB_ERR_TIMEOUT = -3
 MAX_SEGS = 4
-API_VERSION = 1
+API_VERSION = 2
 MODE_WINDOW, MODE_GATHER, MODE_STEM = 0, 1, 2
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH = 1, 2, 4, 8
 OP_CONV, OP_POOL = 0, 1
 
 
 class Segment(C.Structure):
-    _fields_ = [("offset", C.c_uint64), ("pitch", C.c_int32), ("ch_offset", C.c_int32),
-                ("channels", C.c_int32), ("height", C.c_int32), ("width", C.c_int32), ("up2", C.c_int32)]
+    _fields_ = [("offset", C.c_uint64), ("plane_stride", C.c_uint64), ("chunk_offset", C.c_int32),
+                ("channels", C.c_int32), ("height", C.c_int32), ("width", C.c_int32), ("up2", C.c_int32),
+                ("guard", C.c_int32)]
 
 
 class ConvDesc(C.Structure):

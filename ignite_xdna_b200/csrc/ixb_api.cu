@@ -72,32 +72,43 @@ int sm_count() {
   return cached[dev];
 }
 
-// The bytes a view can touch for `batch` images: from its offset to the end of the last image.
+// A view touches, for `batch` images, every chunk plane it names from `guard` pixels before the
+// first image to `guard` pixels after the last; all of it must lie inside the arena, the planes
+// must not overlap, and the 16-byte copies need 16-byte alignment.
 int check_seg(const ixb_segment& s, int batch, uint64_t arena_bytes, bool image, const char* what,
               std::string& err) {
   char buf[256];
-  const int need_pitch = image ? 4 : 16;
-  if (s.height < 1 || s.width < 1 || s.channels < 1 || s.pitch < 1 || s.ch_offset < 0) {
+  if (s.height < 1 || s.width < 1 || s.channels < 1 || s.chunk_offset < 0 || s.guard < 0) {
     snprintf(buf, sizeof buf, "%s: empty or negative view", what);
     err = buf;
     return -1;
   }
-  if (s.offset % 16 || s.pitch % need_pitch || s.ch_offset % 16 || s.ch_offset + s.channels > s.pitch) {
-    snprintf(buf, sizeof buf, "%s: misaligned view (offset %llu pitch %d ch_offset %d channels %d)", what,
-             (unsigned long long)s.offset, s.pitch, s.ch_offset, s.channels);
+  const unsigned long long pix = (unsigned long long)batch * (s.height + 2) * (unsigned long long)(s.width + 2);
+  if (image) {
+    if (s.channels != 3 || s.chunk_offset || s.guard || s.offset % 16 || s.offset + pix * 4 > arena_bytes) {
+      snprintf(buf, sizeof buf, "%s: the image tensor is one guard-free plane of 4-byte pixels inside the arena",
+               what);
+      err = buf;
+      return -1;
+    }
+    return 0;
+  }
+  if (s.channels % 16 || s.offset % 16 || s.plane_stride % 16) {
+    snprintf(buf, sizeof buf, "%s: misaligned view (offset %llu plane %llu channels %d)", what,
+             (unsigned long long)s.offset, (unsigned long long)s.plane_stride, s.channels);
     err = buf;
     return -1;
   }
-  if (!image && s.channels % 16) {
-    snprintf(buf, sizeof buf, "%s: %d channels is not a multiple of 16", what, s.channels);
+  const unsigned long long nch = s.channels / 16;
+  if (nch > 1 && s.plane_stride < (pix + 2ull * s.guard) * 16) {
+    snprintf(buf, sizeof buf, "%s: chunk planes overlap", what);
     err = buf;
     return -1;
   }
-  const unsigned long long bytes =
-      (unsigned long long)batch * (s.height + 2) * (unsigned long long)(s.width + 2) * s.pitch;
-  if (s.offset + bytes > arena_bytes) {
-    snprintf(buf, sizeof buf, "%s: view ends at %llu, past the %llu-byte arena", what,
-             (unsigned long long)(s.offset + bytes), (unsigned long long)arena_bytes);
+  const unsigned long long first = (unsigned long long)s.chunk_offset * s.plane_stride;
+  if (s.offset + first < 16ull * s.guard ||
+      s.offset + first + (nch - 1) * s.plane_stride + (pix + s.guard) * 16 > arena_bytes) {
+    snprintf(buf, sizeof buf, "%s: view reaches outside the %llu-byte arena", what, (unsigned long long)arena_bytes);
     err = buf;
     return -1;
   }
@@ -106,15 +117,14 @@ int check_seg(const ixb_segment& s, int batch, uint64_t arena_bytes, bool image,
 
 SegDev seg_dev(const ixb_segment& s, uint8_t* arena, int chunk_begin) {
   SegDev d;
-  d.base = reinterpret_cast<const int8_t*>(arena + s.offset);
-  d.img_stride = (long long)(s.height + 2) * (s.width + 2) * s.pitch;
-  d.pitch = s.pitch;
-  d.ch_off = s.ch_offset;
+  d.base = reinterpret_cast<const int8_t*>(arena + s.offset + (uint64_t)s.chunk_offset * s.plane_stride);
+  d.plane = (long long)s.plane_stride;
   d.chunk_begin = chunk_begin;
   d.chunks = (s.channels + 15) / 16;
   d.H = s.height;
   d.W = s.width;
   d.up2 = s.up2;
+  d.P = (s.height + 2) * (s.width + 2);
   return d;
 }
 
@@ -175,7 +185,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   if (cin != d.cin) return bad("segment channels do not add up to cin");
   if (d.mode == IXB_MODE_STEM) {
-    if (d.k != 3 || d.stride != 2 || d.nseg != 1 || d.cin != 3 || d.seg[0].pitch != 4 || d.cp != 2)
+    if (d.k != 3 || d.stride != 2 || d.nseg != 1 || d.cin != 3 || d.seg[0].channels != 3 || d.cp != 2)
       return bad("STEM mode is a 3x3 stride-2 conv of the 3-channel 4-byte-pixel image with cp = 2");
     if (d.in_h % 2 || d.in_w % 2) return bad("STEM needs an even input size");
   }
@@ -189,20 +199,22 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.pair_groups = p.kblocks;
     p.win_origin = pad * (d.in_w + 2) + pad;
     b_block = d.cp * d.k * d.k * d.n_tile * 32;
-    p.m_total = (long long)batch * (d.in_h + 2) * (d.in_w + 2);
+    p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * (d.in_h + 2) * (d.in_w + 2));
   } else if (d.mode == IXB_MODE_GATHER) {
     p.pair_groups = (pairs + d.cp - 1) / d.cp;
     p.kblocks = d.k * d.k * p.pair_groups;
     p.taps_per_block = 1;
     b_block = d.cp * d.n_tile * 32;
-    p.m_total = (long long)batch * d.out_h * d.out_w;
+    p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * d.out_w);
   } else {
     p.kblocks = 1;
     p.pair_groups = 1;
     p.taps_per_block = 1;
     b_block = 2 * d.n_tile * 32;
-    p.m_total = (long long)batch * d.out_h * d.out_w;
+    p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * d.out_w);
   }
+  if ((long long)batch * (d.in_h + 2) * (d.in_w + 2) >= 0x7fff0000LL)
+    return bad("more pixels than 32-bit pixel indices cover");
   const long long ntiles = d.cout / d.n_tile;
   if ((unsigned long long)ntiles * p.kblocks * b_block != d.w_bytes) {
     snprintf(buf, sizeof buf, "packed weights are %llu bytes, the tiling needs %llu",
@@ -226,7 +238,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   p.b_block_bytes = b_block;
   const int b_total = p.kblocks * b_block;
-  const int extra = 512 + 256 + 1024;   // barriers, activation table, bias
+  const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * 512 * 8);  // barriers, table, bias, rows
   const int budget = kSmemLimit - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
@@ -245,7 +257,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     if (mt == 1) return bad("a pipeline stage does not fit shared memory");
   }
   p.m_tiles = (int)((p.m_total + p.tile_rows - 1) / p.tile_rows);
-  p.bar_off = p.a_off + p.stages * p.stage_bytes;
+  p.tbl_off = p.a_off + p.stages * p.stage_bytes;
+  p.bar_off = p.tbl_off + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * p.tile_rows * 8);
   p.lut_off = p.bar_off + 512;
   p.bias_off = p.lut_off + 256;
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
@@ -295,8 +308,16 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
       if (!same(d.seg[i])) return bad("WINDOW views must share the input geometry");
     if (!d.out_nchw && !same(d.out)) return bad("WINDOW output must share the input geometry");
   }
+  if (d.mode == IXB_MODE_WINDOW) {
+    // every window copy stays inside the planes' zero guards
+    for (int i = 0; i < d.nseg; ++i) {
+      const long long end = (long long)p.m_tiles * p.tile_rows + p.win_origin;
+      if (p.win_origin > d.seg[i].guard || end > (long long)batch * (d.in_h + 2) * (d.in_w + 2) + d.seg[i].guard)
+        return bad("input plane guards are smaller than the window over-reach");
+    }
+  }
   const int smem = p.bias_off + 4 * d.n_tile + 1024;
-  const int per_sm = (p.tmem_cols <= 256 && 2 * smem <= 228 * 1024) ? 2 : 1;
+  const int per_sm = 1;
   const long long gm =
       std::max<long long>(1, std::min<long long>(p.m_tiles, ((long long)sms * per_sm + ntiles - 1) / ntiles));
   L.grid = dim3((unsigned)gm, (unsigned)ntiles, 1);
@@ -358,6 +379,10 @@ int build_pool(const ixb_pool_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   L.p.H = d.in.height;
   L.p.W = d.in.width;
   L.p.chunks = d.in.channels / 16;
+  if (d.in.height * d.in.width * 16 * 3 > kSmemLimit) {
+    err = "pool plane does not fit shared memory";
+    return -1;
+  }
   L.grid = dim3(L.p.chunks, batch, 1);
   return 0;
 }
@@ -540,8 +565,8 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
     bad = fail(IXB_ERR_INVALID, "image staging outside the arena");
   else if (plan->input_lut_offset + 256 > s->arena_bytes) bad = fail(IXB_ERR_INVALID, "input table outside the arena");
   else if (check_seg(plan->input, B, s->arena_bytes, true, "stem input", err)) bad = fail(IXB_ERR_INVALID, err);
-  else if (plan->input.height != plan->img_h || plan->input.width != plan->img_w || plan->input.pitch != 4)
-    bad = fail(IXB_ERR_INVALID, "stem input view must be img_h x img_w x 4 bytes");
+  else if (plan->input.height != plan->img_h || plan->input.width != plan->img_w || plan->input.channels != 3)
+    bad = fail(IXB_ERR_INVALID, "stem input view must be the img_h x img_w 3-channel image");
   else if (plan->egress_offset + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes)
     bad = fail(IXB_ERR_INVALID, "egress outside the arena");
   if (!bad) bad = s->prepare(B);

@@ -9,28 +9,36 @@
 // Because 128 << shift is a multiple of 2^shift, this equals the reference's uint8 rule
 // sat_u8(rne(bias_acc + sum w * q)) - 128 exactly.
 //
+// Storage: one plane per 16-channel chunk, [batch][H+2][W+2] pixels of 16 bytes with a zero
+// halo ring per image and zero guard pixels around the plane. A K-chunk of 128 output pixels is
+// then 128 contiguous 16-byte rows in global memory, which is exactly a column of UMMA core
+// matrices in shared memory.
+//
 // GEMM view: M = output pixels, N = output channels (n_tile per CTA, one TMEM column each),
 // K = input channels x taps in 32-byte steps. A tile is MT blocks of 128 pixels; block b
-// accumulates into TMEM columns [b * n_tile, (b+1) * n_tile). Activations are int8 NHWC with a
-// one-pixel zero halo, so:
+// accumulates into TMEM columns [b * n_tile, (b+1) * n_tile).
 //  * WINDOW (stride 1, same resolution): the tile is 128*MT consecutive pixels of the
 //    flattened padded image; tap (ky, kx) of output pixel m reads padded pixel
-//    m + (ky-1)(W+2) + (kx-1), so ONE window of 128*MT + 2((W+2)+1) pixels per 32 input channels
-//    feeds all nine taps: each tap is the same smem window seen through a descriptor whose
-//    start address moves by 16 bytes per pixel of shift. Halo outputs are computed and dropped.
+//    m + (ky-1)(W+2) + (kx-1), so ONE window of 128*MT + 2((W+2)+1) pixels per chunk feeds all
+//    nine taps: each tap is the same smem window seen through a descriptor whose start moves
+//    16 bytes per pixel of shift. A window is one contiguous bulk copy (TMA engine) per chunk,
+//    issued by a single producer thread. Halo outputs are computed and dropped.
 //  * GATHER (stride 2, or an input read through a nearest-2x upsample): the tile is 128*MT
-//    interior output pixels; each tap's rows are gathered with 16-byte cp.async.
+//    interior output pixels; 128 producer threads gather each tap's rows with 16-byte cp.async
+//    from a per-tile table of output coordinates.
 //  * STEM: the 3-channel image stored as 4-byte pixels; one 16-byte K-chunk is 4 pixels x
-//    4 channels of one input row, so K = 3 rows x 16 bytes (+16 zero) covers the 3x3 window.
+//    4 channels of one input row, so K = 3 rows x 16 bytes (+16 zero-weight bytes) covers the
+//    3x3 stride-2 window.
 // Shared-memory operands use the K-major no-swizzle core-matrix layout: A as
 // [chunk][pixel][16 B] (SBO 128 B, LBO = rows x 16 B), B as [n/8][chunk][8][16 B]
 // (SBO 256 B, LBO 128 B), prepacked on the host so one bulk copy lands a K-block.
 //
-// The kernel is persistent and warp-specialised (288 threads):
-//   warps 0-3  epilogue: TMEM -> registers -> integer epilogue -> global (TMEM lane quarter = warp)
-//   warps 4-7  producers: cp.async A loads into a ring of stages, completion tracked by the
-//              stage's mbarrier (cp.async.mbarrier.arrive); producer 0 also bulk-copies B
-//   warp 8     one thread issues tcgen05.mma and commits stages / accumulators
+// The kernel is persistent and warp-specialised (416 threads):
+//   warps 0-7   epilogue: TMEM -> registers -> integer epilogue -> global; warp w reads TMEM
+//               lane quarter w % 4, warpgroups 0 and 1 split the (block, 16-column) pieces
+//   warps 8-11  producers: A loads into a ring of stages, completion on the stage mbarrier;
+//               producer 0 also bulk-copies streamed weights
+//   warp 12     one thread issues tcgen05.mma and commits stages and accumulators
 // Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next. When a
 // CTA's weights fit, they are loaded once and stay resident in shared memory.
 #pragma once
@@ -41,22 +49,21 @@
 namespace ixb {
 
 struct SegDev {
-  const int8_t* base;    // padded pixel (0,0) of image 0
-  long long img_stride;  // bytes per image
-  int pitch, ch_off;
+  const int8_t* base;  // padded pixel 0 of image 0 in the view's first chunk plane
+  long long plane;     // bytes between chunk planes
   int chunk_begin, chunks;  // 16-channel chunks of the logical input this view supplies
-  int H, W, up2;
+  int H, W, up2, P;         // stored size, upsampled view, padded pixels per image
 };
 
 struct ConvParams {
   int mode, k, stride, pad;
   int H, W, Ho, Wo, batch;
-  long long m_total;
+  int m_total;
   int cin_chunks, cp, kblocks, taps_per_block, pair_groups;
   int mt, tile_rows, m_tiles;
   int rowsA, win_origin;
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
-  int b_resident, a_off, bar_off, lut_off, bias_off;
+  int b_resident, a_off, tbl_off, bar_off, lut_off, bias_off;
   int n_tile, acc_cols, tmem_cols;
   uint32_t idesc;
   int nseg;
@@ -76,130 +83,208 @@ struct ConvParams {
   int cout;
 };
 
+constexpr int kEpiWarps = 8;
+constexpr int kProducerWarp0 = 8;
 constexpr int kProducerThreads = 128;
-constexpr int kConvThreads = 288;
+constexpr int kMmaWarp = 12;
+constexpr int kConvThreads = 416;
 constexpr int kBlockM = 128;
 
-template <int MODE>
-__device__ __forceinline__ void conv_load_a(const ConvParams& p, uint8_t* As, int kb, long long m0, int tid) {
-  const int nch = 2 * p.cp;
-  const int c = tid % nch;  // 128 is a multiple of nch, so each thread keeps one chunk
-  const int step = kProducerThreads / nch;
-  uint8_t* dst = As + c * p.rowsA * 16;
-  if (MODE == IXB_MODE_STEM) {
-    const SegDev& s = p.seg[0];
-    const long long hw = (long long)p.Ho * p.Wo;
-    for (int r = tid / nch; r < p.tile_rows; r += step) {
-      const long long m = m0 + r;
-      const bool ok = c < 3 && m < p.m_total;
-      const int8_t* src = s.base;
-      if (ok) {
-        const long long img = m / hw;
-        const int rem = (int)(m - img * hw);
-        const int y = rem / p.Wo, x = rem - (rem / p.Wo) * p.Wo;
-        // padded row 2y + ky, padded columns 2x .. 2x+3 (input columns 2x-1 .. 2x+2)
-        src = s.base + img * s.img_stride + ((long long)(2 * y + c) * (s.W + 2) + 2 * x) * s.pitch;
-      }
-      cp_async8(dst + r * 16, src, ok ? 8u : 0u);
-      cp_async8(dst + r * 16 + 8, ok ? src + 8 : src, ok ? 8u : 0u);
-    }
-    return;
-  }
-  int gc, tap = 0;
-  if (MODE == IXB_MODE_WINDOW) {
-    gc = kb * nch + c;
-  } else {
-    tap = kb / p.pair_groups;
-    gc = (kb - tap * p.pair_groups) * nch + c;
-  }
+__device__ __forceinline__ void producer_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ int seg_of_chunk(const ConvParams& p, int gc) {
   int si = -1;
 #pragma unroll
   for (int s = 0; s < IXB_MAX_SEGS; ++s)
     if (s < p.nseg && gc >= p.seg[s].chunk_begin && gc < p.seg[s].chunk_begin + p.seg[s].chunks) si = s;
-  const bool cvalid = si >= 0;
-  const SegDev& s = p.seg[cvalid ? si : 0];
-  const int8_t* cbase = s.base + s.ch_off + (cvalid ? (gc - s.chunk_begin) * 16 : 0);
-  if (MODE == IXB_MODE_WINDOW) {
-    const long long wb = m0 - p.win_origin;
-    for (int px = tid / nch; px < p.rowsA; px += step) {
-      const long long m = wb + px;
-      const bool ok = cvalid && m >= 0 && m < p.m_total;
-      cp_async16(dst + px * 16, ok ? cbase + m * s.pitch : s.base, ok ? 16u : 0u);
-    }
-  } else {
-    const int ky = tap / p.k, kx = tap - (tap / p.k) * p.k;
-    const long long hw = (long long)p.Ho * p.Wo;
-    for (int r = tid / nch; r < p.tile_rows; r += step) {
-      const long long m = m0 + r;
-      const bool ok = cvalid && m < p.m_total;
-      const int8_t* src = s.base;
-      if (ok) {
-        const long long img = m / hw;
-        const int rem = (int)(m - img * hw);
-        const int y = rem / p.Wo, x = rem - (rem / p.Wo) * p.Wo;
-        int iy = y * p.stride + ky - p.pad, ix = x * p.stride + kx - p.pad;
-        if (s.up2) { iy >>= 1; ix >>= 1; }
-        src = cbase + img * s.img_stride + ((long long)(iy + 1) * (s.W + 2) + (ix + 1)) * s.pitch;
+  return si;
+}
+
+// Round half to even of x / 2^s, s in [1, 16], without branches: the floor of
+// (x + 2^(s-1) - 1 + bit s of x) / 2^s.
+__device__ __forceinline__ int rne_pos(int x, int s, int half_m1) { return (x + half_m1 + ((x >> s) & 1)) >> s; }
+
+// ---------------------------------------------------------------- producers
+template <int MODE>
+__device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                               int ntile) {
+  const int nch = 2 * p.cp;
+  const int S = p.stages;
+  const uint32_t chunk_bytes = (uint32_t)p.rowsA * 16;
+  int stage = 0;
+  uint32_t ph = 0;
+  for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+    const long long wb = (long long)t * p.tile_rows - p.win_origin;
+    for (int kb = 0; kb < p.kblocks; ++kb) {
+      mbar_wait(&empty[stage], ph ^ 1);
+      uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
+      const int valid = min(nch, p.cin_chunks - kb * nch);
+      uint32_t bytes = (uint32_t)valid * chunk_bytes + (p.b_resident ? 0u : (uint32_t)p.b_block_bytes);
+      mbar_arrive_expect_tx(&full[stage], bytes);
+      for (int c = 0; c < valid; ++c) {
+        const int gc = kb * nch + c;
+        const SegDev& s = p.seg[seg_of_chunk(p, gc)];
+        bulk_g2s(As + c * chunk_bytes, s.base + (long long)(gc - s.chunk_begin) * s.plane + wb * 16, chunk_bytes,
+                 &full[stage]);
       }
-      cp_async16(dst + r * 16, src, ok ? 16u : 0u);
+      if (!p.b_resident)
+        bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
+                 p.b_block_bytes, &full[stage]);
+      if (++stage == S) {
+        stage = 0;
+        ph ^= 1;
+      }
     }
   }
 }
 
 template <int MODE>
-__device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, long long m0, int ntile,
-                                                   int warp, int lane, const int8_t* lut_s, const int* bias_s) {
+__device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                               int ntile, int ptid) {
+  const int nch = 2 * p.cp;
+  const int c = ptid % nch;  // 128 is a multiple of nch, so each thread keeps one chunk
+  const int step = kProducerThreads / nch;
+  const int S = p.stages;
+  const int hw = p.Ho * p.Wo;
+  int2* tbl = reinterpret_cast<int2*>(smem + p.tbl_off);
+  int stage = 0;
+  uint32_t ph = 0;
+  int it = 0;
+  for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x, ++it) {
+    const int m0 = t * p.tile_rows;
+    int2* T = tbl + (it & 1) * p.tile_rows;
+    for (int r = ptid; r < p.tile_rows; r += kProducerThreads) {
+      const int m = m0 + r;
+      if (m < p.m_total) {
+        const int img = m / hw;
+        const int rem = m - img * hw;
+        const int y = rem / p.Wo;
+        T[r] = make_int2(img, (y << 16) | (rem - y * p.Wo));
+      } else {
+        T[r] = make_int2(-1, 0);
+      }
+    }
+    producer_bar_sync();
+    for (int kb = 0; kb < p.kblocks; ++kb) {
+      mbar_wait(&empty[stage], ph ^ 1);
+      uint8_t* dst = smem + p.a_off + stage * p.stage_bytes + c * p.rowsA * 16;
+      if (MODE == IXB_MODE_STEM) {
+        const SegDev& s = p.seg[0];
+        if (c < 3) {
+          for (int r = ptid / nch; r < p.tile_rows; r += step) {
+            const int2 e = T[r];
+            if (e.x >= 0) {
+              const int y = e.y >> 16, x = e.y & 0xFFFF;
+              // padded row 2y + ky, padded columns 2x .. 2x+3 (input columns 2x-1 .. 2x+2)
+              const int8_t* src = s.base + ((long long)e.x * s.P + (2 * y + c) * (s.W + 2) + 2 * x) * 4;
+              cp_async8(dst + r * 16, src, 8u);
+              cp_async8(dst + r * 16 + 8, src + 8, 8u);
+            } else {
+              cp_async16(dst + r * 16, s.base, 0u);
+            }
+          }
+        }
+      } else {
+        const int tap = kb / p.pair_groups;
+        const int gc = (kb - tap * p.pair_groups) * nch + c;
+        const int ky = tap / p.k, kx = tap - (tap / p.k) * p.k;
+        const int si = seg_of_chunk(p, gc);
+        if (si >= 0) {
+          const SegDev& s = p.seg[si];
+          const int8_t* cbase = s.base + (long long)(gc - s.chunk_begin) * s.plane;
+          for (int r = ptid / nch; r < p.tile_rows; r += step) {
+            const int2 e = T[r];
+            if (e.x >= 0) {
+              int iy = (e.y >> 16) * p.stride + ky - p.pad, ix = (e.y & 0xFFFF) * p.stride + kx - p.pad;
+              if (s.up2) {
+                iy >>= 1;
+                ix >>= 1;
+              }
+              cp_async16(dst + r * 16, cbase + ((long long)e.x * s.P + (iy + 1) * (s.W + 2) + (ix + 1)) * 16, 16u);
+            } else {
+              cp_async16(dst + r * 16, s.base, 0u);
+            }
+          }
+        }
+      }
+      cp_async_mbar_arrive(&full[stage]);
+      if (!p.b_resident && ptid == 0) {
+        mbar_arrive_expect_tx(&full[stage], p.b_block_bytes);
+        bulk_g2s(smem + p.a_off + stage * p.stage_bytes + p.a_stage_bytes,
+                 p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes, p.b_block_bytes, &full[stage]);
+      }
+      if (++stage == S) {
+        stage = 0;
+        ph ^= 1;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- epilogue
+template <int MODE>
+__device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
+                                                   int lane, const int8_t* lut_s, const int* bias_s) {
+  const int q = warp & 3, g = warp >> 2;
+  const int nj = p.n_tile / 16;
+  const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0;
+  const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0;
   for (int b = 0; b < p.mt; ++b) {
-    const int row = b * kBlockM + warp * 32 + lane;
-    const long long m = m0 + row;
+    const int m = m0 + b * kBlockM + q * 32 + lane;
     bool valid = m < p.m_total;
-    long long opix = 0, img = 0;
-    int oy = 0, ox = 0;
+    int opix, img, oy, ox;
     if (MODE == IXB_MODE_WINDOW) {
-      const long long P = (long long)(p.H + 2) * (p.W + 2);
+      const int P = (p.H + 2) * (p.W + 2);
       img = m / P;
-      const int rem = (int)(m - img * P);
+      const int rem = m - img * P;
       const int yp = rem / (p.W + 2), xp = rem - (rem / (p.W + 2)) * (p.W + 2);
       valid = valid && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
       opix = m;
       oy = yp - 1;
       ox = xp - 1;
     } else {
-      const long long hw = (long long)p.Ho * p.Wo;
+      const int hw = p.Ho * p.Wo;
       img = m / hw;
-      const int rem = (int)(m - img * hw);
+      const int rem = m - img * hw;
       oy = rem / p.Wo;
       ox = rem - oy * p.Wo;
-      opix = img * (long long)(p.Ho + 2) * (p.Wo + 2) + (long long)(oy + 1) * (p.Wo + 2) + (ox + 1);
+      opix = img * (p.Ho + 2) * (p.Wo + 2) + (oy + 1) * (p.Wo + 2) + (ox + 1);
     }
-    const uint32_t tl = tacc + b * p.n_tile + ((uint32_t)(warp * 32) << 16);
-    for (int j = 0; j < p.n_tile / 16; ++j) {
+    const uint32_t tl = tacc + b * p.n_tile + ((uint32_t)(q * 32) << 16);
+    for (int j = 0; j < nj; ++j) {
+      if (((b * nj + j) & 1) != g) continue;  // the two warpgroups take alternate pieces
       uint32_t v[16];
       tmem_ld16(tl + j * 16, v);
       tmem_ld_wait();
       if (!valid) continue;
-      const int cl = j * 16;                 // channel within the n-tile
-      const int co = ntile * p.n_tile + cl;  // output channel
+      const int cl = j * 16;                   // channel within the n-tile
+      const int oc = ntile * nj + j;           // output chunk
       int8_t rv[16];
       if (p.has_res)
         *reinterpret_cast<uint4*>(rv) =
-            *reinterpret_cast<const uint4*>(p.res.base + opix * p.res.pitch + p.res.ch_off + co);
+            *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)opix * 16);
       alignas(16) int8_t ov[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int a = (int)v[i] + bias_s[cl + i];
-        int t = lut_s[clamp_i8(rne_shift(a, p.shift)) + 128];
-        if (p.has_res) t = clamp_i8(rne_shift((t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r), p.res_shift));
+        const int r1 = s > 0 ? rne_pos(a, s, hs) : a;
+        int t = lut_s[clamp_i8(r1) + 128];
+        if (p.has_res) {
+          const int y = (t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
+          t = clamp_i8(rs > 0 ? rne_pos(y, rs, rhs) : y);
+        }
         ov[i] = (int8_t)t;
       }
       if (!p.out_nchw) {
-        *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + opix * p.out.pitch + p.out.ch_off + co) =
-            *reinterpret_cast<const uint4*>(ov);
+        *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane +
+                                  (long long)opix * 16) = *reinterpret_cast<const uint4*>(ov);
       } else {
-        int8_t* e = p.egress + img * p.egress_img + (long long)oy * p.Wo + ox;
+        int8_t* e = p.egress + (long long)img * p.egress_img + oy * p.Wo + ox;
         const long long plane = (long long)p.Ho * p.Wo;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) e[(co + i) * plane] = ov[i];
+        for (int i = 0; i < 16; ++i) e[(ntile * p.n_tile + cl + i) * plane] = ov[i];
       }
     }
   }
@@ -226,15 +311,16 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
-  if (tid == kConvThreads - 32) {
-    const uint32_t fcount = kProducerThreads + (p.b_resident ? 0 : 1);
+  if (tid == kMmaWarp * 32) {
+    const uint32_t fcount =
+        (MODE == IXB_MODE_WINDOW) ? 1u : (uint32_t)kProducerThreads + (p.b_resident ? 0u : 1u);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], fcount);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], kEpiWarps * 32);
     }
     mbar_init(bres_bar, 1);
     fence_mbar_init();
@@ -246,36 +332,21 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 4 && warp < 8) {
+  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
     // ------------------------------------------------------------ producers
-    const int ptid = tid - 128;
+    const int ptid = tid - kProducerWarp0 * 32;
     if (p.b_resident && ptid == 0) {
       mbar_arrive_expect_tx(bres_bar, (uint32_t)(KB * p.b_block_bytes));
       for (int kb = 0; kb < KB; ++kb)
         bulk_g2s(smem + kb * p.b_block_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
                  p.b_block_bytes, bres_bar);
     }
-    int stage = 0;
-    uint32_t ph = 0;
-    for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
-      const long long m0 = (long long)t * p.tile_rows;
-      for (int kb = 0; kb < KB; ++kb) {
-        mbar_wait(&empty[stage], ph ^ 1);
-        uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
-        conv_load_a<MODE>(p, As, kb, m0, ptid);
-        cp_async_mbar_arrive(&full[stage]);
-        if (!p.b_resident && ptid == 0) {
-          mbar_arrive_expect_tx(&full[stage], p.b_block_bytes);
-          bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
-                   p.b_block_bytes, &full[stage]);
-        }
-        if (++stage == S) {
-          stage = 0;
-          ph ^= 1;
-        }
-      }
+    if (MODE == IXB_MODE_WINDOW) {
+      if (ptid == 0) produce_window<MODE>(p, smem, full, empty, ntile);
+    } else {
+      produce_gather<MODE>(p, smem, full, empty, ntile, ptid);
     }
-  } else if (warp == 8) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       if (p.b_resident) mbar_wait(bres_bar, 0);
@@ -288,7 +359,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
         const uint32_t d0 = tmem + acc * p.acc_cols;
         for (int kb = 0; kb < KB; ++kb) {
           mbar_wait(&full[stage], ph);
-          fence_proxy_async_smem();
+          if (MODE != IXB_MODE_WINDOW) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
           tc_fence_after();
           const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes);
           const uint32_t b0 = p.b_resident ? smem_u32(smem) + kb * p.b_block_bytes : a0 + p.a_stage_bytes;
@@ -316,14 +387,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 0-3)
+    // ------------------------------------------------------------ epilogue (warps 0-7)
     int acc = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
       mbar_wait(&acc_full[acc], aph);
       tc_fence_after();
-      conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, (long long)t * p.tile_rows, ntile, warp, lane, lut_s,
-                               bias_s);
+      conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias_s);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       acc ^= 1;

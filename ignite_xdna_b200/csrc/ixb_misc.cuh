@@ -50,9 +50,10 @@ __device__ __forceinline__ uint4 vmax16(uint4 a, uint4 b) {
 
 // SPPF: out[k] = pool5^(k+1)(in) for k = 0, 1, 2, each a 5x5 stride-1 max with -128 padding
 // (uint8 0 in the reference, graph_reference.py:64-72; three chained MaxPool layers,
-// graph_ir.py:1120-1133). One CTA per (16-channel chunk, image); the whole plane of the
-// chunk lives in shared memory as 16-byte pixels and each pool is a row pass then a
-// column pass of per-byte signed maxima.
+// graph_ir.py:1120-1133). One CTA per (16-channel chunk plane, image); the image's plane lives
+// in shared memory as 16-byte pixels and each pool is a row pass then a column pass of
+// per-byte signed maxima. Out-of-image taps are skipped, which equals -128 padding because the
+// window centre is always inside.
 __global__ void __launch_bounds__(256) sppf_kernel(const __grid_constant__ PoolParams p) {
   extern __shared__ uint4 pool_smem[];
   const int n = p.H * p.W;
@@ -60,13 +61,12 @@ __global__ void __launch_bounds__(256) sppf_kernel(const __grid_constant__ PoolP
   uint4* tmp = cur + n;
   uint4* nxt = tmp + n;
   const int chunk = blockIdx.x;
-  const long long img = blockIdx.y;
+  const int img = blockIdx.y;
   const int W2 = p.W + 2;
+  const int8_t* src = p.in.base + (long long)chunk * p.in.plane + (long long)img * p.in.P * 16;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int y = i / p.W, x = i - (i / p.W) * p.W;
-    cur[i] = *reinterpret_cast<const uint4*>(p.in.base + img * p.in.img_stride +
-                                             ((long long)(y + 1) * W2 + x + 1) * p.in.pitch + p.in.ch_off +
-                                             chunk * 16);
+    cur[i] = *reinterpret_cast<const uint4*>(src + ((y + 1) * W2 + x + 1) * 16);
   }
   __syncthreads();
   for (int k = 0; k < 3; ++k) {
@@ -78,15 +78,14 @@ __global__ void __launch_bounds__(256) sppf_kernel(const __grid_constant__ PoolP
       tmp[i] = m;
     }
     __syncthreads();
-    const SegDev& o = p.out[k];
+    int8_t* dst = const_cast<int8_t*>(p.out[k].base) + (long long)chunk * p.out[k].plane + (long long)img * p.out[k].P * 16;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       const int y = i / p.W, x = i - (i / p.W) * p.W;
       uint4 m = tmp[i];
       for (int d = -2; d <= 2; ++d)
         if (d != 0 && y + d >= 0 && y + d < p.H) m = vmax16(m, tmp[(y + d) * p.W + x]);
       nxt[i] = m;
-      *reinterpret_cast<uint4*>(const_cast<int8_t*>(o.base) + img * o.img_stride +
-                                ((long long)(y + 1) * W2 + x + 1) * o.pitch + o.ch_off + chunk * 16) = m;
+      *reinterpret_cast<uint4*>(dst + ((y + 1) * W2 + x + 1) * 16) = m;
     }
     __syncthreads();
     uint4* t = cur;

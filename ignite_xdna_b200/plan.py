@@ -4,10 +4,12 @@ HBM layout (one arena per GPU, sized for ``max_batch`` images):
 
 * image staging, uint8 [B][3][H][W], and the pixel -> int8 input table;
 * the stem input, int8 [B][H+2][W+2][4] (3 channels + 1 zero, zero halo ring);
-* activation buffers, int8 [B][h+2][w+2][pitch] with a one-pixel zero halo. Tensors read
-  together as one concat (a C2f's cv1/m outputs, SPPF's cv1 and pools, the PAN concats at
-  one resolution) share a buffer as consecutive channel ranges, so the concat is free and
-  every producer writes straight into its slice. Stored values are t = q - 128;
+* activation buffers: one plane per 16-channel chunk, int8 [B][h+2][w+2][16] with a one-pixel
+  zero halo per image and zero guard pixels before and after the plane (a window copy may
+  reach past the first and last image). Tensors read together as one concat (a C2f's cv1/m
+  outputs, SPPF's cv1 and pools, the PAN concats at one resolution) share a buffer as
+  consecutive chunk planes, so the concat is free and every producer writes whole planes of
+  its own. Stored values are t = q - 128;
 * the egress, int8 [B][egress bytes]: the six heads as NCHW, back to back in head order, the
   head convs write it directly (read_heads' int8 NCHW egress, graph_session.py:903-930);
 * constants: weights packed per (n-tile, K-block) in the UMMA core-matrix layout, int32
@@ -37,13 +39,20 @@ def _align(x: int, a: int = ALIGN) -> int:
 
 @dataclass
 class Store:
-    """Where one tensor lives: buffer offset, pitch, channel offset."""
+    """Where one tensor lives: chunk plane 0's padded pixel 0, plane stride, first chunk."""
     offset: int
-    pitch: int
-    ch_offset: int
+    plane_stride: int
+    chunk_offset: int
     channels: int
     height: int
     width: int
+    guard: int = 0
+
+
+def plane_guard(width: int) -> int:
+    """Zero pixels around a plane: a window copy reaches up to a 512-row tile plus one padded
+    row and pixel past the last image, and one padded row and pixel before the first."""
+    return 512 + 2 * (width + 3) + 64
 
 
 @dataclass
@@ -77,10 +86,6 @@ class DevicePlan:
     const_blob: np.ndarray
     c_plan: object = None
     keep: list = field(default_factory=list)
-
-    def tensor_bytes(self, name: str, batch: int) -> int:
-        s = self.stores[name]
-        return batch * (s.height + 2) * (s.width + 2) * s.pitch
 
 
 def input_lut_t(scale: float) -> np.ndarray:
@@ -220,20 +225,22 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
 
     images_offset = alloc(max_batch * 3 * H * W)
     input_lut_offset = alloc(256)
-    input_store = Store(alloc(max_batch * (H + 2) * (W + 2) * 4), 4, 0, 3, H, W)
+    input_store = Store(alloc(max_batch * (H + 2) * (W + 2) * 4), 0, 0, 3, H, W, 0)
     stores: Dict[str, Store] = {}
     for grp in _storage_groups(ir, heads):
         infos = [ir.tensors[t] for t in grp]
         for t in infos:
             if t.channels % 16:
                 raise ValueError(f"{t.name}: {t.channels} channels is not a multiple of 16")
-        pitch = sum(t.channels for t in infos)
         h, w = infos[0].height, infos[0].width
-        base = alloc(max_batch * (h + 2) * (w + 2) * pitch)
+        guard = plane_guard(w)
+        plane = _align((max_batch * (h + 2) * (w + 2) + 2 * guard) * 16)
+        nch = sum(t.channels for t in infos) // 16
+        base = alloc(nch * plane) + guard * 16
         ch = 0
         for t in infos:
-            stores[t.name] = Store(base, pitch, ch, t.channels, h, w)
-            ch += t.channels
+            stores[t.name] = Store(base, plane, ch, t.channels, h, w, guard)
+            ch += t.channels // 16
     head_offsets: Dict[str, int] = {}
     eb = 0
     for name in HEAD_NAMES:
@@ -275,14 +282,16 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
     def seg_of(s: Segment) -> L.Segment:
         if s.tensor == ir.input:
             st = input_store
-            return L.Segment(st.offset, 4, 0, 3, st.height, st.width, 0)
+            return L.Segment(st.offset, 0, 0, 3, st.height, st.width, 0, 0)
         st = stores[s.tensor]
-        return L.Segment(st.offset, st.pitch, st.ch_offset + s.block_offset * 8, s.blocks * 8, st.height,
-                         st.width, int(s.up2))
+        if s.block_offset % 2 or s.blocks % 2:
+            raise ValueError(f"{s.tensor}: channel view not aligned to 16-channel chunks")
+        return L.Segment(st.offset, st.plane_stride, st.chunk_offset + s.block_offset // 2, s.blocks * 8,
+                         st.height, st.width, int(s.up2), st.guard)
 
     def whole(name: str) -> L.Segment:
         st = stores[name]
-        return L.Segment(st.offset, st.pitch, st.ch_offset, st.channels, st.height, st.width, 0)
+        return L.Segment(st.offset, st.plane_stride, st.chunk_offset, st.channels, st.height, st.width, 0, st.guard)
 
     plan_convs = []
     index_of = {}
@@ -357,16 +366,17 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
 
 
 def _merge_segments(segs: List[L.Segment]) -> List[L.Segment]:
-    """Adjacent views of one buffer (same offset, consecutive channels) become one view."""
+    """Adjacent views of one buffer (same planes, consecutive chunks) become one view."""
     out: List[L.Segment] = []
     for s in segs:
         if out:
             p = out[-1]
-            if (p.offset == s.offset and p.pitch == s.pitch and not p.up2 and not s.up2
-                    and p.ch_offset + p.channels == s.ch_offset):
+            if (p.offset == s.offset and p.plane_stride == s.plane_stride and not p.up2 and not s.up2
+                    and p.chunk_offset + p.channels // 16 == s.chunk_offset):
                 p.channels += s.channels
                 continue
-        out.append(L.Segment(s.offset, s.pitch, s.ch_offset, s.channels, s.height, s.width, s.up2))
+        out.append(L.Segment(s.offset, s.plane_stride, s.chunk_offset, s.channels, s.height, s.width, s.up2,
+                             s.guard))
     return out
 
 
@@ -386,7 +396,7 @@ def c_plan(dp: DevicePlan) -> L.Plan:
     p.images_offset = dp.images_offset
     p.input_lut_offset = dp.input_lut_offset
     s = dp.input_store
-    p.input = L.Segment(s.offset, 4, 0, 3, s.height, s.width, 0)
+    p.input = L.Segment(s.offset, 0, 0, 3, s.height, s.width, 0, 0)
     p.egress_offset = dp.egress_offset
     p.egress_image_bytes = dp.egress_image_bytes
     p.arena_bytes = dp.arena_bytes

@@ -210,10 +210,14 @@ class GraphSession:
             v = raw.view(np.int8).reshape(b, st.height + 2, st.width + 2, 4)[:, 1:-1, 1:-1, :3]
             return (v.astype(np.int16) + 128).astype(np.uint8).transpose(0, 3, 1, 2)
         st = self.plan.stores[name]
-        n = b * (st.height + 2) * (st.width + 2) * st.pitch
-        raw = self.arena[st.offset:st.offset + n].cpu().numpy().view(np.int8)
-        v = raw.reshape(b, st.height + 2, st.width + 2, st.pitch)[:, 1:-1, 1:-1, st.ch_offset:st.ch_offset + st.channels]
-        return (v.astype(np.int16) + 128).astype(np.uint8).transpose(0, 3, 1, 2)
+        P = (st.height + 2) * (st.width + 2)
+        out = np.empty((b, st.channels, st.height, st.width), dtype=np.uint8)
+        for c in range(st.channels // 16):
+            o = st.offset + (st.chunk_offset + c) * st.plane_stride
+            raw = self.arena[o:o + b * P * 16].cpu().numpy().view(np.int8).reshape(b, st.height + 2, st.width + 2, 16)
+            v = raw[:, 1:-1, 1:-1, :].transpose(0, 3, 1, 2)
+            out[:, 16 * c:16 * c + 16] = (v.astype(np.int16) + 128).astype(np.uint8)
+        return out
 
     def profile(self, batch: int, iters: int = 3):
         """Mean device milliseconds per op (layer-by-layer launches with events)."""

@@ -44,10 +44,10 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 1
+#define IXB_API_VERSION 2
 
 /* Conv A-operand modes. */
-#define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one padded pixel window per K-block */
+#define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
 #define IXB_MODE_GATHER 1   /* stride 2 or an up2 input: per-pixel gather per tap */
 #define IXB_MODE_STEM 2     /* 3x3 stride-2 conv over the 4-byte-pixel image tensor */
 
@@ -57,16 +57,20 @@ extern "C" {
 #define IXB_ASYNC 4         /* return after enqueueing; ixb_session_wait completes the call */
 #define IXB_NO_GRAPH 8      /* launch layer by layer instead of replaying the captured graph */
 
-/* One stored activation tensor viewed as [batch][H+2][W+2][pitch] int8 (t = q - 128) with a
- * zero halo ring, or a channel range of it. */
+/* One stored activation tensor, or a channel range of it. Activations are int8 (t = q - 128)
+ * stored as one plane per 16-channel chunk: plane c holds [batch][H+2][W+2] pixels of 16 bytes
+ * (channels 16c .. 16c+15) with a zero one-pixel halo ring around every image and `guard` zero
+ * pixels before and after the plane. The image tensor the stem reads is a single plane of
+ * 4-byte pixels (3 channels + 1 zero) without guards. */
 typedef struct ixb_segment {
-  uint64_t offset;     /* arena byte offset of padded pixel (0,0) of image 0 */
-  int32_t pitch;       /* bytes per stored pixel; multiple of 16 (4 for the image tensor) */
-  int32_t ch_offset;   /* first channel of the view; multiple of 16 */
-  int32_t channels;    /* channels of the view; multiple of 16 (3 for the image tensor) */
-  int32_t height;      /* stored height (unpadded) */
-  int32_t width;       /* stored width (unpadded) */
-  int32_t up2;         /* 1: read as its nearest-2x upsampling */
+  uint64_t offset;       /* arena byte offset of padded pixel 0 of image 0 in the tensor's chunk plane 0 */
+  uint64_t plane_stride; /* bytes from one chunk plane to the next */
+  int32_t chunk_offset;  /* first chunk plane of the view */
+  int32_t channels;      /* channels of the view: multiple of 16 (3 for the image tensor) */
+  int32_t height;        /* stored height (unpadded) */
+  int32_t width;         /* stored width (unpadded) */
+  int32_t up2;           /* 1: read as its nearest-2x upsampling */
+  int32_t guard;         /* zero pixels before and after every plane */
 } ixb_segment;
 
 typedef struct ixb_conv_desc {
@@ -87,8 +91,8 @@ typedef struct ixb_conv_desc {
   int32_t has_residual;
   ixb_segment residual;
   int32_t res_lsh_main, res_lsh_res, res_shift;
-  int32_t out_nchw;    /* 0: write out (NHWC view); 1: write int8 NCHW into the egress */
-  ixb_segment out;     /* NHWC destination view (out_nchw == 0) */
+  int32_t out_nchw;    /* 0: write the out view; 1: write int8 NCHW into the egress */
+  ixb_segment out;     /* destination view (out_nchw == 0) */
   uint64_t egress_offset;       /* arena offset of this head inside image 0's egress */
   uint64_t egress_image_bytes;  /* egress bytes per image */
 } ixb_conv_desc;
@@ -112,7 +116,7 @@ typedef struct ixb_plan {
   const ixb_op* ops;
   uint64_t images_offset;       /* uint8 [max_batch][3][H][W] staging */
   uint64_t input_lut_offset;    /* int8[256]: pixel -> t */
-  ixb_segment input;            /* padded NHWC4 image tensor the stem reads */
+  ixb_segment input;            /* padded 4-byte-pixel image tensor the stem reads */
   uint64_t egress_offset;       /* int8 [max_batch][egress_image_bytes] */
   uint64_t egress_image_bytes;
   uint64_t arena_bytes;

@@ -34,9 +34,9 @@ def _operand(smem: np.ndarray, start: int, lbo: int, sbo: int, rows: int) -> np.
 
 
 def _seg_params(d, s, chunk_begin):
-    return dict(off=int(s.offset), pitch=int(s.pitch), ch_off=int(s.ch_offset), chunk_begin=chunk_begin,
-                chunks=(int(s.channels) + 15) // 16, H=int(s.height), W=int(s.width), up2=int(s.up2),
-                img=(int(s.height) + 2) * (int(s.width) + 2) * int(s.pitch))
+    return dict(base=int(s.offset) + int(s.chunk_offset) * int(s.plane_stride), plane=int(s.plane_stride),
+                chunk_begin=chunk_begin, chunks=(int(s.channels) + 15) // 16, H=int(s.height), W=int(s.width),
+                up2=int(s.up2), P=(int(s.height) + 2) * (int(s.width) + 2))
 
 
 def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
@@ -93,7 +93,7 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         img = m // (Ho * Wo)
                         rem = m - img * Ho * Wo
                         y, x = rem // Wo, rem % Wo
-                        src = s["off"] + img * s["img"] + ((2 * y + c) * (s["W"] + 2) + 2 * x) * s["pitch"]
+                        src = s["base"] + (img * s["P"] + (2 * y + c) * (s["W"] + 2) + 2 * x) * 4
                         for rr in np.nonzero(ok)[0]:
                             smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[src[rr]:src[rr] + 16]
                         continue
@@ -107,12 +107,12 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                     if not si:
                         continue
                     s = segs[si[-1]]
-                    cbase = s["off"] + s["ch_off"] + (gc - s["chunk_begin"]) * 16
+                    cbase = s["base"] + (gc - s["chunk_begin"]) * s["plane"]
                     if mode == L.MODE_WINDOW:
                         px = np.arange(rowsA)
                         m = m0 - win_origin + px
-                        ok = (m >= 0) & (m < m_total)
-                        src = cbase + m * s["pitch"]
+                        ok = np.ones_like(m, dtype=bool)      # one bulk copy; the plane guards are zero
+                        src = cbase + m * 16
                         rows = px
                     else:
                         r = np.arange(TM)
@@ -125,7 +125,7 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         iy, ix = y * stride + ky - pad, x * stride + kx - pad
                         if s["up2"]:
                             iy, ix = iy >> 1, ix >> 1
-                        src = cbase + img * s["img"] + ((iy + 1) * (s["W"] + 2) + ix + 1) * s["pitch"]
+                        src = cbase + (img * s["P"] + (iy + 1) * (s["W"] + 2) + ix + 1) * 16
                         rows = r
                     for rr, sa in zip(rows[ok], src[ok]):
                         smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[sa:sa + 16]
@@ -162,14 +162,17 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
             t2 = lut[t1 + 128]
             if d.has_residual:
                 r = d.residual
-                ra = (r.offset + opix[:, None] * r.pitch + r.ch_offset + co[None, :])
+                rb = r.offset + r.chunk_offset * r.plane_stride
+                ra = rb + (co[None, :] // 16) * r.plane_stride + opix[:, None] * 16 + (co[None, :] % 16)
                 rv = arena[np.where(valid[:, None], ra, 0)].view(np.int8).astype(np.int64)
                 t2 = np.clip(_rne((t2 << d.res_lsh_main) + (rv << d.res_lsh_res), d.res_shift), -128, 127)
             out = t2.astype(np.int8).view(np.uint8)
             for rr in np.nonzero(valid)[0]:
                 if not d.out_nchw:
-                    base = d.out.offset + opix[rr] * d.out.pitch + d.out.ch_offset + nt * n_tile
-                    arena[base:base + n_tile] = out[rr]
+                    ob = d.out.offset + d.out.chunk_offset * d.out.plane_stride
+                    for j in range(n_tile // 16):
+                        a0 = ob + (nt * n_tile // 16 + j) * d.out.plane_stride + opix[rr] * 16
+                        arena[a0:a0 + 16] = out[rr, 16 * j:16 * j + 16]
                 else:
                     plane = Ho * Wo
                     e = d.egress_offset + img[rr] * d.egress_image_bytes + oy[rr] * Wo + ox[rr]
@@ -179,23 +182,24 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
 def run_pool(arena: np.ndarray, pd, batch: int) -> None:
     s = pd.inp
     H, W, C = s.height, s.width, s.channels
-    img_b = (H + 2) * (W + 2) * s.pitch
-    for b in range(batch):
-        base = s.offset + b * img_b
-        v = arena[base:base + img_b].view(np.int8).reshape(H + 2, W + 2, s.pitch)
-        cur = v[1:-1, 1:-1, s.ch_offset:s.ch_offset + C].astype(np.int64)
-        for kk in range(3):
-            p = np.full((H + 4, W + 4, C), -128, dtype=np.int64)
-            p[2:-2, 2:-2] = cur
-            nxt = np.full((H, W, C), -128, dtype=np.int64)
-            for dy in range(5):
-                for dx in range(5):
-                    nxt = np.maximum(nxt, p[dy:dy + H, dx:dx + W])
-            o = pd.out[kk]
-            ob = o.offset + b * (o.height + 2) * (o.width + 2) * o.pitch
-            ov = arena[ob:ob + img_b].view(np.int8).reshape(H + 2, W + 2, o.pitch)
-            ov[1:-1, 1:-1, o.ch_offset:o.ch_offset + C] = nxt.astype(np.int8)
-            cur = nxt
+    P = (H + 2) * (W + 2)
+    for c in range(C // 16):
+        for b in range(batch):
+            base = s.offset + (s.chunk_offset + c) * s.plane_stride + b * P * 16
+            v = arena[base:base + P * 16].view(np.int8).reshape(H + 2, W + 2, 16)
+            cur = v[1:-1, 1:-1].astype(np.int64)
+            for kk in range(3):
+                p = np.full((H + 4, W + 4, 16), -128, dtype=np.int64)
+                p[2:-2, 2:-2] = cur
+                nxt = np.full((H, W, 16), -128, dtype=np.int64)
+                for dy in range(5):
+                    for dx in range(5):
+                        nxt = np.maximum(nxt, p[dy:dy + H, dx:dx + W])
+                o = pd.out[kk]
+                ob = o.offset + (o.chunk_offset + c) * o.plane_stride + b * P * 16
+                ov = arena[ob:ob + P * 16].view(np.int8).reshape(H + 2, W + 2, 16)
+                ov[1:-1, 1:-1] = nxt.astype(np.int8)
+                cur = nxt
 
 
 def run_network(dp: DevicePlan, images: np.ndarray) -> np.ndarray:

@@ -49,7 +49,9 @@ def test_valid_descriptor_passes_checks_until_launch():
     (lambda d, n: setattr(d.seg[0], "offset", n - 64), "arena"),
     (lambda d, n: setattr(d, "w_offset", n), "weights"),
     (lambda d, n: setattr(d, "shift", 17), "shift"),
-    (lambda d, n: setattr(d.seg[0], "ch_offset", 8), "misaligned"),
+    (lambda d, n: setattr(d.seg[0], "plane_stride", d.seg[0].plane_stride + 8), "misaligned"),
+    (lambda d, n: setattr(d.seg[0], "guard", 0), "guard"),
+    (lambda d, n: setattr(d.out, "chunk_offset", 10 ** 6), "arena"),
     (lambda d, n: setattr(d, "n_tile", 24), "n_tile"),
     (lambda d, n: setattr(d, "cin", d.cin + 16), "cin"),
 ])
@@ -67,4 +69,4 @@ def test_batch_beyond_plan_is_refused():
     dp, descs = _desc()
     lib = L.load()
     rc = lib.ixb_conv_layer(C.byref(descs[5]), C.c_void_p(0x10000), dp.arena_bytes, 100000, None)
-    assert rc == -1 and "arena" in lib.ixb_last_error().decode()
+    assert rc == -1 and any(w in lib.ixb_last_error().decode() for w in ("arena", "overlap", "pixel"))

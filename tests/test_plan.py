@@ -33,9 +33,11 @@ def test_plan_storage_is_disjoint_and_aligned(variant):
     dp = build_plan(ir, 64)
     spans = {}
     for name, st in dp.stores.items():
-        n = 64 * (st.height + 2) * (st.width + 2) * st.pitch
-        spans.setdefault(st.offset, n)
-        assert st.offset % 256 == 0 and st.pitch % 16 == 0 and st.ch_offset % 16 == 0
+        nch = sum(t.channels for n2, t in ir.tensors.items() if n2 in dp.stores and dp.stores[n2].offset == st.offset) // 16
+        start = st.offset - st.guard * 16
+        spans[start] = nch * st.plane_stride
+        assert st.offset % 16 == 0 and st.plane_stride % 256 == 0
+        assert st.plane_stride >= (64 * (st.height + 2) * (st.width + 2) + 2 * st.guard) * 16
     spans[dp.images_offset] = 64 * 3 * dp.img_h * dp.img_w
     spans[dp.input_store.offset] = 64 * (dp.img_h + 2) * (dp.img_w + 2) * 4
     spans[dp.egress_offset] = 64 * dp.egress_image_bytes
