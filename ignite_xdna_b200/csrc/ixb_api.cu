@@ -238,7 +238,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   p.b_block_bytes = b_block;
   const int b_total = p.kblocks * b_block;
-  const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * 512 * 8);  // barriers, table, bias, rows
+  const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * 512 * 16);  // barriers, table, bias, rows
   const int budget = kSmemLimit - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
@@ -258,7 +258,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   p.m_tiles = (int)((p.m_total + p.tile_rows - 1) / p.tile_rows);
   p.tbl_off = p.a_off + p.stages * p.stage_bytes;
-  p.bar_off = p.tbl_off + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * p.tile_rows * 8);
+  p.bar_off = p.tbl_off + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * p.tile_rows * 16);
   p.lut_off = p.bar_off + 512;
   p.bias_off = p.lut_off + 256;
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
@@ -267,6 +267,10 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
   p.lut = reinterpret_cast<const int8_t*>(arena + d.lut_offset);
   p.shift = d.shift;
+  p.fd_P = make_fastdiv((uint32_t)((d.in_h + 2) * (d.in_w + 2)));
+  p.fd_W2 = make_fastdiv((uint32_t)(d.in_w + 2));
+  p.fd_hw = make_fastdiv((uint32_t)(d.out_h * d.out_w));
+  p.fd_Wo = make_fastdiv((uint32_t)d.out_w);
   p.acc_cols = p.mt * d.n_tile;
   int cols = 32;
   while (cols < 2 * p.acc_cols) cols *= 2;

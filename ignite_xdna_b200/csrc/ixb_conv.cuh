@@ -81,6 +81,7 @@ struct ConvParams {
   int8_t* egress;
   long long egress_img;
   int cout;
+  FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wo, Wo
 };
 
 constexpr int kEpiWarps = 8;
@@ -148,22 +149,34 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
   const int step = kProducerThreads / nch;
   const int S = p.stages;
   const int hw = p.Ho * p.Wo;
-  int2* tbl = reinterpret_cast<int2*>(smem + p.tbl_off);
+  // Per tile, one row table entry per output pixel: {pixel of tap (0, 0) in the first view's
+  // padded geometry, image, y, x}; pixel -1 marks rows past the batch.
+  int4* tbl = reinterpret_cast<int4*>(smem + p.tbl_off);
+  const SegDev& s0 = p.seg[0];
+  const int W2_0 = s0.W + 2;
   int stage = 0;
   uint32_t ph = 0;
   int it = 0;
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x, ++it) {
     const int m0 = t * p.tile_rows;
-    int2* T = tbl + (it & 1) * p.tile_rows;
+    int4* T = tbl + (it & 1) * p.tile_rows;
     for (int r = ptid; r < p.tile_rows; r += kProducerThreads) {
       const int m = m0 + r;
       if (m < p.m_total) {
-        const int img = m / hw;
+        const int img = (int)fdiv((uint32_t)m, p.fd_hw);
         const int rem = m - img * hw;
-        const int y = rem / p.Wo;
-        T[r] = make_int2(img, (y << 16) | (rem - y * p.Wo));
+        const int y = (int)fdiv((uint32_t)rem, p.fd_Wo);
+        const int x = rem - y * p.Wo;
+        int base;
+        if (MODE == IXB_MODE_STEM)
+          base = img * s0.P + 2 * y * W2_0 + 2 * x;   // padded row 2y + ky, padded column 2x
+        else if (s0.up2)
+          base = img * s0.P + ((y >> 1) + 1) * W2_0 + (x >> 1) + 1;
+        else
+          base = img * s0.P + (y * p.stride - p.pad + 1) * W2_0 + (x * p.stride - p.pad + 1);
+        T[r] = make_int4(base, img, y, x);
       } else {
-        T[r] = make_int2(-1, 0);
+        T[r] = make_int4(-1, 0, 0, 0);
       }
     }
     producer_bar_sync();
@@ -171,18 +184,16 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
       mbar_wait(&empty[stage], ph ^ 1);
       uint8_t* dst = smem + p.a_off + stage * p.stage_bytes + c * p.rowsA * 16;
       if (MODE == IXB_MODE_STEM) {
-        const SegDev& s = p.seg[0];
         if (c < 3) {
+          const int8_t* cb = s0.base + (long long)c * W2_0 * 4;
           for (int r = ptid / nch; r < p.tile_rows; r += step) {
-            const int2 e = T[r];
-            if (e.x >= 0) {
-              const int y = e.y >> 16, x = e.y & 0xFFFF;
-              // padded row 2y + ky, padded columns 2x .. 2x+3 (input columns 2x-1 .. 2x+2)
-              const int8_t* src = s.base + ((long long)e.x * s.P + (2 * y + c) * (s.W + 2) + 2 * x) * 4;
+            const int pb = T[r].x;
+            if (pb >= 0) {
+              const int8_t* src = cb + (long long)pb * 4;
               cp_async8(dst + r * 16, src, 8u);
               cp_async8(dst + r * 16 + 8, src + 8, 8u);
             } else {
-              cp_async16(dst + r * 16, s.base, 0u);
+              cp_async16(dst + r * 16, s0.base, 0u);
             }
           }
         }
@@ -194,17 +205,26 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
         if (si >= 0) {
           const SegDev& s = p.seg[si];
           const int8_t* cbase = s.base + (long long)(gc - s.chunk_begin) * s.plane;
-          for (int r = ptid / nch; r < p.tile_rows; r += step) {
-            const int2 e = T[r];
-            if (e.x >= 0) {
-              int iy = (e.y >> 16) * p.stride + ky - p.pad, ix = (e.y & 0xFFFF) * p.stride + kx - p.pad;
-              if (s.up2) {
-                iy >>= 1;
-                ix >>= 1;
+          if (si == 0 || (s.up2 == s0.up2 && s.W == s0.W && s.P == s0.P)) {
+            // same geometry as the first view: the table's pixel base plus the tap offset
+            const int8_t* tb = cbase + (long long)(ky * (s.W + 2) + kx) * 16;
+            for (int r = ptid / nch; r < p.tile_rows; r += step) {
+              const int pb = T[r].x;
+              cp_async16(dst + r * 16, pb >= 0 ? tb + (long long)pb * 16 : s.base, pb >= 0 ? 16u : 0u);
+            }
+          } else {
+            for (int r = ptid / nch; r < p.tile_rows; r += step) {
+              const int4 e = T[r];
+              if (e.x >= 0) {
+                int iy = e.z * p.stride + ky - p.pad, ix = e.w * p.stride + kx - p.pad;
+                if (s.up2) {
+                  iy >>= 1;
+                  ix >>= 1;
+                }
+                cp_async16(dst + r * 16, cbase + ((long long)e.y * s.P + (iy + 1) * (s.W + 2) + (ix + 1)) * 16, 16u);
+              } else {
+                cp_async16(dst + r * 16, s.base, 0u);
               }
-              cp_async16(dst + r * 16, cbase + ((long long)e.x * s.P + (iy + 1) * (s.W + 2) + (ix + 1)) * 16, 16u);
-            } else {
-              cp_async16(dst + r * 16, s.base, 0u);
             }
           }
         }
@@ -224,67 +244,96 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
 }
 
 // ---------------------------------------------------------------- epilogue
+// 16 accumulators of one row -> 16 int8 outputs: bias, RNE shift, int8 clamp, table, residual.
+template <bool RES>
+__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const int4* bias4, const int8_t* lut_s, int s,
+                                            int hs, int lsb, const ConvParams& p, int rs, int rhs, int rlsb,
+                                            uint4 r4) {
+  alignas(16) int8_t ov[16];
+  const int8_t* rv = reinterpret_cast<const int8_t*>(&r4);
+#pragma unroll
+  for (int q4 = 0; q4 < 4; ++q4) {
+    const int4 b4 = bias4[q4];
+    const int bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * q4 + e;
+      const int a = (int)v[i] + bb[e];
+      const int r1 = (a + hs + ((a >> s) & lsb)) >> s;   // round half to even, exact for s in [0, 16]
+      int t = lut_s[clamp_i8(r1) + 128];
+      if (RES) {
+        const int y = (t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
+        t = clamp_i8((y + rhs + ((y >> rs) & rlsb)) >> rs);
+      }
+      ov[i] = (int8_t)t;
+    }
+  }
+  return *reinterpret_cast<const uint4*>(ov);
+}
+
 template <int MODE>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
-                                                   int lane, const int8_t* lut_s, const int* bias_s) {
+                                                   int lane, const int8_t* lut_s, const int4* bias4_s) {
   const int q = warp & 3, g = warp >> 2;
   const int nj = p.n_tile / 16;
-  const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0;
-  const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0;
+  const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
+  const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
+  // the two warpgroups split 16-column chunks when there are several, else the 128-row blocks
+  const bool split_cols = nj >= 2;
   for (int b = 0; b < p.mt; ++b) {
+    if (!split_cols && (b & 1) != g) continue;
     const int m = m0 + b * kBlockM + q * 32 + lane;
     bool valid = m < p.m_total;
     int opix, img, oy, ox;
     if (MODE == IXB_MODE_WINDOW) {
-      const int P = (p.H + 2) * (p.W + 2);
-      img = m / P;
-      const int rem = m - img * P;
-      const int yp = rem / (p.W + 2), xp = rem - (rem / (p.W + 2)) * (p.W + 2);
+      img = (int)fdiv((uint32_t)m, p.fd_P);
+      const int rem = m - img * (int)p.fd_P.d;
+      const int yp = (int)fdiv((uint32_t)rem, p.fd_W2), xp = rem - yp * (p.W + 2);
       valid = valid && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
       opix = m;
       oy = yp - 1;
       ox = xp - 1;
     } else {
-      const int hw = p.Ho * p.Wo;
-      img = m / hw;
-      const int rem = m - img * hw;
-      oy = rem / p.Wo;
+      img = (int)fdiv((uint32_t)m, p.fd_hw);
+      const int rem = m - img * (int)p.fd_hw.d;
+      oy = (int)fdiv((uint32_t)rem, p.fd_Wo);
       ox = rem - oy * p.Wo;
       opix = img * (p.Ho + 2) * (p.Wo + 2) + (oy + 1) * (p.Wo + 2) + (ox + 1);
     }
     const uint32_t tl = tacc + b * p.n_tile + ((uint32_t)(q * 32) << 16);
-    for (int j = 0; j < nj; ++j) {
-      if (((b * nj + j) & 1) != g) continue;  // the two warpgroups take alternate pieces
-      uint32_t v[16];
+    const int j0 = split_cols ? g : 0, dj = split_cols ? 2 : 1;
+    for (int j = j0; j < nj; j += 2 * dj) {
+      // two 16-column loads per wait
+      const int j2 = j + dj;
+      uint32_t v[16], w[16];
       tmem_ld16(tl + j * 16, v);
+      if (j2 < nj) tmem_ld16(tl + j2 * 16, w);
       tmem_ld_wait();
       if (!valid) continue;
-      const int cl = j * 16;                   // channel within the n-tile
-      const int oc = ntile * nj + j;           // output chunk
-      int8_t rv[16];
-      if (p.has_res)
-        *reinterpret_cast<uint4*>(rv) =
-            *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)opix * 16);
-      alignas(16) int8_t ov[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int a = (int)v[i] + bias_s[cl + i];
-        const int r1 = s > 0 ? rne_pos(a, s, hs) : a;
-        int t = lut_s[clamp_i8(r1) + 128];
+#pragma unroll 1
+      for (int u = 0; u < 2; ++u) {
+        const int jj = u ? j2 : j;
+        if (jj >= nj) break;
+        const int oc = ntile * nj + jj;  // output chunk
+        uint4 r4 = make_uint4(0, 0, 0, 0);
+        uint4 o;
         if (p.has_res) {
-          const int y = (t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
-          t = clamp_i8(rs > 0 ? rne_pos(y, rs, rhs) : y);
+          r4 = *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)opix * 16);
+          o = epilogue16<true>(u ? w : v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
+        } else {
+          o = epilogue16<false>(u ? w : v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
         }
-        ov[i] = (int8_t)t;
-      }
-      if (!p.out_nchw) {
-        *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane +
-                                  (long long)opix * 16) = *reinterpret_cast<const uint4*>(ov);
-      } else {
-        int8_t* e = p.egress + (long long)img * p.egress_img + oy * p.Wo + ox;
-        const long long plane = (long long)p.Ho * p.Wo;
+        if (!p.out_nchw) {
+          *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane +
+                                    (long long)opix * 16) = o;
+        } else {
+          int8_t* e = p.egress + (long long)img * p.egress_img + oy * p.Wo + ox;
+          const long long plane = (long long)p.Ho * p.Wo;
+          const int8_t* ob = reinterpret_cast<const int8_t*>(&o);
+          const int c0 = ntile * p.n_tile + jj * 16;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) e[(ntile * p.n_tile + cl + i) * plane] = ov[i];
+          for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
+        }
       }
     }
   }
@@ -304,6 +353,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
   int8_t* lut_s = reinterpret_cast<int8_t*>(smem + p.lut_off);
   int* bias_s = reinterpret_cast<int*>(smem + p.bias_off);
+  const int4* bias4_s = reinterpret_cast<const int4*>(smem + p.bias_off);
   const int ntile = blockIdx.y;
   const int KB = p.kblocks;
 
@@ -393,7 +443,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
     for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
       mbar_wait(&acc_full[acc], aph);
       tc_fence_after();
-      conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias_s);
+      conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       acc ^= 1;

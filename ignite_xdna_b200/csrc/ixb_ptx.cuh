@@ -16,9 +16,12 @@ namespace ixb {
 // Error bits of the device flag.
 enum : unsigned { DEV_ERR_WAIT_TIMEOUT = 1u, DEV_ERR_BAD_ARGS = 2u };
 
-// Polls before a bounded wait gives up: each try_wait itself suspends for a bounded time,
-// so this is seconds, far above any legitimate wait in these kernels.
-constexpr uint32_t kWaitLimit = 1u << 22;
+// A bounded wait gives up after this many nanoseconds of %globaltimer: seconds, far above any
+// legitimate wait in these kernels.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Suspend hint (ns) for mbarrier.try_wait: a waiting warp sleeps instead of spinning on issue
+// slots the working warps need; the phase completing wakes it.
+constexpr uint32_t kSuspendHintNs = 20000;
 
 // The library is one translation unit (ixb_api.cu includes every kernel header), so the
 // flag is defined here; the host reads and clears it with cudaMemcpyFromSymbol.
@@ -48,17 +51,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 // Bounded wait: returns false (and raises the device flag) if the phase never completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
+  }
   set_dev_error(DEV_ERR_WAIT_TIMEOUT);
   return false;
 }
@@ -160,6 +172,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- integer helpers
+// n / d for 0 <= n < 2^31 by a multiply: m = floor(2^32 (2^s - d) / d) + 1, s = ceil(log2 d),
+// q = (umulhi(n, m) + n) >> s (division by invariant integers, Granlund & Montgomery 1994).
+struct FastDiv {
+  uint32_t d, m, s;
+};
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  const uint32_t m = (uint32_t)((((1ull << 32) * ((1ull << s) - d)) / d) + 1);
+  return FastDiv{d, m, s};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) { return (__umulhi(n, f.m) + n) >> f.s; }
 
 // ---------------------------------------------------------------- integer epilogue
 // Arithmetic shift right by s (0..30) rounding half to even; s <= 0 shifts left.

@@ -55,3 +55,19 @@ def test_k_order_covers_every_tap_and_pair_once():
             blocks = conv_kblocks(mode, k, cin, cp)
             seen = [x for b in blocks for x in b if x[1] < (cin + 31) // 32]
             assert sorted(seen) == sorted({(t, p) for t in range(k * k) for p in range((cin + 31) // 32)})
+
+
+def test_fast_division_formula_is_exact():
+    """The kernels divide pixel indices (< 2^31) by invariant divisors with
+    q = (umulhi(n, m) + n) >> s, m = floor(2^32 (2^s - d) / d) + 1, s = ceil(log2 d)."""
+    rng = np.random.default_rng(0)
+    divisors = list(range(1, 2000)) + [162 * 162, 322 * 322, 642 * 642, 6400, 25600, 102400, 1 << 20, 12345679]
+    for d in divisors:
+        s = int(np.ceil(np.log2(d))) if d > 1 else 0
+        while (1 << s) < d:
+            s += 1
+        m = ((1 << 32) * ((1 << s) - d)) // d + 1
+        n = np.concatenate([rng.integers(0, 2 ** 31, 4000, dtype=np.int64), np.arange(0, 3 * d + 5),
+                            np.array([2 ** 31 - 1, 2 ** 31 - 2, d * (2 ** 31 // d) - 1])]).astype(np.uint64)
+        q = (((n * np.uint64(m)) >> np.uint64(32)) + n) >> np.uint64(s)
+        assert np.array_equal(q, n // np.uint64(d)), d
