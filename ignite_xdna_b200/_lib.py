@@ -80,6 +80,8 @@ _SIGS = {
     "ixb_session_launches": (C.c_int, [C.c_void_p, C.c_int]),
     "ixb_session_profile": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]),
     "ixb_conv_layer": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
+    "ixb_conv_layer_stats": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p,
+                                       C.c_void_p, C.c_int64]),
     "ixb_conv_launch_info": (C.c_int, [C.POINTER(ConvDesc), C.c_uint64, C.c_int, C.POINTER(C.c_int32), C.c_int]),
     "ixb_pool_layer": (C.c_int, [C.POINTER(PoolDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
     "ixb_quantize_images": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),

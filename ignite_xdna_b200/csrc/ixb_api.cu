@@ -715,6 +715,17 @@ int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, in
   return launch_conv(L, static_cast<cudaStream_t>(stream));
 }
 
+int ixb_conv_layer_stats(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream,
+                         uint64_t* stats, int64_t stats_words) {
+  if (!d || !arena || !stats) return fail(IXB_ERR_INVALID, "null argument");
+  ConvLaunch L;
+  std::string err;
+  if (build_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
+  if ((int64_t)L.grid.x * L.grid.y * kStatWords > stats_words) return fail(IXB_ERR_INVALID, "stats buffer too small");
+  L.p.stats = reinterpret_cast<unsigned long long*>(stats);
+  return launch_conv(L, static_cast<cudaStream_t>(stream));
+}
+
 int ixb_conv_launch_info(const ixb_conv_desc* d, uint64_t arena_bytes, int batch, int32_t* info, int n) {
   if (!d || !info) return fail(IXB_ERR_INVALID, "null argument");
   ConvLaunch L;

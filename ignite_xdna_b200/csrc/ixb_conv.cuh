@@ -82,6 +82,21 @@ struct ConvParams {
   long long egress_img;
   int cout;
   FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wo, Wo
+  unsigned long long* stats;          // optional per-CTA role counters (kStatWords per CTA), or null
+};
+
+// Per-CTA role counters (clock64 cycles) written when ConvParams::stats is set.
+enum : int {
+  kStatEpiWait = 0,   // epilogue warp 0 waiting for an accumulator
+  kStatEpiWork,       // epilogue warp 0 draining accumulators
+  kStatMmaWaitFull,   // MMA thread waiting for loaded stages
+  kStatMmaWaitAcc,    // MMA thread waiting for a free accumulator
+  kStatMmaIssue,      // MMA thread issuing
+  kStatProdWait,      // producer 0 waiting for free stages
+  kStatProdWork,      // producer 0 issuing loads
+  kStatTotal,         // CTA lifetime
+  kStatTiles,
+  kStatWords = 16
 };
 
 constexpr int kEpiWarps = 8;
@@ -116,10 +131,14 @@ __device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* sme
   const uint32_t chunk_bytes = (uint32_t)p.rowsA * 16;
   int stage = 0;
   uint32_t ph = 0;
+  long long tw = 0, tk = 0;
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
     const long long wb = (long long)t * p.tile_rows - p.win_origin;
     for (int kb = 0; kb < p.kblocks; ++kb) {
+      const long long c0 = clock64();
       mbar_wait(&empty[stage], ph ^ 1);
+      const long long c1 = clock64();
+      tw += c1 - c0;
       uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
       const int valid = min(nch, p.cin_chunks - kb * nch);
       uint32_t bytes = (uint32_t)valid * chunk_bytes + (p.b_resident ? 0u : (uint32_t)p.b_block_bytes);
@@ -133,11 +152,17 @@ __device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* sme
       if (!p.b_resident)
         bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
                  p.b_block_bytes, &full[stage]);
+      tk += clock64() - c1;
       if (++stage == S) {
         stage = 0;
         ph ^= 1;
       }
     }
+  }
+  if (p.stats) {
+    unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
+    st[kStatProdWait] = tw;
+    st[kStatProdWork] = tk;
   }
 }
 
@@ -152,6 +177,8 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
   // Per tile, one row table entry per output pixel: {pixel of tap (0, 0) in the first view's
   // padded geometry, image, y, x}; pixel -1 marks rows past the batch.
   int4* tbl = reinterpret_cast<int4*>(smem + p.tbl_off);
+  long long tw = 0;
+  const long long cstart = clock64();
   const SegDev& s0 = p.seg[0];
   const int W2_0 = s0.W + 2;
   int stage = 0;
@@ -181,7 +208,10 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
     }
     producer_bar_sync();
     for (int kb = 0; kb < p.kblocks; ++kb) {
+      const long long c0 = clock64();
       mbar_wait(&empty[stage], ph ^ 1);
+      const long long c1 = clock64();
+      tw += c1 - c0;
       uint8_t* dst = smem + p.a_off + stage * p.stage_bytes + c * p.rowsA * 16;
       if (MODE == IXB_MODE_STEM) {
         if (c < 3) {
@@ -240,6 +270,11 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
         ph ^= 1;
       }
     }
+  }
+  if (p.stats && ptid == 0) {
+    unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
+    st[kStatProdWait] = tw;
+    st[kStatProdWork] = clock64() - cstart - tw;
   }
 }
 
@@ -356,6 +391,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
   const int4* bias4_s = reinterpret_cast<const int4*>(smem + p.bias_off);
   const int ntile = blockIdx.y;
   const int KB = p.kblocks;
+  const long long t_start = clock64();
 
   if (warp == 0) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -403,12 +439,19 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
       const uint32_t lbo_a = p.rowsA * 16;
       int stage = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
+      long long wf = 0, wa = 0, wi = 0;
       for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+        long long c0 = clock64();
         mbar_wait(&acc_empty[acc], aph ^ 1);
+        long long c1 = clock64();
+        wa += c1 - c0;
         tc_fence_after();
         const uint32_t d0 = tmem + acc * p.acc_cols;
         for (int kb = 0; kb < KB; ++kb) {
+          c0 = clock64();
           mbar_wait(&full[stage], ph);
+          c1 = clock64();
+          wf += c1 - c0;
           if (MODE != IXB_MODE_WINDOW) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
           tc_fence_after();
           const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes);
@@ -426,6 +469,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
             }
           }
           umma_commit(&empty[stage]);
+          wi += clock64() - c1;
           if (++stage == S) {
             stage = 0;
             ph ^= 1;
@@ -435,25 +479,45 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
         acc ^= 1;
         if (acc == 0) aph ^= 1;
       }
+      if (p.stats) {
+        unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
+        st[kStatMmaWaitFull] = wf;
+        st[kStatMmaWaitAcc] = wa;
+        st[kStatMmaIssue] = wi;
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 0-7)
     int acc = 0;
     uint32_t aph = 0;
+    long long ew = 0, ek = 0;
+    int tiles = 0;
     for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+      const long long c0 = clock64();
       mbar_wait(&acc_full[acc], aph);
+      const long long c1 = clock64();
+      ew += c1 - c0;
       tc_fence_after();
       conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
+      ek += clock64() - c1;
+      ++tiles;
       acc ^= 1;
       if (acc == 0) aph ^= 1;
+    }
+    if (p.stats && tid == 0) {
+      unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
+      st[kStatEpiWait] = ew;
+      st[kStatEpiWork] = ek;
+      st[kStatTiles] = tiles;
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, p.tmem_cols);
+  if (p.stats && tid == 0) p.stats[(blockIdx.y * gridDim.x + blockIdx.x) * kStatWords + kStatTotal] = clock64() - t_start;
 }
 
 }  // namespace ixb

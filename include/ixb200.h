@@ -150,6 +150,11 @@ int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms);
 /* One layer on caller-owned device memory: arena is the base every offset refers to. */
 int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);
 int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);
+/* ixb_conv_layer with per-CTA role counters: stats (device memory, stats_words uint64) receives
+ * 16 words per CTA (grid.x * grid.y CTAs, see ixb_conv_launch_info): clock64 cycles the epilogue,
+ * MMA and producer roles spent waiting and working, the CTA lifetime and its tile count. */
+int ixb_conv_layer_stats(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream,
+                         uint64_t* stats, int64_t stats_words);
 /* The launch a conv descriptor gets for `batch` images (host-side decision, no GPU needed):
  * info = {blocks of 128 pixels per tile, tile rows, tiles, pipeline stages, weights resident,
  *         grid.x, grid.y, shared bytes, TMEM columns, K-blocks, A rows per stage, pairs per K-block}. */
