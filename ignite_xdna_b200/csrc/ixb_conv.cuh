@@ -306,6 +306,60 @@ __device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const int4*
   return *reinterpret_cast<const uint4*>(ov);
 }
 
+struct RowInfo {
+  int opix, img, oy, ox;
+  bool valid;
+};
+
+template <int MODE>
+__device__ __forceinline__ RowInfo decode_row(const ConvParams& p, int m) {
+  RowInfo r;
+  r.valid = m < p.m_total;
+  if (MODE == IXB_MODE_WINDOW) {
+    r.img = (int)fdiv((uint32_t)m, p.fd_P);
+    const int rem = m - r.img * (int)p.fd_P.d;
+    const int yp = (int)fdiv((uint32_t)rem, p.fd_W2), xp = rem - yp * (p.W + 2);
+    r.valid = r.valid && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
+    r.opix = m;
+    r.oy = yp - 1;
+    r.ox = xp - 1;
+  } else {
+    r.img = (int)fdiv((uint32_t)m, p.fd_hw);
+    const int rem = m - r.img * (int)p.fd_hw.d;
+    r.oy = (int)fdiv((uint32_t)rem, p.fd_Wo);
+    r.ox = rem - r.oy * p.Wo;
+    r.opix = r.img * (p.Ho + 2) * (p.Wo + 2) + (r.oy + 1) * (p.Wo + 2) + (r.ox + 1);
+  }
+  return r;
+}
+
+__device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
+                                            const int4* bias4_s, const int8_t* lut_s, int s, int hs, int lsb, int rs,
+                                            int rhs, int rlsb) {
+  const int nj = p.n_tile / 16;
+  const int oc = ntile * nj + jj;  // output chunk
+  uint4 o;
+  if (p.has_res) {
+    const uint4 r4 = *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)r.opix * 16);
+    o = epilogue16<true>(v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
+  } else {
+    o = epilogue16<false>(v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
+  }
+  if (!p.out_nchw) {
+    *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
+  } else {
+    int8_t* e = p.egress + (long long)r.img * p.egress_img + r.oy * p.Wo + r.ox;
+    const long long plane = (long long)p.Ho * p.Wo;
+    const int8_t* ob = reinterpret_cast<const int8_t*>(&o);
+    const int c0 = ntile * p.n_tile + jj * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
+  }
+}
+
+// Drain one accumulator: warp w reads TMEM lane quarter w % 4; the two warpgroups take
+// alternate 16-column chunks when there are several, else alternate 128-row blocks. A thread
+// issues the TMEM loads of two pieces before one wait so their latencies overlap.
 template <int MODE>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const int8_t* lut_s, const int4* bias4_s) {
@@ -313,64 +367,30 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
   const int nj = p.n_tile / 16;
   const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
-  // the two warpgroups split 16-column chunks when there are several, else the 128-row blocks
-  const bool split_cols = nj >= 2;
-  for (int b = 0; b < p.mt; ++b) {
-    if (!split_cols && (b & 1) != g) continue;
-    const int m = m0 + b * kBlockM + q * 32 + lane;
-    bool valid = m < p.m_total;
-    int opix, img, oy, ox;
-    if (MODE == IXB_MODE_WINDOW) {
-      img = (int)fdiv((uint32_t)m, p.fd_P);
-      const int rem = m - img * (int)p.fd_P.d;
-      const int yp = (int)fdiv((uint32_t)rem, p.fd_W2), xp = rem - yp * (p.W + 2);
-      valid = valid && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
-      opix = m;
-      oy = yp - 1;
-      ox = xp - 1;
-    } else {
-      img = (int)fdiv((uint32_t)m, p.fd_hw);
-      const int rem = m - img * (int)p.fd_hw.d;
-      oy = (int)fdiv((uint32_t)rem, p.fd_Wo);
-      ox = rem - oy * p.Wo;
-      opix = img * (p.Ho + 2) * (p.Wo + 2) + (oy + 1) * (p.Wo + 2) + (ox + 1);
+  const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
+  // this thread's pieces in order: (block, chunk)
+  const int nb = p.mt;
+  const int npieces = nb * nj;
+  int k = g;  // piece index; pieces alternate between the warpgroups
+  while (k < npieces) {
+    const int k2 = k + 2;
+    const int b1 = (nj >= 2) ? k / nj : k, j1 = (nj >= 2) ? k % nj : 0;
+    uint32_t v[16], w[16];
+    tmem_ld16(lane_base + b1 * p.n_tile + j1 * 16, v);
+    const bool two = k2 < npieces;
+    int b2 = 0, j2 = 0;
+    if (two) {
+      b2 = (nj >= 2) ? k2 / nj : k2;
+      j2 = (nj >= 2) ? k2 % nj : 0;
+      tmem_ld16(lane_base + b2 * p.n_tile + j2 * 16, w);
     }
-    const uint32_t tl = tacc + b * p.n_tile + ((uint32_t)(q * 32) << 16);
-    const int j0 = split_cols ? g : 0, dj = split_cols ? 2 : 1;
-    for (int j = j0; j < nj; j += 2 * dj) {
-      // two 16-column loads per wait
-      const int j2 = j + dj;
-      uint32_t v[16], w[16];
-      tmem_ld16(tl + j * 16, v);
-      if (j2 < nj) tmem_ld16(tl + j2 * 16, w);
-      tmem_ld_wait();
-      if (!valid) continue;
-#pragma unroll 1
-      for (int u = 0; u < 2; ++u) {
-        const int jj = u ? j2 : j;
-        if (jj >= nj) break;
-        const int oc = ntile * nj + jj;  // output chunk
-        uint4 r4 = make_uint4(0, 0, 0, 0);
-        uint4 o;
-        if (p.has_res) {
-          r4 = *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)opix * 16);
-          o = epilogue16<true>(u ? w : v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
-        } else {
-          o = epilogue16<false>(u ? w : v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
-        }
-        if (!p.out_nchw) {
-          *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane +
-                                    (long long)opix * 16) = o;
-        } else {
-          int8_t* e = p.egress + (long long)img * p.egress_img + oy * p.Wo + ox;
-          const long long plane = (long long)p.Ho * p.Wo;
-          const int8_t* ob = reinterpret_cast<const int8_t*>(&o);
-          const int c0 = ntile * p.n_tile + jj * 16;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
-        }
-      }
-    }
+    const RowInfo r1 = decode_row<MODE>(p, m0 + b1 * kBlockM + q * 32 + lane);
+    RowInfo r2 = r1;
+    if (two && b2 != b1) r2 = decode_row<MODE>(p, m0 + b2 * kBlockM + q * 32 + lane);
+    tmem_ld_wait();
+    if (r1.valid) store_piece(p, r1, ntile, j1, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    if (two && r2.valid) store_piece(p, r2, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    k += 4;
   }
 }
 
@@ -454,17 +474,26 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
           wf += c1 - c0;
           if (MODE != IXB_MODE_WINDOW) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
           tc_fence_after();
+          // Descriptors are built once per stage; stepping the operand start is adding
+          // (byte offset >> 4) to the low 14-bit address field, which cannot carry (smem < 256 KB).
           const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes);
           const uint32_t b0 = p.b_resident ? smem_u32(smem) + kb * p.b_block_bytes : a0 + p.a_stage_bytes;
+          const uint64_t adesc0 = umma_desc(a0, lbo_a, 128);
+          const uint64_t bdesc0 = umma_desc(b0, 128, 256);
+          const uint32_t b_step = (uint32_t)(p.n_tile * 32) >> 4;
           for (int pp = 0; pp < p.cp; ++pp) {
+            const uint64_t adesc_p = adesc0 + ((pp * 2 * lbo_a) >> 4);
             for (int tap = 0; tap < p.taps_per_block; ++tap) {
               uint32_t shift_px = 0;
               if (MODE == IXB_MODE_WINDOW) shift_px = (tap / p.k) * (p.W + 2) + (tap - (tap / p.k) * p.k);
-              const uint64_t bd = umma_desc(b0 + (pp * p.taps_per_block + tap) * p.n_tile * 32, 128, 256);
+              const uint64_t bd = bdesc0 + (uint64_t)((pp * p.taps_per_block + tap) * b_step);
               const uint32_t accum = (kb > 0 || pp > 0 || tap > 0) ? 1u : 0u;
+              uint64_t ad = adesc_p + shift_px;   // 16 bytes per pixel of shift
+              uint32_t dt = d0;
               for (int b = 0; b < p.mt; ++b) {
-                const uint64_t ad = umma_desc(a0 + pp * 2 * lbo_a + (b * kBlockM + shift_px) * 16, lbo_a, 128);
-                umma_s8(d0 + b * p.n_tile, ad, bd, p.idesc, accum);
+                umma_s8(dt, ad, bd, p.idesc, accum);
+                ad += (kBlockM * 16) >> 4;
+                dt += p.n_tile;
               }
             }
           }
