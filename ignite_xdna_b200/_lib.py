@@ -82,6 +82,8 @@ _SIGS = {
     "ixb_conv_layer": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
     "ixb_conv_layer_stats": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p,
                                        C.c_void_p, C.c_int64]),
+    "ixb_conv_schedule": (C.c_int, [C.POINTER(ConvDesc), C.POINTER(C.c_int32), C.c_int, C.POINTER(C.c_int32),
+                                    C.c_int]),
     "ixb_conv_launch_info": (C.c_int, [C.POINTER(ConvDesc), C.c_uint64, C.c_int, C.POINTER(C.c_int32), C.c_int]),
     "ixb_pool_layer": (C.c_int, [C.POINTER(PoolDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
     "ixb_quantize_images": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
@@ -131,6 +133,22 @@ def conv_launch_info(desc, arena_bytes: int, batch: int) -> dict:
     info = (C.c_int32 * len(LAUNCH_FIELDS))()
     check(load().ixb_conv_launch_info(C.byref(desc), arena_bytes, batch, info, len(LAUNCH_FIELDS)))
     return dict(zip(LAUNCH_FIELDS, list(info)))
+
+
+def conv_schedule(desc):
+    """(K-blocks, MMAs) of a conv: K-block dicts and per MMA ((tap, slot), (tap, slot) or None)."""
+    kb = (C.c_int32 * (8 * 512))()
+    ops = (C.c_int32 * (4 * 4096))()
+    n = check(load().ixb_conv_schedule(C.byref(desc), kb, 512, ops, 4096))
+    blocks = []
+    for i in range(n):
+        c0, nc, tap, op0, nops, boff, bbytes, _ = kb[8 * i:8 * i + 8]
+        mm = []
+        for j in range(op0, op0 + nops):
+            t0, s0, t1, s1 = ops[4 * j:4 * j + 4]
+            mm.append(((t0, s0), (t1, s1) if t1 >= 0 else None))
+        blocks.append({"chunk0": c0, "nchunks": nc, "tap": tap, "ops": mm, "b_off": boff, "b_bytes": bbytes})
+    return blocks
 
 
 def check(rc: int) -> int:

@@ -128,6 +128,66 @@ SegDev seg_dev(const ixb_segment& s, uint8_t* arena, int chunk_begin) {
   return d;
 }
 
+// K schedule of a conv: the K-blocks (input chunks in the A stage, gather tap, MMAs, weights)
+// and per MMA the (tap, A slot) of its two 32-byte K-halves. The weight packer
+// (ignite_xdna_b200/plan.py) lays B out in exactly this order.
+//  WINDOW: full chunk pairs, cp pairs per K-block, every tap of a pair (both halves one tap);
+//          an odd last chunk gets a K-block of its own whose MMAs pair consecutive taps of
+//          that chunk (the second K-half is the same chunk shifted by the next tap).
+//  GATHER: K-blocks tap-major over groups of cp pairs; a missing second chunk becomes a second
+//          K-half of zero weights (read one row past its slot, inside the stage's slack).
+//  STEM:   one K-block, chunks 0..3 = the three 16-byte image rows and a zero row.
+struct SchedKB {
+  int chunk0, nchunks, tap, op0, nops, b_off, b_bytes;
+};
+struct SchedOp {
+  int tap0, slot0, tap1, slot1;  // tap1 < 0: the second K-half multiplies zero weights
+};
+
+int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>& kbs, std::vector<SchedOp>& ops) {
+  kbs.clear();
+  ops.clear();
+  const int taps = d.k * d.k;
+  const int opb = d.n_tile * 32;
+  int b_off = 0;
+  auto push_kb = [&](int chunk0, int nchunks, int tap, int op0) {
+    const int nops = (int)ops.size() - op0;
+    kbs.push_back(SchedKB{chunk0, nchunks, tap, op0, nops, b_off, nops * opb});
+    b_off += nops * opb;
+  };
+  if (d.mode == IXB_MODE_STEM) {
+    ops.push_back(SchedOp{0, 0, 0, 1});
+    ops.push_back(SchedOp{0, 2, 0, 3});
+    push_kb(0, 4, 0, 0);
+  } else if (d.mode == IXB_MODE_WINDOW) {
+    const int E = cin_chunks / 2, odd = cin_chunks % 2;
+    for (int g = 0; g * d.cp < E; ++g) {
+      const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size();
+      for (int i = 0; i < prs; ++i)
+        for (int t = 0; t < taps; ++t) ops.push_back(SchedOp{t, 2 * i, t, 2 * i + 1});
+      push_kb(2 * g * d.cp, 2 * prs, 0, op0);
+    }
+    if (odd) {
+      const int op0 = (int)ops.size();
+      for (int t = 0; t < taps; t += 2) ops.push_back(SchedOp{t, 0, t + 1 < taps ? t + 1 : -1, 0});
+      push_kb(2 * E, 1, 0, op0);
+    }
+  } else {
+    const int pairs = (cin_chunks + 1) / 2;
+    for (int t = 0; t < taps; ++t) {
+      for (int g = 0; g * d.cp < pairs; ++g) {
+        const int prs = std::min(d.cp, pairs - g * d.cp), op0 = (int)ops.size();
+        const int loaded = std::min(2 * prs, cin_chunks - 2 * g * d.cp);
+        // a pair whose second chunk does not exist multiplies zero weights in its second half
+        for (int i = 0; i < prs; ++i)
+          ops.push_back(SchedOp{t, 2 * i, 2 * i + 1 < loaded ? t : -1, 2 * i + 1 < loaded ? 2 * i + 1 : 0});
+        push_kb(2 * g * d.cp, loaded, t, op0);
+      }
+    }
+  }
+  return 0;
+}
+
 struct ConvLaunch {
   ConvParams p;
   dim3 grid;
@@ -191,34 +251,33 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   if (d.mode == IXB_MODE_WINDOW && d.stride != 1) return bad("WINDOW mode is stride 1");
   p.cin_chunks = chunk;
-  const int pairs = (chunk + 1) / 2;
-  int b_block;
   if (d.mode == IXB_MODE_WINDOW) {
-    p.kblocks = (pairs + d.cp - 1) / d.cp;
-    p.taps_per_block = d.k * d.k;
-    p.pair_groups = p.kblocks;
     p.win_origin = pad * (d.in_w + 2) + pad;
-    b_block = d.cp * d.k * d.k * d.n_tile * 32;
     p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * (d.in_h + 2) * (d.in_w + 2));
-  } else if (d.mode == IXB_MODE_GATHER) {
-    p.pair_groups = (pairs + d.cp - 1) / d.cp;
-    p.kblocks = d.k * d.k * p.pair_groups;
-    p.taps_per_block = 1;
-    b_block = d.cp * d.n_tile * 32;
-    p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * d.out_w);
   } else {
-    p.kblocks = 1;
-    p.pair_groups = 1;
-    p.taps_per_block = 1;
-    b_block = 2 * d.n_tile * 32;
+    p.win_origin = 0;
     p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * d.out_w);
   }
   if ((long long)batch * (d.in_h + 2) * (d.in_w + 2) >= 0x7fff0000LL)
     return bad("more pixels than 32-bit pixel indices cover");
+  std::vector<SchedKB> kbs;
+  std::vector<SchedOp> ops;
+  build_schedule(d, chunk, kbs, ops);
+  if ((int)kbs.size() > kMaxKBlocks) return bad("too many K-blocks for the schedule table");
+  p.kblocks = (int)kbs.size();
+  p.taps_per_block = 0;
+  p.pair_groups = 0;
+  int slots = 0, b_stage_max = 0;
+  for (const SchedKB& k : kbs) {
+    slots = std::max(slots, k.nchunks);
+    b_stage_max = std::max(b_stage_max, k.b_bytes);
+  }
+  p.b_stage_max = b_stage_max;
+  const int b_total = kbs.back().b_off + kbs.back().b_bytes;
   const long long ntiles = d.cout / d.n_tile;
-  if ((unsigned long long)ntiles * p.kblocks * b_block != d.w_bytes) {
-    snprintf(buf, sizeof buf, "packed weights are %llu bytes, the tiling needs %llu",
-             (unsigned long long)d.w_bytes, (unsigned long long)(ntiles * p.kblocks * b_block));
+  if ((unsigned long long)ntiles * b_total != d.w_bytes) {
+    snprintf(buf, sizeof buf, "packed weights are %llu bytes, the schedule needs %llu",
+             (unsigned long long)d.w_bytes, (unsigned long long)(ntiles * b_total));
     err = buf;
     return -1;
   }
@@ -236,18 +295,18 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
       break;
     }
   }
-  p.b_block_bytes = b_block;
-  const int b_total = p.kblocks * b_block;
+  p.b_block_bytes = b_stage_max;
   const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * 512 * 16);  // barriers, table, bias, rows
   const int budget = kSmemLimit - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
     p.tile_rows = 128 * mt;
     p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + 2 * p.win_origin : p.tile_rows;
-    p.a_stage_bytes = 2 * d.cp * p.rowsA * 16;
+    // 16 spare bytes: a single-tap MMA's unused second K-half reads one row past its slot
+    p.a_stage_bytes = slots * p.rowsA * 16 + 16;
     p.b_resident = b_total <= budget / 2 ? 1 : 0;
     const int res_bytes = p.b_resident ? round_up(b_total, 1024) : 0;
-    p.stage_bytes = round_up(p.a_stage_bytes + (p.b_resident ? 0 : b_block), 1024);
+    p.stage_bytes = round_up(p.a_stage_bytes + (p.b_resident ? 0 : b_stage_max), 1024);
     const int S = std::min(6, (budget - res_bytes) / p.stage_bytes);
     if (S >= 2) {
       p.stages = S;
@@ -262,7 +321,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.lut_off = p.bar_off + 512;
   p.bias_off = p.lut_off + 256;
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
-  p.w_ntile_stride = (long long)p.kblocks * b_block;
+  p.w_ntile_stride = (long long)b_total;
   p.wpack = arena + d.w_offset;
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
   p.lut = reinterpret_cast<const int8_t*>(arena + d.lut_offset);
@@ -276,6 +335,55 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   while (cols < 2 * p.acc_cols) cols *= 2;
   p.tmem_cols = cols;
   p.idesc = umma_idesc_s8(kBlockM, d.n_tile);
+  {
+    // kernel op table: A start / LBO from (tap, slot) and the geometry, deduplicated per K-block
+    auto shift_of = [&](int t) { return d.mode == IXB_MODE_WINDOW ? (t / d.k) * (d.in_w + 2) + (t % d.k) : 0; };
+    std::vector<uint32_t> ta;
+    std::vector<uint16_t> tb;
+    for (size_t i = 0; i < kbs.size(); ++i) {
+      const SchedKB& k = kbs[i];
+      std::vector<uint32_t> ka;
+      std::vector<uint16_t> kbv;
+      for (int o = 0; o < k.nops; ++o) {
+        const SchedOp& op = ops[k.op0 + o];
+        const int a_start = op.slot0 * p.rowsA + shift_of(op.tap0);
+        int lbo = 1;
+        if (op.tap1 >= 0) lbo = op.slot1 * p.rowsA + shift_of(op.tap1) - a_start;
+        if (lbo <= 0 || lbo >= (1 << 14) || a_start >= (1 << 14)) return bad("MMA operand offsets out of range");
+        // rows read: a_start .. a_start + tile_rows - 1 (+ lbo for the second K-half), within the A region + 16
+        if ((long long)(a_start + lbo + p.tile_rows) * 16 > p.a_stage_bytes)
+          return bad("an MMA operand reads past its stage");
+        ka.push_back((uint32_t)a_start | ((uint32_t)lbo << 16));
+        kbv.push_back((uint16_t)(o * d.n_tile * 32 / 16));
+      }
+      // reuse an identical run already in the table
+      int found = -1;
+      for (size_t st = 0; st + ka.size() <= ta.size() && found < 0; ++st) {
+        bool eq = true;
+        for (size_t j = 0; j < ka.size() && eq; ++j) eq = ta[st + j] == ka[j] && tb[st + j] == kbv[j];
+        if (eq) found = (int)st;
+      }
+      if (found < 0) {
+        found = (int)ta.size();
+        ta.insert(ta.end(), ka.begin(), ka.end());
+        tb.insert(tb.end(), kbv.begin(), kbv.end());
+      }
+      if ((int)ta.size() > kMaxOps) return bad("too many MMAs for the op table");
+      KBlockDev& kd = p.kb[i];
+      kd.b_off = k.b_off;
+      kd.b_bytes = k.b_bytes;
+      kd.op0 = (int16_t)found;
+      kd.nops = (int16_t)k.nops;
+      kd.chunk0 = (int16_t)k.chunk0;
+      kd.nchunks = (int16_t)k.nchunks;
+      kd.tap = (int16_t)k.tap;
+      kd.pad_ = 0;
+    }
+    for (size_t i = 0; i < ta.size(); ++i) {
+      p.op_a[i] = ta[i];
+      p.op_b[i] = tb[i];
+    }
+  }
   p.has_res = d.has_residual;
   if (d.has_residual) {
     if (d.mode != IXB_MODE_WINDOW) return bad("a residual needs WINDOW mode");
@@ -724,6 +832,30 @@ int ixb_conv_layer_stats(const ixb_conv_desc* d, void* arena, uint64_t arena_byt
   if ((int64_t)L.grid.x * L.grid.y * kStatWords > stats_words) return fail(IXB_ERR_INVALID, "stats buffer too small");
   L.p.stats = reinterpret_cast<unsigned long long*>(stats);
   return launch_conv(L, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_conv_schedule(const ixb_conv_desc* d, int32_t* kb_out, int max_kb, int32_t* ops_out, int max_ops) {
+  if (!d || !kb_out || !ops_out) return fail(IXB_ERR_INVALID, "null argument");
+  int chunks = 0;
+  for (int i = 0; i < d->nseg && i < IXB_MAX_SEGS; ++i) chunks += (d->seg[i].channels + 15) / 16;
+  if (d->mode == IXB_MODE_STEM) chunks = 1;
+  if (d->n_tile < 16 || d->k < 1 || d->cp < 1) return fail(IXB_ERR_INVALID, "bad conv shape");
+  std::vector<SchedKB> kbs;
+  std::vector<SchedOp> ops;
+  build_schedule(*d, chunks, kbs, ops);
+  if ((int)kbs.size() > max_kb || (int)ops.size() > max_ops) return fail(IXB_ERR_INVALID, "schedule buffers too small");
+  for (size_t i = 0; i < kbs.size(); ++i) {
+    const SchedKB& k = kbs[i];
+    const int32_t v[8] = {k.chunk0, k.nchunks, k.tap, k.op0, k.nops, k.b_off, k.b_bytes, 0};
+    for (int j = 0; j < 8; ++j) kb_out[8 * i + j] = v[j];
+  }
+  for (size_t i = 0; i < ops.size(); ++i) {
+    ops_out[4 * i] = ops[i].tap0;
+    ops_out[4 * i + 1] = ops[i].slot0;
+    ops_out[4 * i + 2] = ops[i].tap1;
+    ops_out[4 * i + 3] = ops[i].slot1;
+  }
+  return (int)kbs.size();
 }
 
 int ixb_conv_launch_info(const ixb_conv_desc* d, uint64_t arena_bytes, int batch, int32_t* info, int n) {

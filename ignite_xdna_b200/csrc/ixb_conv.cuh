@@ -55,6 +55,15 @@ struct SegDev {
   int H, W, up2, P;         // stored size, upsampled view, padded pixels per image
 };
 
+// One K-block: which input chunks its A stage holds (slots 0..nchunks-1 = chunks chunk0..), the tap
+// a gather reads, its MMAs (op0 .. op0+nops-1 of the op table) and its weights.
+struct KBlockDev {
+  int b_off, b_bytes;
+  int16_t op0, nops, chunk0, nchunks, tap, pad_;
+};
+constexpr int kMaxKBlocks = 96;
+constexpr int kMaxOps = 160;
+
 struct ConvParams {
   int mode, k, stride, pad;
   int H, W, Ho, Wo, batch;
@@ -83,6 +92,10 @@ struct ConvParams {
   int cout;
   FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wo, Wo
   unsigned long long* stats;          // optional per-CTA role counters (kStatWords per CTA), or null
+  int b_stage_max;                    // largest K-block of weights (stage B region when streamed)
+  KBlockDev kb[kMaxKBlocks];          // the K schedule
+  uint32_t op_a[kMaxOps];             // per MMA: A start (16-byte units from the stage) | LBO (16-byte units) << 16
+  uint16_t op_b[kMaxOps];             // per MMA: B start (16-byte units from the K-block's weights)
 };
 
 // Per-CTA role counters (clock64 cycles) written when ConvParams::stats is set.
@@ -126,7 +139,6 @@ __device__ __forceinline__ int rne_pos(int x, int s, int half_m1) { return (x + 
 template <int MODE>
 __device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                                int ntile) {
-  const int nch = 2 * p.cp;
   const int S = p.stages;
   const uint32_t chunk_bytes = (uint32_t)p.rowsA * 16;
   int stage = 0;
@@ -140,18 +152,17 @@ __device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* sme
       const long long c1 = clock64();
       tw += c1 - c0;
       uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
-      const int valid = min(nch, p.cin_chunks - kb * nch);
-      uint32_t bytes = (uint32_t)valid * chunk_bytes + (p.b_resident ? 0u : (uint32_t)p.b_block_bytes);
+      const KBlockDev& K = p.kb[kb];
+      uint32_t bytes = (uint32_t)K.nchunks * chunk_bytes + (p.b_resident ? 0u : (uint32_t)K.b_bytes);
       mbar_arrive_expect_tx(&full[stage], bytes);
-      for (int c = 0; c < valid; ++c) {
-        const int gc = kb * nch + c;
+      for (int c = 0; c < K.nchunks; ++c) {
+        const int gc = K.chunk0 + c;
         const SegDev& s = p.seg[seg_of_chunk(p, gc)];
         bulk_g2s(As + c * chunk_bytes, s.base + (long long)(gc - s.chunk_begin) * s.plane + wb * 16, chunk_bytes,
                  &full[stage]);
       }
       if (!p.b_resident)
-        bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
-                 p.b_block_bytes, &full[stage]);
+        bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + K.b_off, K.b_bytes, &full[stage]);
       tk += clock64() - c1;
       if (++stage == S) {
         stage = 0;
@@ -228,10 +239,11 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
           }
         }
       } else {
-        const int tap = kb / p.pair_groups;
-        const int gc = (kb - tap * p.pair_groups) * nch + c;
+        const KBlockDev& K = p.kb[kb];
+        const int tap = K.tap;
+        const int gc = c < K.nchunks ? K.chunk0 + c : -1;
         const int ky = tap / p.k, kx = tap - (tap / p.k) * p.k;
-        const int si = seg_of_chunk(p, gc);
+        const int si = gc >= 0 ? seg_of_chunk(p, gc) : -1;
         if (si >= 0) {
           const SegDev& s = p.seg[si];
           const int8_t* cbase = s.base + (long long)(gc - s.chunk_begin) * s.plane;
@@ -261,9 +273,10 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
       }
       cp_async_mbar_arrive(&full[stage]);
       if (!p.b_resident && ptid == 0) {
-        mbar_arrive_expect_tx(&full[stage], p.b_block_bytes);
-        bulk_g2s(smem + p.a_off + stage * p.stage_bytes + p.a_stage_bytes,
-                 p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes, p.b_block_bytes, &full[stage]);
+        const KBlockDev& K = p.kb[kb];
+        mbar_arrive_expect_tx(&full[stage], K.b_bytes);
+        bulk_g2s(smem + p.a_off + stage * p.stage_bytes + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + K.b_off,
+                 K.b_bytes, &full[stage]);
       }
       if (++stage == S) {
         stage = 0;
@@ -442,10 +455,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
     // ------------------------------------------------------------ producers
     const int ptid = tid - kProducerWarp0 * 32;
     if (p.b_resident && ptid == 0) {
-      mbar_arrive_expect_tx(bres_bar, (uint32_t)(KB * p.b_block_bytes));
+      const int total = p.kb[KB - 1].b_off + p.kb[KB - 1].b_bytes;
+      mbar_arrive_expect_tx(bres_bar, (uint32_t)total);
       for (int kb = 0; kb < KB; ++kb)
-        bulk_g2s(smem + kb * p.b_block_bytes, p.wpack + ntile * p.w_ntile_stride + (long long)kb * p.b_block_bytes,
-                 p.b_block_bytes, bres_bar);
+        bulk_g2s(smem + p.kb[kb].b_off, p.wpack + ntile * p.w_ntile_stride + p.kb[kb].b_off, p.kb[kb].b_bytes, bres_bar);
     }
     if (MODE == IXB_MODE_WINDOW) {
       if (ptid == 0) produce_window<MODE>(p, smem, full, empty, ntile);
@@ -456,7 +469,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       if (p.b_resident) mbar_wait(bres_bar, 0);
-      const uint32_t lbo_a = p.rowsA * 16;
       int stage = 0, acc = 0;
       uint32_t ph = 0, aph = 0;
       long long wf = 0, wa = 0, wi = 0;
@@ -474,27 +486,24 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
           wf += c1 - c0;
           if (MODE != IXB_MODE_WINDOW) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
           tc_fence_after();
-          // Descriptors are built once per stage; stepping the operand start is adding
-          // (byte offset >> 4) to the low 14-bit address field, which cannot carry (smem < 256 KB).
-          const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes);
-          const uint32_t b0 = p.b_resident ? smem_u32(smem) + kb * p.b_block_bytes : a0 + p.a_stage_bytes;
-          const uint64_t adesc0 = umma_desc(a0, lbo_a, 128);
-          const uint64_t bdesc0 = umma_desc(b0, 128, 256);
-          const uint32_t b_step = (uint32_t)(p.n_tile * 32) >> 4;
-          for (int pp = 0; pp < p.cp; ++pp) {
-            const uint64_t adesc_p = adesc0 + ((pp * 2 * lbo_a) >> 4);
-            for (int tap = 0; tap < p.taps_per_block; ++tap) {
-              uint32_t shift_px = 0;
-              if (MODE == IXB_MODE_WINDOW) shift_px = (tap / p.k) * (p.W + 2) + (tap - (tap / p.k) * p.k);
-              const uint64_t bd = bdesc0 + (uint64_t)((pp * p.taps_per_block + tap) * b_step);
-              const uint32_t accum = (kb > 0 || pp > 0 || tap > 0) ? 1u : 0u;
-              uint64_t ad = adesc_p + shift_px;   // 16 bytes per pixel of shift
-              uint32_t dt = d0;
-              for (int b = 0; b < p.mt; ++b) {
-                umma_s8(dt, ad, bd, p.idesc, accum);
-                ad += (kBlockM * 16) >> 4;
-                dt += p.n_tile;
-              }
+          // A descriptor = stage base + op's start and LBO (16-byte units) + 128 rows per block;
+          // B descriptor = K-block weights base + op's start. Additions to the low 14-bit address
+          // field cannot carry (shared memory < 256 KB).
+          const KBlockDev& K = p.kb[kb];
+          const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes) >> 4;
+          const uint32_t b0 = (p.b_resident ? (smem_u32(smem) + K.b_off) : ((a0 << 4) + p.a_stage_bytes)) >> 4;
+          const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+          const uint64_t bdesc0 = umma_desc(b0 << 4, 128, 256);
+          for (int o = 0; o < K.nops; ++o) {
+            const uint32_t opa = p.op_a[K.op0 + o];
+            const uint64_t bd = bdesc0 + p.op_b[K.op0 + o];
+            const uint32_t accum = (kb > 0 || o > 0) ? 1u : 0u;
+            uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
+            uint32_t dt = d0;
+            for (int b = 0; b < p.mt; ++b) {
+              umma_s8(dt, ad, bd, p.idesc, accum);
+              ad += (kBlockM * 16) >> 4;
+              dt += p.n_tile;
             }
           }
           umma_commit(&empty[stage]);

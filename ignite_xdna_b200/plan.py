@@ -15,8 +15,9 @@ HBM layout (one arena per GPU, sized for ``max_batch`` images):
 * constants: weights packed per (n-tile, K-block) in the UMMA core-matrix layout, int32
   biases, the int8 activation tables.
 
-The packing here and the K-block walk in ``csrc/ixb_conv.cuh`` are two sides of one contract:
-``conv_kblocks`` is the single definition of the K order.
+The K order is the kernel's: ``_lib.conv_schedule`` returns the schedule the library builds for a
+conv (which input chunks each K-block loads and which (tap, chunk) pairs each MMA multiplies),
+and ``pack_weights`` lays the weights out in exactly that order.
 """
 from __future__ import annotations
 
@@ -121,62 +122,45 @@ def choose_cp(mode: int, k: int, cin: int) -> int:
     return 4 if pairs >= 4 else (2 if pairs >= 2 else 1)
 
 
-def conv_kblocks(mode: int, k: int, cin: int, cp: int) -> List[List[Tuple[int, int]]]:
-    """K order: per K-block, per MMA, the (tap, 32-channel pair) it multiplies.
-
-    WINDOW: K-block = cp pairs x all taps (pair-major); GATHER: K-block = one tap x cp pairs,
-    blocks tap-major; STEM: one block of two 32-byte halves of the 64-byte image K row."""
-    pairs = (cin + 31) // 32
-    taps = k * k
-    if mode == L.MODE_STEM:
-        return [[(0, 0), (0, 1)]]
-    groups = (pairs + cp - 1) // cp
-    blocks = []
-    if mode == L.MODE_WINDOW:
-        for g in range(groups):
-            blocks.append([(t, g * cp + p) for p in range(cp) for t in range(taps)])
-    else:
-        for t in range(taps):
-            for g in range(groups):
-                blocks.append([(t, g * cp + p) for p in range(cp)])
-    return blocks
-
-
 def _core_layout(b: np.ndarray) -> np.ndarray:
     """[n, 32] K-major bytes -> UMMA no-swizzle core matrices [n/8][2][8][16]."""
     n = b.shape[0]
     return b.reshape(n // 8, 8, 2, 16).transpose(0, 2, 1, 3).reshape(-1)
 
 
-def pack_weights(layer: ConvLayer, mode: int, n_tile: int, cp: int) -> np.ndarray:
+def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule) -> np.ndarray:
+    """Weights of every n-tile as the schedule's MMAs' [n_tile][32] K-slices, each in the UMMA
+    core-matrix layout; a slice's two 16-byte K-halves are the (tap, chunk) pairs of its MMA."""
     w = layer.weights.astype(np.int8)       # [cout][cin][k][k]
     cout, cin, k, _ = w.shape
+    nchunks = (cin + 15) // 16
     if mode == L.MODE_STEM:
-        # K byte 16*ky + 4*j + ci holds w[n][ci][ky][j] (j = kx); row ky = 3 and pixel j = 3 are zero
-        kk = np.zeros((cout, 64), dtype=np.int8)
+        # chunk ky (0..2) holds the image row ky: byte 4*j + ci = w[n][ci][ky][j] (j = kx); chunk 3 is zero
+        stem = np.zeros((4, cout, 16), dtype=np.int8)
         for ky in range(3):
             for j in range(3):
                 for ci in range(3):
-                    kk[:, 16 * ky + 4 * j + ci] = w[:, ci, ky, j]
-        mats = [kk[:, 0:32], kk[:, 32:64]]
-        blocks = [[0, 1]]
-        out = []
-        for nt in range(cout // n_tile):
-            sl = slice(nt * n_tile, (nt + 1) * n_tile)
-            out.append(np.concatenate([_core_layout(np.ascontiguousarray(mats[i][sl])) for i in blocks[0]]))
-        return np.concatenate(out).view(np.uint8)
-    pairs = (cin + 31) // 32
-    wp = np.zeros((cout, pairs * 32, k * k), dtype=np.int8)
-    wp[:, :cin, :] = w.reshape(cout, cin, k * k)
+                    stem[ky, :, 4 * j + ci] = w[:, ci, ky, j]
+
+        def piece(chunk, tap):
+            return stem[chunk]
+    else:
+        wp = np.zeros((cout, nchunks * 16, k * k), dtype=np.int8)
+        wp[:, :cin, :] = w.reshape(cout, cin, k * k)
+
+        def piece(chunk, tap):
+            if chunk >= nchunks:
+                return np.zeros((cout, 16), dtype=np.int8)
+            return wp[:, 16 * chunk:16 * chunk + 16, tap]
+    zero = np.zeros((cout, 16), dtype=np.int8)
     out = []
     for nt in range(cout // n_tile):
         sl = slice(nt * n_tile, (nt + 1) * n_tile)
-        for block in conv_kblocks(mode, k, cin, cp):
-            for tap, pair in block:
-                if pair >= pairs:
-                    out.append(np.zeros(n_tile * 32, dtype=np.int8))
-                else:
-                    out.append(_core_layout(np.ascontiguousarray(wp[sl, pair * 32:(pair + 1) * 32, tap])))
+        for blk in schedule:
+            for (t0, s0), second in blk["ops"]:
+                h0 = piece(blk["chunk0"] + s0, t0)
+                h1 = piece(blk["chunk0"] + second[1], second[0]) if second is not None else zero
+                out.append(_core_layout(np.ascontiguousarray(np.concatenate([h0[sl], h1[sl]], axis=1))))
     return np.concatenate(out).view(np.uint8)
 
 
@@ -266,8 +250,15 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
         mode = conv_mode(layer, ir)
         n_tile = choose_n_tile(layer.cout)
         cp = choose_cp(mode, layer.k, layer.cin)
-        wp = pack_weights(layer, mode, n_tile, cp)
+        shape = L.ConvDesc()
+        shape.mode, shape.k, shape.stride, shape.n_tile, shape.cp = mode, layer.k, layer.stride, n_tile, cp
+        shape.cin, shape.cout = layer.cin, layer.cout
+        shape.nseg = 1
+        shape.seg[0].channels = layer.cin if mode != L.MODE_STEM else 3
+        sched = L.conv_schedule(shape)
+        wp = pack_weights(layer, mode, n_tile, sched)
         cpl = ConvPlan(layer, mode, n_tile, cp, wp)
+        cpl.schedule = sched
         cpl.w_rel = cput(wp)
         cpl.bias_rel = cput(layer.bias_int8_domain().astype(np.int32))
         cpl.lut_rel = cput(layer.lut_t())

@@ -155,6 +155,12 @@ int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, in
  * MMA and producer roles spent waiting and working, the CTA lifetime and its tile count. */
 int ixb_conv_layer_stats(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream,
                          uint64_t* stats, int64_t stats_words);
+/* The K schedule of a conv descriptor (shape fields only: mode, k, n_tile, cp, segment channels).
+ * kb_out: 8 int32 per K-block {first chunk, chunks, gather tap, first MMA, MMAs, weight offset,
+ * weight bytes, 0}; ops_out: 4 int32 per MMA {tap, A slot, tap, A slot} of its two 32-byte
+ * K-halves (second tap -1: zero weights). Returns the number of K-blocks. The packed weights of
+ * one n-tile are the MMAs' [n_tile][32] K-slices in this order. */
+int ixb_conv_schedule(const ixb_conv_desc* d, int32_t* kb_out, int max_kb, int32_t* ops_out, int max_ops);
 /* The launch a conv descriptor gets for `batch` images (host-side decision, no GPU needed):
  * info = {blocks of 128 pixels per tile, tile rows, tiles, pipeline stages, weights resident,
  *         grid.x, grid.y, shared bytes, TMEM columns, K-blocks, A rows per stage, pairs per K-block}. */

@@ -41,49 +41,46 @@ def _seg_params(d, s, chunk_begin):
 
 def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
     info = L.conv_launch_info(d, arena_bytes, batch)
+    sched = L.conv_schedule(d)
     MT = info["mt"]
     TM = 128 * MT
     mode, k, stride = d.mode, d.k, d.stride
     pad = k // 2
     H, W, Ho, Wo = d.in_h, d.in_w, d.out_h, d.out_w
-    cp, n_tile = d.cp, d.n_tile
+    n_tile = d.n_tile
     segs, chunk = [], 0
     for i in range(d.nseg):
         sp = _seg_params(d, d.seg[i], chunk)
         chunk += sp["chunks"]
         segs.append(sp)
-    cin_chunks = chunk
-    pairs = (cin_chunks + 1) // 2
     if mode == L.MODE_WINDOW:
-        kblocks = (pairs + cp - 1) // cp
-        taps_pb, groups = k * k, kblocks
         win_origin = pad * (W + 2) + pad
         rowsA = TM + 2 * win_origin
-        b_block = cp * k * k * n_tile * 32
         m_total = batch * (H + 2) * (W + 2)
-    elif mode == L.MODE_GATHER:
-        groups = (pairs + cp - 1) // cp
-        kblocks, taps_pb, rowsA, win_origin = k * k * groups, 1, TM, 0
-        b_block = cp * n_tile * 32
-        m_total = batch * Ho * Wo
     else:
-        kblocks, taps_pb, groups, rowsA, win_origin = 1, 1, 1, TM, 0
-        b_block = 2 * n_tile * 32
+        win_origin = 0
+        rowsA = TM
         m_total = batch * Ho * Wo
-    assert (d.cout // n_tile) * kblocks * b_block == d.w_bytes
-    assert info["kblocks"] == kblocks and info["rows_a"] == rowsA
-    a_bytes = 2 * cp * rowsA * 16
+    assert info["kblocks"] == len(sched) and info["rows_a"] == rowsA
+    b_total = sched[-1]["b_off"] + sched[-1]["b_bytes"]
+    assert (d.cout // n_tile) * b_total == d.w_bytes
+    slots = max(b["nchunks"] for b in sched)
+    a_bytes = slots * rowsA * 16 + 16
+
+    def shift_of(t):
+        return (t // k) * (W + 2) + (t % k) if mode == L.MODE_WINDOW else 0
+
     bias = arena[d.bias_offset:d.bias_offset + 4 * d.cout].view(np.int32).astype(np.int64)
     lut = arena[d.lut_offset:d.lut_offset + 256].view(np.int8).astype(np.int64)
-    nch = 2 * cp
     for mt in range((m_total + TM - 1) // TM):
         m0 = mt * TM
         for nt in range(d.cout // n_tile):
             acc = np.zeros((TM, n_tile), dtype=np.int64)
-            for kb in range(kblocks):
-                smem = np.zeros(a_bytes + b_block, dtype=np.uint8)
-                # ---- A
-                for c in range(nch):
+            for blk in sched:
+                smem = np.zeros(a_bytes, dtype=np.uint8)
+                # ---- A: the K-block's chunks into slots 0..nchunks-1
+                for c in range(blk["nchunks"]):
+                    gc = blk["chunk0"] + c
                     dst0 = c * rowsA * 16
                     if mode == L.MODE_STEM:
                         r = np.arange(TM)
@@ -97,12 +94,6 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         for rr in np.nonzero(ok)[0]:
                             smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[src[rr]:src[rr] + 16]
                         continue
-                    if mode == L.MODE_WINDOW:
-                        gc = kb * nch + c
-                        tap = 0
-                    else:
-                        tap = kb // groups
-                        gc = (kb - tap * groups) * nch + c
                     si = [i for i, s in enumerate(segs) if s["chunk_begin"] <= gc < s["chunk_begin"] + s["chunks"]]
                     if not si:
                         continue
@@ -115,6 +106,7 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         src = cbase + m * 16
                         rows = px
                     else:
+                        tap = blk["tap"]
                         r = np.arange(TM)
                         m = m0 + r
                         ok = m < m_total
@@ -129,18 +121,16 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         rows = r
                     for rr, sa in zip(rows[ok], src[ok]):
                         smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[sa:sa + 16]
-                # ---- B (one bulk copy)
-                wsrc = d.w_offset + nt * kblocks * b_block + kb * b_block
-                smem[a_bytes:a_bytes + b_block] = arena[wsrc:wsrc + b_block]
-                # ---- MMAs
-                lbo_a = rowsA * 16
-                for pp in range(cp):
-                    for t in range(taps_pb):
-                        shift_px = (t // k) * (W + 2) + (t % k) if mode == L.MODE_WINDOW else 0
-                        B = _operand(smem, a_bytes + (pp * taps_pb + t) * n_tile * 32, 128, 256, n_tile)
-                        for blk in range(MT):
-                            A = _operand(smem, pp * 2 * lbo_a + (blk * 128 + shift_px) * 16, lbo_a, 128, 128)
-                            acc[blk * 128:(blk + 1) * 128] += A @ B.T
+                # ---- B of this K-block, then its MMAs
+                wsrc = d.w_offset + nt * b_total + blk["b_off"]
+                bmem = arena[wsrc:wsrc + blk["b_bytes"]]
+                for o, ((t0, s0), second) in enumerate(blk["ops"]):
+                    a_start = s0 * rowsA + shift_of(t0)
+                    lbo = (second[1] * rowsA + shift_of(second[0]) - a_start) if second is not None else 1
+                    B = _operand(bmem, o * n_tile * 32, 128, 256, n_tile)
+                    for blk_m in range(MT):
+                        A = _operand(smem, (a_start + blk_m * 128) * 16, lbo * 16, 128, 128)
+                        acc[blk_m * 128:(blk_m + 1) * 128] += A @ B.T
             # ---- epilogue
             m = m0 + np.arange(TM)
             valid = m < m_total

@@ -6,7 +6,7 @@ import ixb_oracle as O
 import kernel_model as KM
 from ignite_xdna_b200 import _lib as L
 from ignite_xdna_b200 import build_yolov8, random_images
-from ignite_xdna_b200.plan import build_plan, conv_kblocks, input_lut_t
+from ignite_xdna_b200.plan import build_plan, input_lut_t
 
 
 @pytest.mark.parametrize("imgsz,batch,sms", [(64, 2, None), (96, 1, None), (64, 2, "1"), (96, 1, "2")])
@@ -49,12 +49,39 @@ def test_plan_storage_is_disjoint_and_aligned(variant):
     assert dp.egress_image_bytes == 1_209_600
 
 
-def test_k_order_covers_every_tap_and_pair_once():
-    for mode in (L.MODE_WINDOW, L.MODE_GATHER):
-        for k, cin, cp in ((3, 80, 1), (1, 384, 4), (3, 576, 2), (1, 48, 2)):
-            blocks = conv_kblocks(mode, k, cin, cp)
-            seen = [x for b in blocks for x in b if x[1] < (cin + 31) // 32]
-            assert sorted(seen) == sorted({(t, p) for t in range(k * k) for p in range((cin + 31) // 32)})
+def _sched(mode, k, cin, cp, n_tile=32):
+    d = L.ConvDesc()
+    d.mode, d.k, d.stride, d.n_tile, d.cp, d.cin, d.cout, d.nseg = mode, k, 1, n_tile, cp, cin, n_tile, 1
+    d.seg[0].channels = cin
+    return L.conv_schedule(d)
+
+
+@pytest.mark.parametrize("mode", [L.MODE_WINDOW, L.MODE_GATHER])
+@pytest.mark.parametrize("k,cin,cp", [(3, 80, 1), (1, 384, 4), (3, 576, 2), (1, 48, 2), (3, 16, 1), (1, 16, 1),
+                                      (3, 48, 1), (1, 80, 4)])
+def test_schedule_covers_every_tap_and_chunk_once(mode, k, cin, cp):
+    nchunks = (cin + 15) // 16
+    seen = []
+    for blk in _sched(mode, k, cin, cp):
+        assert blk["nchunks"] <= 2 * cp
+        for first, second in blk["ops"]:
+            for half in (first, second):
+                if half is None:
+                    continue
+                tap, slot = half
+                chunk = blk["chunk0"] + slot
+                if chunk < nchunks:
+                    assert slot < blk["nchunks"]
+                    seen.append((tap if mode == L.MODE_WINDOW else blk["tap"], chunk))
+    assert sorted(seen) == sorted((t, c) for t in range(k * k) for c in range(nchunks))
+
+
+def test_odd_chunk_taps_are_paired():
+    """A 16-channel 3x3 conv needs 5 MMAs per 128 pixels, not 9."""
+    blocks = _sched(L.MODE_WINDOW, 3, 16, 1)
+    assert len(blocks) == 1 and len(blocks[0]["ops"]) == 5
+    blocks = _sched(L.MODE_WINDOW, 3, 80, 1)
+    assert sum(len(b["ops"]) for b in blocks) == 2 * 9 + 5
 
 
 def test_fast_division_formula_is_exact():
