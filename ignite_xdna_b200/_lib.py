@@ -18,7 +18,7 @@ ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupport
 IXB_ERR_TIMEOUT = -3
 MAX_SEGS = 4
 API_VERSION = 2
-MODE_WINDOW, MODE_GATHER, MODE_STEM = 0, 1, 2
+MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH = 1, 2, 4, 8
 OP_CONV, OP_POOL = 0, 1
 
@@ -136,18 +136,21 @@ def conv_launch_info(desc, arena_bytes: int, batch: int) -> dict:
 
 
 def conv_schedule(desc):
-    """(K-blocks, MMAs) of a conv: K-block dicts and per MMA ((tap, slot), (tap, slot) or None)."""
+    """The kernel's K schedule of a conv: per K-block {chunk0, nchunks, tap0, ntaps, ops, b_off, b_bytes},
+    A slot s holding chunk chunk0 + s // ntaps at tap tap0 + s % ntaps; per MMA ((slot, chunk, tap),
+    (slot, chunk, tap) or None) for its two 32-byte K-halves (None: zero weights)."""
     kb = (C.c_int32 * (8 * 512))()
-    ops = (C.c_int32 * (4 * 4096))()
+    ops = (C.c_int32 * (6 * 4096))()
     n = check(load().ixb_conv_schedule(C.byref(desc), kb, 512, ops, 4096))
     blocks = []
     for i in range(n):
-        c0, nc, tap, op0, nops, boff, bbytes, _ = kb[8 * i:8 * i + 8]
+        c0, nc, t0, nt, op0, nops, boff, bbytes = kb[8 * i:8 * i + 8]
         mm = []
         for j in range(op0, op0 + nops):
-            t0, s0, t1, s1 = ops[4 * j:4 * j + 4]
-            mm.append(((t0, s0), (t1, s1) if t1 >= 0 else None))
-        blocks.append({"chunk0": c0, "nchunks": nc, "tap": tap, "ops": mm, "b_off": boff, "b_bytes": bbytes})
+            s0, ch0, tp0, s1, ch1, tp1 = ops[6 * j:6 * j + 6]
+            mm.append(((s0, ch0, tp0), (s1, ch1, tp1) if ch1 >= 0 else None))
+        blocks.append({"chunk0": c0, "nchunks": nc, "tap0": t0, "ntaps": nt, "ops": mm, "b_off": boff,
+                       "b_bytes": bbytes})
     return blocks
 
 

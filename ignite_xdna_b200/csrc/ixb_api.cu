@@ -4,6 +4,8 @@
 // or writes must lie inside the arena for the batch size used, with the alignment the
 // 16-byte copies and stores need. A session replays one captured CUDA graph per batch size
 // (input staging -> image ingress -> every layer -> head egress) on its own stream.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -74,7 +76,8 @@ int sm_count() {
 
 // A view touches, for `batch` images, every chunk plane it names from `guard` pixels before the
 // first image to `guard` pixels after the last; all of it must lie inside the arena, the planes
-// must not overlap, and the 16-byte copies need 16-byte alignment.
+// must not overlap, and the 16-byte copies need 16-byte alignment. The image tensor is one plane
+// of 8-byte pixels [batch][H+2][W+4].
 int check_seg(const ixb_segment& s, int batch, uint64_t arena_bytes, bool image, const char* what,
               std::string& err) {
   char buf[256];
@@ -83,16 +86,17 @@ int check_seg(const ixb_segment& s, int batch, uint64_t arena_bytes, bool image,
     err = buf;
     return -1;
   }
-  const unsigned long long pix = (unsigned long long)batch * (s.height + 2) * (unsigned long long)(s.width + 2);
   if (image) {
-    if (s.channels != 3 || s.chunk_offset || s.guard || s.offset % 16 || s.offset + pix * 4 > arena_bytes) {
-      snprintf(buf, sizeof buf, "%s: the image tensor is one guard-free plane of 4-byte pixels inside the arena",
+    const unsigned long long bytes = (unsigned long long)batch * (s.height + 2) * (unsigned long long)(s.width + 4) * 8;
+    if (s.channels != 3 || s.chunk_offset || s.guard || s.offset % 16 || s.width % 2 || s.offset + bytes > arena_bytes) {
+      snprintf(buf, sizeof buf, "%s: the image tensor is one guard-free plane of 8-byte pixels inside the arena",
                what);
       err = buf;
       return -1;
     }
     return 0;
   }
+  const unsigned long long pix = (unsigned long long)batch * (s.height + 2) * (unsigned long long)(s.width + 2);
   if (s.channels % 16 || s.offset % 16 || s.plane_stride % 16) {
     snprintf(buf, sizeof buf, "%s: misaligned view (offset %llu plane %llu channels %d)", what,
              (unsigned long long)s.offset, (unsigned long long)s.plane_stride, s.channels);
@@ -125,23 +129,25 @@ SegDev seg_dev(const ixb_segment& s, uint8_t* arena, int chunk_begin) {
   d.W = s.width;
   d.up2 = s.up2;
   d.P = (s.height + 2) * (s.width + 2);
+  const long long img_bytes = (long long)d.P * 16;
+  d.plane_images = (s.plane_stride && s.plane_stride % img_bytes == 0) ? (int)(s.plane_stride / img_bytes) : 0;
   return d;
 }
 
-// K schedule of a conv: the K-blocks (input chunks in the A stage, gather tap, MMAs, weights)
-// and per MMA the (tap, A slot) of its two 32-byte K-halves. The weight packer
-// (ignite_xdna_b200/plan.py) lays B out in exactly this order.
-//  WINDOW: full chunk pairs, cp pairs per K-block, every tap of a pair (both halves one tap);
-//          an odd last chunk gets a K-block of its own whose MMAs pair consecutive taps of
-//          that chunk (the second K-half is the same chunk shifted by the next tap).
-//  GATHER: K-blocks tap-major over groups of cp pairs; a missing second chunk becomes a second
-//          K-half of zero weights (read one row past its slot, inside the stage's slack).
-//  STEM:   one K-block, chunks 0..3 = the three 16-byte image rows and a zero row.
+// K schedule of a conv: the K-blocks (A slots, MMAs, weights) and per MMA the (slot, chunk, tap)
+// of its two 32-byte K-halves. The weight packer (ignite_xdna_b200/plan.py) lays B out in exactly
+// this order. Slot s of a K-block holds chunk chunk0 + s / ntaps at tap tap0 + s % ntaps.
+//  WINDOW: full chunk pairs, cp pairs per K-block, all taps as window shifts of the pair's slots;
+//          an odd last chunk gets a K-block whose MMAs pair consecutive taps of that chunk.
+//  IM2COL: K-blocks tap-major over groups of cp full pairs; an odd last chunk gets K-blocks of two
+//          taps each (slots = the chunk at tap t and t + 1).
+//  GATHER: K-blocks over groups of cp pairs (1x1); a missing second chunk is a zero-weight half.
+//  STEM:   one K-block of six slots: tap 2 * ky + p is the pixel pair p of image row ky.
 struct SchedKB {
-  int chunk0, nchunks, tap, op0, nops, b_off, b_bytes;
+  int chunk0, nchunks, tap0, ntaps, op0, nops, b_off, b_bytes;
 };
 struct SchedOp {
-  int tap0, slot0, tap1, slot1;  // tap1 < 0: the second K-half multiplies zero weights
+  int slot0, chunk0, tap0, slot1, chunk1, tap1;  // chunk1 < 0: the second half multiplies zero weights
 };
 
 int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>& kbs, std::vector<SchedOp>& ops) {
@@ -150,38 +156,53 @@ int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>&
   const int taps = d.k * d.k;
   const int opb = d.n_tile * 32;
   int b_off = 0;
-  auto push_kb = [&](int chunk0, int nchunks, int tap, int op0) {
+  auto push_kb = [&](int chunk0, int nchunks, int tap0, int ntaps, int op0) {
     const int nops = (int)ops.size() - op0;
-    kbs.push_back(SchedKB{chunk0, nchunks, tap, op0, nops, b_off, nops * opb});
+    kbs.push_back(SchedKB{chunk0, nchunks, tap0, ntaps, op0, nops, b_off, nops * opb});
     b_off += nops * opb;
   };
+  const int E = cin_chunks / 2, odd = cin_chunks % 2;
   if (d.mode == IXB_MODE_STEM) {
-    ops.push_back(SchedOp{0, 0, 0, 1});
-    ops.push_back(SchedOp{0, 2, 0, 3});
-    push_kb(0, 4, 0, 0);
+    for (int ky = 0; ky < 3; ++ky) ops.push_back(SchedOp{2 * ky, 0, 2 * ky, 2 * ky + 1, 0, 2 * ky + 1});
+    push_kb(0, 1, 0, 6, 0);
   } else if (d.mode == IXB_MODE_WINDOW) {
-    const int E = cin_chunks / 2, odd = cin_chunks % 2;
     for (int g = 0; g * d.cp < E; ++g) {
-      const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size();
+      const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
       for (int i = 0; i < prs; ++i)
-        for (int t = 0; t < taps; ++t) ops.push_back(SchedOp{t, 2 * i, t, 2 * i + 1});
-      push_kb(2 * g * d.cp, 2 * prs, 0, op0);
+        for (int t = 0; t < taps; ++t) ops.push_back(SchedOp{2 * i, c0 + 2 * i, t, 2 * i + 1, c0 + 2 * i + 1, t});
+      push_kb(c0, 2 * prs, 0, 1, op0);
     }
     if (odd) {
       const int op0 = (int)ops.size();
-      for (int t = 0; t < taps; t += 2) ops.push_back(SchedOp{t, 0, t + 1 < taps ? t + 1 : -1, 0});
-      push_kb(2 * E, 1, 0, op0);
+      for (int t = 0; t < taps; t += 2)
+        ops.push_back(t + 1 < taps ? SchedOp{0, 2 * E, t, 0, 2 * E, t + 1} : SchedOp{0, 2 * E, t, 0, -1, 0});
+      push_kb(2 * E, 1, 0, 1, op0);
+    }
+  } else if (d.mode == IXB_MODE_IM2COL) {
+    for (int t = 0; t < taps; ++t) {
+      for (int g = 0; g * d.cp < E; ++g) {
+        const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
+        for (int i = 0; i < prs; ++i) ops.push_back(SchedOp{2 * i, c0 + 2 * i, t, 2 * i + 1, c0 + 2 * i + 1, t});
+        push_kb(c0, 2 * prs, t, 1, op0);
+      }
+    }
+    if (odd) {
+      for (int t = 0; t < taps; t += 2) {
+        const int op0 = (int)ops.size(), nt = std::min(2, taps - t);
+        ops.push_back(nt == 2 ? SchedOp{0, 2 * E, t, 1, 2 * E, t + 1} : SchedOp{0, 2 * E, t, 0, -1, 0});
+        push_kb(2 * E, 1, t, nt, op0);
+      }
     }
   } else {
     const int pairs = (cin_chunks + 1) / 2;
     for (int t = 0; t < taps; ++t) {
       for (int g = 0; g * d.cp < pairs; ++g) {
-        const int prs = std::min(d.cp, pairs - g * d.cp), op0 = (int)ops.size();
-        const int loaded = std::min(2 * prs, cin_chunks - 2 * g * d.cp);
-        // a pair whose second chunk does not exist multiplies zero weights in its second half
+        const int prs = std::min(d.cp, pairs - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
+        const int loaded = std::min(2 * prs, cin_chunks - c0);
         for (int i = 0; i < prs; ++i)
-          ops.push_back(SchedOp{t, 2 * i, 2 * i + 1 < loaded ? t : -1, 2 * i + 1 < loaded ? 2 * i + 1 : 0});
-        push_kb(2 * g * d.cp, loaded, t, op0);
+          ops.push_back(2 * i + 1 < loaded ? SchedOp{2 * i, c0 + 2 * i, t, 2 * i + 1, c0 + 2 * i + 1, t}
+                                           : SchedOp{2 * i, c0 + 2 * i, t, 0, -1, 0});
+        push_kb(c0, loaded, t, 1, op0);
       }
     }
   }
@@ -192,7 +213,7 @@ struct ConvLaunch {
   ConvParams p;
   dim3 grid;
   int smem;
-  int mode, stages;
+  int mode, stages, threads;
 };
 
 int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, ConvLaunch& L,
@@ -203,7 +224,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     return -1;
   };
   if (batch < 1) return bad("batch < 1");
-  if (d.mode < IXB_MODE_WINDOW || d.mode > IXB_MODE_STEM) return bad("unknown conv mode");
+  if (d.mode < IXB_MODE_WINDOW || d.mode > IXB_MODE_IM2COL) return bad("unknown conv mode");
   if (!(d.k == 1 || d.k == 3) || !(d.stride == 1 || d.stride == 2)) return bad("k must be 1 or 3, stride 1 or 2");
   if (d.nseg < 1 || d.nseg > IXB_MAX_SEGS) return bad("1..4 input segments");
   const int pad = d.k / 2;
@@ -238,18 +259,28 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     if (sh != d.in_h || sw != d.in_w) return bad("input segment size differs from the conv input size");
     if (s.up2 && (d.mode != IXB_MODE_GATHER || d.k != 1 || d.stride != 1))
       return bad("an up2 input needs GATHER mode and a 1x1 stride-1 conv");
-    if (d.mode == IXB_MODE_WINDOW && s.up2) return bad("WINDOW mode reads no up2 input");
     p.seg[i] = seg_dev(s, arena, chunk);
-    chunk += p.seg[i].chunks;
+    chunk += image ? 1 : p.seg[i].chunks;
     cin += s.channels;
   }
   if (cin != d.cin) return bad("segment channels do not add up to cin");
-  if (d.mode == IXB_MODE_STEM) {
-    if (d.k != 3 || d.stride != 2 || d.nseg != 1 || d.cin != 3 || d.seg[0].channels != 3 || d.cp != 2)
-      return bad("STEM mode is a 3x3 stride-2 conv of the 3-channel 4-byte-pixel image with cp = 2");
-    if (d.in_h % 2 || d.in_w % 2) return bad("STEM needs an even input size");
+  switch (d.mode) {
+    case IXB_MODE_WINDOW:
+      if (d.stride != 1) return bad("WINDOW mode is stride 1");
+      break;
+    case IXB_MODE_STEM:
+      if (d.k != 3 || d.stride != 2 || d.nseg != 1 || d.cin != 3 || d.in_h % 2 || d.in_w % 2)
+        return bad("STEM mode is a 3x3 stride-2 conv of the 3-channel image with an even size");
+      break;
+    case IXB_MODE_IM2COL:
+      if (d.k != 3 || d.stride != 2 || d.nseg != 1 || d.in_h % 2 || d.in_w % 2 || !p.seg[0].plane_images)
+        return bad("IM2COL mode is a 3x3 stride-2 conv of one view with whole-image plane strides and an even size");
+      if (d.in_w + 2 > 256 * 16 || d.in_h + 2 > 65535) return bad("IM2COL input too large");
+      break;
+    default:
+      if (d.k != 1 || d.stride != 1) return bad("GATHER mode is a 1x1 stride-1 conv");
+      break;
   }
-  if (d.mode == IXB_MODE_WINDOW && d.stride != 1) return bad("WINDOW mode is stride 1");
   p.cin_chunks = chunk;
   if (d.mode == IXB_MODE_WINDOW) {
     p.win_origin = pad * (d.in_w + 2) + pad;
@@ -258,21 +289,18 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.win_origin = 0;
     p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * d.out_w);
   }
-  if ((long long)batch * (d.in_h + 2) * (d.in_w + 2) >= 0x7fff0000LL)
+  if ((long long)batch * (d.in_h + 2) * (d.in_w + 4) >= 0x7fff0000LL)
     return bad("more pixels than 32-bit pixel indices cover");
   std::vector<SchedKB> kbs;
   std::vector<SchedOp> ops;
   build_schedule(d, chunk, kbs, ops);
   if ((int)kbs.size() > kMaxKBlocks) return bad("too many K-blocks for the schedule table");
   p.kblocks = (int)kbs.size();
-  p.taps_per_block = 0;
-  p.pair_groups = 0;
   int slots = 0, b_stage_max = 0;
   for (const SchedKB& k : kbs) {
-    slots = std::max(slots, k.nchunks);
+    slots = std::max(slots, k.nchunks * k.ntaps);
     b_stage_max = std::max(b_stage_max, k.b_bytes);
   }
-  p.b_stage_max = b_stage_max;
   const int b_total = kbs.back().b_off + kbs.back().b_bytes;
   const long long ntiles = d.cout / d.n_tile;
   if ((unsigned long long)ntiles * b_total != d.w_bytes) {
@@ -296,7 +324,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     }
   }
   p.b_block_bytes = b_stage_max;
-  const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * 512 * 16);  // barriers, table, bias, rows
+  const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_GATHER ? 2 * 512 * 16 : 0);  // barriers, table, bias, rows
   const int budget = kSmemLimit - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
@@ -317,10 +345,13 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   p.m_tiles = (int)((p.m_total + p.tile_rows - 1) / p.tile_rows);
   p.tbl_off = p.a_off + p.stages * p.stage_bytes;
-  p.bar_off = p.tbl_off + (d.mode == IXB_MODE_WINDOW ? 0 : 2 * p.tile_rows * 16);
+  p.bar_off = p.tbl_off + (d.mode == IXB_MODE_GATHER ? 2 * p.tile_rows * 16 : 0);
   p.lut_off = p.bar_off + 512;
   p.bias_off = p.lut_off + 256;
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
+  if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.tile_rows > 1024)
+    return bad("an im2col load carries at most 1024 pixels");
+  p.issuers = p.mt >= 2 ? 2 : 1;
   p.w_ntile_stride = (long long)b_total;
   p.wpack = arena + d.w_offset;
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
@@ -336,7 +367,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.tmem_cols = cols;
   p.idesc = umma_idesc_s8(kBlockM, d.n_tile);
   {
-    // kernel op table: A start / LBO from (tap, slot) and the geometry, deduplicated per K-block
+    // kernel op table: A start / LBO from (slot, tap) and the geometry, deduplicated per K-block
     auto shift_of = [&](int t) { return d.mode == IXB_MODE_WINDOW ? (t / d.k) * (d.in_w + 2) + (t % d.k) : 0; };
     std::vector<uint32_t> ta;
     std::vector<uint16_t> tb;
@@ -348,7 +379,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
         const SchedOp& op = ops[k.op0 + o];
         const int a_start = op.slot0 * p.rowsA + shift_of(op.tap0);
         int lbo = 1;
-        if (op.tap1 >= 0) lbo = op.slot1 * p.rowsA + shift_of(op.tap1) - a_start;
+        if (op.chunk1 >= 0) lbo = op.slot1 * p.rowsA + shift_of(op.tap1) - a_start;
         if (lbo <= 0 || lbo >= (1 << 14) || a_start >= (1 << 14)) return bad("MMA operand offsets out of range");
         // rows read: a_start .. a_start + tile_rows - 1 (+ lbo for the second K-half), within the A region + 16
         if ((long long)(a_start + lbo + p.tile_rows) * 16 > p.a_stage_bytes)
@@ -356,7 +387,6 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
         ka.push_back((uint32_t)a_start | ((uint32_t)lbo << 16));
         kbv.push_back((uint16_t)(o * d.n_tile * 32 / 16));
       }
-      // reuse an identical run already in the table
       int found = -1;
       for (size_t st = 0; st + ka.size() <= ta.size() && found < 0; ++st) {
         bool eq = true;
@@ -376,8 +406,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
       kd.nops = (int16_t)k.nops;
       kd.chunk0 = (int16_t)k.chunk0;
       kd.nchunks = (int16_t)k.nchunks;
-      kd.tap = (int16_t)k.tap;
-      kd.pad_ = 0;
+      kd.tap0 = (int16_t)k.tap0;
+      kd.ntaps = (int16_t)k.ntaps;
     }
     for (size_t i = 0; i < ta.size(); ++i) {
       p.op_a[i] = ta[i];
@@ -414,13 +444,10 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.egress_img = (long long)d.egress_image_bytes;
   }
   if (d.mode == IXB_MODE_WINDOW) {
-    // every view shares the padded geometry the flattened pixel index walks
     auto same = [&](const ixb_segment& s) { return s.height == d.in_h && s.width == d.in_w; };
     for (int i = 0; i < d.nseg; ++i)
       if (!same(d.seg[i])) return bad("WINDOW views must share the input geometry");
     if (!d.out_nchw && !same(d.out)) return bad("WINDOW output must share the input geometry");
-  }
-  if (d.mode == IXB_MODE_WINDOW) {
     // every window copy stays inside the planes' zero guards
     for (int i = 0; i < d.nseg; ++i) {
       const long long end = (long long)p.m_tiles * p.tile_rows + p.win_origin;
@@ -429,13 +456,65 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     }
   }
   const int smem = p.bias_off + 4 * d.n_tile + 1024;
-  const int per_sm = 1;
-  const long long gm =
-      std::max<long long>(1, std::min<long long>(p.m_tiles, ((long long)sms * per_sm + ntiles - 1) / ntiles));
+  const long long gm = std::max<long long>(1, std::min<long long>(p.m_tiles, ((long long)sms + ntiles - 1) / ntiles));
   L.grid = dim3((unsigned)gm, (unsigned)ntiles, 1);
   L.smem = smem;
   L.mode = d.mode;
   L.stages = p.stages;
+  L.threads = conv_threads(d.mode);
+  return 0;
+}
+
+// The TMA im2col map of an IM2COL or STEM conv (needs the driver; done at launch, not in the checks).
+// IM2COL: the view's chunk planes as one 4-D tensor {16 B, W+2, H+2, images}: chunk c of image n is
+// image c * plane_images + n; corners 0 / -2 and element strides 2 walk the 3x3 stride-2 windows.
+// STEM: the image plane as 16-byte pixel pairs {16 B, (W+4)/2, H+2, batch}: element strides (1, 2).
+int encode_im2col(ConvLaunch& L, const ixb_conv_desc& d, uint8_t* arena, int batch, std::string& err) {
+  static PFN_cuTensorMapEncodeIm2col_v12000 enc = nullptr;
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", (void**)&enc, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !enc) {
+      enc = nullptr;
+      err = "cuTensorMapEncodeIm2col is not available";
+      return -1;
+    }
+  }
+  ConvParams& p = L.p;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t es[4];
+  void* base;
+  if (d.mode == IXB_MODE_IM2COL) {
+    const SegDev& s = p.seg[0];
+    base = const_cast<int8_t*>(s.base);
+    dims[0] = 16;
+    dims[1] = (cuuint64_t)(s.W + 2);
+    dims[2] = (cuuint64_t)(s.H + 2);
+    dims[3] = (cuuint64_t)((long long)(s.chunks - 1) * s.plane_images + batch);
+    strides[0] = 16;
+    strides[1] = (cuuint64_t)(s.W + 2) * 16;
+    strides[2] = (cuuint64_t)s.P * 16;
+    es[0] = 1; es[1] = 2; es[2] = 2; es[3] = 1;
+  } else {
+    const ixb_segment& s = d.seg[0];
+    base = arena + s.offset;
+    dims[0] = 16;
+    dims[1] = (cuuint64_t)((s.width + 4) / 2);
+    dims[2] = (cuuint64_t)(s.height + 2);
+    dims[3] = (cuuint64_t)batch;
+    strides[0] = 16;
+    strides[1] = (cuuint64_t)(s.width + 4) * 8;
+    strides[2] = (cuuint64_t)(s.height + 2) * (s.width + 4) * 8;
+    es[0] = 1; es[1] = 1; es[2] = 2; es[3] = 1;
+  }
+  int lower[2] = {0, 0}, upper[2] = {-2, -2};
+  CUresult r = enc(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, lower, upper, 16,
+                   (cuuint32_t)p.tile_rows, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeIm2col failed (" + std::to_string((int)r) + ")";
+    return -1;
+  }
   return 0;
 }
 
@@ -446,7 +525,7 @@ int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
     IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     configured = true;
   }
-  conv_kernel<MODE><<<L.grid, kConvThreads, L.smem, st>>>(L.p);
+  conv_kernel<MODE><<<L.grid, conv_threads(MODE), L.smem, st>>>(L.p);
   IXB_CUDA(cudaGetLastError());
   return 0;
 }
@@ -455,8 +534,17 @@ int launch_conv(const ConvLaunch& L, cudaStream_t st) {
   switch (L.mode) {
     case IXB_MODE_WINDOW: return launch_conv_m<IXB_MODE_WINDOW>(L, st);
     case IXB_MODE_GATHER: return launch_conv_m<IXB_MODE_GATHER>(L, st);
+    case IXB_MODE_IM2COL: return launch_conv_m<IXB_MODE_IM2COL>(L, st);
     default: return launch_conv_m<IXB_MODE_STEM>(L, st);
   }
+}
+
+// Host checks, then (for im2col modes) the tensor map: everything a launch needs.
+int prepare_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, ConvLaunch& L,
+                 std::string& err) {
+  if (build_conv(d, arena, arena_bytes, batch, L, err)) return -1;
+  if (d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) return encode_im2col(L, d, arena, batch, err);
+  return 0;
 }
 
 struct PoolLaunch {
@@ -557,7 +645,7 @@ struct ixb_session {
     std::vector<PoolLaunch> pl(pools.size());
     std::string err;
     for (size_t i = 0; i < convs.size(); ++i)
-      if (build_conv(convs[i], arena, arena_bytes, batch, cl[i], err))
+      if (prepare_conv(convs[i], arena, arena_bytes, batch, cl[i], err))
         return fail(IXB_ERR_INVALID, "conv " + std::to_string(i) + ": " + err);
     for (size_t i = 0; i < pools.size(); ++i)
       if (build_pool(pools[i], arena, arena_bytes, batch, pl[i], err))
@@ -819,7 +907,7 @@ int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, in
   if (!d || !arena) return fail(IXB_ERR_INVALID, "null argument");
   ConvLaunch L;
   std::string err;
-  if (build_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
+  if (prepare_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
   return launch_conv(L, static_cast<cudaStream_t>(stream));
 }
 
@@ -828,7 +916,7 @@ int ixb_conv_layer_stats(const ixb_conv_desc* d, void* arena, uint64_t arena_byt
   if (!d || !arena || !stats) return fail(IXB_ERR_INVALID, "null argument");
   ConvLaunch L;
   std::string err;
-  if (build_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
+  if (prepare_conv(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
   if ((int64_t)L.grid.x * L.grid.y * kStatWords > stats_words) return fail(IXB_ERR_INVALID, "stats buffer too small");
   L.p.stats = reinterpret_cast<unsigned long long*>(stats);
   return launch_conv(L, static_cast<cudaStream_t>(stream));
@@ -839,21 +927,21 @@ int ixb_conv_schedule(const ixb_conv_desc* d, int32_t* kb_out, int max_kb, int32
   int chunks = 0;
   for (int i = 0; i < d->nseg && i < IXB_MAX_SEGS; ++i) chunks += (d->seg[i].channels + 15) / 16;
   if (d->mode == IXB_MODE_STEM) chunks = 1;
-  if (d->n_tile < 16 || d->k < 1 || d->cp < 1) return fail(IXB_ERR_INVALID, "bad conv shape");
+  if (d->n_tile < 16 || d->k < 1 || d->cp < 1 || d->mode < 0 || d->mode > IXB_MODE_IM2COL)
+    return fail(IXB_ERR_INVALID, "bad conv shape");
   std::vector<SchedKB> kbs;
   std::vector<SchedOp> ops;
   build_schedule(*d, chunks, kbs, ops);
   if ((int)kbs.size() > max_kb || (int)ops.size() > max_ops) return fail(IXB_ERR_INVALID, "schedule buffers too small");
   for (size_t i = 0; i < kbs.size(); ++i) {
     const SchedKB& k = kbs[i];
-    const int32_t v[8] = {k.chunk0, k.nchunks, k.tap, k.op0, k.nops, k.b_off, k.b_bytes, 0};
+    const int32_t v[8] = {k.chunk0, k.nchunks, k.tap0, k.ntaps, k.op0, k.nops, k.b_off, k.b_bytes};
     for (int j = 0; j < 8; ++j) kb_out[8 * i + j] = v[j];
   }
   for (size_t i = 0; i < ops.size(); ++i) {
-    ops_out[4 * i] = ops[i].tap0;
-    ops_out[4 * i + 1] = ops[i].slot0;
-    ops_out[4 * i + 2] = ops[i].tap1;
-    ops_out[4 * i + 3] = ops[i].slot1;
+    const SchedOp& o = ops[i];
+    const int32_t v[6] = {o.slot0, o.chunk0, o.tap0, o.slot1, o.chunk1, o.tap1};
+    for (int j = 0; j < 6; ++j) ops_out[6 * i + j] = v[j];
   }
   return (int)kbs.size();
 }

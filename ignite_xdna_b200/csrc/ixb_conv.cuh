@@ -10,39 +10,42 @@
 // sat_u8(rne(bias_acc + sum w * q)) - 128 exactly.
 //
 // Storage: one plane per 16-channel chunk, [batch][H+2][W+2] pixels of 16 bytes with a zero
-// halo ring per image and zero guard pixels around the plane. A K-chunk of 128 output pixels is
-// then 128 contiguous 16-byte rows in global memory, which is exactly a column of UMMA core
-// matrices in shared memory.
+// halo ring per image and zero guard pixels around the plane; plane strides are whole images,
+// so a tensor map can address chunk c, image n as image c * (plane / image) + n. A K-chunk of
+// 128 output pixels is then 128 rows of 16 bytes, a column of UMMA core matrices in smem.
 //
 // GEMM view: M = output pixels, N = output channels (n_tile per CTA, one TMEM column each),
-// K = input channels x taps in 32-byte steps. A tile is MT blocks of 128 pixels; block b
-// accumulates into TMEM columns [b * n_tile, (b+1) * n_tile).
-//  * WINDOW (stride 1, same resolution): the tile is 128*MT consecutive pixels of the
-//    flattened padded image; tap (ky, kx) of output pixel m reads padded pixel
-//    m + (ky-1)(W+2) + (kx-1), so ONE window of 128*MT + 2((W+2)+1) pixels per chunk feeds all
-//    nine taps: each tap is the same smem window seen through a descriptor whose start moves
-//    16 bytes per pixel of shift. A window is one contiguous bulk copy (TMA engine) per chunk,
-//    issued by a single producer thread. Halo outputs are computed and dropped.
-//  * GATHER (stride 2, or an input read through a nearest-2x upsample): the tile is 128*MT
-//    interior output pixels; 128 producer threads gather each tap's rows with 16-byte cp.async
-//    from a per-tile table of output coordinates.
-//  * STEM: the 3-channel image stored as 4-byte pixels; one 16-byte K-chunk is 4 pixels x
-//    4 channels of one input row, so K = 3 rows x 16 bytes (+16 zero-weight bytes) covers the
-//    3x3 stride-2 window.
-// Shared-memory operands use the K-major no-swizzle core-matrix layout: A as
-// [chunk][pixel][16 B] (SBO 128 B, LBO = rows x 16 B), B as [n/8][chunk][8][16 B]
-// (SBO 256 B, LBO 128 B), prepacked on the host so one bulk copy lands a K-block.
+// K = input channels x taps in 32-byte MMA steps. A tile is MT blocks of 128 pixels; block b
+// accumulates into TMEM columns [b * n_tile, (b+1) * n_tile). A-operand producers by mode:
+//  * WINDOW (stride 1, same resolution): the tile is 128*MT consecutive pixels of the flattened
+//    padded image; tap (ky, kx) of output pixel m reads padded pixel m + (ky-1)(W+2) + (kx-1), so
+//    ONE window of 128*MT + 2((W+2)+1) pixels per chunk feeds all nine taps, each tap the same smem
+//    window through a descriptor whose start moves 16 bytes per pixel of shift. A window is one
+//    bulk copy (TMA engine) per chunk. Halo outputs are computed and dropped.
+//  * IM2COL (3x3 stride 2): the tile is 128*MT interior output pixels; per (tap, chunk) one TMA
+//    im2col load walks the filter positions (element stride 2, corners 0/-2 on the padded plane)
+//    and lands the tile's rows for that tap.
+//  * STEM: the image stored as 8-byte pixels (3 channels + 5 zero) and read as 16-byte pixel pairs;
+//    output pixel (y, x) tap (ky, pair p) is the pair at padded row 2y+ky, column 2x+2p: six TMA
+//    im2col loads (3 rows x 2 pairs) cover the 3x3 stride-2 window.
+//  * GATHER (a 1x1 conv over a concat that includes a nearest-2x upsampled view): per-row 16-byte
+//    cp.async gathers by 128 producer threads from a per-tile table of output coordinates.
+// Shared-memory operands use the K-major no-swizzle core-matrix layout: A as [slot][pixel][16 B]
+// (SBO 128 B), B as [n/8][K-half][8][16 B] (SBO 256 B, LBO 128 B), prepacked on the host in the
+// schedule's order. Each MMA's A descriptor carries its own start and LBO: the two 32-byte K-halves
+// are two A slots (two chunks of one tap, or one chunk at two taps).
 //
-// The kernel is persistent and warp-specialised (416 threads):
-//   warps 0-7   epilogue: TMEM -> registers -> integer epilogue -> global; warp w reads TMEM
-//               lane quarter w % 4, warpgroups 0 and 1 split the (block, 16-column) pieces
-//   warps 8-11  producers: A loads into a ring of stages, completion on the stage mbarrier;
-//               producer 0 also bulk-copies streamed weights
-//   warp 12     one thread issues tcgen05.mma and commits stages and accumulators
-// Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next. When a
-// CTA's weights fit, they are loaded once and stay resident in shared memory.
+// The kernel is persistent and warp-specialised:
+//   epilogue warps (12, or 8 for GATHER): TMEM -> registers -> integer epilogue -> global; warp w
+//            reads TMEM lane quarter w % 4, the warpgroups take alternate (block, 16-column) pieces
+//   producer: one thread issuing bulk / TMA copies (4 warps of cp.async for GATHER)
+//   two MMA warps: one thread each issues tcgen05.mma for alternate 128-row blocks (a single
+//            issuer alone reaches only ~55-70 cycles per small-N MMA, two reach ~40)
+// Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next. When a CTA's
+// weights fit, they are loaded once and stay resident in shared memory.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include "ixb_ptx.cuh"
 #include "../../include/ixb200.h"
 
@@ -53,27 +56,30 @@ struct SegDev {
   long long plane;     // bytes between chunk planes
   int chunk_begin, chunks;  // 16-channel chunks of the logical input this view supplies
   int H, W, up2, P;         // stored size, upsampled view, padded pixels per image
+  int plane_images;         // plane stride in images
 };
 
-// One K-block: which input chunks its A stage holds (slots 0..nchunks-1 = chunks chunk0..), the tap
-// a gather reads, its MMAs (op0 .. op0+nops-1 of the op table) and its weights.
+// One K-block: its A slots (slot s holds chunk chunk0 + s / ntaps at tap tap0 + s % ntaps; for
+// WINDOW ntaps = 1 and the taps live in the MMA ops as window shifts), its MMAs (op0 .. op0+nops-1
+// of the op table) and its weights.
 struct KBlockDev {
   int b_off, b_bytes;
-  int16_t op0, nops, chunk0, nchunks, tap, pad_;
+  int16_t op0, nops, chunk0, nchunks, tap0, ntaps;
 };
 constexpr int kMaxKBlocks = 96;
 constexpr int kMaxOps = 160;
 
 struct ConvParams {
+  alignas(64) CUtensorMap tmap;  // TMA im2col map (IM2COL, STEM)
   int mode, k, stride, pad;
   int H, W, Ho, Wo, batch;
   int m_total;
-  int cin_chunks, cp, kblocks, taps_per_block, pair_groups;
+  int cin_chunks, cp, kblocks;
   int mt, tile_rows, m_tiles;
   int rowsA, win_origin;
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
   int b_resident, a_off, tbl_off, bar_off, lut_off, bias_off;
-  int n_tile, acc_cols, tmem_cols;
+  int n_tile, acc_cols, tmem_cols, issuers;
   uint32_t idesc;
   int nseg;
   SegDev seg[IXB_MAX_SEGS];
@@ -92,7 +98,6 @@ struct ConvParams {
   int cout;
   FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wo, Wo
   unsigned long long* stats;          // optional per-CTA role counters (kStatWords per CTA), or null
-  int b_stage_max;                    // largest K-block of weights (stage B region when streamed)
   KBlockDev kb[kMaxKBlocks];          // the K schedule
   uint32_t op_a[kMaxOps];             // per MMA: A start (16-byte units from the stage) | LBO (16-byte units) << 16
   uint16_t op_b[kMaxOps];             // per MMA: B start (16-byte units from the K-block's weights)
@@ -102,9 +107,9 @@ struct ConvParams {
 enum : int {
   kStatEpiWait = 0,   // epilogue warp 0 waiting for an accumulator
   kStatEpiWork,       // epilogue warp 0 draining accumulators
-  kStatMmaWaitFull,   // MMA thread waiting for loaded stages
-  kStatMmaWaitAcc,    // MMA thread waiting for a free accumulator
-  kStatMmaIssue,      // MMA thread issuing
+  kStatMmaWaitFull,   // MMA issuer 0 waiting for loaded stages
+  kStatMmaWaitAcc,    // MMA issuer 0 waiting for a free accumulator
+  kStatMmaIssue,      // MMA issuer 0 issuing
   kStatProdWait,      // producer 0 waiting for free stages
   kStatProdWork,      // producer 0 issuing loads
   kStatTotal,         // CTA lifetime
@@ -112,12 +117,13 @@ enum : int {
   kStatWords = 16
 };
 
-constexpr int kEpiWarps = 8;
-constexpr int kProducerWarp0 = 8;
-constexpr int kProducerThreads = 128;
-constexpr int kMmaWarp = 12;
-constexpr int kConvThreads = 416;
 constexpr int kBlockM = 128;
+// Warp layout per mode.
+__host__ __device__ constexpr int epi_warps(int mode) { return mode == IXB_MODE_GATHER ? 8 : 12; }
+__host__ __device__ constexpr int prod_warps(int mode) { return mode == IXB_MODE_GATHER ? 4 : 1; }
+__host__ __device__ constexpr int mma_warp0(int mode) { return epi_warps(mode) + prod_warps(mode); }
+__host__ __device__ constexpr int conv_threads(int mode) { return 32 * (mma_warp0(mode) + 2); }
+constexpr int kGatherThreads = 128;
 
 __device__ __forceinline__ void producer_bar_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -131,21 +137,40 @@ __device__ __forceinline__ int seg_of_chunk(const ConvParams& p, int gc) {
   return si;
 }
 
-// Round half to even of x / 2^s, s in [1, 16], without branches: the floor of
-// (x + 2^(s-1) - 1 + bit s of x) / 2^s.
-__device__ __forceinline__ int rne_pos(int x, int s, int half_m1) { return (x + half_m1 + ((x >> s) & 1)) >> s; }
+// TMA im2col load of the map's pixelsPerColumn rows, 16 bytes each, completing on bar.
+__device__ __forceinline__ void tma_im2col(void* dst, const CUtensorMap* tm, int w, int h, int n, int off_w, int off_h,
+                                           uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(0), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"((uint16_t)off_w), "h"((uint16_t)off_h)
+      : "memory");
+}
+
+__device__ __forceinline__ void write_stats(const ConvParams& p, int idx, unsigned long long v) {
+  if (p.stats) p.stats[(blockIdx.y * gridDim.x + blockIdx.x) * kStatWords + idx] = v;
+}
 
 // ---------------------------------------------------------------- producers
+// One thread: bulk (WINDOW) or TMA im2col (IM2COL, STEM) copies per K-block, plus streamed weights.
 template <int MODE>
-__device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+__device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                                int ntile) {
   const int S = p.stages;
-  const uint32_t chunk_bytes = (uint32_t)p.rowsA * 16;
+  const uint32_t slot_bytes = (uint32_t)p.rowsA * 16;
   int stage = 0;
   uint32_t ph = 0;
   long long tw = 0, tk = 0;
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
-    const long long wb = (long long)t * p.tile_rows - p.win_origin;
+    const int m0 = t * p.tile_rows;
+    const long long wb = (long long)m0 - p.win_origin;
+    int img0 = 0, y0 = 0, x0 = 0;
+    if (MODE != IXB_MODE_WINDOW) {
+      img0 = (int)fdiv((uint32_t)m0, p.fd_hw);
+      const int rem = m0 - img0 * (int)p.fd_hw.d;
+      y0 = (int)fdiv((uint32_t)rem, p.fd_Wo);
+      x0 = rem - y0 * p.Wo;
+    }
     for (int kb = 0; kb < p.kblocks; ++kb) {
       const long long c0 = clock64();
       mbar_wait(&empty[stage], ph ^ 1);
@@ -153,13 +178,23 @@ __device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* sme
       tw += c1 - c0;
       uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
       const KBlockDev& K = p.kb[kb];
-      uint32_t bytes = (uint32_t)K.nchunks * chunk_bytes + (p.b_resident ? 0u : (uint32_t)K.b_bytes);
-      mbar_arrive_expect_tx(&full[stage], bytes);
-      for (int c = 0; c < K.nchunks; ++c) {
-        const int gc = K.chunk0 + c;
-        const SegDev& s = p.seg[seg_of_chunk(p, gc)];
-        bulk_g2s(As + c * chunk_bytes, s.base + (long long)(gc - s.chunk_begin) * s.plane + wb * 16, chunk_bytes,
-                 &full[stage]);
+      const int nslots = K.nchunks * K.ntaps;
+      mbar_arrive_expect_tx(&full[stage], (uint32_t)nslots * (MODE == IXB_MODE_WINDOW ? slot_bytes : p.tile_rows * 16u) +
+                                              (p.b_resident ? 0u : (uint32_t)K.b_bytes));
+      for (int sl = 0; sl < nslots; ++sl) {
+        const int gc = K.chunk0 + sl / K.ntaps;
+        const int tap = K.tap0 + sl % K.ntaps;
+        if (MODE == IXB_MODE_WINDOW) {
+          const SegDev& s = p.seg[seg_of_chunk(p, gc)];
+          bulk_g2s(As + sl * slot_bytes, s.base + (long long)(gc - s.chunk_begin) * s.plane + wb * 16, slot_bytes,
+                   &full[stage]);
+        } else if (MODE == IXB_MODE_IM2COL) {
+          const SegDev& s = p.seg[0];
+          tma_im2col(As + sl * slot_bytes, &p.tmap, 2 * x0, 2 * y0, (gc - s.chunk_begin) * s.plane_images + img0,
+                     tap % 3, tap / 3, &full[stage]);
+        } else {  // STEM: tap = 2 * ky + pair
+          tma_im2col(As + sl * slot_bytes, &p.tmap, x0, 2 * y0, img0, tap & 1, tap >> 1, &full[stage]);
+        }
       }
       if (!p.b_resident)
         bulk_g2s(As + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + K.b_off, K.b_bytes, &full[stage]);
@@ -170,49 +205,35 @@ __device__ __forceinline__ void produce_window(const ConvParams& p, uint8_t* sme
       }
     }
   }
-  if (p.stats) {
-    unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
-    st[kStatProdWait] = tw;
-    st[kStatProdWork] = tk;
-  }
+  write_stats(p, kStatProdWait, tw);
+  write_stats(p, kStatProdWork, tk);
 }
 
-template <int MODE>
+// 128 threads: 16-byte cp.async row gathers (a concat including an upsampled view).
 __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                                int ntile, int ptid) {
   const int nch = 2 * p.cp;
-  const int c = ptid % nch;  // 128 is a multiple of nch, so each thread keeps one chunk
-  const int step = kProducerThreads / nch;
+  const int c = ptid % nch;  // 128 is a multiple of nch, so each thread keeps one slot
+  const int step = kGatherThreads / nch;
   const int S = p.stages;
   const int hw = p.Ho * p.Wo;
-  // Per tile, one row table entry per output pixel: {pixel of tap (0, 0) in the first view's
-  // padded geometry, image, y, x}; pixel -1 marks rows past the batch.
+  // Per tile, one row table entry per output pixel: {image, y, x}; image -1 marks rows past the batch.
   int4* tbl = reinterpret_cast<int4*>(smem + p.tbl_off);
   long long tw = 0;
   const long long cstart = clock64();
-  const SegDev& s0 = p.seg[0];
-  const int W2_0 = s0.W + 2;
   int stage = 0;
   uint32_t ph = 0;
   int it = 0;
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x, ++it) {
     const int m0 = t * p.tile_rows;
     int4* T = tbl + (it & 1) * p.tile_rows;
-    for (int r = ptid; r < p.tile_rows; r += kProducerThreads) {
+    for (int r = ptid; r < p.tile_rows; r += kGatherThreads) {
       const int m = m0 + r;
       if (m < p.m_total) {
         const int img = (int)fdiv((uint32_t)m, p.fd_hw);
         const int rem = m - img * hw;
         const int y = (int)fdiv((uint32_t)rem, p.fd_Wo);
-        const int x = rem - y * p.Wo;
-        int base;
-        if (MODE == IXB_MODE_STEM)
-          base = img * s0.P + 2 * y * W2_0 + 2 * x;   // padded row 2y + ky, padded column 2x
-        else if (s0.up2)
-          base = img * s0.P + ((y >> 1) + 1) * W2_0 + (x >> 1) + 1;
-        else
-          base = img * s0.P + (y * p.stride - p.pad + 1) * W2_0 + (x * p.stride - p.pad + 1);
-        T[r] = make_int4(base, img, y, x);
+        T[r] = make_int4(img, y, rem - y * p.Wo, 0);
       } else {
         T[r] = make_int4(-1, 0, 0, 0);
       }
@@ -221,59 +242,26 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
     for (int kb = 0; kb < p.kblocks; ++kb) {
       const long long c0 = clock64();
       mbar_wait(&empty[stage], ph ^ 1);
-      const long long c1 = clock64();
-      tw += c1 - c0;
+      tw += clock64() - c0;
       uint8_t* dst = smem + p.a_off + stage * p.stage_bytes + c * p.rowsA * 16;
-      if (MODE == IXB_MODE_STEM) {
-        if (c < 3) {
-          const int8_t* cb = s0.base + (long long)c * W2_0 * 4;
-          for (int r = ptid / nch; r < p.tile_rows; r += step) {
-            const int pb = T[r].x;
-            if (pb >= 0) {
-              const int8_t* src = cb + (long long)pb * 4;
-              cp_async8(dst + r * 16, src, 8u);
-              cp_async8(dst + r * 16 + 8, src + 8, 8u);
-            } else {
-              cp_async16(dst + r * 16, s0.base, 0u);
-            }
-          }
-        }
-      } else {
-        const KBlockDev& K = p.kb[kb];
-        const int tap = K.tap;
-        const int gc = c < K.nchunks ? K.chunk0 + c : -1;
-        const int ky = tap / p.k, kx = tap - (tap / p.k) * p.k;
-        const int si = gc >= 0 ? seg_of_chunk(p, gc) : -1;
-        if (si >= 0) {
-          const SegDev& s = p.seg[si];
-          const int8_t* cbase = s.base + (long long)(gc - s.chunk_begin) * s.plane;
-          if (si == 0 || (s.up2 == s0.up2 && s.W == s0.W && s.P == s0.P)) {
-            // same geometry as the first view: the table's pixel base plus the tap offset
-            const int8_t* tb = cbase + (long long)(ky * (s.W + 2) + kx) * 16;
-            for (int r = ptid / nch; r < p.tile_rows; r += step) {
-              const int pb = T[r].x;
-              cp_async16(dst + r * 16, pb >= 0 ? tb + (long long)pb * 16 : s.base, pb >= 0 ? 16u : 0u);
-            }
+      const KBlockDev& K = p.kb[kb];
+      const int gc = c < K.nchunks ? K.chunk0 + c : -1;
+      const int si = gc >= 0 ? seg_of_chunk(p, gc) : -1;
+      if (si >= 0) {
+        const SegDev& s = p.seg[si];
+        const int8_t* cbase = s.base + (long long)(gc - s.chunk_begin) * s.plane;
+        for (int r = ptid / nch; r < p.tile_rows; r += step) {
+          const int4 e = T[r];
+          if (e.x >= 0) {
+            const int iy = s.up2 ? (e.y >> 1) : e.y, ix = s.up2 ? (e.z >> 1) : e.z;
+            cp_async16(dst + r * 16, cbase + ((long long)e.x * s.P + (iy + 1) * (s.W + 2) + (ix + 1)) * 16, 16u);
           } else {
-            for (int r = ptid / nch; r < p.tile_rows; r += step) {
-              const int4 e = T[r];
-              if (e.x >= 0) {
-                int iy = e.z * p.stride + ky - p.pad, ix = e.w * p.stride + kx - p.pad;
-                if (s.up2) {
-                  iy >>= 1;
-                  ix >>= 1;
-                }
-                cp_async16(dst + r * 16, cbase + ((long long)e.y * s.P + (iy + 1) * (s.W + 2) + (ix + 1)) * 16, 16u);
-              } else {
-                cp_async16(dst + r * 16, s.base, 0u);
-              }
-            }
+            cp_async16(dst + r * 16, s.base, 0u);
           }
         }
       }
       cp_async_mbar_arrive(&full[stage]);
       if (!p.b_resident && ptid == 0) {
-        const KBlockDev& K = p.kb[kb];
         mbar_arrive_expect_tx(&full[stage], K.b_bytes);
         bulk_g2s(smem + p.a_off + stage * p.stage_bytes + p.a_stage_bytes, p.wpack + ntile * p.w_ntile_stride + K.b_off,
                  K.b_bytes, &full[stage]);
@@ -284,10 +272,72 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
       }
     }
   }
-  if (p.stats && ptid == 0) {
-    unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
-    st[kStatProdWait] = tw;
-    st[kStatProdWork] = clock64() - cstart - tw;
+  if (ptid == 0) {
+    write_stats(p, kStatProdWait, tw);
+    write_stats(p, kStatProdWork, clock64() - cstart - tw);
+  }
+}
+
+// ---------------------------------------------------------------- MMA issuer
+// Issuer `who` of `p.issuers` issues the MMAs of blocks b = who, who + issuers, ... of every tile.
+template <int MODE>
+__device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                          uint64_t* acc_full, uint64_t* acc_empty, uint64_t* bres_bar, uint32_t tmem,
+                                          int who) {
+  if (p.b_resident) mbar_wait(bres_bar, 0);
+  const int S = p.stages;
+  int stage = 0, acc = 0;
+  uint32_t ph = 0, aph = 0;
+  long long wf = 0, wa = 0, wi = 0;
+  const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);  // SBO 128 B, sm_100 descriptor
+  for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+    long long c0 = clock64();
+    mbar_wait(&acc_empty[acc], aph ^ 1);
+    long long c1 = clock64();
+    wa += c1 - c0;
+    tc_fence_after();
+    const uint32_t d0 = tmem + acc * p.acc_cols;
+    for (int kb = 0; kb < p.kblocks; ++kb) {
+      c0 = clock64();
+      mbar_wait(&full[stage], ph);
+      c1 = clock64();
+      wf += c1 - c0;
+      if (MODE == IXB_MODE_GATHER) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
+      tc_fence_after();
+      // A descriptor = stage base + op start / LBO (16-byte units) + 128 rows per block; B = K-block
+      // weights + op start. Additions to the low 14-bit address field cannot carry (smem < 256 KB).
+      const KBlockDev& K = p.kb[kb];
+      const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes) >> 4;
+      const uint32_t b0 = p.b_resident ? smem_u32(smem) + K.b_off : ((a0 << 4) + p.a_stage_bytes);
+      const uint64_t bdesc0 = umma_desc(b0, 128, 256);
+      for (int o = 0; o < K.nops; ++o) {
+        const uint32_t opa = p.op_a[K.op0 + o];
+        const uint64_t bd = bdesc0 + p.op_b[K.op0 + o];
+        const uint32_t accum = (kb > 0 || o > 0) ? 1u : 0u;
+        uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
+        ad += (uint64_t)(who * ((kBlockM * 16) >> 4));
+        uint32_t dt = d0 + who * p.n_tile;
+        for (int b = who; b < p.mt; b += p.issuers) {
+          umma_s8(dt, ad, bd, p.idesc, accum);
+          ad += (uint64_t)(p.issuers * ((kBlockM * 16) >> 4));
+          dt += p.issuers * p.n_tile;
+        }
+      }
+      umma_commit(&empty[stage]);
+      wi += clock64() - c1;
+      if (++stage == S) {
+        stage = 0;
+        ph ^= 1;
+      }
+    }
+    umma_commit(&acc_full[acc]);
+    acc ^= 1;
+    if (acc == 0) aph ^= 1;
+  }
+  if (who == 0) {
+    write_stats(p, kStatMmaWaitFull, wf);
+    write_stats(p, kStatMmaWaitAcc, wa);
+    write_stats(p, kStatMmaIssue, wi);
   }
 }
 
@@ -370,31 +420,29 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
   }
 }
 
-// Drain one accumulator: warp w reads TMEM lane quarter w % 4; the two warpgroups take
-// alternate 16-column chunks when there are several, else alternate 128-row blocks. A thread
-// issues the TMEM loads of two pieces before one wait so their latencies overlap.
+// Drain one accumulator: warp w reads TMEM lane quarter w % 4; the warpgroups take alternate
+// pieces (128-row block, 16-column chunk). A thread issues the TMEM loads of two pieces before one
+// wait so their latencies overlap.
 template <int MODE>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const int8_t* lut_s, const int4* bias4_s) {
+  constexpr int ngroups = epi_warps(MODE) / 4;
   const int q = warp & 3, g = warp >> 2;
   const int nj = p.n_tile / 16;
   const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
   const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
-  // this thread's pieces in order: (block, chunk)
-  const int nb = p.mt;
-  const int npieces = nb * nj;
-  int k = g;  // piece index; pieces alternate between the warpgroups
-  while (k < npieces) {
-    const int k2 = k + 2;
-    const int b1 = (nj >= 2) ? k / nj : k, j1 = (nj >= 2) ? k % nj : 0;
+  const int npieces = p.mt * nj;
+  for (int k = g; k < npieces; k += 2 * ngroups) {
+    const int k2 = k + ngroups;
+    const int b1 = k / nj, j1 = k - (k / nj) * nj;
     uint32_t v[16], w[16];
     tmem_ld16(lane_base + b1 * p.n_tile + j1 * 16, v);
     const bool two = k2 < npieces;
     int b2 = 0, j2 = 0;
     if (two) {
-      b2 = (nj >= 2) ? k2 / nj : k2;
-      j2 = (nj >= 2) ? k2 % nj : 0;
+      b2 = k2 / nj;
+      j2 = k2 - b2 * nj;
       tmem_ld16(lane_base + b2 * p.n_tile + j2 * 16, w);
     }
     const RowInfo r1 = decode_row<MODE>(p, m0 + b1 * kBlockM + q * 32 + lane);
@@ -403,12 +451,12 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     tmem_ld_wait();
     if (r1.valid) store_piece(p, r1, ntile, j1, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
     if (two && r2.valid) store_piece(p, r2, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
-    k += 4;
   }
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_constant__ ConvParams p) {
+__global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __grid_constant__ ConvParams p) {
+  constexpr int EPI = epi_warps(MODE), PW0 = EPI, MW0 = mma_warp0(MODE);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -430,102 +478,49 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
     tmem_alloc(tmem_slot, p.tmem_cols);
     tmem_relinquish();
   }
-  if (tid == kMmaWarp * 32) {
-    const uint32_t fcount =
-        (MODE == IXB_MODE_WINDOW) ? 1u : (uint32_t)kProducerThreads + (p.b_resident ? 0u : 1u);
+  if (tid == MW0 * 32) {
+    const uint32_t fcount = (MODE == IXB_MODE_GATHER) ? (uint32_t)kGatherThreads + (p.b_resident ? 0u : 1u) : 1u;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], fcount);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], p.issuers);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps * 32);
+      mbar_init(&acc_full[b], p.issuers);
+      mbar_init(&acc_empty[b], EPI * 32);
     }
     mbar_init(bres_bar, 1);
     fence_mbar_init();
   }
-  for (int i = tid; i < 256; i += kConvThreads) lut_s[i] = p.lut[i];
-  for (int i = tid; i < p.n_tile; i += kConvThreads) bias_s[i] = p.bias[ntile * p.n_tile + i];
+  if (MODE == IXB_MODE_IM2COL || MODE == IXB_MODE_STEM) {
+    if (tid == PW0 * 32) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap) : "memory");
+  }
+  for (int i = tid; i < 256; i += conv_threads(MODE)) lut_s[i] = p.lut[i];
+  for (int i = tid; i < p.n_tile; i += conv_threads(MODE)) bias_s[i] = p.bias[ntile * p.n_tile + i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
+  if (warp >= PW0 && warp < MW0) {
     // ------------------------------------------------------------ producers
-    const int ptid = tid - kProducerWarp0 * 32;
+    const int ptid = tid - PW0 * 32;
     if (p.b_resident && ptid == 0) {
       const int total = p.kb[KB - 1].b_off + p.kb[KB - 1].b_bytes;
       mbar_arrive_expect_tx(bres_bar, (uint32_t)total);
       for (int kb = 0; kb < KB; ++kb)
         bulk_g2s(smem + p.kb[kb].b_off, p.wpack + ntile * p.w_ntile_stride + p.kb[kb].b_off, p.kb[kb].b_bytes, bres_bar);
     }
-    if (MODE == IXB_MODE_WINDOW) {
-      if (ptid == 0) produce_window<MODE>(p, smem, full, empty, ntile);
-    } else {
-      produce_gather<MODE>(p, smem, full, empty, ntile, ptid);
+    if (MODE == IXB_MODE_GATHER) {
+      produce_gather(p, smem, full, empty, ntile, ptid);
+    } else if (ptid == 0) {
+      produce_single<MODE>(p, smem, full, empty, ntile);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      if (p.b_resident) mbar_wait(bres_bar, 0);
-      int stage = 0, acc = 0;
-      uint32_t ph = 0, aph = 0;
-      long long wf = 0, wa = 0, wi = 0;
-      for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
-        long long c0 = clock64();
-        mbar_wait(&acc_empty[acc], aph ^ 1);
-        long long c1 = clock64();
-        wa += c1 - c0;
-        tc_fence_after();
-        const uint32_t d0 = tmem + acc * p.acc_cols;
-        for (int kb = 0; kb < KB; ++kb) {
-          c0 = clock64();
-          mbar_wait(&full[stage], ph);
-          c1 = clock64();
-          wf += c1 - c0;
-          if (MODE != IXB_MODE_WINDOW) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
-          tc_fence_after();
-          // A descriptor = stage base + op's start and LBO (16-byte units) + 128 rows per block;
-          // B descriptor = K-block weights base + op's start. Additions to the low 14-bit address
-          // field cannot carry (shared memory < 256 KB).
-          const KBlockDev& K = p.kb[kb];
-          const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes) >> 4;
-          const uint32_t b0 = (p.b_resident ? (smem_u32(smem) + K.b_off) : ((a0 << 4) + p.a_stage_bytes)) >> 4;
-          const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
-          const uint64_t bdesc0 = umma_desc(b0 << 4, 128, 256);
-          for (int o = 0; o < K.nops; ++o) {
-            const uint32_t opa = p.op_a[K.op0 + o];
-            const uint64_t bd = bdesc0 + p.op_b[K.op0 + o];
-            const uint32_t accum = (kb > 0 || o > 0) ? 1u : 0u;
-            uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
-            uint32_t dt = d0;
-            for (int b = 0; b < p.mt; ++b) {
-              umma_s8(dt, ad, bd, p.idesc, accum);
-              ad += (kBlockM * 16) >> 4;
-              dt += p.n_tile;
-            }
-          }
-          umma_commit(&empty[stage]);
-          wi += clock64() - c1;
-          if (++stage == S) {
-            stage = 0;
-            ph ^= 1;
-          }
-        }
-        umma_commit(&acc_full[acc]);
-        acc ^= 1;
-        if (acc == 0) aph ^= 1;
-      }
-      if (p.stats) {
-        unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
-        st[kStatMmaWaitFull] = wf;
-        st[kStatMmaWaitAcc] = wa;
-        st[kStatMmaIssue] = wi;
-      }
-    }
+  } else if (warp >= MW0) {
+    // ------------------------------------------------------------ MMA issuers
+    const int who = warp - MW0;
+    if (lane == 0 && who < p.issuers) issue_mma<MODE>(p, smem, full, empty, acc_full, acc_empty, bres_bar, tmem, who);
   } else {
-    // ------------------------------------------------------------ epilogue (warps 0-7)
+    // ------------------------------------------------------------ epilogue
     int acc = 0;
     uint32_t aph = 0;
     long long ew = 0, ek = 0;
@@ -544,18 +539,17 @@ __global__ void __launch_bounds__(kConvThreads, 1) conv_kernel(const __grid_cons
       acc ^= 1;
       if (acc == 0) aph ^= 1;
     }
-    if (p.stats && tid == 0) {
-      unsigned long long* st = p.stats + (blockIdx.y * gridDim.x + blockIdx.x) * kStatWords;
-      st[kStatEpiWait] = ew;
-      st[kStatEpiWork] = ek;
-      st[kStatTiles] = tiles;
+    if (tid == 0) {
+      write_stats(p, kStatEpiWait, ew);
+      write_stats(p, kStatEpiWork, ek);
+      write_stats(p, kStatTiles, tiles);
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, p.tmem_cols);
-  if (p.stats && tid == 0) p.stats[(blockIdx.y * gridDim.x + blockIdx.x) * kStatWords + kStatTotal] = clock64() - t_start;
+  if (tid == 0) write_stats(p, kStatTotal, clock64() - t_start);
 }
 
 }  // namespace ixb

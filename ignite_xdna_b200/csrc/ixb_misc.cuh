@@ -1,5 +1,5 @@
 // Bandwidth-bound kernels of the XINT8 graph: image ingress (pixel -> int8 lookup into the
-// padded 4-byte-pixel stem tensor) and SPPF (three chained 5x5 stride-1 max-pools).
+// padded 8-byte-pixel stem tensor) and SPPF (three chained 5x5 stride-1 max-pools).
 #pragma once
 #include <cstdint>
 #include "ixb_ptx.cuh"
@@ -7,9 +7,10 @@
 
 namespace ixb {
 
-// uint8 pixels [B][3][H][W] -> int8 [B][H+2][W+2][4] (channels 0..2 = lut[pixel], channel 3 = 0;
-// the halo is left untouched and stays zero). One thread per 4 horizontally adjacent pixels.
-// The lookup is the model input's QuantizeLinear, graph_session.py:144-149 input_lut.
+// uint8 pixels [B][3][H][W] -> int8 [B][H+2][W+4][8] (bytes 0..2 = lut[pixel] of the three channels,
+// bytes 3..7 = 0; halo columns and rows are left untouched and stay zero). One thread per 4
+// horizontally adjacent pixels. The lookup is the model input's QuantizeLinear
+// (graph_session.py:144-149 input_lut).
 __global__ void __launch_bounds__(256) quantize_images_kernel(const uint8_t* __restrict__ img,
                                                                const int8_t* __restrict__ lut, int B, int H,
                                                                int W, int8_t* __restrict__ out) {
@@ -28,12 +29,12 @@ __global__ void __launch_bounds__(256) quantize_images_kernel(const uint8_t* __r
     const uint32_t r = __ldg(reinterpret_cast<const uint32_t*>(src));
     const uint32_t g = __ldg(reinterpret_cast<const uint32_t*>(src + plane));
     const uint32_t bl = __ldg(reinterpret_cast<const uint32_t*>(src + 2 * plane));
-    uint32_t* dst = reinterpret_cast<uint32_t*>(out + ((b * (H + 2) + y + 1) * (long long)(W + 2) + x4 + 1) * 4);
+    uint2* dst = reinterpret_cast<uint2*>(out + ((b * (H + 2) + y + 1) * (long long)(W + 4) + x4 + 1) * 8);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t w = (uint32_t)lut_s[(r >> (8 * j)) & 0xFF] | ((uint32_t)lut_s[(g >> (8 * j)) & 0xFF] << 8) |
                          ((uint32_t)lut_s[(bl >> (8 * j)) & 0xFF] << 16);
-      dst[j] = w;
+      dst[j] = make_uint2(w, 0u);
     }
   }
 }

@@ -3,7 +3,8 @@
 HBM layout (one arena per GPU, sized for ``max_batch`` images):
 
 * image staging, uint8 [B][3][H][W], and the pixel -> int8 input table;
-* the stem input, int8 [B][H+2][W+2][4] (3 channels + 1 zero, zero halo ring);
+* the stem input, int8 [B][H+2][W+4][8] (3 channels + 5 zero bytes per pixel, one zero halo
+  column on the left and three on the right, so 16-byte pixel pairs cover every stem window);
 * activation buffers: one plane per 16-channel chunk, int8 [B][h+2][w+2][16] with a one-pixel
   zero halo per image and zero guard pixels before and after the plane (a window copy may
   reach past the first and last image). Tensors read together as one concat (a C2f's cv1/m
@@ -56,6 +57,13 @@ def plane_guard(width: int) -> int:
     return 512 + 2 * (width + 3) + 64
 
 
+def plane_stride(batch: int, height: int, width: int, guard: int) -> int:
+    """Bytes per chunk plane: the images plus both guards, rounded up to whole images so a tensor
+    map can address chunk c, image n as image c * (stride / image bytes) + n."""
+    img = (height + 2) * (width + 2) * 16
+    return -(-(batch * img + 2 * guard * 16) // img) * img
+
+
 @dataclass
 class ConvPlan:
     layer: ConvLayer
@@ -99,9 +107,13 @@ def input_lut_t(scale: float) -> np.ndarray:
 def conv_mode(layer: ConvLayer, ir: GraphIR) -> int:
     if layer.inputs[0].tensor == ir.input:
         return L.MODE_STEM
-    if layer.stride == 1 and not any(s.up2 for s in layer.inputs):
+    if any(s.up2 for s in layer.inputs):
+        return L.MODE_GATHER
+    if layer.stride == 1:
         return L.MODE_WINDOW
-    return L.MODE_GATHER
+    if layer.k == 3 and layer.stride == 2 and len({s.tensor for s in layer.inputs}) == 1:
+        return L.MODE_IM2COL
+    raise ValueError(f"{layer.name}: no conv mode for k={layer.k} stride={layer.stride}")
 
 
 def choose_n_tile(cout: int) -> int:
@@ -130,36 +142,36 @@ def _core_layout(b: np.ndarray) -> np.ndarray:
 
 def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule) -> np.ndarray:
     """Weights of every n-tile as the schedule's MMAs' [n_tile][32] K-slices, each in the UMMA
-    core-matrix layout; a slice's two 16-byte K-halves are the (tap, chunk) pairs of its MMA."""
+    core-matrix layout; a slice's two 16-byte K-halves are the (chunk, tap) of the MMA's halves."""
     w = layer.weights.astype(np.int8)       # [cout][cin][k][k]
     cout, cin, k, _ = w.shape
     nchunks = (cin + 15) // 16
     if mode == L.MODE_STEM:
-        # chunk ky (0..2) holds the image row ky: byte 4*j + ci = w[n][ci][ky][j] (j = kx); chunk 3 is zero
-        stem = np.zeros((4, cout, 16), dtype=np.int8)
+        # tap 2*ky + p is the 16-byte pixel pair p of image row ky: image pixel 2x + 2p + j (j = 0, 1)
+        # at kx = 2p + j, bytes 8*j + ci; kx = 3 and channels 3..7 are zero
+        stem = np.zeros((6, cout, 16), dtype=np.int8)
         for ky in range(3):
-            for j in range(3):
+            for kx in range(3):
+                pr, j = divmod(kx, 2)
                 for ci in range(3):
-                    stem[ky, :, 4 * j + ci] = w[:, ci, ky, j]
+                    stem[2 * ky + pr, :, 8 * j + ci] = w[:, ci, ky, kx]
 
         def piece(chunk, tap):
-            return stem[chunk]
+            return stem[tap]
     else:
         wp = np.zeros((cout, nchunks * 16, k * k), dtype=np.int8)
         wp[:, :cin, :] = w.reshape(cout, cin, k * k)
 
         def piece(chunk, tap):
-            if chunk >= nchunks:
-                return np.zeros((cout, 16), dtype=np.int8)
             return wp[:, 16 * chunk:16 * chunk + 16, tap]
     zero = np.zeros((cout, 16), dtype=np.int8)
     out = []
     for nt in range(cout // n_tile):
         sl = slice(nt * n_tile, (nt + 1) * n_tile)
         for blk in schedule:
-            for (t0, s0), second in blk["ops"]:
-                h0 = piece(blk["chunk0"] + s0, t0)
-                h1 = piece(blk["chunk0"] + second[1], second[0]) if second is not None else zero
+            for (_, c0, t0), second in blk["ops"]:
+                h0 = piece(c0, t0)
+                h1 = piece(second[1], second[2]) if second is not None else zero
                 out.append(_core_layout(np.ascontiguousarray(np.concatenate([h0[sl], h1[sl]], axis=1))))
     return np.concatenate(out).view(np.uint8)
 
@@ -209,7 +221,7 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
 
     images_offset = alloc(max_batch * 3 * H * W)
     input_lut_offset = alloc(256)
-    input_store = Store(alloc(max_batch * (H + 2) * (W + 2) * 4), 0, 0, 3, H, W, 0)
+    input_store = Store(alloc(max_batch * (H + 2) * (W + 4) * 8), 0, 0, 3, H, W, 0)
     stores: Dict[str, Store] = {}
     for grp in _storage_groups(ir, heads):
         infos = [ir.tensors[t] for t in grp]
@@ -218,7 +230,7 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
                 raise ValueError(f"{t.name}: {t.channels} channels is not a multiple of 16")
         h, w = infos[0].height, infos[0].width
         guard = plane_guard(w)
-        plane = _align((max_batch * (h + 2) * (w + 2) + 2 * guard) * 16)
+        plane = plane_stride(max_batch, h, w, guard)
         nch = sum(t.channels for t in infos) // 16
         base = alloc(nch * plane) + guard * 16
         ch = 0

@@ -206,8 +206,8 @@ class GraphSession:
             return (h.astype(np.int16) + 128).astype(np.uint8)
         if name == self.ir.input:
             st = self.plan.input_store
-            raw = self.arena[st.offset:st.offset + b * (st.height + 2) * (st.width + 2) * 4].cpu().numpy()
-            v = raw.view(np.int8).reshape(b, st.height + 2, st.width + 2, 4)[:, 1:-1, 1:-1, :3]
+            raw = self.arena[st.offset:st.offset + b * (st.height + 2) * (st.width + 4) * 8].cpu().numpy()
+            v = raw.view(np.int8).reshape(b, st.height + 2, st.width + 4, 8)[:, 1:-1, 1:st.width + 1, :3]
             return (v.astype(np.int16) + 128).astype(np.uint8).transpose(0, 3, 1, 2)
         st = self.plan.stores[name]
         P = (st.height + 2) * (st.width + 2)

@@ -48,8 +48,9 @@ extern "C" {
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
-#define IXB_MODE_GATHER 1   /* stride 2 or an up2 input: per-pixel gather per tap */
-#define IXB_MODE_STEM 2     /* 3x3 stride-2 conv over the 4-byte-pixel image tensor */
+#define IXB_MODE_GATHER 1   /* 1x1 conv over a concat with an up2 view: per-pixel cp.async gathers */
+#define IXB_MODE_STEM 2     /* 3x3 stride-2 conv over the image tensor (TMA im2col over pixel pairs) */
+#define IXB_MODE_IM2COL 3   /* 3x3 stride-2 conv: TMA im2col loads per (tap, chunk) */
 
 /* ixb_session_run flags */
 #define IXB_IN_DEVICE 1     /* images is a device pointer; NULL: the images already sit in the staging buffer */
@@ -60,8 +61,9 @@ extern "C" {
 /* One stored activation tensor, or a channel range of it. Activations are int8 (t = q - 128)
  * stored as one plane per 16-channel chunk: plane c holds [batch][H+2][W+2] pixels of 16 bytes
  * (channels 16c .. 16c+15) with a zero one-pixel halo ring around every image and `guard` zero
- * pixels before and after the plane. The image tensor the stem reads is a single plane of
- * 4-byte pixels (3 channels + 1 zero) without guards. */
+ * pixels before and after the plane; IM2COL inputs need plane_stride to be a whole number of
+ * images. The image tensor the stem reads is a single guard-free plane of 8-byte pixels
+ * (3 channels + 5 zero) [batch][H+2][W+4]: one halo column on the left, three on the right. */
 typedef struct ixb_segment {
   uint64_t offset;       /* arena byte offset of padded pixel 0 of image 0 in the tensor's chunk plane 0 */
   uint64_t plane_stride; /* bytes from one chunk plane to the next */
@@ -156,10 +158,12 @@ int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, in
 int ixb_conv_layer_stats(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream,
                          uint64_t* stats, int64_t stats_words);
 /* The K schedule of a conv descriptor (shape fields only: mode, k, n_tile, cp, segment channels).
- * kb_out: 8 int32 per K-block {first chunk, chunks, gather tap, first MMA, MMAs, weight offset,
- * weight bytes, 0}; ops_out: 4 int32 per MMA {tap, A slot, tap, A slot} of its two 32-byte
- * K-halves (second tap -1: zero weights). Returns the number of K-blocks. The packed weights of
- * one n-tile are the MMAs' [n_tile][32] K-slices in this order. */
+ * kb_out: 8 int32 per K-block {first chunk, chunks, first tap, taps, first MMA, MMAs, weight offset,
+ * weight bytes}: A slot s holds chunk (first chunk + s / taps) at tap (first tap + s % taps).
+ * ops_out: 6 int32 per MMA {slot, chunk, tap, slot, chunk, tap} of its two 32-byte K-halves; for
+ * WINDOW the tap of a half is its window shift; a second half with chunk -1 multiplies zero
+ * weights. Returns the number of K-blocks. The packed weights of one n-tile are the MMAs'
+ * [n_tile][32] K-slices in this order. */
 int ixb_conv_schedule(const ixb_conv_desc* d, int32_t* kb_out, int max_kb, int32_t* ops_out, int max_ops);
 /* The launch a conv descriptor gets for `batch` images (host-side decision, no GPU needed):
  * info = {blocks of 128 pixels per tile, tile rows, tiles, pipeline stages, weights resident,

@@ -64,7 +64,7 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
     assert info["kblocks"] == len(sched) and info["rows_a"] == rowsA
     b_total = sched[-1]["b_off"] + sched[-1]["b_bytes"]
     assert (d.cout // n_tile) * b_total == d.w_bytes
-    slots = max(b["nchunks"] for b in sched)
+    slots = max(b["nchunks"] * b["ntaps"] for b in sched)
     a_bytes = slots * rowsA * 16 + 16
 
     def shift_of(t):
@@ -78,19 +78,21 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
             acc = np.zeros((TM, n_tile), dtype=np.int64)
             for blk in sched:
                 smem = np.zeros(a_bytes, dtype=np.uint8)
-                # ---- A: the K-block's chunks into slots 0..nchunks-1
-                for c in range(blk["nchunks"]):
-                    gc = blk["chunk0"] + c
-                    dst0 = c * rowsA * 16
+                # ---- A: slot s = chunk chunk0 + s // ntaps at tap tap0 + s % ntaps
+                for sl in range(blk["nchunks"] * blk["ntaps"]):
+                    gc = blk["chunk0"] + sl // blk["ntaps"]
+                    tap = blk["tap0"] + sl % blk["ntaps"]
+                    dst0 = sl * rowsA * 16
                     if mode == L.MODE_STEM:
                         r = np.arange(TM)
                         m = m0 + r
-                        ok = (c < 3) & (m < m_total)
-                        s = segs[0]
+                        ok = m < m_total
+                        s = d.seg[0]
                         img = m // (Ho * Wo)
                         rem = m - img * Ho * Wo
                         y, x = rem // Wo, rem % Wo
-                        src = s["base"] + (img * s["P"] + (2 * y + c) * (s["W"] + 2) + 2 * x) * 4
+                        ky, pr = tap // 2, tap % 2
+                        src = s.offset + ((img * (s.height + 2) + 2 * y + ky) * (s.width + 4) + 2 * x + 2 * pr) * 8
                         for rr in np.nonzero(ok)[0]:
                             smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[src[rr]:src[rr] + 16]
                         continue
@@ -106,7 +108,6 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         src = cbase + m * 16
                         rows = px
                     else:
-                        tap = blk["tap"]
                         r = np.arange(TM)
                         m = m0 + r
                         ok = m < m_total
@@ -124,9 +125,9 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                 # ---- B of this K-block, then its MMAs
                 wsrc = d.w_offset + nt * b_total + blk["b_off"]
                 bmem = arena[wsrc:wsrc + blk["b_bytes"]]
-                for o, ((t0, s0), second) in enumerate(blk["ops"]):
+                for o, ((s0, _, t0), second) in enumerate(blk["ops"]):
                     a_start = s0 * rowsA + shift_of(t0)
-                    lbo = (second[1] * rowsA + shift_of(second[0]) - a_start) if second is not None else 1
+                    lbo = (second[0] * rowsA + shift_of(second[2]) - a_start) if second is not None else 1
                     B = _operand(bmem, o * n_tile * 32, 128, 256, n_tile)
                     for blk_m in range(MT):
                         A = _operand(smem, (a_start + blk_m * 128) * 16, lbo * 16, 128, 128)
@@ -200,9 +201,10 @@ def run_network(dp: DevicePlan, images: np.ndarray) -> np.ndarray:
     lut = arena[dp.input_lut_offset:dp.input_lut_offset + 256].view(np.int8)
     s = dp.input_store
     for b in range(batch):
-        base = s.offset + b * (s.height + 2) * (s.width + 2) * 4
-        v = arena[base:base + (s.height + 2) * (s.width + 2) * 4].view(np.int8).reshape(s.height + 2, s.width + 2, 4)
-        v[1:-1, 1:-1, :3] = lut[images[b].transpose(1, 2, 0)]
+        n = (s.height + 2) * (s.width + 4) * 8
+        base = s.offset + b * n
+        v = arena[base:base + n].view(np.int8).reshape(s.height + 2, s.width + 4, 8)
+        v[1:-1, 1:s.width + 1, :3] = lut[images[b].transpose(1, 2, 0)]
     convs = [c.desc for c in dp.convs]
     for kind, idx in dp.ops:
         if kind == L.OP_CONV:

@@ -36,10 +36,10 @@ def test_plan_storage_is_disjoint_and_aligned(variant):
         nch = sum(t.channels for n2, t in ir.tensors.items() if n2 in dp.stores and dp.stores[n2].offset == st.offset) // 16
         start = st.offset - st.guard * 16
         spans[start] = nch * st.plane_stride
-        assert st.offset % 16 == 0 and st.plane_stride % 256 == 0
+        assert st.offset % 16 == 0 and st.plane_stride % ((st.height + 2) * (st.width + 2) * 16) == 0
         assert st.plane_stride >= (64 * (st.height + 2) * (st.width + 2) + 2 * st.guard) * 16
     spans[dp.images_offset] = 64 * 3 * dp.img_h * dp.img_w
-    spans[dp.input_store.offset] = 64 * (dp.img_h + 2) * (dp.img_w + 2) * 4
+    spans[dp.input_store.offset] = 64 * (dp.img_h + 2) * (dp.img_w + 4) * 8
     spans[dp.egress_offset] = 64 * dp.egress_image_bytes
     spans[dp.const_offset] = dp.const_blob.size
     iv = sorted(spans.items())
@@ -56,32 +56,41 @@ def _sched(mode, k, cin, cp, n_tile=32):
     return L.conv_schedule(d)
 
 
-@pytest.mark.parametrize("mode", [L.MODE_WINDOW, L.MODE_GATHER])
+@pytest.mark.parametrize("mode", [L.MODE_WINDOW, L.MODE_GATHER, L.MODE_IM2COL])
 @pytest.mark.parametrize("k,cin,cp", [(3, 80, 1), (1, 384, 4), (3, 576, 2), (1, 48, 2), (3, 16, 1), (1, 16, 1),
                                       (3, 48, 1), (1, 80, 4)])
 def test_schedule_covers_every_tap_and_chunk_once(mode, k, cin, cp):
+    if mode == L.MODE_IM2COL and k != 3:
+        pytest.skip("IM2COL is the 3x3 stride-2 conv")
+    if mode == L.MODE_GATHER and k != 1:
+        pytest.skip("GATHER is the 1x1 conv over an upsampled concat")
     nchunks = (cin + 15) // 16
     seen = []
     for blk in _sched(mode, k, cin, cp):
-        assert blk["nchunks"] <= 2 * cp
+        nslots = blk["nchunks"] * blk["ntaps"]
         for first, second in blk["ops"]:
             for half in (first, second):
                 if half is None:
                     continue
-                tap, slot = half
-                chunk = blk["chunk0"] + slot
-                if chunk < nchunks:
-                    assert slot < blk["nchunks"]
-                    seen.append((tap if mode == L.MODE_WINDOW else blk["tap"], chunk))
+                slot, chunk, tap = half
+                assert slot < nslots
+                if mode != L.MODE_WINDOW:     # the slot's loaded (chunk, tap) is the half's
+                    assert chunk == blk["chunk0"] + slot // blk["ntaps"]
+                    assert tap == blk["tap0"] + slot % blk["ntaps"]
+                else:
+                    assert chunk == blk["chunk0"] + slot
+                seen.append((tap, chunk))
     assert sorted(seen) == sorted((t, c) for t in range(k * k) for c in range(nchunks))
 
 
 def test_odd_chunk_taps_are_paired():
-    """A 16-channel 3x3 conv needs 5 MMAs per 128 pixels, not 9."""
+    """A 16-channel 3x3 conv needs 5 MMAs per 128 pixels, not 9, window or im2col."""
     blocks = _sched(L.MODE_WINDOW, 3, 16, 1)
     assert len(blocks) == 1 and len(blocks[0]["ops"]) == 5
     blocks = _sched(L.MODE_WINDOW, 3, 80, 1)
     assert sum(len(b["ops"]) for b in blocks) == 2 * 9 + 5
+    blocks = _sched(L.MODE_IM2COL, 3, 16, 1)
+    assert sum(len(b["ops"]) for b in blocks) == 5
 
 
 def test_fast_division_formula_is_exact():
