@@ -17,7 +17,7 @@ IXB_OK = 0
 ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
 IXB_ERR_TIMEOUT = -3
 MAX_SEGS = 4
-API_VERSION = 2
+API_VERSION = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH = 1, 2, 4, 8
 OP_CONV, OP_POOL = 0, 1
@@ -54,7 +54,8 @@ class Plan(C.Structure):
                 ("n_convs", C.c_int32), ("n_pools", C.c_int32), ("n_ops", C.c_int32),
                 ("convs", C.POINTER(ConvDesc)), ("pools", C.POINTER(PoolDesc)), ("ops", C.POINTER(Op)),
                 ("images_offset", C.c_uint64), ("input_lut_offset", C.c_uint64), ("input", Segment),
-                ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64), ("arena_bytes", C.c_uint64)]
+                ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64), ("arena_bytes", C.c_uint64),
+                ("images_offset_alt", C.c_uint64), ("egress_offset_alt", C.c_uint64)]
 
 
 class IxbError(RuntimeError):
@@ -76,6 +77,10 @@ _SIGS = {
     "ixb_session_stream": (C.c_void_p, [C.c_void_p]),
     "ixb_session_run": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
     "ixb_session_wait": (C.c_int, [C.c_void_p, C.c_int]),
+    "ixb_session_submit": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.POINTER(C.c_uint64)]),
+    "ixb_session_wait_ticket": (C.c_int, [C.c_void_p, C.c_uint64, C.c_int]),
+    "ixb_session_streams": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                      C.POINTER(C.c_void_p)]),
     "ixb_session_last_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     "ixb_session_launches": (C.c_int, [C.c_void_p, C.c_int]),
     "ixb_session_profile": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]),

@@ -624,7 +624,8 @@ int read_device_error() {
 
 struct ixb_session {
   int device = 0;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;             // compute
+  cudaStream_t h2d = nullptr, d2h = nullptr;  // copy streams of submitted runs
   uint8_t* arena = nullptr;
   uint64_t arena_bytes = 0;
   bool own_arena = false;
@@ -632,15 +633,38 @@ struct ixb_session {
   std::vector<ixb_conv_desc> convs;
   std::vector<ixb_pool_desc> pools;
   std::vector<ixb_op> ops;
+  // launches and graphs per (batch, slot): key = 2 * batch + slot
   std::map<int, std::vector<ConvLaunch>> conv_launch;
   std::map<int, std::vector<PoolLaunch>> pool_launch;
   std::map<int, cudaGraphExec_t> graphs;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev_done = nullptr;
   bool pending = false;
   float last_ms = 0.f;
+  struct Slot {
+    uint64_t ticket = 0;
+    bool busy = false;
+    cudaEvent_t h2d_done = nullptr, t0 = nullptr, t1 = nullptr, d2h_done = nullptr;
+  } slots[2];
+  uint64_t next_ticket = 1;
 
-  int prepare(int batch) {
-    if (conv_launch.count(batch)) return 0;
+  bool two_slots() const { return plan.images_offset_alt && plan.egress_offset_alt; }
+  uint64_t images_at(int slot) const { return slot ? plan.images_offset_alt : plan.images_offset; }
+  uint64_t egress_at(int slot) const { return slot ? plan.egress_offset_alt : plan.egress_offset; }
+
+  int prepare(int batch, int slot = 0) {
+    const int key = 2 * batch + slot;
+    if (conv_launch.count(key)) return 0;
+    if (slot) {
+      // the second slot differs only in where the head convs write the egress
+      if (int r = prepare(batch, 0)) return r;
+      std::vector<ConvLaunch> cl = conv_launch[2 * batch];
+      const long long delta = (long long)plan.egress_offset_alt - (long long)plan.egress_offset;
+      for (ConvLaunch& L : cl)
+        if (L.p.out_nchw) L.p.egress += delta;
+      conv_launch[key] = std::move(cl);
+      pool_launch[key] = pool_launch[2 * batch];
+      return 0;
+    }
     std::vector<ConvLaunch> cl(convs.size());
     std::vector<PoolLaunch> pl(pools.size());
     std::string err;
@@ -650,39 +674,41 @@ struct ixb_session {
     for (size_t i = 0; i < pools.size(); ++i)
       if (build_pool(pools[i], arena, arena_bytes, batch, pl[i], err))
         return fail(IXB_ERR_INVALID, "pool " + std::to_string(i) + ": " + err);
-    conv_launch[batch] = std::move(cl);
-    pool_launch[batch] = std::move(pl);
+    conv_launch[key] = std::move(cl);
+    pool_launch[key] = std::move(pl);
     return 0;
   }
 
-  int enqueue_op(int batch, int i) {
+  int enqueue_op(int batch, int i, int slot = 0) {
     const ixb_op& op = ops[i];
-    if (op.kind == IXB_OP_CONV) return launch_conv(conv_launch[batch][op.index], stream);
-    return launch_pool(pool_launch[batch][op.index], stream);
+    const int key = 2 * batch + slot;
+    if (op.kind == IXB_OP_CONV) return launch_conv(conv_launch[key][op.index], stream);
+    return launch_pool(pool_launch[key][op.index], stream);
   }
 
-  int enqueue_ingress(int batch) {
-    return launch_quantize(arena + plan.images_offset, reinterpret_cast<const int8_t*>(arena + plan.input_lut_offset),
+  int enqueue_ingress(int batch, int slot = 0) {
+    return launch_quantize(arena + images_at(slot), reinterpret_cast<const int8_t*>(arena + plan.input_lut_offset),
                            batch, plan.img_h, plan.img_w, reinterpret_cast<int8_t*>(arena + plan.input.offset),
                            stream);
   }
 
-  int enqueue(int batch) {
-    if (int r = enqueue_ingress(batch)) return r;
+  int enqueue(int batch, int slot = 0) {
+    if (int r = enqueue_ingress(batch, slot)) return r;
     for (size_t i = 0; i < ops.size(); ++i)
-      if (int r = enqueue_op(batch, (int)i)) return r;
+      if (int r = enqueue_op(batch, (int)i, slot)) return r;
     return 0;
   }
 
-  int graph_for(int batch, cudaGraphExec_t* out) {
-    auto it = graphs.find(batch);
+  int graph_for(int batch, cudaGraphExec_t* out, int slot = 0) {
+    const int key = 2 * batch + slot;
+    auto it = graphs.find(key);
     if (it != graphs.end()) {
       *out = it->second;
       return 0;
     }
     cudaGraph_t g = nullptr;
     IXB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-    int r = enqueue(batch);
+    int r = enqueue(batch, slot);
     cudaError_t e = cudaStreamEndCapture(stream, &g);
     if (r) {
       if (g) cudaGraphDestroy(g);
@@ -693,11 +719,27 @@ struct ixb_session {
     e = cudaGraphInstantiate(&exec, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
-    graphs[batch] = exec;
+    graphs[key] = exec;
     *out = exec;
     return 0;
   }
+
+  bool any_busy() const { return slots[0].busy || slots[1].busy; }
 };
+
+// Poll an event until it completes or the timeout runs out (spin first: a step takes milliseconds).
+int wait_event(cudaEvent_t ev, int timeout_ms) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return 0;
+    if (e != cudaErrorNotReady) return cuda_fail(e, "run");
+    const auto us = std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0);
+    if (us.count() >= 1000LL * timeout_ms) return fail(IXB_ERR_TIMEOUT, "run did not finish within the timeout");
+    if (us.count() < 5000) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
 
 extern "C" {
 
@@ -769,6 +811,12 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
     bad = fail(IXB_ERR_INVALID, "stem input view must be the img_h x img_w 3-channel image");
   else if (plan->egress_offset + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes)
     bad = fail(IXB_ERR_INVALID, "egress outside the arena");
+  else if ((plan->images_offset_alt != 0) != (plan->egress_offset_alt != 0))
+    bad = fail(IXB_ERR_INVALID, "the second pipeline slot needs both a staging and an egress buffer");
+  else if (plan->images_offset_alt &&
+           (plan->images_offset_alt % 16 || plan->images_offset_alt + img_bytes > s->arena_bytes ||
+            plan->egress_offset_alt + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes))
+    bad = fail(IXB_ERR_INVALID, "second pipeline slot outside the arena");
   if (!bad) bad = s->prepare(B);
   if (bad) {
     if (s->own_arena) cudaFree(s->arena);
@@ -776,9 +824,17 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
     return bad;
   }
   cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->h2d, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->d2h, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
   if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->ev_done, cudaEventDisableTiming);
+  for (auto& sl : s->slots) {
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.h2d_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreate(&sl.t0);
+    if (e == cudaSuccess) e = cudaEventCreate(&sl.t1);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.d2h_done, cudaEventDisableTiming);
+  }
   if (e != cudaSuccess) {
     int r = cuda_fail(e, "stream/event creation");
     ixb_session_destroy(s);
@@ -792,7 +848,14 @@ int ixb_session_destroy(ixb_session* s) {
   if (!s) return 0;
   cudaSetDevice(s->device);
   if (s->stream) cudaStreamSynchronize(s->stream);
+  if (s->h2d) cudaStreamSynchronize(s->h2d);
+  if (s->d2h) cudaStreamSynchronize(s->d2h);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& sl : s->slots)
+    for (cudaEvent_t ev : {sl.h2d_done, sl.t0, sl.t1, sl.d2h_done})
+      if (ev) cudaEventDestroy(ev);
+  if (s->h2d) cudaStreamDestroy(s->h2d);
+  if (s->d2h) cudaStreamDestroy(s->d2h);
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
   if (s->ev_done) cudaEventDestroy(s->ev_done);
@@ -815,6 +878,7 @@ int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* eg
   if (!s) return fail(IXB_ERR_INVALID, "null session");
   if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
   if (s->pending) return fail(IXB_ERR_INVALID, "the previous asynchronous run was not waited for");
+  if (s->any_busy()) return fail(IXB_ERR_INVALID, "submitted runs are still in flight");
   if (!(flags & IXB_IN_DEVICE) && !images) return fail(IXB_ERR_INVALID, "null images");
   if (!(flags & IXB_OUT_DEVICE) && !egress) return fail(IXB_ERR_INVALID, "null egress");
   const bool copy_in = images != nullptr, copy_out = egress != nullptr;
@@ -866,6 +930,57 @@ int ixb_session_wait(ixb_session* s, int timeout_ms) {
   return read_device_error();
 }
 
+int ixb_session_submit(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, uint64_t* ticket) {
+  if (!s || !images || !egress || !ticket) return fail(IXB_ERR_INVALID, "null argument");
+  if (!s->two_slots()) return fail(IXB_ERR_UNSUPPORTED, "the plan has no second pipeline slot");
+  if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
+  if (s->pending) return fail(IXB_ERR_INVALID, "a synchronous run is pending");
+  IXB_CUDA(cudaSetDevice(s->device));
+  const uint64_t t = s->next_ticket;
+  const int slot = (int)(t & 1);
+  ixb_session::Slot& sl = s->slots[slot];
+  if (sl.busy)  // the run two tickets back still owns this slot's buffers
+    if (int r = ixb_session_wait_ticket(s, sl.ticket, 60000)) return r;
+  if (int r = s->prepare(batch, slot)) return r;
+  cudaGraphExec_t exec;
+  if (int r = s->graph_for(batch, &exec, slot)) return r;
+  const size_t in_bytes = (size_t)batch * 3 * s->plan.img_h * s->plan.img_w;
+  IXB_CUDA(cudaMemcpyAsync(s->arena + s->images_at(slot), images, in_bytes, cudaMemcpyDefault, s->h2d));
+  IXB_CUDA(cudaEventRecord(sl.h2d_done, s->h2d));
+  IXB_CUDA(cudaStreamWaitEvent(s->stream, sl.h2d_done, 0));
+  IXB_CUDA(cudaEventRecord(sl.t0, s->stream));
+  IXB_CUDA(cudaGraphLaunch(exec, s->stream));
+  IXB_CUDA(cudaEventRecord(sl.t1, s->stream));
+  IXB_CUDA(cudaStreamWaitEvent(s->d2h, sl.t1, 0));
+  IXB_CUDA(cudaMemcpyAsync(egress, s->arena + s->egress_at(slot), (size_t)batch * s->plan.egress_image_bytes,
+                           cudaMemcpyDefault, s->d2h));
+  IXB_CUDA(cudaEventRecord(sl.d2h_done, s->d2h));
+  sl.ticket = t;
+  sl.busy = true;
+  s->next_ticket = t + 1;
+  *ticket = t;
+  return 0;
+}
+
+int ixb_session_wait_ticket(ixb_session* s, uint64_t ticket, int timeout_ms) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (ticket == 0 || ticket >= s->next_ticket) return fail(IXB_ERR_INVALID, "unknown ticket");
+  ixb_session::Slot& sl = s->slots[ticket & 1];
+  if (!sl.busy || sl.ticket != ticket) return 0;  // already completed and collected
+  if (int r = wait_event(sl.d2h_done, timeout_ms)) return r;
+  sl.busy = false;
+  cudaEventElapsedTime(&s->last_ms, sl.t0, sl.t1);
+  return read_device_error();
+}
+
+int ixb_session_streams(ixb_session* s, void** compute, void** h2d, void** d2h) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (compute) *compute = s->stream;
+  if (h2d) *h2d = s->h2d;
+  if (d2h) *d2h = s->d2h;
+  return 0;
+}
+
 int ixb_session_last_ms(ixb_session* s, float* ms) {
   if (!s || !ms) return fail(IXB_ERR_INVALID, "null argument");
   *ms = s->last_ms;
@@ -876,6 +991,7 @@ int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms) {
   if (!s || !ms || iters < 1) return fail(IXB_ERR_INVALID, "bad profile arguments");
   if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
   if (s->pending) return fail(IXB_ERR_INVALID, "a run is pending");
+  if (s->any_busy()) return fail(IXB_ERR_INVALID, "submitted runs are still in flight");
   IXB_CUDA(cudaSetDevice(s->device));
   if (int r = s->prepare(batch)) return r;
   const size_t n = s->ops.size();

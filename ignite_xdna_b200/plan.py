@@ -93,6 +93,8 @@ class DevicePlan:
     ops: List[Tuple[int, int]]
     const_offset: int
     const_blob: np.ndarray
+    images_offset_alt: int = 0
+    egress_offset_alt: int = 0
     c_plan: object = None
     keep: list = field(default_factory=list)
 
@@ -220,6 +222,7 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
         return o
 
     images_offset = alloc(max_batch * 3 * H * W)
+    images_offset_alt = alloc(max_batch * 3 * H * W)     # second pipeline slot
     input_lut_offset = alloc(256)
     input_store = Store(alloc(max_batch * (H + 2) * (W + 4) * 8), 0, 0, 3, H, W, 0)
     stores: Dict[str, Store] = {}
@@ -245,6 +248,7 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
         eb += t.channels * t.height * t.width
     egress_image_bytes = eb
     egress_offset = alloc(max_batch * egress_image_bytes)
+    egress_offset_alt = alloc(max_batch * egress_image_bytes)
 
     # constants
     const_parts: List[Tuple[int, np.ndarray]] = []
@@ -365,7 +369,8 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
                       images_offset=images_offset, input_lut_offset=const_offset + ilut_rel,
                       input_store=input_store, egress_offset=egress_offset, egress_image_bytes=egress_image_bytes,
                       head_offsets=head_offsets, stores=stores, convs=convs, pools=pools, ops=ops,
-                      const_offset=const_offset, const_blob=blob)
+                      const_offset=const_offset, const_blob=blob, images_offset_alt=images_offset_alt,
+                      egress_offset_alt=egress_offset_alt)
 
 
 def _merge_segments(segs: List[L.Segment]) -> List[L.Segment]:
@@ -403,6 +408,8 @@ def c_plan(dp: DevicePlan) -> L.Plan:
     p.egress_offset = dp.egress_offset
     p.egress_image_bytes = dp.egress_image_bytes
     p.arena_bytes = dp.arena_bytes
+    p.images_offset_alt = dp.images_offset_alt
+    p.egress_offset_alt = dp.egress_offset_alt
     dp.keep = [convs, pools, ops]
     dp.c_plan = p
     return p

@@ -33,6 +33,46 @@ def _torch():
     return torch
 
 
+class RunHandle:
+    """One submitted batch in flight (the reference's ``runtime/session.py`` ``RunHandle`` :40-85).
+
+    ``wait`` blocks until the batch's heads are in host memory and returns them as int8
+    [B, egress_image_bytes]. Without an ``out`` buffer the result lives in the session's pinned
+    egress slot, which the submit two tickets later reuses: a handle still unwaited at that point
+    is completed first and keeps a private copy."""
+
+    def __init__(self, session: "GraphSession", ticket: int, batch: int, egress: np.ndarray, keep: Any):
+        self._s = session
+        self.ticket = int(ticket)
+        self.batch = int(batch)
+        self._egress = egress
+        self._keep = keep          # host/device input buffers that must outlive the copies
+        self._result: Optional[np.ndarray] = None
+
+    @property
+    def done(self) -> bool:
+        return self._result is not None
+
+    def wait(self, timeout_ms: int = 2000) -> np.ndarray:
+        if self._result is None:
+            rc = self._s.lib.ixb_session_wait_ticket(self._s._h, C.c_uint64(self.ticket), int(timeout_ms))
+            if rc == L.IXB_ERR_TIMEOUT:
+                raise TimeoutError(f"submitted run {self.ticket} did not complete within {timeout_ms} ms")
+            L.check(rc)
+            ms = C.c_float()
+            self._s.lib.ixb_session_last_ms(self._s._h, C.byref(ms))
+            self.gpu_ms = float(ms.value)
+            self._result = self._egress
+            self._keep = None
+        return self._result
+
+    def _retire(self) -> None:
+        """Complete the run and detach its result from the slot buffer about to be reused."""
+        out = self.wait(60000)
+        if self._s._owns(out):
+            self._result = out.copy()
+
+
 class GraphSession:
     """Whole-network XINT8 YOLOv8 on one B200: persistent arena, one CUDA graph per batch size."""
 
@@ -63,6 +103,10 @@ class GraphSession:
         self._staged = 0
         self.last_dispatch_ms = 0.0
         self.last_host_ms = 0.0
+        self._next_ticket = 1
+        self._inflight = [None, None]     # RunHandle per pipeline slot
+        self._pin_in = [None, None]
+        self._pin_out = [None, None]
 
     # ------------------------------------------------------------------ status
     @property
@@ -73,6 +117,13 @@ class GraphSession:
     @property
     def stream_handle(self) -> int:
         return int(self.lib.ixb_session_stream(self._h) or 0)
+
+    def streams(self):
+        """(compute, h2d, d2h) cudaStream_t handles as ints: the session's compute stream and the
+        copy streams of ``run_async``."""
+        c, h, d = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        L.check(self.lib.ixb_session_streams(self._h, C.byref(c), C.byref(h), C.byref(d)))
+        return int(c.value or 0), int(h.value or 0), int(d.value or 0)
 
     def launches(self, batch: int) -> int:
         return L.check(self.lib.ixb_session_launches(self._h, int(batch)))
@@ -109,6 +160,7 @@ class GraphSession:
     def stage_input(self, input_tensor: Any) -> None:
         """Copy a batch of images into the device staging buffer (no compute)."""
         torch = _torch()
+        self._drain()
         x = self._as_pixels(input_tensor)
         b = self._check_shape(x.shape)
         n = b * self.in_image_bytes
@@ -120,8 +172,74 @@ class GraphSession:
         torch.cuda.synchronize(self.device)
         self._staged = b
 
+    # ------------------------------------------------------------------ pipelined runs
+    def _owns(self, a: np.ndarray) -> bool:
+        for t in self._pin_out:
+            if t is not None and np.shares_memory(a, t.numpy()):
+                return True
+        return False
+
+    def _drain(self) -> None:
+        for h in self._inflight:
+            if h is not None and not h.done:
+                h._retire()
+        self._inflight = [None, None]
+
+    def run_async(self, input_tensor: Any, unswizzle: bool = True, out: Optional[np.ndarray] = None) -> RunHandle:
+        """Submit a batch and return at once (the reference's ``InferenceSession.run_async``,
+        runtime/session.py:1280-1318).
+
+        The images' host-to-device copy, the network and the heads' device-to-host copy run on
+        three streams ordered by events, and consecutive submits alternate between two staging
+        and egress slots, so one batch's copies overlap the next batch's compute. ``input_tensor``
+        is as for ``run``; a pinned CPU or a CUDA tensor is copied from in place (and must not be
+        changed until the handle completes), anything else is first copied into the slot's pinned
+        staging buffer. ``out``, if given, is an int8 [>=B, egress_image_bytes] array (pinned for
+        overlap) that receives the heads; ``unswizzle`` is accepted for compatibility."""
+        torch = _torch()
+        x = self._as_pixels(input_tensor)
+        b = self._check_shape(x.shape)
+        slot = self._next_ticket & 1
+        prev = self._inflight[slot]
+        if prev is not None and not prev.done:
+            prev._retire()
+        n = b * self.in_image_bytes
+        if isinstance(x, torch.Tensor) and (x.is_cuda or x.is_pinned()):
+            if x.is_cuda:
+                torch.cuda.current_stream(x.device).synchronize()
+            src, keep = x, x
+        else:
+            if self._pin_in[slot] is None:
+                self._pin_in[slot] = torch.empty(self.max_batch * self.in_image_bytes, dtype=torch.uint8,
+                                                 pin_memory=True)
+            buf = self._pin_in[slot]
+            host = x if isinstance(x, torch.Tensor) else torch.from_numpy(x)
+            buf[:n].copy_(host.reshape(-1))
+            src, keep = buf, None
+        if out is None:
+            if self._pin_out[slot] is None:
+                self._pin_out[slot] = torch.empty((self.max_batch, self.out_bytes), dtype=torch.int8,
+                                                  pin_memory=True)
+            egress = self._pin_out[slot].numpy()[:b]
+        else:
+            egress = out
+            if egress.dtype != np.int8 or not egress.flags.c_contiguous or egress.size < b * self.out_bytes:
+                raise ValueError(f"out must be a contiguous int8 array of at least {b} x {self.out_bytes}")
+            egress = egress.reshape(-1)[:b * self.out_bytes].reshape(b, self.out_bytes)
+        ticket = C.c_uint64()
+        L.check(self.lib.ixb_session_submit(self._h, C.c_void_p(src.data_ptr()), b,
+                                            egress.ctypes.data_as(C.c_void_p), C.byref(ticket)))
+        if ticket.value != self._next_ticket:
+            raise RuntimeError(f"engine issued ticket {ticket.value}, expected {self._next_ticket}")
+        self._next_ticket += 1
+        h = RunHandle(self, ticket.value, b, egress, keep)
+        self._inflight[slot] = h
+        self._last_batch = b
+        return h
+
     def dispatch(self, timeout_ms: int = 10000, batch: Optional[int] = None) -> None:
         """Run the network on the staged images; heads stay in the device egress."""
+        self._drain()
         b = int(batch or self._staged)
         if b < 1:
             raise RuntimeError("no staged input")
@@ -156,6 +274,7 @@ class GraphSession:
         ``unswizzle`` and ``max_segments`` are accepted for compatibility: the heads are always NCHW
         and the network is one segment."""
         torch = _torch()
+        self._drain()
         t0 = time.perf_counter()
         if input_tensor is None:
             b = self._staged
@@ -221,6 +340,7 @@ class GraphSession:
 
     def profile(self, batch: int, iters: int = 3):
         """Mean device milliseconds per op (layer-by-layer launches with events)."""
+        self._drain()
         ms = (C.c_float * len(self.plan.ops))()
         L.check(self.lib.ixb_session_profile(self._h, int(batch), int(iters), ms))
         return list(ms)
@@ -229,6 +349,10 @@ class GraphSession:
     def close(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
+            try:
+                self._drain()
+            except Exception:
+                pass
             self.lib.ixb_session_destroy(h)
             self._h = C.c_void_p()
         self.arena = None

@@ -44,7 +44,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 2
+#define IXB_API_VERSION 3
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -122,6 +122,8 @@ typedef struct ixb_plan {
   uint64_t egress_offset;       /* int8 [max_batch][egress_image_bytes] */
   uint64_t egress_image_bytes;
   uint64_t arena_bytes;
+  uint64_t images_offset_alt;   /* second pipeline slot: staging and egress of the same sizes */
+  uint64_t egress_offset_alt;   /* (0, 0: the session runs one slot and ixb_session_submit is refused) */
 } ixb_plan;
 
 typedef struct ixb_session ixb_session;
@@ -141,6 +143,19 @@ void* ixb_session_stream(ixb_session* s);    /* the cudaStream_t every launch go
  * or device memory with IXB_OUT_DEVICE). Copies are issued on the session stream. */
 int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, int flags);
 int ixb_session_wait(ixb_session* s, int timeout_ms);
+/* Pipelined asynchronous run, the reference's ignite_run_async / ignite_wait (c_api/ignite.h:102-124):
+ * the images are copied in on one copy stream, the network runs on the compute stream, the heads
+ * are copied out on another copy stream. Two runs alternate between the plan's two staging and
+ * egress slots, so one run's copies overlap the other's compute. images / egress are host
+ * pointers (pinned, for the copies to overlap) or device pointers; both must stay valid until the
+ * ticket completes. Tickets count up from 1; ticket t uses slot t % 2, and a submit whose slot is
+ * still held by ticket t - 2 first waits for it (60 s at most). ixb_session_run is refused while
+ * submitted runs are in flight. ixb_session_wait_ticket returns 0 at once for a ticket already
+ * collected, and IXB_ERR_TIMEOUT if the run has not finished within timeout_ms. */
+int ixb_session_submit(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, uint64_t* ticket);
+int ixb_session_wait_ticket(ixb_session* s, uint64_t ticket, int timeout_ms);
+/* The compute stream and the two copy streams (cudaStream_t) of a session. */
+int ixb_session_streams(ixb_session* s, void** compute, void** h2d, void** d2h);
 /* Device milliseconds of the last completed run (CUDA events around the graph launch). */
 int ixb_session_last_ms(ixb_session* s, float* ms);
 /* Number of kernels one run of `batch` images launches. */

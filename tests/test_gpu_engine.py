@@ -123,3 +123,29 @@ def test_profile_reports_every_op():
     assert len(ms) == len(sess.plan.ops) and all(v > 0 for v in ms)
     assert sess.launches(2) == 1 + len(sess.plan.ops)
     sess.close()
+
+
+def test_submitted_runs_match_synchronous_runs():
+    """Pipelined submits (two slots, three streams) return the same heads as ``run``, in order,
+    whether waited at once, two in flight, or retired by a later submit; mixed batch sizes."""
+    import torch
+    sess = InferenceSession.from_spec("yolov8n", imgsz=96, max_batch=4)
+    batches = [random_images(b, 96, seed=40 + i) for i, b in enumerate((4, 3, 4, 1, 2, 4))]
+    ref = [np.array(sess.run(x)) for x in batches]
+    hs = [sess.run_async(x) for x in batches[:2]]
+    assert np.array_equal(hs[0].wait(), ref[0]) and np.array_equal(hs[1].wait(), ref[1])
+    # four submits without waiting: the third and fourth retire the first two
+    hs = [sess.run_async(torch.from_numpy(x).pin_memory() if i % 2 else x) for i, x in enumerate(batches[2:])]
+    for h, r in zip(hs, ref[2:]):
+        assert np.array_equal(h.wait(), r)
+    assert hs[0].wait() is hs[0].wait()
+    # caller-provided output buffer, device input
+    out = np.zeros((4, sess.out_bytes), dtype=np.int8)
+    h = sess.run_async(torch.from_numpy(batches[0]).cuda(), out=out)
+    h.wait()
+    assert np.array_equal(out, ref[0])
+    # a synchronous run after submits drains them first
+    h = sess.run_async(batches[1])
+    assert np.array_equal(np.array(sess.run(batches[3])), ref[3])
+    assert np.array_equal(h.wait(), ref[1])
+    sess.close()
