@@ -259,7 +259,8 @@ def run_gpu(args):
     B = args.batch
     imgs = random_images(B, args.imgsz, seed=100 + rank)
     pinned_in = torch.from_numpy(imgs).pin_memory()
-    pinned_out = [torch.empty((B, sess.out_bytes), dtype=torch.int8).pin_memory().numpy() for _ in range(2)]
+    depth = sess.pipeline_depth
+    pinned_out = [torch.empty((B, sess.out_bytes), dtype=torch.int8).pin_memory().numpy() for _ in range(depth)]
     sess.stage_input(imgs)
     dev = torch.device("cuda", local)
     h_compute, h_h2d, h_d2h = sess.streams()
@@ -271,15 +272,15 @@ def run_gpu(args):
         L.check(lib.ixb_session_wait(sess._h, 60000))
 
     def e2e_steps(k):
-        """k batches through GraphSession.run_async: pinned images in, pinned heads out, two in
-        flight; step i's H2D and step i-1's D2H overlap the compute between them."""
-        prev = None
+        """k batches through GraphSession.run_async: pinned images in, pinned heads out, up to
+        ``depth`` in flight, so step i+1's H2D and step i-1's D2H overlap step i's compute."""
+        hs = []
         for i in range(k):
-            h = sess.run_async(pinned_in, out=pinned_out[i & 1])
-            if prev is not None:
-                prev.wait(60000)
-            prev = h
-        prev.wait(60000)
+            hs.append(sess.run_async(pinned_in, out=pinned_out[i % depth]))
+            if len(hs) == depth:
+                hs.pop(0).wait(60000)
+        for h in hs:
+            h.wait(60000)
 
     def timed_e2e(k):
         barrier(world)
@@ -344,7 +345,7 @@ def run_gpu(args):
                 "h2d_bytes_per_step": int(B * sess.in_image_bytes), "d2h_bytes_per_step": int(B * sess.out_bytes),
                 "path": "GraphSession.run_async (C ABI ixb_session_submit / ixb_session_wait_ticket): pinned host "
                         "images -> H2D stream -> graph on the compute stream -> D2H stream -> pinned host heads, "
-                        "two batches in flight; CUDA events from the first H2D to the last D2H"},
+                        f"{depth} batches in flight; CUDA events from the first H2D to the last D2H"},
         "roofline": {"bound": "hbm", "kernel": "ixb::conv_kernel (all conv launches of one step)",
                      "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,

@@ -17,7 +17,8 @@ IXB_OK = 0
 ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
 IXB_ERR_TIMEOUT = -3
 MAX_SEGS = 4
-API_VERSION = 3
+API_VERSION = 4
+MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH = 1, 2, 4, 8
 OP_CONV, OP_POOL = 0, 1
@@ -55,7 +56,9 @@ class Plan(C.Structure):
                 ("convs", C.POINTER(ConvDesc)), ("pools", C.POINTER(PoolDesc)), ("ops", C.POINTER(Op)),
                 ("images_offset", C.c_uint64), ("input_lut_offset", C.c_uint64), ("input", Segment),
                 ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64), ("arena_bytes", C.c_uint64),
-                ("images_offset_alt", C.c_uint64), ("egress_offset_alt", C.c_uint64)]
+                ("extra_slots", C.c_int32), ("reserved", C.c_int32),
+                ("extra_images_offset", C.c_uint64 * MAX_EXTRA_SLOTS),
+                ("extra_egress_offset", C.c_uint64 * MAX_EXTRA_SLOTS)]
 
 
 class IxbError(RuntimeError):

@@ -633,7 +633,8 @@ struct ixb_session {
   std::vector<ixb_conv_desc> convs;
   std::vector<ixb_pool_desc> pools;
   std::vector<ixb_op> ops;
-  // launches and graphs per (batch, slot): key = 2 * batch + slot
+  // launches and graphs per (batch, slot): key = batch * kSlots + slot
+  static constexpr int kSlots = 1 + IXB_MAX_EXTRA_SLOTS;
   std::map<int, std::vector<ConvLaunch>> conv_launch;
   std::map<int, std::vector<PoolLaunch>> pool_launch;
   std::map<int, cudaGraphExec_t> graphs;
@@ -644,25 +645,26 @@ struct ixb_session {
     uint64_t ticket = 0;
     bool busy = false;
     cudaEvent_t h2d_done = nullptr, t0 = nullptr, t1 = nullptr, d2h_done = nullptr;
-  } slots[2];
+  } slots[kSlots];
   uint64_t next_ticket = 1;
 
-  bool two_slots() const { return plan.images_offset_alt && plan.egress_offset_alt; }
-  uint64_t images_at(int slot) const { return slot ? plan.images_offset_alt : plan.images_offset; }
-  uint64_t egress_at(int slot) const { return slot ? plan.egress_offset_alt : plan.egress_offset; }
+  int depth() const { return 1 + plan.extra_slots; }
+  int slot_of(uint64_t ticket) const { return (int)((ticket - 1) % (uint64_t)depth()); }
+  uint64_t images_at(int slot) const { return slot ? plan.extra_images_offset[slot - 1] : plan.images_offset; }
+  uint64_t egress_at(int slot) const { return slot ? plan.extra_egress_offset[slot - 1] : plan.egress_offset; }
 
   int prepare(int batch, int slot = 0) {
-    const int key = 2 * batch + slot;
+    const int key = batch * kSlots + slot;
     if (conv_launch.count(key)) return 0;
     if (slot) {
-      // the second slot differs only in where the head convs write the egress
+      // other slots differ only in where the head convs write the egress
       if (int r = prepare(batch, 0)) return r;
-      std::vector<ConvLaunch> cl = conv_launch[2 * batch];
-      const long long delta = (long long)plan.egress_offset_alt - (long long)plan.egress_offset;
+      std::vector<ConvLaunch> cl = conv_launch[batch * kSlots];
+      const long long delta = (long long)egress_at(slot) - (long long)plan.egress_offset;
       for (ConvLaunch& L : cl)
         if (L.p.out_nchw) L.p.egress += delta;
       conv_launch[key] = std::move(cl);
-      pool_launch[key] = pool_launch[2 * batch];
+      pool_launch[key] = pool_launch[batch * kSlots];
       return 0;
     }
     std::vector<ConvLaunch> cl(convs.size());
@@ -681,7 +683,7 @@ struct ixb_session {
 
   int enqueue_op(int batch, int i, int slot = 0) {
     const ixb_op& op = ops[i];
-    const int key = 2 * batch + slot;
+    const int key = batch * kSlots + slot;
     if (op.kind == IXB_OP_CONV) return launch_conv(conv_launch[key][op.index], stream);
     return launch_pool(pool_launch[key][op.index], stream);
   }
@@ -700,7 +702,7 @@ struct ixb_session {
   }
 
   int graph_for(int batch, cudaGraphExec_t* out, int slot = 0) {
-    const int key = 2 * batch + slot;
+    const int key = batch * kSlots + slot;
     auto it = graphs.find(key);
     if (it != graphs.end()) {
       *out = it->second;
@@ -724,7 +726,11 @@ struct ixb_session {
     return 0;
   }
 
-  bool any_busy() const { return slots[0].busy || slots[1].busy; }
+  bool any_busy() const {
+    for (const Slot& sl : slots)
+      if (sl.busy) return true;
+    return false;
+  }
 };
 
 // Poll an event until it completes or the timeout runs out (spin first: a step takes milliseconds).
@@ -811,12 +817,12 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
     bad = fail(IXB_ERR_INVALID, "stem input view must be the img_h x img_w 3-channel image");
   else if (plan->egress_offset + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes)
     bad = fail(IXB_ERR_INVALID, "egress outside the arena");
-  else if ((plan->images_offset_alt != 0) != (plan->egress_offset_alt != 0))
-    bad = fail(IXB_ERR_INVALID, "the second pipeline slot needs both a staging and an egress buffer");
-  else if (plan->images_offset_alt &&
-           (plan->images_offset_alt % 16 || plan->images_offset_alt + img_bytes > s->arena_bytes ||
-            plan->egress_offset_alt + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes))
-    bad = fail(IXB_ERR_INVALID, "second pipeline slot outside the arena");
+  else if (plan->extra_slots < 0 || plan->extra_slots > IXB_MAX_EXTRA_SLOTS)
+    bad = fail(IXB_ERR_INVALID, "extra_slots outside [0, IXB_MAX_EXTRA_SLOTS]");
+  for (int i = 0; !bad && i < plan->extra_slots; ++i)
+    if (plan->extra_images_offset[i] % 16 || plan->extra_images_offset[i] + img_bytes > s->arena_bytes ||
+        plan->extra_egress_offset[i] + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes)
+      bad = fail(IXB_ERR_INVALID, "pipeline slot " + std::to_string(i + 1) + " outside the arena");
   if (!bad) bad = s->prepare(B);
   if (bad) {
     if (s->own_arena) cudaFree(s->arena);
@@ -932,14 +938,13 @@ int ixb_session_wait(ixb_session* s, int timeout_ms) {
 
 int ixb_session_submit(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, uint64_t* ticket) {
   if (!s || !images || !egress || !ticket) return fail(IXB_ERR_INVALID, "null argument");
-  if (!s->two_slots()) return fail(IXB_ERR_UNSUPPORTED, "the plan has no second pipeline slot");
   if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
   if (s->pending) return fail(IXB_ERR_INVALID, "a synchronous run is pending");
   IXB_CUDA(cudaSetDevice(s->device));
   const uint64_t t = s->next_ticket;
-  const int slot = (int)(t & 1);
+  const int slot = s->slot_of(t);
   ixb_session::Slot& sl = s->slots[slot];
-  if (sl.busy)  // the run two tickets back still owns this slot's buffers
+  if (sl.busy)  // the run `depth` tickets back still owns this slot's buffers
     if (int r = ixb_session_wait_ticket(s, sl.ticket, 60000)) return r;
   if (int r = s->prepare(batch, slot)) return r;
   cudaGraphExec_t exec;
@@ -965,7 +970,7 @@ int ixb_session_submit(ixb_session* s, const uint8_t* images, int batch, int8_t*
 int ixb_session_wait_ticket(ixb_session* s, uint64_t ticket, int timeout_ms) {
   if (!s) return fail(IXB_ERR_INVALID, "null session");
   if (ticket == 0 || ticket >= s->next_ticket) return fail(IXB_ERR_INVALID, "unknown ticket");
-  ixb_session::Slot& sl = s->slots[ticket & 1];
+  ixb_session::Slot& sl = s->slots[s->slot_of(ticket)];
   if (!sl.busy || sl.ticket != ticket) return 0;  // already completed and collected
   if (int r = wait_event(sl.d2h_done, timeout_ms)) return r;
   sl.busy = false;

@@ -93,8 +93,8 @@ class DevicePlan:
     ops: List[Tuple[int, int]]
     const_offset: int
     const_blob: np.ndarray
-    images_offset_alt: int = 0
-    egress_offset_alt: int = 0
+    extra_images_offsets: Tuple[int, ...] = ()
+    extra_egress_offsets: Tuple[int, ...] = ()
     c_plan: object = None
     keep: list = field(default_factory=list)
 
@@ -206,9 +206,13 @@ def _storage_groups(ir: GraphIR, heads: set) -> List[List[str]]:
     return groups
 
 
-def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
+def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePlan:
+    """Arena layout, packed constants and kernel descriptors for ``ir`` at up to ``max_batch``
+    images; ``pipeline_depth`` staging/egress pairs serve the submitted-run ring."""
     if max_batch < 1:
         raise ValueError("max_batch must be >= 1")
+    if not 1 <= pipeline_depth <= 1 + L.MAX_EXTRA_SLOTS:
+        raise ValueError(f"pipeline_depth must be in [1, {1 + L.MAX_EXTRA_SLOTS}]")
     timg = ir.tensors[ir.input]
     H, W = timg.height, timg.width
     head_tensor = dict(ir.outputs)
@@ -222,7 +226,7 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
         return o
 
     images_offset = alloc(max_batch * 3 * H * W)
-    images_offset_alt = alloc(max_batch * 3 * H * W)     # second pipeline slot
+    extra_images = tuple(alloc(max_batch * 3 * H * W) for _ in range(pipeline_depth - 1))
     input_lut_offset = alloc(256)
     input_store = Store(alloc(max_batch * (H + 2) * (W + 4) * 8), 0, 0, 3, H, W, 0)
     stores: Dict[str, Store] = {}
@@ -248,7 +252,7 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
         eb += t.channels * t.height * t.width
     egress_image_bytes = eb
     egress_offset = alloc(max_batch * egress_image_bytes)
-    egress_offset_alt = alloc(max_batch * egress_image_bytes)
+    extra_egress = tuple(alloc(max_batch * egress_image_bytes) for _ in range(pipeline_depth - 1))
 
     # constants
     const_parts: List[Tuple[int, np.ndarray]] = []
@@ -369,8 +373,8 @@ def build_plan(ir: GraphIR, max_batch: int) -> DevicePlan:
                       images_offset=images_offset, input_lut_offset=const_offset + ilut_rel,
                       input_store=input_store, egress_offset=egress_offset, egress_image_bytes=egress_image_bytes,
                       head_offsets=head_offsets, stores=stores, convs=convs, pools=pools, ops=ops,
-                      const_offset=const_offset, const_blob=blob, images_offset_alt=images_offset_alt,
-                      egress_offset_alt=egress_offset_alt)
+                      const_offset=const_offset, const_blob=blob, extra_images_offsets=extra_images,
+                      extra_egress_offsets=extra_egress)
 
 
 def _merge_segments(segs: List[L.Segment]) -> List[L.Segment]:
@@ -408,8 +412,10 @@ def c_plan(dp: DevicePlan) -> L.Plan:
     p.egress_offset = dp.egress_offset
     p.egress_image_bytes = dp.egress_image_bytes
     p.arena_bytes = dp.arena_bytes
-    p.images_offset_alt = dp.images_offset_alt
-    p.egress_offset_alt = dp.egress_offset_alt
+    p.extra_slots = len(dp.extra_images_offsets)
+    for i, (a, b) in enumerate(zip(dp.extra_images_offsets, dp.extra_egress_offsets)):
+        p.extra_images_offset[i] = a
+        p.extra_egress_offset[i] = b
     dp.keep = [convs, pools, ops]
     dp.c_plan = p
     return p

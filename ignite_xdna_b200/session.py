@@ -38,8 +38,8 @@ class RunHandle:
 
     ``wait`` blocks until the batch's heads are in host memory and returns them as int8
     [B, egress_image_bytes]. Without an ``out`` buffer the result lives in the session's pinned
-    egress slot, which the submit two tickets later reuses: a handle still unwaited at that point
-    is completed first and keeps a private copy."""
+    egress slot, which the submit ``pipeline_depth`` tickets later reuses: a handle still unwaited
+    at that point is completed first and keeps a private copy."""
 
     def __init__(self, session: "GraphSession", ticket: int, batch: int, egress: np.ndarray, keep: Any):
         self._s = session
@@ -76,7 +76,7 @@ class RunHandle:
 class GraphSession:
     """Whole-network XINT8 YOLOv8 on one B200: persistent arena, one CUDA graph per batch size."""
 
-    def __init__(self, ir: GraphIR, device_index: int = 0, max_batch: int = 64):
+    def __init__(self, ir: GraphIR, device_index: int = 0, max_batch: int = 64, pipeline_depth: int = 3):
         torch = _torch()
         if not torch.cuda.is_available():
             raise RuntimeError("GraphSession needs a CUDA device; this engine has no CPU path")
@@ -85,7 +85,7 @@ class GraphSession:
         self.device_index = int(device_index)
         self.device = torch.device("cuda", self.device_index)
         self.max_batch = int(max_batch)
-        self.plan: DevicePlan = build_plan(ir, self.max_batch)
+        self.plan: DevicePlan = build_plan(ir, self.max_batch, pipeline_depth)
         self.arena = torch.zeros(self.plan.arena_bytes, dtype=torch.uint8, device=self.device)
         blob = torch.from_numpy(self.plan.const_blob)
         self.arena[self.plan.const_offset:self.plan.const_offset + blob.numel()].copy_(blob.to(self.device))
@@ -104,9 +104,10 @@ class GraphSession:
         self.last_dispatch_ms = 0.0
         self.last_host_ms = 0.0
         self._next_ticket = 1
-        self._inflight = [None, None]     # RunHandle per pipeline slot
-        self._pin_in = [None, None]
-        self._pin_out = [None, None]
+        self.pipeline_depth = 1 + len(self.plan.extra_images_offsets)
+        self._inflight = [None] * self.pipeline_depth     # RunHandle per pipeline slot
+        self._pin_in = [None] * self.pipeline_depth
+        self._pin_out = [None] * self.pipeline_depth
 
     # ------------------------------------------------------------------ status
     @property
@@ -183,15 +184,16 @@ class GraphSession:
         for h in self._inflight:
             if h is not None and not h.done:
                 h._retire()
-        self._inflight = [None, None]
+        self._inflight = [None] * self.pipeline_depth
 
     def run_async(self, input_tensor: Any, unswizzle: bool = True, out: Optional[np.ndarray] = None) -> RunHandle:
         """Submit a batch and return at once (the reference's ``InferenceSession.run_async``,
         runtime/session.py:1280-1318).
 
         The images' host-to-device copy, the network and the heads' device-to-host copy run on
-        three streams ordered by events, and consecutive submits alternate between two staging
-        and egress slots, so one batch's copies overlap the next batch's compute. ``input_tensor``
+        three streams ordered by events, and consecutive submits rotate through
+        ``pipeline_depth`` staging and egress slots (three by default), so one batch's H2D copy,
+        another's compute and a third's D2H copy proceed together. ``input_tensor``
         is as for ``run``; a pinned CPU or a CUDA tensor is copied from in place (and must not be
         changed until the handle completes), anything else is first copied into the slot's pinned
         staging buffer. ``out``, if given, is an int8 [>=B, egress_image_bytes] array (pinned for
@@ -199,7 +201,7 @@ class GraphSession:
         torch = _torch()
         x = self._as_pixels(input_tensor)
         b = self._check_shape(x.shape)
-        slot = self._next_ticket & 1
+        slot = (self._next_ticket - 1) % self.pipeline_depth
         prev = self._inflight[slot]
         if prev is not None and not prev.done:
             prev._retire()
@@ -380,12 +382,12 @@ class InferenceSession:
 
     @classmethod
     def from_spec(cls, model: str = "yolov8n", seed: int = 0, imgsz: int = 640, device_index: int = 0,
-                  max_batch: int = 64, **kw) -> GraphSession:
+                  max_batch: int = 64, pipeline_depth: int = 3, **kw) -> GraphSession:
         """Open a session on the seeded synthetic XINT8 graph ``model`` in {yolov8n, yolov8s, yolov8m}."""
         from .yolov8 import build_yolov8
         variant = model.replace("yolov8", "")
         return GraphSession(build_yolov8(variant, imgsz=imgsz, seed=seed, **kw), device_index=device_index,
-                            max_batch=max_batch)
+                            max_batch=max_batch, pipeline_depth=pipeline_depth)
 
     @classmethod
     def from_file(cls, path: Union[str, Path], device_index: int = 0, max_batch: int = 64, **kwargs) -> GraphSession:

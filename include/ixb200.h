@@ -44,7 +44,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 3
+#define IXB_API_VERSION 4
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -108,6 +108,7 @@ typedef struct ixb_pool_desc {  /* SPPF: out_k = pool5^k(in), k = 1..3, pad -128
 #define IXB_OP_POOL 1
 typedef struct ixb_op { int32_t kind, index; } ixb_op;
 
+#define IXB_MAX_EXTRA_SLOTS 3
 typedef struct ixb_plan {
   int32_t api_version;
   int32_t max_batch;
@@ -122,8 +123,12 @@ typedef struct ixb_plan {
   uint64_t egress_offset;       /* int8 [max_batch][egress_image_bytes] */
   uint64_t egress_image_bytes;
   uint64_t arena_bytes;
-  uint64_t images_offset_alt;   /* second pipeline slot: staging and egress of the same sizes */
-  uint64_t egress_offset_alt;   /* (0, 0: the session runs one slot and ixb_session_submit is refused) */
+  /* Further staging/egress pairs (same sizes as images_offset / egress_offset) for the
+   * ixb_session_submit ring, which is 1 + extra_slots deep; slot 0 is the pair above. */
+  int32_t extra_slots;          /* 0 .. IXB_MAX_EXTRA_SLOTS */
+  int32_t reserved;
+  uint64_t extra_images_offset[IXB_MAX_EXTRA_SLOTS];
+  uint64_t extra_egress_offset[IXB_MAX_EXTRA_SLOTS];
 } ixb_plan;
 
 typedef struct ixb_session ixb_session;
@@ -145,11 +150,12 @@ int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* eg
 int ixb_session_wait(ixb_session* s, int timeout_ms);
 /* Pipelined asynchronous run, the reference's ignite_run_async / ignite_wait (c_api/ignite.h:102-124):
  * the images are copied in on one copy stream, the network runs on the compute stream, the heads
- * are copied out on another copy stream. Two runs alternate between the plan's two staging and
- * egress slots, so one run's copies overlap the other's compute. images / egress are host
- * pointers (pinned, for the copies to overlap) or device pointers; both must stay valid until the
- * ticket completes. Tickets count up from 1; ticket t uses slot t % 2, and a submit whose slot is
- * still held by ticket t - 2 first waits for it (60 s at most). ixb_session_run is refused while
+ * are copied out on another copy stream, all ordered by events. Submitted runs rotate through the
+ * plan's 1 + extra_slots staging/egress pairs, so with three slots one run's H2D copy, another's
+ * compute and a third's D2H copy proceed together. images / egress are host pointers (pinned, for
+ * the copies to overlap) or device pointers; both must stay valid until the ticket completes.
+ * Tickets count up from 1; ticket t uses slot (t - 1) % depth, and a submit whose slot is still
+ * held by ticket t - depth first waits for it (60 s at most). ixb_session_run is refused while
  * submitted runs are in flight. ixb_session_wait_ticket returns 0 at once for a ticket already
  * collected, and IXB_ERR_TIMEOUT if the run has not finished within timeout_ms. */
 int ixb_session_submit(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, uint64_t* ticket);

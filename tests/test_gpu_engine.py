@@ -125,16 +125,18 @@ def test_profile_reports_every_op():
     sess.close()
 
 
-def test_submitted_runs_match_synchronous_runs():
-    """Pipelined submits (two slots, three streams) return the same heads as ``run``, in order,
-    whether waited at once, two in flight, or retired by a later submit; mixed batch sizes."""
+@pytest.mark.parametrize("depth", [1, 2, 3])
+def test_submitted_runs_match_synchronous_runs(depth):
+    """Pipelined submits (a ring of ``depth`` slots, three streams) return the same heads as
+    ``run``, in order, whether waited at once, several in flight, or retired by a later submit;
+    mixed batch sizes."""
     import torch
-    sess = InferenceSession.from_spec("yolov8n", imgsz=96, max_batch=4)
+    sess = InferenceSession.from_spec("yolov8n", imgsz=96, max_batch=4, pipeline_depth=depth)
     batches = [random_images(b, 96, seed=40 + i) for i, b in enumerate((4, 3, 4, 1, 2, 4))]
     ref = [np.array(sess.run(x)) for x in batches]
     hs = [sess.run_async(x) for x in batches[:2]]
     assert np.array_equal(hs[0].wait(), ref[0]) and np.array_equal(hs[1].wait(), ref[1])
-    # four submits without waiting: the third and fourth retire the first two
+    # four submits without waiting: submits beyond the ring's depth retire the oldest runs
     hs = [sess.run_async(torch.from_numpy(x).pin_memory() if i % 2 else x) for i, x in enumerate(batches[2:])]
     for h, r in zip(hs, ref[2:]):
         assert np.array_equal(h.wait(), r)

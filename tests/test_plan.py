@@ -41,6 +41,10 @@ def test_plan_storage_is_disjoint_and_aligned(variant):
     spans[dp.images_offset] = 64 * 3 * dp.img_h * dp.img_w
     spans[dp.input_store.offset] = 64 * (dp.img_h + 2) * (dp.img_w + 4) * 8
     spans[dp.egress_offset] = 64 * dp.egress_image_bytes
+    assert len(dp.extra_images_offsets) == len(dp.extra_egress_offsets) == 2
+    for a, e in zip(dp.extra_images_offsets, dp.extra_egress_offsets):
+        spans[a] = 64 * 3 * dp.img_h * dp.img_w
+        spans[e] = 64 * dp.egress_image_bytes
     spans[dp.const_offset] = dp.const_blob.size
     iv = sorted(spans.items())
     for (a, n), (b, _) in zip(iv, iv[1:]):
