@@ -89,16 +89,52 @@ def cpu_baseline(ir, imgsz, cores):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
+    """SM clock and throttle reasons sampled DURING the timed region: NVML every 5 ms in a thread
+    (the timed region lasts tens of milliseconds), else ``nvidia-smi -lms 100``. Reads only."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, device_index):
         self.dev = device_index
-        self.rows = []
+        self.rows = []          # (sm_mhz, max_mhz, set of reasons)
         self.proc = None
+        self.nvml = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.dev)
+        try:
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
 
     def __enter__(self):
+        try:
+            self.nvml, h = self._nvml_handle()
+            mx = self.nvml.nvmlDeviceGetMaxClockInfo(h, self.nvml.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        mhz = self.nvml.nvmlDeviceGetClockInfo(h, self.nvml.NVML_CLOCK_SM)
+                        bits = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except Exception:
+                        break
+                    self.rows.append((float(mhz), float(mx), {n for n, b in self.REASONS.items() if bits & b}))
+                    self.stop.wait(0.005)
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "100"],
@@ -110,10 +146,19 @@ class ClockSampler:
         return self
 
     def _read(self):
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+            r = [x.strip() for x in line.split(",")]
+            try:
+                self.rows.append((float(r[1]), float(r[2]),
+                                  {n for n, v in zip(names, r[5:9]) if v.lower().startswith("active")}))
+            except (ValueError, IndexError):
+                continue
 
     def __exit__(self, *a):
+        self.stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -123,20 +168,12 @@ class ClockSampler:
         return False
 
     def summary(self):
-        mhz, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for r in self.rows:
-            try:
-                mhz.append(float(r[1]))
-                mx = float(r[2])
-            except (ValueError, IndexError):
-                continue
-            for n, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not mhz:
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(mhz)}
+        reasons = set().union(*(r[2] for r in self.rows))
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.rows[-1][1],
+                "reasons": sorted(reasons), "samples": len(self.rows),
+                "source": "nvml 5 ms" if self.nvml is not None else "nvidia-smi 100 ms"}
 
 
 # ---------------------------------------------------------------- helpers
