@@ -15,7 +15,9 @@ LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 IXB_OK = 0
 ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
+IXB_ERR_INVALID = -1
 IXB_ERR_TIMEOUT = -3
+IXB_ERR_UNSUPPORTED = -5
 MAX_SEGS = 4
 API_VERSION = 4
 MAX_EXTRA_SLOTS = 3
@@ -98,6 +100,7 @@ _SIGS = {
     "ixb_i8gemm_srs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                  C.c_int, C.c_void_p]),
     "ixb_i8gemm_i32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ixb_gemm_plan_info": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int32), C.c_int]),
     "ixb_w4a8_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                 C.c_int, C.c_void_p]),
     "ixb_w4a8_gemv": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,

@@ -608,6 +608,131 @@ int launch_quantize(const uint8_t* images, const int8_t* lut, int batch, int h, 
   return 0;
 }
 
+// ---------------------------------------------------------------- int8 GEMM
+PFN_cuTensorMapEncodeTiled_v12000 tiled_encoder(std::string& err) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&enc, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !enc) {
+      enc = nullptr;
+      err = "cuTensorMapEncodeTiled is not available";
+    }
+  }
+  return enc;
+}
+
+// Tensor map of an int8 [rows][K] K-major matrix: boxes of 128 bytes of K by box_rows rows,
+// 128-byte swizzled (the UMMA K-major SW128 layout).
+int encode_kmajor(CUtensorMap* map, const void* base, long long rows, int K, int box_rows, std::string& err) {
+  auto enc = tiled_encoder(err);
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
+    return -1;
+  }
+  return 0;
+}
+
+struct GemmLaunch {
+  GemmParams p;
+  int grid, smem;
+};
+
+// Tile shape, pipeline depth and grid for an M x N x K int8 GEMM. The accumulator of a tile is
+// MT blocks of 128 rows by BN columns; two of them (2 * MT * BN <= 512 TMEM columns) let the
+// epilogue of one tile overlap the next. MT grows only while the tiles still cover every SM.
+int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err) {
+  if (M < 1 || N < 16 || N % 16 || K < 16 || K % 16) {
+    err = "GEMM shape needs M >= 1, N and K multiples of 16";
+    return -1;
+  }
+  if (K > 65536) {
+    err = "K above 65536 could overflow the int32 accumulator";
+    return -1;
+  }
+  GemmParams& p = L.p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.bn = N <= 256 ? N : (N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 256));
+  p.n_tiles = (N + p.bn - 1) / p.bn;
+  const int sms = sm_count();
+  p.mt = 1;
+  for (int cand : {4, 2}) {
+    const long long tiles = ((M + 128LL * cand - 1) / (128LL * cand)) * p.n_tiles;
+    if (cand * p.bn <= 256 && tiles >= sms) {
+      p.mt = cand;
+      break;
+    }
+  }
+  p.m_tiles = (int)((M + 128LL * p.mt - 1) / (128LL * p.mt));
+  p.kblocks = (K + kGemmBK - 1) / kGemmBK;
+  p.stage_bytes = p.mt * kGemmABlock + p.bn * kGemmBK;
+  p.stage_tx = p.stage_bytes;
+  const int budget = kSmemLimit - 1024 - 256;
+  p.stages = std::min(kGemmMaxStages, budget / p.stage_bytes);
+  if (p.stages < 2) {
+    err = "two GEMM pipeline stages do not fit shared memory";
+    return -1;
+  }
+  p.bar_off = p.stages * p.stage_bytes;
+  p.acc_cols = p.mt * p.bn;
+  int cols = 32;
+  while (cols < 2 * p.acc_cols) cols *= 2;
+  p.tmem_cols = cols;
+  p.idesc = umma_idesc_s8(128, p.bn);
+  const long long tiles = (long long)p.m_tiles * p.n_tiles;
+  if (tiles > 0x7fffffffLL) {
+    err = "too many GEMM tiles";
+    return -1;
+  }
+  L.grid = (int)std::min<long long>(tiles, sms);
+  L.smem = 1024 + p.bar_off + 256;
+  return 0;
+}
+
+int launch_gemm(GemmLaunch& L, cudaStream_t st) {
+  static bool attr = false;
+  if (!attr) {
+    IXB_CUDA(cudaFuncSetAttribute(gemm_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    attr = true;
+  }
+  gemm_kernel<8><<<L.grid, gemm_threads(8), L.smem, st>>>(L.p);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
+int run_i8gemm(const int8_t* a, const int8_t* b, const int32_t* bias, int8_t* out8, int32_t* out32, int M, int N,
+               int K, int shift, int kind, void* stream) {
+  if (!a || !b || (kind == GEMM_OUT_SRS && (!bias || !out8)) || (kind == GEMM_OUT_I32 && !out32))
+    return fail(IXB_ERR_INVALID, "null argument");
+  if (!aligned16(a) || !aligned16(b) || (bias && !aligned16(bias)) || (out8 && !aligned16(out8)) ||
+      (out32 && !aligned16(out32)))
+    return fail(IXB_ERR_INVALID, "GEMM operands must be 16-byte aligned");
+  if (kind == GEMM_OUT_SRS && (shift < 0 || shift > 23)) return fail(IXB_ERR_INVALID, "shift outside [0, 23]");
+  GemmLaunch L;
+  std::string err;
+  if (plan_gemm(L, M, N, K, err)) return fail(IXB_ERR_INVALID, err);
+  L.p.out_kind = kind;
+  L.p.bias = bias;
+  L.p.shift = shift;
+  L.p.out8 = out8;
+  L.p.out32 = out32;
+  if (encode_kmajor(&L.p.ta, a, M, K, 128, err) || encode_kmajor(&L.p.tb, b, N, K, L.p.bn, err))
+    return fail(IXB_ERR_CUDA, err);
+  return launch_gemm(L, static_cast<cudaStream_t>(stream));
+}
+
 int read_device_error() {
   unsigned int v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_dev_error, sizeof v);
@@ -1085,6 +1210,33 @@ int ixb_pool_layer(const ixb_pool_desc* d, void* arena, uint64_t arena_bytes, in
   std::string err;
   if (build_pool(*d, static_cast<uint8_t*>(arena), arena_bytes, batch, L, err)) return fail(IXB_ERR_INVALID, err);
   return launch_pool(L, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_i8gemm_srs(const int8_t* a, const int8_t* b, const int32_t* bias, int8_t* out, int M, int N, int K, int shift,
+                   void* stream) {
+  return run_i8gemm(a, b, bias, out, nullptr, M, N, K, shift, GEMM_OUT_SRS, stream);
+}
+
+int ixb_i8gemm_i32(const int8_t* a, const int8_t* b, int32_t* out, int M, int N, int K, void* stream) {
+  return run_i8gemm(a, b, nullptr, nullptr, out, M, N, K, 0, GEMM_OUT_I32, stream);
+}
+
+int ixb_w4a8_gemm(const int8_t*, const uint8_t*, const int8_t*, const int32_t*, int8_t*, int, int, int, void*) {
+  return fail(IXB_ERR_UNSUPPORTED, "W4A8 GEMM is not built yet");
+}
+int ixb_w4a8_gemv(const int8_t*, const uint8_t*, const int8_t*, const int32_t*, int8_t*, int, int, void*) {
+  return fail(IXB_ERR_UNSUPPORTED, "W4A8 GEMV is not built yet");
+}
+
+int ixb_gemm_plan_info(int M, int N, int K, int32_t* info, int n) {
+  if (!info) return fail(IXB_ERR_INVALID, "null argument");
+  GemmLaunch L;
+  std::string err;
+  if (plan_gemm(L, M, N, K, err)) return fail(IXB_ERR_INVALID, err);
+  const int32_t v[10] = {L.p.bn, L.p.mt, L.p.m_tiles, L.p.n_tiles, L.p.kblocks, L.p.stages, L.grid, L.smem,
+                         L.p.tmem_cols, L.p.stage_bytes};
+  for (int i = 0; i < n && i < 10; ++i) info[i] = v[i];
+  return 0;
 }
 
 int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w, int8_t* padded_nhwc4,

@@ -1,16 +1,233 @@
-// int8 GEMM + pow2 SRS and W4A8 GEMM/GEMV entry points.
+// int8 GEMM on the 5th-generation tensor cores (tcgen05, kind::i8) with the pow2 SRS epilogue,
+// and its raw int32 form.
+//
+//   out[m][n] = clamp(rne((sum_k a[m][k] * b[n][k] + bias[n]) >> shift), -128, 127)   (SRS)
+//   out[m][n] = sum_k a[m][k] * b[n][k]                                               (I32)
+//
+// Both are exact for K <= 65536, any int32 bias and shift <= 23: the product cannot overflow
+// int32, and a bias sum that would is saturated, which clamps to the same int8.
+//
+// a is int8 [M][K] row-major; b is int8 [N][K], i.e. B of C = A.B given K-major (the layout
+// int8 tensor-core GEMMs take). The rounding is round-half-to-even and the clamp saturates,
+// the SRS rule of the reference's engine (engine_emulator.py:149-162, engine.cc:186-191);
+// the int32 product is the exact integer GEMM of kernels/int8_matmul_sweep.
+//
+// Persistent and warp-specialised: one thread issues TMA tile loads (A: MT boxes of 128 rows x
+// 128 bytes of K, B: one box of BN rows x 128 bytes, both 128-byte swizzled), one thread issues
+// tcgen05.mma (M = 128 per block, N = BN, K = 32 per instruction, four per stage), and EPI warps
+// drain the two TMEM accumulators (MT blocks x BN columns each) through the integer epilogue, so
+// the epilogue of tile i overlaps the MMAs of tile i + 1. TMA zero-fills rows past M or N and K
+// past its end, so ragged shapes need no padding in memory.
 #pragma once
-#include "../../include/ixb200.h"
+#include <cstdint>
+#include <cuda.h>
+#include "ixb_ptx.cuh"
 
-extern "C" {
-int ixb_i8gemm_srs(const int8_t*, const int8_t*, const int32_t*, int8_t*, int, int, int, int, void*) {
-  return IXB_ERR_UNSUPPORTED;
+namespace ixb {
+
+constexpr int kGemmBK = 128;                 // K bytes per stage: one 128-byte swizzle row
+constexpr int kGemmABlock = 128 * kGemmBK;   // one 128-row A box
+constexpr int kGemmMaxStages = 8;
+enum : int { GEMM_OUT_SRS = 0, GEMM_OUT_I32 = 1 };
+
+struct GemmParams {
+  alignas(64) CUtensorMap ta;  // A [M][K], box {128 B, 128 rows}, SWIZZLE_128B
+  alignas(64) CUtensorMap tb;  // B [N][K], box {128 B, BN rows}, SWIZZLE_128B
+  int M, N, K;
+  int bn, mt, m_tiles, n_tiles, kblocks, stages;
+  int stage_bytes, stage_tx, bar_off;
+  int acc_cols, tmem_cols;
+  uint32_t idesc;
+  int out_kind;
+  const int32_t* bias;
+  int shift;
+  int8_t* out8;
+  int32_t* out32;
+};
+
+// K-major operand in the 128-byte swizzle layout TMA writes: rows of 128 bytes, 8-row atoms of
+// 1024 bytes (SBO), 16-byte chunks XOR-permuted by the row within the atom. Successive 32-byte
+// K steps advance the start address inside the atom.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;                // LBO: unused by swizzled K-major layouts
+  d |= (uint64_t)(1024 >> 4) << 32;      // SBO: next 8-row atom
+  d |= (uint64_t)1 << 46;                // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;                // layout: 128-byte swizzle
+  return d;
 }
-int ixb_i8gemm_i32(const int8_t*, const int8_t*, int32_t*, int, int, int, void*) { return IXB_ERR_UNSUPPORTED; }
-int ixb_w4a8_gemm(const int8_t*, const uint8_t*, const int8_t*, const int32_t*, int8_t*, int, int, int, void*) {
-  return IXB_ERR_UNSUPPORTED;
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
-int ixb_w4a8_gemv(const int8_t*, const uint8_t*, const int8_t*, const int32_t*, int8_t*, int, int, void*) {
-  return IXB_ERR_UNSUPPORTED;
+
+constexpr int gemm_threads(int epi) { return 32 * (epi + 2); }
+
+template <int EPI>
+__global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+  constexpr int PW = EPI, MW = EPI + 1;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  const int tiles = p.m_tiles * p.n_tiles;
+
+  if (warp == MW) {
+    tmem_alloc(tmem_slot, p.tmem_cols);
+    tmem_relinquish();
+  }
+  if (tid == PW * 32) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], EPI * 32);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.ta) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tb) : "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == PW) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int mtile = t / p.n_tiles, ntile = t - mtile * p.n_tiles;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * p.stage_bytes;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)p.stage_tx);
+          for (int b = 0; b < p.mt; ++b)
+            tma_load_2d(st + b * kGemmABlock, &p.ta, kb * kGemmBK, (mtile * p.mt + b) * 128, &full[s]);
+          tma_load_2d(st + p.mt * kGemmABlock, &p.tb, kb * kGemmBK, ntile * p.bn, &full[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == MW) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], aph ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + acc * p.acc_cols;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + s * p.stage_bytes);
+          const int ksteps = min(kGemmBK / 32, (p.K - kb * kGemmBK + 31) / 32);
+          for (int j = 0; j < ksteps; ++j) {
+            const uint64_t bd = umma_desc_sw128(st + p.mt * kGemmABlock + j * 32);
+            for (int b = 0; b < p.mt; ++b)
+              umma_s8(d0 + b * p.bn, umma_desc_sw128(st + b * kGemmABlock + j * 32), bd, p.idesc,
+                      (kb | j) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(&empty[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1;
+      }
+      if (issued) {
+        umma_commit(done);  // every MMA this CTA issued has finished before TMEM is released
+        mbar_wait(done, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    constexpr int NG = EPI / 4;
+    const int q = warp & 3, g = warp >> 2;
+    const int nch = p.bn / 16;
+    const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      if (!mbar_wait(&acc_full[acc], aph)) break;
+      tc_fence_after();
+      const int mtile = t / p.n_tiles, ntile = t - mtile * p.n_tiles;
+      const uint32_t base = tmem + acc * p.acc_cols + ((uint32_t)(q * 32) << 16);
+      for (int k = g; k < p.mt * nch; k += NG) {
+        const int b = k / nch, c = k - b * nch;
+        uint32_t v[16];
+        tmem_ld16(base + b * p.bn + c * 16, v);
+        tmem_ld_wait();
+        const int row = (mtile * p.mt + b) * 128 + q * 32 + lane;
+        const int col = ntile * p.bn + c * 16;
+        if (row >= p.M || col >= p.N) continue;
+        if (p.out_kind == GEMM_OUT_I32) {
+          uint4* o = reinterpret_cast<uint4*>(p.out32 + (long long)row * p.N + col);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+          const int4* b4 = reinterpret_cast<const int4*>(p.bias + col);
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int4 bb = __ldg(b4 + i);
+            const int bv[4] = {bb.x, bb.y, bb.z, bb.w};
+            uint32_t packed = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              // saturating adds: a sum past int32 saturates, which for shift <= 23 still clamps
+              // to the same int8 as the exact value
+              const int a = add_sat((int)v[4 * i + e], bv[e]);
+              const int r = clamp_i8(add_sat(a, hs + ((a >> s) & lsb)) >> s);
+              packed |= (uint32_t)(r & 0xFF) << (8 * e);
+            }
+            w[i] = packed;
+          }
+          *reinterpret_cast<uint4*>(p.out8 + (long long)row * p.N + col) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == MW) tmem_dealloc(tmem, p.tmem_cols);
 }
-}
+
+}  // namespace ixb

@@ -63,13 +63,17 @@ __device__ __forceinline__ unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: returns false (and raises the device flag) if the phase never completes.
+__device__ __forceinline__ bool wait_timed_out() {
+  return (*reinterpret_cast<volatile unsigned int*>(&g_dev_error) & DEV_ERR_WAIT_TIMEOUT) != 0;
+}
+// Bounded wait: returns false (and raises the device flag) if the phase never completes. Once any
+// wait has timed out, later waits give up at once, so a stuck launch ends after one time limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) break;
+    if (global_ns() - t0 > kWaitLimitNs || wait_timed_out()) break;
   }
   set_dev_error(DEV_ERR_WAIT_TIMEOUT);
   return false;
@@ -197,5 +201,10 @@ __device__ __forceinline__ int rne_shift(int x, int s) {
   return q + ((r > h) | ((r == h) & (q & 1)));
 }
 __device__ __forceinline__ int clamp_i8(int x) { return min(max(x, -128), 127); }
+__device__ __forceinline__ int add_sat(int a, int b) {
+  int d;
+  asm("add.sat.s32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 }  // namespace ixb

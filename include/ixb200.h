@@ -193,13 +193,19 @@ int ixb_conv_launch_info(const ixb_conv_desc* d, uint64_t arena_bytes, int batch
 int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w,
                         int8_t* padded_nhwc4, void* stream);
 
-/* int8 GEMM + pow2 SRS: out[m][n] = clamp(rne((sum_k a[m][k] * b[n][k] + bias[n]) >> shift), -128, 127).
- * a: int8 [M][K] row-major, b: int8 [N][K] (K-major), bias int32 [N]; M % 128 == 0,
- * N % 16 == 0, K % 32 == 0. All pointers device memory. */
+/* int8 GEMM + pow2 SRS (the int8 GEMM of kernels/int8_matmul_sweep with the SRS rule of
+ * engine_emulator.py:149-162): out[m][n] = clamp(rne((sum_k a[m][k] * b[n][k] + bias[n]) >> shift),
+ * -128, 127), round half to even. a: int8 [M][K] row-major; b: int8 [N][K], i.e. B of C = A.B stored
+ * K-major (pass B.T contiguous); bias int32 [N]; out int8 [M][N]. Device pointers, 16-byte aligned;
+ * M >= 1, N and K multiples of 16 (pad K with zeros), K <= 65536, shift in [0, 23]. Enqueued on
+ * `stream` (a cudaStream_t, NULL for the default stream); returns before the GEMM finishes. */
 int ixb_i8gemm_srs(const int8_t* a, const int8_t* b, const int32_t* bias, int8_t* out,
                    int M, int N, int K, int shift, void* stream);
-/* Same product without the epilogue: int32 out [M][N]. */
+/* Same product without the epilogue: int32 out [M][N] (exact). */
 int ixb_i8gemm_i32(const int8_t* a, const int8_t* b, int32_t* out, int M, int N, int K, void* stream);
+/* The launch plan of an M x N x K GEMM (host only, no GPU needed): {BN, MT, M tiles, N tiles,
+ * K blocks, stages, grid, shared bytes, TMEM columns, stage bytes}. */
+int ixb_gemm_plan_info(int M, int N, int K, int32_t* info, int n);
 
 /* W4A8: a int8 [M][K]; w uint8 [N][K/2] (two int4 per byte along K, even k in the low nibble);
  * gpos int8 [N][K/128] group positions; shift int32 [N]; out int8 [M][N]:

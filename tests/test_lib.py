@@ -70,3 +70,30 @@ def test_batch_beyond_plan_is_refused():
     lib = L.load()
     rc = lib.ixb_conv_layer(C.byref(descs[5]), C.c_void_p(0x10000), dp.arena_bytes, 100000, None)
     assert rc == -1 and any(w in lib.ixb_last_error().decode() for w in ("arena", "overlap", "pixel"))
+
+
+def test_gemm_plan_fits_the_hardware():
+    import ctypes as C
+    lib = L.load()
+    for M, N, K in [(256, 256, 256), (8192, 8192, 8192), (1000, 48, 144), (2 * 160 * 160 * 64, 32, 288),
+                    (512, 11008, 4096), (129, 16, 16), (128, 512, 65536)]:
+        info = (C.c_int32 * 10)()
+        assert lib.ixb_gemm_plan_info(M, N, K, info, 10) == 0, (M, N, K)
+        bn, mt, mtiles, ntiles, kblocks, stages, grid, smem, tcols, stage_bytes = list(info)
+        assert bn % 16 == 0 and 16 <= bn <= 256 and N % 16 == 0
+        assert mt * 128 * mtiles >= M and bn * ntiles >= N and kblocks * 128 >= K
+        assert 2 * mt * bn <= tcols <= 512 and tcols & (tcols - 1) == 0
+        assert stages >= 2 and smem <= 227 * 1024 and stage_bytes * stages + 1024 + 256 <= smem
+        assert 1 <= grid <= 148
+
+
+def test_gemm_refuses_bad_shapes_without_touching_the_gpu():
+    import ctypes as C
+    lib = L.load()
+    info = (C.c_int32 * 10)()
+    for M, N, K in [(0, 16, 16), (16, 24, 16), (16, 16, 8), (16, 16, 65552)]:
+        assert lib.ixb_gemm_plan_info(M, N, K, info, 10) == L.IXB_ERR_INVALID
+    x = C.c_void_p(16)
+    assert lib.ixb_i8gemm_srs(x, x, x, x, 16, 16, 16, 24, None) == L.IXB_ERR_INVALID
+    assert lib.ixb_i8gemm_srs(None, x, x, x, 16, 16, 16, 3, None) == L.IXB_ERR_INVALID
+    assert lib.ixb_i8gemm_i32(C.c_void_p(17), x, x, 16, 16, 16, None) == L.IXB_ERR_INVALID
