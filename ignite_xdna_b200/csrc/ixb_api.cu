@@ -22,6 +22,7 @@
 #include "ixb_conv.cuh"
 #include "ixb_gemm.cuh"
 #include "ixb_misc.cuh"
+#include "ixb_w4a8.cuh"
 #include "ixb_ptx.cuh"
 
 using namespace ixb;
@@ -649,9 +650,13 @@ struct GemmLaunch {
 // Tile shape, pipeline depth and grid for an M x N x K int8 GEMM. The accumulator of a tile is
 // MT blocks of 128 rows by BN columns; two of them (2 * MT * BN <= 512 TMEM columns) let the
 // epilogue of one tile overlap the next. MT grows only while the tiles still cover every SM.
-int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err) {
+int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = GEMM_B_TMA) {
   if (M < 1 || N < 16 || N % 16 || K < 16 || K % 16) {
     err = "GEMM shape needs M >= 1, N and K multiples of 16";
+    return -1;
+  }
+  if (bsrc == GEMM_B_W4 && K % kW4Group) {
+    err = "W4A8 needs K a multiple of the 128-value group";
     return -1;
   }
   if (K > 65536) {
@@ -662,21 +667,30 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err) {
   p.M = M;
   p.N = N;
   p.K = K;
-  p.bn = N <= 256 ? N : (N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 256));
-  p.n_tiles = (N + p.bn - 1) / p.bn;
   const int sms = sm_count();
-  p.mt = 1;
-  for (int cand : {4, 2}) {
-    const long long tiles = ((M + 128LL * cand - 1) / (128LL * cand)) * p.n_tiles;
-    if (cand * p.bn <= 256 && tiles >= sms) {
-      p.mt = cand;
-      break;
+  if (bsrc == GEMM_B_W4) {
+    // every B element is unpacked once per tile: as many 128-row blocks per tile as M needs
+    // (up to 4), and BN = 256 / MT, so the unpack work per MMA stays small
+    p.mt = (int)std::min<long long>(4, (M + 127) / 128);
+    if (p.mt == 3) p.mt = 4;
+    p.bn = std::min(256 / p.mt, N);
+  } else {
+    p.bn = N <= 256 ? N : (N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 256));
+    p.mt = 1;
+    const int nt = (N + p.bn - 1) / p.bn;
+    for (int cand : {4, 2}) {
+      const long long tiles = ((M + 128LL * cand - 1) / (128LL * cand)) * nt;
+      if (cand * p.bn <= 256 && tiles >= sms) {
+        p.mt = cand;
+        break;
+      }
     }
   }
+  p.n_tiles = (N + p.bn - 1) / p.bn;
   p.m_tiles = (int)((M + 128LL * p.mt - 1) / (128LL * p.mt));
   p.kblocks = (K + kGemmBK - 1) / kGemmBK;
   p.stage_bytes = p.mt * kGemmABlock + p.bn * kGemmBK;
-  p.stage_tx = p.stage_bytes;
+  p.stage_tx = bsrc == GEMM_B_W4 ? p.mt * kGemmABlock : p.stage_bytes;
   const int budget = kSmemLimit - 1024 - 256;
   p.stages = std::min(kGemmMaxStages, budget / p.stage_bytes);
   if (p.stages < 2) {
@@ -699,13 +713,14 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err) {
   return 0;
 }
 
+template <int BSRC>
 int launch_gemm(GemmLaunch& L, cudaStream_t st) {
   static bool attr = false;
   if (!attr) {
-    IXB_CUDA(cudaFuncSetAttribute(gemm_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    IXB_CUDA(cudaFuncSetAttribute(gemm_kernel<8, BSRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     attr = true;
   }
-  gemm_kernel<8><<<L.grid, gemm_threads(8), L.smem, st>>>(L.p);
+  gemm_kernel<8, BSRC><<<L.grid, gemm_threads(8, BSRC), L.smem, st>>>(L.p);
   IXB_CUDA(cudaGetLastError());
   return 0;
 }
@@ -730,7 +745,16 @@ int run_i8gemm(const int8_t* a, const int8_t* b, const int32_t* bias, int8_t* ou
   L.p.out32 = out32;
   if (encode_kmajor(&L.p.ta, a, M, K, 128, err) || encode_kmajor(&L.p.tb, b, N, K, L.p.bn, err))
     return fail(IXB_ERR_CUDA, err);
-  return launch_gemm(L, static_cast<cudaStream_t>(stream));
+  return launch_gemm<GEMM_B_TMA>(L, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- W4A8
+uint64_t w4a8_image_bytes(int K, int N) { return (uint64_t)N * (K / 2) + (uint64_t)N * (K / kW4Group); }
+
+int check_w4a8_shape(int N, int K) {
+  if (N < 16 || N % 16 || K < kW4Group || K % kW4Group || K > 65536)
+    return fail(IXB_ERR_INVALID, "W4A8 needs N a multiple of 16 and K a multiple of 128, at most 65536");
+  return 0;
 }
 
 int read_device_error() {
@@ -740,6 +764,7 @@ int read_device_error() {
   if (v) {
     unsigned int z = 0;
     cudaMemcpyToSymbol(g_dev_error, &z, sizeof z);
+    if (v == DEV_ERR_BAD_ARGS) return fail(IXB_ERR_INVALID, "a kernel found invalid input values");
     return fail(IXB_ERR_DEVICE, "a kernel's bounded wait gave up (device error flag " + std::to_string(v) + ")");
   }
   return 0;
@@ -1221,18 +1246,67 @@ int ixb_i8gemm_i32(const int8_t* a, const int8_t* b, int32_t* out, int M, int N,
   return run_i8gemm(a, b, nullptr, nullptr, out, M, N, K, 0, GEMM_OUT_I32, stream);
 }
 
-int ixb_w4a8_gemm(const int8_t*, const uint8_t*, const int8_t*, const int32_t*, int8_t*, int, int, int, void*) {
-  return fail(IXB_ERR_UNSUPPORTED, "W4A8 GEMM is not built yet");
-}
-int ixb_w4a8_gemv(const int8_t*, const uint8_t*, const int8_t*, const int32_t*, int8_t*, int, int, void*) {
-  return fail(IXB_ERR_UNSUPPORTED, "W4A8 GEMV is not built yet");
+int ixb_w4a8_image_bytes(int K, int N, uint64_t* bytes) {
+  if (!bytes) return fail(IXB_ERR_INVALID, "null argument");
+  if (int r = check_w4a8_shape(N, K)) return r;
+  *bytes = w4a8_image_bytes(K, N);
+  return 0;
 }
 
-int ixb_gemm_plan_info(int M, int N, int K, int32_t* info, int n) {
+int ixb_w4a8_prepare(const uint8_t* w_kn, const int8_t* gpos, int K, int N, uint8_t* image, void* stream) {
+  if (!w_kn || !gpos || !image) return fail(IXB_ERR_INVALID, "null argument");
+  if (int r = check_w4a8_shape(N, K)) return r;
+  if (!aligned16(image)) return fail(IXB_ERR_INVALID, "the weight image must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  IXB_CUDA(cudaStreamSynchronize(st));
+  if (int r = read_device_error()) return r;  // start from a clear flag
+  const long long words = (long long)N * (K / 8);
+  const int blocks = (int)std::min<long long>((words + 255) / 256, 148LL * 32);
+  w4a8_pack_kernel<<<blocks, 256, 0, st>>>(w_kn, K, N, image);
+  IXB_CUDA(cudaGetLastError());
+  w4a8_groups_kernel<<<(N + 255) / 256, 256, 0, st>>>(gpos, K / kW4Group, N, image + (uint64_t)N * (K / 2));
+  IXB_CUDA(cudaGetLastError());
+  IXB_CUDA(cudaStreamSynchronize(st));
+  if (int r = read_device_error())
+    return r == IXB_ERR_INVALID ? fail(r, "a column's group positions span more than 4 (max - min > 4)") : r;
+  return 0;
+}
+
+int ixb_w4a8_gemm(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out, int M, int N, int K,
+                  void* stream) {
+  if (!a || !image || !shift || !out) return fail(IXB_ERR_INVALID, "null argument");
+  if (int r = check_w4a8_shape(N, K)) return r;
+  if (!aligned16(a) || !aligned16(image) || !aligned16(out) || !aligned16(shift))
+    return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
+  GemmLaunch L;
+  std::string err;
+  if (plan_gemm(L, M, N, K, err, GEMM_B_W4)) return fail(IXB_ERR_INVALID, err);
+  L.p.out_kind = GEMM_OUT_SRS;
+  L.p.out8 = out;
+  L.p.shift_vec = shift;
+  L.p.wq = image;
+  L.p.eg = image + (uint64_t)N * (K / 2);
+  if (encode_kmajor(&L.p.ta, a, M, K, 128, err)) return fail(IXB_ERR_CUDA, err);
+  return launch_gemm<GEMM_B_W4>(L, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out, int N, int K,
+                  void* stream) {
+  if (!a || !image || !shift || !out) return fail(IXB_ERR_INVALID, "null argument");
+  if (int r = check_w4a8_shape(N, K)) return r;
+  if (!aligned16(a) || !aligned16(image)) return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
+  const int warps = 8;
+  w4a8_gemv_kernel<<<(N + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, image, image + (uint64_t)N * (K / 2), shift, out, N, K);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int ixb_gemm_plan_info(int M, int N, int K, int w4a8, int32_t* info, int n) {
   if (!info) return fail(IXB_ERR_INVALID, "null argument");
   GemmLaunch L;
   std::string err;
-  if (plan_gemm(L, M, N, K, err)) return fail(IXB_ERR_INVALID, err);
+  if (plan_gemm(L, M, N, K, err, w4a8 ? GEMM_B_W4 : GEMM_B_TMA)) return fail(IXB_ERR_INVALID, err);
   const int32_t v[10] = {L.p.bn, L.p.mt, L.p.m_tiles, L.p.n_tiles, L.p.kblocks, L.p.stages, L.grid, L.smem,
                          L.p.tmem_cols, L.p.stage_bytes};
   for (int i = 0; i < n && i < 10; ++i) info[i] = v[i];

@@ -22,6 +22,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include "ixb_ptx.cuh"
+#include "ixb_w4a8.cuh"
 
 namespace ixb {
 
@@ -43,6 +44,10 @@ struct GemmParams {
   int shift;
   int8_t* out8;
   int32_t* out32;
+  // W4A8 (B from the packed int4 weight image, unpacked by the B warps)
+  const uint8_t* wq;         // [N][K/2]
+  const uint8_t* eg;         // [N][K/128]
+  const int32_t* shift_vec;  // per output column, or null for `shift`
 };
 
 // K-major operand in the 128-byte swizzle layout TMA writes: rows of 128 bytes, 8-row atoms of
@@ -65,11 +70,59 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
       : "memory");
 }
 
-constexpr int gemm_threads(int epi) { return 32 * (epi + 2); }
+enum : int { GEMM_B_TMA = 0, GEMM_B_W4 = 1 };
+constexpr int kW4Warps = 4;  // warps unpacking int4 weights into the B stage (GEMM_B_W4)
+constexpr int gemm_threads(int epi, int bsrc) { return 32 * (epi + 2 + (bsrc == GEMM_B_W4 ? kW4Warps : 0)); }
 
-template <int EPI>
-__global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
-  constexpr int PW = EPI, MW = EPI + 1;
+// B warps of the W4A8 GEMM: per stage, BN rows x 128 values of K (one group) from the packed
+// image, 16 values (8 bytes) per item, 8 items per row so a row's 64 bytes load coalesced; each
+// item becomes one 16-byte chunk of the 128-byte swizzled row (chunk c at c ^ (row % 8)).
+__device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                           int ut) {
+  constexpr int UT = kW4Warps * 32;
+  const int S = p.stages, G = p.K / 128;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int items = 8 * p.bn;
+  int s = 0;
+  uint32_t ph = 0;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int ntile = t % p.n_tiles;
+    const int n0 = ntile * p.bn;
+    for (int kb = 0; kb < p.kblocks; ++kb) {
+      if (!mbar_wait(&empty[s], ph ^ 1)) return;
+      uint8_t* bst = smem + s * p.stage_bytes + p.mt * kGemmABlock;
+      for (int i = ut; i < items; i += UT) {
+        const int r = i >> 3, c = i & 7;
+        const int n = n0 + r;
+        uint4 o = make_uint4(0, 0, 0, 0);
+        if (n < p.N) {
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(p.wq + (long long)n * (p.K / 2) + kb * 64 + c * 8));
+          const uint32_t e = __ldg(p.eg + (long long)n * G + kb);
+          o = make_uint4(w4_lo16(w.x), w4_hi16(w.x), w4_lo16(w.y), w4_hi16(w.y));
+          if (e) {
+            const uint32_t keep = (0xFFu >> e) * 0x01010101u;
+            const uint32_t fill = ((0xFFu << (8 - e)) & 0xFFu);
+            o.x = sra8_lanes(o.x, e, keep, fill);
+            o.y = sra8_lanes(o.y, e, keep, fill);
+            o.z = sra8_lanes(o.z, e, keep, fill);
+            o.w = sra8_lanes(o.w, e, keep, fill);
+          }
+        }
+        *reinterpret_cast<uint4*>(bst + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = o;
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
+      mbar_arrive(&full[s]);
+      if (++s == S) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+  }
+}
+
+template <int EPI, int BSRC>
+__global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+  constexpr int PW = EPI, MW = EPI + 1, UW0 = EPI + 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -88,7 +141,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid
   }
   if (tid == PW * 32) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], BSRC == GEMM_B_W4 ? 1 + kW4Warps * 32 : 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -98,7 +151,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid
     mbar_init(done, 1);
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.ta) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tb) : "memory");
+    if (BSRC == GEMM_B_TMA) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tb) : "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -122,7 +175,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid
           mbar_arrive_expect_tx(&full[s], (uint32_t)p.stage_tx);
           for (int b = 0; b < p.mt; ++b)
             tma_load_2d(st + b * kGemmABlock, &p.ta, kb * kGemmBK, (mtile * p.mt + b) * 128, &full[s]);
-          tma_load_2d(st + p.mt * kGemmABlock, &p.tb, kb * kGemmBK, ntile * p.bn, &full[s]);
+          if (BSRC == GEMM_B_TMA) tma_load_2d(st + p.mt * kGemmABlock, &p.tb, kb * kGemmBK, ntile * p.bn, &full[s]);
           if (++s == S) {
             s = 0;
             ph ^= 1;
@@ -130,6 +183,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid
         }
       }
     }
+  } else if (BSRC == GEMM_B_W4 && warp >= UW0) {
+    // ------------------------------------------------------------ int4 -> int8 B producers
+    produce_w4(p, smem, full, empty, tid - UW0 * 32);
   } else if (warp == MW) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -197,6 +253,20 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1) gemm_kernel(const __grid
           uint4* o = reinterpret_cast<uint4*>(p.out32 + (long long)row * p.N + col);
 #pragma unroll
           for (int i = 0; i < 4; ++i) o[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else if (p.shift_vec) {
+          // W4A8: no bias, one shift per output column
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int r = clamp_i8(rne_shift((int)v[4 * i + e], __ldg(p.shift_vec + col + 4 * i + e)));
+              packed |= (uint32_t)(r & 0xFF) << (8 * e);
+            }
+            w[i] = packed;
+          }
+          *reinterpret_cast<uint4*>(p.out8 + (long long)row * p.N + col) = make_uint4(w[0], w[1], w[2], w[3]);
         } else {
           const int4* b4 = reinterpret_cast<const int4*>(p.bias + col);
           uint32_t w[4];

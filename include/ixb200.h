@@ -22,9 +22,10 @@
  *                        results/aie/graph_engine_yolov8n_phoenix_20260913T2210Z.log:12-98).
  *   ixb_i8gemm_srs       int8 x int8 -> int32 GEMM (kernels/int8_matmul_sweep) with the pow2
  *                        SRS epilogue of compiler/engine_emulator.py:149-162 in the int8 domain.
- *   ixb_w4a8_gemm / ixb_w4a8_gemv
+ *   ixb_w4a8_prepare / ixb_w4a8_gemm / ixb_w4a8_gemv
  *                        int8 x packed int4 -> int32 (kernels/w4a8_probe/w4a8_kernels.cc:288-305,
- *                        mm_i8i4_native) plus a group-aligned pow2 SRS epilogue.
+ *                        mm_i8i4_native; operand packing w4a8_probe.py:197-201) plus a
+ *                        group-aligned pow2 SRS epilogue.
  */
 #ifndef IXB200_H
 #define IXB200_H
@@ -203,17 +204,30 @@ int ixb_i8gemm_srs(const int8_t* a, const int8_t* b, const int32_t* bias, int8_t
                    int M, int N, int K, int shift, void* stream);
 /* Same product without the epilogue: int32 out [M][N] (exact). */
 int ixb_i8gemm_i32(const int8_t* a, const int8_t* b, int32_t* out, int M, int N, int K, void* stream);
-/* The launch plan of an M x N x K GEMM (host only, no GPU needed): {BN, MT, M tiles, N tiles,
- * K blocks, stages, grid, shared bytes, TMEM columns, stage bytes}. */
-int ixb_gemm_plan_info(int M, int N, int K, int32_t* info, int n);
+/* The launch plan of an M x N x K GEMM, or of a W4A8 GEMM when w4a8 != 0 (host only, no GPU
+ * needed): {BN, MT, M tiles, N tiles, K blocks, stages, grid, shared bytes, TMEM columns,
+ * stage bytes}. */
+int ixb_gemm_plan_info(int M, int N, int K, int w4a8, int32_t* info, int n);
 
-/* W4A8: a int8 [M][K]; w uint8 [N][K/2] (two int4 per byte along K, even k in the low nibble);
- * gpos int8 [N][K/128] group positions; shift int32 [N]; out int8 [M][N]:
- * out = clamp(rne((sum_g (a_g . w_g) << (pmax_n - gpos[n][g])) >> shift[n]), -128, 127). */
-int ixb_w4a8_gemm(const int8_t* a, const uint8_t* w, const int8_t* gpos, const int32_t* shift,
-                  int8_t* out, int M, int N, int K, void* stream);
-int ixb_w4a8_gemv(const int8_t* a, const uint8_t* w, const int8_t* gpos, const int32_t* shift,
-                  int8_t* out, int N, int K, void* stream);
+/* W4A8: int8 activations x int4 weights with per-group pow2 scales (groups of 128 along K).
+ * The weights come in the reference's operand format (kernels/w4a8_probe/w4a8_probe.py:197-201,
+ * tools/int4_prefill_model.py:154-200): w_kn uint8 [K][N/2], two int4 per byte along N, element
+ * 2j in the low nibble, two's complement; gpos int8 [K/128][N] the group positions (scale
+ * exponents). With d = max_g gpos[g][n] - gpos[g][n], which must lie in [0, 4]:
+ *   acc[m][n] = sum_g (sum_{k in g} a[m][k] * w[k][n]) << d,
+ *   out[m][n] = clamp(rne(acc[m][n] >> shift[n]), -128, 127),  shift int32 [N] in [0, 23].
+ * (The reference kernels stop at the raw int32 A.B; the group step is this engine's.)
+ * ixb_w4a8_prepare turns (w_kn, gpos) into the engine's weight image (ixb_w4a8_image_bytes of
+ * device memory) once; it waits for the stream and refuses a column whose group positions span
+ * more than 4. N a multiple of 16, K a multiple of 128, at most 65536; device pointers, 16-byte
+ * aligned. ixb_w4a8_gemm (prefill, M rows; tcgen05) and ixb_w4a8_gemv (M = 1; split-K warp
+ * reduction) are enqueued on `stream`. */
+int ixb_w4a8_image_bytes(int K, int N, uint64_t* bytes);
+int ixb_w4a8_prepare(const uint8_t* w_kn, const int8_t* gpos, int K, int N, uint8_t* image, void* stream);
+int ixb_w4a8_gemm(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out,
+                  int M, int N, int K, void* stream);
+int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out,
+                  int N, int K, void* stream);
 
 /* sizeof of ixb_segment, ixb_conv_desc, ixb_pool_desc, ixb_plan (for binding checks). */
 int ixb_abi_sizes(uint64_t* sizes, int n);

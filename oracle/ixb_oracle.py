@@ -182,25 +182,27 @@ def unpack_int4(p: np.ndarray) -> np.ndarray:
     return np.where(out >= 8, out - 16, out).astype(np.int8)
 
 
-def w4a8_acc(a: np.ndarray, w_packed: np.ndarray, group_pos: np.ndarray, group: int = 128) -> np.ndarray:
-    """int64 accumulator Σ_g (Σ_{k in g} a_k w_k) << (p_max - p_g).
+def w4a8_acc(a: np.ndarray, w_kn: np.ndarray, gpos: np.ndarray, group: int = 128) -> np.ndarray:
+    """int64 accumulator sum_g (sum_{k in g} a_k w_kn) << (p_max - p_g).
 
-    a int8 [M,K]; w_packed uint8 [N, K/2] (K-major, low nibble = even k); group_pos int [N, K/group]."""
-    w = unpack_int4(w_packed).astype(np.int64)                  # [N, K]
+    a int8 [M,K]; w_kn uint8 [K, N/2], the reference's operand (two int4 per byte along N, element
+    2j in the low nibble: w4a8_probe.py:197-201, int4_prefill_model.py Int4MmulReference);
+    gpos int [K/group, N] group positions, p_max their max per column. The group step is the
+    engine's own (the reference kernels output the raw int32 A.B)."""
+    w = unpack_int4(w_kn).astype(np.int64)                       # [K, N]
     m, k = a.shape
-    n = w.shape[0]
-    pmax = group_pos.max(axis=1, keepdims=True)                 # [N,1]
-    acc = np.zeros((m, n), dtype=np.int64)
+    pmax = gpos.max(axis=0).astype(np.int64)                      # [N]
+    acc = np.zeros((m, w.shape[1]), dtype=np.int64)
     a64 = a.astype(np.int64)
     for g in range(k // group):
-        part = a64[:, g * group:(g + 1) * group] @ w[:, g * group:(g + 1) * group].T
-        acc += part << (pmax - group_pos[:, g:g + 1]).T
+        part = a64[:, g * group:(g + 1) * group] @ w[g * group:(g + 1) * group]
+        acc += part << (pmax - gpos[g].astype(np.int64))[None, :]
     return acc
 
 
-def w4a8_srs(a, w_packed, group_pos, shift: np.ndarray, group: int = 128) -> np.ndarray:
-    """W4A8 output: per output channel RNE shift (int8 clamp) of the group-aligned accumulator."""
-    acc = w4a8_acc(a, w_packed, group_pos, group)
+def w4a8_srs(a, w_kn, gpos, shift: np.ndarray, group: int = 128) -> np.ndarray:
+    """W4A8 output: per output column RNE shift and int8 clamp of the group-aligned accumulator."""
+    acc = w4a8_acc(a, w_kn, gpos, group)
     out = np.empty(acc.shape, dtype=np.int8)
     for s in np.unique(shift):
         cols = np.nonzero(shift == s)[0]

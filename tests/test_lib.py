@@ -78,7 +78,7 @@ def test_gemm_plan_fits_the_hardware():
     for M, N, K in [(256, 256, 256), (8192, 8192, 8192), (1000, 48, 144), (2 * 160 * 160 * 64, 32, 288),
                     (512, 11008, 4096), (129, 16, 16), (128, 512, 65536)]:
         info = (C.c_int32 * 10)()
-        assert lib.ixb_gemm_plan_info(M, N, K, info, 10) == 0, (M, N, K)
+        assert lib.ixb_gemm_plan_info(M, N, K, 0, info, 10) == 0, (M, N, K)
         bn, mt, mtiles, ntiles, kblocks, stages, grid, smem, tcols, stage_bytes = list(info)
         assert bn % 16 == 0 and 16 <= bn <= 256 and N % 16 == 0
         assert mt * 128 * mtiles >= M and bn * ntiles >= N and kblocks * 128 >= K
@@ -92,8 +92,27 @@ def test_gemm_refuses_bad_shapes_without_touching_the_gpu():
     lib = L.load()
     info = (C.c_int32 * 10)()
     for M, N, K in [(0, 16, 16), (16, 24, 16), (16, 16, 8), (16, 16, 65552)]:
-        assert lib.ixb_gemm_plan_info(M, N, K, info, 10) == L.IXB_ERR_INVALID
+        assert lib.ixb_gemm_plan_info(M, N, K, 0, info, 10) == L.IXB_ERR_INVALID
     x = C.c_void_p(16)
     assert lib.ixb_i8gemm_srs(x, x, x, x, 16, 16, 16, 24, None) == L.IXB_ERR_INVALID
     assert lib.ixb_i8gemm_srs(None, x, x, x, 16, 16, 16, 3, None) == L.IXB_ERR_INVALID
     assert lib.ixb_i8gemm_i32(C.c_void_p(17), x, x, 16, 16, 16, None) == L.IXB_ERR_INVALID
+
+
+def test_w4a8_plan_and_refusals():
+    import ctypes as C
+    lib = L.load()
+    info = (C.c_int32 * 10)()
+    for M, N, K in [(512, 11008, 4096), (512, 4096, 11008), (1, 4096, 128), (200, 64, 256)]:
+        assert lib.ixb_gemm_plan_info(M, N, K, 1, info, 10) == 0
+        bn, mt, mtiles, ntiles, kblocks, stages, grid, smem, tcols, stage_bytes = list(info)
+        assert mt * bn <= 256 and bn % 16 == 0 and kblocks * 128 == K and mt * 128 * mtiles >= M
+        assert stages >= 2 and smem <= 227 * 1024 and 2 * mt * bn <= tcols <= 512
+    assert lib.ixb_gemm_plan_info(512, 64, 200, 1, info, 10) == L.IXB_ERR_INVALID   # K not a whole group
+    nbytes = C.c_uint64()
+    assert lib.ixb_w4a8_image_bytes(4096, 11008, C.byref(nbytes)) == 0
+    assert nbytes.value == 11008 * 2048 + 11008 * 32
+    assert lib.ixb_w4a8_image_bytes(100, 16, C.byref(nbytes)) == L.IXB_ERR_INVALID
+    x = C.c_void_p(16)
+    assert lib.ixb_w4a8_gemv(x, x, x, x, 24, 128, None) == L.IXB_ERR_INVALID
+    assert lib.ixb_w4a8_gemm(x, x, None, x, 16, 16, 128, None) == L.IXB_ERR_INVALID
