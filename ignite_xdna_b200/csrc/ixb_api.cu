@@ -16,6 +16,7 @@
 #include <map>
 #include <string>
 #include <thread>
+#include <utility>
 #include <vector>
 
 #include "../../include/ixb200.h"
@@ -519,6 +520,33 @@ int encode_im2col(ConvLaunch& L, const ixb_conv_desc& d, uint8_t* arena, int bat
   return 0;
 }
 
+// Kernels of a network step are launched with programmatic stream serialization: each may begin
+// its setup while the previous kernel drains (the kernels wait for the previous grid before any
+// activation access). IXB_PDL=0 turns it off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("IXB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <int MODE>
 int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
   static bool configured = false;
@@ -526,8 +554,7 @@ int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
     IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     configured = true;
   }
-  conv_kernel<MODE><<<L.grid, conv_threads(MODE), L.smem, st>>>(L.p);
-  IXB_CUDA(cudaGetLastError());
+  IXB_CUDA(launch_dependent(conv_kernel<MODE>, L.grid, dim3(conv_threads(MODE)), L.smem, st, L.p));
   return 0;
 }
 
@@ -594,8 +621,7 @@ int launch_pool(const PoolLaunch& L, cudaStream_t st) {
     IXB_CUDA(cudaFuncSetAttribute(sppf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     configured = true;
   }
-  sppf_kernel<<<L.grid, 256, L.smem, st>>>(L.p);
-  IXB_CUDA(cudaGetLastError());
+  IXB_CUDA(launch_dependent(sppf_kernel, L.grid, dim3(256), L.smem, st, L.p));
   return 0;
 }
 

@@ -473,6 +473,7 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
   const int ntile = blockIdx.y;
   const int KB = p.kblocks;
   const long long t_start = clock64();
+  grid_dep_launch();
 
   if (warp == 0) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -510,6 +511,7 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
       for (int kb = 0; kb < KB; ++kb)
         bulk_g2s(smem + p.kb[kb].b_off, p.wpack + ntile * p.w_ntile_stride + p.kb[kb].b_off, p.kb[kb].b_bytes, bres_bar);
     }
+    grid_dep_wait();  // activations of the previous layer from here on
     if (MODE == IXB_MODE_GATHER) {
       produce_gather(p, smem, full, empty, ntile, ptid);
     } else if (ptid == 0) {
@@ -521,6 +523,7 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
     if (lane == 0 && who < p.issuers) issue_mma<MODE>(p, smem, full, empty, acc_full, acc_empty, bres_bar, tmem, who);
   } else {
     // ------------------------------------------------------------ epilogue
+    grid_dep_wait();  // residual reads and output writes follow the previous layer
     int acc = 0;
     uint32_t aph = 0;
     long long ew = 0, ek = 0;

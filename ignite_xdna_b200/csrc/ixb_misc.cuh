@@ -15,8 +15,10 @@ __global__ void __launch_bounds__(256) quantize_images_kernel(const uint8_t* __r
                                                                const int8_t* __restrict__ lut, int B, int H,
                                                                int W, int8_t* __restrict__ out) {
   __shared__ uint8_t lut_s[256];
+  grid_dep_launch();
   for (int i = threadIdx.x; i < 256; i += blockDim.x) lut_s[i] = (uint8_t)lut[i];
   __syncthreads();
+  grid_dep_wait();
   const int wq = W >> 2;
   const long long total = (long long)B * H * wq;
   const long long plane = (long long)H * W;
@@ -65,6 +67,8 @@ __global__ void __launch_bounds__(256) sppf_kernel(const __grid_constant__ PoolP
   const int img = blockIdx.y;
   const int W2 = p.W + 2;
   const int8_t* src = p.in.base + (long long)chunk * p.in.plane + (long long)img * p.in.P * 16;
+  grid_dep_launch();
+  grid_dep_wait();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int y = i / p.W, x = i - (i / p.W) * p.W;
     cur[i] = *reinterpret_cast<const uint4*>(src + ((y + 1) * W2 + x + 1) * 16);

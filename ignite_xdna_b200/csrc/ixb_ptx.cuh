@@ -79,6 +79,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// The kernels of one network step are launched so that each may start while the previous one
+// drains: a kernel sets up (shared memory, TMEM, barriers, constant loads) and then waits here
+// until the previous grid has completed and its writes are visible, before it touches any
+// activation. Without the launch attribute the wait returns at once.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream begin its setup once every CTA of this grid has started.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------- copies
 // 16-byte global -> shared copy; src_bytes 0 zero-fills the destination.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {

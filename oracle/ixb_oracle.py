@@ -159,9 +159,16 @@ def srs_i8(acc, shift: int) -> np.ndarray:
     return np.clip(rne_shift(acc, shift), -128, 127).astype(np.int8)
 
 
+def exact_matmul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Integer a @ b as int64 through float64 BLAS: exact while every partial sum stays below 2^53
+    in magnitude, which int8 operands guarantee for K < 2^38."""
+    assert a.shape[-1] < (1 << 38)
+    return (a.astype(np.float64) @ b.astype(np.float64)).astype(np.int64)
+
+
 def i8gemm_srs(a: np.ndarray, b: np.ndarray, bias: np.ndarray, shift: int) -> np.ndarray:
     """int8 A [M,K] x int8 B [N,K] (K-major) + int32 bias [N], then RNE shift and int8 clamp."""
-    acc = a.astype(np.int64) @ b.astype(np.int64).T + bias.astype(np.int64)[None, :]
+    acc = exact_matmul(a, b.T) + bias.astype(np.int64)[None, :]
     return srs_i8(acc, shift)
 
 
@@ -193,9 +200,8 @@ def w4a8_acc(a: np.ndarray, w_kn: np.ndarray, gpos: np.ndarray, group: int = 128
     m, k = a.shape
     pmax = gpos.max(axis=0).astype(np.int64)                      # [N]
     acc = np.zeros((m, w.shape[1]), dtype=np.int64)
-    a64 = a.astype(np.int64)
     for g in range(k // group):
-        part = a64[:, g * group:(g + 1) * group] @ w[g * group:(g + 1) * group]
+        part = exact_matmul(a[:, g * group:(g + 1) * group], w[g * group:(g + 1) * group])
         acc += part << (pmax - gpos[g].astype(np.int64))[None, :]
     return acc
 
