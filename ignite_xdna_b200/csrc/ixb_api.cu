@@ -48,6 +48,7 @@ int cuda_fail(cudaError_t e, const char* what) {
   } while (0)
 
 constexpr int kSmemLimit = 227 * 1024;
+constexpr int kConvDynSmem = kSmemLimit - 256;  // the conv kernel holds its 256-byte table statically
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
@@ -327,7 +328,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   }
   p.b_block_bytes = b_stage_max;
   const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_GATHER ? 2 * 512 * 16 : 0);  // barriers, table, bias, rows
-  const int budget = kSmemLimit - 1024 - extra;
+  const int budget = kConvDynSmem - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
     p.tile_rows = 128 * mt;
@@ -353,7 +354,17 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
   if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.tile_rows > 1024)
     return bad("an im2col load carries at most 1024 pixels");
-  p.issuers = p.mt >= 2 ? 2 : 1;
+  // Warps: MMA-heavy tiles (long K over one or two 128-row blocks) take 8 epilogue and 4 MMA
+  // warps, the rest 12 epilogue and 2 MMA warps (GATHER always 8 + 4). With fewer blocks than
+  // issuers, K splits into `parts` partial accumulators per block while TMEM holds two tiles.
+  int mma_per_block = 0;
+  for (const SchedKB& k : kbs) mma_per_block += k.nops;
+  p.ew = (d.mode == IXB_MODE_GATHER || (p.mt <= 2 && mma_per_block >= 16)) ? 8 : 12;
+  const int mw = mma_warps(p.ew);
+  p.parts = 1;
+  while (p.mt * p.parts * 2 <= mw && 2 * p.mt * d.n_tile * (p.parts * 2) <= 512 && p.parts * 2 <= p.kblocks)
+    p.parts *= 2;
+  p.issuers = std::min(mw, p.mt * p.parts);
   p.w_ntile_stride = (long long)b_total;
   p.wpack = arena + d.w_offset;
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
@@ -363,7 +374,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.fd_W2 = make_fastdiv((uint32_t)(d.in_w + 2));
   p.fd_hw = make_fastdiv((uint32_t)(d.out_h * d.out_w));
   p.fd_Wo = make_fastdiv((uint32_t)d.out_w);
-  p.acc_cols = p.mt * d.n_tile;
+  p.acc_cols = p.mt * p.parts * d.n_tile;
   int cols = 32;
   while (cols < 2 * p.acc_cols) cols *= 2;
   p.tmem_cols = cols;
@@ -458,12 +469,13 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     }
   }
   const int smem = p.bias_off + 4 * d.n_tile + 1024;
+  if (smem > kConvDynSmem) return bad("shared memory plan exceeds the limit");
   const long long gm = std::max<long long>(1, std::min<long long>(p.m_tiles, ((long long)sms + ntiles - 1) / ntiles));
   L.grid = dim3((unsigned)gm, (unsigned)ntiles, 1);
   L.smem = smem;
   L.mode = d.mode;
   L.stages = p.stages;
-  L.threads = conv_threads(d.mode);
+  L.threads = conv_threads(d.mode, p.ew);
   return 0;
 }
 
@@ -547,23 +559,26 @@ cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, int 
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-template <int MODE>
+template <int MODE, int EW>
 int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
-    IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kConvDynSmem));
     configured = true;
   }
-  IXB_CUDA(launch_dependent(conv_kernel<MODE>, L.grid, dim3(conv_threads(MODE)), L.smem, st, L.p));
+  IXB_CUDA(launch_dependent(conv_kernel<MODE, EW>, L.grid, dim3(conv_threads(MODE, EW)), L.smem, st, L.p));
   return 0;
 }
 
 int launch_conv(const ConvLaunch& L, cudaStream_t st) {
+  const bool e12 = L.p.ew == 12;
   switch (L.mode) {
-    case IXB_MODE_WINDOW: return launch_conv_m<IXB_MODE_WINDOW>(L, st);
-    case IXB_MODE_GATHER: return launch_conv_m<IXB_MODE_GATHER>(L, st);
-    case IXB_MODE_IM2COL: return launch_conv_m<IXB_MODE_IM2COL>(L, st);
-    default: return launch_conv_m<IXB_MODE_STEM>(L, st);
+    case IXB_MODE_WINDOW:
+      return e12 ? launch_conv_m<IXB_MODE_WINDOW, 12>(L, st) : launch_conv_m<IXB_MODE_WINDOW, 8>(L, st);
+    case IXB_MODE_GATHER: return launch_conv_m<IXB_MODE_GATHER, 8>(L, st);
+    case IXB_MODE_IM2COL:
+      return e12 ? launch_conv_m<IXB_MODE_IM2COL, 12>(L, st) : launch_conv_m<IXB_MODE_IM2COL, 8>(L, st);
+    default: return e12 ? launch_conv_m<IXB_MODE_STEM, 12>(L, st) : launch_conv_m<IXB_MODE_STEM, 8>(L, st);
   }
 }
 

@@ -79,7 +79,8 @@ struct ConvParams {
   int rowsA, win_origin;
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
   int b_resident, a_off, tbl_off, bar_off, lut_off, bias_off;
-  int n_tile, acc_cols, tmem_cols, issuers;
+  int n_tile, acc_cols, tmem_cols, issuers, parts;  // MMA issuing threads; partial accumulators per block
+  int ew;                                           // epilogue warps (8 or 12)
   uint32_t idesc;
   int nseg;
   SegDev seg[IXB_MAX_SEGS];
@@ -119,10 +120,15 @@ enum : int {
 
 constexpr int kBlockM = 128;
 // Warp layout per mode.
-__host__ __device__ constexpr int epi_warps(int mode) { return mode == IXB_MODE_GATHER ? 8 : 12; }
+// Warp layout per (mode, epilogue warps EW): EW epilogue warps, the producer warps, then the MMA
+// warps, one issuing thread each (a warp issues an MMA only every ~100 cycles, so MMA-heavy layers
+// take four). At most 16 warps: four per SM sub-partition keeps 128 registers per thread.
+//   EW = 12: 12 epilogue + 1 producer + 2 MMA (epilogue-heavy layers)
+//   EW = 8:   8 epilogue + 1 producer + 4 MMA (MMA-heavy layers); GATHER: 8 + 4 + 4
 __host__ __device__ constexpr int prod_warps(int mode) { return mode == IXB_MODE_GATHER ? 4 : 1; }
-__host__ __device__ constexpr int mma_warp0(int mode) { return epi_warps(mode) + prod_warps(mode); }
-__host__ __device__ constexpr int conv_threads(int mode) { return 32 * (mma_warp0(mode) + 2); }
+__host__ __device__ constexpr int mma_warp0(int mode, int ew) { return ew + prod_warps(mode); }
+__host__ __device__ constexpr int mma_warps(int ew) { return ew == 12 ? 2 : 4; }
+__host__ __device__ constexpr int conv_threads(int mode, int ew) { return 32 * (mma_warp0(mode, ew) + mma_warps(ew)); }
 constexpr int kGatherThreads = 128;
 
 __device__ __forceinline__ void producer_bar_sync() {
@@ -279,52 +285,65 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
 }
 
 // ---------------------------------------------------------------- MMA issuer
-// Issuer `who` of `p.issuers` issues the MMAs of blocks b = who, who + issuers, ... of every tile.
+// p.issuers MMA threads (one per MMA warp) share a tile's MT 128-row blocks:
+//  * MT >= issuers (parts = 1): issuer `who` drives blocks who, who + issuers, ... over every K-block;
+//  * MT < issuers: K is split into parts = issuers / MT partial accumulators per block; issuer `who`
+//    drives block who / parts over the K-blocks kb with kb % parts == who % parts.
+// Partial accumulator (block b, part) sits at TMEM columns (b * parts + part) * n_tile; the epilogue
+// adds the parts. Several issuing warps keep the tensor core fed where one warp's issue rate
+// (about one MMA per 100 cycles) would limit it. Stage kb is released by the issuers that read it.
 template <int MODE>
 __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                           uint64_t* acc_full, uint64_t* acc_empty, uint64_t* bres_bar, uint32_t tmem,
                                           int who) {
   if (p.b_resident) mbar_wait(bres_bar, 0);
-  const int S = p.stages;
+  const int S = p.stages, P = p.parts;
+  const int part = who % P;
+  const int b_first = P > 1 ? who / P : who;
+  const int b_step = P > 1 ? p.mt : p.issuers;  // P > 1: one block per issuer
   int stage = 0, acc = 0;
   uint32_t ph = 0, aph = 0;
   long long wf = 0, wa = 0, wi = 0;
-  const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);  // SBO 128 B, sm_100 descriptor
+  // A: SBO 128 B, sm_100 descriptor; blocks are 128 rows (128 16-byte units) apart in a stage
+  const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+  const uint32_t a_base = smem_u32(smem + p.a_off) >> 4;
+  const uint32_t w_base = smem_u32(smem);
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
     long long c0 = clock64();
     mbar_wait(&acc_empty[acc], aph ^ 1);
     long long c1 = clock64();
     wa += c1 - c0;
     tc_fence_after();
-    const uint32_t d0 = tmem + acc * p.acc_cols;
+    const uint32_t d_acc = tmem + acc * p.acc_cols;
+    uint32_t accum = 0;
     for (int kb = 0; kb < p.kblocks; ++kb) {
-      c0 = clock64();
-      mbar_wait(&full[stage], ph);
-      c1 = clock64();
-      wf += c1 - c0;
-      if (MODE == IXB_MODE_GATHER) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
-      tc_fence_after();
-      // A descriptor = stage base + op start / LBO (16-byte units) + 128 rows per block; B = K-block
-      // weights + op start. Additions to the low 14-bit address field cannot carry (smem < 256 KB).
-      const KBlockDev& K = p.kb[kb];
-      const uint32_t a0 = smem_u32(smem + p.a_off + stage * p.stage_bytes) >> 4;
-      const uint32_t b0 = p.b_resident ? smem_u32(smem) + K.b_off : ((a0 << 4) + p.a_stage_bytes);
-      const uint64_t bdesc0 = umma_desc(b0, 128, 256);
-      for (int o = 0; o < K.nops; ++o) {
-        const uint32_t opa = p.op_a[K.op0 + o];
-        const uint64_t bd = bdesc0 + p.op_b[K.op0 + o];
-        const uint32_t accum = (kb > 0 || o > 0) ? 1u : 0u;
-        uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
-        ad += (uint64_t)(who * ((kBlockM * 16) >> 4));
-        uint32_t dt = d0 + who * p.n_tile;
-        for (int b = who; b < p.mt; b += p.issuers) {
-          umma_s8(dt, ad, bd, p.idesc, accum);
-          ad += (uint64_t)(p.issuers * ((kBlockM * 16) >> 4));
-          dt += p.issuers * p.n_tile;
+      if (kb % P == part) {
+        c0 = clock64();
+        mbar_wait(&full[stage], ph);
+        c1 = clock64();
+        wf += c1 - c0;
+        if (MODE == IXB_MODE_GATHER) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
+        tc_fence_after();
+        // A descriptor = stage base + op start / LBO (16-byte units) + block; B = K-block weights
+        // + op start. Additions to the low 14-bit address field cannot carry (smem < 256 KB).
+        const KBlockDev& K = p.kb[kb];
+        const uint32_t a0 = a_base + (uint32_t)((stage * p.stage_bytes) >> 4);
+        const uint32_t b0 = p.b_resident ? w_base + K.b_off : ((a_base << 4) + stage * p.stage_bytes + p.a_stage_bytes);
+        const uint64_t bdesc0 = umma_desc(b0, 128, 256);
+        const int o0 = K.op0, o1 = K.op0 + K.nops;
+#pragma unroll 2
+        for (int o = o0; o < o1; ++o) {
+          const uint32_t opa = p.op_a[o];
+          const uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
+          const uint64_t bd = bdesc0 + p.op_b[o];
+          for (int b = b_first; b < p.mt; b += b_step)
+            umma_s8(d_acc + (uint32_t)((b * P + part) * p.n_tile), ad + (uint64_t)(b * ((kBlockM * 16) >> 4)), bd,
+                    p.idesc, accum);
+          accum = 1u;
         }
+        umma_commit(&empty[stage]);
+        wi += clock64() - c1;
       }
-      umma_commit(&empty[stage]);
-      wi += clock64() - c1;
       if (++stage == S) {
         stage = 0;
         ph ^= 1;
@@ -343,11 +362,13 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
 
 // ---------------------------------------------------------------- epilogue
 // 16 accumulators of one row -> 16 int8 outputs: bias, RNE shift, int8 clamp, table, residual.
+// `lut` points at entry 128 of the 256-byte table (static shared memory), so it is indexed by the
+// clamped value directly; the bytes are gathered into words with byte permutes.
 template <bool RES>
-__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const int4* bias4, const int8_t* lut_s, int s,
+__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const int4* bias4, const uint8_t* lut, int s,
                                             int hs, int lsb, const ConvParams& p, int rs, int rhs, int rlsb,
                                             uint4 r4) {
-  alignas(16) int8_t ov[16];
+  uint32_t t[16];
   const int8_t* rv = reinterpret_cast<const int8_t*>(&r4);
 #pragma unroll
   for (int q4 = 0; q4 < 4; ++q4) {
@@ -358,15 +379,20 @@ __device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const int4*
       const int i = 4 * q4 + e;
       const int a = (int)v[i] + bb[e];
       const int r1 = (a + hs + ((a >> s) & lsb)) >> s;   // round half to even, exact for s in [0, 16]
-      int t = lut_s[clamp_i8(r1) + 128];
+      uint32_t u = lut[clamp_i8(r1)];
       if (RES) {
-        const int y = (t << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
-        t = clamp_i8((y + rhs + ((y >> rs) & rlsb)) >> rs);
+        const int y = ((int)(int8_t)u << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
+        u = (uint32_t)clamp_i8((y + rhs + ((y >> rs) & rlsb)) >> rs);
       }
-      ov[i] = (int8_t)t;
+      t[i] = u;
     }
   }
-  return *reinterpret_cast<const uint4*>(ov);
+  uint4 o;
+  o.x = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
+  o.y = __byte_perm(__byte_perm(t[4], t[5], 0x0040), __byte_perm(t[6], t[7], 0x0040), 0x5410);
+  o.z = __byte_perm(__byte_perm(t[8], t[9], 0x0040), __byte_perm(t[10], t[11], 0x0040), 0x5410);
+  o.w = __byte_perm(__byte_perm(t[12], t[13], 0x0040), __byte_perm(t[14], t[15], 0x0040), 0x5410);
+  return o;
 }
 
 struct RowInfo {
@@ -397,7 +423,7 @@ __device__ __forceinline__ RowInfo decode_row(const ConvParams& p, int m) {
 }
 
 __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
-                                            const int4* bias4_s, const int8_t* lut_s, int s, int hs, int lsb, int rs,
+                                            const int4* bias4_s, const uint8_t* lut_s, int s, int hs, int lsb, int rs,
                                             int rhs, int rlsb) {
   const int nj = p.n_tile / 16;
   const int oc = ntile * nj + jj;  // output chunk
@@ -423,16 +449,39 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 // Drain one accumulator: warp w reads TMEM lane quarter w % 4; the warpgroups take alternate
 // pieces (128-row block, 16-column chunk). A thread issues the TMEM loads of two pieces before one
 // wait so their latencies overlap.
-template <int MODE>
+template <int MODE, int EW>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
-                                                   int lane, const int8_t* lut_s, const int4* bias4_s) {
-  constexpr int ngroups = epi_warps(MODE) / 4;
+                                                   int lane, const uint8_t* lut_s, const int4* bias4_s) {
+  constexpr int ngroups = EW / 4;
   const int q = warp & 3, g = warp >> 2;
   const int nj = p.n_tile / 16;
   const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
   const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
   const int npieces = p.mt * nj;
+  const int P = p.parts;
+  if (P > 1) {
+    // K split over P issuers: a piece is the sum of its P partial accumulators
+    for (int k = g; k < npieces; k += ngroups) {
+      const int b1 = k / nj, j1 = k - (k / nj) * nj;
+      const uint32_t c = lane_base + b1 * P * p.n_tile + j1 * 16;
+      uint32_t v[16], w[16];
+      tmem_ld16(c, v);
+      tmem_ld16(c + p.n_tile, w);
+      const RowInfo r1 = decode_row<MODE>(p, m0 + b1 * kBlockM + q * 32 + lane);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] += w[i];
+      for (int q2 = 2; q2 < P; ++q2) {
+        tmem_ld16(c + q2 * p.n_tile, w);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] += w[i];
+      }
+      if (r1.valid) store_piece(p, r1, ntile, j1, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    }
+    return;
+  }
   for (int k = g; k < npieces; k += 2 * ngroups) {
     const int k2 = k + ngroups;
     const int b1 = k / nj, j1 = k - (k / nj) * nj;
@@ -454,9 +503,9 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
   }
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __grid_constant__ ConvParams p) {
-  constexpr int EPI = epi_warps(MODE), PW0 = EPI, MW0 = mma_warp0(MODE);
+template <int MODE, int EW>
+__global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const __grid_constant__ ConvParams p) {
+  constexpr int EPI = EW, PW0 = EPI, MW0 = mma_warp0(MODE, EW);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -467,7 +516,8 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* bres_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
-  int8_t* lut_s = reinterpret_cast<int8_t*>(smem + p.lut_off);
+  __shared__ uint8_t lut_tab[256];  // static: the epilogue indexes it from a constant address
+  const uint8_t* lut_s = lut_tab + 128;
   int* bias_s = reinterpret_cast<int*>(smem + p.bias_off);
   const int4* bias4_s = reinterpret_cast<const int4*>(smem + p.bias_off);
   const int ntile = blockIdx.y;
@@ -483,7 +533,7 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
     const uint32_t fcount = (MODE == IXB_MODE_GATHER) ? (uint32_t)kGatherThreads + (p.b_resident ? 0u : 1u) : 1u;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], fcount);
-      mbar_init(&empty[s], p.issuers);
+      mbar_init(&empty[s], p.issuers / p.parts);  // the issuers that read a stage's K-block
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], p.issuers);
@@ -495,8 +545,8 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
   if (MODE == IXB_MODE_IM2COL || MODE == IXB_MODE_STEM) {
     if (tid == PW0 * 32) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap) : "memory");
   }
-  for (int i = tid; i < 256; i += conv_threads(MODE)) lut_s[i] = p.lut[i];
-  for (int i = tid; i < p.n_tile; i += conv_threads(MODE)) bias_s[i] = p.bias[ntile * p.n_tile + i];
+  for (int i = tid; i < 256; i += conv_threads(MODE, EW)) lut_tab[i] = (uint8_t)p.lut[i];
+  for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -534,7 +584,7 @@ __global__ void __launch_bounds__(conv_threads(MODE), 1) conv_kernel(const __gri
       const long long c1 = clock64();
       ew += c1 - c0;
       tc_fence_after();
-      conv_epilogue_tile<MODE>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s);
+      conv_epilogue_tile<MODE, EW>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       ek += clock64() - c1;
