@@ -406,6 +406,114 @@ def run_gpu(args):
     return 0
 
 
+# ---------------------------------------------------------------- GEMM microbenchmarks
+GEMM_SHAPES = [(256, 256, 256), (1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192),
+               (160 * 160 * 64, 16, 144), (160 * 160 * 64, 32, 288), (80 * 80 * 64, 64, 576),
+               (80 * 80 * 64, 80, 720), (40 * 40 * 64, 128, 1152), (20 * 20 * 64, 256, 2304)]
+W4A8_SHAPES = [(4096, 11008), (11008, 4096)]   # (K, N) of the MLP projections
+
+
+def _time_events(fn, iters, warmup, flush=None):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def run_gemm_workloads(args):
+    """int8 GEMM + SRS (config: M=N=K sweep and YOLOv8n convs as im2col GEMMs) and W4A8 (MLP
+    projections at M=512 prefill and M=1 GEMV): one JSON line, per-shape device times with CUDA
+    events, L2 flushed between launches, torch._int_mm (cuBLASLt int8) timed beside the GEMM."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from ignite_xdna_b200 import _lib as L
+    lib = L.load()
+    hbm, bf16, kind = load_peaks()
+    int8_peak = 2 * bf16
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rows = []
+    if args.workload == "i8gemm":
+        for M, N, K in GEMM_SHAPES:
+            a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+            b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+            bias = torch.randint(-(1 << 20), 1 << 20, (N,), dtype=torch.int32, device="cuda", generator=g)
+            out = torch.empty((M, N), dtype=torch.int8, device="cuda")
+            fn = lambda: L.check(lib.ixb_i8gemm_srs(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()),  # noqa: E731
+                                                    C.c_void_p(bias.data_ptr()), C.c_void_p(out.data_ptr()),
+                                                    M, N, K, 8, None))
+            ms = _time_events(fn, args.steps, args.warmup, flush)
+            bt = b.t()
+            ms_lib = _time_events(lambda: torch._int_mm(a, bt), args.steps, args.warmup, flush)
+            tops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            rows.append({"M": M, "N": N, "K": K, "ms": round(ms, 4), "tops": round(tops, 1),
+                         "tc_frac": round(tops / int8_peak, 4),
+                         "hbm_gbs": round((M * K + N * K + M * N) / (ms * 1e-3) / 1e9, 1),
+                         "cublaslt_int_mm_ms": round(ms_lib, 4),
+                         "cublaslt_tops": round(2.0 * M * N * K / (ms_lib * 1e-3) / 1e12, 1)})
+        head = rows[3]
+        metric, unit, value = "int8 GEMM + pow2 SRS TOP/s at M=N=K=8192", "TOP/s", head["tops"]
+        roof = {"bound": "tensor", "achieved": head["tops"], "peak": round(int8_peak, 1), "unit": "TFLOP/s",
+                "frac": head["tc_frac"], "traffic": None,
+                "peak_source": f"2 x {kind} dense bf16 ({bf16} TF/s, MEASURED_PEAKS.json): int8 rate of tcgen05"}
+    else:
+        rng = np.random.default_rng(0)
+        for K, N in W4A8_SHAPES:
+            w = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+            wk = ((w[:, 0::2].astype(np.int16) & 0xF) | ((w[:, 1::2].astype(np.int16) & 0xF) << 4)).astype(np.uint8)
+            gpos = (5 + rng.integers(0, 4, size=(K // 128, N))).astype(np.int8)
+            nbytes = C.c_uint64()
+            L.check(lib.ixb_w4a8_image_bytes(K, N, C.byref(nbytes)))
+            img = torch.empty(nbytes.value, dtype=torch.uint8, device="cuda")
+            dw, dg = torch.from_numpy(wk).cuda(), torch.from_numpy(gpos).cuda()
+            L.check(lib.ixb_w4a8_prepare(C.c_void_p(dw.data_ptr()), C.c_void_p(dg.data_ptr()), K, N,
+                                         C.c_void_p(img.data_ptr()), None))
+            shift = torch.full((N,), 10, dtype=torch.int32, device="cuda")
+            for M in (512, 1):
+                a = torch.randn((M, K), device="cuda", generator=g).mul_(24).round_().clamp_(-127, 127).to(torch.int8)
+                out = torch.empty((M, N), dtype=torch.int8, device="cuda")
+                if M == 1:
+                    fn = lambda: L.check(lib.ixb_w4a8_gemv(C.c_void_p(a.data_ptr()), C.c_void_p(img.data_ptr()),  # noqa: E731
+                                                           C.c_void_p(shift.data_ptr()), C.c_void_p(out.data_ptr()),
+                                                           N, K, None))
+                else:
+                    fn = lambda: L.check(lib.ixb_w4a8_gemm(C.c_void_p(a.data_ptr()), C.c_void_p(img.data_ptr()),  # noqa: E731
+                                                           C.c_void_p(shift.data_ptr()), C.c_void_p(out.data_ptr()),
+                                                           M, N, K, None))
+                ms = _time_events(fn, args.steps, args.warmup, flush)
+                wbytes = K * N // 2 + N * (K // 128)
+                rows.append({"M": M, "N": N, "K": K, "ms": round(ms, 4),
+                             "tops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 2),
+                             "hbm_gbs": round((wbytes + M * K + M * N) / (ms * 1e-3) / 1e9, 1),
+                             "kernel": "ixb_w4a8_gemv (split-K warp reduction)" if M == 1
+                             else "ixb_w4a8_gemm (tcgen05, int4 unpack warps)"})
+        gemv = [r for r in rows if r["M"] == 1]
+        metric, unit = "W4A8 GEMV weight-stream GB/s (K=4096,N=11008 and K=11008,N=4096)", "GB/s"
+        value = round(statistics.mean(r["hbm_gbs"] for r in gemv), 1)
+        roof = {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": round(value / hbm, 4),
+                "traffic": None, "peak_source": f"{kind} hbm_gbs (MEASURED_PEAKS.json)"}
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x int8 -> int32" if args.workload == "i8gemm" else "int8 x int4 -> int32",
+            "data": "synthetic (seeded uniform operands)", "config": {"workload": args.workload,
+                                                                        "l2": "256 MiB written between launches"},
+            "roofline": roof, "shapes": rows, "gpu_launches": len(rows) * args.steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -416,11 +524,15 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--imgsz", type=int, default=640)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", default="yolo", choices=["yolo", "i8gemm", "w4a8"],
+                    help="yolo: the whole-network benchmark; i8gemm / w4a8: the kernel microbenchmarks")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "yolo":
+        return run_gemm_workloads(args)
     return run_gpu(args)
 
 

@@ -598,6 +598,7 @@ struct PoolLaunch {
 
 int build_pool(const ixb_pool_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, PoolLaunch& L,
                std::string& err) {
+  memset(&L.p, 0, sizeof L.p);
   if (check_seg(d.in, batch, arena_bytes, false, "pool input", err)) return -1;
   if (d.in.up2) {
     err = "pool input cannot be an up2 view";
@@ -705,6 +706,7 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
     return -1;
   }
   GemmParams& p = L.p;
+  memset(&p, 0, sizeof p);  // every pointer a variant does not use stays null
   p.M = M;
   p.N = N;
   p.K = K;
