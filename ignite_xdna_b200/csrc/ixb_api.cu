@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -21,6 +22,7 @@
 
 #include "../../include/ixb200.h"
 #include "ixb_conv.cuh"
+#include "ixb_decode.cuh"
 #include "ixb_gemm.cuh"
 #include "ixb_misc.cuh"
 #include "ixb_w4a8.cuh"
@@ -1353,6 +1355,64 @@ int ixb_gemm_plan_info(int M, int N, int K, int w4a8, int32_t* info, int n) {
   const int32_t v[10] = {L.p.bn, L.p.mt, L.p.m_tiles, L.p.n_tiles, L.p.kblocks, L.p.stages, L.grid, L.smem,
                          L.p.tmem_cols, L.p.stage_bytes};
   for (int i = 0; i < n && i < 10; ++i) info[i] = v[i];
+  return 0;
+}
+
+int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
+                    const float* letterbox, int32_t capacity, float* boxes, float* scores, int32_t* classes,
+                    int32_t* counts, void* stream) {
+  if (!d || !egress || !letterbox || !boxes || !scores || !classes || !counts || batch < 1 || capacity < 0)
+    return fail(IXB_ERR_INVALID, "bad decode arguments");
+  if (d->reg_max != kDfl) return fail(IXB_ERR_UNSUPPORTED, "decode implements the 16-bin DFL head (reg_max 16)");
+  if (d->num_classes < 1 || d->num_classes > 256) return fail(IXB_ERR_INVALID, "num_classes outside [1, 256]");
+  if (!d->anchor_x || !d->anchor_y || !d->strides) return fail(IXB_ERR_INVALID, "null anchor tables");
+  if (reinterpret_cast<uintptr_t>(boxes) & 15) return fail(IXB_ERR_INVALID, "boxes must be 16-byte aligned");
+  DecodeParams p;
+  memset(&p, 0, sizeof p);
+  int total = 0;
+  for (int h = 0; h < 3; ++h) {
+    const ixb_decode_head& hd = d->head[h];
+    if (!hd.dfl_exp || !hd.sigmoid || hd.anchors < 1 || hd.anchor_offset != total)
+      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + ": missing tables or anchors out of order");
+    const uint64_t box_end = hd.box_offset + (uint64_t)4 * kDfl * hd.anchors;
+    const uint64_t cls_end = hd.cls_offset + (uint64_t)d->num_classes * hd.anchors;
+    if (box_end > egress_image_bytes || cls_end > egress_image_bytes)
+      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + " outside the image's egress");
+    total += hd.anchors;
+    DecodeHeadDev& o = p.head[h];
+    o.box_off = (long long)hd.box_offset;
+    o.cls_off = (long long)hd.cls_offset;
+    o.dfl_exp = hd.dfl_exp;
+    o.sigmoid = hd.sigmoid;
+    o.sigmoid_low = hd.sigmoid_low;
+    // an integer class maximum m survives when m > q_threshold, i.e. m > floor(q_threshold)
+    const double qt = hd.q_threshold;
+    o.qi = !(qt < 127.0) ? 127 : (qt < -129.0 ? -129 : (int)std::floor(qt));
+    o.anchors = hd.anchors;
+    o.anchor_offset = hd.anchor_offset;
+  }
+  if (total > kDecodeMaxAnchors) return fail(IXB_ERR_INVALID, "more than 8400 anchors per image");
+  p.egress = egress;
+  p.egress_image_bytes = (long long)egress_image_bytes;
+  p.anchor_x = d->anchor_x;
+  p.anchor_y = d->anchor_y;
+  p.strides = d->strides;
+  p.num_classes = d->num_classes;
+  p.conf = d->conf;
+  p.iou = d->iou;
+  p.letterbox = letterbox;
+  p.capacity = capacity;
+  p.out_box = boxes;
+  p.out_score = scores;
+  p.out_class = classes;
+  p.out_count = counts;
+  static bool attr = false;
+  if (!attr) {
+    IXB_CUDA(cudaFuncSetAttribute(yolo_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem_bytes()));
+    attr = true;
+  }
+  yolo_decode_kernel<<<batch, kDecodeThreads, decode_smem_bytes(), static_cast<cudaStream_t>(stream)>>>(p);
+  IXB_CUDA(cudaGetLastError());
   return 0;
 }
 

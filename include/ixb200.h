@@ -229,6 +229,39 @@ int ixb_w4a8_gemm(const int8_t* a, const uint8_t* image, const int32_t* shift, i
 int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out,
                   int N, int K, void* stream);
 
+/* YOLOv8 detect decode + NMS on the GPU: the detections of the reference's
+ * pipelines/decode_native.c yolo_decode_int8 (:407-540), bit for bit, for `batch` images of int8
+ * heads in the engine's egress layout (device memory, image i at egress + i * egress_image_bytes).
+ * Per head: the box and class heads' byte offsets inside an image's egress (int8 NCHW, 4 * 16 and
+ * num_classes channels over `anchors`), the tables the reference builds with numpy
+ * (dfl_exp float [256][256], sigmoid float [256], sigmoid_low int32 [256] or NULL;
+ * pipelines/decode_native.py:125-153) and the prune threshold q_threshold; anchor_x / anchor_y /
+ * strides float [sum of anchors] (yolo_pipeline.py:191-203). letterbox float [batch][3] holds
+ * pad_top, pad_left, scale per image. Writes per image up to `capacity` detections in NMS order:
+ * boxes float [batch][capacity][4] (x0, y0, w, h in source pixels), scores float [batch][capacity],
+ * classes int32 [batch][capacity], counts int32 [batch] (-3 where more than `capacity` survive,
+ * as the reference). All pointers device memory; reg_max must be 16; at most 8400 anchors and
+ * 256 classes per image. Enqueued on `stream`. */
+typedef struct ixb_decode_head {
+  uint64_t box_offset, cls_offset;
+  const float* dfl_exp;
+  const float* sigmoid;
+  const int32_t* sigmoid_low;
+  double q_threshold;
+  int32_t anchors, anchor_offset;
+} ixb_decode_head;
+typedef struct ixb_decode_desc {
+  ixb_decode_head head[3];
+  const float* anchor_x;
+  const float* anchor_y;
+  const float* strides;
+  int32_t reg_max, num_classes;
+  float conf, iou;
+} ixb_decode_desc;
+int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
+                    const float* letterbox, int32_t capacity, float* boxes, float* scores, int32_t* classes,
+                    int32_t* counts, void* stream);
+
 /* sizeof of ixb_segment, ixb_conv_desc, ixb_pool_desc, ixb_plan (for binding checks). */
 int ixb_abi_sizes(uint64_t* sizes, int n);
 
