@@ -85,24 +85,37 @@ __global__ void __launch_bounds__(256) w4a8_gemv_kernel(const int8_t* __restrict
   const uint8_t* row = wq + (long long)n * (K / 2);
   const uint8_t* erow = eg + (long long)n * (K / kW4Group);
   int acc = 0;
-#pragma unroll 4
-  for (int k0 = lane * 32; k0 < K; k0 += 1024) {
-    uint4 w;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
-                 : "l"(row + k0 / 2));
-    const int4 a0 = __ldg(reinterpret_cast<const int4*>(a + k0));
-    const int4 a1 = __ldg(reinterpret_cast<const int4*>(a + k0) + 1);
-    int p = 0;
-    p = __dp4a((int)w4_lo16(w.x), a0.x, p);
-    p = __dp4a((int)w4_hi16(w.x), a0.y, p);
-    p = __dp4a((int)w4_lo16(w.y), a0.z, p);
-    p = __dp4a((int)w4_hi16(w.y), a0.w, p);
-    p = __dp4a((int)w4_lo16(w.z), a1.x, p);
-    p = __dp4a((int)w4_hi16(w.z), a1.y, p);
-    p = __dp4a((int)w4_lo16(w.w), a1.z, p);
-    p = __dp4a((int)w4_hi16(w.w), a1.w, p);
-    acc += p >> __ldg(erow + (k0 >> 7));  // p = 16 * sum a * w, a multiple of 16: exact
+  // all of a lane's weight loads (up to 8 x 16 bytes) are in flight before the first is used
+  constexpr int kBatch = 8;
+  for (int kb = lane * 32; kb < K; kb += 1024 * kBatch) {
+    uint4 w[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int k0 = kb + j * 1024;
+      if (k0 < K)
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[j].x), "=r"(w[j].y), "=r"(w[j].z), "=r"(w[j].w)
+                     : "l"(row + k0 / 2));
+      else
+        w[j] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int k0 = kb + j * 1024;
+      if (k0 >= K) break;
+      const int4 a0 = __ldg(reinterpret_cast<const int4*>(a + k0));
+      const int4 a1 = __ldg(reinterpret_cast<const int4*>(a + k0) + 1);
+      int p = 0;
+      p = __dp4a((int)w4_lo16(w[j].x), a0.x, p);
+      p = __dp4a((int)w4_hi16(w[j].x), a0.y, p);
+      p = __dp4a((int)w4_lo16(w[j].y), a0.z, p);
+      p = __dp4a((int)w4_hi16(w[j].y), a0.w, p);
+      p = __dp4a((int)w4_lo16(w[j].z), a1.x, p);
+      p = __dp4a((int)w4_hi16(w[j].z), a1.y, p);
+      p = __dp4a((int)w4_lo16(w[j].w), a1.z, p);
+      p = __dp4a((int)w4_hi16(w[j].w), a1.w, p);
+      acc += p >> __ldg(erow + (k0 >> 7));  // p = 16 * sum a * w, a multiple of 16: exact
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
