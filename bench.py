@@ -346,11 +346,12 @@ def run_gpu(args):
 
     for _ in range(args.warmup):
         device_step()
-    with ClockSampler(local) as clocks:
-        ms = timed(device_step, args.steps)
-    ms = max_over_ranks(ms, world, local)
     e2e_steps(max(3, args.warmup))
-    ms_e2e = max_over_ranks(timed_e2e(args.steps), world, local)
+    with ClockSampler(local) as clocks:     # over both timed regions
+        ms = timed(device_step, args.steps)
+        ms_e2e = timed_e2e(args.steps)
+    ms = max_over_ranks(ms, world, local)
+    ms_e2e = max_over_ranks(ms_e2e, world, local)
     # per-op device times (layer-by-layer launches with events on the session stream)
     prof = sess.profile(B, iters=max(2, min(args.steps, 5)))
     conv_ops = [i for i, (k, _) in enumerate(sess.plan.ops) if k == L.OP_CONV]
@@ -517,7 +518,7 @@ def run_gemm_workloads(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ixb", choices=["ixb", "reference"])
     ap.add_argument("--model", default="yolov8n", choices=["yolov8n", "yolov8s", "yolov8m"])

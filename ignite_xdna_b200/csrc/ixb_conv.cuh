@@ -446,60 +446,79 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
   }
 }
 
-// Drain one accumulator: warp w reads TMEM lane quarter w % 4; the warpgroups take alternate
-// pieces (128-row block, 16-column chunk). A thread issues the TMEM loads of two pieces before one
-// wait so their latencies overlap.
+// Drain one accumulator: warp w reads TMEM lane quarter w % 4. The tile's units (128-row block,
+// 16-column chunk), in block-major order, are split into one contiguous share per warpgroup, so a
+// thread decodes its row once per block; it issues the TMEM loads of two units before one wait
+// so their latencies overlap. With K split over P issuers a unit is the sum of P partial
+// accumulators.
 template <int MODE, int EW>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const uint8_t* lut_s, const int4* bias4_s) {
-  constexpr int ngroups = EW / 4;
+  constexpr int NG = EW / 4;
   const int q = warp & 3, g = warp >> 2;
-  const int nj = p.n_tile / 16;
+  const int nj = p.n_tile >> 4;
   const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
   const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
-  const int npieces = p.mt * nj;
   const int P = p.parts;
-  if (P > 1) {
-    // K split over P issuers: a piece is the sum of its P partial accumulators
-    for (int k = g; k < npieces; k += ngroups) {
-      const int b1 = k / nj, j1 = k - (k / nj) * nj;
-      const uint32_t c = lane_base + b1 * P * p.n_tile + j1 * 16;
-      uint32_t v[16], w[16];
-      tmem_ld16(c, v);
-      tmem_ld16(c + p.n_tile, w);
-      const RowInfo r1 = decode_row<MODE>(p, m0 + b1 * kBlockM + q * 32 + lane);
+  const int units = p.mt * nj;
+  const int u_end = ((g + 1) * units) / NG;
+  int u = (g * units) / NG;
+  // (b, j) of unit u without a division: walk from the share's start
+  int b = 0, j = u;
+  while (j >= nj) {
+    j -= nj;
+    ++b;
+  }
+  const int row_in_block = q * 32 + lane;
+  int decoded_b = -1;
+  RowInfo r{};
+  while (u < u_end) {
+    const bool two = u + 1 < u_end;
+    const int b2 = (j + 1 == nj) ? b + 1 : b, j2 = (j + 1 == nj) ? 0 : j + 1;
+    uint32_t v[16], w[16];
+    const uint32_t c1 = lane_base + (uint32_t)((b * P) * p.n_tile + j * 16);
+    const uint32_t c2 = lane_base + (uint32_t)((b2 * P) * p.n_tile + j2 * 16);
+    if (P == 1) {
+      tmem_ld16(c1, v);
+      if (two) tmem_ld16(c2, w);
+      if (b != decoded_b) {
+        r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
+        decoded_b = b;
+      }
+      tmem_ld_wait();
+      if (r.valid) store_piece(p, r, ntile, j, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      if (two) {
+        if (b2 != decoded_b) {
+          r = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
+          decoded_b = b2;
+        }
+        if (r.valid) store_piece(p, r, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      }
+      u += 2;
+      b = two && j2 + 1 == nj ? b2 + 1 : b2;
+      j = two ? (j2 + 1 == nj ? 0 : j2 + 1) : j2;
+    } else {
+      tmem_ld16(c1, v);
+      tmem_ld16(c1 + p.n_tile, w);
+      if (b != decoded_b) {
+        r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
+        decoded_b = b;
+      }
       tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] += w[i];
       for (int q2 = 2; q2 < P; ++q2) {
-        tmem_ld16(c + q2 * p.n_tile, w);
+        tmem_ld16(c1 + q2 * p.n_tile, w);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] += w[i];
       }
-      if (r1.valid) store_piece(p, r1, ntile, j1, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      if (r.valid) store_piece(p, r, ntile, j, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      u += 1;
+      b = b2;
+      j = j2;
     }
-    return;
-  }
-  for (int k = g; k < npieces; k += 2 * ngroups) {
-    const int k2 = k + ngroups;
-    const int b1 = k / nj, j1 = k - (k / nj) * nj;
-    uint32_t v[16], w[16];
-    tmem_ld16(lane_base + b1 * p.n_tile + j1 * 16, v);
-    const bool two = k2 < npieces;
-    int b2 = 0, j2 = 0;
-    if (two) {
-      b2 = k2 / nj;
-      j2 = k2 - b2 * nj;
-      tmem_ld16(lane_base + b2 * p.n_tile + j2 * 16, w);
-    }
-    const RowInfo r1 = decode_row<MODE>(p, m0 + b1 * kBlockM + q * 32 + lane);
-    RowInfo r2 = r1;
-    if (two && b2 != b1) r2 = decode_row<MODE>(p, m0 + b2 * kBlockM + q * 32 + lane);
-    tmem_ld_wait();
-    if (r1.valid) store_piece(p, r1, ntile, j1, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
-    if (two && r2.valid) store_piece(p, r2, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
   }
 }
 
