@@ -186,7 +186,7 @@ def dist_setup(args):
         import torch.distributed as dist
         import torch
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 

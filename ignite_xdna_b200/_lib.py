@@ -22,7 +22,7 @@ MAX_SEGS = 4
 API_VERSION = 4
 MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
-IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH = 1, 2, 4, 8
+IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH, IN_STORE = 1, 2, 4, 8, 16
 OP_CONV, OP_POOL = 0, 1
 
 
@@ -108,6 +108,11 @@ _SIGS = {
     "ixb_w4a8_gemv": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "ixb_decode_yolo": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_uint64, C.c_void_p, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "ixb_letterbox_frames": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64, C.c_void_p,
+                                       C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint64, C.POINTER(C.c_float),
+                                       C.c_void_p]),
+    "ixb_session_letterbox": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64,
+                                        C.POINTER(C.c_float)]),
 }
 
 

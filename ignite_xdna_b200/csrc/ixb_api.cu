@@ -329,7 +329,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     }
   }
   p.b_block_bytes = b_stage_max;
-  const int extra = 512 + 256 + 1024 + (d.mode == IXB_MODE_GATHER ? 2 * 512 * 16 : 0);  // barriers, table, bias, rows
+  // barriers, bias, gather row tables
+  const int extra = 512 + 1024 + (d.mode == IXB_MODE_GATHER ? 2 * 512 * 16 : 0);
   const int budget = kConvDynSmem - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
@@ -351,22 +352,17 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.m_tiles = (int)((p.m_total + p.tile_rows - 1) / p.tile_rows);
   p.tbl_off = p.a_off + p.stages * p.stage_bytes;
   p.bar_off = p.tbl_off + (d.mode == IXB_MODE_GATHER ? 2 * p.tile_rows * 16 : 0);
-  p.lut_off = p.bar_off + 512;
-  p.bias_off = p.lut_off + 256;
+  p.bias_off = p.bar_off + 512;
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
   if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.tile_rows > 1024)
     return bad("an im2col load carries at most 1024 pixels");
   // Warps: MMA-heavy tiles (long K over one or two 128-row blocks) take 8 epilogue and 4 MMA
-  // warps, the rest 12 epilogue and 2 MMA warps (GATHER always 8 + 4). With fewer blocks than
-  // issuers, K splits into `parts` partial accumulators per block while TMEM holds two tiles.
+  // warps, the rest 12 epilogue and 3 MMA warps (GATHER always 8 + 4); the issuers split each
+  // K-block's MMAs between them.
   int mma_per_block = 0;
   for (const SchedKB& k : kbs) mma_per_block += k.nops;
   p.ew = (d.mode == IXB_MODE_GATHER || (p.mt <= 2 && mma_per_block >= 16)) ? 8 : 12;
-  const int mw = mma_warps(p.ew);
-  p.parts = 1;
-  while (p.mt * p.parts * 2 <= mw && 2 * p.mt * d.n_tile * (p.parts * 2) <= 512 && p.parts * 2 <= p.kblocks)
-    p.parts *= 2;
-  p.issuers = std::min(mw, p.mt * p.parts);
+  p.issuers = mma_warps(p.ew);
   p.w_ntile_stride = (long long)b_total;
   p.wpack = arena + d.w_offset;
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
@@ -376,7 +372,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.fd_W2 = make_fastdiv((uint32_t)(d.in_w + 2));
   p.fd_hw = make_fastdiv((uint32_t)(d.out_h * d.out_w));
   p.fd_Wo = make_fastdiv((uint32_t)d.out_w);
-  p.acc_cols = p.mt * p.parts * d.n_tile;
+  p.acc_cols = p.mt * d.n_tile;
   int cols = 32;
   while (cols < 2 * p.acc_cols) cols *= 2;
   p.tmem_cols = cols;
@@ -889,15 +885,16 @@ struct ixb_session {
                            stream);
   }
 
-  int enqueue(int batch, int slot = 0) {
-    if (int r = enqueue_ingress(batch, slot)) return r;
+  int enqueue(int batch, int slot = 0, bool ingress = true) {
+    if (ingress)
+      if (int r = enqueue_ingress(batch, slot)) return r;
     for (size_t i = 0; i < ops.size(); ++i)
       if (int r = enqueue_op(batch, (int)i, slot)) return r;
     return 0;
   }
 
-  int graph_for(int batch, cudaGraphExec_t* out, int slot = 0) {
-    const int key = batch * kSlots + slot;
+  int graph_for(int batch, cudaGraphExec_t* out, int slot = 0, bool ingress = true) {
+    const int key = (batch * kSlots + slot) * 2 + (ingress ? 0 : 1);
     auto it = graphs.find(key);
     if (it != graphs.end()) {
       *out = it->second;
@@ -905,7 +902,7 @@ struct ixb_session {
     }
     cudaGraph_t g = nullptr;
     IXB_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-    int r = enqueue(batch, slot);
+    int r = enqueue(batch, slot, ingress);
     cudaError_t e = cudaStreamEndCapture(stream, &g);
     if (r) {
       if (g) cudaGraphDestroy(g);
@@ -1080,7 +1077,9 @@ int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* eg
   if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
   if (s->pending) return fail(IXB_ERR_INVALID, "the previous asynchronous run was not waited for");
   if (s->any_busy()) return fail(IXB_ERR_INVALID, "submitted runs are still in flight");
-  if (!(flags & IXB_IN_DEVICE) && !images) return fail(IXB_ERR_INVALID, "null images");
+  const bool in_store = (flags & IXB_IN_STORE) != 0;
+  if (!(flags & IXB_IN_DEVICE) && !in_store && !images) return fail(IXB_ERR_INVALID, "null images");
+  if (in_store && images) return fail(IXB_ERR_INVALID, "IXB_IN_STORE runs take no images");
   if (!(flags & IXB_OUT_DEVICE) && !egress) return fail(IXB_ERR_INVALID, "null egress");
   const bool copy_in = images != nullptr, copy_out = egress != nullptr;
   IXB_CUDA(cudaSetDevice(s->device));
@@ -1092,10 +1091,10 @@ int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* eg
                              s->stream));
   IXB_CUDA(cudaEventRecord(s->ev0, s->stream));
   if (flags & IXB_NO_GRAPH) {
-    if (int r = s->enqueue(batch)) return r;
+    if (int r = s->enqueue(batch, 0, !in_store)) return r;
   } else {
     cudaGraphExec_t exec;
-    if (int r = s->graph_for(batch, &exec)) return r;
+    if (int r = s->graph_for(batch, &exec, 0, !in_store)) return r;
     IXB_CUDA(cudaGraphLaunch(exec, s->stream));
   }
   IXB_CUDA(cudaEventRecord(s->ev1, s->stream));
@@ -1414,6 +1413,68 @@ int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, u
   yolo_decode_kernel<<<batch, kDecodeThreads, decode_smem_bytes(), static_cast<cudaStream_t>(stream)>>>(p);
   IXB_CUDA(cudaGetLastError());
   return 0;
+}
+
+int ixb_letterbox_frames(const uint8_t* frames, int batch, int src_w, int src_h, int src_stride, uint64_t frame_bytes,
+                         const int8_t* lut, int8_t* out, int dst_w, int dst_h, int out_row_pixels,
+                         uint64_t out_image_bytes, float* letterbox, void* stream) {
+  if (!frames || !lut || !out || batch < 1 || src_w < 1 || src_h < 1 || dst_w < 1 || dst_h < 1)
+    return fail(IXB_ERR_INVALID, "bad letterbox arguments");
+  if (src_stride < 3 * src_w || frame_bytes < (uint64_t)src_stride * (src_h - 1) + 3ull * src_w ||
+      out_row_pixels < dst_w || out_image_bytes < (uint64_t)out_row_pixels * 8 * (dst_h - 1) + 8ull * dst_w)
+    return fail(IXB_ERR_INVALID, "letterbox strides smaller than the rows they hold");
+  if (reinterpret_cast<uintptr_t>(out) & 7) return fail(IXB_ERR_INVALID, "letterbox output must be 8-byte aligned");
+  // the reference's float32 letterbox geometry (preprocess_simd.c:352-363)
+  const float scale_w = (float)dst_w / (float)src_w, scale_h = (float)dst_h / (float)src_h;
+  const float scale = scale_w < scale_h ? scale_w : scale_h;
+  int nw = (int)std::floor((float)src_w * scale + 0.5f), nh = (int)std::floor((float)src_h * scale + 0.5f);
+  if (nw > dst_w) nw = dst_w;
+  if (nh > dst_h) nh = dst_h;
+  if (nw < 1 || nh < 1) return fail(IXB_ERR_INVALID, "letterboxed image is empty");
+  LetterboxParams p;
+  memset(&p, 0, sizeof p);
+  p.frames = frames;
+  p.frame_bytes = (long long)frame_bytes;
+  p.src_w = src_w;
+  p.src_h = src_h;
+  p.src_stride = src_stride;
+  p.dst_w = dst_w;
+  p.dst_h = dst_h;
+  p.nw = nw;
+  p.nh = nh;
+  p.pad_top = (dst_h - nh) / 2;
+  p.pad_left = (dst_w - nw) / 2;
+  p.fx = (float)src_w / (float)nw;
+  p.fy = (float)src_h / (float)nh;
+  p.lut = lut;
+  p.out = out;
+  p.out_row_pixels = out_row_pixels;
+  p.out_image_bytes = (long long)out_image_bytes;
+  p.batch = batch;
+  if (letterbox) {
+    letterbox[0] = (float)p.pad_top;
+    letterbox[1] = (float)p.pad_left;
+    letterbox[2] = scale;
+  }
+  const long long total = (long long)batch * dst_h * dst_w;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+  letterbox_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int ixb_session_letterbox(ixb_session* s, const uint8_t* frames, int batch, int src_w, int src_h, int src_stride,
+                          uint64_t frame_bytes, float* letterbox) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
+  if (s->pending || s->any_busy()) return fail(IXB_ERR_INVALID, "runs are still in flight");
+  IXB_CUDA(cudaSetDevice(s->device));
+  const ixb_plan& pl = s->plan;
+  const int row = pl.img_w + 4;
+  int8_t* base = reinterpret_cast<int8_t*>(s->arena + pl.input.offset) + ((long long)row + 1) * 8;
+  return ixb_letterbox_frames(frames, batch, src_w, src_h, src_stride, frame_bytes,
+                              reinterpret_cast<const int8_t*>(s->arena + pl.input_lut_offset), base, pl.img_w, pl.img_h,
+                              row, (uint64_t)(pl.img_h + 2) * row * 8, letterbox, s->stream);
 }
 
 int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w, int8_t* padded_nhwc4,

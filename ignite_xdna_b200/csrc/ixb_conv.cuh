@@ -69,6 +69,7 @@ struct KBlockDev {
 constexpr int kMaxKBlocks = 96;
 constexpr int kMaxOps = 160;
 
+
 struct ConvParams {
   alignas(64) CUtensorMap tmap;  // TMA im2col map (IM2COL, STEM)
   int mode, k, stride, pad;
@@ -78,8 +79,8 @@ struct ConvParams {
   int mt, tile_rows, m_tiles;
   int rowsA, win_origin;
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
-  int b_resident, a_off, tbl_off, bar_off, lut_off, bias_off;
-  int n_tile, acc_cols, tmem_cols, issuers, parts;  // MMA issuing threads; partial accumulators per block
+  int b_resident, a_off, tbl_off, bar_off, bias_off;
+  int n_tile, acc_cols, tmem_cols, issuers;  // MMA issuing threads
   int ew;                                           // epilogue warps (8 or 12)
   uint32_t idesc;
   int nseg;
@@ -123,11 +124,11 @@ constexpr int kBlockM = 128;
 // Warp layout per (mode, epilogue warps EW): EW epilogue warps, the producer warps, then the MMA
 // warps, one issuing thread each (a warp issues an MMA only every ~100 cycles, so MMA-heavy layers
 // take four). At most 16 warps: four per SM sub-partition keeps 128 registers per thread.
-//   EW = 12: 12 epilogue + 1 producer + 2 MMA (epilogue-heavy layers)
+//   EW = 12: 12 epilogue + 1 producer + 3 MMA (epilogue-heavy layers)
 //   EW = 8:   8 epilogue + 1 producer + 4 MMA (MMA-heavy layers); GATHER: 8 + 4 + 4
 __host__ __device__ constexpr int prod_warps(int mode) { return mode == IXB_MODE_GATHER ? 4 : 1; }
 __host__ __device__ constexpr int mma_warp0(int mode, int ew) { return ew + prod_warps(mode); }
-__host__ __device__ constexpr int mma_warps(int ew) { return ew == 12 ? 2 : 4; }
+__host__ __device__ constexpr int mma_warps(int ew) { return ew == 12 ? 3 : 4; }
 __host__ __device__ constexpr int conv_threads(int mode, int ew) { return 32 * (mma_warp0(mode, ew) + mma_warps(ew)); }
 constexpr int kGatherThreads = 128;
 
@@ -285,65 +286,58 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
 }
 
 // ---------------------------------------------------------------- MMA issuer
-// p.issuers MMA threads (one per MMA warp) share a tile's MT 128-row blocks:
-//  * MT >= issuers (parts = 1): issuer `who` drives blocks who, who + issuers, ... over every K-block;
-//  * MT < issuers: K is split into parts = issuers / MT partial accumulators per block; issuer `who`
-//    drives block who / parts over the K-blocks kb with kb % parts == who % parts.
-// Partial accumulator (block b, part) sits at TMEM columns (b * parts + part) * n_tile; the epilogue
-// adds the parts. Several issuing warps keep the tensor core fed where one warp's issue rate
-// (about one MMA per 100 cycles) would limit it. Stage kb is released by the issuers that read it.
+// The accumulators start at zero (the epilogue clears each one after draining it, and the kernel
+// clears both at start), so every MMA accumulates and a K-block's MMAs can be issued by several
+// threads in any order: issuer `who` of p.issuers takes the K-block's ops o with
+// (o - op0) % issuers == who, for every 128-row block of the tile. One warp issues an MMA only
+// every ~100 cycles; the tensor core takes one every ~40-64, so several issuing warps keep it fed.
+// Every issuer commits every stage, so a stage is released when all of its MMAs are done.
 template <int MODE>
 __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                           uint64_t* acc_full, uint64_t* acc_empty, uint64_t* bres_bar, uint32_t tmem,
                                           int who) {
   if (p.b_resident) mbar_wait(bres_bar, 0);
-  const int S = p.stages, P = p.parts;
-  const int part = who % P;
-  const int b_first = P > 1 ? who / P : who;
-  const int b_step = P > 1 ? p.mt : p.issuers;  // P > 1: one block per issuer
+  const int S = p.stages, I = p.issuers;
   int stage = 0, acc = 0;
   uint32_t ph = 0, aph = 0;
-  long long wf = 0, wa = 0, wi = 0;
+  uint32_t wf = 0, wa = 0, wi = 0;  // role cycles (32-bit: a launch lasts far less than 2^32 cycles)
   // A: SBO 128 B, sm_100 descriptor; blocks are 128 rows (128 16-byte units) apart in a stage
   const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
   const uint32_t a_base = smem_u32(smem + p.a_off) >> 4;
   const uint32_t w_base = smem_u32(smem);
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
-    long long c0 = clock64();
+    uint32_t c0 = (uint32_t)clock();
     mbar_wait(&acc_empty[acc], aph ^ 1);
-    long long c1 = clock64();
+    uint32_t c1 = (uint32_t)clock();
     wa += c1 - c0;
     tc_fence_after();
     const uint32_t d_acc = tmem + acc * p.acc_cols;
-    uint32_t accum = 0;
     for (int kb = 0; kb < p.kblocks; ++kb) {
-      if (kb % P == part) {
-        c0 = clock64();
-        mbar_wait(&full[stage], ph);
-        c1 = clock64();
-        wf += c1 - c0;
-        if (MODE == IXB_MODE_GATHER) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
-        tc_fence_after();
-        // A descriptor = stage base + op start / LBO (16-byte units) + block; B = K-block weights
-        // + op start. Additions to the low 14-bit address field cannot carry (smem < 256 KB).
-        const KBlockDev& K = p.kb[kb];
-        const uint32_t a0 = a_base + (uint32_t)((stage * p.stage_bytes) >> 4);
-        const uint32_t b0 = p.b_resident ? w_base + K.b_off : ((a_base << 4) + stage * p.stage_bytes + p.a_stage_bytes);
-        const uint64_t bdesc0 = umma_desc(b0, 128, 256);
-        const int o0 = K.op0, o1 = K.op0 + K.nops;
+      c0 = (uint32_t)clock();
+      mbar_wait(&full[stage], ph);
+      c1 = (uint32_t)clock();
+      wf += c1 - c0;
+      if (MODE == IXB_MODE_GATHER) fence_proxy_async_smem();  // cp.async (generic proxy) writes -> UMMA reads
+      tc_fence_after();
+      // A descriptor = stage base + op start / LBO (16-byte units) + block; B = K-block weights
+      // + op start. Additions to the low 14-bit address field cannot carry (smem < 256 KB). The
+      // op table is read from the kernel parameters with warp-uniform indices, so the descriptors
+      // stay in uniform registers, which tcgen05.mma takes its operands from.
+      const KBlockDev& K = p.kb[kb];
+      const uint32_t a0 = a_base + (uint32_t)((stage * p.stage_bytes) >> 4);
+      const uint32_t b0 = p.b_resident ? w_base + K.b_off : ((a_base << 4) + stage * p.stage_bytes + p.a_stage_bytes);
+      const uint64_t bdesc0 = umma_desc(b0, 128, 256);
+      const int o1 = K.op0 + K.nops;
 #pragma unroll 2
-        for (int o = o0; o < o1; ++o) {
-          const uint32_t opa = p.op_a[o];
-          const uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
-          const uint64_t bd = bdesc0 + p.op_b[o];
-          for (int b = b_first; b < p.mt; b += b_step)
-            umma_s8(d_acc + (uint32_t)((b * P + part) * p.n_tile), ad + (uint64_t)(b * ((kBlockM * 16) >> 4)), bd,
-                    p.idesc, accum);
-          accum = 1u;
-        }
-        umma_commit(&empty[stage]);
-        wi += clock64() - c1;
+      for (int o = K.op0 + who; o < o1; o += I) {
+        const uint32_t opa = p.op_a[o];
+        const uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
+        const uint64_t bd = bdesc0 + p.op_b[o];
+        for (int b = 0; b < p.mt; ++b)
+          umma_s8(d_acc + (uint32_t)(b * p.n_tile), ad + (uint64_t)(b * ((kBlockM * 16) >> 4)), bd, p.idesc, 1u);
       }
+      umma_commit(&empty[stage]);
+      wi += (uint32_t)clock() - c1;
       if (++stage == S) {
         stage = 0;
         ph ^= 1;
@@ -460,7 +454,6 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
   const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
   const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
-  const int P = p.parts;
   const int units = p.mt * nj;
   const int u_end = ((g + 1) * units) / NG;
   int u = (g * units) / NG;
@@ -477,49 +470,31 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     const bool two = u + 1 < u_end;
     const int b2 = (j + 1 == nj) ? b + 1 : b, j2 = (j + 1 == nj) ? 0 : j + 1;
     uint32_t v[16], w[16];
-    const uint32_t c1 = lane_base + (uint32_t)((b * P) * p.n_tile + j * 16);
-    const uint32_t c2 = lane_base + (uint32_t)((b2 * P) * p.n_tile + j2 * 16);
-    if (P == 1) {
-      tmem_ld16(c1, v);
-      if (two) tmem_ld16(c2, w);
-      if (b != decoded_b) {
-        r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
-        decoded_b = b;
-      }
-      tmem_ld_wait();
-      if (r.valid) store_piece(p, r, ntile, j, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
-      if (two) {
-        if (b2 != decoded_b) {
-          r = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
-          decoded_b = b2;
-        }
-        if (r.valid) store_piece(p, r, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
-      }
-      u += 2;
-      b = two && j2 + 1 == nj ? b2 + 1 : b2;
-      j = two ? (j2 + 1 == nj ? 0 : j2 + 1) : j2;
-    } else {
-      tmem_ld16(c1, v);
-      tmem_ld16(c1 + p.n_tile, w);
-      if (b != decoded_b) {
-        r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
-        decoded_b = b;
-      }
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] += w[i];
-      for (int q2 = 2; q2 < P; ++q2) {
-        tmem_ld16(c1 + q2 * p.n_tile, w);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] += w[i];
-      }
-      if (r.valid) store_piece(p, r, ntile, j, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
-      u += 1;
-      b = b2;
-      j = j2;
+    const uint32_t c1 = lane_base + (uint32_t)(b * p.n_tile + j * 16);
+    const uint32_t c2 = lane_base + (uint32_t)(b2 * p.n_tile + j2 * 16);
+    tmem_ld16(c1, v);
+    if (two) tmem_ld16(c2, w);
+    if (b != decoded_b) {
+      r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
+      decoded_b = b;
     }
+    tmem_ld_wait();
+    // clear the drained columns for the next tile's MMAs, which all accumulate
+    tmem_zero16(c1);
+    if (two) tmem_zero16(c2);
+    if (r.valid) store_piece(p, r, ntile, j, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    if (two) {
+      if (b2 != decoded_b) {
+        r = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
+        decoded_b = b2;
+      }
+      if (r.valid) store_piece(p, r, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    }
+    u += 2;
+    b = two && j2 + 1 == nj ? b2 + 1 : b2;
+    j = two ? (j2 + 1 == nj ? 0 : j2 + 1) : j2;
   }
+  tmem_st_wait();  // the zeros are in TMEM before the accumulator is handed back
 }
 
 template <int MODE, int EW>
@@ -552,7 +527,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
     const uint32_t fcount = (MODE == IXB_MODE_GATHER) ? (uint32_t)kGatherThreads + (p.b_resident ? 0u : 1u) : 1u;
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], fcount);
-      mbar_init(&empty[s], p.issuers / p.parts);  // the issuers that read a stage's K-block
+      mbar_init(&empty[s], p.issuers);  // every issuer commits every stage
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], p.issuers);
@@ -570,6 +545,15 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp < EPI) {
+    // both accumulators start at zero: every MMA accumulates (see issue_mma)
+    const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+    for (int c = (warp >> 2) * 16; c < 2 * p.acc_cols; c += (EPI / 4) * 16) tmem_zero16(tmem + lanes + (uint32_t)c);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   if (warp >= PW0 && warp < MW0) {
     // ------------------------------------------------------------ producers
@@ -589,7 +573,8 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   } else if (warp >= MW0) {
     // ------------------------------------------------------------ MMA issuers
     const int who = warp - MW0;
-    if (lane == 0 && who < p.issuers) issue_mma<MODE>(p, smem, full, empty, acc_full, acc_empty, bres_bar, tmem, who);
+    if (lane == 0 && who < p.issuers)
+      issue_mma<MODE>(p, smem, full, empty, acc_full, acc_empty, bres_bar, tmem, who);
   } else {
     // ------------------------------------------------------------ epilogue
     grid_dep_wait();  // residual reads and output writes follow the previous layer

@@ -41,6 +41,76 @@ __global__ void __launch_bounds__(256) quantize_images_kernel(const uint8_t* __r
   }
 }
 
+// Letterbox ingress: a BGR uint8 frame (any size, row stride) -> letterboxed, Q11-bilinear
+// resized, quantized 8-byte pixels (bytes 0..2 = lut[R], lut[G], lut[B]) in the stem's padded input,
+// the same bytes as the reference's pipelines/preprocess_simd.c fused_preprocess_bgr_to_c8_plane
+// (:331-590): scale = min(dst / src) in float32, nw/nh = floor(src * scale + 0.5), centred pads,
+// per output column sx = (x + 0.5) * (src_w / nw) - 0.5 clamped at the edges with the weight
+// bx1 = floor(alpha * 2048 + 0.5) (float32, written with round-to-nearest intrinsics so nothing
+// contracts), rows likewise, then ((p00 bx0 + p01 bx1 + 1024) >> 11) by0 + (...) by1 + 1024 >> 11
+// in integers; outside the resized image the pad pixel lut[114]. One thread per output pixel.
+struct LetterboxParams {
+  const uint8_t* frames;
+  long long frame_bytes;
+  int src_w, src_h, src_stride;
+  int dst_w, dst_h, nw, nh, pad_top, pad_left;
+  float fx, fy;
+  const int8_t* lut;
+  int8_t* out;           // pixel (0, 0) of image 0 in the padded input
+  int out_row_pixels;    // padded row length in 8-byte pixels
+  long long out_image_bytes;
+  int batch;
+};
+
+__device__ __forceinline__ void letterbox_axis(int i, float f, int src, int& i0, int& i1, int& w0, int& w1) {
+  const float sv = __fsub_rn(__fmul_rn(__fadd_rn((float)i, 0.5f), f), 0.5f);
+  int a = (int)floorf(sv);
+  if (a < 0) a = 0;
+  int b = a + 1;
+  if (b >= src) b = src - 1;
+  float al = __fsub_rn(sv, (float)a);
+  al = fminf(fmaxf(al, 0.0f), 1.0f);
+  const int wb = (int)floorf(__fadd_rn(__fmul_rn(al, 2048.0f), 0.5f));
+  i0 = a;
+  i1 = b;
+  w0 = 2048 - wb;
+  w1 = wb;
+}
+
+__global__ void __launch_bounds__(256) letterbox_kernel(const __grid_constant__ LetterboxParams p) {
+  __shared__ int8_t lut_s[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut_s[i] = p.lut[i];
+  __syncthreads();
+  const long long total = (long long)p.batch * p.dst_h * p.dst_w;
+  const uint32_t pad = (uint8_t)lut_s[114] * 0x010101u;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (long long)gridDim.x * blockDim.x) {
+    const int img = (int)(t / ((long long)p.dst_h * p.dst_w));
+    const int rem = (int)(t - (long long)img * p.dst_h * p.dst_w);
+    const int y = rem / p.dst_w, x = rem - y * p.dst_w;
+    const int iy = y - p.pad_top, ix = x - p.pad_left;
+    uint32_t v = pad;
+    if (iy >= 0 && iy < p.nh && ix >= 0 && ix < p.nw) {
+      int x0, x1, bx0, bx1, y0, y1, by0, by1;
+      letterbox_axis(ix, p.fx, p.src_w, x0, x1, bx0, bx1);
+      letterbox_axis(iy, p.fy, p.src_h, y0, y1, by0, by1);
+      const uint8_t* f = p.frames + (long long)img * p.frame_bytes;
+      const uint8_t* r0 = f + (long long)y0 * p.src_stride;
+      const uint8_t* r1 = f + (long long)y1 * p.src_stride;
+      uint32_t o = 0;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {  // source B, G, R -> output bytes 2, 1, 0
+        const int top = (r0[x0 * 3 + c] * bx0 + r0[x1 * 3 + c] * bx1 + 1024) >> 11;
+        const int bot = (r1[x0 * 3 + c] * bx0 + r1[x1 * 3 + c] * bx1 + 1024) >> 11;
+        const int val = (top * by0 + bot * by1 + 1024) >> 11;
+        o |= (uint32_t)(uint8_t)lut_s[val] << (8 * (2 - c));
+      }
+      v = o;
+    }
+    *reinterpret_cast<uint2*>(p.out + img * p.out_image_bytes + ((long long)y * p.out_row_pixels + x) * 8) =
+        make_uint2(v, 0u);
+  }
+}
+
 struct PoolParams {
   SegDev in;
   SegDev out[3];

@@ -58,6 +58,7 @@ extern "C" {
 #define IXB_OUT_DEVICE 2    /* egress is a device pointer; NULL: leave the heads in the session's egress buffer */
 #define IXB_ASYNC 4         /* return after enqueueing; ixb_session_wait completes the call */
 #define IXB_NO_GRAPH 8      /* launch layer by layer instead of replaying the captured graph */
+#define IXB_IN_STORE 16     /* the stem's input already holds the images (ixb_session_letterbox): no ingress */
 
 /* One stored activation tensor, or a channel range of it. Activations are int8 (t = q - 128)
  * stored as one plane per 16-channel chunk: plane c holds [batch][H+2][W+2] pixels of 16 bytes
@@ -261,6 +262,22 @@ typedef struct ixb_decode_desc {
 int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
                     const float* letterbox, int32_t capacity, float* boxes, float* scores, int32_t* classes,
                     int32_t* counts, void* stream);
+
+/* Letterbox ingress, the reference's pipelines/preprocess_simd.c fused_preprocess_bgr_to_c8_plane
+ * (:331-590; graph_session.py stage_image :866-889) on the GPU, byte for byte: `batch` BGR uint8
+ * frames of src_w x src_h (row stride src_stride, frame_bytes apart; device memory) are letterboxed
+ * into dst_w x dst_h with the reference's float32 scale and Q11 bilinear weights and quantized
+ * through the int8 input table lut (lut[pixel] = the model input's t = q - 128), as 8-byte pixels
+ * (bytes 0..2 = R, G, B; 3..7 untouched) at out (pixel (0, 0) of image 0), rows of out_row_pixels
+ * pixels, images out_image_bytes apart. letterbox (host float[3]) receives pad_top, pad_left and
+ * scale, the values the decode takes. Enqueued on `stream`. */
+int ixb_letterbox_frames(const uint8_t* frames, int batch, int src_w, int src_h, int src_stride, uint64_t frame_bytes,
+                         const int8_t* lut, int8_t* out, int dst_w, int dst_h, int out_row_pixels,
+                         uint64_t out_image_bytes, float* letterbox, void* stream);
+/* The same into a session's stem input, on the session stream; run the network afterwards with
+ * ixb_session_run(s, NULL, batch, egress, flags | IXB_IN_STORE). */
+int ixb_session_letterbox(ixb_session* s, const uint8_t* frames, int batch, int src_w, int src_h, int src_stride,
+                          uint64_t frame_bytes, float* letterbox);
 
 /* sizeof of ixb_segment, ixb_conv_desc, ixb_pool_desc, ixb_plan (for binding checks). */
 int ixb_abi_sizes(uint64_t* sizes, int n);
