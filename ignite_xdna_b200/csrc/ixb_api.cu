@@ -147,7 +147,8 @@ SegDev seg_dev(const ixb_segment& s, uint8_t* arena, int chunk_begin) {
 //  IM2COL: K-blocks tap-major over groups of cp full pairs; an odd last chunk gets K-blocks of two
 //          taps each (slots = the chunk at tap t and t + 1).
 //  GATHER: K-blocks over groups of cp pairs (1x1); a missing second chunk is a zero-weight half.
-//  STEM:   one K-block of six slots: tap 2 * ky + p is the pixel pair p of image row ky.
+//  STEM:   one K-block of three slots, one per image row ky; tap 2 * ky + p is pixel pair p of that
+//          row, pair 1 read as the slot one row on.
 struct SchedKB {
   int chunk0, nchunks, tap0, ntaps, op0, nops, b_off, b_bytes;
 };
@@ -168,8 +169,10 @@ int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>&
   };
   const int E = cin_chunks / 2, odd = cin_chunks % 2;
   if (d.mode == IXB_MODE_STEM) {
-    for (int ky = 0; ky < 3; ++ky) ops.push_back(SchedOp{2 * ky, 0, 2 * ky, 2 * ky + 1, 0, 2 * ky + 1});
-    push_kb(0, 1, 0, 6, 0);
+    // slot ky holds image row ky; the MMA's two K-halves are pairs 0 and 1 of that row (tap 2ky+p),
+    // the second read one row on in the same slot
+    for (int ky = 0; ky < 3; ++ky) ops.push_back(SchedOp{ky, 0, 2 * ky, ky, 0, 2 * ky + 1});
+    push_kb(0, 1, 0, 3, 0);
   } else if (d.mode == IXB_MODE_WINDOW) {
     for (int g = 0; g * d.cp < E; ++g) {
       const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
@@ -249,6 +252,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.W = d.in_w;
   p.Ho = d.out_h;
   p.Wo = d.out_w;
+  p.Wm = d.mode == IXB_MODE_STEM ? d.out_w + 1 : d.out_w;
   p.batch = batch;
   p.cp = d.cp;
   p.n_tile = d.n_tile;
@@ -292,7 +296,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * (d.in_h + 2) * (d.in_w + 2));
   } else {
     p.win_origin = 0;
-    p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * d.out_w);
+    p.m_total = (int)std::min<long long>(0x7fffffffLL, (long long)batch * d.out_h * p.Wm);
   }
   if ((long long)batch * (d.in_h + 2) * (d.in_w + 4) >= 0x7fff0000LL)
     return bad("more pixels than 32-bit pixel indices cover");
@@ -335,7 +339,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   for (;; mt /= 2) {
     p.mt = mt;
     p.tile_rows = 128 * mt;
-    p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + 2 * p.win_origin : p.tile_rows;
+    p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + 2 * p.win_origin
+              : (d.mode == IXB_MODE_STEM ? p.tile_rows + 8 : p.tile_rows);  // STEM: rows for the pair shift
     // 16 spare bytes: a single-tap MMA's unused second K-half reads one row past its slot
     p.a_stage_bytes = slots * p.rowsA * 16 + 16;
     p.b_resident = b_total <= budget / 2 ? 1 : 0;
@@ -354,7 +359,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.bar_off = p.tbl_off + (d.mode == IXB_MODE_GATHER ? 2 * p.tile_rows * 16 : 0);
   p.bias_off = p.bar_off + 512;
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
-  if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.tile_rows > 1024)
+  if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.rowsA > 1024)
     return bad("an im2col load carries at most 1024 pixels");
   // Warps: MMA-heavy tiles (long K over one or two 128-row blocks) take 8 epilogue and 4 MMA
   // warps, the rest 12 epilogue and 3 MMA warps (GATHER always 8 + 4); the issuers split each
@@ -370,8 +375,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.shift = d.shift;
   p.fd_P = make_fastdiv((uint32_t)((d.in_h + 2) * (d.in_w + 2)));
   p.fd_W2 = make_fastdiv((uint32_t)(d.in_w + 2));
-  p.fd_hw = make_fastdiv((uint32_t)(d.out_h * d.out_w));
-  p.fd_Wo = make_fastdiv((uint32_t)d.out_w);
+  p.fd_hw = make_fastdiv((uint32_t)(d.out_h * p.Wm));
+  p.fd_Wo = make_fastdiv((uint32_t)p.Wm);
   p.acc_cols = p.mt * d.n_tile;
   int cols = 32;
   while (cols < 2 * p.acc_cols) cols *= 2;
@@ -379,7 +384,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.idesc = umma_idesc_s8(kBlockM, d.n_tile);
   {
     // kernel op table: A start / LBO from (slot, tap) and the geometry, deduplicated per K-block
-    auto shift_of = [&](int t) { return d.mode == IXB_MODE_WINDOW ? (t / d.k) * (d.in_w + 2) + (t % d.k) : 0; };
+    auto shift_of = [&](int t) {
+      return d.mode == IXB_MODE_WINDOW ? (t / d.k) * (d.in_w + 2) + (t % d.k) : (d.mode == IXB_MODE_STEM ? (t & 1) : 0);
+    };
     std::vector<uint32_t> ta;
     std::vector<uint16_t> tb;
     for (size_t i = 0; i < kbs.size(); ++i) {
@@ -519,9 +526,12 @@ int encode_im2col(ConvLaunch& L, const ixb_conv_desc& d, uint8_t* arena, int bat
     strides[2] = (cuuint64_t)(s.height + 2) * (s.width + 4) * 8;
     es[0] = 1; es[1] = 1; es[2] = 2; es[3] = 1;
   }
-  int lower[2] = {0, 0}, upper[2] = {-2, -2};
+  // corners (W, H): IM2COL and STEM walk Ho rows of stride-2 windows; STEM walks Wo + 1 pairs per
+  // row (a spare output column, so the pair-1 shift stays within the row) and loads tile + 8 rows
+  int lower[2] = {0, 0}, upper[2] = {d.mode == IXB_MODE_STEM ? -1 : -2, -2};
   CUresult r = enc(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, lower, upper, 16,
-                   (cuuint32_t)p.tile_rows, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   (cuuint32_t)(d.mode == IXB_MODE_STEM ? p.rowsA : p.tile_rows), es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     err = "cuTensorMapEncodeIm2col failed (" + std::to_string((int)r) + ")";

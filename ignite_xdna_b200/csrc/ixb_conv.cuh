@@ -26,8 +26,10 @@
 //    im2col load walks the filter positions (element stride 2, corners 0/-2 on the padded plane)
 //    and lands the tile's rows for that tap.
 //  * STEM: the image stored as 8-byte pixels (3 channels + 5 zero) and read as 16-byte pixel pairs;
-//    output pixel (y, x) tap (ky, pair p) is the pair at padded row 2y+ky, column 2x+2p: six TMA
-//    im2col loads (3 rows x 2 pairs) cover the 3x3 stride-2 window.
+//    output pixel (y, x) tap (ky, pair p) is the pair at padded row 2y+ky, column 2x+2p. Pair p = 1
+//    of output x is pair 0 of output x + 1, so one TMA im2col load per image row ky (tile + 8 rows)
+//    serves both pairs, the second as the same slot one row on; the M space carries one spare output
+//    column per row (computed, then dropped) so that shift never crosses into the next output row.
 //  * GATHER (a 1x1 conv over a concat that includes a nearest-2x upsampled view): per-row 16-byte
 //    cp.async gathers by 128 producer threads from a per-tile table of output coordinates.
 // Shared-memory operands use the K-major no-swizzle core-matrix layout: A as [slot][pixel][16 B]
@@ -98,7 +100,8 @@ struct ConvParams {
   int8_t* egress;
   long long egress_img;
   int cout;
-  FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wo, Wo
+  FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wm, Wm
+  int Wm;                             // output row length in M space: Wo, or Wo + 1 for STEM
   unsigned long long* stats;          // optional per-CTA role counters (kStatWords per CTA), or null
   KBlockDev kb[kMaxKBlocks];          // the K schedule
   uint32_t op_a[kMaxOps];             // per MMA: A start (16-byte units from the stage) | LBO (16-byte units) << 16
@@ -176,7 +179,7 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
       img0 = (int)fdiv((uint32_t)m0, p.fd_hw);
       const int rem = m0 - img0 * (int)p.fd_hw.d;
       y0 = (int)fdiv((uint32_t)rem, p.fd_Wo);
-      x0 = rem - y0 * p.Wo;
+      x0 = rem - y0 * p.Wm;
     }
     for (int kb = 0; kb < p.kblocks; ++kb) {
       const long long c0 = clock64();
@@ -186,7 +189,7 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
       uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
       const KBlockDev& K = p.kb[kb];
       const int nslots = K.nchunks * K.ntaps;
-      mbar_arrive_expect_tx(&full[stage], (uint32_t)nslots * (MODE == IXB_MODE_WINDOW ? slot_bytes : p.tile_rows * 16u) +
+      mbar_arrive_expect_tx(&full[stage], (uint32_t)nslots * (MODE == IXB_MODE_IM2COL ? p.tile_rows * 16u : slot_bytes) +
                                               (p.b_resident ? 0u : (uint32_t)K.b_bytes));
       for (int sl = 0; sl < nslots; ++sl) {
         const int gc = K.chunk0 + sl / K.ntaps;
@@ -199,8 +202,8 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
           const SegDev& s = p.seg[0];
           tma_im2col(As + sl * slot_bytes, &p.tmap, 2 * x0, 2 * y0, (gc - s.chunk_begin) * s.plane_images + img0,
                      tap % 3, tap / 3, &full[stage]);
-        } else {  // STEM: tap = 2 * ky + pair
-          tma_im2col(As + sl * slot_bytes, &p.tmap, x0, 2 * y0, img0, tap & 1, tap >> 1, &full[stage]);
+        } else {  // STEM: slot = image row ky; pair 1 of output x is pair 0 of x + 1, one row on
+          tma_im2col(As + sl * slot_bytes, &p.tmap, x0, 2 * y0, img0, 0, tap, &full[stage]);
         }
       }
       if (!p.b_resident)
@@ -410,7 +413,8 @@ __device__ __forceinline__ RowInfo decode_row(const ConvParams& p, int m) {
     r.img = (int)fdiv((uint32_t)m, p.fd_hw);
     const int rem = m - r.img * (int)p.fd_hw.d;
     r.oy = (int)fdiv((uint32_t)rem, p.fd_Wo);
-    r.ox = rem - r.oy * p.Wo;
+    r.ox = rem - r.oy * p.Wm;
+    r.valid = r.valid && r.ox < p.Wo;  // STEM computes one spare column per output row
     r.opix = r.img * (p.Ho + 2) * (p.Wo + 2) + (r.oy + 1) * (p.Wo + 2) + (r.ox + 1);
   }
   return r;

@@ -172,6 +172,7 @@ class GraphSession:
             dst.copy_(torch.from_numpy(x.reshape(-1)).to(self.device))
         torch.cuda.synchronize(self.device)
         self._staged = b
+        self._staged_store = False
 
     # ------------------------------------------------------------------ pipelined runs
     def _owns(self, a: np.ndarray) -> bool:
@@ -239,13 +240,41 @@ class GraphSession:
         self._last_batch = b
         return h
 
+    def stage_image(self, img_bgr: Any):
+        """Letterbox, resize and quantize one BGR frame into the stem's input on the device (the
+        reference's ``GraphSession.stage_image``, graph_session.py:866-889); returns the letterbox
+        ``((pad_top, pad_left), scale)`` for box decoding."""
+        lb = self.stage_images(img_bgr[None])
+        return (int(lb[0, 0]), int(lb[0, 1])), float(lb[0, 2])
+
+    def stage_images(self, frames: Any) -> np.ndarray:
+        """uint8 BGR frames [B, H, W, 3] (host or CUDA, all one size) -> letterboxed into the stem's
+        input by the GPU kernel; returns float32 [B, 3] (pad_top, pad_left, scale) per image."""
+        torch = _torch()
+        self._drain()
+        x = frames if isinstance(frames, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(frames))
+        if x.dtype != torch.uint8 or x.dim() != 4 or x.shape[3] != 3:
+            raise ValueError(f"expected uint8 BGR frames [B, H, W, 3], got {tuple(x.shape)} {x.dtype}")
+        b = int(x.shape[0])
+        if not 1 <= b <= self.max_batch:
+            raise ValueError(f"batch {b} outside [1, {self.max_batch}]")
+        x = x.contiguous().to(self.device)
+        h, w = int(x.shape[1]), int(x.shape[2])
+        lb = (C.c_float * 3)()
+        L.check(self.lib.ixb_session_letterbox(self._h, C.c_void_p(x.data_ptr()), b, w, h, 3 * w, 3 * w * h, lb))
+        torch.cuda.synchronize(self.device)
+        self._staged = b
+        self._staged_store = True
+        return np.tile(np.array(list(lb), dtype=np.float32), (b, 1))
+
     def dispatch(self, timeout_ms: int = 10000, batch: Optional[int] = None) -> None:
         """Run the network on the staged images; heads stay in the device egress."""
         self._drain()
         b = int(batch or self._staged)
         if b < 1:
             raise RuntimeError("no staged input")
-        L.check(self.lib.ixb_session_run(self._h, None, b, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
+        src = L.IN_STORE if getattr(self, "_staged_store", False) else L.IN_DEVICE
+        L.check(self.lib.ixb_session_run(self._h, None, b, None, src | L.OUT_DEVICE | L.ASYNC))
         self._wait(timeout_ms)
         self._last_batch = b
 
@@ -282,7 +311,8 @@ class GraphSession:
             b = self._staged
             if b < 1:
                 raise RuntimeError("no staged input")
-            L.check(self.lib.ixb_session_run(self._h, None, b, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
+            src = L.IN_STORE if getattr(self, "_staged_store", False) else L.IN_DEVICE
+            L.check(self.lib.ixb_session_run(self._h, None, b, None, src | L.OUT_DEVICE | L.ASYNC))
         else:
             x = self._as_pixels(input_tensor)
             b = self._check_shape(x.shape)

@@ -53,14 +53,15 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
         sp = _seg_params(d, d.seg[i], chunk)
         chunk += sp["chunks"]
         segs.append(sp)
+    Wm = Wo + 1 if mode == L.MODE_STEM else Wo    # STEM computes one spare column per output row
     if mode == L.MODE_WINDOW:
         win_origin = pad * (W + 2) + pad
         rowsA = TM + 2 * win_origin
         m_total = batch * (H + 2) * (W + 2)
     else:
         win_origin = 0
-        rowsA = TM
-        m_total = batch * Ho * Wo
+        rowsA = TM + 8 if mode == L.MODE_STEM else TM
+        m_total = batch * Ho * Wm
     assert info["kblocks"] == len(sched) and info["rows_a"] == rowsA
     b_total = sched[-1]["b_off"] + sched[-1]["b_bytes"]
     assert (d.cout // n_tile) * b_total == d.w_bytes
@@ -68,7 +69,9 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
     a_bytes = slots * rowsA * 16 + 16
 
     def shift_of(t):
-        return (t // k) * (W + 2) + (t % k) if mode == L.MODE_WINDOW else 0
+        if mode == L.MODE_WINDOW:
+            return (t // k) * (W + 2) + (t % k)
+        return t & 1 if mode == L.MODE_STEM else 0
 
     bias = arena[d.bias_offset:d.bias_offset + 4 * d.cout].view(np.int32).astype(np.int64)
     lut = arena[d.lut_offset:d.lut_offset + 256].view(np.int8).astype(np.int64)
@@ -84,15 +87,16 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                     tap = blk["tap0"] + sl % blk["ntaps"]
                     dst0 = sl * rowsA * 16
                     if mode == L.MODE_STEM:
-                        r = np.arange(TM)
+                        # slot = image row ky (the K-block's taps 0..2), pair 0 of every M row
+                        r = np.arange(rowsA)
                         m = m0 + r
                         ok = m < m_total
                         s = d.seg[0]
-                        img = m // (Ho * Wo)
-                        rem = m - img * Ho * Wo
-                        y, x = rem // Wo, rem % Wo
-                        ky, pr = tap // 2, tap % 2
-                        src = s.offset + ((img * (s.height + 2) + 2 * y + ky) * (s.width + 4) + 2 * x + 2 * pr) * 8
+                        img = m // (Ho * Wm)
+                        rem = m - img * Ho * Wm
+                        y, x = rem // Wm, rem % Wm
+                        ky = tap
+                        src = s.offset + ((img * (s.height + 2) + 2 * y + ky) * (s.width + 4) + 2 * x) * 8
                         for rr in np.nonzero(ok)[0]:
                             smem[dst0 + rr * 16:dst0 + rr * 16 + 16] = arena[src[rr]:src[rr] + 16]
                         continue
@@ -143,9 +147,10 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                 valid &= (yp >= 1) & (yp <= H) & (xp >= 1) & (xp <= W)
                 opix, oy, ox = m, yp - 1, xp - 1
             else:
-                img = m // (Ho * Wo)
-                rem = m - img * Ho * Wo
-                oy, ox = rem // Wo, rem % Wo
+                img = m // (Ho * Wm)
+                rem = m - img * Ho * Wm
+                oy, ox = rem // Wm, rem % Wm
+                valid &= ox < Wo
                 opix = img * (Ho + 2) * (Wo + 2) + (oy + 1) * (Wo + 2) + ox + 1
             co = nt * n_tile + np.arange(n_tile)
             a = acc + bias[co][None, :]
