@@ -144,8 +144,9 @@ SegDev seg_dev(const ixb_segment& s, uint8_t* arena, int chunk_begin) {
 // this order. Slot s of a K-block holds chunk chunk0 + s / ntaps at tap tap0 + s % ntaps.
 //  WINDOW: full chunk pairs, cp pairs per K-block, all taps as window shifts of the pair's slots;
 //          an odd last chunk gets a K-block whose MMAs pair consecutive taps of that chunk.
-//  IM2COL: K-blocks tap-major over groups of cp full pairs; an odd last chunk gets K-blocks of two
-//          taps each (slots = the chunk at tap t and t + 1).
+//  IM2COL: K-blocks per (image row ky, group of cp full pairs) holding the loaded taps kx = 0, 1 of
+//          each chunk (slot = chunk * 2 + kx) and the MMAs of kx = 0, 1, 2 (kx = 2 reads the kx = 0
+//          slot one row on); an odd last chunk gets one K-block of its six loaded taps.
 //  GATHER: K-blocks over groups of cp pairs (1x1); a missing second chunk is a zero-weight half.
 //  STEM:   one K-block of three slots, one per image row ky; tap 2 * ky + p is pixel pair p of that
 //          row, pair 1 read as the slot one row on.
@@ -187,19 +188,35 @@ int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>&
       push_kb(2 * E, 1, 0, 1, op0);
     }
   } else if (d.mode == IXB_MODE_IM2COL) {
-    for (int t = 0; t < taps; ++t) {
+    // Loaded taps: kx = 0 and 1 of each image row ky (loaded tap 2 ky + kx); kx = 2 of output x is
+    // kx = 0 of output x + 1, read as the kx = 0 slot one row on. Per (ky, chunk group) a K-block
+    // holds both loaded taps of its chunks and the MMAs of all three kx.
+    for (int ky = 0; ky < 3; ++ky) {
       for (int g = 0; g * d.cp < E; ++g) {
         const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
-        for (int i = 0; i < prs; ++i) ops.push_back(SchedOp{2 * i, c0 + 2 * i, t, 2 * i + 1, c0 + 2 * i + 1, t});
-        push_kb(c0, 2 * prs, t, 1, op0);
+        for (int kx = 0; kx < 3; ++kx) {
+          const int t = 3 * ky + kx, lx = kx == 2 ? 0 : kx;
+          for (int i = 0; i < prs; ++i)
+            ops.push_back(SchedOp{2 * (2 * i) + lx, c0 + 2 * i, t, 2 * (2 * i + 1) + lx, c0 + 2 * i + 1, t});
+        }
+        push_kb(c0, 2 * prs, 2 * ky, 2, op0);
       }
     }
     if (odd) {
+      // the last chunk alone: its six loaded taps in one K-block, consecutive taps paired
+      // (an MMA's second K-half must lie above its first: halves are ordered by slot, then shift)
+      auto slot_of = [](int t) { return 2 * (t / 3) + (t % 3 == 1 ? 1 : 0); };
+      auto addr_of = [&](int t) { return 2 * slot_of(t) + (t % 3 == 2 ? 1 : 0); };
+      const int op0 = (int)ops.size();
       for (int t = 0; t < taps; t += 2) {
-        const int op0 = (int)ops.size(), nt = std::min(2, taps - t);
-        ops.push_back(nt == 2 ? SchedOp{0, 2 * E, t, 1, 2 * E, t + 1} : SchedOp{0, 2 * E, t, 0, -1, 0});
-        push_kb(2 * E, 1, t, nt, op0);
+        if (t + 1 >= taps) {
+          ops.push_back(SchedOp{slot_of(t), 2 * E, t, 0, -1, 0});
+        } else {
+          const int lo = addr_of(t) < addr_of(t + 1) ? t : t + 1, hi = lo == t ? t + 1 : t;
+          ops.push_back(SchedOp{slot_of(lo), 2 * E, lo, slot_of(hi), 2 * E, hi});
+        }
       }
+      push_kb(2 * E, 1, 0, 6, op0);
     }
   } else {
     const int pairs = (cin_chunks + 1) / 2;
@@ -252,7 +269,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.W = d.in_w;
   p.Ho = d.out_h;
   p.Wo = d.out_w;
-  p.Wm = d.mode == IXB_MODE_STEM ? d.out_w + 1 : d.out_w;
+  // STEM and IM2COL compute one spare output column per row so that a one-row descriptor shift
+  // (the neighbouring tap) never crosses into the next output row
+  p.Wm = (d.mode == IXB_MODE_STEM || d.mode == IXB_MODE_IM2COL) ? d.out_w + 1 : d.out_w;
   p.batch = batch;
   p.cp = d.cp;
   p.n_tile = d.n_tile;
@@ -340,7 +359,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.mt = mt;
     p.tile_rows = 128 * mt;
     p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + 2 * p.win_origin
-              : (d.mode == IXB_MODE_STEM ? p.tile_rows + 8 : p.tile_rows);  // STEM: rows for the pair shift
+              : ((d.mode == IXB_MODE_STEM || d.mode == IXB_MODE_IM2COL) ? p.tile_rows + 8 : p.tile_rows);
     // 16 spare bytes: a single-tap MMA's unused second K-half reads one row past its slot
     p.a_stage_bytes = slots * p.rowsA * 16 + 16;
     p.b_resident = b_total <= budget / 2 ? 1 : 0;
@@ -385,7 +404,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   {
     // kernel op table: A start / LBO from (slot, tap) and the geometry, deduplicated per K-block
     auto shift_of = [&](int t) {
-      return d.mode == IXB_MODE_WINDOW ? (t / d.k) * (d.in_w + 2) + (t % d.k) : (d.mode == IXB_MODE_STEM ? (t & 1) : 0);
+      if (d.mode == IXB_MODE_WINDOW) return (t / d.k) * (d.in_w + 2) + (t % d.k);
+      if (d.mode == IXB_MODE_STEM) return t & 1;
+      return d.mode == IXB_MODE_IM2COL && t % 3 == 2 ? 1 : 0;
     };
     std::vector<uint32_t> ta;
     std::vector<uint16_t> tb;
@@ -526,12 +547,11 @@ int encode_im2col(ConvLaunch& L, const ixb_conv_desc& d, uint8_t* arena, int bat
     strides[2] = (cuuint64_t)(s.height + 2) * (s.width + 4) * 8;
     es[0] = 1; es[1] = 1; es[2] = 2; es[3] = 1;
   }
-  // corners (W, H): IM2COL and STEM walk Ho rows of stride-2 windows; STEM walks Wo + 1 pairs per
-  // row (a spare output column, so the pair-1 shift stays within the row) and loads tile + 8 rows
-  int lower[2] = {0, 0}, upper[2] = {d.mode == IXB_MODE_STEM ? -1 : -2, -2};
+  // corners (W, H): Ho rows of stride-2 windows, and Wo + 1 window positions per row (a spare output
+  // column, so the one-row shift to the neighbouring tap stays within the row); tile + 8 rows a load
+  int lower[2] = {0, 0}, upper[2] = {-1, -2};
   CUresult r = enc(&p.tmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, lower, upper, 16,
-                   (cuuint32_t)(d.mode == IXB_MODE_STEM ? p.rowsA : p.tile_rows), es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_NONE,
+                   (cuuint32_t)p.rowsA, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     err = "cuTensorMapEncodeIm2col failed (" + std::to_string((int)r) + ")";

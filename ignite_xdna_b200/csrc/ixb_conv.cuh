@@ -22,9 +22,10 @@
 //    ONE window of 128*MT + 2((W+2)+1) pixels per chunk feeds all nine taps, each tap the same smem
 //    window through a descriptor whose start moves 16 bytes per pixel of shift. A window is one
 //    bulk copy (TMA engine) per chunk. Halo outputs are computed and dropped.
-//  * IM2COL (3x3 stride 2): the tile is 128*MT interior output pixels; per (tap, chunk) one TMA
-//    im2col load walks the filter positions (element stride 2, corners 0/-2 on the padded plane)
-//    and lands the tile's rows for that tap.
+//  * IM2COL (3x3 stride 2): the tile is 128*MT output pixels (one spare column per output row); per
+//    (image row ky, kx in {0, 1}, chunk) one TMA im2col load walks the filter positions (element
+//    stride 2 on the padded plane) and lands the tile's rows (+ 8) for that tap; kx = 2 of output x
+//    is kx = 0 of output x + 1, read as that slot one row on.
 //  * STEM: the image stored as 8-byte pixels (3 channels + 5 zero) and read as 16-byte pixel pairs;
 //    output pixel (y, x) tap (ky, pair p) is the pair at padded row 2y+ky, column 2x+2p. Pair p = 1
 //    of output x is pair 0 of output x + 1, so one TMA im2col load per image row ky (tile + 8 rows)
@@ -189,8 +190,7 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
       uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
       const KBlockDev& K = p.kb[kb];
       const int nslots = K.nchunks * K.ntaps;
-      mbar_arrive_expect_tx(&full[stage], (uint32_t)nslots * (MODE == IXB_MODE_IM2COL ? p.tile_rows * 16u : slot_bytes) +
-                                              (p.b_resident ? 0u : (uint32_t)K.b_bytes));
+      mbar_arrive_expect_tx(&full[stage], (uint32_t)nslots * slot_bytes + (p.b_resident ? 0u : (uint32_t)K.b_bytes));
       for (int sl = 0; sl < nslots; ++sl) {
         const int gc = K.chunk0 + sl / K.ntaps;
         const int tap = K.tap0 + sl % K.ntaps;
@@ -198,10 +198,10 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
           const SegDev& s = p.seg[seg_of_chunk(p, gc)];
           bulk_g2s(As + sl * slot_bytes, s.base + (long long)(gc - s.chunk_begin) * s.plane + wb * 16, slot_bytes,
                    &full[stage]);
-        } else if (MODE == IXB_MODE_IM2COL) {
+        } else if (MODE == IXB_MODE_IM2COL) {  // loaded tap = 2 ky + kx, kx in {0, 1}
           const SegDev& s = p.seg[0];
           tma_im2col(As + sl * slot_bytes, &p.tmap, 2 * x0, 2 * y0, (gc - s.chunk_begin) * s.plane_images + img0,
-                     tap % 3, tap / 3, &full[stage]);
+                     tap & 1, tap >> 1, &full[stage]);
         } else {  // STEM: slot = image row ky; pair 1 of output x is pair 0 of x + 1, one row on
           tma_im2col(As + sl * slot_bytes, &p.tmap, x0, 2 * y0, img0, 0, tap, &full[stage]);
         }

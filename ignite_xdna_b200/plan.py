@@ -131,8 +131,8 @@ def choose_cp(mode: int, k: int, cin: int) -> int:
     if mode == L.MODE_STEM:
         return 2
     pairs = (cin + 31) // 32
-    if mode == L.MODE_WINDOW and k == 3:
-        return 1
+    if (mode == L.MODE_WINDOW and k == 3) or mode == L.MODE_IM2COL:
+        return 1    # 3x3: a K-block already carries the MMAs of 9 (window) or 3 (im2col) taps per pair
     return 4 if pairs >= 4 else (2 if pairs >= 2 else 1)
 
 

@@ -53,14 +53,14 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
         sp = _seg_params(d, d.seg[i], chunk)
         chunk += sp["chunks"]
         segs.append(sp)
-    Wm = Wo + 1 if mode == L.MODE_STEM else Wo    # STEM computes one spare column per output row
+    Wm = Wo + 1 if mode in (L.MODE_STEM, L.MODE_IM2COL) else Wo    # one spare column per output row
     if mode == L.MODE_WINDOW:
         win_origin = pad * (W + 2) + pad
         rowsA = TM + 2 * win_origin
         m_total = batch * (H + 2) * (W + 2)
     else:
         win_origin = 0
-        rowsA = TM + 8 if mode == L.MODE_STEM else TM
+        rowsA = TM + 8 if mode in (L.MODE_STEM, L.MODE_IM2COL) else TM
         m_total = batch * Ho * Wm
     assert info["kblocks"] == len(sched) and info["rows_a"] == rowsA
     b_total = sched[-1]["b_off"] + sched[-1]["b_bytes"]
@@ -71,7 +71,9 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
     def shift_of(t):
         if mode == L.MODE_WINDOW:
             return (t // k) * (W + 2) + (t % k)
-        return t & 1 if mode == L.MODE_STEM else 0
+        if mode == L.MODE_STEM:
+            return t & 1
+        return 1 if mode == L.MODE_IM2COL and t % 3 == 2 else 0
 
     bias = arena[d.bias_offset:d.bias_offset + 4 * d.cout].view(np.int32).astype(np.int64)
     lut = arena[d.lut_offset:d.lut_offset + 256].view(np.int8).astype(np.int64)
@@ -112,13 +114,16 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                         src = cbase + m * 16
                         rows = px
                     else:
-                        r = np.arange(TM)
+                        r = np.arange(rowsA)
                         m = m0 + r
                         ok = m < m_total
-                        img = m // (Ho * Wo)
-                        rem = m - img * Ho * Wo
-                        y, x = rem // Wo, rem % Wo
-                        ky, kx = tap // k, tap % k
+                        img = m // (Ho * Wm)
+                        rem = m - img * Ho * Wm
+                        y, x = rem // Wm, rem % Wm
+                        if mode == L.MODE_IM2COL:
+                            ky, kx = tap // 2, tap % 2           # loaded tap 2 ky + kx
+                        else:
+                            ky, kx = tap // k, tap % k
                         iy, ix = y * stride + ky - pad, x * stride + kx - pad
                         if s["up2"]:
                             iy, ix = iy >> 1, ix >> 1

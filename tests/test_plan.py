@@ -78,7 +78,11 @@ def test_schedule_covers_every_tap_and_chunk_once(mode, k, cin, cp):
                     continue
                 slot, chunk, tap = half
                 assert slot < nslots
-                if mode != L.MODE_WINDOW:     # the slot's loaded (chunk, tap) is the half's
+                if mode == L.MODE_IM2COL:     # the slot's loaded tap 2 ky + kx; kx = 2 reads kx = 0
+                    assert chunk == blk["chunk0"] + slot // blk["ntaps"]
+                    lt = blk["tap0"] + slot % blk["ntaps"]
+                    assert tap // 3 == lt // 2 and (tap % 3 == lt % 2 or (tap % 3 == 2 and lt % 2 == 0))
+                elif mode != L.MODE_WINDOW:   # the slot's loaded (chunk, tap) is the half's
                     assert chunk == blk["chunk0"] + slot // blk["ntaps"]
                     assert tap == blk["tap0"] + slot % blk["ntaps"]
                 else:
