@@ -1364,6 +1364,24 @@ int ixb_w4a8_gemm(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   return launch_gemm<GEMM_B_W4>(L, static_cast<cudaStream_t>(stream));
 }
 
+int ixb_u8i4_gemm_i32(const uint8_t* a, const uint8_t* image, int32_t* out, int M, int N, int K, void* stream) {
+  if (!a || !image || !out) return fail(IXB_ERR_INVALID, "null argument");
+  if (int r = check_w4a8_shape(N, K)) return r;
+  if (K > 32768) return fail(IXB_ERR_INVALID, "K above 32768 could overflow the int32 product of uint8 x int4");
+  if (!aligned16(a) || !aligned16(image) || !aligned16(out))
+    return fail(IXB_ERR_INVALID, "u8i4 operands must be 16-byte aligned");
+  GemmLaunch L;
+  std::string err;
+  if (plan_gemm(L, M, N, K, err, GEMM_B_W4)) return fail(IXB_ERR_INVALID, err);
+  L.p.idesc = umma_idesc_u8s8(128, L.p.bn);
+  L.p.out_kind = GEMM_OUT_I32;
+  L.p.out32 = out;
+  L.p.wq = image;
+  L.p.eg = image + (uint64_t)N * (K / 2);
+  if (encode_kmajor(&L.p.ta, a, M, K, 128, err)) return fail(IXB_ERR_CUDA, err);
+  return launch_gemm<GEMM_B_W4>(L, static_cast<cudaStream_t>(stream));
+}
+
 int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out, int N, int K,
                   void* stream) {
   if (!a || !image || !shift || !out) return fail(IXB_ERR_INVALID, "null argument");

@@ -158,6 +158,8 @@ __host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
          | ((uint32_t)(n >> 3) << 17)       // N / 8
          | ((uint32_t)(m >> 4) << 24);      // M / 16
 }
+// The same with an unsigned 8-bit A (A format 0): u8 x s8 -> s32.
+__host__ __device__ constexpr uint32_t umma_idesc_u8s8(int m, int n) { return umma_idesc_s8(m, n) & ~(7u << 7); }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
 __device__ __forceinline__ void umma_s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,

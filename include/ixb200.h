@@ -229,6 +229,11 @@ int ixb_w4a8_gemm(const int8_t* a, const uint8_t* image, const int32_t* shift, i
                   int M, int N, int K, void* stream);
 int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, int8_t* out,
                   int N, int K, void* stream);
+/* The engine's other operand pair, uint8 activations x int4 weights (the reference's
+ * kernels/int4_study/u8i4_kernels.cc mm_u8i4_* and tools/int4_prefill_model.py Int4MmulReference):
+ * out int32 [M][N] = sum_k a[m][k] * (w[k][n] << d), a uint8 [M][K], the weight image of
+ * ixb_w4a8_prepare (equal group positions give d = 0, the plain product), K <= 32768. */
+int ixb_u8i4_gemm_i32(const uint8_t* a, const uint8_t* image, int32_t* out, int M, int N, int K, void* stream);
 
 /* YOLOv8 detect decode + NMS on the GPU: the detections of the reference's
  * pipelines/decode_native.c yolo_decode_int8 (:407-540), bit for bit, for `batch` images of int8

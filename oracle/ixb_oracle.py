@@ -206,6 +206,12 @@ def w4a8_acc(a: np.ndarray, w_kn: np.ndarray, gpos: np.ndarray, group: int = 128
     return acc
 
 
+def u8i4_i32(a_u8: np.ndarray, w_kn: np.ndarray) -> np.ndarray:
+    """uint8 A [M,K] x int4 B [K,N] (packed [K, N/2], low nibble first) -> int64 [M,N], the
+    reference's Int4MmulReference.execute (tools/int4_prefill_model.py:182-207) at any size."""
+    return exact_matmul(np.asarray(a_u8, dtype=np.uint8).astype(np.int64), unpack_int4(w_kn).astype(np.int64))
+
+
 def w4a8_srs(a, w_kn, gpos, shift: np.ndarray, group: int = 128) -> np.ndarray:
     """W4A8 output: per output column RNE shift and int8 clamp of the group-aligned accumulator."""
     acc = w4a8_acc(a, w_kn, gpos, group)

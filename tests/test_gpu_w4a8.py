@@ -93,3 +93,41 @@ def test_w4a8_refuses_group_spread_above_4():
     gpos[0, 5] -= 0
     rc, _ = prepare(w, gpos, 256, 64)
     assert rc == L.IXB_ERR_INVALID
+
+
+def _u8i4_gpu(a_u8, w_kn, K, N):
+    import torch
+    lib = L.load()
+    gpos = np.zeros((K // 128, N), dtype=np.int8)
+    rc, img = prepare(w_kn, gpos, K, N)
+    L.check(rc)
+    da = _dev(a_u8)
+    out = torch.empty((a_u8.shape[0], N), dtype=torch.int32, device="cuda")
+    L.check(lib.ixb_u8i4_gemm_i32(C.c_void_p(da.data_ptr()), C.c_void_p(img.data_ptr()), C.c_void_p(out.data_ptr()),
+                                  a_u8.shape[0], N, K, None))
+    torch.cuda.synchronize()
+    return out.cpu().numpy().astype(np.int64)
+
+
+def test_u8i4_matches_reference_known_answers(golden_dir):
+    """The reference's Int4MmulReference tiles (4x8 uint8 x 8x16 int4), zero-padded to K = 128."""
+    kat = np.load(golden_dir / "u8i4_kat.npz")
+    for i in range(6):
+        a = np.zeros((4, 128), dtype=np.uint8)
+        a[:, :8] = kat[f"a{i}"]
+        w = np.zeros((128, 16), dtype=np.int8)
+        w[:8] = O.unpack_int4(kat[f"b{i}_packed"])
+        assert np.array_equal(_u8i4_gpu(a, O.pack_int4(w), 128, 16), kat[f"c{i}"])
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (77, 272, 1152), (300, 64, 32768)])
+def test_u8i4_gemm_matches_oracle(M, N, K):
+    rng = np.random.default_rng(M + K)
+    a = rng.integers(0, 256, size=(M, K), dtype=np.uint8)
+    if K == 32768:
+        a[:] = 255      # the int32 bound: 255 * 8 * K
+    w = rng.integers(-8, 8, size=(K, N), dtype=np.int8)
+    if K == 32768:
+        w[:] = -8
+    wk = O.pack_int4(w)
+    assert np.array_equal(_u8i4_gpu(a, wk, K, N), O.u8i4_i32(a, wk))

@@ -100,3 +100,9 @@ def test_full_graph_hashes(hashes, variant):
     heads = O.heads_int8(ir, t)
     for name, v in h["heads"].items():
         assert sha(heads[name][0]) == v, name
+
+
+def test_u8i4_oracle_matches_reference_known_answers(golden_dir):
+    kat = np.load(golden_dir / "u8i4_kat.npz")
+    for i in range(6):
+        assert np.array_equal(O.u8i4_i32(kat[f"a{i}"], kat[f"b{i}_packed"]), kat[f"c{i}"])
