@@ -476,9 +476,12 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.out = seg_dev(d.out, arena, 0);
   } else {
     const unsigned long long plane = (unsigned long long)d.out_h * d.out_w;
-    if (d.egress_image_bytes < plane * d.cout ||
-        d.egress_offset + (unsigned long long)(batch - 1) * d.egress_image_bytes + plane * d.cout > arena_bytes)
+    const int ech = d.egress_channels ? d.egress_channels : d.cout;
+    if (ech < 0 || ech > d.cout || d.cout - ech >= 16) return bad("egress channels must lie in (cout - 16, cout]");
+    if (d.egress_image_bytes < plane * ech ||
+        d.egress_offset + (unsigned long long)(batch - 1) * d.egress_image_bytes + plane * ech > arena_bytes)
       return bad("head egress outside the arena");
+    p.egress_ch = ech;
     p.egress = reinterpret_cast<int8_t*>(arena + d.egress_offset);
     p.egress_img = (long long)d.egress_image_bytes;
   }

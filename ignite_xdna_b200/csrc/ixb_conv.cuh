@@ -100,6 +100,7 @@ struct ConvParams {
   SegDev out;
   int8_t* egress;
   long long egress_img;
+  int egress_ch;  // channels the head writes (the rest of cout are zero-weight padding)
   int cout;
   FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wm, Wm
   int Wm;                             // output row length in M space: Wo, or Wo + 1 for STEM
@@ -439,8 +440,12 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
     const long long plane = (long long)p.Ho * p.Wo;
     const int8_t* ob = reinterpret_cast<const int8_t*>(&o);
     const int c0 = ntile * p.n_tile + jj * 16;
+    if (c0 + 16 <= p.egress_ch) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
+      for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
+    } else {
+      for (int i = 0; c0 + i < p.egress_ch; ++i) e[(c0 + i) * plane] = ob[i];
+    }
   }
 }
 

@@ -3,7 +3,8 @@
 Same contract as the reference's ``src/ignite_xdna/runtime/heads.py`` (``HeadSpec`` :47-76,
 ``DetectHeadLayout`` :79-140, ``HeadStatus`` :143-150): per head a byte offset, a 4-D shape,
 a dequantisation scale and zero point 0; unpacking is zero-copy. Here the layout is produced
-by the engine's own plan (heads back to back in ``HEAD_NAMES`` order per image) and carries a
+by the engine's own plan (heads back to back in the graph's output order per image: the six
+detect heads ``HEAD_NAMES``, then for a pose graph the three keypoint heads) and carries a
 leading batch dimension.
 """
 from __future__ import annotations
@@ -13,7 +14,7 @@ from typing import Dict, Mapping, Optional, Tuple
 
 import numpy as np
 
-from .yolov8 import HEAD_NAMES
+from .yolov8 import HEAD_NAMES  # noqa: F401  (re-exported: the detect heads' names)
 
 
 @dataclass(frozen=True)
@@ -71,7 +72,7 @@ def layout_from_plan(dp) -> DetectHeadLayout:
     ir = dp.ir
     tensor_of = dict(ir.outputs)
     specs = []
-    for name in HEAD_NAMES:
+    for name, _ in ir.outputs:
         t = ir.tensors[tensor_of[name]]
         specs.append(HeadSpec(name, (t.channels, t.height, t.width), dp.head_offsets[name], t.scale, 0))
     return DetectHeadLayout(tuple(specs), dp.egress_image_bytes)

@@ -29,7 +29,6 @@ import numpy as np
 
 from . import _lib as L
 from .graph import ConvLayer, GraphIR, PoolLayer, Segment
-from .yolov8 import HEAD_NAMES
 
 ALIGN = 256
 TILE_M = 128
@@ -118,6 +117,12 @@ def conv_mode(layer: ConvLayer, ir: GraphIR) -> int:
     raise ValueError(f"{layer.name}: no conv mode for k={layer.k} stride={layer.stride}")
 
 
+def pad16(c: int) -> int:
+    """Channels as stored: whole 16-channel chunks (a tensor of 51 or 1 channels keeps zero channels
+    up to its last chunk; its producer has zero weights and bias there, its consumers zero weights)."""
+    return (c + 15) // 16 * 16
+
+
 def choose_n_tile(cout: int) -> int:
     if cout <= 256:
         return cout
@@ -142,10 +147,15 @@ def _core_layout(b: np.ndarray) -> np.ndarray:
     return b.reshape(n // 8, 8, 2, 16).transpose(0, 2, 1, 3).reshape(-1)
 
 
-def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule) -> np.ndarray:
+def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule,
+                 cin_map: Optional[np.ndarray] = None) -> np.ndarray:
     """Weights of every n-tile as the schedule's MMAs' [n_tile][32] K-slices, each in the UMMA
-    core-matrix layout; a slice's two 16-byte K-halves are the (chunk, tap) of the MMA's halves."""
+    core-matrix layout; a slice's two 16-byte K-halves are the (chunk, tap) of the MMA's halves.
+    ``cin_map`` places input channel i at stored channel cin_map[i] (inputs padded to whole chunks);
+    the stored channels it does not name get zero weights."""
     w = layer.weights.astype(np.int8)       # [cout][cin][k][k]
+    if w.shape[0] % n_tile:                 # output channels padded to whole chunks: zero weights
+        w = np.concatenate([w, np.zeros((pad16(w.shape[0]) - w.shape[0],) + w.shape[1:], np.int8)])
     cout, cin, k, _ = w.shape
     nchunks = (cin + 15) // 16
     if mode == L.MODE_STEM:
@@ -161,8 +171,10 @@ def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule) -> np.ndarr
         def piece(chunk, tap):
             return stem[tap]
     else:
-        wp = np.zeros((cout, nchunks * 16, k * k), dtype=np.int8)
-        wp[:, :cin, :] = w.reshape(cout, cin, k * k)
+        if cin_map is None:
+            cin_map = np.arange(cin)
+        wp = np.zeros((cout, (int(cin_map[-1]) + 16) // 16 * 16, k * k), dtype=np.int8)
+        wp[:, cin_map, :] = w.reshape(cout, cin, k * k)
 
         def piece(chunk, tap):
             return wp[:, 16 * chunk:16 * chunk + 16, tap]
@@ -206,6 +218,35 @@ def _storage_groups(ir: GraphIR, heads: set) -> List[List[str]]:
     return groups
 
 
+def _cin_map(ir: GraphIR, layer: ConvLayer) -> np.ndarray:
+    """Stored channel of each of the layer's input channels across its (padded) segments."""
+    parts, base = [], 0
+    for s in layer.inputs:
+        t = ir.tensors[s.tensor]
+        parts.append(base + np.arange(min(s.blocks * 8, t.channels - s.block_offset * 8)))
+        base += _seg_channels(ir, s)
+    m = np.concatenate(parts)
+    if m.size != layer.cin:
+        raise ValueError(f"{layer.name}: segments carry {m.size} channels, weights {layer.cin}")
+    return m
+
+
+def _seg_channels(ir: GraphIR, s: Segment) -> int:
+    """Channels a segment view reads as stored: whole chunks; a view that ends inside a chunk must
+    end at its tensor's last channel (the stored zero channels then complete the chunk)."""
+    if s.tensor == ir.input:
+        return 3
+    t = ir.tensors[s.tensor]
+    if s.block_offset % 2:
+        raise ValueError(f"{s.tensor}: channel view not aligned to 16-channel chunks")
+    real = min(s.blocks * 8, t.channels - s.block_offset * 8)
+    if real % 16:
+        if s.block_offset * 8 + real != t.channels:
+            raise ValueError(f"{s.tensor}: channel view ends inside a 16-channel chunk")
+        real = pad16(real)
+    return real
+
+
 def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePlan:
     """Arena layout, packed constants and kernel descriptors for ``ir`` at up to ``max_batch``
     images; ``pipeline_depth`` staging/egress pairs serve the submitted-run ring."""
@@ -233,20 +274,20 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePl
     for grp in _storage_groups(ir, heads):
         infos = [ir.tensors[t] for t in grp]
         for t in infos:
-            if t.channels % 16:
-                raise ValueError(f"{t.name}: {t.channels} channels is not a multiple of 16")
+            if t.channels % 16 and len(infos) > 1:
+                raise ValueError(f"{t.name}: a concatenated tensor of {t.channels} channels (not whole chunks)")
         h, w = infos[0].height, infos[0].width
         guard = plane_guard(w)
         plane = plane_stride(max_batch, h, w, guard)
-        nch = sum(t.channels for t in infos) // 16
+        nch = sum(pad16(t.channels) for t in infos) // 16
         base = alloc(nch * plane) + guard * 16
         ch = 0
         for t in infos:
-            stores[t.name] = Store(base, plane, ch, t.channels, h, w, guard)
-            ch += t.channels // 16
+            stores[t.name] = Store(base, plane, ch, pad16(t.channels), h, w, guard)
+            ch += pad16(t.channels) // 16
     head_offsets: Dict[str, int] = {}
     eb = 0
-    for name in HEAD_NAMES:
+    for name, _ in ir.outputs:
         t = ir.tensors[head_tensor[name]]
         head_offsets[name] = eb
         eb += t.channels * t.height * t.width
@@ -268,19 +309,23 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePl
     convs: List[ConvPlan] = []
     for layer in ir.conv_layers():
         mode = conv_mode(layer, ir)
-        n_tile = choose_n_tile(layer.cout)
-        cp = choose_cp(mode, layer.k, layer.cin)
+        cin_p = 3 if mode == L.MODE_STEM else sum(_seg_channels(ir, sg) for sg in layer.inputs)
+        cout_p = pad16(layer.cout)
+        n_tile = choose_n_tile(cout_p)
+        cp = choose_cp(mode, layer.k, cin_p)
         shape = L.ConvDesc()
         shape.mode, shape.k, shape.stride, shape.n_tile, shape.cp = mode, layer.k, layer.stride, n_tile, cp
-        shape.cin, shape.cout = layer.cin, layer.cout
+        shape.cin, shape.cout = cin_p, cout_p
         shape.nseg = 1
-        shape.seg[0].channels = layer.cin if mode != L.MODE_STEM else 3
+        shape.seg[0].channels = cin_p
         sched = L.conv_schedule(shape)
-        wp = pack_weights(layer, mode, n_tile, sched)
+        wp = pack_weights(layer, mode, n_tile, sched, None if mode == L.MODE_STEM else _cin_map(ir, layer))
         cpl = ConvPlan(layer, mode, n_tile, cp, wp)
         cpl.schedule = sched
         cpl.w_rel = cput(wp)
-        cpl.bias_rel = cput(layer.bias_int8_domain().astype(np.int32))
+        bias = np.zeros(cout_p, dtype=np.int32)
+        bias[:layer.cout] = layer.bias_int8_domain().astype(np.int32)
+        cpl.bias_rel = cput(bias)
         cpl.lut_rel = cput(layer.lut_t())
         convs.append(cpl)
     ilut_rel = cput(input_lut_t(timg.scale))
@@ -295,9 +340,7 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePl
             st = input_store
             return L.Segment(st.offset, 0, 0, 3, st.height, st.width, 0, 0)
         st = stores[s.tensor]
-        if s.block_offset % 2 or s.blocks % 2:
-            raise ValueError(f"{s.tensor}: channel view not aligned to 16-channel chunks")
-        return L.Segment(st.offset, st.plane_stride, st.chunk_offset + s.block_offset // 2, s.blocks * 8,
+        return L.Segment(st.offset, st.plane_stride, st.chunk_offset + s.block_offset // 2, _seg_channels(ir, s),
                          st.height, st.width, int(s.up2), st.guard)
 
     def whole(name: str) -> L.Segment:
@@ -316,7 +359,8 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePl
         d.k, d.stride = layer.k, layer.stride
         d.in_h, d.in_w = src.height * up, src.width * up
         d.out_h, d.out_w = t_out.height, t_out.width
-        d.cin, d.cout = layer.cin, layer.cout
+        d.cin = sum(_seg_channels(ir, sg) for sg in layer.inputs) if cpl.mode != L.MODE_STEM else 3
+        d.cout = pad16(layer.cout)
         d.n_tile, d.cp = cpl.n_tile, cpl.cp
         segs = _merge_segments([seg_of(s) for s in layer.inputs])
         if len(segs) > L.MAX_SEGS:
@@ -340,6 +384,7 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3) -> DevicePl
             d.out_nchw = 1
             d.egress_offset = egress_offset + head_offsets[name]
             d.egress_image_bytes = egress_image_bytes
+            d.egress_channels = layer.cout
         else:
             d.out = whole(layer.output)
         cpl.desc = d

@@ -24,7 +24,7 @@ import numpy as np
 
 from . import _lib as L
 from .graph import GraphIR
-from .heads import HEAD_NAMES, HeadStatus, layout_from_plan
+from .heads import HeadStatus, layout_from_plan
 from .plan import DevicePlan, build_plan, c_plan
 
 
@@ -96,7 +96,7 @@ class GraphSession:
                                             C.c_void_p(self.arena.data_ptr()), self.plan.arena_bytes, C.byref(h)))
         self._h = h
         self.layout = layout_from_plan(self.plan)
-        self.head_names = HEAD_NAMES
+        self.head_names = tuple(n for n, _ in self.plan.ir.outputs)
         self.in_image_bytes = 3 * self.plan.img_h * self.plan.img_w
         self.out_bytes = self.plan.egress_image_bytes
         self._egress = np.zeros((self.max_batch, self.out_bytes), dtype=np.int8)
@@ -112,7 +112,7 @@ class GraphSession:
     # ------------------------------------------------------------------ status
     @property
     def head_status(self) -> HeadStatus:
-        return HeadStatus(True, f"{len(HEAD_NAMES)} heads in the plan's egress, {self.out_bytes} bytes per image",
+        return HeadStatus(True, f"{len(self.head_names)} heads in the plan's egress, {self.out_bytes} bytes per image",
                           self.layout)
 
     @property
@@ -368,7 +368,7 @@ class GraphSession:
             raw = self.arena[o:o + b * P * 16].cpu().numpy().view(np.int8).reshape(b, st.height + 2, st.width + 2, 16)
             v = raw[:, 1:-1, 1:-1, :].transpose(0, 3, 1, 2)
             out[:, 16 * c:16 * c + 16] = (v.astype(np.int16) + 128).astype(np.uint8)
-        return out
+        return out[:, :self.ir.tensors[name].channels]     # stored zero channels past a ragged tail
 
     def profile(self, batch: int, iters: int = 3):
         """Mean device milliseconds per op (layer-by-layer launches with events)."""
@@ -413,9 +413,13 @@ class InferenceSession:
     @classmethod
     def from_spec(cls, model: str = "yolov8n", seed: int = 0, imgsz: int = 640, device_index: int = 0,
                   max_batch: int = 64, pipeline_depth: int = 3, **kw) -> GraphSession:
-        """Open a session on the seeded synthetic XINT8 graph ``model`` in {yolov8n, yolov8s, yolov8m}."""
+        """Open a session on the seeded synthetic XINT8 graph ``model`` in {yolov8n, yolov8s, yolov8m},
+        or their YOLOv8-pose versions ``yolov8n-pose`` ... (nine heads: one class plus keypoints)."""
         from .yolov8 import build_yolov8
         variant = model.replace("yolov8", "")
+        if variant.endswith("-pose"):
+            variant = variant[:-len("-pose")]
+            kw["task"] = "pose"
         return GraphSession(build_yolov8(variant, imgsz=imgsz, seed=seed, **kw), device_index=device_index,
                             max_batch=max_batch, pipeline_depth=pipeline_depth)
 

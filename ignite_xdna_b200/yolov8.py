@@ -40,6 +40,10 @@ from .graph import ConvLayer, GraphIR, PoolLayer, Segment, TensorInfo
 from .silu import fit_sigmoid
 
 HEAD_NAMES = ("p3_box", "p3_cls", "p4_box", "p4_cls", "p5_box", "p5_cls")
+# YOLOv8-pose keeps the detect heads with one class and adds a keypoint branch (cv4): 17 keypoints x
+# (x, y, visibility) = 51 channels per level (the reference's runtime/heads.py POSE_HEAD_NAMES)
+POSE_HEAD_NAMES = HEAD_NAMES + ("p3_kpt", "p4_kpt", "p5_kpt")
+POSE_KPT_CHANNELS = 51
 VARIANTS = {"n": (0.33, 0.25, 1024), "s": (0.33, 0.50, 1024), "m": (0.67, 0.75, 768)}
 INPUT_POS = 7
 BUILD_VERSION = 1
@@ -55,9 +59,13 @@ class ModelSpec:
     nc: int = 80
     reg_max: int = 16
     bias_std: float = 0.1
+    task: str = "detect"      # or "pose": one class and the keypoint heads
 
     def key(self) -> str:
-        blob = json.dumps({**asdict(self), "v": BUILD_VERSION}, sort_keys=True).encode()
+        d = asdict(self)
+        if d["task"] == "detect":
+            del d["task"]         # detect models keep the keys they had before pose existed
+        blob = json.dumps({**d, "v": BUILD_VERSION}, sort_keys=True).encode()
         return hashlib.sha256(blob).hexdigest()[:16]
 
 
@@ -189,6 +197,12 @@ class _Arch:
             c = self.conv(f"/model.22/cv3.{i}/cv3.{i}.2/Conv", [self.seg(c)], nc, 1, 1, act=False)
             self.g.heads[f"p{i + 3}_box"] = b
             self.g.heads[f"p{i + 3}_cls"] = c
+            if self.spec.task == "pose":
+                ck = max(c2 // 4, POSE_KPT_CHANNELS)
+                k = self.conv(f"/model.22/cv4.{i}/cv4.{i}.0/conv/Conv", [self.seg(feat)], ck, 3, 1)
+                k = self.conv(f"/model.22/cv4.{i}/cv4.{i}.1/conv/Conv", [self.seg(k)], ck, 3, 1)
+                k = self.conv(f"/model.22/cv4.{i}/cv4.{i}.2/Conv", [self.seg(k)], POSE_KPT_CHANNELS, 1, 1, act=False)
+                self.g.heads[f"p{i + 3}_kpt"] = k
         return self.g
 
 
@@ -351,7 +365,7 @@ def _build(spec: ModelSpec) -> GraphIR:
         wq = _quantize_pow2(L.w, p_w)
         bscale = 2.0 ** -(p_in + p_w)
         bq = np.clip(np.rint(L.b.astype(np.float64) / bscale), -(2 ** 31), 2 ** 31 - 1).astype(np.int32)
-        segs = [Segment(t, off // 8, cc // 8 if cc >= 8 else 1, up) for t, off, cc, up in L.src]
+        segs = [Segment(t, off // 8, (cc + 7) // 8, up) for t, off, cc, up in L.src]
         layer = ConvLayer(name=L.name, index=len(layers), inputs=segs, in_scale=2.0 ** -p_in, k=L.k, stride=L.s,
                           pad=L.k // 2, weights=wq, bias_q=bq, bias_scale=bscale, weight_scale=2.0 ** -p_w,
                           conv_scale=2.0 ** -p_pre, output=L.out)
@@ -380,9 +394,10 @@ def _build(spec: ModelSpec) -> GraphIR:
         if acc_bound >= 2 ** 31 or int(np.abs(layer.bias_acc()).max()) >= 2 ** 31:
             raise ValueError(f"{L.name}: accumulator may leave int32")
         layers.append(layer)
-    outputs = [(name, g.heads[name]) for name in HEAD_NAMES]
+    names = POSE_HEAD_NAMES if spec.task == "pose" else HEAD_NAMES
+    outputs = [(name, g.heads[name]) for name in names]
     return GraphIR(tensors=tensors, layers=layers, input="images", outputs=outputs, silu_sigmoid=True,
-                   task="detect", spec={**asdict(spec), "key": spec.key()})
+                   task=spec.task, spec={**asdict(spec), "key": spec.key()})
 
 
 def default_cache_dir() -> Path:
@@ -393,9 +408,13 @@ def default_cache_dir() -> Path:
 
 
 def build_yolov8(variant: str = "n", imgsz: int = 640, seed: int = 0, cache: bool = True, **kw) -> GraphIR:
-    """The quantized synthetic YOLOv8 graph for ``variant`` in {"n", "s", "m"}."""
+    """The quantized synthetic YOLOv8 graph for ``variant`` in {"n", "s", "m"}; ``task="pose"``
+    builds YOLOv8-pose (one class, keypoint heads)."""
+    if kw.get("task") == "pose":
+        kw.setdefault("nc", 1)
     spec = ModelSpec(variant=variant, imgsz=imgsz, seed=seed, **kw)
-    path = default_cache_dir() / f"yolov8{variant}_{imgsz}_{spec.key()}.pkl"
+    tag = "-pose" if spec.task == "pose" else ""
+    path = default_cache_dir() / f"yolov8{variant}{tag}_{imgsz}_{spec.key()}.pkl"
     if cache and path.exists():
         with open(path, "rb") as f:
             return pickle.load(f)

@@ -45,7 +45,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 4
+#define IXB_API_VERSION 5
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -82,7 +82,7 @@ typedef struct ixb_conv_desc {
   int32_t k, stride;   /* 1 or 3; 1 or 2 */
   int32_t in_h, in_w;  /* logical input size (after any up2) */
   int32_t out_h, out_w;
-  int32_t cin, cout;   /* logical channels; cout multiple of 16 */
+  int32_t cin, cout;   /* stored channels (whole 16-channel chunks); cout multiple of 16 */
   int32_t n_tile;      /* output channels per CTA (multiple of 16, <= 256, divides cout) */
   int32_t cp;          /* 32-channel pairs of input per K-block */
   int32_t nseg;
@@ -99,6 +99,10 @@ typedef struct ixb_conv_desc {
   ixb_segment out;     /* destination view (out_nchw == 0) */
   uint64_t egress_offset;       /* arena offset of this head inside image 0's egress */
   uint64_t egress_image_bytes;  /* egress bytes per image */
+  int32_t egress_channels;      /* channels of the head in the egress (<= cout; 0: cout). A head
+                                   whose channel count is not a multiple of 16 computes cout =
+                                   the next multiple with zero weights and writes only these. */
+  int32_t reserved2;
 } ixb_conv_desc;
 
 typedef struct ixb_pool_desc {  /* SPPF: out_k = pool5^k(in), k = 1..3, pad -128 */

@@ -14,6 +14,8 @@ Outputs (all small, committed):
 * ``yolov8n_s96.npz``    the same at 96x96
 * ``graph_hashes.json``  per-tensor sha256 of run_direct at 640x640 for YOLOv8n/s/m (one image
                          each) plus a fingerprint of each synthetic model
+* ``yolov8n_pose_s64.npz`` every tensor of run_direct on a 64x64 YOLOv8n-pose, two images, and
+  ``pose_hashes.json`` its per-tensor sha256 at 640x640 (``--pose`` writes only these two)
 """
 from __future__ import annotations
 
@@ -86,7 +88,7 @@ def to_reference_ir(ir, R):
             layers.append(gi.PoolLayer(L.name, L.index, gi.Segment(L.input.tensor, L.input.block_offset,
                                                                     L.input.blocks), L.output))
     return gi.GraphIR(tensors=tensors, layers=layers, input=ir.input, outputs=list(ir.outputs),
-                      silu_sigmoid=True, task="detect")
+                      silu_sigmoid=True, task=getattr(ir, "task", "detect"))
 
 
 def ref_input(R, ir, pixels):
@@ -152,8 +154,8 @@ def make_kat(R, irs):
     np.savez_compressed(HERE / "kat.npz", **out)
 
 
-def make_small(R, imgsz):
-    ir = build_yolov8("n", imgsz=imgsz)
+def make_small(R, imgsz, task="detect"):
+    ir = build_yolov8("n", imgsz=imgsz, task=task)
     rir = to_reference_ir(ir, R)
     imgs = random_images(2, imgsz, seed=7)
     out = {"images": imgs}
@@ -161,8 +163,23 @@ def make_small(R, imgsz):
         t = R["graph_reference"].run_direct(rir, ref_input(R, ir, im))
         for name, v in t.items():
             out[f"{i}|{name}"] = v
-    np.savez_compressed(HERE / f"yolov8n_s{imgsz}.npz", **out)
+    tag = "_pose" if task == "pose" else ""
+    np.savez_compressed(HERE / f"yolov8n{tag}_s{imgsz}.npz", **out)
     return ir
+
+
+def hash_entry(R, ir):
+    rir = to_reference_ir(ir, R)
+    img = random_images(1, 640, seed=0)[0]
+    t = R["graph_reference"].run_direct(rir, ref_input(R, ir, img))
+    return {
+        "spec": {k: v for k, v in ir.spec.items()},
+        "fingerprint": fingerprint(ir),
+        "image_seed": 0,
+        "tensors": {name: sha(v) for name, v in t.items()},
+        "heads": {hn: sha((t[tn].astype(np.int16) - 128).astype(np.int8)) for hn, tn in ir.outputs},
+        "positions": {n: ti.scale for n, ti in ir.tensors.items()},
+    }
 
 
 def make_hashes(R):
@@ -171,28 +188,31 @@ def make_hashes(R):
     for variant in ("n", "s", "m"):
         ir = build_yolov8(variant, imgsz=640)
         irs.append(ir)
-        rir = to_reference_ir(ir, R)
-        img = random_images(1, 640, seed=0)[0]
-        t = R["graph_reference"].run_direct(rir, ref_input(R, ir, img))
-        res[f"yolov8{variant}"] = {
-            "spec": {k: v for k, v in ir.spec.items()},
-            "fingerprint": fingerprint(ir),
-            "image_seed": 0,
-            "tensors": {name: sha(v) for name, v in t.items()},
-            "heads": {hn: sha((t[tn].astype(np.int16) - 128).astype(np.int8)) for hn, tn in ir.outputs},
-            "positions": {n: ti.scale for n, ti in ir.tensors.items()},
-        }
-        print(f"yolov8{variant}: {len(t)} tensors")
+        res[f"yolov8{variant}"] = hash_entry(R, ir)
+        print(f"yolov8{variant}: {len(res[f'yolov8{variant}']['tensors'])} tensors")
     with open(HERE / "graph_hashes.json", "w") as f:
         json.dump(res, f, indent=1, sort_keys=True)
     return irs
 
 
+def make_pose(R):
+    make_small(R, 64, task="pose")
+    ir = build_yolov8("n", imgsz=640, task="pose")
+    res = {"yolov8n-pose": hash_entry(R, ir)}
+    with open(HERE / "pose_hashes.json", "w") as f:
+        json.dump(res, f, indent=1, sort_keys=True)
+
+
 def main():
     R = load_reference()
+    if "--pose" in sys.argv[1:]:
+        make_pose(R)
+        print("pose fixtures written to", HERE)
+        return
     small = [make_small(R, 64), make_small(R, 96)]
     irs = make_hashes(R)
     make_kat(R, irs + small)
+    make_pose(R)
     print("golden fixtures written to", HERE)
 
 

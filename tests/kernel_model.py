@@ -177,7 +177,8 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                 else:
                     plane = Ho * Wo
                     e = d.egress_offset + img[rr] * d.egress_image_bytes + oy[rr] * Wo + ox[rr]
-                    arena[e + co * plane] = out[rr]
+                    keep = co < (d.egress_channels or d.cout)
+                    arena[e + co[keep] * plane] = out[rr][keep]
 
 
 def run_pool(arena: np.ndarray, pd, batch: int) -> None:

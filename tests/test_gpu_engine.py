@@ -40,6 +40,37 @@ def test_small_graph_every_tensor(imgsz, batch, sms, monkeypatch):
     sess.close()
 
 
+@pytest.mark.parametrize("imgsz,batch,sms", [(64, 2, None), (96, 2, "2")])
+def test_pose_graph_every_tensor(imgsz, batch, sms, monkeypatch):
+    """YOLOv8-pose: one-class heads and 51-channel keypoint convs run on zero-padded 16-channel
+    chunks; every stored tensor and all nine heads equal the oracle."""
+    if sms:
+        monkeypatch.setenv("IXB_SM_COUNT", sms)
+    sess = InferenceSession.from_spec("yolov8n-pose", imgsz=imgsz, max_batch=batch)
+    assert len(sess.head_names) == 9
+    imgs = random_images(batch, imgsz, seed=5 + imgsz)
+    out = sess.run_yolo_monolithic(imgs)
+    for b in range(batch):
+        ref = O.run_image(sess.ir, imgs[b])
+        for name in ref:
+            got = sess.read_tensor(name, batch=batch)[b]
+            assert np.array_equal(got, ref[name]), f"image {b} tensor {name}"
+        assert np.array_equal(out["raw_output"][b], O.egress_int8(sess.ir, ref))
+        assert out["p3_kpt"][b].shape == (51, imgsz // 8, imgsz // 8)
+    sess.close()
+
+
+def test_pose_640_matches_reference_hashes(golden_dir):
+    h = json.loads((golden_dir / "pose_hashes.json").read_text())["yolov8n-pose"]
+    sess = InferenceSession.from_spec("yolov8n-pose", imgsz=640, max_batch=1)
+    out = sess.run_yolo_monolithic(random_images(1, 640, seed=h["image_seed"]))
+    for name, v in h["heads"].items():
+        assert sha(out[name][0]) == v, name
+    for name, v in h["tensors"].items():
+        assert sha(sess.read_tensor(name, batch=1)[0]) == v, name
+    sess.close()
+
+
 def test_yolov8n_640_matches_reference_hashes(hashes):
     h = hashes["yolov8n"]
     sess = InferenceSession.from_spec("yolov8n", imgsz=640, max_batch=2)

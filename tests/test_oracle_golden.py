@@ -78,10 +78,13 @@ def test_int4_packing_matches_reference(kat):
     assert np.array_equal(O.unpack_int4(kat["int4_b_packed"]), kat["int4_b"])
 
 
-@pytest.mark.parametrize("imgsz", [64, 96])
-def test_small_graph_every_tensor(golden_dir, imgsz):
-    z = np.load(golden_dir / f"yolov8n_s{imgsz}.npz")
-    ir = build_yolov8("n", imgsz=imgsz)
+@pytest.mark.parametrize("imgsz,task", [(64, "detect"), (96, "detect"), (64, "pose")])
+def test_small_graph_every_tensor(golden_dir, imgsz, task):
+    """YOLOv8-pose adds one-class heads and 51-channel keypoint branches (channels that are not
+    whole 16-channel chunks)."""
+    tag = "_pose" if task == "pose" else ""
+    z = np.load(golden_dir / f"yolov8n{tag}_s{imgsz}.npz")
+    ir = build_yolov8("n", imgsz=imgsz, task=task)
     for i, im in enumerate(z["images"]):
         t = O.run_image(ir, im)
         names = [k.split("|", 1)[1] for k in z.files if k.startswith(f"{i}|")]
@@ -98,6 +101,19 @@ def test_full_graph_hashes(hashes, variant):
     bad = [n for n, v in h["tensors"].items() if sha(t[n]) != v]
     assert not bad, bad[:5]
     heads = O.heads_int8(ir, t)
+    for name, v in h["heads"].items():
+        assert sha(heads[name][0]) == v, name
+
+
+def test_pose_graph_hashes(golden_dir):
+    h = json.loads((golden_dir / "pose_hashes.json").read_text())["yolov8n-pose"]
+    ir = build_yolov8("n", imgsz=640, task="pose")
+    assert sorted(h["heads"]) == sorted(n for n, _ in ir.outputs)
+    t = O.run_image(ir, random_images(1, 640, seed=h["image_seed"])[0])
+    bad = [n for n, v in h["tensors"].items() if sha(t[n]) != v]
+    assert not bad, bad[:5]
+    heads = O.heads_int8(ir, t)
+    assert [heads[n].shape[1] for n in ("p3_cls", "p3_kpt")] == [1, 51]
     for name, v in h["heads"].items():
         assert sha(heads[name][0]) == v, name
 

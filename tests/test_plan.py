@@ -20,6 +20,24 @@ def test_kernel_model_matches_oracle(imgsz, batch, sms, monkeypatch):
     assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
 
 
+def test_pose_plan_pads_ragged_channels_and_matches_oracle():
+    """One-class heads and 51-channel keypoint branches: storage and output channels round up to
+    whole 16-channel chunks (zero weights and bias), the heads write only their real channels."""
+    ir = build_yolov8("n", imgsz=64, task="pose")
+    dp = build_plan(ir, 2)
+    by_out = {c.layer.output: c.desc for c in dp.convs}
+    kpt = ir.tensors[dict(ir.outputs)["p3_kpt"]]
+    assert kpt.channels == 51 and by_out[kpt.name].cout == 64 and by_out[kpt.name].egress_channels == 51
+    cls = dict(ir.outputs)["p4_cls"]
+    assert by_out[cls].cout == 16 and by_out[cls].egress_channels == 1
+    mid = [c for c in dp.convs if c.layer.cout == 51 and c.layer.output not in dict(ir.outputs).values()]
+    assert mid and all(dp.stores[c.layer.output].channels == 64 for c in mid)
+    assert dp.egress_image_bytes == sum(ir.tensors[t].channels * ir.tensors[t].height * ir.tensors[t].width
+                                        for _, t in ir.outputs)
+    imgs = random_images(2, 64, seed=11)
+    assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
+
+
 def test_input_table_is_reference_lut():
     lut = input_lut_t(2.0 ** -7)
     ref = O.input_lut(2.0 ** -7).astype(np.int16) - 128
