@@ -354,7 +354,7 @@ def run_gpu(args):
     ms_e2e = max_over_ranks(ms_e2e, world, local)
     # per-op device times (layer-by-layer launches with events on the session stream)
     prof = sess.profile(B, iters=max(2, min(args.steps, 5)))
-    conv_ops = [i for i, (k, _) in enumerate(sess.plan.ops) if k == L.OP_CONV]
+    conv_ops = [i for i, (k, _) in enumerate(sess.plan.ops) if (k & 0xFF) == L.OP_CONV]
     conv_ms = sum(prof[i] for i in conv_ops)
     nbytes, nops = conv_algorithmic(sess.ir, B)
     hbm_peak, bf16_peak, peak_kind = load_peaks()

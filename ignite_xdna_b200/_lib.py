@@ -24,6 +24,8 @@ MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH, IN_STORE = 1, 2, 4, 8, 16
 OP_CONV, OP_POOL = 0, 1
+OP_WITH_PREV = 0x100     # a conv that runs concurrently with the op(s) before it (branch group)
+MAX_BRANCHES = 8
 
 
 class Segment(C.Structure):

@@ -239,10 +239,12 @@ struct ConvLaunch {
   dim3 grid;
   int smem;
   int mode, stages, threads;
+  bool pdl = true;  // programmatic dependent launch after the previous kernel of its stream
 };
 
+// sm_budget: the SMs the launch may spread over (a branch group's share), 0 for all of them.
 int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, ConvLaunch& L,
-               std::string& err) {
+               std::string& err, int sm_budget = 0) {
   char buf[256];
   auto bad = [&](const char* m) {
     err = m;
@@ -342,7 +344,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   if (d.lut_offset + 256 > arena_bytes) return bad("activation table outside the arena");
   // Tile of MT blocks of 128 pixels: the largest MT that keeps two accumulators within TMEM
   // (2 * MT * n_tile <= 512 columns) and still leaves two tiles per SM to spread.
-  const int sms = sm_count();
+  const int sms = sm_budget > 0 ? std::min(sm_budget, sm_count()) : sm_count();
   int mt = 1;
   for (int cand : {4, 2}) {
     const long long tiles = (p.m_total + 128LL * cand - 1) / (128LL * cand);
@@ -575,7 +577,7 @@ bool pdl_enabled() {
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st,
+cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, bool pdl,
                              Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -586,7 +588,7 @@ cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, int 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = pdl && pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
@@ -597,7 +599,7 @@ int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
     IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kConvDynSmem));
     configured = true;
   }
-  IXB_CUDA(launch_dependent(conv_kernel<MODE, EW>, L.grid, dim3(conv_threads(MODE, EW)), L.smem, st, L.p));
+  IXB_CUDA(launch_dependent(conv_kernel<MODE, EW>, L.grid, dim3(conv_threads(MODE, EW)), L.smem, st, L.pdl, L.p));
   return 0;
 }
 
@@ -615,8 +617,8 @@ int launch_conv(const ConvLaunch& L, cudaStream_t st) {
 
 // Host checks, then (for im2col modes) the tensor map: everything a launch needs.
 int prepare_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int batch, ConvLaunch& L,
-                 std::string& err) {
-  if (build_conv(d, arena, arena_bytes, batch, L, err)) return -1;
+                 std::string& err, int sm_budget = 0) {
+  if (build_conv(d, arena, arena_bytes, batch, L, err, sm_budget)) return -1;
   if (d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) return encode_im2col(L, d, arena, batch, err);
   return 0;
 }
@@ -668,7 +670,7 @@ int launch_pool(const PoolLaunch& L, cudaStream_t st) {
     IXB_CUDA(cudaFuncSetAttribute(sppf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     configured = true;
   }
-  IXB_CUDA(launch_dependent(sppf_kernel, L.grid, dim3(256), L.smem, st, L.p));
+  IXB_CUDA(launch_dependent(sppf_kernel, L.grid, dim3(256), L.smem, st, true, L.p));
   return 0;
 }
 
@@ -844,6 +846,43 @@ int read_device_error() {
   return 0;
 }
 
+// Arena bytes an access touches: `count` repeats of [start, start + len), `stride` bytes apart.
+struct Span {
+  unsigned long long start, len, stride;
+  int count;
+};
+
+Span view_span(const ixb_segment& s, int batch) {
+  if (!s.plane_stride)  // the stem's image store: one block of 8-byte pixels
+    return {s.offset, (unsigned long long)batch * (s.height + 2) * (s.width + 4) * 8, 0, 1};
+  const unsigned long long chunks = (unsigned long long)(s.channels + 15) / 16;
+  return {s.offset - (unsigned long long)s.guard * 16 + (unsigned long long)s.chunk_offset * s.plane_stride,
+          chunks * s.plane_stride, 0, 1};
+}
+
+bool spans_overlap(const Span& a, const Span& b) {
+  auto end = [](const Span& s) { return s.start + (s.count > 1 ? (s.count - 1) * s.stride : 0) + s.len; };
+  if (a.start >= end(b) || b.start >= end(a)) return false;
+  if (a.count > 1 && b.count > 1 && a.stride == b.stride && a.len <= a.stride && b.len <= b.stride) {
+    // pieces repeating with one period (heads inside the per-image egress): compare within a period
+    const unsigned long long S = a.stride;
+    const unsigned long long d = b.start >= a.start ? (b.start - a.start) % S : (S - (a.start - b.start) % S) % S;
+    return d < a.len || S - d < b.len;
+  }
+  return true;  // conservative
+}
+
+void conv_spans(const ixb_conv_desc& d, int batch, std::vector<Span>& rd, std::vector<Span>& wr) {
+  for (int i = 0; i < d.nseg && i < IXB_MAX_SEGS; ++i) rd.push_back(view_span(d.seg[i], batch));
+  if (d.has_residual) rd.push_back(view_span(d.residual, batch));
+  if (d.out_nchw) {
+    const int ech = d.egress_channels ? d.egress_channels : d.cout;
+    wr.push_back({d.egress_offset, (unsigned long long)d.out_h * d.out_w * ech, d.egress_image_bytes, batch});
+  } else {
+    wr.push_back(view_span(d.out, batch));
+  }
+}
+
 }  // namespace
 
 struct ixb_session {
@@ -857,6 +896,10 @@ struct ixb_session {
   std::vector<ixb_conv_desc> convs;
   std::vector<ixb_pool_desc> pools;
   std::vector<ixb_op> ops;
+  // branch groups: [begin, end) runs of ops joined by IXB_OP_WITH_PREV (a lone op is a group of one)
+  std::vector<std::pair<int, int>> groups;
+  cudaStream_t side[IXB_MAX_BRANCHES - 1] = {};
+  cudaEvent_t ev_fork = nullptr, ev_join[IXB_MAX_BRANCHES - 1] = {};
   // launches and graphs per (batch, slot): key = batch * kSlots + slot
   static constexpr int kSlots = 1 + IXB_MAX_EXTRA_SLOTS;
   std::map<int, std::vector<ConvLaunch>> conv_launch;
@@ -894,9 +937,32 @@ struct ixb_session {
     std::vector<ConvLaunch> cl(convs.size());
     std::vector<PoolLaunch> pl(pools.size());
     std::string err;
-    for (size_t i = 0; i < convs.size(); ++i)
-      if (prepare_conv(convs[i], arena, arena_bytes, batch, cl[i], err))
+    // a branch group splits the SMs between its convs in proportion to their MACs (at least one
+    // CTA per output-channel tile each); the members after the first start from the fork, not PDL
+    std::vector<int> budget(convs.size(), 0);
+    std::vector<char> forked(convs.size(), 0);
+    const int sms = sm_count();
+    for (const auto& g : groups) {
+      if (g.second - g.first < 2) continue;
+      double total = 0.0;
+      std::vector<double> w;
+      for (int i = g.first; i < g.second; ++i) {
+        const ixb_conv_desc& d = convs[ops[i].index];
+        w.push_back((double)d.out_h * d.out_w * d.cin * d.k * d.k * d.cout);
+        total += w.back();
+      }
+      for (int i = g.first; i < g.second; ++i) {
+        const ixb_conv_desc& d = convs[ops[i].index];
+        const int nt = d.n_tile > 0 ? std::max(1, d.cout / d.n_tile) : 1;
+        budget[ops[i].index] = std::max(nt, (int)(sms * w[i - g.first] / std::max(total, 1.0)));
+        forked[ops[i].index] = i > g.first;
+      }
+    }
+    for (size_t i = 0; i < convs.size(); ++i) {
+      if (prepare_conv(convs[i], arena, arena_bytes, batch, cl[i], err, budget[i]))
         return fail(IXB_ERR_INVALID, "conv " + std::to_string(i) + ": " + err);
+      cl[i].pdl = !forked[i];
+    }
     for (size_t i = 0; i < pools.size(); ++i)
       if (build_pool(pools[i], arena, arena_bytes, batch, pl[i], err))
         return fail(IXB_ERR_INVALID, "pool " + std::to_string(i) + ": " + err);
@@ -905,11 +971,12 @@ struct ixb_session {
     return 0;
   }
 
-  int enqueue_op(int batch, int i, int slot = 0) {
+  int enqueue_op(int batch, int i, int slot = 0, cudaStream_t st = nullptr) {
     const ixb_op& op = ops[i];
     const int key = batch * kSlots + slot;
-    if (op.kind == IXB_OP_CONV) return launch_conv(conv_launch[key][op.index], stream);
-    return launch_pool(pool_launch[key][op.index], stream);
+    if (!st) st = stream;
+    if ((op.kind & 0xFF) == IXB_OP_CONV) return launch_conv(conv_launch[key][op.index], st);
+    return launch_pool(pool_launch[key][op.index], st);
   }
 
   int enqueue_ingress(int batch, int slot = 0) {
@@ -921,8 +988,22 @@ struct ixb_session {
   int enqueue(int batch, int slot = 0, bool ingress = true) {
     if (ingress)
       if (int r = enqueue_ingress(batch, slot)) return r;
-    for (size_t i = 0; i < ops.size(); ++i)
-      if (int r = enqueue_op(batch, (int)i, slot)) return r;
+    for (const auto& g : groups) {
+      if (g.second - g.first == 1) {
+        if (int r = enqueue_op(batch, g.first, slot)) return r;
+        continue;
+      }
+      // fork: members after the first run on side streams, then the compute stream joins them all
+      const int n = g.second - g.first;
+      IXB_CUDA(cudaEventRecord(ev_fork, stream));
+      for (int k = 1; k < n; ++k) IXB_CUDA(cudaStreamWaitEvent(side[k - 1], ev_fork, 0));
+      if (int r = enqueue_op(batch, g.first, slot)) return r;
+      for (int k = 1; k < n; ++k) {
+        if (int r = enqueue_op(batch, g.first + k, slot, side[k - 1])) return r;
+        IXB_CUDA(cudaEventRecord(ev_join[k - 1], side[k - 1]));
+      }
+      for (int k = 1; k < n; ++k) IXB_CUDA(cudaStreamWaitEvent(stream, ev_join[k - 1], 0));
+    }
     return 0;
   }
 
@@ -998,8 +1079,7 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
   if (plan->api_version != IXB_API_VERSION) return fail(IXB_ERR_INVALID, "plan api_version mismatch");
   if (plan->max_batch < 1 || plan->n_ops < 1 || plan->n_convs < 1) return fail(IXB_ERR_INVALID, "empty plan");
   if (plan->arena_bytes > arena_bytes && arena) return fail(IXB_ERR_INVALID, "arena smaller than the plan");
-  IXB_CUDA(cudaSetDevice(device));
-  auto* s = new ixb_session();
+  auto* s = new ixb_session();  // the op list and branch groups are checked before any CUDA call
   s->device = device;
   s->plan = *plan;
   s->convs.assign(plan->convs, plan->convs + plan->n_convs);
@@ -1008,13 +1088,52 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
   s->plan.convs = nullptr;
   s->plan.pools = nullptr;
   s->plan.ops = nullptr;
-  for (const ixb_op& op : s->ops) {
-    if ((op.kind == IXB_OP_CONV && (op.index < 0 || op.index >= plan->n_convs)) ||
-        (op.kind == IXB_OP_POOL && (op.index < 0 || op.index >= plan->n_pools)) ||
-        (op.kind != IXB_OP_CONV && op.kind != IXB_OP_POOL)) {
+  for (size_t i = 0; i < s->ops.size(); ++i) {
+    const ixb_op& op = s->ops[i];
+    const int kind = op.kind & 0xFF;
+    const bool with_prev = (op.kind & IXB_OP_WITH_PREV) != 0;
+    if ((kind == IXB_OP_CONV && (op.index < 0 || op.index >= plan->n_convs)) ||
+        (kind == IXB_OP_POOL && (op.index < 0 || op.index >= plan->n_pools)) ||
+        (kind != IXB_OP_CONV && kind != IXB_OP_POOL) || (op.kind & ~(0xFF | IXB_OP_WITH_PREV))) {
       delete s;
       return fail(IXB_ERR_INVALID, "op list names a missing layer");
     }
+    if (!with_prev) {
+      s->groups.push_back({(int)i, (int)i + 1});
+      continue;
+    }
+    if (i == 0 || kind != IXB_OP_CONV || (s->ops[i - 1].kind & 0xFF) != IXB_OP_CONV ||
+        s->groups.back().second - s->groups.back().first >= IXB_MAX_BRANCHES) {
+      delete s;
+      return fail(IXB_ERR_INVALID, "IXB_OP_WITH_PREV joins convs only, at most IXB_MAX_BRANCHES per group");
+    }
+    s->groups.back().second = (int)i + 1;
+  }
+  // no member of a branch group may read or write what another member writes
+  for (const auto& g : s->groups) {
+    if (g.second - g.first < 2) continue;
+    const int n = g.second - g.first;
+    std::vector<std::vector<Span>> rd(n), wr(n);
+    for (int k = 0; k < n; ++k) conv_spans(s->convs[s->ops[g.first + k].index], plan->max_batch, rd[k], wr[k]);
+    for (int x = 0; x < n; ++x)
+      for (int y = 0; y < n; ++y) {
+        if (x == y) continue;
+        bool hit = false;
+        for (const Span& w : wr[x]) {
+          for (const Span& r : rd[y]) hit = hit || spans_overlap(w, r);
+          for (const Span& w2 : wr[y]) hit = hit || spans_overlap(w, w2);
+        }
+        if (hit) {
+          const int op = g.first + std::max(x, y);
+          delete s;
+          return fail(IXB_ERR_INVALID, "branch group at op " + std::to_string(op) +
+                                           ": a member reads or writes what another member writes");
+        }
+      }
+  }
+  if (cudaError_t e = cudaSetDevice(device)) {
+    delete s;
+    return cuda_fail(e, "cudaSetDevice");
   }
   s->arena_bytes = arena ? arena_bytes : plan->arena_bytes;
   if (arena) {
@@ -1060,6 +1179,11 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
   if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
   if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->ev_done, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->ev_fork, cudaEventDisableTiming);
+  for (int k = 0; k < IXB_MAX_BRANCHES - 1; ++k) {
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->side[k], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->ev_join[k], cudaEventDisableTiming);
+  }
   for (auto& sl : s->slots) {
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.h2d_done, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreate(&sl.t0);
@@ -1090,6 +1214,12 @@ int ixb_session_destroy(ixb_session* s) {
   if (s->ev0) cudaEventDestroy(s->ev0);
   if (s->ev1) cudaEventDestroy(s->ev1);
   if (s->ev_done) cudaEventDestroy(s->ev_done);
+  for (int k = 0; k < IXB_MAX_BRANCHES - 1; ++k) {
+    if (s->side[k]) cudaStreamSynchronize(s->side[k]);
+    if (s->side[k]) cudaStreamDestroy(s->side[k]);
+    if (s->ev_join[k]) cudaEventDestroy(s->ev_join[k]);
+  }
+  if (s->ev_fork) cudaEventDestroy(s->ev_fork);
   if (s->stream) cudaStreamDestroy(s->stream);
   if (s->own_arena && s->arena) cudaFree(s->arena);
   delete s;

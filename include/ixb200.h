@@ -112,6 +112,15 @@ typedef struct ixb_pool_desc {  /* SPPF: out_k = pool5^k(in), k = 1..3, pad -128
 
 #define IXB_OP_CONV 0
 #define IXB_OP_POOL 1
+/* Flag or'ed into a conv op's kind: the conv runs concurrently with the op(s) before it in its
+ * branch group (a run of ops joined by this flag, at most IXB_MAX_BRANCHES). No member of a group
+ * may read or write what another member writes; session creation checks this on the arena views.
+ * The group's members run on separate streams (forked from and joined back into the compute
+ * stream, inside the CUDA graph) with the SMs split between them in proportion to their MACs, so
+ * small latency-bound convs at 40x40 and 20x20 overlap the large ones instead of each holding
+ * the whole GPU for a few microseconds. */
+#define IXB_OP_WITH_PREV 0x100
+#define IXB_MAX_BRANCHES 8
 typedef struct ixb_op { int32_t kind, index; } ixb_op;
 
 #define IXB_MAX_EXTRA_SLOTS 3

@@ -218,7 +218,7 @@ def run_network(dp: DevicePlan, images: np.ndarray) -> np.ndarray:
         v[1:-1, 1:s.width + 1, :3] = lut[images[b].transpose(1, 2, 0)]
     convs = [c.desc for c in dp.convs]
     for kind, idx in dp.ops:
-        if kind == L.OP_CONV:
+        if (kind & 0xFF) == L.OP_CONV:
             run_conv(arena, convs[idx], batch, dp.arena_bytes)
         else:
             run_pool(arena, dp.pools[idx][1], batch)

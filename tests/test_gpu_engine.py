@@ -71,6 +71,28 @@ def test_pose_640_matches_reference_hashes(golden_dir):
     sess.close()
 
 
+@pytest.mark.parametrize("model", ["yolov8n", "yolov8n-pose"])
+def test_branch_groups_equal_the_serial_order(model, monkeypatch):
+    """Independent convs of a dependency level run concurrently on forked streams; the result
+    equals the graph's own serial order, tensor for tensor (the eager, graph-less fork/join is
+    covered by test_graph_replay_equals_layer_by_layer_launches)."""
+    imgs = random_images(4, 320, seed=77)
+    outs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("IXB_BRANCHES", flag)
+        sess = InferenceSession.from_spec(model, imgsz=320, max_batch=4)
+        assert any(k & L.OP_WITH_PREV for k, _ in sess.plan.ops) == (flag == "1")
+        out = sess.run_yolo_monolithic(imgs)["raw_output"].copy()
+        tensors = {n: sess.read_tensor(n, batch=4) for n in list(sess.ir.tensors)[-20:]}
+        outs[flag] = (out, tensors)
+        sess.close()
+    assert np.array_equal(outs["1"][0], outs["0"][0])
+    for n in outs["0"][1]:
+        assert np.array_equal(outs["1"][1][n], outs["0"][1][n]), n
+    ref = O.run_batch_egress(build_yolov8("n", imgsz=320, task="pose" if "pose" in model else "detect"), imgs[:1])
+    assert np.array_equal(outs["1"][0][:1], ref)
+
+
 def test_yolov8n_640_matches_reference_hashes(hashes):
     h = hashes["yolov8n"]
     sess = InferenceSession.from_spec("yolov8n", imgsz=640, max_batch=2)

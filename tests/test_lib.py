@@ -72,6 +72,42 @@ def test_batch_beyond_plan_is_refused():
     assert rc == -1 and any(w in lib.ixb_last_error().decode() for w in ("arena", "overlap", "pixel"))
 
 
+def _create(dp, ops):
+    """ixb_session_create on the plan with ``ops`` as its op list (no arena: validation only)."""
+    from ignite_xdna_b200.plan import c_plan
+    p = c_plan(dp)
+    arr = (L.Op * len(ops))(*[L.Op(k, i) for k, i in ops])
+    p.ops, p.n_ops = arr, len(ops)
+    lib = L.load()
+    h = C.c_void_p()
+    rc = lib.ixb_session_create(C.byref(p), 0, None, 0, C.byref(h))
+    if rc == 0:
+        lib.ixb_session_destroy(h)
+    return rc, lib.ixb_last_error().decode()
+
+
+def test_branch_groups_pass_the_hazard_check():
+    """The planner's branch groups are accepted: session creation gets past the op checks (to the
+    first CUDA call, on a machine without a GPU)."""
+    dp = build_plan(build_yolov8("n", imgsz=64), 2, branches=True)
+    assert any(k & L.OP_WITH_PREV for k, _ in dp.ops)
+    rc, msg = _create(dp, dp.ops)
+    assert rc == 0 or "branch group" not in msg and "op list" not in msg
+
+
+def test_branch_group_with_a_dependency_is_refused():
+    dp, _ = _desc()
+    ops = [(k & 0xFF, i) for k, i in dp.ops]
+    # a conv joined to its own producer: reads what the other member writes
+    j = next(n for n in range(1, len(ops)) if ops[n][0] == L.OP_CONV and ops[n - 1][0] == L.OP_CONV)
+    ops[j] = (ops[j][0] | L.OP_WITH_PREV, ops[j][1])
+    rc, msg = _create(dp, ops)
+    assert rc == L.IXB_ERR_INVALID and "branch group" in msg
+    ops = [(k & 0xFF, i) for k, i in dp.ops]
+    ops[0] = (ops[0][0] | L.OP_WITH_PREV, ops[0][1])
+    assert _create(dp, ops)[0] == L.IXB_ERR_INVALID
+
+
 def test_gemm_plan_fits_the_hardware():
     import ctypes as C
     lib = L.load()

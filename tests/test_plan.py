@@ -38,6 +38,42 @@ def test_pose_plan_pads_ragged_channels_and_matches_oracle():
     assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
 
 
+@pytest.mark.parametrize("task", ["detect", "pose"])
+def test_branch_schedule_is_a_valid_order(task):
+    """Every op once; each op after all producers of what it reads; the members of a branch group
+    neither read nor write each other's outputs; without branches the order is the graph's."""
+    ir = build_yolov8("n", imgsz=64, task=task)
+    dp = build_plan(ir, 2, branches=True)
+    plain = build_plan(ir, 2, branches=False)
+    assert sorted((k & 0xFF, i) for k, i in dp.ops) == sorted(plain.ops)
+    assert not any(k & L.OP_WITH_PREV for k, _ in plain.ops)
+
+    def rw(k, i):
+        if (k & 0xFF) == L.OP_CONV:
+            layer = dp.convs[i].layer
+            r = {s.tensor for s in layer.inputs} | ({layer.residual.tensor} if layer.residual else set())
+            return r, {layer.output}
+        chain = dp.pools[i][0]
+        return {chain[0].input.tensor}, {p.output for p in chain}
+    groups = []
+    for k, i in dp.ops:
+        if k & L.OP_WITH_PREV:
+            groups[-1].append((k, i))
+        else:
+            groups.append([(k, i)])
+    written = {ir.input}
+    for g in groups:
+        # every member reads only what earlier groups wrote (so nothing of its own group)
+        for k, i in g:
+            assert rw(k, i)[0] <= written
+        written |= set().union(*[rw(k, i)[1] for k, i in g])
+    sizes, run = [], 0
+    for k, _ in dp.ops:
+        run = run + 1 if k & L.OP_WITH_PREV else 1
+        sizes.append(run)
+    assert max(sizes) >= 2 and max(sizes) <= L.MAX_BRANCHES
+
+
 def test_input_table_is_reference_lut():
     lut = input_lut_t(2.0 ** -7)
     ref = O.input_lut(2.0 ** -7).astype(np.int16) - 128
