@@ -92,6 +92,7 @@ _SIGS = {
     "ixb_session_last_ms": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     "ixb_session_launches": (C.c_int, [C.c_void_p, C.c_int]),
     "ixb_session_profile": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_float)]),
+    "ixb_session_trace": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_uint64)]),
     "ixb_conv_layer": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p]),
     "ixb_conv_layer_stats": (C.c_int, [C.POINTER(ConvDesc), C.c_void_p, C.c_uint64, C.c_int, C.c_void_p,
                                        C.c_void_p, C.c_int64]),

@@ -1349,6 +1349,53 @@ int ixb_session_last_ms(ixb_session* s, float* ms) {
   return 0;
 }
 
+int ixb_session_trace(ixb_session* s, int batch, int iters, uint64_t* ns) {
+  if (!s || !ns || iters < 1) return fail(IXB_ERR_INVALID, "bad trace arguments");
+  if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
+  if (s->pending) return fail(IXB_ERR_INVALID, "a run is pending");
+  if (s->any_busy()) return fail(IXB_ERR_INVALID, "submitted runs are still in flight");
+  IXB_CUDA(cudaSetDevice(s->device));
+  if (int r = s->prepare(batch)) return r;
+  const size_t n = s->ops.size();
+  const int key = batch * ixb_session::kSlots;
+  unsigned long long* buf = nullptr;
+  IXB_CUDA(cudaMalloc(&buf, n * 3 * sizeof(unsigned long long)));
+  std::vector<unsigned long long> init(n * 3);
+  for (size_t i = 0; i < n; ++i) {
+    init[3 * i] = init[3 * i + 1] = ~0ull;
+    init[3 * i + 2] = 0;
+  }
+  // a traced copy of the launches, captured into its own graph (the session's graphs stay as they are)
+  std::vector<ConvLaunch> traced = s->conv_launch[key];
+  for (size_t i = 0; i < n; ++i)
+    if ((s->ops[i].kind & 0xFF) == IXB_OP_CONV) traced[s->ops[i].index].p.trace = buf + 3 * i;
+  std::swap(s->conv_launch[key], traced);
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int rc = 0;
+  cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    rc = s->enqueue(batch, 0, true);
+    e = cudaStreamEndCapture(s->stream, &g);
+  }
+  std::swap(s->conv_launch[key], traced);
+  if (!rc && e == cudaSuccess) e = cudaGraphInstantiate(&exec, g, 0);
+  if (g) cudaGraphDestroy(g);
+  for (int it = 0; it < iters && !rc && e == cudaSuccess; ++it) {
+    e = cudaMemcpyAsync(buf, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  }
+  if (!rc && e == cudaSuccess)
+    e = cudaMemcpy(init.data(), buf, init.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  if (exec) cudaGraphExecDestroy(exec);
+  cudaFree(buf);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "trace run");
+  for (size_t i = 0; i < n * 3; ++i) ns[i] = (init[i] == ~0ull) ? 0 : init[i];
+  return read_device_error();
+}
+
 int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms) {
   if (!s || !ms || iters < 1) return fail(IXB_ERR_INVALID, "bad profile arguments");
   if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");

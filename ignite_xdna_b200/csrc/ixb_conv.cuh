@@ -105,6 +105,7 @@ struct ConvParams {
   FastDiv fd_P, fd_W2, fd_hw, fd_Wo;  // padded pixels per image, padded width, Ho*Wm, Wm
   int Wm;                             // output row length in M space: Wo, or Wo + 1 for STEM
   unsigned long long* stats;          // optional per-CTA role counters (kStatWords per CTA), or null
+  unsigned long long* trace;          // optional launch timeline (globaltimer ns), or null: see trace_mark
   KBlockDev kb[kMaxKBlocks];          // the K schedule
   uint32_t op_a[kMaxOps];             // per MMA: A start (16-byte units from the stage) | LBO (16-byte units) << 16
   uint16_t op_b[kMaxOps];             // per MMA: B start (16-byte units from the K-block's weights)
@@ -157,6 +158,16 @@ __device__ __forceinline__ void tma_im2col(void* dst, const CUtensorMap* tm, int
       "[%6], {%7, %8};" ::"r"(smem_u32(dst)),
       "l"(tm), "r"(0), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"((uint16_t)off_w), "h"((uint16_t)off_h)
       : "memory");
+}
+
+// Launch timeline, when ConvParams::trace is set: word 0 = earliest CTA start, word 1 = earliest
+// time a CTA's producer was past the wait for the previous kernel (its inputs were ready),
+// word 2 = latest CTA end. Words 0 and 1 start at ~0, word 2 at 0.
+__device__ __forceinline__ void trace_mark(unsigned long long* tr, int word) {
+  if (!tr) return;
+  const unsigned long long t = global_ns();
+  if (word < 2) atomicMin(tr + word, t);
+  else atomicMax(tr + word, t);
 }
 
 __device__ __forceinline__ void write_stats(const ConvParams& p, int idx, unsigned long long v) {
@@ -527,6 +538,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   const int KB = p.kblocks;
   const long long t_start = clock64();
   grid_dep_launch();
+  if (tid == 0) trace_mark(p.trace, 0);
 
   if (warp == 0) {
     tmem_alloc(tmem_slot, p.tmem_cols);
@@ -574,6 +586,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
         bulk_g2s(smem + p.kb[kb].b_off, p.wpack + ntile * p.w_ntile_stride + p.kb[kb].b_off, p.kb[kb].b_bytes, bres_bar);
     }
     grid_dep_wait();  // activations of the previous layer from here on
+    if (ptid == 0) trace_mark(p.trace, 1);
     if (MODE == IXB_MODE_GATHER) {
       produce_gather(p, smem, full, empty, ntile, ptid);
     } else if (ptid == 0) {
@@ -616,6 +629,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, p.tmem_cols);
   if (tid == 0) write_stats(p, kStatTotal, clock64() - t_start);
+  if (tid == 0) trace_mark(p.trace, 2);
 }
 
 }  // namespace ixb

@@ -370,6 +370,17 @@ class GraphSession:
             out[:, 16 * c:16 * c + 16] = (v.astype(np.int16) + 128).astype(np.uint8)
         return out[:, :self.ir.tensors[name].channels]     # stored zero channels past a ragged tail
 
+    def trace(self, batch: int, iters: int = 3):
+        """Device timeline of a graph run: per op (start, inputs ready, end) in microseconds from the
+        first op's start, as the ops execute in the graph (pool ops: None)."""
+        self._drain()
+        n = len(self.plan.ops)
+        ns = (C.c_uint64 * (3 * n))()
+        L.check(self.lib.ixb_session_trace(self._h, int(batch), int(iters), ns))
+        v = np.array(ns[:], dtype=np.int64).reshape(n, 3)
+        t0 = v[v[:, 0] > 0, 0].min()
+        return [None if r[0] == 0 else tuple((r - t0) / 1000.0) for r in v]
+
     def profile(self, batch: int, iters: int = 3):
         """Mean device milliseconds per op (layer-by-layer launches with events)."""
         self._drain()

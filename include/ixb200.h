@@ -184,6 +184,12 @@ int ixb_session_launches(ixb_session* s, int batch);
 /* Runs the network `iters` times layer by layer with an event pair around each launch;
  * writes the mean milliseconds of op i to ms[i] (n_ops entries). */
 int ixb_session_profile(ixb_session* s, int batch, int iters, float* ms);
+/* Device timeline of one run as it executes in the graph (programmatic dependent launches and
+ * branch groups included): runs a copy of the run's graph whose conv launches mark the global
+ * timer, `iters` times, and writes for op i of the last run ns[3i..3i+2] = {earliest CTA start,
+ * earliest time its inputs were ready (past the wait for the previous kernel), latest CTA end}
+ * in globaltimer nanoseconds (n_ops * 3 entries; 0 for pool ops, which do not mark). */
+int ixb_session_trace(ixb_session* s, int batch, int iters, uint64_t* ns);
 
 /* One layer on caller-owned device memory: arena is the base every offset refers to. */
 int ixb_conv_layer(const ixb_conv_desc* d, void* arena, uint64_t arena_bytes, int batch, void* stream);

@@ -175,6 +175,15 @@ def test_profile_reports_every_op():
     ms = sess.profile(2, iters=2)
     assert len(ms) == len(sess.plan.ops) and all(v > 0 for v in ms)
     assert sess.launches(2) == 1 + len(sess.plan.ops)
+    tr = sess.trace(2, iters=2)
+    conv = [t for t in tr if t is not None]
+    assert len(conv) == len(sess.plan.convs)
+    assert all(0 <= s <= r <= e for s, r, e in conv)
+    ends = [e for _, _, e in conv]
+    assert all(b >= a for a, b in zip(ends, ends[1:]))   # serial order: each op ends after the last
+    assert ends[-1] < 10_000                               # the whole run within 10 ms
+    a = sess.run(random_images(2, 128, seed=5))            # the session's own graph is untouched
+    assert np.array_equal(a, O.run_batch_egress(sess.ir, random_images(2, 128, seed=5)))
     sess.close()
 
 
