@@ -301,8 +301,8 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
 }
 
 // ---------------------------------------------------------------- MMA issuer
-// The accumulators start at zero (the epilogue clears each one after draining it, and the kernel
-// clears both at start), so every MMA accumulates and a K-block's MMAs can be issued by several
+// The accumulators start at the bias (the epilogue resets each one after draining it, and the
+// kernel sets both at start), so every MMA accumulates and a K-block's MMAs can be issued by several
 // threads in any order: issuer `who` of p.issuers takes the K-block's ops o with
 // (o - op0) % issuers == who, for every 128-row block of the tile. One warp issues an MMA only
 // every ~100 cycles; the tensor core takes one every ~40-64, so several issuing warps keep it fed.
@@ -370,23 +370,21 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
 }
 
 // ---------------------------------------------------------------- epilogue
-// 16 accumulators of one row -> 16 int8 outputs: bias, RNE shift, int8 clamp, table, residual.
+// 16 accumulators of one row (bias included) -> 16 int8 outputs: RNE shift, int8 clamp, table,
+// residual.
 // `lut` points at entry 128 of the 256-byte table (static shared memory), so it is indexed by the
 // clamped value directly; the bytes are gathered into words with byte permutes.
 template <bool RES>
-__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const int4* bias4, const uint8_t* lut, int s,
-                                            int hs, int lsb, const ConvParams& p, int rs, int rhs, int rlsb,
-                                            uint4 r4) {
+__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, int s, int hs, int lsb,
+                                            const ConvParams& p, int rs, int rhs, int rlsb, uint4 r4) {
   uint32_t t[16];
   const int8_t* rv = reinterpret_cast<const int8_t*>(&r4);
 #pragma unroll
   for (int q4 = 0; q4 < 4; ++q4) {
-    const int4 b4 = bias4[q4];
-    const int bb[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int i = 4 * q4 + e;
-      const int a = (int)v[i] + bb[e];
+      const int a = (int)v[i];  // the accumulator started at the bias
       const int r1 = (a + hs + ((a >> s) & lsb)) >> s;   // round half to even, exact for s in [0, 16]
       uint32_t u = lut[clamp_i8(r1)];
       if (RES) {
@@ -433,16 +431,15 @@ __device__ __forceinline__ RowInfo decode_row(const ConvParams& p, int m) {
 }
 
 __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
-                                            const int4* bias4_s, const uint8_t* lut_s, int s, int hs, int lsb, int rs,
-                                            int rhs, int rlsb) {
+                                            const uint8_t* lut_s, int s, int hs, int lsb, int rs, int rhs, int rlsb) {
   const int nj = p.n_tile / 16;
   const int oc = ntile * nj + jj;  // output chunk
   uint4 o;
   if (p.has_res) {
     const uint4 r4 = *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)r.opix * 16);
-    o = epilogue16<true>(v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
+    o = epilogue16<true>(v, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
   } else {
-    o = epilogue16<false>(v, bias4_s + jj * 4, lut_s, s, hs, lsb, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
+    o = epilogue16<false>(v, lut_s, s, hs, lsb, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
   }
   if (!p.out_nchw) {
     *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
@@ -463,13 +460,15 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 // Drain one accumulator: warp w reads TMEM lane quarter w % 4. The tile's units (128-row block,
 // 16-column chunk), in block-major order, are split into one contiguous share per warpgroup, so a
 // thread decodes its row once per block; it issues the TMEM loads of two units before one wait
-// so their latencies overlap. With K split over P issuers a unit is the sum of P partial
-// accumulators.
+// so their latencies overlap. Which warpgroup takes which share rotates with the CTA's tile count
+// `it`: when the units do not divide evenly (4 units over 3 warpgroups), each warpgroup takes the
+// larger share in turn instead of one always lagging. A drained unit is set back to the bias, the
+// value the next tile's accumulation starts from.
 template <int MODE, int EW>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
-                                                   int lane, const uint8_t* lut_s, const int4* bias4_s) {
+                                                   int lane, const uint8_t* lut_s, const int4* bias4_s, int it) {
   constexpr int NG = EW / 4;
-  const int q = warp & 3, g = warp >> 2;
+  const int q = warp & 3, g = ((warp >> 2) + it) % NG;
   const int nj = p.n_tile >> 4;
   const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
@@ -499,22 +498,22 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
       decoded_b = b;
     }
     tmem_ld_wait();
-    // clear the drained columns for the next tile's MMAs, which all accumulate
-    tmem_zero16(c1);
-    if (two) tmem_zero16(c2);
-    if (r.valid) store_piece(p, r, ntile, j, v, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
+    tmem_fill16(c1, bias4_s + j * 4);
+    if (two) tmem_fill16(c2, bias4_s + j2 * 4);
+    if (r.valid) store_piece(p, r, ntile, j, v, lut_s, s, hs, lsb, rs, rhs, rlsb);
     if (two) {
       if (b2 != decoded_b) {
         r = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
         decoded_b = b2;
       }
-      if (r.valid) store_piece(p, r, ntile, j2, w, bias4_s, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      if (r.valid) store_piece(p, r, ntile, j2, w, lut_s, s, hs, lsb, rs, rhs, rlsb);
     }
     u += 2;
     b = two && j2 + 1 == nj ? b2 + 1 : b2;
     j = two ? (j2 + 1 == nj ? 0 : j2 + 1) : j2;
   }
-  tmem_st_wait();  // the zeros are in TMEM before the accumulator is handed back
+  tmem_st_wait();  // the biases are in TMEM before the accumulator is handed back
 }
 
 template <int MODE, int EW>
@@ -567,9 +566,10 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp < EPI) {
-    // both accumulators start at zero: every MMA accumulates (see issue_mma)
+    // both accumulators start at the bias: every MMA accumulates (see issue_mma)
     const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
-    for (int c = (warp >> 2) * 16; c < 2 * p.acc_cols; c += (EPI / 4) * 16) tmem_zero16(tmem + lanes + (uint32_t)c);
+    for (int c = (warp >> 2) * 16; c < 2 * p.acc_cols; c += (EPI / 4) * 16)
+      tmem_fill16(tmem + lanes + (uint32_t)c, bias4_s + ((c % p.n_tile) >> 4) * 4);
     tmem_st_wait();
   }
   tc_fence_before();
@@ -610,7 +610,8 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
       const long long c1 = clock64();
       ew += c1 - c0;
       tc_fence_after();
-      conv_epilogue_tile<MODE, EW>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s);
+      conv_epilogue_tile<MODE, EW>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s,
+                                   tiles);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       ek += clock64() - c1;

@@ -194,6 +194,16 @@ __device__ __forceinline__ void tmem_zero16(uint32_t taddr) {
       "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(0u)
       : "memory");
 }
+// 16 columns of this warp's 32 TMEM lanes set to b[0..15] (the same 16 values in every lane).
+__device__ __forceinline__ void tmem_fill16(uint32_t taddr, const int4* b) {
+  const int4 a0 = b[0], a1 = b[1], a2 = b[2], a3 = b[3];
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(a0.x), "r"(a0.y), "r"(a0.z), "r"(a0.w), "r"(a1.x), "r"(a1.y), "r"(a1.z), "r"(a1.w), "r"(a2.x), "r"(a2.y),
+      "r"(a2.z), "r"(a2.w), "r"(a3.x), "r"(a3.y), "r"(a3.z), "r"(a3.w)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- integer helpers
