@@ -430,13 +430,20 @@ __device__ __forceinline__ RowInfo decode_row(const ConvParams& p, int m) {
   return r;
 }
 
+// The residual's 16 bytes for (row, output chunk of n-tile `ntile`, chunk jj), loaded ahead of use.
+__device__ __forceinline__ uint4 residual_load(const ConvParams& p, const RowInfo& r, int ntile, int jj) {
+  if (!p.has_res || !r.valid) return make_uint4(0, 0, 0, 0);
+  const int oc = ntile * (p.n_tile >> 4) + jj;
+  return *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)r.opix * 16);
+}
+
 __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
-                                            const uint8_t* lut_s, int s, int hs, int lsb, int rs, int rhs, int rlsb) {
+                                            uint4 r4, const uint8_t* lut_s, int s, int hs, int lsb, int rs, int rhs,
+                                            int rlsb) {
   const int nj = p.n_tile / 16;
   const int oc = ntile * nj + jj;  // output chunk
   uint4 o;
   if (p.has_res) {
-    const uint4 r4 = *reinterpret_cast<const uint4*>(p.res.base + (long long)oc * p.res.plane + (long long)r.opix * 16);
     o = epilogue16<true>(v, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
   } else {
     o = epilogue16<false>(v, lut_s, s, hs, lsb, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
@@ -452,17 +459,19 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 #pragma unroll
       for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
     } else {
-      for (int i = 0; c0 + i < p.egress_ch; ++i) e[(c0 + i) * plane] = ob[i];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (c0 + i < p.egress_ch) e[(c0 + i) * plane] = ob[i];
     }
   }
 }
 
 // Drain one accumulator: warp w reads TMEM lane quarter w % 4. The tile's units (128-row block,
 // 16-column chunk), in block-major order, are split into one contiguous share per warpgroup, so a
-// thread decodes its row once per block; it issues the TMEM loads of two units before one wait
-// so their latencies overlap. Which warpgroup takes which share rotates with the CTA's tile count
-// `it`: when the units do not divide evenly (4 units over 3 warpgroups), each warpgroup takes the
-// larger share in turn instead of one always lagging. A drained unit is set back to the bias, the
+// thread decodes its row once per block; it issues the TMEM loads (and residual loads) of two
+// units before one wait so their latencies overlap. Which warpgroup takes which share rotates with
+// the CTA's tile count `it`: when the units do not divide evenly (4 units over 3 warpgroups), each
+// warpgroup takes the larger share in turn instead of one always lagging. A drained unit is set back to the bias, the
 // value the next tile's accumulation starts from.
 template <int MODE, int EW>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
@@ -497,17 +506,21 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
       r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
       decoded_b = b;
     }
+    const RowInfo r1 = r;
+    RowInfo r2 = r;
+    if (two && b2 != b) r2 = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
+    // residual loads in flight together with the TMEM loads
+    const uint4 x1 = residual_load(p, r1, ntile, j);
+    const uint4 x2 = two ? residual_load(p, r2, ntile, j2) : make_uint4(0, 0, 0, 0);
     tmem_ld_wait();
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c1, bias4_s + j * 4);
     if (two) tmem_fill16(c2, bias4_s + j2 * 4);
-    if (r.valid) store_piece(p, r, ntile, j, v, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    if (r1.valid) store_piece(p, r1, ntile, j, v, x1, lut_s, s, hs, lsb, rs, rhs, rlsb);
     if (two) {
-      if (b2 != decoded_b) {
-        r = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
-        decoded_b = b2;
-      }
-      if (r.valid) store_piece(p, r, ntile, j2, w, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      r = r2;
+      decoded_b = b2;
+      if (r2.valid) store_piece(p, r2, ntile, j2, w, x2, lut_s, s, hs, lsb, rs, rhs, rlsb);
     }
     u += 2;
     b = two && j2 + 1 == nj ? b2 + 1 : b2;
