@@ -374,8 +374,33 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
 // residual.
 // `lut` points at entry 128 of the 256-byte table (static shared memory), so it is indexed by the
 // clamped value directly; the bytes are gathered into words with byte permutes.
+// Round half to even of a / 2^s from c = a + 2^(s-1) (the half is folded into the bias the
+// accumulator starts from): c >> s rounds half up; it is one too large exactly when a lies halfway
+// and c >> s is odd, i.e. when the low s + 1 bits of c are 1 followed by s zeros. That test is
+// t = (2^(s+1) - ((c & (2^(s+1) - 1)) ^ 2^s)) >> (s + 1), done as a multiply-high so that the
+// integer-multiply pipe takes part of the work off the integer ALU pipe, which the epilogue
+// otherwise saturates. For s = 0 the constants make t = 0 (no rounding).
+struct RneK {
+  int s;
+  uint32_t mk, hk, w2, um;  // 2^(s+1) - 1, 2^s, 2^(s+1), 2^(31-s)   (s = 0: 0, 1, 2, 2^31)
+};
+__device__ __forceinline__ RneK make_rne(int s) {
+  RneK k;
+  k.s = s;
+  k.mk = s > 0 ? (2u << s) - 1u : 0u;
+  k.hk = s > 0 ? (1u << s) : 1u;
+  k.w2 = 2u * k.hk;
+  k.um = 1u << (31 - s);
+  return k;
+}
+__device__ __forceinline__ int rne_from_half_up(int c, const RneK& k) {
+  const int q = c >> k.s;
+  const uint32_t w = k.w2 - (((uint32_t)c & k.mk) ^ k.hk);  // in [1, 2^(s+1)]; 2^(s+1) only on a tie to odd
+  return q - (int)__umulhi(w, k.um);
+}
+
 template <bool RES>
-__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, int s, int hs, int lsb,
+__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, const RneK& k,
                                             const ConvParams& p, int rs, int rhs, int rlsb, uint4 r4) {
   uint32_t t[16];
   const int8_t* rv = reinterpret_cast<const int8_t*>(&r4);
@@ -384,8 +409,8 @@ __device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int i = 4 * q4 + e;
-      const int a = (int)v[i];  // the accumulator started at the bias
-      const int r1 = (a + hs + ((a >> s) & lsb)) >> s;   // round half to even, exact for s in [0, 16]
+      // the accumulator started at the bias plus 2^(s-1): round half to even, exact for s in [0, 16]
+      const int r1 = rne_from_half_up((int)v[i], k);
       uint32_t u = lut[clamp_i8(r1)];
       if (RES) {
         const int y = ((int)(int8_t)u << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
@@ -438,15 +463,15 @@ __device__ __forceinline__ uint4 residual_load(const ConvParams& p, const RowInf
 }
 
 __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
-                                            uint4 r4, const uint8_t* lut_s, int s, int hs, int lsb, int rs, int rhs,
+                                            uint4 r4, const uint8_t* lut_s, const RneK& rk, int rs, int rhs,
                                             int rlsb) {
   const int nj = p.n_tile / 16;
   const int oc = ntile * nj + jj;  // output chunk
   uint4 o;
   if (p.has_res) {
-    o = epilogue16<true>(v, lut_s, s, hs, lsb, p, rs, rhs, rlsb, r4);
+    o = epilogue16<true>(v, lut_s, rk, p, rs, rhs, rlsb, r4);
   } else {
-    o = epilogue16<false>(v, lut_s, s, hs, lsb, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
+    o = epilogue16<false>(v, lut_s, rk, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
   }
   if (!p.out_nchw) {
     *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
@@ -479,7 +504,7 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
   constexpr int NG = EW / 4;
   const int q = warp & 3, g = ((warp >> 2) + it) % NG;
   const int nj = p.n_tile >> 4;
-  const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
+  const RneK rk = make_rne(p.shift);
   const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
   const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
   const int units = p.mt * nj;
@@ -516,11 +541,11 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c1, bias4_s + j * 4);
     if (two) tmem_fill16(c2, bias4_s + j2 * 4);
-    if (r1.valid) store_piece(p, r1, ntile, j, v, x1, lut_s, s, hs, lsb, rs, rhs, rlsb);
+    if (r1.valid) store_piece(p, r1, ntile, j, v, x1, lut_s, rk, rs, rhs, rlsb);
     if (two) {
       r = r2;
       decoded_b = b2;
-      if (r2.valid) store_piece(p, r2, ntile, j2, w, x2, lut_s, s, hs, lsb, rs, rhs, rlsb);
+      if (r2.valid) store_piece(p, r2, ntile, j2, w, x2, lut_s, rk, rs, rhs, rlsb);
     }
     u += 2;
     b = two && j2 + 1 == nj ? b2 + 1 : b2;
@@ -573,7 +598,9 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
     if (tid == PW0 * 32) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap) : "memory");
   }
   for (int i = tid; i < 256; i += conv_threads(MODE, EW)) lut_tab[i] = (uint8_t)p.lut[i];
-  for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i];
+  // the accumulators start at the bias plus 2^(shift-1), the half that rounds the SRS shift
+  const int half = p.shift > 0 ? 1 << (p.shift - 1) : 0;
+  for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i] + half;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
