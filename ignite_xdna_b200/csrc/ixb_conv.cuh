@@ -493,11 +493,12 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 
 // Drain one accumulator: warp w reads TMEM lane quarter w % 4. The tile's units (128-row block,
 // 16-column chunk), in block-major order, are split into one contiguous share per warpgroup, so a
-// thread decodes its row once per block; it issues the TMEM loads (and residual loads) of two
-// units before one wait so their latencies overlap. Which warpgroup takes which share rotates with
-// the CTA's tile count `it`: when the units do not divide evenly (4 units over 3 warpgroups), each
-// warpgroup takes the larger share in turn instead of one always lagging. A drained unit is set back to the bias, the
-// value the next tile's accumulation starts from.
+// thread decodes its row once per block. One unit at a time (16 accumulators in registers): two
+// units in flight measured slower, the extra registers cost the arithmetic its interleaving. Which
+// warpgroup takes which share rotates with the CTA's tile count `it`: when the units do not divide
+// evenly (4 units over 3 warpgroups), each warpgroup takes the larger share in turn instead of one
+// always lagging. A drained unit is set back to the bias, the value the next tile's accumulation
+// starts from.
 template <int MODE, int EW>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const uint8_t* lut_s, const int4* bias4_s, int it) {
@@ -519,37 +520,23 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
   const int row_in_block = q * 32 + lane;
   int decoded_b = -1;
   RowInfo r{};
-  while (u < u_end) {
-    const bool two = u + 1 < u_end;
-    const int b2 = (j + 1 == nj) ? b + 1 : b, j2 = (j + 1 == nj) ? 0 : j + 1;
-    uint32_t v[16], w[16];
-    const uint32_t c1 = lane_base + (uint32_t)(b * p.n_tile + j * 16);
-    const uint32_t c2 = lane_base + (uint32_t)(b2 * p.n_tile + j2 * 16);
-    tmem_ld16(c1, v);
-    if (two) tmem_ld16(c2, w);
+  for (; u < u_end; ++u) {
+    uint32_t v[16];
+    const uint32_t c = lane_base + (uint32_t)(b * p.n_tile + j * 16);
+    tmem_ld16(c, v);
     if (b != decoded_b) {
       r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
       decoded_b = b;
     }
-    const RowInfo r1 = r;
-    RowInfo r2 = r;
-    if (two && b2 != b) r2 = decode_row<MODE>(p, m0 + b2 * kBlockM + row_in_block);
-    // residual loads in flight together with the TMEM loads
-    const uint4 x1 = residual_load(p, r1, ntile, j);
-    const uint4 x2 = two ? residual_load(p, r2, ntile, j2) : make_uint4(0, 0, 0, 0);
+    const uint4 x = residual_load(p, r, ntile, j);  // in flight together with the TMEM load
     tmem_ld_wait();
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
-    tmem_fill16(c1, bias4_s + j * 4);
-    if (two) tmem_fill16(c2, bias4_s + j2 * 4);
-    if (r1.valid) store_piece(p, r1, ntile, j, v, x1, lut_s, rk, rs, rhs, rlsb);
-    if (two) {
-      r = r2;
-      decoded_b = b2;
-      if (r2.valid) store_piece(p, r2, ntile, j2, w, x2, lut_s, rk, rs, rhs, rlsb);
+    tmem_fill16(c, bias4_s + j * 4);
+    if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, rk, rs, rhs, rlsb);
+    if (++j == nj) {
+      j = 0;
+      ++b;
     }
-    u += 2;
-    b = two && j2 + 1 == nj ? b2 + 1 : b2;
-    j = two ? (j2 + 1 == nj ? 0 : j2 + 1) : j2;
   }
   tmem_st_wait();  // the biases are in TMEM before the accumulator is handed back
 }
