@@ -677,9 +677,11 @@ int launch_pool(const PoolLaunch& L, cudaStream_t st) {
 int launch_quantize(const uint8_t* images, const int8_t* lut, int batch, int h, int w, int8_t* out,
                     cudaStream_t st) {
   if (w % 4) return fail(IXB_ERR_INVALID, "image width must be a multiple of 4");
-  const long long items = (long long)batch * h * (w / 4);
+  const long long items = (long long)batch * h * (w / 2 + 1);
+  if (items >= (1LL << 31)) return fail(IXB_ERR_INVALID, "too many pixels for one ingress launch");
   const int blocks = (int)std::min<long long>((items + 255) / 256, 148LL * 16);
-  quantize_images_kernel<<<blocks, 256, 0, st>>>(images, lut, batch, h, w, out);
+  quantize_images_kernel<<<blocks, 256, 0, st>>>(images, lut, batch, h, w, make_fastdiv((uint32_t)(w / 2 + 1)),
+                                                 make_fastdiv((uint32_t)h), out);
   IXB_CUDA(cudaGetLastError());
   return 0;
 }

@@ -8,36 +8,36 @@
 namespace ixb {
 
 // uint8 pixels [B][3][H][W] -> int8 [B][H+2][W+4][8] (bytes 0..2 = lut[pixel] of the three channels,
-// bytes 3..7 = 0; halo columns and rows are left untouched and stay zero). One thread per 4
-// horizontally adjacent pixels. The lookup is the model input's QuantizeLinear
-// (graph_session.py:144-149 input_lut).
+// bytes 3..7 = 0). One thread per 16-byte pixel pair of the padded row: pair k covers padded
+// columns 2k and 2k + 1, i.e. image columns 2k - 1 and 2k (column -1 and column W are the zero
+// halo, written as zeros), so a warp's stores are 512 contiguous bytes of whole sectors. Halo rows
+// and padded columns past W + 1 are left untouched and stay zero. The item index splits into
+// (image, row, pair) by multiply-shift divisions (items < 2^31). The lookup is the model input's
+// QuantizeLinear (graph_session.py:144-149 input_lut).
 __global__ void __launch_bounds__(256) quantize_images_kernel(const uint8_t* __restrict__ img,
                                                                const int8_t* __restrict__ lut, int B, int H,
-                                                               int W, int8_t* __restrict__ out) {
+                                                               int W, FastDiv fd_pairs, FastDiv fd_h,
+                                                               int8_t* __restrict__ out) {
   __shared__ uint8_t lut_s[256];
   grid_dep_launch();
   for (int i = threadIdx.x; i < 256; i += blockDim.x) lut_s[i] = (uint8_t)lut[i];
   __syncthreads();
   grid_dep_wait();
-  const int wq = W >> 2;
-  const long long total = (long long)B * H * wq;
+  const int pairs = W / 2 + 1;
+  const int total = B * H * pairs;
   const long long plane = (long long)H * W;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long b = i / ((long long)H * wq);
-    const int rem = (int)(i - b * H * wq);
-    const int y = rem / wq, x4 = (rem - (rem / wq) * wq) * 4;
-    const uint8_t* src = img + b * 3 * plane + (long long)y * W + x4;
-    const uint32_t r = __ldg(reinterpret_cast<const uint32_t*>(src));
-    const uint32_t g = __ldg(reinterpret_cast<const uint32_t*>(src + plane));
-    const uint32_t bl = __ldg(reinterpret_cast<const uint32_t*>(src + 2 * plane));
-    uint2* dst = reinterpret_cast<uint2*>(out + ((b * (H + 2) + y + 1) * (long long)(W + 4) + x4 + 1) * 8);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t w = (uint32_t)lut_s[(r >> (8 * j)) & 0xFF] | ((uint32_t)lut_s[(g >> (8 * j)) & 0xFF] << 8) |
-                         ((uint32_t)lut_s[(bl >> (8 * j)) & 0xFF] << 16);
-      dst[j] = make_uint2(w, 0u);
-    }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int row = (int)fdiv((uint32_t)i, fd_pairs);  // b * H + y
+    const int k = i - row * pairs;
+    const int b = (int)fdiv((uint32_t)row, fd_h), y = row - b * H;
+    const uint8_t* src = img + (long long)b * 3 * plane + (long long)y * W;
+    auto px = [&](int x) -> uint32_t {
+      if (x < 0 || x >= W) return 0u;
+      return (uint32_t)lut_s[__ldg(src + x)] | ((uint32_t)lut_s[__ldg(src + plane + x)] << 8) |
+             ((uint32_t)lut_s[__ldg(src + 2 * plane + x)] << 16);
+    };
+    const uint32_t w0 = px(2 * k - 1), w1 = px(2 * k);
+    *reinterpret_cast<uint4*>(out + (((long long)b * (H + 2) + y + 1) * (W + 4) + 2 * k) * 8) = make_uint4(w0, 0u, w1, 0u);
   }
 }
 
