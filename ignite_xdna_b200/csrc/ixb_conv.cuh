@@ -370,54 +370,38 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
 }
 
 // ---------------------------------------------------------------- epilogue
-// 16 accumulators of one row (bias included) -> 16 int8 outputs: RNE shift, int8 clamp, table,
-// residual.
+// 16 accumulators of one row (bias included) -> 16 int8 outputs: RNE shift and int8 clamp (one
+// float conversion), table, residual.
 // `lut` points at entry 128 of the 256-byte table (static shared memory), so it is indexed by the
 // clamped value directly; the bytes are gathered into words with byte permutes.
-// Round half to even of a / 2^s from c = a + 2^(s-1) (the half is folded into the bias the
-// accumulator starts from): c >> s rounds half up; it is one too large exactly when a lies halfway
-// and c >> s is odd, i.e. when the low s + 1 bits of c are 1 followed by s zeros. That test is
-// t = (2^(s+1) - ((c & (2^(s+1) - 1)) ^ 2^s)) >> (s + 1), done as a multiply-high so that the
-// integer-multiply pipe takes part of the work off the integer ALU pipe, which the epilogue
-// otherwise saturates. For s = 0 the constants make t = 0 (no rounding).
-struct RneK {
-  int s;
-  uint32_t mk, hk, w2, um;  // 2^(s+1) - 1, 2^s, 2^(s+1), 2^(31-s)   (s = 0: 0, 1, 2, 2^31)
-};
-__device__ __forceinline__ RneK make_rne(int s) {
-  RneK k;
-  k.s = s;
-  k.mk = s > 0 ? (2u << s) - 1u : 0u;
-  k.hk = s > 0 ? (1u << s) : 1u;
-  k.w2 = 2u * k.hk;
-  k.um = 1u << (31 - s);
-  return k;
-}
-__device__ __forceinline__ int rne_from_half_up(int c, const RneK& k) {
-  const int q = c >> k.s;
-  const uint32_t w = k.w2 - (((uint32_t)c & k.mk) ^ k.hk);  // in [1, 2^(s+1)]; 2^(s+1) only on a tie to odd
-  return q - (int)__umulhi(w, k.um);
+// Shift-round-saturate through the float unit: sat_s8(rne(c / 2^s)) as f = float(c) (round to
+// nearest), f * 2^-s (exact: a power of two, no overflow or underflow for s in [0, 16]), then a
+// float -> s8 conversion that rounds to nearest even and saturates. Exact for every int32 c: for
+// |c| < 2^24 float(c) == c, and for |c| >= 2^24 both |c / 2^s| and |f * 2^-s| are >= 256, so the
+// exact and the float path saturate to the same end. Three instructions (plus a sign extension
+// of the byte) where the integer form takes seven; the epilogue's arithmetic bounds most layers.
+__device__ __forceinline__ float pow2_neg(int s) { return __int_as_float((127 - s) << 23); }
+__device__ __forceinline__ int srs_s8(int c, float scale) {
+  const float f = __int2float_rn(c) * scale;
+  int r;
+  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(f));
+  return (int)(int8_t)r;  // the s8 result, sign-extended whatever the register's upper bits hold
 }
 
 template <bool RES>
-__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, const RneK& k,
-                                            const ConvParams& p, int rs, int rhs, int rlsb, uint4 r4) {
+__device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, float scale,
+                                            const ConvParams& p, float rscale, uint4 r4) {
   uint32_t t[16];
   const int8_t* rv = reinterpret_cast<const int8_t*>(&r4);
 #pragma unroll
-  for (int q4 = 0; q4 < 4; ++q4) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int i = 4 * q4 + e;
-      // the accumulator started at the bias plus 2^(s-1): round half to even, exact for s in [0, 16]
-      const int r1 = rne_from_half_up((int)v[i], k);
-      uint32_t u = lut[clamp_i8(r1)];
-      if (RES) {
-        const int y = ((int)(int8_t)u << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);
-        u = (uint32_t)clamp_i8((y + rhs + ((y >> rs) & rlsb)) >> rs);
-      }
-      t[i] = u;
+  for (int i = 0; i < 16; ++i) {
+    // the accumulator started at the bias: t1 = clamp(rne(acc >> shift)), then the table
+    uint32_t u = lut[srs_s8((int)v[i], scale)];
+    if (RES) {
+      const int y = ((int)(int8_t)u << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);  // |y| < 2^24
+      u = (uint32_t)(uint8_t)srs_s8(y, rscale);
     }
+    t[i] = u;
   }
   uint4 o;
   o.x = __byte_perm(__byte_perm(t[0], t[1], 0x0040), __byte_perm(t[2], t[3], 0x0040), 0x5410);
@@ -463,15 +447,14 @@ __device__ __forceinline__ uint4 residual_load(const ConvParams& p, const RowInf
 }
 
 __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
-                                            uint4 r4, const uint8_t* lut_s, const RneK& rk, int rs, int rhs,
-                                            int rlsb) {
+                                            uint4 r4, const uint8_t* lut_s, float scale, float rscale) {
   const int nj = p.n_tile / 16;
   const int oc = ntile * nj + jj;  // output chunk
   uint4 o;
   if (p.has_res) {
-    o = epilogue16<true>(v, lut_s, rk, p, rs, rhs, rlsb, r4);
+    o = epilogue16<true>(v, lut_s, scale, p, rscale, r4);
   } else {
-    o = epilogue16<false>(v, lut_s, rk, p, rs, rhs, rlsb, make_uint4(0, 0, 0, 0));
+    o = epilogue16<false>(v, lut_s, scale, p, rscale, make_uint4(0, 0, 0, 0));
   }
   if (!p.out_nchw) {
     *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
@@ -505,8 +488,7 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
   constexpr int NG = EW / 4;
   const int q = warp & 3, g = ((warp >> 2) + it) % NG;
   const int nj = p.n_tile >> 4;
-  const RneK rk = make_rne(p.shift);
-  const int rs = p.res_shift, rhs = rs > 0 ? (1 << (rs - 1)) - 1 : 0, rlsb = rs > 0 ? 1 : 0;
+  const float scale = pow2_neg(p.shift), rscale = pow2_neg(p.res_shift);
   const uint32_t lane_base = tacc + ((uint32_t)(q * 32) << 16);
   const int units = p.mt * nj;
   const int u_end = ((g + 1) * units) / NG;
@@ -532,7 +514,7 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     tmem_ld_wait();
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c, bias4_s + j * 4);
-    if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, rk, rs, rhs, rlsb);
+    if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale);
     if (++j == nj) {
       j = 0;
       ++b;
@@ -585,9 +567,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
     if (tid == PW0 * 32) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap) : "memory");
   }
   for (int i = tid; i < 256; i += conv_threads(MODE, EW)) lut_tab[i] = (uint8_t)p.lut[i];
-  // the accumulators start at the bias plus 2^(shift-1), the half that rounds the SRS shift
-  const int half = p.shift > 0 ? 1 << (p.shift - 1) : 0;
-  for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i] + half;
+  for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

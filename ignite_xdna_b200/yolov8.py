@@ -391,8 +391,7 @@ def _build(spec: ModelSpec) -> GraphIR:
         if not 0 <= layer.shift_out <= 16:
             raise ValueError(f"{L.name}: shift {layer.shift_out} outside [0, 16]")
         acc_bound = int(np.abs(layer.bias_int8_domain()).max()) + L.cin * L.k * L.k * 127 * 128
-        # the conv kernel's accumulator also carries the SRS rounding half, 2^(shift-1) <= 2^15
-        if acc_bound + 2 ** 15 >= 2 ** 31 or int(np.abs(layer.bias_acc()).max()) >= 2 ** 31:
+        if acc_bound >= 2 ** 31 or int(np.abs(layer.bias_acc()).max()) >= 2 ** 31:
             raise ValueError(f"{L.name}: accumulator may leave int32")
         layers.append(layer)
     names = POSE_HEAD_NAMES if spec.task == "pose" else HEAD_NAMES

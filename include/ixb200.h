@@ -89,8 +89,7 @@ typedef struct ixb_conv_desc {
   ixb_segment seg[IXB_MAX_SEGS];
   uint64_t w_offset;   /* packed weights: [cout/n_tile][kblocks][block bytes] */
   uint64_t w_bytes;
-  uint64_t bias_offset;/* int32[cout]: bias_q << e; |bias| + sum |w * t| + 2^(shift-1) must fit
-                          int32 (the accumulator carries the rounding half) */
+  uint64_t bias_offset;/* int32[cout]: bias_q << e */
   uint64_t lut_offset; /* int8[256]: activation over t1 + 128 */
   int32_t shift;       /* SRS shift, 0..16 */
   int32_t has_residual;

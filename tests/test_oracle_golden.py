@@ -38,23 +38,18 @@ def test_rne_shift_is_bankers_rounding():
         assert np.array_equal(O.rne_shift(x, s), np.round(x / (1 << s)).astype(np.int64))
 
 
-def test_half_up_rounding_identity_of_the_conv_epilogue():
-    """The conv kernel rounds from c = a + 2^(s-1) (the half rides in the accumulator's starting
-    value): q = c >> s, minus one exactly on a tie to an odd quotient, detected as
-    (2^(s+1) - ((c & (2^(s+1)-1)) ^ 2^s)) * 2^(31-s) >> 32 (a 32-bit multiply-high). The same
-    integer steps here must equal rne_shift for every shift the engine accepts."""
-    lo, hi = -2 ** 31 + 2 ** 15, 2 ** 31 - 2 ** 15    # accumulators leave 2^15 of int32 headroom
-    a = np.concatenate([np.arange(-70000, 70000), np.array([lo, hi - 1]),
-                        np.random.default_rng(5).integers(lo, hi, 200000)]).astype(np.int64)
+def test_float_shift_round_saturate_equals_the_integer_rule():
+    """The conv epilogue computes sat_s8(rne(c / 2^s)) as float32(c) (round to nearest) times 2^-s,
+    converted back rounding half to even with saturation. The same float32 steps here must equal
+    clip(rne_shift(c, s)) for every shift the engine accepts, across the whole int32 range (exact:
+    float32 holds every |c| < 2^24, and larger values saturate either way)."""
+    c = np.concatenate([np.arange(-70000, 70000), np.array([-2 ** 31, 2 ** 31 - 1, 2 ** 24 - 1, 2 ** 24 + 1,
+                                                           -(2 ** 24) - 3, 127 << 16, (127 << 16) + (1 << 15)]),
+                        np.random.default_rng(5).integers(-2 ** 31, 2 ** 31, 300000)]).astype(np.int64)
     for s in range(17):
-        mk = (2 << s) - 1 if s else 0
-        hk = (1 << s) if s else 1
-        c = a + ((1 << (s - 1)) if s else 0)
-        assert c.min() >= -2 ** 31 and c.max() < 2 ** 31          # stays in int32
-        cu = c & 0xFFFFFFFF
-        w = (2 * hk - ((cu & mk) ^ hk)) & 0xFFFFFFFF
-        t = (w * (1 << (31 - s))) >> 32
-        assert np.array_equal((c >> s) - t, O.rne_shift(a, s)), s
+        f = c.astype(np.float32) * np.float32(2.0 ** -s)
+        got = np.clip(np.rint(f), -128, 127).astype(np.int64)   # rint: round half to even
+        assert np.array_equal(got, np.clip(O.rne_shift(c, s), -128, 127)), s
 
 
 def test_residual_rule_matches_reference(kat):
