@@ -901,6 +901,7 @@ struct ixb_session {
   // branch groups: [begin, end) runs of ops joined by IXB_OP_WITH_PREV (a lone op is a group of one)
   std::vector<std::pair<int, int>> groups;
   cudaStream_t side[IXB_MAX_BRANCHES - 1] = {};
+  std::vector<double> conv_cost;  // measured ms of branch-group members run alone (empty: use MACs)
   cudaEvent_t ev_fork = nullptr, ev_join[IXB_MAX_BRANCHES - 1] = {};
   // launches and graphs per (batch, slot): key = batch * kSlots + slot
   static constexpr int kSlots = 1 + IXB_MAX_EXTRA_SLOTS;
@@ -939,8 +940,11 @@ struct ixb_session {
     std::vector<ConvLaunch> cl(convs.size());
     std::vector<PoolLaunch> pl(pools.size());
     std::string err;
-    // a branch group splits the SMs between its convs in proportion to their MACs (at least one
-    // CTA per output-channel tile each); the members after the first start from the fork, not PDL
+    // a branch group splits the SMs between its convs in proportion to their device time run alone
+    // on the whole GPU (measured when the session is created; MACs until then), at least one CTA
+    // per output-channel tile each: members that scale with SMs then take as long as the group's
+    // serial time, while latency-bound ones overlap. Members after the first start from the fork,
+    // not by programmatic dependent launch.
     std::vector<int> budget(convs.size(), 0);
     std::vector<char> forked(convs.size(), 0);
     const int sms = sm_count();
@@ -950,13 +954,14 @@ struct ixb_session {
       std::vector<double> w;
       for (int i = g.first; i < g.second; ++i) {
         const ixb_conv_desc& d = convs[ops[i].index];
-        w.push_back((double)d.out_h * d.out_w * d.cin * d.k * d.k * d.cout);
+        w.push_back(conv_cost.empty() ? (double)d.out_h * d.out_w * d.cin * d.k * d.k * d.cout
+                                      : conv_cost[ops[i].index]);
         total += w.back();
       }
       for (int i = g.first; i < g.second; ++i) {
         const ixb_conv_desc& d = convs[ops[i].index];
         const int nt = d.n_tile > 0 ? std::max(1, d.cout / d.n_tile) : 1;
-        budget[ops[i].index] = std::max(nt, (int)(sms * w[i - g.first] / std::max(total, 1.0)));
+        budget[ops[i].index] = std::max(nt, (int)(sms * w[i - g.first] / (total > 0.0 ? total : 1.0)));
         forked[ops[i].index] = i > g.first;
       }
     }
@@ -971,6 +976,47 @@ struct ixb_session {
     conv_launch[key] = std::move(cl);
     pool_launch[key] = std::move(pl);
     return 0;
+  }
+
+  // Device time of each branch-group member run alone on the whole GPU at `batch` images (mean
+  // of three launches after one warm-up), for the SM shares; the launches then rebuild.
+  int measure_costs(int batch) {
+    bool any = false;
+    for (const auto& g : groups) any = any || g.second - g.first > 1;
+    if (!any) return 0;
+    std::vector<double> cost(convs.size(), 0.0);
+    cudaEvent_t a = nullptr, b = nullptr;
+    IXB_CUDA(cudaEventCreate(&a));
+    cudaError_t e = cudaEventCreate(&b);
+    int rc = e == cudaSuccess ? 0 : cuda_fail(e, "event creation");
+    std::string err;
+    for (const auto& g : groups) {
+      if (rc || g.second - g.first < 2) continue;
+      for (int i = g.first; i < g.second && !rc; ++i) {
+        const int idx = ops[i].index;
+        ConvLaunch L;
+        if (prepare_conv(convs[idx], arena, arena_bytes, batch, L, err)) {
+          rc = fail(IXB_ERR_INVALID, "conv " + std::to_string(idx) + ": " + err);
+          break;
+        }
+        L.pdl = false;
+        rc = launch_conv(L, stream);
+        if (!rc && cudaEventRecord(a, stream) != cudaSuccess) rc = fail(IXB_ERR_CUDA, "event record");
+        for (int r = 0; r < 3 && !rc; ++r) rc = launch_conv(L, stream);
+        if (!rc && cudaEventRecord(b, stream) != cudaSuccess) rc = fail(IXB_ERR_CUDA, "event record");
+        float ms = 0.f;
+        if (!rc && cudaEventSynchronize(b) != cudaSuccess) rc = fail(IXB_ERR_CUDA, "event synchronize");
+        if (!rc) cudaEventElapsedTime(&ms, a, b);
+        cost[idx] = ms / 3.0;
+      }
+    }
+    cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+    if (rc) return rc;
+    conv_cost = std::move(cost);
+    conv_launch.clear();
+    pool_launch.clear();
+    return read_device_error();
   }
 
   int enqueue_op(int batch, int i, int slot = 0, cudaStream_t st = nullptr) {
@@ -1194,6 +1240,13 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
   }
   if (e != cudaSuccess) {
     int r = cuda_fail(e, "stream/event creation");
+    ixb_session_destroy(s);
+    return r;
+  }
+  // branch-group shares from measured member times, then the launches rebuild with them
+  int r = s->measure_costs(B);
+  if (!r) r = s->prepare(B);
+  if (r) {
     ixb_session_destroy(s);
     return r;
   }
