@@ -388,6 +388,22 @@ __device__ __forceinline__ int srs_s8(int c, float scale) {
   return (int)(int8_t)r;  // the s8 result, sign-extended whatever the register's upper bits hold
 }
 
+// A linear layer (identity table, the detect heads): the same rounding, the int8 saturation done by
+// the packing conversion, two of which pack four values (no table lookups, no byte permutes).
+__device__ __forceinline__ uint32_t pack_sat_s8(int r0, int r1, int r2, int r3) {
+  uint32_t hi, w;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(r3), "r"(r2), "r"(0u));  // bytes {r2, r3}
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(r1), "r"(r0), "r"(hi));  // {r0, r1, r2, r3}
+  return w;
+}
+__device__ __forceinline__ uint4 epilogue16_linear(const uint32_t (&v)[16], float scale) {
+  int r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = __float2int_rn(__int2float_rn((int)v[i]) * scale);
+  return make_uint4(pack_sat_s8(r[0], r[1], r[2], r[3]), pack_sat_s8(r[4], r[5], r[6], r[7]),
+                    pack_sat_s8(r[8], r[9], r[10], r[11]), pack_sat_s8(r[12], r[13], r[14], r[15]));
+}
+
 template <bool RES>
 __device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, float scale,
                                             const ConvParams& p, float rscale, uint4 r4) {
@@ -447,11 +463,14 @@ __device__ __forceinline__ uint4 residual_load(const ConvParams& p, const RowInf
 }
 
 __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& r, int ntile, int jj, const uint32_t (&v)[16],
-                                            uint4 r4, const uint8_t* lut_s, float scale, float rscale) {
+                                            uint4 r4, const uint8_t* lut_s, float scale, float rscale,
+                                            bool linear) {
   const int nj = p.n_tile / 16;
   const int oc = ntile * nj + jj;  // output chunk
   uint4 o;
-  if (p.has_res) {
+  if (linear && !p.has_res) {
+    o = epilogue16_linear(v, scale);
+  } else if (p.has_res) {
     o = epilogue16<true>(v, lut_s, scale, p, rscale, r4);
   } else {
     o = epilogue16<false>(v, lut_s, scale, p, rscale, make_uint4(0, 0, 0, 0));
@@ -484,7 +503,8 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 // starts from.
 template <int MODE, int EW>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
-                                                   int lane, const uint8_t* lut_s, const int4* bias4_s, int it) {
+                                                   int lane, const uint8_t* lut_s, const int4* bias4_s, int it,
+                                                   bool linear) {
   constexpr int NG = EW / 4;
   const int q = warp & 3, g = ((warp >> 2) + it) % NG;
   const int nj = p.n_tile >> 4;
@@ -514,7 +534,7 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     tmem_ld_wait();
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c, bias4_s + j * 4);
-    if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale);
+    if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
     if (++j == nj) {
       j = 0;
       ++b;
@@ -567,6 +587,9 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
     if (tid == PW0 * 32) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap) : "memory");
   }
   for (int i = tid; i < 256; i += conv_threads(MODE, EW)) lut_tab[i] = (uint8_t)p.lut[i];
+  // a linear layer's table is the identity (entry i holds i - 128): its epilogue skips the lookups.
+  // Thread i < 256 wrote entry i itself, so each reads its own write.
+  const bool linear = __syncthreads_and(tid >= 256 || lut_tab[tid] == (uint8_t)(tid - 128)) != 0;
   for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i];
   tc_fence_before();
   __syncthreads();
@@ -618,7 +641,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
       ew += c1 - c0;
       tc_fence_after();
       conv_epilogue_tile<MODE, EW>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s,
-                                   tiles);
+                                   tiles, linear);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       ek += clock64() - c1;
