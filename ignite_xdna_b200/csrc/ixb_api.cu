@@ -382,12 +382,10 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
   if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.rowsA > 1024)
     return bad("an im2col load carries at most 1024 pixels");
-  // Warps: MMA-heavy tiles (long K over one or two 128-row blocks) take 8 epilogue and 4 MMA
-  // warps, the rest 12 epilogue and 3 MMA warps (GATHER always 8 + 4); the issuers split each
-  // K-block's MMAs between them.
-  int mma_per_block = 0;
-  for (const SchedKB& k : kbs) mma_per_block += k.nops;
-  p.ew = (d.mode == IXB_MODE_GATHER || (p.mt <= 2 && mma_per_block >= 16)) ? 8 : 12;
+  // Warps: 12 epilogue + 1 producer + 3 MMA warps (GATHER: 8 + 4 producer warps + 4); the issuers
+  // split each K-block's MMAs between them. (8 epilogue + 4 MMA warps for MMA-heavy tiles measured
+  // no faster on any YOLOv8n layer and slower on some.)
+  p.ew = d.mode == IXB_MODE_GATHER ? 8 : 12;
   p.issuers = mma_warps(p.ew);
   p.w_ntile_stride = (long long)b_total;
   p.wpack = arena + d.w_offset;
@@ -604,14 +602,11 @@ int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
 }
 
 int launch_conv(const ConvLaunch& L, cudaStream_t st) {
-  const bool e12 = L.p.ew == 12;
   switch (L.mode) {
-    case IXB_MODE_WINDOW:
-      return e12 ? launch_conv_m<IXB_MODE_WINDOW, 12>(L, st) : launch_conv_m<IXB_MODE_WINDOW, 8>(L, st);
+    case IXB_MODE_WINDOW: return launch_conv_m<IXB_MODE_WINDOW, 12>(L, st);
     case IXB_MODE_GATHER: return launch_conv_m<IXB_MODE_GATHER, 8>(L, st);
-    case IXB_MODE_IM2COL:
-      return e12 ? launch_conv_m<IXB_MODE_IM2COL, 12>(L, st) : launch_conv_m<IXB_MODE_IM2COL, 8>(L, st);
-    default: return e12 ? launch_conv_m<IXB_MODE_STEM, 12>(L, st) : launch_conv_m<IXB_MODE_STEM, 8>(L, st);
+    case IXB_MODE_IM2COL: return launch_conv_m<IXB_MODE_IM2COL, 12>(L, st);
+    default: return launch_conv_m<IXB_MODE_STEM, 12>(L, st);
   }
 }
 

@@ -39,11 +39,12 @@
 // are two A slots (two chunks of one tap, or one chunk at two taps).
 //
 // The kernel is persistent and warp-specialised:
-//   epilogue warps (12, or 8 for GATHER): TMEM -> registers -> integer epilogue -> global; warp w
-//            reads TMEM lane quarter w % 4, the warpgroups take alternate (block, 16-column) pieces
+//   epilogue warps (12, or 8 for GATHER): TMEM -> registers -> epilogue -> global; warp w reads
+//            TMEM lane quarter w % 4, the warpgroups take shares of the tile's (block, 16-column)
+//            units
 //   producer: one thread issuing bulk / TMA copies (4 warps of cp.async for GATHER)
-//   two MMA warps: one thread each issues tcgen05.mma for alternate 128-row blocks (a single
-//            issuer alone reaches only ~55-70 cycles per small-N MMA, two reach ~40)
+//   MMA warps (3, or 4 for GATHER): one thread each issues its share of each K-block's MMAs (a
+//            single issuer alone reaches only ~55-70 cycles per small-N MMA)
 // Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next. When a CTA's
 // weights fit, they are loaded once and stay resident in shared memory.
 #pragma once
@@ -126,12 +127,11 @@ enum : int {
 };
 
 constexpr int kBlockM = 128;
-// Warp layout per mode.
 // Warp layout per (mode, epilogue warps EW): EW epilogue warps, the producer warps, then the MMA
-// warps, one issuing thread each (a warp issues an MMA only every ~100 cycles, so MMA-heavy layers
-// take four). At most 16 warps: four per SM sub-partition keeps 128 registers per thread.
-//   EW = 12: 12 epilogue + 1 producer + 3 MMA (epilogue-heavy layers)
-//   EW = 8:   8 epilogue + 1 producer + 4 MMA (MMA-heavy layers); GATHER: 8 + 4 + 4
+// warps, one issuing thread each (a warp issues an MMA only every ~100 cycles, so several issue).
+// At most 16 warps: four per SM sub-partition keeps 128 registers per thread.
+//   EW = 12: 12 epilogue + 1 producer + 3 MMA (WINDOW, IM2COL, STEM)
+//   EW = 8:   8 epilogue + 4 producer + 4 MMA (GATHER)
 __host__ __device__ constexpr int prod_warps(int mode) { return mode == IXB_MODE_GATHER ? 4 : 1; }
 __host__ __device__ constexpr int mma_warp0(int mode, int ew) { return ew + prod_warps(mode); }
 __host__ __device__ constexpr int mma_warps(int ew) { return ew == 12 ? 3 : 4; }
