@@ -234,6 +234,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     const int q = warp & 3, g = warp >> 2;
     const int nch = p.bn / 16;
     const int s = p.shift, hs = s > 0 ? (1 << (s - 1)) - 1 : 0, lsb = s > 0 ? 1 : 0;
+    // shifts up to 16 round through the float unit (exact: see the conv epilogue's srs_s8)
+    const bool fsrs = s <= 16;
+    const float fscale = __int_as_float((127 - (fsrs ? s : 0)) << 23);
     int acc = 0;
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -280,7 +283,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
               // saturating adds: a sum past int32 saturates, which for shift <= 23 still clamps
               // to the same int8 as the exact value
               const int a = add_sat((int)v[4 * i + e], bv[e]);
-              const int r = clamp_i8(add_sat(a, hs + ((a >> s) & lsb)) >> s);
+              int r;
+              if (fsrs) {
+                asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(__int2float_rn(a) * fscale));
+                r = (int)(int8_t)r;
+              } else {
+                r = clamp_i8(add_sat(a, hs + ((a >> s) & lsb)) >> s);
+              }
               packed |= (uint32_t)(r & 0xFF) << (8 * e);
             }
             w[i] = packed;
