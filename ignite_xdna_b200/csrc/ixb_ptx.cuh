@@ -68,12 +68,14 @@ __device__ __forceinline__ bool wait_timed_out() {
 }
 // Bounded wait: returns false (and raises the device flag) if the phase never completes. Once any
 // wait has timed out, later waits give up at once, so a stuck launch ends after one time limit.
+// The clock and the flag (a global load) are checked every 16th retry only, so a warp that keeps
+// retrying costs the working warps few issue slots and no memory traffic.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
-  for (;;) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs || wait_timed_out()) break;
+    if ((i & 15) == 0 && (global_ns() - t0 > kWaitLimitNs || wait_timed_out())) break;
   }
   set_dev_error(DEV_ERR_WAIT_TIMEOUT);
   return false;
