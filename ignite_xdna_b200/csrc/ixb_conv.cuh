@@ -84,6 +84,7 @@ struct ConvParams {
   int rowsA, win_origin;
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
   int b_resident, a_off, tbl_off, bar_off, bias_off;
+  int ctab_off;  // WINDOW: per input chunk the address of its plane (image 0, padded pixel 0)
   int n_tile, acc_cols, tmem_cols, issuers;  // MMA issuing threads
   int ew;                                           // epilogue warps (8 or 12)
   uint32_t idesc;
@@ -207,9 +208,10 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
         const int gc = K.chunk0 + sl / K.ntaps;
         const int tap = K.tap0 + sl % K.ntaps;
         if (MODE == IXB_MODE_WINDOW) {
-          const SegDev& s = p.seg[seg_of_chunk(p, gc)];
-          bulk_g2s(As + sl * slot_bytes, s.base + (long long)(gc - s.chunk_begin) * s.plane + wb * 16, slot_bytes,
-                   &full[stage]);
+          // the chunk's plane from the shared-memory table (a dynamically indexed read of the kernel
+          // parameters costs a few hundred cycles per copy)
+          const int8_t* const* ctab = reinterpret_cast<const int8_t* const*>(smem + p.ctab_off);
+          bulk_g2s(As + sl * slot_bytes, ctab[gc] + wb * 16, slot_bytes, &full[stage]);
         } else if (MODE == IXB_MODE_IM2COL) {  // loaded tap = 2 ky + kx, kx in {0, 1}
           const SegDev& s = p.seg[0];
           tma_im2col(As + sl * slot_bytes, &p.tmap, 2 * x0, 2 * y0, (gc - s.chunk_begin) * s.plane_images + img0,
@@ -632,6 +634,13 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   // Thread i < 256 wrote entry i itself, so each reads its own write.
   const bool linear = __syncthreads_and(tid >= 256 || lut_tab[tid] == (uint8_t)(tid - 128)) != 0;
   for (int i = tid; i < p.n_tile; i += conv_threads(MODE, EW)) bias_s[i] = p.bias[ntile * p.n_tile + i];
+  if (MODE == IXB_MODE_WINDOW) {
+    const int8_t** ctab = reinterpret_cast<const int8_t**>(smem + p.ctab_off);
+    for (int gc = tid; gc < p.cin_chunks; gc += conv_threads(MODE, EW)) {
+      const SegDev& s = p.seg[seg_of_chunk(p, gc)];
+      ctab[gc] = s.base + (long long)(gc - s.chunk_begin) * s.plane;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
