@@ -201,23 +201,27 @@ __device__ __forceinline__ void produce_single(const ConvParams& p, uint8_t* sme
       const long long c1 = clock64();
       tw += c1 - c0;
       uint8_t* As = smem + p.a_off + stage * p.stage_bytes;
-      const KBlockDev& K = p.kb[kb];
+      const KBlockDev K = p.kb[kb];  // one read of the K-block's entry per K-block
       const int nslots = K.nchunks * K.ntaps;
       mbar_arrive_expect_tx(&full[stage], (uint32_t)nslots * slot_bytes + (p.b_resident ? 0u : (uint32_t)K.b_bytes));
-      for (int sl = 0; sl < nslots; ++sl) {
-        const int gc = K.chunk0 + sl / K.ntaps;
-        const int tap = K.tap0 + sl % K.ntaps;
-        if (MODE == IXB_MODE_WINDOW) {
-          // the chunk's plane from the shared-memory table (a dynamically indexed read of the kernel
-          // parameters costs a few hundred cycles per copy)
-          const int8_t* const* ctab = reinterpret_cast<const int8_t* const*>(smem + p.ctab_off);
-          bulk_g2s(As + sl * slot_bytes, ctab[gc] + wb * 16, slot_bytes, &full[stage]);
-        } else if (MODE == IXB_MODE_IM2COL) {  // loaded tap = 2 ky + kx, kx in {0, 1}
-          const SegDev& s = p.seg[0];
-          tma_im2col(As + sl * slot_bytes, &p.tmap, 2 * x0, 2 * y0, (gc - s.chunk_begin) * s.plane_images + img0,
-                     tap & 1, tap >> 1, &full[stage]);
-        } else {  // STEM: slot = image row ky; pair 1 of output x is pair 0 of x + 1, one row on
-          tma_im2col(As + sl * slot_bytes, &p.tmap, x0, 2 * y0, img0, 0, tap, &full[stage]);
+      if (MODE == IXB_MODE_WINDOW) {
+        // one slot per chunk (the taps are window shifts); the chunk's plane comes from the
+        // shared-memory table (a dynamically indexed read of the kernel parameters costs a few
+        // hundred cycles per copy)
+        const int8_t* const* ctab = reinterpret_cast<const int8_t* const*>(smem + p.ctab_off);
+        for (int sl = 0; sl < nslots; ++sl)
+          bulk_g2s(As + sl * slot_bytes, ctab[K.chunk0 + sl] + wb * 16, slot_bytes, &full[stage]);
+      } else {
+        for (int sl = 0; sl < nslots; ++sl) {
+          const int gc = K.chunk0 + sl / K.ntaps;
+          const int tap = K.tap0 + sl % K.ntaps;
+          if (MODE == IXB_MODE_IM2COL) {  // loaded tap = 2 ky + kx, kx in {0, 1}
+            const SegDev& s = p.seg[0];
+            tma_im2col(As + sl * slot_bytes, &p.tmap, 2 * x0, 2 * y0, (gc - s.chunk_begin) * s.plane_images + img0,
+                       tap & 1, tap >> 1, &full[stage]);
+          } else {  // STEM: slot = image row ky; pair 1 of output x is pair 0 of x + 1, one row on
+            tma_im2col(As + sl * slot_bytes, &p.tmap, x0, 2 * y0, img0, 0, tap, &full[stage]);
+          }
         }
       }
       if (!p.b_resident)
