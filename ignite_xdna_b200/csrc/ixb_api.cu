@@ -379,7 +379,6 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.tbl_off = p.a_off + p.stages * p.stage_bytes;
   p.bar_off = p.tbl_off + (d.mode == IXB_MODE_GATHER ? 2 * p.tile_rows * 16 : 0);
   p.bias_off = p.bar_off + 512;
-  if ((2 * p.stages + 6) * 8 + 4 > 512) return bad("too many pipeline stages");
   if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.rowsA > 1024)
     return bad("an im2col load carries at most 1024 pixels");
   // Warps: 12 epilogue + 1 producer + 3 MMA warps (GATHER: 8 + 4 producer warps + 4); the issuers
@@ -397,9 +396,14 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.fd_hw = make_fastdiv((uint32_t)(d.out_h * p.Wm));
   p.fd_Wo = make_fastdiv((uint32_t)p.Wm);
   p.acc_cols = p.mt * d.n_tile;
+  // as many accumulators as TMEM's 512 columns hold, 2 to 8: the spare ones let the MMAs run
+  // ahead of the epilogue and absorb the jitter between the two
+  p.nacc = std::max(2, std::min(kMaxAcc, 512 / p.acc_cols));
+  if (p.nacc * p.acc_cols > 512) return bad("the accumulators do not fit TMEM");
   int cols = 32;
-  while (cols < 2 * p.acc_cols) cols *= 2;
+  while (cols < p.nacc * p.acc_cols) cols *= 2;
   p.tmem_cols = cols;
+  if ((2 * p.stages + 2 * p.nacc + 1) * 8 + 4 > 512) return bad("too many pipeline stages");
   p.idesc = umma_idesc_s8(kBlockM, d.n_tile);
   {
     // kernel op table: A start / LBO from (slot, tap) and the geometry, deduplicated per K-block

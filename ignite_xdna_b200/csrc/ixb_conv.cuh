@@ -43,10 +43,11 @@
 //            TMEM lane quarter w % 4, the warpgroups take shares of the tile's (block, 16-column)
 //            units
 //   producer: one thread issuing bulk / TMA copies (4 warps of cp.async for GATHER)
-//   MMA warps (3, or 4 for GATHER): one thread each issues its share of each K-block's MMAs (a
-//            single issuer alone reaches only ~55-70 cycles per small-N MMA)
-// Two TMEM accumulators let the epilogue of one tile overlap the MMAs of the next. When a CTA's
-// weights fit, they are loaded once and stay resident in shared memory.
+//   MMA warps (3, or 4 for GATHER): each issues its share of each K-block's MMAs from one elected
+//            lane (a single issuing thread reaches only ~95 cycles per MMA)
+// Several TMEM accumulators (two for the widest tiles, up to eight for narrow ones) let the
+// epilogue of one tile overlap the MMAs of the next ones and absorb the jitter between the two
+// sides. When a CTA's weights fit, they are loaded once and stay resident in shared memory.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -72,6 +73,7 @@ struct KBlockDev {
 };
 constexpr int kMaxKBlocks = 96;
 constexpr int kMaxOps = 160;
+constexpr int kMaxAcc = 8;
 
 
 struct ConvParams {
@@ -85,7 +87,8 @@ struct ConvParams {
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
   int b_resident, a_off, tbl_off, bar_off, bias_off;
   int ctab_off;  // WINDOW: per input chunk the address of its plane (image 0, padded pixel 0)
-  int n_tile, acc_cols, tmem_cols, issuers;  // MMA issuing threads
+  int n_tile, acc_cols, tmem_cols, issuers;  // MMA issuing warps
+  int nacc;                                  // TMEM accumulators (2 .. kMaxAcc) of acc_cols columns
   int ew;                                           // epilogue warps (8 or 12)
   uint32_t idesc;
   int nseg;
@@ -129,7 +132,7 @@ enum : int {
 
 constexpr int kBlockM = 128;
 // Warp layout per (mode, epilogue warps EW): EW epilogue warps, the producer warps, then the MMA
-// warps, one issuing thread each (a warp issues an MMA only every ~100 cycles, so several issue).
+// warps (a warp issues an MMA only every ~95 cycles, so several issue).
 // At most 16 warps: four per SM sub-partition keeps 128 registers per thread.
 //   EW = 12: 12 epilogue + 1 producer + 3 MMA (WINDOW, IM2COL, STEM)
 //   EW = 8:   8 epilogue + 4 producer + 4 MMA (GATHER)
@@ -308,17 +311,23 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
 
 // ---------------------------------------------------------------- MMA issuer
 // The accumulators start at the bias (the epilogue resets each one after draining it, and the
-// kernel sets both at start), so every MMA accumulates and a K-block's MMAs can be issued by several
-// threads in any order: issuer `who` of p.issuers takes the K-block's ops o with
-// (o - op0) % issuers == who, for every 128-row block of the tile. One warp issues an MMA only
-// every ~100 cycles; the tensor core takes one every ~40-64, so several issuing warps keep it fed.
-// Every issuer commits every stage, so a stage is released when all of its MMAs are done.
+// kernel sets them all at start), so every MMA accumulates and a K-block's MMAs can be issued by
+// several threads in any order. A K-block's MMAs are its items (op o, 128-row block b), numbered
+// i = (o - op0) * mt + b; issuer `who` of p.issuers takes the items with i % issuers == who, so the
+// issuers share the work evenly even when a K-block has fewer ops than issuers (1x1 layers). One
+// thread issues an MMA only every ~95 cycles; an M=128, K=32 MMA occupies the tensor core for ~39
+// cycles at N <= 32 (its A and B operands read from shared memory), 48 at N = 64, 64 at N = 128,
+// so three issuers keep it fed. Every issuer commits every stage, so a stage is released when all
+// of its MMAs are done.
+// Each issuer is a whole warp: the loop runs on all 32 lanes from a warp index made uniform by a
+// shuffle, so the op-table reads and the descriptors live in uniform registers, and one elected
+// lane issues each MMA and commit (a single-lane branch measured ~2.5 % slower over a whole step).
 template <int MODE>
 __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
                                           uint64_t* acc_full, uint64_t* acc_empty, uint64_t* bres_bar, uint32_t tmem,
                                           int who) {
   if (p.b_resident) mbar_wait(bres_bar, 0);
-  const int S = p.stages, I = p.issuers;
+  const int S = p.stages, I = p.issuers, NA = p.nacc;
   int stage = 0, acc = 0;
   uint32_t ph = 0, aph = 0;
   uint32_t wf = 0, wa = 0, wi = 0;  // role cycles (32-bit: a launch lasts far less than 2^32 cycles)
@@ -326,6 +335,7 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
   const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
   const uint32_t a_base = smem_u32(smem + p.a_off) >> 4;
   const uint32_t w_base = smem_u32(smem);
+  const int mt_lg = __ffs(p.mt) - 1;  // mt is 1, 2 or 4
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
     uint32_t c0 = (uint32_t)clock();
     mbar_wait(&acc_empty[acc], aph ^ 1);
@@ -348,27 +358,33 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
       const uint32_t a0 = a_base + (uint32_t)((stage * p.stage_bytes) >> 4);
       const uint32_t b0 = p.b_resident ? w_base + K.b_off : ((a_base << 4) + stage * p.stage_bytes + p.a_stage_bytes);
       const uint64_t bdesc0 = umma_desc(b0, 128, 256);
-      const int o1 = K.op0 + K.nops;
+      const int items = (int)K.nops << mt_lg;
 #pragma unroll 2
-      for (int o = K.op0 + who; o < o1; o += I) {
+      for (int i = who; i < items; i += I) {
+        const int o = K.op0 + (i >> mt_lg), b = i & (p.mt - 1);
         const uint32_t opa = p.op_a[o];
         const uint64_t ad = a_hi | (uint64_t)((a0 + (opa & 0xFFFFu)) | ((opa >> 16) << 16));
         const uint64_t bd = bdesc0 + p.op_b[o];
-        for (int b = 0; b < p.mt; ++b)
+        if (elect_one())
           umma_s8(d_acc + (uint32_t)(b * p.n_tile), ad + (uint64_t)(b * ((kBlockM * 16) >> 4)), bd, p.idesc, 1u);
+        __syncwarp();
       }
-      umma_commit(&empty[stage]);
+      if (elect_one()) umma_commit(&empty[stage]);
+      __syncwarp();
       wi += (uint32_t)clock() - c1;
       if (++stage == S) {
         stage = 0;
         ph ^= 1;
       }
     }
-    umma_commit(&acc_full[acc]);
-    acc ^= 1;
-    if (acc == 0) aph ^= 1;
+    if (elect_one()) umma_commit(&acc_full[acc]);
+    __syncwarp();
+    if (++acc == NA) {
+      acc = 0;
+      aph ^= 1;
+    }
   }
-  if (who == 0) {
+  if (who == 0 && (threadIdx.x & 31) == 0) {
     write_stats(p, kStatMmaWaitFull, wf);
     write_stats(p, kStatMmaWaitAcc, wa);
     write_stats(p, kStatMmaIssue, wi);
@@ -545,7 +561,11 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 // evenly (4 units over 3 warpgroups), each warpgroup takes the larger share in turn instead of one
 // always lagging. A drained unit is set back to the bias, the value the next tile's accumulation
 // starts from.
-template <int MODE, int EW>
+// KIND picks the layer's epilogue once per kernel, so that the hot loop holds only its own path:
+// with every path inlined in one loop (table, linear, residual, NCHW head) the 1x1 layers measured
+// ~20 % slower.
+enum : int { kEpiTable = 0, kEpiLinear = 1, kEpiResidual = 2, kEpiGeneric = 3 };
+template <int MODE, int EW, int KIND>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const uint8_t* lut_s, const int4* bias4_s, int it,
                                                    bool linear) {
@@ -577,17 +597,63 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
       advance_row<MODE>(p, r, m0 + b * kBlockM + row_in_block);
       decoded_b = b;
     }
-    const uint4 x = residual_load(p, r, ntile, j);  // in flight together with the TMEM load
+    // the residual is in flight together with the TMEM load
+    const uint4 x = (KIND == kEpiResidual || KIND == kEpiGeneric) ? residual_load(p, r, ntile, j) : make_uint4(0, 0, 0, 0);
     tmem_ld_wait();
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c, bias4_s + j * 4);
-    if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
+    if (r.valid) {
+      if (KIND == kEpiGeneric) {
+        store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
+      } else {
+        uint4 o;
+        if (KIND == kEpiLinear)
+          o = epilogue16_linear(v, scale);
+        else
+          o = epilogue16<KIND == kEpiResidual>(v, lut_s, scale, p, rscale, x);
+        *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)(ntile * nj + j) * p.out.plane +
+                                  (long long)r.opix * 16) = o;
+      }
+    }
     if (++j == nj) {
       j = 0;
       ++b;
     }
   }
   tmem_st_wait();  // the biases are in TMEM before the accumulator is handed back
+}
+
+// The epilogue warps' loop over the CTA's tiles: wait for an accumulator, drain it, hand it back.
+template <int MODE, int EW, int KIND>
+__device__ __forceinline__ void epilogue_role(const ConvParams& p, uint64_t* acc_full, uint64_t* acc_empty,
+                                              uint32_t tmem, int ntile, int warp, int lane, const uint8_t* lut_s,
+                                              const int4* bias4_s, bool linear) {
+  int acc = 0;
+  uint32_t aph = 0;
+  long long ew = 0, ek = 0;
+  int tiles = 0;
+  for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+    const long long c0 = clock64();
+    mbar_wait(&acc_full[acc], aph);
+    const long long c1 = clock64();
+    ew += c1 - c0;
+    tc_fence_after();
+    conv_epilogue_tile<MODE, EW, KIND>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s,
+                                       bias4_s, tiles, linear);
+    tc_fence_before();
+    mbar_arrive(&acc_empty[acc]);
+    ek += clock64() - c1;
+    ++tiles;
+    if (++acc == p.nacc) {
+      acc = 0;
+      aph ^= 1;
+    }
+  }
+  if (threadIdx.x == 0) {
+    write_stats(p, kStatEpiWait, ew);
+    write_stats(p, kStatEpiWork, ek);
+    write_stats(p, kStatTiles, tiles);
+  }
 }
 
 template <int MODE, int EW>
@@ -600,8 +666,8 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* bres_bar = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + p.nacc;
+  uint64_t* bres_bar = acc_empty + p.nacc;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
   __shared__ uint8_t lut_tab[256];  // static: the epilogue indexes it from a constant address
   const uint8_t* lut_s = lut_tab + 128;
@@ -623,7 +689,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
       mbar_init(&full[s], fcount);
       mbar_init(&empty[s], p.issuers);  // every issuer commits every stage
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < p.nacc; ++b) {
       mbar_init(&acc_full[b], p.issuers);
       mbar_init(&acc_empty[b], EPI * 32);
     }
@@ -650,9 +716,9 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp < EPI) {
-    // both accumulators start at the bias: every MMA accumulates (see issue_mma)
+    // every accumulator starts at the bias: every MMA accumulates (see issue_mma)
     const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
-    for (int c = (warp >> 2) * 16; c < 2 * p.acc_cols; c += (EPI / 4) * 16)
+    for (int c = (warp >> 2) * 16; c < p.nacc * p.acc_cols; c += (EPI / 4) * 16)
       tmem_fill16(tmem + lanes + (uint32_t)c, bias4_s + ((c % p.n_tile) >> 4) * 4);
     tmem_st_wait();
   }
@@ -678,36 +744,20 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
     }
   } else if (warp >= MW0) {
     // ------------------------------------------------------------ MMA issuers
-    const int who = warp - MW0;
-    if (lane == 0 && who < p.issuers)
+    const int who = __shfl_sync(0xffffffffu, warp - MW0, 0);  // warp-uniform for the compiler
+    if (who < p.issuers)
       issue_mma<MODE>(p, smem, full, empty, acc_full, acc_empty, bres_bar, tmem, who);
   } else {
     // ------------------------------------------------------------ epilogue
     grid_dep_wait();  // residual reads and output writes follow the previous layer
-    int acc = 0;
-    uint32_t aph = 0;
-    long long ew = 0, ek = 0;
-    int tiles = 0;
-    for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
-      const long long c0 = clock64();
-      mbar_wait(&acc_full[acc], aph);
-      const long long c1 = clock64();
-      ew += c1 - c0;
-      tc_fence_after();
-      conv_epilogue_tile<MODE, EW>(p, tmem + acc * p.acc_cols, t * p.tile_rows, ntile, warp, lane, lut_s, bias4_s,
-                                   tiles, linear);
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
-      ek += clock64() - c1;
-      ++tiles;
-      acc ^= 1;
-      if (acc == 0) aph ^= 1;
-    }
-    if (tid == 0) {
-      write_stats(p, kStatEpiWait, ew);
-      write_stats(p, kStatEpiWork, ek);
-      write_stats(p, kStatTiles, tiles);
-    }
+    if (p.out_nchw)
+      epilogue_role<MODE, EW, kEpiGeneric>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
+    else if (p.has_res)
+      epilogue_role<MODE, EW, kEpiResidual>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
+    else if (linear)
+      epilogue_role<MODE, EW, kEpiLinear>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
+    else
+      epilogue_role<MODE, EW, kEpiTable>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
   }
   tc_fence_before();
   __syncthreads();
