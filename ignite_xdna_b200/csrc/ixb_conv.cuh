@@ -477,44 +477,6 @@ __device__ __forceinline__ RowInfo decode_row(const ConvParams& p, int m) {
   return r;
 }
 
-// The row 128 further on in M space than r's row m - 128, from r's coordinates with a few
-// additions and wraps instead of two divisions (the epilogue walks its share block by block).
-template <int MODE>
-__device__ __forceinline__ void advance_row(const ConvParams& p, RowInfo& r, int m) {
-  if (MODE == IXB_MODE_WINDOW) {
-    int xp = r.ox + 1 + kBlockM, yp = r.oy + 1, img = r.img;
-    const int W2 = p.W + 2;
-    while (xp >= W2) {
-      xp -= W2;
-      ++yp;
-    }
-    while (yp >= p.H + 2) {
-      yp -= p.H + 2;
-      ++img;
-    }
-    r.img = img;
-    r.oy = yp - 1;
-    r.ox = xp - 1;
-    r.opix = m;
-    r.valid = m < p.m_total && yp >= 1 && yp <= p.H && xp >= 1 && xp <= p.W;
-  } else {
-    int ox = r.ox + kBlockM, oy = r.oy, img = r.img;
-    while (ox >= p.Wm) {
-      ox -= p.Wm;
-      ++oy;
-    }
-    while (oy >= p.Ho) {
-      oy -= p.Ho;
-      ++img;
-    }
-    r.img = img;
-    r.oy = oy;
-    r.ox = ox;
-    r.valid = m < p.m_total && ox < p.Wo;
-    r.opix = img * (p.Ho + 2) * (p.Wo + 2) + (oy + 1) * (p.Wo + 2) + (ox + 1);
-  }
-}
-
 // The residual's 16 bytes for (row, output chunk of n-tile `ntile`, chunk jj), loaded ahead of use.
 __device__ __forceinline__ uint4 residual_load(const ConvParams& p, const RowInfo& r, int ntile, int jj) {
   if (!p.has_res || !r.valid) return make_uint4(0, 0, 0, 0);
@@ -590,11 +552,8 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     uint32_t v[16];
     const uint32_t c = lane_base + (uint32_t)(b * p.n_tile + j * 16);
     tmem_ld16(c, v);
-    if (decoded_b < 0) {
+    if (b != decoded_b) {  // two multiply-shift divisions per block
       r = decode_row<MODE>(p, m0 + b * kBlockM + row_in_block);
-      decoded_b = b;
-    } else if (b != decoded_b) {  // the next block: b == decoded_b + 1
-      advance_row<MODE>(p, r, m0 + b * kBlockM + row_in_block);
       decoded_b = b;
     }
     // the residual is in flight together with the TMEM load
@@ -602,18 +561,19 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     tmem_ld_wait();
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c, bias4_s + j * 4);
-    if (r.valid) {
-      if (KIND == kEpiGeneric) {
-        store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
-      } else {
-        uint4 o;
-        if (KIND == kEpiLinear)
-          o = epilogue16_linear(v, scale);
-        else
-          o = epilogue16<KIND == kEpiResidual>(v, lut_s, scale, p, rscale, x);
+    if (KIND == kEpiGeneric) {
+      if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
+    } else {
+      // every lane computes (halo rows too: their residual reads as zero), only valid rows store,
+      // so the arithmetic is not a divergent branch
+      uint4 o;
+      if (KIND == kEpiLinear)
+        o = epilogue16_linear(v, scale);
+      else
+        o = epilogue16<KIND == kEpiResidual>(v, lut_s, scale, p, rscale, x);
+      if (r.valid)
         *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)(ntile * nj + j) * p.out.plane +
                                   (long long)r.opix * 16) = o;
-      }
     }
     if (++j == nj) {
       j = 0;
