@@ -354,8 +354,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     }
   }
   p.b_block_bytes = b_stage_max;
-  // barriers, bias, gather row tables
-  const int extra = 512 + 1024 + 8 * chunk + 16 + (d.mode == IXB_MODE_GATHER ? 2 * 512 * 16 : 0);
+  // barriers, bias, per-chunk table (WINDOW: plane addresses, GATHER: GatherChunk), gather row tables
+  const int ctab_entry = d.mode == IXB_MODE_GATHER ? (int)sizeof(GatherChunk) : 8;
+  const int extra = 512 + 1024 + ctab_entry * chunk + 16 + (d.mode == IXB_MODE_GATHER ? 2 * 512 * 16 : 0);
   const int budget = kConvDynSmem - 1024 - extra;
   for (;; mt /= 2) {
     p.mt = mt;
@@ -502,7 +503,7 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     }
   }
   p.ctab_off = round_up(p.bias_off + 4 * d.n_tile, 16);
-  const int smem = p.ctab_off + 8 * p.cin_chunks + 1024;
+  const int smem = p.ctab_off + ctab_entry * p.cin_chunks + 1024;
   if (smem > kConvDynSmem) return bad("shared memory plan exceeds the limit");
   const long long gm = std::max<long long>(1, std::min<long long>(p.m_tiles, ((long long)sms + ntiles - 1) / ntiles));
   L.grid = dim3((unsigned)gm, (unsigned)ntiles, 1);

@@ -75,6 +75,13 @@ constexpr int kMaxKBlocks = 96;
 constexpr int kMaxOps = 160;
 constexpr int kMaxAcc = 8;
 
+// GATHER: one input chunk as the producer reads it, from a shared-memory table filled at start
+// (a dynamically indexed read of the kernel parameters' segment table costs hundreds of cycles).
+struct GatherChunk {
+  const int8_t* base;  // the chunk's plane: padded pixel 0 of image 0
+  int P, W2, up2, pad;  // padded pixels per image, padded width, nearest-2x upsampled view
+};
+
 
 struct ConvParams {
   alignas(64) CUtensorMap tmap;  // TMA im2col map (IM2COL, STEM)
@@ -86,7 +93,7 @@ struct ConvParams {
   int rowsA, win_origin;
   int a_stage_bytes, b_block_bytes, stage_bytes, stages;
   int b_resident, a_off, tbl_off, bar_off, bias_off;
-  int ctab_off;  // WINDOW: per input chunk the address of its plane (image 0, padded pixel 0)
+  int ctab_off;  // per input chunk: WINDOW its plane's address, GATHER its GatherChunk (shared memory)
   int n_tile, acc_cols, tmem_cols, issuers;  // MMA issuing warps
   int nacc;                                  // TMEM accumulators (2 .. kMaxAcc) of acc_cols columns
   int ew;                                           // epilogue warps (8 or 12)
@@ -250,6 +257,7 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
   const int hw = p.Ho * p.Wo;
   // Per tile, one row table entry per output pixel: {image, y, x}; image -1 marks rows past the batch.
   int4* tbl = reinterpret_cast<int4*>(smem + p.tbl_off);
+  const GatherChunk* gtab = reinterpret_cast<const GatherChunk*>(smem + p.ctab_off);
   long long tw = 0;
   const long long cstart = clock64();
   int stage = 0;
@@ -275,19 +283,16 @@ __device__ __forceinline__ void produce_gather(const ConvParams& p, uint8_t* sme
       mbar_wait(&empty[stage], ph ^ 1);
       tw += clock64() - c0;
       uint8_t* dst = smem + p.a_off + stage * p.stage_bytes + c * p.rowsA * 16;
-      const KBlockDev& K = p.kb[kb];
-      const int gc = c < K.nchunks ? K.chunk0 + c : -1;
-      const int si = gc >= 0 ? seg_of_chunk(p, gc) : -1;
-      if (si >= 0) {
-        const SegDev& s = p.seg[si];
-        const int8_t* cbase = s.base + (long long)(gc - s.chunk_begin) * s.plane;
+      const KBlockDev K = p.kb[kb];  // one read per K-block
+      if (c < K.nchunks) {
+        const GatherChunk g = gtab[K.chunk0 + c];
         for (int r = ptid / nch; r < p.tile_rows; r += step) {
           const int4 e = T[r];
           if (e.x >= 0) {
-            const int iy = s.up2 ? (e.y >> 1) : e.y, ix = s.up2 ? (e.z >> 1) : e.z;
-            cp_async16(dst + r * 16, cbase + ((long long)e.x * s.P + (iy + 1) * (s.W + 2) + (ix + 1)) * 16, 16u);
+            const int iy = g.up2 ? (e.y >> 1) : e.y, ix = g.up2 ? (e.z >> 1) : e.z;
+            cp_async16(dst + r * 16, g.base + ((long long)e.x * g.P + (iy + 1) * g.W2 + (ix + 1)) * 16, 16u);
           } else {
-            cp_async16(dst + r * 16, s.base, 0u);
+            cp_async16(dst + r * 16, g.base, 0u);
           }
         }
       }
@@ -669,6 +674,13 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
     for (int gc = tid; gc < p.cin_chunks; gc += conv_threads(MODE, EW)) {
       const SegDev& s = p.seg[seg_of_chunk(p, gc)];
       ctab[gc] = s.base + (long long)(gc - s.chunk_begin) * s.plane;
+    }
+  }
+  if (MODE == IXB_MODE_GATHER) {
+    GatherChunk* gtab = reinterpret_cast<GatherChunk*>(smem + p.ctab_off);
+    for (int gc = tid; gc < p.cin_chunks; gc += conv_threads(MODE, EW)) {
+      const SegDev& s = p.seg[seg_of_chunk(p, gc)];  // the host checks that the segments tile the chunks
+      gtab[gc] = GatherChunk{s.base + (long long)(gc - s.chunk_begin) * s.plane, s.P, s.W + 2, s.up2, 0};
     }
   }
   tc_fence_before();
