@@ -19,7 +19,7 @@ IXB_ERR_INVALID = -1
 IXB_ERR_TIMEOUT = -3
 IXB_ERR_UNSUPPORTED = -5
 MAX_SEGS = 4
-API_VERSION = 5
+API_VERSION = 6
 MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH, IN_STORE = 1, 2, 4, 8, 16
@@ -44,7 +44,8 @@ class ConvDesc(C.Structure):
                 ("residual", Segment), ("res_lsh_main", C.c_int32), ("res_lsh_res", C.c_int32),
                 ("res_shift", C.c_int32), ("out_nchw", C.c_int32), ("out", Segment),
                 ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64),
-                ("egress_channels", C.c_int32), ("reserved2", C.c_int32)]
+                ("egress_channels", C.c_int32), ("has_out_up2", C.c_int32),
+                ("out_up2", Segment)]
 
 
 class PoolDesc(C.Structure):

@@ -490,6 +490,15 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.egress = reinterpret_cast<int8_t*>(arena + d.egress_offset);
     p.egress_img = (long long)d.egress_image_bytes;
   }
+  p.has_up2 = d.has_out_up2 ? 1 : 0;
+  if (d.has_out_up2) {
+    if (d.out_nchw) return bad("an NCHW head has no upsampled output");
+    if (check_seg(d.out_up2, batch, arena_bytes, false, "conv upsampled output", err)) return -1;
+    if (d.out_up2.height != 2 * d.out_h || d.out_up2.width != 2 * d.out_w || d.out_up2.channels != d.cout ||
+        d.out_up2.up2)
+      return bad("the upsampled output view must be 2 out_h x 2 out_w x cout");
+    p.out2 = seg_dev(d.out_up2, arena, 0);
+  }
   if (d.mode == IXB_MODE_WINDOW) {
     auto same = [&](const ixb_segment& s) { return s.height == d.in_h && s.width == d.in_w; };
     for (int i = 0; i < d.nseg; ++i)
@@ -884,6 +893,7 @@ void conv_spans(const ixb_conv_desc& d, int batch, std::vector<Span>& rd, std::v
   } else {
     wr.push_back(view_span(d.out, batch));
   }
+  if (d.has_out_up2) wr.push_back(view_span(d.out_up2, batch));
 }
 
 }  // namespace

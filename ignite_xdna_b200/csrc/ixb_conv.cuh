@@ -110,6 +110,8 @@ struct ConvParams {
   int res_lsh_m, res_lsh_r, res_shift;
   int out_nchw;
   SegDev out;
+  int has_up2;  // also write every output pixel 2x2 into out2 (the upsampled copy)
+  SegDev out2;
   int8_t* egress;
   long long egress_img;
   int egress_ch;  // channels the head writes (the rest of cout are zero-weight padding)
@@ -504,6 +506,15 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
   }
   if (!p.out_nchw) {
     *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
+    if (p.has_up2) {  // pixel (y, x) -> (2y + dy, 2x + dx) of the upsampled copy
+      const int W2 = p.out2.W + 2;
+      uint4* u = reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out2.base) + (long long)oc * p.out2.plane +
+                                          ((long long)r.img * p.out2.P + (long long)(2 * r.oy + 1) * W2 + 2 * r.ox + 1) * 16);
+      u[0] = o;
+      u[1] = o;
+      u[W2] = o;
+      u[W2 + 1] = o;
+    }
   } else {
     int8_t* e = p.egress + (long long)r.img * p.egress_img + r.oy * p.Wo + r.ox;
     const long long plane = (long long)p.Ho * p.Wo;
@@ -722,7 +733,7 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   } else {
     // ------------------------------------------------------------ epilogue
     grid_dep_wait();  // residual reads and output writes follow the previous layer
-    if (p.out_nchw)
+    if (p.out_nchw || p.has_up2)
       epilogue_role<MODE, EW, kEpiGeneric>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
     else if (p.has_res)
       epilogue_role<MODE, EW, kEpiResidual>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);

@@ -45,7 +45,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 5
+#define IXB_API_VERSION 6
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -102,7 +102,12 @@ typedef struct ixb_conv_desc {
   int32_t egress_channels;      /* channels of the head in the egress (<= cout; 0: cout). A head
                                    whose channel count is not a multiple of 16 computes cout =
                                    the next multiple with zero weights and writes only these. */
-  int32_t reserved2;
+  int32_t has_out_up2;          /* 1: also write the output nearest-2x upsampled into out_up2 */
+  ixb_segment out_up2;          /* (2 out_h) x (2 out_w) x cout view, written when has_out_up2: every
+                                   output pixel (y, x) also lands at (2y + dy, 2x + dx), dy, dx in
+                                   {0, 1}, so a consumer of the upsampled tensor (the top-down path's
+                                   concat) reads it as a plain tensor with bulk copies instead of
+                                   gathering 16-byte rows. Not with out_nchw. */
 } ixb_conv_desc;
 
 typedef struct ixb_pool_desc {  /* SPPF: out_k = pool5^k(in), k = 1..3, pad -128 */

@@ -174,6 +174,15 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                     for j in range(n_tile // 16):
                         a0 = ob + (nt * n_tile // 16 + j) * d.out.plane_stride + opix[rr] * 16
                         arena[a0:a0 + 16] = out[rr, 16 * j:16 * j + 16]
+                    if d.has_out_up2:  # the 2x2-replicated copy at twice the resolution
+                        u = d.out_up2
+                        W2, P2 = u.width + 2, (u.height + 2) * (u.width + 2)
+                        for j in range(n_tile // 16):
+                            base = u.offset + (nt * n_tile // 16 + j) * u.plane_stride
+                            for dy in (0, 1):
+                                for dx in (0, 1):
+                                    a0 = base + (img[rr] * P2 + (2 * oy[rr] + 1 + dy) * W2 + 2 * ox[rr] + 1 + dx) * 16
+                                    arena[a0:a0 + 16] = out[rr, 16 * j:16 * j + 16]
                 else:
                     plane = Ho * Wo
                     e = d.egress_offset + img[rr] * d.egress_image_bytes + oy[rr] * Wo + ox[rr]

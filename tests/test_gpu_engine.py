@@ -40,6 +40,23 @@ def test_small_graph_every_tensor(imgsz, batch, sms, monkeypatch):
     sess.close()
 
 
+@pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 3)])
+def test_gathered_upsample_every_tensor(imgsz, batch, monkeypatch):
+    """IXB_UP2=0: the concat convs read the upsampled tensors through per-row gathers (GATHER mode)
+    instead of the producers' 2x2-replicated copies; every tensor must still equal the oracle."""
+    monkeypatch.setenv("IXB_UP2", "0")
+    sess = InferenceSession.from_spec("yolov8n", imgsz=imgsz, max_batch=batch)
+    assert sum(c.mode == L.MODE_GATHER for c in sess.plan.convs) == 2
+    imgs = random_images(batch, imgsz, seed=5 + imgsz)
+    out = sess.run_yolo_monolithic(imgs)
+    for b in range(batch):
+        ref = O.run_image(sess.ir, imgs[b])
+        for name in ref:
+            assert np.array_equal(sess.read_tensor(name, batch=batch)[b], ref[name]), f"image {b} tensor {name}"
+        assert np.array_equal(out["raw_output"][b], O.egress_int8(sess.ir, ref))
+    sess.close()
+
+
 @pytest.mark.parametrize("imgsz,batch,sms", [(64, 2, None), (96, 2, "2")])
 def test_pose_graph_every_tensor(imgsz, batch, sms, monkeypatch):
     """YOLOv8-pose: one-class heads and 51-channel keypoint convs run on zero-padded 16-channel

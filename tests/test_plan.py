@@ -20,6 +20,16 @@ def test_kernel_model_matches_oracle(imgsz, batch, sms, monkeypatch):
     assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
 
 
+def test_kernel_model_with_gathered_upsample_matches_oracle(monkeypatch):
+    """IXB_UP2=0: the concat convs gather the upsampled tensors (GATHER mode)."""
+    monkeypatch.setenv("IXB_UP2", "0")
+    ir = build_yolov8("n", imgsz=64)
+    dp = build_plan(ir, 2)
+    assert sum(c.mode == L.MODE_GATHER for c in dp.convs) == 2 and not dp.upsampled_stores
+    imgs = random_images(2, 64, seed=12)
+    assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
+
+
 def test_pose_plan_pads_ragged_channels_and_matches_oracle():
     """One-class heads and 51-channel keypoint branches: storage and output channels round up to
     whole 16-channel chunks (zero weights and bias), the heads write only their real channels."""
@@ -100,6 +110,13 @@ def test_plan_storage_is_disjoint_and_aligned(variant):
         spans[a] = 64 * 3 * dp.img_h * dp.img_w
         spans[e] = 64 * dp.egress_image_bytes
     spans[dp.const_offset] = dp.const_blob.size
+    assert len(dp.upsampled_stores) == 2  # the top-down path's two upsampled tensors
+    for name, st in dp.upsampled_stores.items():
+        t = ir.tensors[name]
+        assert (st.height, st.width) == (2 * t.height, 2 * t.width)
+        spans[st.offset - st.guard * 16] = st.channels // 16 * st.plane_stride
+    assert not any(c.mode == L.MODE_GATHER for c in dp.convs)
+    assert sum(c.desc.has_out_up2 for c in dp.convs) == 2
     iv = sorted(spans.items())
     for (a, n), (b, _) in zip(iv, iv[1:]):
         assert a + n <= b
