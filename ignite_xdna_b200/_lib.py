@@ -19,9 +19,10 @@ IXB_ERR_INVALID = -1
 IXB_ERR_TIMEOUT = -3
 IXB_ERR_UNSUPPORTED = -5
 MAX_SEGS = 4
-API_VERSION = 6
+API_VERSION = 7
 MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
+OUT2_NONE, OUT2_UP2, OUT2_S2D, OUT2_S2D_ONLY = 0, 1, 2, 3
 IN_DEVICE, OUT_DEVICE, ASYNC, NO_GRAPH, IN_STORE = 1, 2, 4, 8, 16
 OP_CONV, OP_POOL = 0, 1
 OP_WITH_PREV = 0x100     # a conv that runs concurrently with the op(s) before it (branch group)
@@ -38,14 +39,15 @@ class ConvDesc(C.Structure):
     _fields_ = [("mode", C.c_int32), ("k", C.c_int32), ("stride", C.c_int32),
                 ("in_h", C.c_int32), ("in_w", C.c_int32), ("out_h", C.c_int32), ("out_w", C.c_int32),
                 ("cin", C.c_int32), ("cout", C.c_int32), ("n_tile", C.c_int32), ("cp", C.c_int32),
+                ("s2d_in", C.c_int32),
                 ("nseg", C.c_int32), ("seg", Segment * MAX_SEGS),
                 ("w_offset", C.c_uint64), ("w_bytes", C.c_uint64), ("bias_offset", C.c_uint64),
                 ("lut_offset", C.c_uint64), ("shift", C.c_int32), ("has_residual", C.c_int32),
                 ("residual", Segment), ("res_lsh_main", C.c_int32), ("res_lsh_res", C.c_int32),
                 ("res_shift", C.c_int32), ("out_nchw", C.c_int32), ("out", Segment),
                 ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64),
-                ("egress_channels", C.c_int32), ("has_out_up2", C.c_int32),
-                ("out_up2", Segment)]
+                ("egress_channels", C.c_int32), ("out2_kind", C.c_int32),
+                ("reserved3", C.c_int32), ("out2", Segment)]
 
 
 class PoolDesc(C.Structure):

@@ -174,6 +174,38 @@ int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>&
     // the second read one row on in the same slot
     for (int ky = 0; ky < 3; ++ky) ops.push_back(SchedOp{ky, 0, 2 * ky, ky, 0, 2 * ky + 1});
     push_kb(0, 1, 0, 3, 0);
+  } else if (d.mode == IXB_MODE_WINDOW && d.s2d_in) {
+    // Space-to-depth view of a stride-2 3x3 conv: chunk c is phase (ry, rx) = (p / 2, p % 2),
+    // p = c / (cin_chunks / 4); tap t of the 2x2 is (dy, dx) = (t / 2 - 1, t % 2 - 1). Output (y, x)
+    // tap (ky, kx) of the 3x3 reads input (2y + ky - 1, 2x + kx - 1): phase 1 one pixel back for
+    // k = 0, phase 0 for k = 1, phase 1 for k = 2, so a (chunk, tap) pair carries weights unless
+    // it reaches back (d = -1) in a phase-0 direction. Per K-block of 2 cp chunks, the valid pairs
+    // are ordered by their A address (slot, then shift) and paired into MMAs, an odd one with a
+    // zero half: 9 of 16 pairs, the 3x3's own K.
+    const int C = cin_chunks / 4;
+    auto valid = [&](int c, int t) {
+      const int ph = c / C, ry = ph / 2, rx = ph % 2;
+      return !((t / 2 == 0 && ry == 0) || (t % 2 == 0 && rx == 0));
+    };
+    const int sh[4] = {0, 1, d.in_w + 2, d.in_w + 3};
+    for (int g = 0; g * d.cp < E; ++g) {
+      const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
+      std::vector<std::pair<long long, std::pair<int, int>>> halves;  // (address, (slot, tap))
+      for (int sl = 0; sl < 2 * prs; ++sl)
+        for (int t = 0; t < 4; ++t)
+          if (valid(c0 + sl, t)) halves.push_back({(long long)sl * (1LL << 40) + sh[t], {sl, t}});
+      std::sort(halves.begin(), halves.end());
+      for (size_t i = 0; i < halves.size(); i += 2) {
+        const int s0 = halves[i].second.first, t0 = halves[i].second.second;
+        if (i + 1 < halves.size()) {
+          const int s1 = halves[i + 1].second.first, t1 = halves[i + 1].second.second;
+          ops.push_back(SchedOp{s0, c0 + s0, t0, s1, c0 + s1, t1});
+        } else {
+          ops.push_back(SchedOp{s0, c0 + s0, t0, 0, -1, 0});
+        }
+      }
+      push_kb(c0, 2 * prs, 0, 1, op0);
+    }
   } else if (d.mode == IXB_MODE_WINDOW) {
     for (int g = 0; g * d.cp < E; ++g) {
       const int prs = std::min(d.cp, E - g * d.cp), op0 = (int)ops.size(), c0 = 2 * g * d.cp;
@@ -252,11 +284,20 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   };
   if (batch < 1) return bad("batch < 1");
   if (d.mode < IXB_MODE_WINDOW || d.mode > IXB_MODE_IM2COL) return bad("unknown conv mode");
-  if (!(d.k == 1 || d.k == 3) || !(d.stride == 1 || d.stride == 2)) return bad("k must be 1 or 3, stride 1 or 2");
+  if (d.s2d_in) {
+    // a stride-2 3x3 conv over the space-to-depth view: a stride-1 2x2 conv, output size = view size
+    if (d.mode != IXB_MODE_WINDOW || d.k != 2 || d.stride != 1 || d.cin % 64)
+      return bad("a space-to-depth input needs a WINDOW 2x2 stride-1 conv over 4 x whole chunks");
+    if (d.out_h != d.in_h || d.out_w != d.in_w) return bad("a space-to-depth conv keeps the view's size");
+  } else {
+    if (!(d.k == 1 || d.k == 3) || !(d.stride == 1 || d.stride == 2)) return bad("k must be 1 or 3, stride 1 or 2");
+    const int pk = d.k / 2;
+    if (d.out_h != (d.in_h + 2 * pk - d.k) / d.stride + 1 || d.out_w != (d.in_w + 2 * pk - d.k) / d.stride + 1)
+      return bad("output size does not follow from input size, k and stride");
+  }
   if (d.nseg < 1 || d.nseg > IXB_MAX_SEGS) return bad("1..4 input segments");
-  const int pad = d.k / 2;
-  if (d.out_h != (d.in_h + 2 * pad - d.k) / d.stride + 1 || d.out_w != (d.in_w + 2 * pad - d.k) / d.stride + 1)
-    return bad("output size does not follow from input size, k and stride");
+  // window reach before a pixel: one row and one column for 3x3 and the 2x2 space-to-depth taps
+  const int pad = d.s2d_in ? 1 : d.k / 2;
   if (d.cout % 16 || d.n_tile % 16 || d.n_tile < 16 || d.n_tile > 256 || d.cout % d.n_tile)
     return bad("cout and n_tile must be multiples of 16, n_tile <= 256 dividing cout");
   if (!(d.cp == 1 || d.cp == 2 || d.cp == 4)) return bad("cp must be 1, 2 or 4");
@@ -361,7 +402,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   for (;; mt /= 2) {
     p.mt = mt;
     p.tile_rows = 128 * mt;
-    p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + 2 * p.win_origin
+    // WINDOW: taps reach win_origin pixels back and (3x3) as far ahead; the 2x2 taps only back
+    p.rowsA = (d.mode == IXB_MODE_WINDOW) ? p.tile_rows + (d.s2d_in ? 1 : 2) * p.win_origin
               : ((d.mode == IXB_MODE_STEM || d.mode == IXB_MODE_IM2COL) ? p.tile_rows + 8 : p.tile_rows);
     // 16 spare bytes: a single-tap MMA's unused second K-half reads one row past its slot
     p.a_stage_bytes = slots * p.rowsA * 16 + 16;
@@ -474,11 +516,15 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.res_shift = d.res_shift;
   }
   p.out_nchw = d.out_nchw;
+  if (d.out2_kind < IXB_OUT2_NONE || d.out2_kind > IXB_OUT2_S2D_ONLY) return bad("unknown out2_kind");
+  if (d.out_nchw && d.out2_kind) return bad("an NCHW head has no second output");
   if (!d.out_nchw) {
-    if (check_seg(d.out, batch, arena_bytes, false, "conv output", err)) return -1;
-    if (d.out.height != d.out_h || d.out.width != d.out_w || d.out.channels != d.cout || d.out.up2)
-      return bad("output view must be out_h x out_w x cout");
-    p.out = seg_dev(d.out, arena, 0);
+    if (d.out2_kind != IXB_OUT2_S2D_ONLY) {  // the space-to-depth-only output leaves `out` unused
+      if (check_seg(d.out, batch, arena_bytes, false, "conv output", err)) return -1;
+      if (d.out.height != d.out_h || d.out.width != d.out_w || d.out.channels != d.cout || d.out.up2)
+        return bad("output view must be out_h x out_w x cout");
+      p.out = seg_dev(d.out, arena, 0);
+    }
   } else {
     const unsigned long long plane = (unsigned long long)d.out_h * d.out_w;
     const int ech = d.egress_channels ? d.egress_channels : d.cout;
@@ -490,20 +536,26 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     p.egress = reinterpret_cast<int8_t*>(arena + d.egress_offset);
     p.egress_img = (long long)d.egress_image_bytes;
   }
-  p.has_up2 = d.has_out_up2 ? 1 : 0;
-  if (d.has_out_up2) {
-    if (d.out_nchw) return bad("an NCHW head has no upsampled output");
-    if (check_seg(d.out_up2, batch, arena_bytes, false, "conv upsampled output", err)) return -1;
-    if (d.out_up2.height != 2 * d.out_h || d.out_up2.width != 2 * d.out_w || d.out_up2.channels != d.cout ||
-        d.out_up2.up2)
-      return bad("the upsampled output view must be 2 out_h x 2 out_w x cout");
-    p.out2 = seg_dev(d.out_up2, arena, 0);
+  p.out2_kind = d.out2_kind;
+  if (d.out2_kind) {
+    if (check_seg(d.out2, batch, arena_bytes, false, "conv second output", err)) return -1;
+    if (d.out2.up2) return bad("the second output view is not an up2 view");
+    if (d.out2_kind == IXB_OUT2_UP2) {
+      if (d.out2.height != 2 * d.out_h || d.out2.width != 2 * d.out_w || d.out2.channels != d.cout)
+        return bad("the upsampled output view must be 2 out_h x 2 out_w x cout");
+    } else {
+      if (d.out_h % 2 || d.out_w % 2 || d.out2.height != d.out_h / 2 || d.out2.width != d.out_w / 2 ||
+          d.out2.channels != 4 * d.cout)
+        return bad("the space-to-depth output view must be out_h/2 x out_w/2 x 4 cout (even sizes)");
+    }
+    p.out2 = seg_dev(d.out2, arena, 0);
   }
   if (d.mode == IXB_MODE_WINDOW) {
     auto same = [&](const ixb_segment& s) { return s.height == d.in_h && s.width == d.in_w; };
     for (int i = 0; i < d.nseg; ++i)
       if (!same(d.seg[i])) return bad("WINDOW views must share the input geometry");
-    if (!d.out_nchw && !same(d.out)) return bad("WINDOW output must share the input geometry");
+    if (!d.out_nchw && d.out2_kind != IXB_OUT2_S2D_ONLY && !same(d.out))
+      return bad("WINDOW output must share the input geometry");
     // every window copy stays inside the planes' zero guards
     for (int i = 0; i < d.nseg; ++i) {
       const long long end = (long long)p.m_tiles * p.tile_rows + p.win_origin;
@@ -890,10 +942,10 @@ void conv_spans(const ixb_conv_desc& d, int batch, std::vector<Span>& rd, std::v
   if (d.out_nchw) {
     const int ech = d.egress_channels ? d.egress_channels : d.cout;
     wr.push_back({d.egress_offset, (unsigned long long)d.out_h * d.out_w * ech, d.egress_image_bytes, batch});
-  } else {
+  } else if (d.out2_kind != IXB_OUT2_S2D_ONLY) {
     wr.push_back(view_span(d.out, batch));
   }
-  if (d.has_out_up2) wr.push_back(view_span(d.out_up2, batch));
+  if (d.out2_kind) wr.push_back(view_span(d.out2, batch));
 }
 
 }  // namespace

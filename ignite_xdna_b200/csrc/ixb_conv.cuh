@@ -110,7 +110,7 @@ struct ConvParams {
   int res_lsh_m, res_lsh_r, res_shift;
   int out_nchw;
   SegDev out;
-  int has_up2;  // also write every output pixel 2x2 into out2 (the upsampled copy)
+  int out2_kind;  // IXB_OUT2_*: a second copy (2x2-upsampled or space-to-depth), or only the latter
   SegDev out2;
   int8_t* egress;
   long long egress_img;
@@ -505,8 +505,14 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
     o = epilogue16<false>(v, lut_s, scale, p, rscale, make_uint4(0, 0, 0, 0));
   }
   if (!p.out_nchw) {
-    *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
-    if (p.has_up2) {  // pixel (y, x) -> (2y + dy, 2x + dx) of the upsampled copy
+    if (p.out2_kind != IXB_OUT2_S2D_ONLY)
+      *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane + (long long)r.opix * 16) = o;
+    if (p.out2_kind >= IXB_OUT2_S2D) {  // pixel (y, x), chunk oc -> (y/2, x/2), chunk phase * chunks + oc
+      const int ph = (r.oy & 1) * 2 + (r.ox & 1);
+      *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out2.base) + (long long)(ph * (p.cout >> 4) + oc) * p.out2.plane +
+                                ((long long)r.img * p.out2.P + (long long)((r.oy >> 1) + 1) * (p.out2.W + 2) +
+                                 (r.ox >> 1) + 1) * 16) = o;
+    } else if (p.out2_kind == IXB_OUT2_UP2) {  // pixel (y, x) -> (2y + dy, 2x + dx) of the upsampled copy
       const int W2 = p.out2.W + 2;
       uint4* u = reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out2.base) + (long long)oc * p.out2.plane +
                                           ((long long)r.img * p.out2.P + (long long)(2 * r.oy + 1) * W2 + 2 * r.ox + 1) * 16);
@@ -542,7 +548,7 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 // KIND picks the layer's epilogue once per kernel, so that the hot loop holds only its own path:
 // with every path inlined in one loop (table, linear, residual, NCHW head) the 1x1 layers measured
 // ~20 % slower.
-enum : int { kEpiTable = 0, kEpiLinear = 1, kEpiResidual = 2, kEpiGeneric = 3 };
+enum : int { kEpiTable = 0, kEpiLinear = 1, kEpiResidual = 2, kEpiGeneric = 3, kEpiTableS2D = 4 };
 template <int MODE, int EW, int KIND>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const uint8_t* lut_s, const int4* bias4_s, int it,
@@ -579,6 +585,20 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     tmem_fill16(c, bias4_s + j * 4);
     if (KIND == kEpiGeneric) {
       if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
+    } else if (KIND == kEpiTableS2D) {
+      // table layer whose consumer is a stride-2 conv: its space-to-depth copy, and the plain
+      // output unless nothing else reads it
+      const uint4 o = epilogue16<false>(v, lut_s, scale, p, rscale, x);
+      if (r.valid) {
+        const int oc = ntile * nj + j;
+        if (p.out2_kind != IXB_OUT2_S2D_ONLY)
+          *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out.base) + (long long)oc * p.out.plane +
+                                    (long long)r.opix * 16) = o;
+        const int ph = (r.oy & 1) * 2 + (r.ox & 1);
+        *reinterpret_cast<uint4*>(const_cast<int8_t*>(p.out2.base) + (long long)(ph * (p.cout >> 4) + oc) * p.out2.plane +
+                                  ((long long)r.img * p.out2.P + (long long)((r.oy >> 1) + 1) * (p.out2.W + 2) +
+                                   (r.ox >> 1) + 1) * 16) = o;
+      }
     } else {
       // every lane computes (halo rows too: their residual reads as zero), only valid rows store,
       // so the arithmetic is not a divergent branch
@@ -733,7 +753,9 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   } else {
     // ------------------------------------------------------------ epilogue
     grid_dep_wait();  // residual reads and output writes follow the previous layer
-    if (p.out_nchw || p.has_up2)
+    if (!p.out_nchw && !p.has_res && !linear && p.out2_kind >= IXB_OUT2_S2D)
+      epilogue_role<MODE, EW, kEpiTableS2D>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
+    else if (p.out_nchw || p.out2_kind)
       epilogue_role<MODE, EW, kEpiGeneric>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
     else if (p.has_res)
       epilogue_role<MODE, EW, kEpiResidual>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);

@@ -72,6 +72,7 @@ class ConvPlan:
     cp: int
     w_packed: np.ndarray
     desc: Optional[object] = None
+    s2d: bool = False  # a stride-2 3x3 run as a 2x2 WINDOW conv over its input's space-to-depth view
 
 
 @dataclass
@@ -96,6 +97,8 @@ class DevicePlan:
     extra_images_offsets: Tuple[int, ...] = ()
     extra_egress_offsets: Tuple[int, ...] = ()
     upsampled_stores: Dict[str, Store] = field(default_factory=dict)  # 2x2 copies (upsampled_copies)
+    s2d_stores: Dict[str, Store] = field(default_factory=dict)        # space-to-depth views (s2d_convs)
+    s2d_only: frozenset = frozenset()  # tensors stored only as their space-to-depth view
     c_plan: object = None
     keep: list = field(default_factory=list)
 
@@ -119,6 +122,48 @@ def upsampled_copies(ir: GraphIR) -> set:
         return set()
     produced = {layer.output for layer in ir.conv_layers()}
     return {s.tensor for layer in ir.conv_layers() for s in layer.inputs if s.up2 and s.tensor in produced}
+
+
+def s2d_convs(ir: GraphIR) -> set:
+    """Stride-2 3x3 convs run as stride-1 2x2 WINDOW convs over the space-to-depth view of their
+    input (four phase planes (row parity, column parity) at half resolution, written by the
+    input's producing conv), so their A operand comes in bulk copies instead of TMA im2col loads
+    of one 16-byte pixel per row. Needs a conv-produced input of whole chunks and even size;
+    IXB_S2D=0 keeps the im2col loads (the IM2COL kernel stays covered by the tests that way)."""
+    if os.environ.get("IXB_S2D", "1") == "0":
+        return set()
+    produced = {layer.output for layer in ir.conv_layers()}
+    out = set()
+    for layer in ir.conv_layers():
+        if layer.k != 3 or layer.stride != 2 or len(layer.inputs) != 1:
+            continue
+        s = layer.inputs[0]
+        t = ir.tensors[s.tensor]
+        if (s.tensor in produced and not s.up2 and s.block_offset == 0 and s.blocks * 8 == t.channels
+                and t.channels % 16 == 0 and t.height % 2 == 0 and t.width % 2 == 0
+                and 9 * (t.channels // 16) <= 300):   # <= 150 MMAs in the kernel's op table
+            out.add(layer.name)
+    return out
+
+
+def s2d_weight_piece(w: np.ndarray, chunks: int):
+    """(chunk, tap) -> [cout, 16] weights of a 3x3 stride-2 conv run over the space-to-depth view:
+    chunk c is phase (ry, rx) = divmod(c // chunks, 2) of input chunk c % chunks, tap t of the 2x2 is
+    (dy, dx) = (t // 2 - 1, t % 2 - 1). Input row 2y + ky - 1 is phase 1, one row back, for ky = 0,
+    phase 0 for ky = 1 and phase 1 for ky = 2 (columns alike); pairs the 3x3 never reads are zero."""
+    def k_of(d, r):
+        if d == -1:
+            return 0 if r == 1 else None
+        return 1 if r == 0 else 2
+
+    def piece(chunk, tap):
+        ry, rx = divmod(chunk // chunks, 2)
+        c = chunk % chunks
+        ky, kx = k_of(tap // 2 - 1, ry), k_of(tap % 2 - 1, rx)
+        if ky is None or kx is None:
+            return np.zeros((w.shape[0], 16), dtype=np.int8)
+        return np.ascontiguousarray(w[:, 16 * c:16 * c + 16, ky, kx])
+    return piece
 
 
 def conv_mode(layer: ConvLayer, ir: GraphIR, upsampled: frozenset = frozenset()) -> int:
@@ -152,6 +197,11 @@ def choose_cp(mode: int, k: int, cin: int) -> int:
     if mode == L.MODE_STEM:
         return 2
     pairs = (cin + 31) // 32
+    if mode == L.MODE_WINDOW and k == 2:
+        # the 2x2 space-to-depth form: 9 of its 16 (phase, tap) pairs carry weights, so a K-block of
+        # one chunk pair may hold a single MMA; two pairs per K-block measured 15-25 % faster on the
+        # 40x40 and 20x20 layers (>= 256 view channels) and slower on the 160x160 one
+        return 2 if cin >= 256 else 1
     if (mode == L.MODE_WINDOW and k == 3) or mode == L.MODE_IM2COL:
         return 1    # 3x3: a K-block already carries the MMAs of 9 (window) or 3 (im2col) taps per pair
     return 4 if pairs >= 4 else (2 if pairs >= 2 else 1)
@@ -164,7 +214,7 @@ def _core_layout(b: np.ndarray) -> np.ndarray:
 
 
 def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule,
-                 cin_map: Optional[np.ndarray] = None) -> np.ndarray:
+                 cin_map: Optional[np.ndarray] = None, s2d: bool = False) -> np.ndarray:
     """Weights of every n-tile as the schedule's MMAs' [n_tile][32] K-slices, each in the UMMA
     core-matrix layout; a slice's two 16-byte K-halves are the (chunk, tap) of the MMA's halves.
     ``cin_map`` places input channel i at stored channel cin_map[i] (inputs padded to whole chunks);
@@ -186,6 +236,8 @@ def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule,
 
         def piece(chunk, tap):
             return stem[tap]
+    elif s2d:
+        piece = s2d_weight_piece(w, nchunks)
     else:
         if cin_map is None:
             cin_map = np.arange(cin)
@@ -355,6 +407,26 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
         plane = plane_stride(max_batch, h, w, guard)
         base = alloc(pad16(t.channels) // 16 * plane) + guard * 16
         stores_up2[name] = Store(base, plane, 0, pad16(t.channels), h, w, guard)
+    # the space-to-depth views of the stride-2 convs' inputs (see s2d_convs)
+    s2d_layers = s2d_convs(ir)
+    s2d_src = {layer.inputs[0].tensor for layer in ir.conv_layers() if layer.name in s2d_layers}
+    stores_s2d: Dict[str, Store] = {}
+    for name in sorted(s2d_src):
+        t = ir.tensors[name]
+        h, w = t.height // 2, t.width // 2
+        guard = plane_guard(w)
+        plane = plane_stride(max_batch, h, w, guard)
+        base = alloc(4 * pad16(t.channels) // 16 * plane) + guard * 16
+        stores_s2d[name] = Store(base, plane, 0, 4 * pad16(t.channels), h, w, guard)
+    # a tensor read by nothing but its space-to-depth consumers is stored only in that view
+    readers: Dict[str, List[str]] = {}
+    for layer in ir.layers:
+        ins = layer.inputs if isinstance(layer, ConvLayer) else [layer.input]
+        for s in ins:
+            readers.setdefault(s.tensor, []).append(layer.name)
+        if isinstance(layer, ConvLayer) and layer.residual is not None:
+            readers.setdefault(layer.residual.tensor, []).append(layer.name)
+    s2d_only = frozenset(n for n in s2d_src if n not in heads and all(r in s2d_layers for r in readers[n]))
     head_offsets: Dict[str, int] = {}
     eb = 0
     for name, _ in ir.outputs:
@@ -378,19 +450,23 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
 
     convs: List[ConvPlan] = []
     for layer in ir.conv_layers():
-        mode = conv_mode(layer, ir, frozenset(upsampled))
+        s2d = layer.name in s2d_layers
+        mode = L.MODE_WINDOW if s2d else conv_mode(layer, ir, frozenset(upsampled))
         cin_p = 3 if mode == L.MODE_STEM else sum(_seg_channels(ir, sg) for sg in layer.inputs)
         cout_p = pad16(layer.cout)
         n_tile = choose_n_tile(cout_p)
-        cp = choose_cp(mode, layer.k, cin_p)
+        k, stride, cin_k = (2, 1, 4 * cin_p) if s2d else (layer.k, layer.stride, cin_p)
+        cp = choose_cp(mode, k, cin_k)
         shape = L.ConvDesc()
-        shape.mode, shape.k, shape.stride, shape.n_tile, shape.cp = mode, layer.k, layer.stride, n_tile, cp
-        shape.cin, shape.cout = cin_p, cout_p
+        shape.mode, shape.k, shape.stride, shape.n_tile, shape.cp = mode, k, stride, n_tile, cp
+        shape.s2d_in = int(s2d)
+        shape.cin, shape.cout = cin_k, cout_p
         shape.nseg = 1
-        shape.seg[0].channels = cin_p
+        shape.seg[0].channels = cin_k
         sched = L.conv_schedule(shape)
-        wp = pack_weights(layer, mode, n_tile, sched, None if mode == L.MODE_STEM else _cin_map(ir, layer))
-        cpl = ConvPlan(layer, mode, n_tile, cp, wp)
+        wp = pack_weights(layer, mode, n_tile, sched, None if mode == L.MODE_STEM or s2d else _cin_map(ir, layer),
+                          s2d=s2d)
+        cpl = ConvPlan(layer, mode, n_tile, cp, wp, s2d=s2d)
         cpl.schedule = sched
         cpl.w_rel = cput(wp)
         bias = np.zeros(cout_p, dtype=np.int32)
@@ -437,6 +513,12 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
         d.cout = pad16(layer.cout)
         d.n_tile, d.cp = cpl.n_tile, cpl.cp
         segs = _merge_segments([seg_of(s) for s in layer.inputs])
+        if cpl.s2d:
+            st = stores_s2d[layer.inputs[0].tensor]
+            d.k, d.stride, d.s2d_in = 2, 1, 1
+            d.in_h, d.in_w = st.height, st.width
+            d.cin = st.channels
+            segs = [L.Segment(st.offset, st.plane_stride, 0, st.channels, st.height, st.width, 0, st.guard)]
         if len(segs) > L.MAX_SEGS:
             raise ValueError(f"{layer.name}: more than {L.MAX_SEGS} input segments")
         d.nseg = len(segs)
@@ -461,10 +543,14 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
             d.egress_channels = layer.cout
         else:
             d.out = whole(layer.output)
-        if layer.output in stores_up2:
-            st = stores_up2[layer.output]
-            d.has_out_up2 = 1
-            d.out_up2 = L.Segment(st.offset, st.plane_stride, 0, st.channels, st.height, st.width, 0, st.guard)
+        second = stores_up2.get(layer.output) or stores_s2d.get(layer.output)
+        if second is not None:
+            if layer.output in stores_up2 and layer.output in stores_s2d:
+                raise ValueError(f"{layer.output}: both an upsampled and a space-to-depth copy")
+            d.out2_kind = (L.OUT2_UP2 if layer.output in stores_up2 else
+                           L.OUT2_S2D_ONLY if layer.output in s2d_only else L.OUT2_S2D)
+            d.out2 = L.Segment(second.offset, second.plane_stride, 0, second.channels, second.height,
+                               second.width, 0, second.guard)
         cpl.desc = d
         plan_convs.append(d)
         index_of[layer.name] = i
@@ -501,7 +587,8 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
                       input_store=input_store, egress_offset=egress_offset, egress_image_bytes=egress_image_bytes,
                       head_offsets=head_offsets, stores=stores, convs=convs, pools=pools, ops=ops,
                       const_offset=const_offset, const_blob=blob, extra_images_offsets=extra_images,
-                      extra_egress_offsets=extra_egress, upsampled_stores=stores_up2)
+                      extra_egress_offsets=extra_egress, upsampled_stores=stores_up2, s2d_stores=stores_s2d,
+                      s2d_only=s2d_only)
 
 
 def _merge_segments(segs: List[L.Segment]) -> List[L.Segment]:

@@ -360,7 +360,20 @@ class GraphSession:
             raw = self.arena[st.offset:st.offset + b * (st.height + 2) * (st.width + 4) * 8].cpu().numpy()
             v = raw.view(np.int8).reshape(b, st.height + 2, st.width + 4, 8)[:, 1:-1, 1:st.width + 1, :3]
             return (v.astype(np.int16) + 128).astype(np.uint8).transpose(0, 3, 1, 2)
-        st = self.plan.stores[name]
+        if name in self.plan.s2d_only:
+            # stored only as its space-to-depth view: phase (ry, rx) = divmod(chunk group, 2)
+            v = self._read_store(self.plan.s2d_stores[name], b)
+            n = v.shape[1] // 4
+            t = self.ir.tensors[name]
+            out = np.empty((b, n, 2 * v.shape[2], 2 * v.shape[3]), dtype=np.uint8)
+            for ph in range(4):
+                ry, rx = divmod(ph, 2)
+                out[:, :, ry::2, rx::2] = v[:, ph * n:(ph + 1) * n]
+            return out[:, :t.channels]
+        return self._read_store(self.plan.stores[name], b)[:, :self.ir.tensors[name].channels]
+
+    def _read_store(self, st, b: int) -> np.ndarray:
+        """uint8 [b, channels, H, W] of one stored tensor (the halo ring dropped)."""
         P = (st.height + 2) * (st.width + 2)
         out = np.empty((b, st.channels, st.height, st.width), dtype=np.uint8)
         for c in range(st.channels // 16):
@@ -368,7 +381,7 @@ class GraphSession:
             raw = self.arena[o:o + b * P * 16].cpu().numpy().view(np.int8).reshape(b, st.height + 2, st.width + 2, 16)
             v = raw[:, 1:-1, 1:-1, :].transpose(0, 3, 1, 2)
             out[:, 16 * c:16 * c + 16] = (v.astype(np.int16) + 128).astype(np.uint8)
-        return out[:, :self.ir.tensors[name].channels]     # stored zero channels past a ragged tail
+        return out     # stored zero channels past a ragged tail are sliced off by the caller
 
     def trace(self, batch: int, iters: int = 3):
         """Device timeline of a graph run: per op (start, inputs ready, end) in microseconds from the

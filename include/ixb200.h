@@ -45,7 +45,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 6
+#define IXB_API_VERSION 7
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -77,6 +77,15 @@ typedef struct ixb_segment {
   int32_t guard;         /* zero pixels before and after every plane */
 } ixb_segment;
 
+/* ixb_conv_desc.out2_kind: a second copy of a conv's output, in the layout its consumer reads. */
+#define IXB_OUT2_NONE 0
+#define IXB_OUT2_UP2 1      /* nearest-2x upsampled: pixel (y, x) also at (2y + dy, 2x + dx), dy, dx in {0, 1};
+                               out2 is (2 out_h) x (2 out_w) x cout */
+#define IXB_OUT2_S2D 2      /* space-to-depth for a stride-2 3x3 consumer: pixel (y, x), chunk c also at
+                               (y / 2, x / 2), chunk ((y % 2) * 2 + x % 2) * (cout / 16) + c; out2 is
+                               (out_h / 2) x (out_w / 2) x 4 cout (out_h, out_w even) */
+#define IXB_OUT2_S2D_ONLY 3 /* the space-to-depth copy only (the tensor has no other consumer): `out` unused */
+
 typedef struct ixb_conv_desc {
   int32_t mode;        /* IXB_MODE_* */
   int32_t k, stride;   /* 1 or 3; 1 or 2 */
@@ -85,6 +94,10 @@ typedef struct ixb_conv_desc {
   int32_t cin, cout;   /* stored channels (whole 16-channel chunks); cout multiple of 16 */
   int32_t n_tile;      /* output channels per CTA (multiple of 16, <= 256, divides cout) */
   int32_t cp;          /* 32-channel pairs of input per K-block */
+  int32_t s2d_in;      /* 1: a stride-2 3x3 conv run as a stride-1 2x2 WINDOW conv (k = 2) over the
+                          space-to-depth view of its input (IXB_OUT2_S2D): in_h x in_w = out_h x out_w,
+                          cin = 4 x the original channels, phase-major; taps at (-1, -1), (-1, 0),
+                          (0, -1), (0, 0); only the 9 (phase, tap) pairs of the 3x3 are scheduled */
   int32_t nseg;
   ixb_segment seg[IXB_MAX_SEGS];
   uint64_t w_offset;   /* packed weights: [cout/n_tile][kblocks][block bytes] */
@@ -102,12 +115,13 @@ typedef struct ixb_conv_desc {
   int32_t egress_channels;      /* channels of the head in the egress (<= cout; 0: cout). A head
                                    whose channel count is not a multiple of 16 computes cout =
                                    the next multiple with zero weights and writes only these. */
-  int32_t has_out_up2;          /* 1: also write the output nearest-2x upsampled into out_up2 */
-  ixb_segment out_up2;          /* (2 out_h) x (2 out_w) x cout view, written when has_out_up2: every
-                                   output pixel (y, x) also lands at (2y + dy, 2x + dx), dy, dx in
-                                   {0, 1}, so a consumer of the upsampled tensor (the top-down path's
-                                   concat) reads it as a plain tensor with bulk copies instead of
-                                   gathering 16-byte rows. Not with out_nchw. */
+  int32_t out2_kind;            /* IXB_OUT2_*: the up2 copy lets the top-down path's concat read the
+                                   upsampled tensor as a plain tensor with bulk copies instead of
+                                   gathering 16-byte rows; the space-to-depth copy turns the stride-2
+                                   3x3 convs into stride-1 2x2 convs fed by bulk copies. Not with
+                                   out_nchw. */
+  int32_t reserved3;
+  ixb_segment out2;             /* the second copy's view (out2_kind != IXB_OUT2_NONE) */
 } ixb_conv_desc;
 
 typedef struct ixb_pool_desc {  /* SPPF: out_k = pool5^k(in), k = 1..3, pad -128 */

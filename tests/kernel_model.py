@@ -45,7 +45,7 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
     MT = info["mt"]
     TM = 128 * MT
     mode, k, stride = d.mode, d.k, d.stride
-    pad = k // 2
+    pad = 1 if d.s2d_in else k // 2   # the 2x2 space-to-depth taps reach one pixel back
     H, W, Ho, Wo = d.in_h, d.in_w, d.out_h, d.out_w
     n_tile = d.n_tile
     segs, chunk = [], 0
@@ -56,7 +56,7 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
     Wm = Wo + 1 if mode in (L.MODE_STEM, L.MODE_IM2COL) else Wo    # one spare column per output row
     if mode == L.MODE_WINDOW:
         win_origin = pad * (W + 2) + pad
-        rowsA = TM + 2 * win_origin
+        rowsA = TM + (1 if d.s2d_in else 2) * win_origin
         m_total = batch * (H + 2) * (W + 2)
     else:
         win_origin = 0
@@ -172,10 +172,19 @@ def run_conv(arena: np.ndarray, d, batch: int, arena_bytes: int) -> None:
                 if not d.out_nchw:
                     ob = d.out.offset + d.out.chunk_offset * d.out.plane_stride
                     for j in range(n_tile // 16):
+                        if d.out2_kind == L.OUT2_S2D_ONLY:
+                            break
                         a0 = ob + (nt * n_tile // 16 + j) * d.out.plane_stride + opix[rr] * 16
                         arena[a0:a0 + 16] = out[rr, 16 * j:16 * j + 16]
-                    if d.has_out_up2:  # the 2x2-replicated copy at twice the resolution
-                        u = d.out_up2
+                    if d.out2_kind in (L.OUT2_S2D, L.OUT2_S2D_ONLY):  # the space-to-depth view
+                        u = d.out2
+                        ph = (oy[rr] % 2) * 2 + ox[rr] % 2
+                        pix = img[rr] * (u.height + 2) * (u.width + 2) + (oy[rr] // 2 + 1) * (u.width + 2) + ox[rr] // 2 + 1
+                        for j in range(n_tile // 16):
+                            a0 = u.offset + (ph * (d.cout // 16) + nt * n_tile // 16 + j) * u.plane_stride + pix * 16
+                            arena[a0:a0 + 16] = out[rr, 16 * j:16 * j + 16]
+                    if d.out2_kind == L.OUT2_UP2:  # the 2x2-replicated copy at twice the resolution
+                        u = d.out2
                         W2, P2 = u.width + 2, (u.height + 2) * (u.width + 2)
                         for j in range(n_tile // 16):
                             base = u.offset + (nt * n_tile // 16 + j) * u.plane_stride

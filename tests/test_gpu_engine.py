@@ -41,6 +41,23 @@ def test_small_graph_every_tensor(imgsz, batch, sms, monkeypatch):
 
 
 @pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 3)])
+def test_im2col_stride2_every_tensor(imgsz, batch, monkeypatch):
+    """IXB_S2D=0: the stride-2 3x3 convs load their A operand with TMA im2col (IM2COL mode) instead
+    of bulk copies of their input's space-to-depth view; every tensor must still equal the oracle."""
+    monkeypatch.setenv("IXB_S2D", "0")
+    sess = InferenceSession.from_spec("yolov8n", imgsz=imgsz, max_batch=batch)
+    assert sum(c.mode == L.MODE_IM2COL for c in sess.plan.convs) == 6
+    imgs = random_images(batch, imgsz, seed=7 + imgsz)
+    out = sess.run_yolo_monolithic(imgs)
+    for b in range(batch):
+        ref = O.run_image(sess.ir, imgs[b])
+        for name in ref:
+            assert np.array_equal(sess.read_tensor(name, batch=batch)[b], ref[name]), f"image {b} tensor {name}"
+        assert np.array_equal(out["raw_output"][b], O.egress_int8(sess.ir, ref))
+    sess.close()
+
+
+@pytest.mark.parametrize("imgsz,batch", [(64, 2), (96, 3)])
 def test_gathered_upsample_every_tensor(imgsz, batch, monkeypatch):
     """IXB_UP2=0: the concat convs read the upsampled tensors through per-row gathers (GATHER mode)
     instead of the producers' 2x2-replicated copies; every tensor must still equal the oracle."""

@@ -58,7 +58,9 @@ def test_valid_descriptor_passes_checks_until_launch():
 def test_host_checks_refuse_out_of_bounds_descriptors(mutate, needle):
     dp, descs = _desc()
     lib = L.load()
-    d = L.ConvDesc.from_buffer_copy(descs[5])
+    # a WINDOW 1x1 (the first conv past the stem block) with a plain output view
+    d = L.ConvDesc.from_buffer_copy(next(x for x in descs[5:] if x.mode == L.MODE_WINDOW and x.k == 1
+                                         and x.out2_kind == L.OUT2_NONE and not x.out_nchw))
     mutate(d, dp.arena_bytes)
     rc = lib.ixb_conv_layer(C.byref(d), C.c_void_p(0x10000), dp.arena_bytes, 2, None)
     assert rc == -1

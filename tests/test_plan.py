@@ -20,6 +20,16 @@ def test_kernel_model_matches_oracle(imgsz, batch, sms, monkeypatch):
     assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
 
 
+def test_kernel_model_with_im2col_stride2_matches_oracle(monkeypatch):
+    """IXB_S2D=0: the stride-2 3x3 convs load their A operand with TMA im2col (IM2COL mode)."""
+    monkeypatch.setenv("IXB_S2D", "0")
+    ir = build_yolov8("n", imgsz=64)
+    dp = build_plan(ir, 2)
+    assert sum(c.mode == L.MODE_IM2COL for c in dp.convs) == 6 and not dp.s2d_stores
+    imgs = random_images(2, 64, seed=13)
+    assert np.array_equal(KM.run_network(dp, imgs), O.run_batch_egress(ir, imgs))
+
+
 def test_kernel_model_with_gathered_upsample_matches_oracle(monkeypatch):
     """IXB_UP2=0: the concat convs gather the upsampled tensors (GATHER mode)."""
     monkeypatch.setenv("IXB_UP2", "0")
@@ -115,8 +125,13 @@ def test_plan_storage_is_disjoint_and_aligned(variant):
         t = ir.tensors[name]
         assert (st.height, st.width) == (2 * t.height, 2 * t.width)
         spans[st.offset - st.guard * 16] = st.channels // 16 * st.plane_stride
-    assert not any(c.mode == L.MODE_GATHER for c in dp.convs)
-    assert sum(c.desc.has_out_up2 for c in dp.convs) == 2
+    assert not any(c.mode in (L.MODE_GATHER, L.MODE_IM2COL) for c in dp.convs)
+    assert sum(c.desc.out2_kind == L.OUT2_UP2 for c in dp.convs) == 2
+    assert sum(c.s2d for c in dp.convs) == 6 and len(dp.s2d_stores) == 6
+    for name, st in dp.s2d_stores.items():
+        t = ir.tensors[name]
+        assert (st.height, st.width, st.channels) == (t.height // 2, t.width // 2, 4 * t.channels)
+        spans[st.offset - st.guard * 16] = st.channels // 16 * st.plane_stride
     iv = sorted(spans.items())
     for (a, n), (b, _) in zip(iv, iv[1:]):
         assert a + n <= b
