@@ -548,7 +548,7 @@ __device__ __forceinline__ void store_piece(const ConvParams& p, const RowInfo& 
 // KIND picks the layer's epilogue once per kernel, so that the hot loop holds only its own path:
 // with every path inlined in one loop (table, linear, residual, NCHW head) the 1x1 layers measured
 // ~20 % slower.
-enum : int { kEpiTable = 0, kEpiLinear = 1, kEpiResidual = 2, kEpiGeneric = 3, kEpiTableS2D = 4 };
+enum : int { kEpiTable = 0, kEpiLinear = 1, kEpiResidual = 2, kEpiGeneric = 3, kEpiTableS2D = 4, kEpiLinearNCHW = 5 };
 template <int MODE, int EW, int KIND>
 __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t tacc, int m0, int ntile, int warp,
                                                    int lane, const uint8_t* lut_s, const int4* bias4_s, int it,
@@ -585,6 +585,24 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     tmem_fill16(c, bias4_s + j * 4);
     if (KIND == kEpiGeneric) {
       if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
+    } else if (KIND == kEpiLinearNCHW) {
+      // a detect head: linear, int8 NCHW into the egress; a warp's 32 rows are 32 pixels, so each
+      // byte store covers up to 32 consecutive bytes of one channel plane
+      const uint4 o = epilogue16_linear(v, scale);
+      if (r.valid) {
+        int8_t* e = p.egress + (long long)r.img * p.egress_img + r.oy * p.Wo + r.ox;
+        const long long plane = (long long)p.Ho * p.Wo;
+        const int8_t* ob = reinterpret_cast<const int8_t*>(&o);
+        const int c0 = ntile * p.n_tile + j * 16;
+        if (c0 + 16 <= p.egress_ch) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) e[(c0 + i) * plane] = ob[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < p.egress_ch) e[(c0 + i) * plane] = ob[i];
+        }
+      }
     } else if (KIND == kEpiTableS2D) {
       // table layer whose consumer is a stride-2 conv: its space-to-depth copy, and the plain
       // output unless nothing else reads it
@@ -753,7 +771,9 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   } else {
     // ------------------------------------------------------------ epilogue
     grid_dep_wait();  // residual reads and output writes follow the previous layer
-    if (!p.out_nchw && !p.has_res && !linear && p.out2_kind >= IXB_OUT2_S2D)
+    if (p.out_nchw && !p.has_res && linear)
+      epilogue_role<MODE, EW, kEpiLinearNCHW>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
+    else if (!p.out_nchw && !p.has_res && !linear && p.out2_kind >= IXB_OUT2_S2D)
       epilogue_role<MODE, EW, kEpiTableS2D>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
     else if (p.out_nchw || p.out2_kind)
       epilogue_role<MODE, EW, kEpiGeneric>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
