@@ -19,7 +19,7 @@ IXB_ERR_INVALID = -1
 IXB_ERR_TIMEOUT = -3
 IXB_ERR_UNSUPPORTED = -5
 MAX_SEGS = 4
-API_VERSION = 7
+API_VERSION = 8
 MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 OUT2_NONE, OUT2_UP2, OUT2_S2D, OUT2_S2D_ONLY = 0, 1, 2, 3
@@ -64,9 +64,9 @@ class Plan(C.Structure):
                 ("convs", C.POINTER(ConvDesc)), ("pools", C.POINTER(PoolDesc)), ("ops", C.POINTER(Op)),
                 ("images_offset", C.c_uint64), ("input_lut_offset", C.c_uint64), ("input", Segment),
                 ("egress_offset", C.c_uint64), ("egress_image_bytes", C.c_uint64), ("arena_bytes", C.c_uint64),
-                ("extra_slots", C.c_int32), ("reserved", C.c_int32),
+                ("extra_slots", C.c_int32), ("input_s2d", C.c_int32),
                 ("extra_images_offset", C.c_uint64 * MAX_EXTRA_SLOTS),
-                ("extra_egress_offset", C.c_uint64 * MAX_EXTRA_SLOTS)]
+                ("extra_egress_offset", C.c_uint64 * MAX_EXTRA_SLOTS), ("input_s2d_view", Segment)]
 
 
 class IxbError(RuntimeError):

@@ -174,7 +174,7 @@ int build_schedule(const ixb_conv_desc& d, int cin_chunks, std::vector<SchedKB>&
     // the second read one row on in the same slot
     for (int ky = 0; ky < 3; ++ky) ops.push_back(SchedOp{ky, 0, 2 * ky, ky, 0, 2 * ky + 1});
     push_kb(0, 1, 0, 3, 0);
-  } else if (d.mode == IXB_MODE_WINDOW && d.s2d_in) {
+  } else if (d.mode == IXB_MODE_WINDOW && d.s2d_in == 1) {
     // Space-to-depth view of a stride-2 3x3 conv: chunk c is phase (ry, rx) = (p / 2, p % 2),
     // p = c / (cin_chunks / 4); tap t of the 2x2 is (dy, dx) = (t / 2 - 1, t % 2 - 1). Output (y, x)
     // tap (ky, kx) of the 3x3 reads input (2y + ky - 1, 2x + kx - 1): phase 1 one pixel back for
@@ -286,8 +286,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   if (d.mode < IXB_MODE_WINDOW || d.mode > IXB_MODE_IM2COL) return bad("unknown conv mode");
   if (d.s2d_in) {
     // a stride-2 3x3 conv over the space-to-depth view: a stride-1 2x2 conv, output size = view size
-    if (d.mode != IXB_MODE_WINDOW || d.k != 2 || d.stride != 1 || d.cin % 64)
-      return bad("a space-to-depth input needs a WINDOW 2x2 stride-1 conv over 4 x whole chunks");
+    if (d.mode != IXB_MODE_WINDOW || d.k != 2 || d.stride != 1 || (d.s2d_in == 1 ? d.cin % 64 : d.cin != 16) ||
+        d.s2d_in < 1 || d.s2d_in > 2)
+      return bad("a space-to-depth input needs a WINDOW 2x2 stride-1 conv over 4 x whole chunks (the image: one chunk)");
     if (d.out_h != d.in_h || d.out_w != d.in_w) return bad("a space-to-depth conv keeps the view's size");
   } else {
     if (!(d.k == 1 || d.k == 3) || !(d.stride == 1 || d.stride == 2)) return bad("k must be 1 or 3, stride 1 or 2");
@@ -748,6 +749,25 @@ int launch_quantize(const uint8_t* images, const int8_t* lut, int batch, int h, 
   return 0;
 }
 
+// The image's space-to-depth view (ixb_plan.input_s2d): from the uint8 images (the ingress), or
+// from the 8-byte-pixel store `in8` (after a letterbox). `view` is the plan's input_s2d_view.
+int launch_ingress_s2d(const uint8_t* images, const int8_t* in8, const int8_t* lut, int batch, int h, int w,
+                       uint8_t* arena, const ixb_segment& view, cudaStream_t st) {
+  if (h % 2 || w % 4) return fail(IXB_ERR_INVALID, "the space-to-depth ingress needs even height, width % 4 == 0");
+  const long long items = (long long)batch * (h / 2) * (w / 2);
+  if (items >= (1LL << 31)) return fail(IXB_ERR_INVALID, "too many pixels for one ingress launch");
+  const int blocks = (int)std::min<long long>((items + 255) / 256, 148LL * 16);
+  const int W2 = w / 2 + 2, P2 = (h / 2 + 2) * W2;
+  int8_t* out = reinterpret_cast<int8_t*>(arena + view.offset);
+  const FastDiv fw = make_fastdiv((uint32_t)(w / 2)), fh = make_fastdiv((uint32_t)(h / 2));
+  if (images)
+    quantize_images_s2d_kernel<<<blocks, 256, 0, st>>>(images, lut, batch, h, w, fw, fh, P2, W2, out);
+  else
+    repack_s2d_kernel<<<blocks, 256, 0, st>>>(in8, batch, h, w, fw, fh, P2, W2, out);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
 // ---------------------------------------------------------------- int8 GEMM
 PFN_cuTensorMapEncodeTiled_v12000 tiled_encoder(std::string& err) {
   static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
@@ -1091,6 +1111,10 @@ struct ixb_session {
   }
 
   int enqueue_ingress(int batch, int slot = 0) {
+    if (plan.input_s2d)
+      return launch_ingress_s2d(arena + images_at(slot), nullptr,
+                                reinterpret_cast<const int8_t*>(arena + plan.input_lut_offset), batch, plan.img_h,
+                                plan.img_w, arena, plan.input_s2d_view, stream);
     return launch_quantize(arena + images_at(slot), reinterpret_cast<const int8_t*>(arena + plan.input_lut_offset),
                            batch, plan.img_h, plan.img_w, reinterpret_cast<int8_t*>(arena + plan.input.offset),
                            stream);
@@ -1270,6 +1294,13 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
   else if (check_seg(plan->input, B, s->arena_bytes, true, "stem input", err)) bad = fail(IXB_ERR_INVALID, err);
   else if (plan->input.height != plan->img_h || plan->input.width != plan->img_w || plan->input.channels != 3)
     bad = fail(IXB_ERR_INVALID, "stem input view must be the img_h x img_w 3-channel image");
+  else if (plan->input_s2d &&
+           (plan->img_h % 2 || check_seg(plan->input_s2d_view, B, s->arena_bytes, false, "stem space-to-depth input", err)))
+    bad = fail(IXB_ERR_INVALID, plan->img_h % 2 ? "a space-to-depth stem input needs an even image height" : err.c_str());
+  else if (plan->input_s2d &&
+           (plan->input_s2d_view.height != plan->img_h / 2 || plan->input_s2d_view.width != plan->img_w / 2 ||
+            plan->input_s2d_view.channels != 16 || plan->input_s2d_view.up2 || plan->input_s2d_view.chunk_offset))
+    bad = fail(IXB_ERR_INVALID, "the stem's space-to-depth view must be one chunk of (img_h/2) x (img_w/2)");
   else if (plan->egress_offset + (unsigned long long)B * plan->egress_image_bytes > s->arena_bytes)
     bad = fail(IXB_ERR_INVALID, "egress outside the arena");
   else if (plan->extra_slots < 0 || plan->extra_slots > IXB_MAX_EXTRA_SLOTS)
@@ -1818,9 +1849,15 @@ int ixb_session_letterbox(ixb_session* s, const uint8_t* frames, int batch, int 
   const ixb_plan& pl = s->plan;
   const int row = pl.img_w + 4;
   int8_t* base = reinterpret_cast<int8_t*>(s->arena + pl.input.offset) + ((long long)row + 1) * 8;
-  return ixb_letterbox_frames(frames, batch, src_w, src_h, src_stride, frame_bytes,
-                              reinterpret_cast<const int8_t*>(s->arena + pl.input_lut_offset), base, pl.img_w, pl.img_h,
-                              row, (uint64_t)(pl.img_h + 2) * row * 8, letterbox, s->stream);
+  if (int r = ixb_letterbox_frames(frames, batch, src_w, src_h, src_stride, frame_bytes,
+                                   reinterpret_cast<const int8_t*>(s->arena + pl.input_lut_offset), base, pl.img_w,
+                                   pl.img_h, row, (uint64_t)(pl.img_h + 2) * row * 8, letterbox, s->stream))
+    return r;
+  // a stem over the space-to-depth view reads the letterboxed image repacked into that view
+  if (pl.input_s2d)
+    return launch_ingress_s2d(nullptr, reinterpret_cast<const int8_t*>(s->arena + pl.input.offset), nullptr, batch,
+                              pl.img_h, pl.img_w, s->arena, pl.input_s2d_view, s->stream);
+  return 0;
 }
 
 int ixb_quantize_images(const uint8_t* images, const int8_t* lut, int batch, int h, int w, int8_t* padded_nhwc4,

@@ -73,6 +73,7 @@ class ConvPlan:
     w_packed: np.ndarray
     desc: Optional[object] = None
     s2d: bool = False  # a stride-2 3x3 run as a 2x2 WINDOW conv over its input's space-to-depth view
+    stem_s2d: bool = False  # the stem as a 2x2 WINDOW conv over the image's space-to-depth view
 
 
 @dataclass
@@ -99,6 +100,7 @@ class DevicePlan:
     upsampled_stores: Dict[str, Store] = field(default_factory=dict)  # 2x2 copies (upsampled_copies)
     s2d_stores: Dict[str, Store] = field(default_factory=dict)        # space-to-depth views (s2d_convs)
     s2d_only: frozenset = frozenset()  # tensors stored only as their space-to-depth view
+    input_s2d_store: Optional[Store] = None  # the image's space-to-depth view, when the stem reads it
     c_plan: object = None
     keep: list = field(default_factory=list)
 
@@ -144,6 +146,28 @@ def s2d_convs(ir: GraphIR) -> set:
                 and 9 * (t.channels // 16) <= 300):   # <= 150 MMAs in the kernel's op table
             out.add(layer.name)
     return out
+
+
+def _s2d_k(d: int, r: int) -> Optional[int]:
+    """The 3x3 tap (ky or kx) that a 2x2 space-to-depth tap d in {-1, 0} reads in phase r, or None:
+    input row 2y + ky - 1 is phase 1 one row back for ky = 0, phase 0 for 1, phase 1 for 2."""
+    if d == -1:
+        return 0 if r == 1 else None
+    return 1 if r == 0 else 2
+
+
+def stem_s2d_piece(w: np.ndarray):
+    """(chunk 0, tap) -> [cout, 16] weights of the stem over the image's space-to-depth view: byte
+    ph * 3 + c of a pixel is channel c of phase ph = 2 ry + rx; bytes 12..15 are zero."""
+    def piece(chunk, tap):
+        out = np.zeros((w.shape[0], 16), dtype=np.int8)
+        for ph in range(4):
+            ry, rx = divmod(ph, 2)
+            ky, kx = _s2d_k(tap // 2 - 1, ry), _s2d_k(tap % 2 - 1, rx)
+            if ky is not None and kx is not None:
+                out[:, 3 * ph:3 * ph + 3] = w[:, :, ky, kx]
+        return out
+    return piece
 
 
 def s2d_weight_piece(w: np.ndarray, chunks: int):
@@ -214,7 +238,7 @@ def _core_layout(b: np.ndarray) -> np.ndarray:
 
 
 def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule,
-                 cin_map: Optional[np.ndarray] = None, s2d: bool = False) -> np.ndarray:
+                 cin_map: Optional[np.ndarray] = None, s2d: bool = False, stem_s2d: bool = False) -> np.ndarray:
     """Weights of every n-tile as the schedule's MMAs' [n_tile][32] K-slices, each in the UMMA
     core-matrix layout; a slice's two 16-byte K-halves are the (chunk, tap) of the MMA's halves.
     ``cin_map`` places input channel i at stored channel cin_map[i] (inputs padded to whole chunks);
@@ -224,7 +248,9 @@ def pack_weights(layer: ConvLayer, mode: int, n_tile: int, schedule,
         w = np.concatenate([w, np.zeros((pad16(w.shape[0]) - w.shape[0],) + w.shape[1:], np.int8)])
     cout, cin, k, _ = w.shape
     nchunks = (cin + 15) // 16
-    if mode == L.MODE_STEM:
+    if stem_s2d:
+        piece = stem_s2d_piece(w)
+    elif mode == L.MODE_STEM:
         # tap 2*ky + p is the 16-byte pixel pair p of image row ky: image pixel 2x + 2p + j (j = 0, 1)
         # at kx = 2p + j, bytes 8*j + ci; kx = 3 and channels 3..7 are zero
         stem = np.zeros((6, cout, 16), dtype=np.int8)
@@ -382,6 +408,13 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
     extra_images = tuple(alloc(max_batch * 3 * H * W) for _ in range(pipeline_depth - 1))
     input_lut_offset = alloc(256)
     input_store = Store(alloc(max_batch * (H + 2) * (W + 4) * 8), 0, 0, 3, H, W, 0)
+    # the stem over the image's space-to-depth view (one 16-byte chunk: 4 phases x 3 channels),
+    # fed by bulk copies instead of TMA im2col loads of 16-byte pixel pairs
+    input_s2d_store = None
+    if os.environ.get("IXB_S2D", "1") != "0" and H % 2 == 0 and W % 4 == 0:
+        guard = plane_guard(W // 2)
+        plane = plane_stride(max_batch, H // 2, W // 2, guard)
+        input_s2d_store = Store(alloc(plane) + guard * 16, plane, 0, 16, H // 2, W // 2, guard)
     stores: Dict[str, Store] = {}
     for grp in _storage_groups(ir, heads):
         infos = [ir.tensors[t] for t in grp]
@@ -451,22 +484,25 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
     convs: List[ConvPlan] = []
     for layer in ir.conv_layers():
         s2d = layer.name in s2d_layers
-        mode = L.MODE_WINDOW if s2d else conv_mode(layer, ir, frozenset(upsampled))
-        cin_p = 3 if mode == L.MODE_STEM else sum(_seg_channels(ir, sg) for sg in layer.inputs)
+        stem_s2d = input_s2d_store is not None and layer.inputs[0].tensor == ir.input
+        mode = L.MODE_WINDOW if s2d or stem_s2d else conv_mode(layer, ir, frozenset(upsampled))
+        cin_p = 3 if mode == L.MODE_STEM or stem_s2d else sum(_seg_channels(ir, sg) for sg in layer.inputs)
         cout_p = pad16(layer.cout)
         n_tile = choose_n_tile(cout_p)
-        k, stride, cin_k = (2, 1, 4 * cin_p) if s2d else (layer.k, layer.stride, cin_p)
+        k, stride, cin_k = ((2, 1, 4 * cin_p) if s2d else (2, 1, 16) if stem_s2d else
+                            (layer.k, layer.stride, cin_p))
         cp = choose_cp(mode, k, cin_k)
         shape = L.ConvDesc()
         shape.mode, shape.k, shape.stride, shape.n_tile, shape.cp = mode, k, stride, n_tile, cp
-        shape.s2d_in = int(s2d)
+        shape.s2d_in = 2 if stem_s2d else int(s2d)
         shape.cin, shape.cout = cin_k, cout_p
         shape.nseg = 1
         shape.seg[0].channels = cin_k
         sched = L.conv_schedule(shape)
-        wp = pack_weights(layer, mode, n_tile, sched, None if mode == L.MODE_STEM or s2d else _cin_map(ir, layer),
-                          s2d=s2d)
-        cpl = ConvPlan(layer, mode, n_tile, cp, wp, s2d=s2d)
+        wp = pack_weights(layer, mode, n_tile, sched,
+                          None if mode == L.MODE_STEM or s2d or stem_s2d else _cin_map(ir, layer),
+                          s2d=s2d, stem_s2d=stem_s2d)
+        cpl = ConvPlan(layer, mode, n_tile, cp, wp, s2d=s2d, stem_s2d=stem_s2d)
         cpl.schedule = sched
         cpl.w_rel = cput(wp)
         bias = np.zeros(cout_p, dtype=np.int32)
@@ -513,6 +549,12 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
         d.cout = pad16(layer.cout)
         d.n_tile, d.cp = cpl.n_tile, cpl.cp
         segs = _merge_segments([seg_of(s) for s in layer.inputs])
+        if cpl.stem_s2d:
+            st = input_s2d_store
+            d.k, d.stride, d.s2d_in = 2, 1, 2
+            d.in_h, d.in_w = st.height, st.width
+            d.cin = 16
+            segs = [L.Segment(st.offset, st.plane_stride, 0, 16, st.height, st.width, 0, st.guard)]
         if cpl.s2d:
             st = stores_s2d[layer.inputs[0].tensor]
             d.k, d.stride, d.s2d_in = 2, 1, 1
@@ -588,7 +630,7 @@ def build_plan(ir: GraphIR, max_batch: int, pipeline_depth: int = 3, branches: O
                       head_offsets=head_offsets, stores=stores, convs=convs, pools=pools, ops=ops,
                       const_offset=const_offset, const_blob=blob, extra_images_offsets=extra_images,
                       extra_egress_offsets=extra_egress, upsampled_stores=stores_up2, s2d_stores=stores_s2d,
-                      s2d_only=s2d_only)
+                      s2d_only=s2d_only, input_s2d_store=input_s2d_store)
 
 
 def _merge_segments(segs: List[L.Segment]) -> List[L.Segment]:
@@ -623,6 +665,10 @@ def c_plan(dp: DevicePlan) -> L.Plan:
     p.input_lut_offset = dp.input_lut_offset
     s = dp.input_store
     p.input = L.Segment(s.offset, 0, 0, 3, s.height, s.width, 0, 0)
+    if dp.input_s2d_store is not None:
+        v = dp.input_s2d_store
+        p.input_s2d = 1
+        p.input_s2d_view = L.Segment(v.offset, v.plane_stride, 0, 16, v.height, v.width, 0, v.guard)
     p.egress_offset = dp.egress_offset
     p.egress_image_bytes = dp.egress_image_bytes
     p.arena_bytes = dp.arena_bytes

@@ -355,6 +355,13 @@ class GraphSession:
             head = [n for n, t in self.ir.outputs if t == name][0]
             h = self.layout.unpack(self.read_heads(batch=b))[head]
             return (h.astype(np.int16) + 128).astype(np.uint8)
+        if name == self.ir.input and self.plan.input_s2d_store is not None:
+            v = self._read_store(self.plan.input_s2d_store, b)     # [b, 16, H/2, W/2], byte ph * 3 + c
+            out = np.empty((b, 3, 2 * v.shape[2], 2 * v.shape[3]), dtype=np.uint8)
+            for ph in range(4):
+                ry, rx = divmod(ph, 2)
+                out[:, :, ry::2, rx::2] = v[:, 3 * ph:3 * ph + 3]
+            return out
         if name == self.ir.input:
             st = self.plan.input_store
             raw = self.arena[st.offset:st.offset + b * (st.height + 2) * (st.width + 4) * 8].cpu().numpy()

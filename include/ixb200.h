@@ -45,7 +45,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 7
+#define IXB_API_VERSION 8
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -94,7 +94,9 @@ typedef struct ixb_conv_desc {
   int32_t cin, cout;   /* stored channels (whole 16-channel chunks); cout multiple of 16 */
   int32_t n_tile;      /* output channels per CTA (multiple of 16, <= 256, divides cout) */
   int32_t cp;          /* 32-channel pairs of input per K-block */
-  int32_t s2d_in;      /* 1: a stride-2 3x3 conv run as a stride-1 2x2 WINDOW conv (k = 2) over the
+  int32_t s2d_in;      /* 2: the stem over the image's space-to-depth view (ixb_plan.input_s2d: one
+                          chunk holding all four phases; taps as for 1).
+                          1: a stride-2 3x3 conv run as a stride-1 2x2 WINDOW conv (k = 2) over the
                           space-to-depth view of its input (IXB_OUT2_S2D): in_h x in_w = out_h x out_w,
                           cin = 4 x the original channels, phase-major; taps at (-1, -1), (-1, 0),
                           (0, -1), (0, 0); only the 9 (phase, tap) pairs of the 3x3 are scheduled */
@@ -160,9 +162,15 @@ typedef struct ixb_plan {
   /* Further staging/egress pairs (same sizes as images_offset / egress_offset) for the
    * ixb_session_submit ring, which is 1 + extra_slots deep; slot 0 is the pair above. */
   int32_t extra_slots;          /* 0 .. IXB_MAX_EXTRA_SLOTS */
-  int32_t reserved;
+  int32_t input_s2d;            /* 1: the stem reads input_s2d_view, the image's space-to-depth view
+                                   (16-byte pixels: byte ((y % 2) * 2 + x % 2) * 3 + c holds channel c
+                                   of image pixel (y, x), bytes 12..15 zero; (H/2) x (W/2), one chunk,
+                                   halo ring and guards like any tensor), which the ingress writes;
+                                   `input` then only stages ixb_session_letterbox's output, repacked
+                                   into the view before the run */
   uint64_t extra_images_offset[IXB_MAX_EXTRA_SLOTS];
   uint64_t extra_egress_offset[IXB_MAX_EXTRA_SLOTS];
+  ixb_segment input_s2d_view;
 } ixb_plan;
 
 typedef struct ixb_session ixb_session;

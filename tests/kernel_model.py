@@ -234,6 +234,16 @@ def run_network(dp: DevicePlan, images: np.ndarray) -> np.ndarray:
         base = s.offset + b * n
         v = arena[base:base + n].view(np.int8).reshape(s.height + 2, s.width + 4, 8)
         v[1:-1, 1:s.width + 1, :3] = lut[images[b].transpose(1, 2, 0)]
+    if dp.input_s2d_store is not None:   # the image's space-to-depth view: byte ph * 3 + c
+        v2 = dp.input_s2d_store
+        P2 = (v2.height + 2) * (v2.width + 2)
+        for b in range(batch):
+            q = lut[images[b]]                                   # [3, H, W]
+            view = arena[v2.offset + b * P2 * 16:v2.offset + (b + 1) * P2 * 16].view(np.int8)
+            view = view.reshape(v2.height + 2, v2.width + 2, 16)
+            for ph in range(4):
+                ry, rx = divmod(ph, 2)
+                view[1:-1, 1:-1, 3 * ph:3 * ph + 3] = q[:, ry::2, rx::2].transpose(1, 2, 0)
     convs = [c.desc for c in dp.convs]
     for kind, idx in dp.ops:
         if (kind & 0xFF) == L.OP_CONV:
