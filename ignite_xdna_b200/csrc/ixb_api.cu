@@ -754,16 +754,19 @@ int launch_quantize(const uint8_t* images, const int8_t* lut, int batch, int h, 
 int launch_ingress_s2d(const uint8_t* images, const int8_t* in8, const int8_t* lut, int batch, int h, int w,
                        uint8_t* arena, const ixb_segment& view, cudaStream_t st) {
   if (h % 2 || w % 4) return fail(IXB_ERR_INVALID, "the space-to-depth ingress needs even height, width % 4 == 0");
-  const long long items = (long long)batch * (h / 2) * (w / 2);
+  const long long items = (long long)batch * (h / 2) * (w / 2);  // view pixels
   if (items >= (1LL << 31)) return fail(IXB_ERR_INVALID, "too many pixels for one ingress launch");
-  const int blocks = (int)std::min<long long>((items + 255) / 256, 148LL * 16);
   const int W2 = w / 2 + 2, P2 = (h / 2 + 2) * W2;
   int8_t* out = reinterpret_cast<int8_t*>(arena + view.offset);
-  const FastDiv fw = make_fastdiv((uint32_t)(w / 2)), fh = make_fastdiv((uint32_t)(h / 2));
-  if (images)
-    quantize_images_s2d_kernel<<<blocks, 256, 0, st>>>(images, lut, batch, h, w, fw, fh, P2, W2, out);
-  else
-    repack_s2d_kernel<<<blocks, 256, 0, st>>>(in8, batch, h, w, fw, fh, P2, W2, out);
+  const FastDiv fh = make_fastdiv((uint32_t)(h / 2));
+  if (images) {  // one thread per pair of view pixels
+    const int blocks = (int)std::min<long long>((items / 2 + 255) / 256, 148LL * 16);
+    quantize_images_s2d_kernel<<<blocks, 256, 0, st>>>(images, lut, batch, h, w, make_fastdiv((uint32_t)(w / 4)),
+                                                       fh, P2, W2, out);
+  } else {
+    const int blocks = (int)std::min<long long>((items + 255) / 256, 148LL * 16);
+    repack_s2d_kernel<<<blocks, 256, 0, st>>>(in8, batch, h, w, make_fastdiv((uint32_t)(w / 2)), fh, P2, W2, out);
+  }
   IXB_CUDA(cudaGetLastError());
   return 0;
 }

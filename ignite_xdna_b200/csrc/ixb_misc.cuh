@@ -114,9 +114,10 @@ __global__ void __launch_bounds__(256) letterbox_kernel(const __grid_constant__ 
 // Image ingress into its space-to-depth view (the stem's input when the stem runs as a 2x2
 // WINDOW conv): uint8 pixels [B][3][H][W] -> 16-byte pixels of the (H/2) x (W/2) view, byte
 // ph * 3 + c = lut[channel c of image pixel (2 sy + ry, 2 sx + rx)], ph = 2 ry + rx, bytes 12..15
-// zero. One thread per view pixel: two-pixel loads from each channel's two rows. The lookup is
-// the model input's QuantizeLinear (graph_session.py:144-149 input_lut). `out` is padded pixel 0
-// of image 0; P2 / W2 are the view's padded pixels per image and padded width.
+// zero. One thread per two neighbouring view pixels: four-pixel (4-byte) loads from each channel's
+// two rows (W % 4 == 0). The lookup is the model input's QuantizeLinear (graph_session.py:144-149
+// input_lut). `out` is padded pixel 0 of image 0; P2 / W2 are the view's padded pixels per image
+// and padded width; fd_w divides by W / 4.
 __global__ void __launch_bounds__(256) quantize_images_s2d_kernel(const uint8_t* __restrict__ img,
                                                                    const int8_t* __restrict__ lut, int B, int H,
                                                                    int W, FastDiv fd_w, FastDiv fd_h, int P2, int W2,
@@ -126,29 +127,31 @@ __global__ void __launch_bounds__(256) quantize_images_s2d_kernel(const uint8_t*
   for (int i = threadIdx.x; i < 256; i += blockDim.x) lut_s[i] = (uint8_t)lut[i];
   __syncthreads();
   grid_dep_wait();
-  const int hw = W / 2, hh = H / 2;
-  const int total = B * hh * hw;
+  const int hq = W / 4, hh = H / 2;  // view pixel pairs per row, view rows
+  const int total = B * hh * hq;
   const long long plane = (long long)H * W;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int row = (int)fdiv((uint32_t)i, fd_w);  // b * hh + sy
-    const int sx = i - row * hw;
+    const int k = i - row * hq;                     // view pixels 2k, 2k + 1
     const int b = (int)fdiv((uint32_t)row, fd_h), sy = row - b * hh;
-    const uint8_t* src = img + (long long)b * 3 * plane + (long long)(2 * sy) * W + 2 * sx;
-    uint32_t q[12];  // q[ph * 3 + c]
+    const uint8_t* src = img + (long long)b * 3 * plane + (long long)(2 * sy) * W + 4 * k;
+    uint32_t q[2][12];  // q[view pixel][ph * 3 + c]
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
 #pragma unroll
       for (int ry = 0; ry < 2; ++ry) {
-        const uint32_t two = __ldg(reinterpret_cast<const uint16_t*>(src + c * plane + ry * W));
-        q[(2 * ry) * 3 + c] = lut_s[two & 0xFF];
-        q[(2 * ry + 1) * 3 + c] = lut_s[two >> 8];
+        const uint32_t four = __ldg(reinterpret_cast<const uint32_t*>(src + c * plane + ry * W));
+#pragma unroll
+        for (int j = 0; j < 4; ++j)  // image column 4k + j: view pixel j / 2, phase column j % 2
+          q[j >> 1][(2 * ry + (j & 1)) * 3 + c] = lut_s[(four >> (8 * j)) & 0xFF];
       }
     }
-    const uint32_t w0 = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
-    const uint32_t w1 = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
-    const uint32_t w2 = q[8] | (q[9] << 8) | (q[10] << 16) | (q[11] << 24);
-    *reinterpret_cast<uint4*>(out + ((long long)b * P2 + (long long)(sy + 1) * W2 + sx + 1) * 16) =
-        make_uint4(w0, w1, w2, 0u);
+    uint4* dst = reinterpret_cast<uint4*>(out + ((long long)b * P2 + (long long)(sy + 1) * W2 + 2 * k + 1) * 16);
+#pragma unroll
+    for (int v = 0; v < 2; ++v)
+      dst[v] = make_uint4(q[v][0] | (q[v][1] << 8) | (q[v][2] << 16) | (q[v][3] << 24),
+                          q[v][4] | (q[v][5] << 8) | (q[v][6] << 16) | (q[v][7] << 24),
+                          q[v][8] | (q[v][9] << 8) | (q[v][10] << 16) | (q[v][11] << 24), 0u);
   }
 }
 
