@@ -731,9 +731,14 @@ int launch_pool(const PoolLaunch& L, cudaStream_t st) {
   static bool configured = false;
   if (!configured) {
     IXB_CUDA(cudaFuncSetAttribute(sppf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    IXB_CUDA(cudaFuncSetAttribute(sppf_pixel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     configured = true;
   }
-  IXB_CUDA(launch_dependent(sppf_kernel, L.grid, dim3(256), L.smem, st, true, L.p));
+  const int n = L.p.H * L.p.W;
+  if (n <= 1024)  // one thread per pixel
+    IXB_CUDA(launch_dependent(sppf_pixel_kernel, L.grid, dim3((unsigned)((n + 31) / 32 * 32)), L.smem, st, true, L.p));
+  else
+    IXB_CUDA(launch_dependent(sppf_kernel, L.grid, dim3(256), L.smem, st, true, L.p));
   return 0;
 }
 

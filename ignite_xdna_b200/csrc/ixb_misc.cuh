@@ -242,4 +242,50 @@ __global__ void __launch_bounds__(256) sppf_kernel(const __grid_constant__ PoolP
   }
 }
 
+// SPPF for planes of at most 1024 pixels (YOLOv8's 20x20 at 640): the same three pools, one
+// thread per pixel (blockDim = n rounded up to whole warps), so each thread splits its pixel index
+// once instead of dividing for every pixel of every pass.
+__global__ void __launch_bounds__(1024) sppf_pixel_kernel(const __grid_constant__ PoolParams p) {
+  extern __shared__ uint4 pool_px[];
+  const int W = p.W, H = p.H, n = H * W;
+  uint4* cur = pool_px;
+  uint4* tmp = cur + n;
+  uint4* nxt = tmp + n;
+  const int t = threadIdx.x;
+  const bool on = t < n;
+  const int y = on ? t / W : 0, x = on ? t - (t / W) * W : 0;
+  const int chunk = blockIdx.x, img = blockIdx.y;
+  const int W2 = W + 2;
+  const int8_t* src = p.in.base + (long long)chunk * p.in.plane + (long long)img * p.in.P * 16;
+  grid_dep_launch();
+  grid_dep_wait();
+  if (on) cur[t] = *reinterpret_cast<const uint4*>(src + ((y + 1) * W2 + x + 1) * 16);
+  __syncthreads();
+  for (int k = 0; k < 3; ++k) {
+    if (on) {
+      uint4 m = cur[t];
+      if (x >= 1) m = vmax16(m, cur[t - 1]);
+      if (x >= 2) m = vmax16(m, cur[t - 2]);
+      if (x + 1 < W) m = vmax16(m, cur[t + 1]);
+      if (x + 2 < W) m = vmax16(m, cur[t + 2]);
+      tmp[t] = m;
+    }
+    __syncthreads();
+    if (on) {
+      uint4 m = tmp[t];
+      if (y >= 1) m = vmax16(m, tmp[t - W]);
+      if (y >= 2) m = vmax16(m, tmp[t - 2 * W]);
+      if (y + 1 < H) m = vmax16(m, tmp[t + W]);
+      if (y + 2 < H) m = vmax16(m, tmp[t + 2 * W]);
+      nxt[t] = m;
+      int8_t* dst = const_cast<int8_t*>(p.out[k].base) + (long long)chunk * p.out[k].plane + (long long)img * p.out[k].P * 16;
+      *reinterpret_cast<uint4*>(dst + ((y + 1) * W2 + x + 1) * 16) = m;
+    }
+    __syncthreads();
+    uint4* s = cur;
+    cur = nxt;
+    nxt = s;
+  }
+}
+
 }  // namespace ixb
