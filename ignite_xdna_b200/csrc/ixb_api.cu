@@ -388,11 +388,11 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   // (2 * MT * n_tile <= 512 columns) and still leaves two tiles per SM to spread.
   const int sms = sm_budget > 0 ? std::min(sm_budget, sm_count()) : sm_count();
   int mt = 1;
-  // WINDOW convs may take 8 blocks (1024 rows; the planner's plane guards cover that reach): for
-  // the 16-channel stem this took 85 to 72 us. IM2COL/STEM loads carry at most 1024 rows with
-  // their halo and the GATHER row tables hold 512, so those stay at 4.
-  for (int cand : {8, 4, 2}) {
-    if (cand == 8 && d.mode != IXB_MODE_WINDOW) continue;
+  // WINDOW convs may take 8 or 16 blocks (up to 2048 rows; the planner's plane guards cover that
+  // reach): for the 16-channel stem this took 85 to 69 us. IM2COL/STEM loads carry at most 1024
+  // rows with their halo and the GATHER row tables hold 512, so those stay at 4.
+  for (int cand : {16, 8, 4, 2}) {
+    if (cand >= 8 && d.mode != IXB_MODE_WINDOW) continue;
     const long long tiles = (p.m_total + 128LL * cand - 1) / (128LL * cand);
     if (cand * d.n_tile <= 256 && tiles * ntiles >= 2LL * sms) {
       mt = cand;

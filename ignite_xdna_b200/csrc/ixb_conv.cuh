@@ -342,7 +342,7 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
   const uint64_t a_hi = ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
   const uint32_t a_base = smem_u32(smem + p.a_off) >> 4;
   const uint32_t w_base = smem_u32(smem);
-  const int mt_lg = __ffs(p.mt) - 1;  // mt is 1, 2, 4 or 8
+  const int mt_lg = __ffs(p.mt) - 1;  // mt is a power of two, 1 .. 16
   for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
     uint32_t c0 = (uint32_t)clock();
     mbar_wait(&acc_empty[acc], aph ^ 1);

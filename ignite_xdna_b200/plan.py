@@ -52,9 +52,9 @@ class Store:
 
 
 def plane_guard(width: int) -> int:
-    """Zero pixels around a plane: a window copy reaches up to a 1024-row tile plus one padded
+    """Zero pixels around a plane: a window copy reaches up to a 2048-row tile plus one padded
     row and pixel past the last image, and one padded row and pixel before the first."""
-    return 1024 + 2 * (width + 3) + 64
+    return 2048 + 2 * (width + 3) + 64
 
 
 def plane_stride(batch: int, height: int, width: int, guard: int) -> int:
