@@ -215,22 +215,100 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def layer_algorithmic(ir, L, batch):
+    """Algorithmic bytes and int8 ops of one conv launch: every input activation read once, the
+    output (and a residual) once, the weights and bias once; 2 ops per MAC."""
+    t = ir.tensors[L.output]
+    nbytes = 0
+    for s in L.inputs:
+        src = ir.tensors[s.tensor]
+        if s.tensor == ir.input:
+            nbytes += batch * 3 * src.height * src.width
+        else:
+            nbytes += batch * s.blocks * 8 * src.height * src.width
+    if L.residual is not None:
+        nbytes += batch * L.cout * t.height * t.width
+    nbytes += batch * L.cout * t.height * t.width + L.weights.size + 4 * L.cout
+    ops = 2 * batch * t.height * t.width * L.cout * L.cin * L.k * L.k
+    return nbytes, ops
+
+
 def conv_algorithmic(ir, batch):
-    """Per-step algorithmic bytes and int8 ops of the conv launches: every input activation
-    read once, every output written once, weights once; 2 ops per MAC."""
+    """Per-step algorithmic bytes and int8 ops of all conv launches."""
     nbytes = ops = 0
     for L in ir.conv_layers():
-        t = ir.tensors[L.output]
-        for s in L.inputs:
-            src = ir.tensors[s.tensor]
-            nbytes += batch * s.blocks * 8 * src.height * src.width if s.tensor != ir.input else 0
-        if L.inputs[0].tensor == ir.input:
-            nbytes += batch * 3 * ir.tensors[ir.input].height * ir.tensors[ir.input].width
-        if L.residual is not None:
-            nbytes += batch * L.cout * t.height * t.width
-        nbytes += batch * L.cout * t.height * t.width + L.weights.size + 4 * L.cout
-        ops += 2 * batch * t.height * t.width * L.cout * L.cin * L.k * L.k
+        b, o = layer_algorithmic(ir, L, batch)
+        nbytes += b
+        ops += o
     return nbytes, ops
+
+
+def per_layer_rows(sess, batch, trace, int8_peak_tops):
+    """One row per conv op from the in-graph trace (ready -> end, under programmatic dependent launch
+    and in the step's own order): microseconds, int8 TOP/s, tensor fraction, algorithmic GB/s."""
+    from ignite_xdna_b200 import _lib as L
+    rows = []
+    for (kind, idx), t in zip(sess.plan.ops, trace):
+        if (kind & 0xFF) != L.OP_CONV or t is None:
+            continue
+        layer = sess.plan.convs[idx].layer
+        nbytes, ops = layer_algorithmic(sess.ir, layer, batch)
+        us = max(t[2] - t[1], 1e-3)
+        tops = ops / (us * 1e-6) / 1e12
+        t_out = sess.ir.tensors[layer.output]
+        rows.append({"op": idx, "layer": layer.name, "k": layer.k, "stride": layer.stride, "cin": layer.cin,
+                     "cout": layer.cout, "out": f"{t_out.height}x{t_out.width}", "us": round(us, 2), "int8_tops": round(tops, 1),
+                     "tc_frac": round(tops / int8_peak_tops, 4),
+                     "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)})
+    return rows
+
+
+def copy_ceiling(sess, pinned_in, pinned_out, world, local, iters=5):
+    """Pure-copy calibration on every rank at once, no compute: the images' pinned H2D and the heads'
+    pinned D2H of one step, alone and together, on the session's copy streams. Returns aggregate
+    GB/s over all ranks (bytes of all ranks / the slowest rank's time) and the e2e images/s these
+    copies alone allow."""
+    import torch
+    dev = torch.device("cuda", local)
+    h_compute, h_h2d, h_d2h = sess.streams()
+    s_h2d = torch.cuda.ExternalStream(h_h2d, device=dev)
+    s_d2h = torch.cuda.ExternalStream(h_d2h, device=dev)
+    B = pinned_in.shape[0]
+    n_in = pinned_in.numel()
+    n_out = B * sess.out_bytes
+    dst_in = sess.arena[sess.plan.images_offset:sess.plan.images_offset + n_in]
+    src_out = sess.arena[sess.plan.egress_offset:sess.plan.egress_offset + n_out]
+    host_in = pinned_in.reshape(-1)
+    host_out = torch.from_numpy(pinned_out.reshape(-1)[:n_out]).view(torch.uint8)
+
+    def timed(h2d, d2h):
+        barrier(world)
+        torch.cuda.synchronize(local)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(s_h2d)
+        ev[2].record(s_d2h)
+        for _ in range(iters):
+            if h2d:
+                with torch.cuda.stream(s_h2d):
+                    dst_in.copy_(host_in, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s_d2h):
+                    host_out.copy_(src_out, non_blocking=True)
+        ev[1].record(s_h2d)
+        ev[3].record(s_d2h)
+        torch.cuda.synchronize(local)
+        ms = max(ev[0].elapsed_time(ev[1]) if h2d else 0.0, ev[2].elapsed_time(ev[3]) if d2h else 0.0)
+        barrier(world)
+        return max_over_ranks(ms, world, local) / iters
+
+    timed(True, True)                                     # warm-up
+    t_in, t_out, t_both = timed(True, False), timed(False, True), timed(True, True)
+    gbs = lambda nb, ms: round(world * nb / (ms * 1e-3) / 1e9, 1)  # noqa: E731
+    return {"h2d_gbs": gbs(n_in, t_in), "d2h_gbs": gbs(n_out, t_out),
+            "both_ms_per_step": round(t_both, 4), "h2d_bytes_per_rank": int(n_in), "d2h_bytes_per_rank": int(n_out),
+            "images_s_ceiling": round(world * B / (t_both * 1e-3), 1),
+            "note": "pinned host <-> HBM copies only, every rank at once, the session's copy streams; "
+                    "images_s_ceiling = what the images-in + heads-out copies alone allow"}
 
 
 # ---------------------------------------------------------------- arms
@@ -352,12 +430,15 @@ def run_gpu(args):
         ms_e2e = timed_e2e(args.steps)
     ms = max_over_ranks(ms, world, local)
     ms_e2e = max_over_ranks(ms_e2e, world, local)
-    # per-op device times (layer-by-layer launches with events on the session stream)
-    prof = sess.profile(B, iters=max(2, min(args.steps, 5)))
-    conv_ops = [i for i, (k, _) in enumerate(sess.plan.ops) if (k & 0xFF) == L.OP_CONV]
-    conv_ms = sum(prof[i] for i in conv_ops)
-    nbytes, nops = conv_algorithmic(sess.ir, B)
+    ceiling = copy_ceiling(sess, pinned_in, pinned_out[0], world, local)
+    # per-layer device times inside the step's own CUDA graph (programmatic dependent launch on):
+    # each conv from the moment its inputs were ready to its last CTA's end
     hbm_peak, bf16_peak, peak_kind = load_peaks()
+    trace = sess.trace(B, iters=3)
+    rows = per_layer_rows(sess, B, trace, 2 * bf16_peak)
+    conv_ms = sum(r["us"] for r in rows) * 1e-3
+    span_ms = max(t[2] for t in trace if t is not None) * 1e-3
+    nbytes, nops = conv_algorithmic(sess.ir, B)
     achieved_gbs = nbytes / (conv_ms * 1e-3) / 1e9
     int8_tops = nops / (conv_ms * 1e-3) / 1e12
     launches = sess.launches(B)
@@ -387,15 +468,23 @@ def run_gpu(args):
         "roofline": {"bound": "hbm", "kernel": "ixb::conv_kernel (all conv launches of one step)",
                      "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,
+                     "traffic_source": "profiles/conv_traffic.json: dram__bytes_read.sum + dram__bytes_write.sum "
+                                       "of the step's conv launches from one ncu capture (one pass)",
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-                     "algorithmic_bytes_per_step": int(nbytes), "conv_ms_per_step": round(conv_ms, 4),
+                     "algorithmic_bytes_per_step": int(nbytes),
+                     "conv_ms_per_step": round(conv_ms, 4),
+                     "conv_time_source": "sum over the step's conv launches of (last CTA end - inputs ready), "
+                                         "traced inside the step's CUDA graph (ixb_session_trace)",
+                     "traced_span_ms": round(span_ms, 4),
+                     "conv_ms_le_step": bool(conv_ms <= ms / args.steps),
                      "int8_tops": round(int8_tops, 1),
                      "int8_tc_frac": round(int8_tops / (2 * bf16_peak), 4),
                      "int8_tc_peak_note": f"2 x {peak_kind} dense bf16 burst ({bf16_peak} TF/s): int8 runs at twice "
                                           f"the bf16 rate on tcgen05"},
         "gpu_launches": int(launches * args.steps),
         "clocks": clocks.summary(),
-        "per_op_ms": [round(x, 4) for x in prof],
+        "copy_ceiling": ceiling,
+        "per_layer": rows,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

@@ -17,9 +17,10 @@ IXB_OK = 0
 ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
 IXB_ERR_INVALID = -1
 IXB_ERR_TIMEOUT = -3
+IXB_ERR_DEVICE = -4
 IXB_ERR_UNSUPPORTED = -5
 MAX_SEGS = 4
-API_VERSION = 8
+API_VERSION = 9
 MAX_EXTRA_SLOTS = 3
 MODE_WINDOW, MODE_GATHER, MODE_STEM, MODE_IM2COL = 0, 1, 2, 3
 OUT2_NONE, OUT2_UP2, OUT2_S2D, OUT2_S2D_ONLY = 0, 1, 2, 3
@@ -82,6 +83,7 @@ _SIGS = {
     "ixb_version": (C.c_int, []),
     "ixb_abi_sizes": (C.c_int, [C.POINTER(C.c_uint64), C.c_int]),
     "ixb_device_error": (C.c_int, [C.POINTER(C.c_int)]),
+    "ixb_check_wait_timeout": (C.c_int, [C.c_int, C.c_void_p]),
     "ixb_session_create": (C.c_int, [C.POINTER(Plan), C.c_int, C.c_void_p, C.c_uint64, C.POINTER(C.c_void_p)]),
     "ixb_session_destroy": (C.c_int, [C.c_void_p]),
     "ixb_session_arena": (C.c_void_p, [C.c_void_p]),

@@ -15,6 +15,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
+#include <set>
 #include <string>
 #include <thread>
 #include <utility>
@@ -53,6 +55,23 @@ constexpr int kSmemLimit = 227 * 1024;
 constexpr int kConvDynSmem = kSmemLimit - 256;  // the conv kernel holds its 256-byte table statically
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device): cudaFuncSetAttribute
+// applies to the current device's context only, so a process with sessions on several GPUs sets
+// it on each. Kernels of one signature share a function-pointer type, so the key is the address.
+template <typename Kern>
+int ensure_smem_limit(Kern kern, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  IXB_CUDA(cudaGetDevice(&dev));
+  const std::pair<const void*, int> key(reinterpret_cast<const void*>(kern), dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return 0;
+  IXB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert(key);
+  return 0;
+}
 
 // SMs the launch planner spreads tiles over: the current device's count (148 on B200), 148
 // when no device answers (host-side checks run without a GPU), or IXB_SM_COUNT when set
@@ -302,7 +321,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   if (d.cout % 16 || d.n_tile % 16 || d.n_tile < 16 || d.n_tile > 256 || d.cout % d.n_tile)
     return bad("cout and n_tile must be multiples of 16, n_tile <= 256 dividing cout");
   if (!(d.cp == 1 || d.cp == 2 || d.cp == 4)) return bad("cp must be 1, 2 or 4");
-  if (d.shift < 0 || d.shift > 16) return bad("shift outside [0, 16]");
+  // SRS shifts: the float path of the epilogue is exact for s <= 16 (and for s < 0, a left shift);
+  // larger s first reduce the accumulator exactly by s - 16 (a sticky bit keeps the rounding).
+  if (d.shift < -31 || d.shift > 47) return bad("shift outside [-31, 47]");
   ConvParams& p = L.p;
   memset(&p, 0, sizeof p);
   p.mode = d.mode;
@@ -391,9 +412,16 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   // WINDOW convs may take 8 or 16 blocks (up to 2048 rows; the planner's plane guards cover that
   // reach): for the 16-channel stem this took 85 to 69 us. IM2COL/STEM loads carry at most 1024
   // rows with their halo and the GATHER row tables hold 512, so those stay at 4.
+  // A WINDOW tile's last window reaches m_tiles * tile_rows + win_origin pixels into the planes: a
+  // candidate whose reach passes the smallest input guard is skipped, so views planned with smaller
+  // guards (1024 + 2 (W + 3) + 64 pixels) still build, with smaller tiles.
+  int min_guard = 0x7fffffff;
+  for (int i = 0; i < d.nseg; ++i) min_guard = std::min(min_guard, d.seg[i].guard);
+  const long long plane_px = (long long)batch * (d.in_h + 2) * (d.in_w + 2);
   for (int cand : {16, 8, 4, 2}) {
     if (cand >= 8 && d.mode != IXB_MODE_WINDOW) continue;
     const long long tiles = (p.m_total + 128LL * cand - 1) / (128LL * cand);
+    if (d.mode == IXB_MODE_WINDOW && tiles * 128LL * cand + p.win_origin > plane_px + min_guard) continue;
     if (cand * d.n_tile <= 256 && tiles * ntiles >= 2LL * sms) {
       mt = cand;
       break;
@@ -438,7 +466,8 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.wpack = arena + d.w_offset;
   p.bias = reinterpret_cast<const int32_t*>(arena + d.bias_offset);
   p.lut = reinterpret_cast<const int8_t*>(arena + d.lut_offset);
-  p.shift = d.shift;
+  p.shift = std::min(d.shift, 16);
+  p.pre_shift = std::max(d.shift - 16, 0);
   p.fd_P = make_fastdiv((uint32_t)((d.in_h + 2) * (d.in_w + 2)));
   p.fd_W2 = make_fastdiv((uint32_t)(d.in_w + 2));
   p.fd_hw = make_fastdiv((uint32_t)(d.out_h * p.Wm));
@@ -512,9 +541,10 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
     if (d.residual.height != d.out_h || d.residual.width != d.out_w || d.residual.channels != d.cout ||
         d.residual.up2)
       return bad("residual view must match the output");
+    // (t2 << lsh_m) + (r << lsh_r) stays below 2^24 in magnitude, where the float rounding is exact
     if (d.res_lsh_main < 0 || d.res_lsh_main > 16 || d.res_lsh_res < 0 || d.res_lsh_res > 16 ||
-        d.res_shift < 0 || d.res_shift > 16)
-      return bad("residual shifts outside [0, 16]");
+        d.res_shift < 0 || d.res_shift > 31)
+      return bad("residual shifts outside [0, 16] (left) or [0, 31] (rounding)");
     p.res = seg_dev(d.residual, arena, 0);
     p.res_lsh_m = d.res_lsh_main;
     p.res_lsh_r = d.res_lsh_res;
@@ -664,11 +694,7 @@ cudaError_t launch_dependent(void (*kern)(KArgs...), dim3 grid, dim3 block, int 
 
 template <int MODE, int EW>
 int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    IXB_CUDA(cudaFuncSetAttribute(conv_kernel<MODE, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kConvDynSmem));
-    configured = true;
-  }
+  if (int r = ensure_smem_limit(conv_kernel<MODE, EW>, kConvDynSmem)) return r;
   IXB_CUDA(launch_dependent(conv_kernel<MODE, EW>, L.grid, dim3(conv_threads(MODE, EW)), L.smem, st, L.pdl, L.p));
   return 0;
 }
@@ -732,12 +758,8 @@ int build_pool(const ixb_pool_desc& d, uint8_t* arena, uint64_t arena_bytes, int
 }
 
 int launch_pool(const PoolLaunch& L, cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    IXB_CUDA(cudaFuncSetAttribute(sppf_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-    IXB_CUDA(cudaFuncSetAttribute(sppf_pixel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-    configured = true;
-  }
+  if (int r = ensure_smem_limit(sppf_kernel, kSmemLimit)) return r;
+  if (int r = ensure_smem_limit(sppf_pixel_kernel, kSmemLimit)) return r;
   const int n = L.p.H * L.p.W;
   if (n <= 1024)  // one thread per pixel
     IXB_CUDA(launch_dependent(sppf_pixel_kernel, L.grid, dim3((unsigned)((n + 31) / 32 * 32)), L.smem, st, true, L.p));
@@ -887,11 +909,7 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
 
 template <int BSRC>
 int launch_gemm(GemmLaunch& L, cudaStream_t st) {
-  static bool attr = false;
-  if (!attr) {
-    IXB_CUDA(cudaFuncSetAttribute(gemm_kernel<8, BSRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-    attr = true;
-  }
+  if (int r = ensure_smem_limit(gemm_kernel<8, BSRC>, kSmemLimit)) return r;
   gemm_kernel<8, BSRC><<<L.grid, gemm_threads(8, BSRC), L.smem, st>>>(L.p);
   IXB_CUDA(cudaGetLastError());
   return 0;
@@ -1210,6 +1228,16 @@ int ixb_abi_sizes(uint64_t* sizes, int n) {
   return 0;
 }
 int ixb_version(void) { return IXB_API_VERSION; }
+
+int ixb_check_wait_timeout(int limit_us, void* stream) {
+  if (limit_us < 1 || limit_us > 2000000) return fail(IXB_ERR_INVALID, "limit_us outside [1, 2000000]");
+  if (int r = read_device_error()) return r;  // start from a clear flag
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bounded_wait_probe_kernel<<<1, 32, 0, st>>>(1000ull * (unsigned long long)limit_us);
+  IXB_CUDA(cudaGetLastError());
+  IXB_CUDA(cudaStreamSynchronize(st));
+  return read_device_error();
+}
 
 int ixb_device_error(int* flag) {
   unsigned int v = 0;
@@ -1794,11 +1822,7 @@ int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, u
   p.out_score = scores;
   p.out_class = classes;
   p.out_count = counts;
-  static bool attr = false;
-  if (!attr) {
-    IXB_CUDA(cudaFuncSetAttribute(yolo_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem_bytes()));
-    attr = true;
-  }
+  if (int r = ensure_smem_limit(yolo_decode_kernel, decode_smem_bytes())) return r;
   yolo_decode_kernel<<<batch, kDecodeThreads, decode_smem_bytes(), static_cast<cudaStream_t>(stream)>>>(p);
   IXB_CUDA(cudaGetLastError());
   return 0;

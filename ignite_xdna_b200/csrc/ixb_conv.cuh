@@ -104,7 +104,8 @@ struct ConvParams {
   long long w_ntile_stride;
   const int32_t* bias;
   const int8_t* lut;
-  int shift;
+  int shift;      // SRS shift of the float path, at most 16 (negative: a left shift)
+  int pre_shift;  // shift - 16 when the layer's shift exceeds 16: an exact sticky pre-reduction first
   int has_res;
   SegDev res;
   int res_lsh_m, res_lsh_r, res_shift;
@@ -409,12 +410,22 @@ __device__ __forceinline__ void issue_mma(const ConvParams& p, uint8_t* smem, ui
 // |c| < 2^24 float(c) == c, and for |c| >= 2^24 both |c / 2^s| and |f * 2^-s| are >= 256, so the
 // exact and the float path saturate to the same end. Three instructions (plus a sign extension
 // of the byte) where the integer form takes seven; the epilogue's arithmetic bounds most layers.
+// A negative s (a left shift) is exact the same way: f * 2^|s| is c * 2^|s| for |c| < 2^24 and
+// saturates otherwise. Shifts above 16 go through pre_reduce first (the generic drain).
 __device__ __forceinline__ float pow2_neg(int s) { return __int_as_float((127 - s) << 23); }
 __device__ __forceinline__ int srs_s8(int c, float scale) {
   const float f = __int2float_rn(c) * scale;
   int r;
   asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(f));
   return (int)(int8_t)r;  // the s8 result, sign-extended whatever the register's upper bits hold
+}
+
+// acc / 2^k rounded to nearest even equals rne(c' / 2^16) for c' = (acc >> k) with the dropped
+// bits or'ed into bit 0 (a sticky bit below the rounding position): the float path then covers
+// SRS shifts of 16 + k exactly, whatever the accumulator's magnitude.
+__device__ __forceinline__ uint32_t pre_reduce(uint32_t v, int k) {
+  const int c = (int)v;  // k in [1, 31]
+  return (uint32_t)(c >> k) | ((v & ((1u << k) - 1u)) != 0u ? 1u : 0u);
 }
 
 // A linear layer (identity table, the detect heads): the same rounding, the int8 saturation done by
@@ -584,6 +595,10 @@ __device__ __forceinline__ void conv_epilogue_tile(const ConvParams& p, uint32_t
     // reset the drained columns to the bias for the next tile's MMAs, which all accumulate
     tmem_fill16(c, bias4_s + j * 4);
     if (KIND == kEpiGeneric) {
+      if (p.pre_shift) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = pre_reduce(v[i], p.pre_shift);
+      }
       if (r.valid) store_piece(p, r, ntile, j, v, x, lut_s, scale, rscale, linear);
     } else if (KIND == kEpiLinearNCHW) {
       // a detect head: linear, int8 NCHW into the egress; a warp's 32 rows are 32 pixels, so each
@@ -771,7 +786,9 @@ __global__ void __launch_bounds__(conv_threads(MODE, EW), 1) conv_kernel(const _
   } else {
     // ------------------------------------------------------------ epilogue
     grid_dep_wait();  // residual reads and output writes follow the previous layer
-    if (p.out_nchw && !p.has_res && linear)
+    if (p.pre_shift)  // SRS shifts above 16: the generic drain, which pre-reduces exactly
+      epilogue_role<MODE, EW, kEpiGeneric>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
+    else if (p.out_nchw && !p.has_res && linear)
       epilogue_role<MODE, EW, kEpiLinearNCHW>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);
     else if (!p.out_nchw && !p.has_res && !linear && p.out2_kind >= IXB_OUT2_S2D)
       epilogue_role<MODE, EW, kEpiTableS2D>(p, acc_full, acc_empty, tmem, ntile, warp, lane, lut_s, bias4_s, linear);

@@ -288,4 +288,17 @@ __global__ void __launch_bounds__(1024) sppf_pixel_kernel(const __grid_constant_
   }
 }
 
+// Self-check of the bounded waits: one thread waits on an mbarrier that nothing arrives at, with a
+// limit of limit_ns; the wait gives up, raises DEV_ERR_WAIT_TIMEOUT in the device flag and the
+// kernel returns normally (no trap, no fault: the context stays usable).
+__global__ void bounded_wait_probe_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_for(&bar, 0, limit_ns);
+}
+
 }  // namespace ixb

@@ -81,15 +81,18 @@ __device__ __forceinline__ bool wait_timed_out() {
 // wait has timed out, later waits give up at once, so a stuck launch ends after one time limit.
 // The clock and the flag (a global load) are checked every 16th retry only, so a warp that keeps
 // retrying costs the working warps few issue slots and no memory traffic.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15) == 0 && (global_ns() - t0 > kWaitLimitNs || wait_timed_out())) break;
+    if ((i & 15) == 0 && (global_ns() - t0 > limit_ns || wait_timed_out())) break;
   }
   set_dev_error(DEV_ERR_WAIT_TIMEOUT);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------- programmatic dependent launch

@@ -45,7 +45,7 @@ extern "C" {
 #define IXB_ERR_UNSUPPORTED -5
 
 #define IXB_MAX_SEGS 4
-#define IXB_API_VERSION 8
+#define IXB_API_VERSION 9
 
 /* Conv A-operand modes. */
 #define IXB_MODE_WINDOW 0   /* stride 1, same-resolution inputs: one bulk-copied pixel window per chunk */
@@ -74,7 +74,10 @@ typedef struct ixb_segment {
   int32_t height;        /* stored height (unpadded) */
   int32_t width;         /* stored width (unpadded) */
   int32_t up2;           /* 1: read as its nearest-2x upsampling */
-  int32_t guard;         /* zero pixels before and after every plane */
+  int32_t guard;         /* zero pixels before and after every plane: at least (W + 3) (one padded
+                            row and pixel) for a 3x3 WINDOW input; a WINDOW conv's tiles are sized so
+                            their window copies stay inside it, and guards of 2048 + 2 (W + 3) + 64
+                            (what ignite_xdna_b200.plan uses) allow the largest, 2048-row tiles */
 } ixb_segment;
 
 /* ixb_conv_desc.out2_kind: a second copy of a conv's output, in the layout its consumer reads. */
@@ -106,7 +109,8 @@ typedef struct ixb_conv_desc {
   uint64_t w_bytes;
   uint64_t bias_offset;/* int32[cout]: bias_q << e */
   uint64_t lut_offset; /* int8[256]: activation over t1 + 128 */
-  int32_t shift;       /* SRS shift, 0..16 */
+  int32_t shift;       /* SRS shift, -31..47 (negative: a saturating left shift; above 16 the
+                          epilogue first reduces the accumulator exactly, with a sticky bit) */
   int32_t has_residual;
   ixb_segment residual;
   int32_t res_lsh_main, res_lsh_res, res_shift;
@@ -335,6 +339,12 @@ int ixb_abi_sizes(uint64_t* sizes, int n);
 
 /* Device error flag (bounded waits that gave up); reading clears it. */
 int ixb_device_error(int* flag);
+/* Self-check of the failure path every kernel's waits share (no reference counterpart: the
+ * reference counts NPU dispatch timeouts on the host, c_api/ignite.cpp:929-945): one kernel waits
+ * on an mbarrier nothing arrives at, gives up after limit_us microseconds (at most 2 s), raises
+ * the device flag and returns. Waits for it on `stream` and returns IXB_ERR_DEVICE when the wait
+ * gave up as designed (the flag is then clear again and the context usable). */
+int ixb_check_wait_timeout(int limit_us, void* stream);
 
 #ifdef __cplusplus
 }

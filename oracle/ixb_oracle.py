@@ -75,8 +75,11 @@ def gather_input(tensors: Dict[str, np.ndarray], segments, height: int, width: i
     return np.concatenate(parts, axis=0)
 
 
-def conv_accumulate(layer, x: np.ndarray) -> np.ndarray:
-    """int64 accumulator Σ w·q + bias_acc over the ZP-padded input (graph_reference.py:40-55)."""
+def conv_accumulate(layer, x: np.ndarray, folded: bool = True) -> np.ndarray:
+    """int64 accumulator Σ w·q + bias_acc over the ZP-padded input (graph_reference.py:40-55).
+
+    folded=False gives the same sum in the signed domain t = q - 128 without the zero-point terms:
+    Σ w·t + (bias_q << e)."""
     cin, h, w = x.shape
     k, s, p = layer.k, layer.stride, layer.pad
     xp = np.full((cin, h + 2 * p, w + 2 * p), ZP, dtype=np.uint8)
@@ -89,11 +92,23 @@ def conv_accumulate(layer, x: np.ndarray) -> np.ndarray:
         for kx in range(k):
             patch = xp[:, ky:ky + s * ho:s, kx:kx + s * wo:s].astype(np.float64)
             acc += np.tensordot(wts[:, :, ky, kx], patch, axes=([1], [0]))
+    if not folded:
+        wsum = layer.weights.astype(np.int64).sum(axis=(1, 2, 3))
+        return acc.astype(np.int64) - ZP * wsum[:, None, None] + layer.bias_int8_domain()[:, None, None]
     return acc.astype(np.int64) + layer.bias_acc()[:, None, None]
 
 
 def conv_direct(layer, x: np.ndarray) -> np.ndarray:
-    """uint8 [Cin][H][W] -> uint8 [Cout][Ho][Wo]: SRS, saturate, activation table (graph_reference.py:56-61)."""
+    """uint8 [Cin][H][W] -> uint8 [Cout][Ho][Wo]: SRS, saturate, activation table (graph_reference.py:56-61).
+
+    A negative SRS shift (a layer whose output scale is finer than its input times weight scale)
+    cannot be expressed through the reference's folded bias, whose ``128 << shift`` term
+    (graph_ir.py:126-134) raises for it; there the oracle applies rne_shift's left-shift rule
+    (engine_emulator.py:149-158) to the signed-domain sum and adds the zero point after the
+    shift, which for every shift >= 0 is the folded rule exactly."""
+    if layer.shift_out < 0:
+        q = sat_u8(rne_shift(conv_accumulate(layer, x, folded=False), layer.shift_out) + ZP)
+        return layer.sigmoid.table[q] if layer.sigmoid is not None else q
     q = sat_u8(rne_shift(conv_accumulate(layer, x), layer.shift_out))
     if layer.sigmoid is not None:
         q = layer.sigmoid.table[q]

@@ -1,6 +1,6 @@
 """Golden fixtures for the GPU decode, from the reference's own decode.
 
-Run where the reference tree is present (``IXB_REFERENCE``, default /root/reference):
+Run with ``IXB_REFERENCE`` set to the reference checkout's root:
 ``python tests/golden/make_decode_golden.py``. It
 * loads the reference's ``pipelines/decode_native.py`` table builders by file path (its package
   and its native-library import stubbed out) and records sha256 of the tables they make for the
@@ -25,7 +25,13 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("IXB_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("IXB_REFERENCE", ""))
+
+
+def require_reference() -> None:
+    """The generators read the reference's own sources: IXB_REFERENCE must name its checkout."""
+    if not os.environ.get("IXB_REFERENCE") or not (REF / "src" / "ignite_xdna").is_dir():
+        raise SystemExit("set IXB_REFERENCE to the reference checkout's root (the tree holding src/ignite_xdna)")
 sys.path[:0] = [str(REPO), str(REPO / "oracle"), str(HERE)]
 
 import ixb_oracle as O  # noqa: E402
@@ -60,6 +66,7 @@ def sha(a) -> str:
 
 
 def main():
+    require_reference()
     subprocess.run(["sh", str(REPO / "oracle" / "build_ref.sh")], check=True)
     R = load_ref_tables()
     lib = ref_decode.load()

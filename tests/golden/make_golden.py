@@ -1,7 +1,7 @@
 """Generate the golden fixtures by running the reference's own integer reference.
 
-Run in a checkout where the reference tree is available (default ``/root/reference``,
-override with ``IXB_REFERENCE``):  ``python tests/golden/make_golden.py``.
+Run with ``IXB_REFERENCE`` set to the reference checkout's root:
+``IXB_REFERENCE=<checkout> python tests/golden/make_golden.py``.
 
 The reference's ``src/ignite_xdna/__init__.py`` and ``compiler/__init__.py`` import
 onnx-dependent modules eagerly and onnx is not installed, so the four modules this path
@@ -31,7 +31,13 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("IXB_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("IXB_REFERENCE", ""))
+
+
+def require_reference() -> None:
+    """The generators read the reference's own sources: IXB_REFERENCE must name its checkout."""
+    if not os.environ.get("IXB_REFERENCE") or not (REF / "src" / "ignite_xdna").is_dir():
+        raise SystemExit("set IXB_REFERENCE to the reference checkout's root (the tree holding src/ignite_xdna)")
 sys.path.insert(0, str(REPO))
 
 from ignite_xdna_b200 import build_yolov8, random_images  # noqa: E402
@@ -204,6 +210,7 @@ def make_pose(R):
 
 
 def main():
+    require_reference()
     R = load_reference()
     if "--pose" in sys.argv[1:]:
         make_pose(R)

@@ -1,6 +1,6 @@
 """Known answers for the uint8 x int4 operand pair, from the reference's own
 tools/int4_prefill_model.py Int4MmulReference (4x8 uint8 x 8x16 int4, packed two per byte):
-``python tests/golden/make_u8i4_golden.py`` (reference tree present) writes ``u8i4_kat.npz``."""
+``IXB_REFERENCE=<checkout> python tests/golden/make_u8i4_golden.py`` writes ``u8i4_kat.npz``."""
 from __future__ import annotations
 
 import os
@@ -10,10 +10,17 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("IXB_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("IXB_REFERENCE", ""))
+
+
+def require_reference() -> None:
+    """The generators read the reference's own sources: IXB_REFERENCE must name its checkout."""
+    if not os.environ.get("IXB_REFERENCE") or not (REF / "src" / "ignite_xdna").is_dir():
+        raise SystemExit("set IXB_REFERENCE to the reference checkout's root (the tree holding src/ignite_xdna)")
 
 
 def main():
+    require_reference()
     sys.path.insert(0, str(REF))     # tools/int4_prefill_model.py imports tools.xdna1_roofline
     try:
         import tools.int4_prefill_model as int4

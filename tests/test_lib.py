@@ -48,7 +48,8 @@ def test_valid_descriptor_passes_checks_until_launch():
     (lambda d, n: setattr(d.out, "offset", n), "arena"),
     (lambda d, n: setattr(d.seg[0], "offset", n - 64), "arena"),
     (lambda d, n: setattr(d, "w_offset", n), "weights"),
-    (lambda d, n: setattr(d, "shift", 17), "shift"),
+    (lambda d, n: setattr(d, "shift", 48), "shift"),
+    (lambda d, n: setattr(d, "shift", -32), "shift"),
     (lambda d, n: setattr(d.seg[0], "plane_stride", d.seg[0].plane_stride + 8), "misaligned"),
     (lambda d, n: setattr(d.seg[0], "guard", 0), "guard"),
     (lambda d, n: setattr(d.out, "chunk_offset", 10 ** 6), "arena"),
@@ -154,3 +155,20 @@ def test_w4a8_plan_and_refusals():
     x = C.c_void_p(16)
     assert lib.ixb_w4a8_gemv(x, x, x, x, 24, 128, None) == L.IXB_ERR_INVALID
     assert lib.ixb_w4a8_gemm(x, x, None, x, 16, 16, 128, None) == L.IXB_ERR_INVALID
+
+
+def test_window_tiles_shrink_to_fit_smaller_guards():
+    """A WINDOW view planned with smaller plane guards (the earlier rule, 1024 + 2 (W + 3) + 64)
+    still builds: the launch planner skips tile sizes whose window copies would pass the guard."""
+    ir = build_yolov8("n", imgsz=640)
+    dp = build_plan(ir, 64)
+    stem = L.ConvDesc.from_buffer_copy(dp.convs[0].desc)      # 16 channels: takes 2048-row tiles
+    full = L.conv_launch_info(stem, dp.arena_bytes, 64)
+    assert full["tile_rows"] == 2048
+    small = L.ConvDesc.from_buffer_copy(stem)
+    for i in range(small.nseg):
+        small.seg[i].guard = 1024 + 2 * (small.in_w + 3) + 64
+    info = L.conv_launch_info(small, dp.arena_bytes, 64)
+    assert info["tile_rows"] < 2048
+    end = info["m_tiles"] * info["tile_rows"] + (small.in_w + 2) + 1
+    assert end <= 64 * (small.in_h + 2) * (small.in_w + 2) + small.seg[0].guard
