@@ -30,6 +30,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "YOLOv8n int8 images/sec at 1/2/4/8 B200 (bs64/GPU, 640²); % int8 TC peak"
 UNIT = "images/s"
 L2_BYTES = 126 * 1024 * 1024
+DET_CAPACITY = 8400   # detections kept per image by the e2e detection stage: every anchor
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
@@ -386,23 +387,27 @@ def run_gpu(args):
         L.check(lib.ixb_session_run(sess._h, None, B, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
         L.check(lib.ixb_session_wait(sess._h, 60000))
 
-    def e2e_steps(k):
-        """k batches through GraphSession.run_async: pinned images in, pinned heads out, up to
+    def e2e_steps(k, detect=False):
+        """k batches through GraphSession.run_async: pinned images in, pinned heads out (or, with
+        ``detect``, the GPU decode + NMS after the network and only the detections out), up to
         ``depth`` in flight, so step i+1's H2D and step i-1's D2H overlap step i's compute."""
         hs = []
         for i in range(k):
-            hs.append(sess.run_async(pinned_in, out=pinned_out[i % depth]))
+            if detect:
+                hs.append(sess.run_async(pinned_in, detect=True))
+            else:
+                hs.append(sess.run_async(pinned_in, out=pinned_out[i % depth]))
             if len(hs) == depth:
                 hs.pop(0).wait(60000)
         for h in hs:
             h.wait(60000)
 
-    def timed_e2e(k):
+    def timed_e2e(k, detect=False):
         barrier(world)
         torch.cuda.synchronize(local)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s_h2d)
-        e2e_steps(k)
+        e2e_steps(k, detect)
         e1.record(s_d2h)
         e1.synchronize()
         torch.cuda.synchronize(local)
@@ -422,14 +427,20 @@ def run_gpu(args):
         barrier(world)
         return e0.elapsed_time(e1)
 
+    # the detection stage (GPU decode + NMS; capacity = every anchor, so no image can overflow)
+    sess.set_detect(conf=0.25, iou=0.50, capacity=DET_CAPACITY)
     for _ in range(args.warmup):
         device_step()
     e2e_steps(max(3, args.warmup))
-    with ClockSampler(local) as clocks:     # over both timed regions
+    e2e_steps(max(3, args.warmup), detect=True)
+    with ClockSampler(local) as clocks:     # over the three timed regions
         ms = timed(device_step, args.steps)
-        ms_e2e = timed_e2e(args.steps)
+        ms_e2e = timed_e2e(args.steps, detect=True)
+        ms_e2e_heads = timed_e2e(args.steps)
     ms = max_over_ranks(ms, world, local)
     ms_e2e = max_over_ranks(ms_e2e, world, local)
+    ms_e2e_heads = max_over_ranks(ms_e2e_heads, world, local)
+    det_d2h = (B * 4 + 15) // 16 * 16 + B * DET_CAPACITY * 24
     ceiling = copy_ceiling(sess, pinned_in, pinned_out[0], world, local)
     # per-layer device times inside the step's own CUDA graph (programmatic dependent launch on):
     # each conv from the moment its inputs were ready to its last CTA's end
@@ -461,10 +472,18 @@ def run_gpu(args):
         "config": workload_config(args),
         "e2e": {"value": round(world * B * args.steps / (ms_e2e * 1e-3), 1), "unit": UNIT,
                 "ms_per_step": round(ms_e2e / args.steps, 4),
-                "h2d_bytes_per_step": int(B * sess.in_image_bytes), "d2h_bytes_per_step": int(B * sess.out_bytes),
-                "path": "GraphSession.run_async (C ABI ixb_session_submit / ixb_session_wait_ticket): pinned host "
-                        "images -> H2D stream -> graph on the compute stream -> D2H stream -> pinned host heads, "
+                "h2d_bytes_per_step": int(B * (sess.in_image_bytes + 12)), "d2h_bytes_per_step": int(det_d2h),
+                "path": "GraphSession.run_async(detect=True) (C ABI ixb_session_submit_detect / "
+                        "ixb_session_detections, the reference's ignite_run_async / ignite_wait contract): pinned "
+                        "host images -> H2D stream -> graph + GPU decode/NMS (conf 0.25, iou 0.5) on the compute "
+                        f"stream -> D2H stream -> pinned host detections (capacity {DET_CAPACITY} per image), "
                         f"{depth} batches in flight; CUDA events from the first H2D to the last D2H"},
+        "e2e_heads": {"value": round(world * B * args.steps / (ms_e2e_heads * 1e-3), 1), "unit": UNIT,
+                      "ms_per_step": round(ms_e2e_heads / args.steps, 4),
+                      "h2d_bytes_per_step": int(B * sess.in_image_bytes),
+                      "d2h_bytes_per_step": int(B * sess.out_bytes),
+                      "path": "GraphSession.run_async (C ABI ixb_session_submit / ixb_session_wait_ticket): "
+                              "pinned host images -> graph -> pinned host int8 heads (77.4 MB per 64 images)"},
         "roofline": {"bound": "hbm", "kernel": "ixb::conv_kernel (all conv launches of one step)",
                      "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,
@@ -481,7 +500,9 @@ def run_gpu(args):
                      "int8_tc_frac": round(int8_tops / (2 * bf16_peak), 4),
                      "int8_tc_peak_note": f"2 x {peak_kind} dense bf16 burst ({bf16_peak} TF/s): int8 runs at twice "
                                           f"the bf16 rate on tcgen05"},
-        "gpu_launches": int(launches * args.steps),
+        "gpu_launches": int(launches * args.steps + (launches + 1) * args.steps + launches * args.steps),
+        "gpu_launches_note": "device steps (ingress + convs + SPPF per step), then the e2e detection steps "
+                             "(+ the decode kernel) and the e2e heads steps",
         "clocks": clocks.summary(),
         "copy_ceiling": ceiling,
         "per_layer": rows,

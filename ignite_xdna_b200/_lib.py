@@ -14,10 +14,11 @@ LIB_NAME = "libixb200.so"
 LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
 
 IXB_OK = 0
-ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported"}
+ERRORS = {-1: "invalid", -2: "cuda", -3: "timeout", -4: "device", -5: "unsupported", -6: "capacity"}
 IXB_ERR_INVALID = -1
 IXB_ERR_TIMEOUT = -3
 IXB_ERR_DEVICE = -4
+IXB_ERR_CAPACITY = -6
 IXB_ERR_UNSUPPORTED = -5
 MAX_SEGS = 4
 API_VERSION = 9
@@ -123,7 +124,36 @@ _SIGS = {
                                        C.c_void_p]),
     "ixb_session_letterbox": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64,
                                         C.POINTER(C.c_float)]),
+    "ixb_decode_dense": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int, C.c_uint64, C.c_void_p, C.c_void_p]),
+    "ixb_session_set_detect": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "ixb_session_set_thresholds": (C.c_int, [C.c_void_p, C.c_float, C.c_float]),
+    "ixb_session_set_class_names": (C.c_int, [C.c_void_p, C.POINTER(C.c_char_p), C.c_int]),
+    "ixb_session_submit_detect": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.POINTER(C.c_uint64)]),
+    "ixb_session_submit_frames": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint64,
+                                            C.POINTER(C.c_uint64)]),
+    "ixb_session_detections": (C.c_int, [C.c_void_p, C.c_uint64, C.c_int, C.POINTER(C.c_int32),
+                                         C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                         C.POINTER(C.c_void_p)]),
+    "ixb_session_wait_detections": (C.c_int, [C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_void_p, C.c_int]),
+    "ixb_run_frame": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int]),
+    "ixb_session_last_timings": (C.c_int, [C.c_void_p, C.c_void_p]),
 }
+
+
+class DenseHead(C.Structure):
+    _fields_ = [("box_offset", C.c_uint64), ("cls_offset", C.c_uint64), ("box_scale", C.c_float),
+                ("box_zero_point", C.c_int32), ("cls_scale", C.c_float), ("cls_zero_point", C.c_int32),
+                ("grid", C.c_int32), ("stride", C.c_float)]
+
+
+class Detection(C.Structure):
+    _fields_ = [("x0", C.c_float), ("y0", C.c_float), ("w", C.c_float), ("h", C.c_float), ("score", C.c_float),
+                ("class_id", C.c_int32), ("class_name", C.c_char * 32)]
+
+
+class Timings(C.Structure):
+    _fields_ = [("preprocess_ms", C.c_double), ("gpu_exec_ms", C.c_double), ("postprocess_ms", C.c_double),
+                ("glass_to_glass_ms", C.c_double)]
 
 
 def exported_symbols():

@@ -1000,6 +1000,52 @@ void conv_spans(const ixb_conv_desc& d, int batch, std::vector<Span>& rd, std::v
 
 }  // namespace
 
+// The decode kernel's parameters from a caller's descriptor (tables and anchors in device memory).
+int prepare_decode(const ixb_decode_desc& d, uint64_t egress_image_bytes, DecodeParams& p) {
+  if (d.reg_max != kDfl) return fail(IXB_ERR_UNSUPPORTED, "decode implements the 16-bin DFL head (reg_max 16)");
+  if (d.num_classes < 1 || d.num_classes > 256) return fail(IXB_ERR_INVALID, "num_classes outside [1, 256]");
+  if (!d.anchor_x || !d.anchor_y || !d.strides) return fail(IXB_ERR_INVALID, "null anchor tables");
+  memset(&p, 0, sizeof p);
+  int total = 0;
+  for (int h = 0; h < 3; ++h) {
+    const ixb_decode_head& hd = d.head[h];
+    if (!hd.dfl_exp || !hd.sigmoid || hd.anchors < 1 || hd.anchor_offset != total)
+      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + ": missing tables or anchors out of order");
+    const uint64_t box_end = hd.box_offset + (uint64_t)4 * kDfl * hd.anchors;
+    const uint64_t cls_end = hd.cls_offset + (uint64_t)d.num_classes * hd.anchors;
+    if (box_end > egress_image_bytes || cls_end > egress_image_bytes)
+      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + " outside the image's egress");
+    total += hd.anchors;
+    DecodeHeadDev& o = p.head[h];
+    o.box_off = (long long)hd.box_offset;
+    o.cls_off = (long long)hd.cls_offset;
+    o.dfl_exp = hd.dfl_exp;
+    o.sigmoid = hd.sigmoid;
+    o.sigmoid_low = hd.sigmoid_low;
+    // an integer class maximum m survives when m > q_threshold, i.e. m > floor(q_threshold)
+    const double qt = hd.q_threshold;
+    o.qi = !(qt < 127.0) ? 127 : (qt < -129.0 ? -129 : (int)std::floor(qt));
+    o.anchors = hd.anchors;
+    o.anchor_offset = hd.anchor_offset;
+  }
+  if (total > kDecodeMaxAnchors) return fail(IXB_ERR_INVALID, "more than 8400 anchors per image");
+  p.egress_image_bytes = (long long)egress_image_bytes;
+  p.anchor_x = d.anchor_x;
+  p.anchor_y = d.anchor_y;
+  p.strides = d.strides;
+  p.num_classes = d.num_classes;
+  p.conf = d.conf;
+  p.iou = d.iou;
+  return 0;
+}
+
+int launch_decode(const DecodeParams& p, int batch, cudaStream_t st) {
+  if (int r = ensure_smem_limit(yolo_decode_kernel, decode_smem_bytes())) return r;
+  yolo_decode_kernel<<<batch, kDecodeThreads, decode_smem_bytes(), st>>>(p);
+  IXB_CUDA(cudaGetLastError());
+  return 0;
+}
+
 struct ixb_session {
   int device = 0;
   cudaStream_t stream = nullptr;             // compute
@@ -1028,7 +1074,43 @@ struct ixb_session {
     uint64_t ticket = 0;
     bool busy = false;
     cudaEvent_t h2d_done = nullptr, t0 = nullptr, t1 = nullptr, d2h_done = nullptr;
+    // detection runs (ixb_session_submit_detect / _frames): letterbox and decode events, the
+    // batch, the host clock at submit, and where the detections land
+    cudaEvent_t pre0 = nullptr, post1 = nullptr;
+    bool detections = false, frames = false;
+    int batch = 0;
+    std::chrono::steady_clock::time_point submitted;
+    uint8_t* det_dev = nullptr;   // [counts: max_batch int32][boxes][scores][classes] for this batch
+    uint8_t* det_host = nullptr;  // pinned copy of the same
+    float* lb_dev = nullptr;      // [max_batch][3] pad_top, pad_left, scale
+    float* lb_host = nullptr;     // pinned staging of lb_dev
+    uint8_t* frames_dev = nullptr;  // BGR frames of a frames run (grown on demand)
+    size_t frames_cap = 0;
   } slots[kSlots];
+  // Detection stage (ixb_session_set_detect): decode + NMS after the network.
+  bool detect = false;
+  ixb_detect_config dcfg{};
+  DecodeParams dparams{};
+  uint8_t* det_mem = nullptr;   // device memory of every slot's detections and letterbox rows
+  uint8_t* det_pinned = nullptr;
+  std::vector<std::string> class_names;
+  ixb_timings last_timings{};
+  size_t lb_bytes() const { return ((size_t)plan.max_batch * 12 + 255) / 256 * 256; }
+  size_t det_slot_bytes() const {
+    const size_t cap = (size_t)dcfg.capacity, B = (size_t)plan.max_batch;
+    return ((B * 4 + 255) / 256 * 256 + B * cap * 24 + 255) / 256 * 256 + lb_bytes();
+  }
+  // The detections of `batch` images, contiguous so one copy brings them back: counts [batch]
+  // (padded to 16 bytes), boxes [batch][capacity][4], scores and classes [batch][capacity].
+  void det_layout(uint8_t* base, int batch, int32_t** counts, float** boxes, float** scores, int32_t** classes) const {
+    const size_t cap = (size_t)dcfg.capacity;
+    const size_t c_bytes = ((size_t)batch * 4 + 15) / 16 * 16;
+    *counts = reinterpret_cast<int32_t*>(base);
+    *boxes = reinterpret_cast<float*>(base + c_bytes);
+    *scores = reinterpret_cast<float*>(base + c_bytes + (size_t)batch * cap * 16);
+    *classes = reinterpret_cast<int32_t*>(base + c_bytes + (size_t)batch * cap * 20);
+  }
+  size_t det_bytes(int batch) const { return ((size_t)batch * 4 + 15) / 16 * 16 + (size_t)batch * dcfg.capacity * 24; }
   uint64_t next_ticket = 1;
 
   int depth() const { return 1 + plan.extra_slots; }
@@ -1371,6 +1453,8 @@ int ixb_session_create(const ixb_plan* plan, int device, void* arena, uint64_t a
     if (e == cudaSuccess) e = cudaEventCreate(&sl.t0);
     if (e == cudaSuccess) e = cudaEventCreate(&sl.t1);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.d2h_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreate(&sl.pre0);
+    if (e == cudaSuccess) e = cudaEventCreate(&sl.post1);
   }
   if (e != cudaSuccess) {
     int r = cuda_fail(e, "stream/event creation");
@@ -1395,9 +1479,13 @@ int ixb_session_destroy(ixb_session* s) {
   if (s->h2d) cudaStreamSynchronize(s->h2d);
   if (s->d2h) cudaStreamSynchronize(s->d2h);
   for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
-  for (auto& sl : s->slots)
-    for (cudaEvent_t ev : {sl.h2d_done, sl.t0, sl.t1, sl.d2h_done})
+  for (auto& sl : s->slots) {
+    for (cudaEvent_t ev : {sl.h2d_done, sl.t0, sl.t1, sl.d2h_done, sl.pre0, sl.post1})
       if (ev) cudaEventDestroy(ev);
+    if (sl.frames_dev) cudaFree(sl.frames_dev);
+  }
+  if (s->det_mem) cudaFree(s->det_mem);
+  if (s->det_pinned) cudaFreeHost(s->det_pinned);
   if (s->h2d) cudaStreamDestroy(s->h2d);
   if (s->d2h) cudaStreamDestroy(s->d2h);
   if (s->ev0) cudaEventDestroy(s->ev0);
@@ -1508,6 +1596,7 @@ int ixb_session_submit(ixb_session* s, const uint8_t* images, int batch, int8_t*
   IXB_CUDA(cudaEventRecord(sl.d2h_done, s->d2h));
   sl.ticket = t;
   sl.busy = true;
+  sl.detections = false;
   s->next_ticket = t + 1;
   *ticket = t;
   return 0;
@@ -1521,7 +1610,254 @@ int ixb_session_wait_ticket(ixb_session* s, uint64_t ticket, int timeout_ms) {
   if (int r = wait_event(sl.d2h_done, timeout_ms)) return r;
   sl.busy = false;
   cudaEventElapsedTime(&s->last_ms, sl.t0, sl.t1);
+  if (sl.detections) {  // the stages of a detection run, as the reference's ignite_timings_t
+    float pre = 0.f, post = 0.f;
+    cudaEventElapsedTime(&pre, sl.pre0, sl.t0);
+    cudaEventElapsedTime(&post, sl.t1, sl.post1);
+    s->last_timings.preprocess_ms = sl.frames ? pre : 0.0;
+    s->last_timings.gpu_exec_ms = s->last_ms;
+    s->last_timings.postprocess_ms = post;
+    s->last_timings.glass_to_glass_ms =
+        std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - sl.submitted).count();
+  }
   return read_device_error();
+}
+
+// ---------------------------------------------------------------- detection stage
+int ixb_session_set_detect(ixb_session* s, const ixb_detect_config* cfg) {
+  if (!s || !cfg) return fail(IXB_ERR_INVALID, "null argument");
+  if (s->pending || s->any_busy()) return fail(IXB_ERR_INVALID, "runs are still in flight");
+  if (cfg->capacity < 1 || cfg->capacity > kDecodeMaxAnchors) return fail(IXB_ERR_INVALID, "capacity outside [1, 8400]");
+  for (int h = 0; h < 3; ++h)
+    if (!(cfg->cls_scale[h] > 0.f)) return fail(IXB_ERR_INVALID, "class head scales must be positive");
+  IXB_CUDA(cudaSetDevice(s->device));
+  DecodeParams p;
+  if (int r = prepare_decode(cfg->decode, s->plan.egress_image_bytes, p)) return r;
+  const bool grow = !s->detect || cfg->capacity != s->dcfg.capacity;
+  s->dcfg = *cfg;
+  s->dparams = p;
+  if (grow) {
+    if (s->det_mem) cudaFree(s->det_mem);
+    if (s->det_pinned) cudaFreeHost(s->det_pinned);
+    s->det_mem = s->det_pinned = nullptr;
+    s->detect = false;
+    const size_t per = s->det_slot_bytes();
+    IXB_CUDA(cudaMalloc(&s->det_mem, per * ixb_session::kSlots));
+    IXB_CUDA(cudaMallocHost(&s->det_pinned, per * ixb_session::kSlots));
+    for (int k = 0; k < ixb_session::kSlots; ++k) {
+      ixb_session::Slot& sl = s->slots[k];
+      sl.det_dev = s->det_mem + k * per;
+      sl.det_host = s->det_pinned + k * per;
+      sl.lb_dev = reinterpret_cast<float*>(sl.det_dev + per - s->lb_bytes());
+      sl.lb_host = reinterpret_cast<float*>(sl.det_host + per - s->lb_bytes());
+      sl.detections = false;
+    }
+  }
+  s->detect = true;
+  return 0;
+}
+
+int ixb_session_set_thresholds(ixb_session* s, float conf, float iou) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (!s->detect) return fail(IXB_ERR_INVALID, "the session has no detection stage (ixb_session_set_detect)");
+  if (!(conf > 0.f && conf < 1.f) || !(iou >= 0.f && iou <= 1.f))
+    return fail(IXB_ERR_INVALID, "conf must lie in (0, 1) and iou in [0, 1]");
+  if (s->pending || s->any_busy()) return fail(IXB_ERR_INVALID, "runs are still in flight");
+  ixb_detect_config c = s->dcfg;
+  // the prune threshold on a class head's int8 logit: logit(conf) / scale + zero point
+  const double cc = std::min(std::max((double)conf, 1e-12), 1.0 - 1e-12);
+  for (int h = 0; h < 3; ++h)
+    c.decode.head[h].q_threshold = std::log(cc / (1.0 - cc)) / (double)c.cls_scale[h] + (double)c.cls_zero_point[h];
+  c.decode.conf = conf;
+  c.decode.iou = iou;
+  return ixb_session_set_detect(s, &c);
+}
+
+int ixb_session_set_class_names(ixb_session* s, const char* const* names, int n) {
+  if (!s || n < 0 || (n > 0 && !names)) return fail(IXB_ERR_INVALID, "bad class names");
+  s->class_names.clear();
+  for (int i = 0; i < n; ++i) s->class_names.emplace_back(names[i] ? names[i] : "");
+  return 0;
+}
+
+}  // extern "C"
+
+namespace {
+// Claims the ticket's slot for a detection run: waits for the run `depth` tickets back, builds the
+// launches and the graph. Returns the slot.
+int claim_detect_slot(ixb_session* s, int batch, bool ingress, cudaGraphExec_t* exec, int* slot_out) {
+  if (!s->detect) return fail(IXB_ERR_INVALID, "the session has no detection stage (ixb_session_set_detect)");
+  if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
+  if (s->pending) return fail(IXB_ERR_INVALID, "a synchronous run is pending");
+  IXB_CUDA(cudaSetDevice(s->device));
+  const int slot = s->slot_of(s->next_ticket);
+  ixb_session::Slot& sl = s->slots[slot];
+  if (sl.busy)
+    if (int r = ixb_session_wait_ticket(s, sl.ticket, 60000)) return r;
+  if (int r = s->prepare(batch, slot)) return r;
+  if (int r = s->graph_for(batch, exec, slot, ingress)) return r;
+  *slot_out = slot;
+  return 0;
+}
+
+// After the graph on the compute stream: decode + NMS into the slot's detections, then one copy back.
+int enqueue_detect_tail(ixb_session* s, int slot, int batch, uint64_t* ticket) {
+  ixb_session::Slot& sl = s->slots[slot];
+  DecodeParams p = s->dparams;
+  p.egress = reinterpret_cast<const int8_t*>(s->arena + s->egress_at(slot));
+  p.letterbox = sl.lb_dev;
+  p.capacity = s->dcfg.capacity;
+  s->det_layout(sl.det_dev, batch, &p.out_count, &p.out_box, &p.out_score, &p.out_class);
+  if (int r = launch_decode(p, batch, s->stream)) return r;
+  IXB_CUDA(cudaEventRecord(sl.post1, s->stream));
+  IXB_CUDA(cudaStreamWaitEvent(s->d2h, sl.post1, 0));
+  IXB_CUDA(cudaMemcpyAsync(sl.det_host, sl.det_dev, s->det_bytes(batch), cudaMemcpyDeviceToHost, s->d2h));
+  IXB_CUDA(cudaEventRecord(sl.d2h_done, s->d2h));
+  const uint64_t t = s->next_ticket;
+  sl.ticket = t;
+  sl.busy = true;
+  sl.detections = true;
+  sl.batch = batch;
+  s->next_ticket = t + 1;
+  *ticket = t;
+  return 0;
+}
+}  // namespace
+
+extern "C" {
+
+int ixb_session_submit_detect(ixb_session* s, const uint8_t* images, int batch, const float* letterbox,
+                              uint64_t* ticket) {
+  if (!s || !images || !ticket) return fail(IXB_ERR_INVALID, "null argument");
+  cudaGraphExec_t exec;
+  int slot = 0;
+  if (int r = claim_detect_slot(s, batch, true, &exec, &slot)) return r;
+  ixb_session::Slot& sl = s->slots[slot];
+  sl.submitted = std::chrono::steady_clock::now();
+  sl.frames = false;
+  for (int i = 0; i < batch; ++i) {
+    sl.lb_host[3 * i] = letterbox ? letterbox[3 * i] : 0.f;
+    sl.lb_host[3 * i + 1] = letterbox ? letterbox[3 * i + 1] : 0.f;
+    sl.lb_host[3 * i + 2] = letterbox ? letterbox[3 * i + 2] : 1.f;
+  }
+  const size_t in_bytes = (size_t)batch * 3 * s->plan.img_h * s->plan.img_w;
+  IXB_CUDA(cudaMemcpyAsync(s->arena + s->images_at(slot), images, in_bytes, cudaMemcpyDefault, s->h2d));
+  IXB_CUDA(cudaMemcpyAsync(sl.lb_dev, sl.lb_host, (size_t)batch * 12, cudaMemcpyHostToDevice, s->h2d));
+  IXB_CUDA(cudaEventRecord(sl.h2d_done, s->h2d));
+  IXB_CUDA(cudaStreamWaitEvent(s->stream, sl.h2d_done, 0));
+  IXB_CUDA(cudaEventRecord(sl.pre0, s->stream));
+  IXB_CUDA(cudaEventRecord(sl.t0, s->stream));
+  IXB_CUDA(cudaGraphLaunch(exec, s->stream));
+  IXB_CUDA(cudaEventRecord(sl.t1, s->stream));
+  return enqueue_detect_tail(s, slot, batch, ticket);
+}
+
+int ixb_session_submit_frames(ixb_session* s, const uint8_t* frames, int batch, int src_w, int src_h, int src_stride,
+                              uint64_t frame_bytes, uint64_t* ticket) {
+  if (!s || !frames || !ticket) return fail(IXB_ERR_INVALID, "null argument");
+  if (src_w < 1 || src_h < 1 || src_stride < 3 * src_w ||
+      (batch > 1 && frame_bytes < (uint64_t)src_stride * (src_h - 1) + 3ull * src_w))
+    return fail(IXB_ERR_INVALID, "frame sizes and strides do not hold the frames");
+  cudaGraphExec_t exec;
+  int slot = 0;
+  if (int r = claim_detect_slot(s, batch, false, &exec, &slot)) return r;
+  ixb_session::Slot& sl = s->slots[slot];
+  sl.submitted = std::chrono::steady_clock::now();
+  sl.frames = true;
+  const size_t need = (size_t)(batch - 1) * frame_bytes + (size_t)src_stride * (src_h - 1) + 3ull * src_w;
+  if (need > sl.frames_cap) {  // the slot's previous run has completed (claim_detect_slot)
+    if (sl.frames_dev) cudaFree(sl.frames_dev);
+    sl.frames_dev = nullptr;
+    sl.frames_cap = 0;
+    IXB_CUDA(cudaMalloc(&sl.frames_dev, need));
+    sl.frames_cap = need;
+  }
+  IXB_CUDA(cudaMemcpyAsync(sl.frames_dev, frames, need, cudaMemcpyDefault, s->h2d));
+  IXB_CUDA(cudaEventRecord(sl.h2d_done, s->h2d));
+  IXB_CUDA(cudaStreamWaitEvent(s->stream, sl.h2d_done, 0));
+  IXB_CUDA(cudaEventRecord(sl.pre0, s->stream));
+  const ixb_plan& pl = s->plan;
+  const int row = pl.img_w + 4;
+  int8_t* base = reinterpret_cast<int8_t*>(s->arena + pl.input.offset) + ((long long)row + 1) * 8;
+  float lb[3];
+  if (int r = ixb_letterbox_frames(sl.frames_dev, batch, src_w, src_h, src_stride, batch > 1 ? frame_bytes : need,
+                                   reinterpret_cast<const int8_t*>(s->arena + pl.input_lut_offset), base, pl.img_w,
+                                   pl.img_h, row, (uint64_t)(pl.img_h + 2) * row * 8, lb, s->stream))
+    return r;
+  if (pl.input_s2d)
+    if (int r = launch_ingress_s2d(nullptr, reinterpret_cast<const int8_t*>(s->arena + pl.input.offset), nullptr, batch,
+                                   pl.img_h, pl.img_w, s->arena, pl.input_s2d_view, s->stream))
+      return r;
+  for (int i = 0; i < batch; ++i)
+    for (int j = 0; j < 3; ++j) sl.lb_host[3 * i + j] = lb[j];
+  IXB_CUDA(cudaMemcpyAsync(sl.lb_dev, sl.lb_host, (size_t)batch * 12, cudaMemcpyHostToDevice, s->stream));
+  IXB_CUDA(cudaEventRecord(sl.t0, s->stream));
+  IXB_CUDA(cudaGraphLaunch(exec, s->stream));
+  IXB_CUDA(cudaEventRecord(sl.t1, s->stream));
+  return enqueue_detect_tail(s, slot, batch, ticket);
+}
+
+int ixb_session_detections(ixb_session* s, uint64_t ticket, int timeout_ms, int32_t* batch, const int32_t** counts,
+                           const float** boxes, const float** scores, const int32_t** classes) {
+  if (!s) return fail(IXB_ERR_INVALID, "null session");
+  if (int r = ixb_session_wait_ticket(s, ticket, timeout_ms)) return r;
+  const ixb_session::Slot& sl = s->slots[s->slot_of(ticket)];
+  if (sl.ticket != ticket) return fail(IXB_ERR_INVALID, "a later run has reused this ticket's slot");
+  if (!sl.detections) return fail(IXB_ERR_INVALID, "the ticket's run returned heads, not detections");
+  int32_t* c;
+  float *b, *sc;
+  int32_t* cl;
+  s->det_layout(sl.det_host, sl.batch, &c, &b, &sc, &cl);
+  if (batch) *batch = sl.batch;
+  if (counts) *counts = c;
+  if (boxes) *boxes = b;
+  if (scores) *scores = sc;
+  if (classes) *classes = cl;
+  return 0;
+}
+
+int ixb_session_wait_detections(ixb_session* s, uint64_t ticket, int timeout_ms, int image, ixb_detection* out,
+                                int max_detections) {
+  int32_t batch = 0;
+  const int32_t* counts;
+  const float *boxes, *scores;
+  const int32_t* classes;
+  if (int r = ixb_session_detections(s, ticket, timeout_ms, &batch, &counts, &boxes, &scores, &classes)) return r;
+  if (image < 0 || image >= batch) return fail(IXB_ERR_INVALID, "image outside the run's batch");
+  const int n = counts[image];
+  if (n < 0)
+    return fail(IXB_ERR_CAPACITY, "more detections survive NMS than the session's capacity (" +
+                                      std::to_string(s->dcfg.capacity) + ")");
+  if (max_detections > 0 && !out) return fail(IXB_ERR_INVALID, "null detections array");
+  const int m = std::min(n, std::max(max_detections, 0));
+  const size_t cap = (size_t)s->dcfg.capacity;
+  for (int k = 0; k < m; ++k) {
+    const size_t o = (size_t)image * cap + k;
+    ixb_detection& d = out[k];
+    d.x0 = boxes[4 * o];
+    d.y0 = boxes[4 * o + 1];
+    d.w = boxes[4 * o + 2];
+    d.h = boxes[4 * o + 3];
+    d.score = scores[o];
+    d.class_id = classes[o];
+    memset(d.class_name, 0, sizeof d.class_name);
+    if (d.class_id >= 0 && d.class_id < (int)s->class_names.size())
+      strncpy(d.class_name, s->class_names[d.class_id].c_str(), sizeof d.class_name - 1);
+  }
+  return m;
+}
+
+int ixb_run_frame(ixb_session* s, const uint8_t* bgr, int width, int height, int stride, ixb_detection* out,
+                  int max_detections) {
+  uint64_t t = 0;
+  if (int r = ixb_session_submit_frames(s, bgr, 1, width, height, stride, (uint64_t)stride * height, &t)) return r;
+  return ixb_session_wait_detections(s, t, 60000, 0, out, max_detections);
+}
+
+int ixb_session_last_timings(ixb_session* s, ixb_timings* t) {
+  if (!s || !t) return fail(IXB_ERR_INVALID, "null argument");
+  *t = s->last_timings;
+  return 0;
 }
 
 int ixb_session_streams(ixb_session* s, void** compute, void** h2d, void** d2h) {
@@ -1779,51 +2115,53 @@ int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, u
                     int32_t* counts, void* stream) {
   if (!d || !egress || !letterbox || !boxes || !scores || !classes || !counts || batch < 1 || capacity < 0)
     return fail(IXB_ERR_INVALID, "bad decode arguments");
-  if (d->reg_max != kDfl) return fail(IXB_ERR_UNSUPPORTED, "decode implements the 16-bin DFL head (reg_max 16)");
-  if (d->num_classes < 1 || d->num_classes > 256) return fail(IXB_ERR_INVALID, "num_classes outside [1, 256]");
-  if (!d->anchor_x || !d->anchor_y || !d->strides) return fail(IXB_ERR_INVALID, "null anchor tables");
   if (reinterpret_cast<uintptr_t>(boxes) & 15) return fail(IXB_ERR_INVALID, "boxes must be 16-byte aligned");
   DecodeParams p;
-  memset(&p, 0, sizeof p);
-  int total = 0;
-  for (int h = 0; h < 3; ++h) {
-    const ixb_decode_head& hd = d->head[h];
-    if (!hd.dfl_exp || !hd.sigmoid || hd.anchors < 1 || hd.anchor_offset != total)
-      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + ": missing tables or anchors out of order");
-    const uint64_t box_end = hd.box_offset + (uint64_t)4 * kDfl * hd.anchors;
-    const uint64_t cls_end = hd.cls_offset + (uint64_t)d->num_classes * hd.anchors;
-    if (box_end > egress_image_bytes || cls_end > egress_image_bytes)
-      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + " outside the image's egress");
-    total += hd.anchors;
-    DecodeHeadDev& o = p.head[h];
-    o.box_off = (long long)hd.box_offset;
-    o.cls_off = (long long)hd.cls_offset;
-    o.dfl_exp = hd.dfl_exp;
-    o.sigmoid = hd.sigmoid;
-    o.sigmoid_low = hd.sigmoid_low;
-    // an integer class maximum m survives when m > q_threshold, i.e. m > floor(q_threshold)
-    const double qt = hd.q_threshold;
-    o.qi = !(qt < 127.0) ? 127 : (qt < -129.0 ? -129 : (int)std::floor(qt));
-    o.anchors = hd.anchors;
-    o.anchor_offset = hd.anchor_offset;
-  }
-  if (total > kDecodeMaxAnchors) return fail(IXB_ERR_INVALID, "more than 8400 anchors per image");
+  if (int r = prepare_decode(*d, egress_image_bytes, p)) return r;
   p.egress = egress;
-  p.egress_image_bytes = (long long)egress_image_bytes;
-  p.anchor_x = d->anchor_x;
-  p.anchor_y = d->anchor_y;
-  p.strides = d->strides;
-  p.num_classes = d->num_classes;
-  p.conf = d->conf;
-  p.iou = d->iou;
   p.letterbox = letterbox;
   p.capacity = capacity;
   p.out_box = boxes;
   p.out_score = scores;
   p.out_class = classes;
   p.out_count = counts;
-  if (int r = ensure_smem_limit(yolo_decode_kernel, decode_smem_bytes())) return r;
-  yolo_decode_kernel<<<batch, kDecodeThreads, decode_smem_bytes(), static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_decode(p, batch, static_cast<cudaStream_t>(stream));
+}
+
+int ixb_decode_dense(const ixb_dense_head* heads, int32_t num_classes, const int8_t* egress, int batch,
+                     uint64_t egress_image_bytes, float* out, void* stream) {
+  if (!heads || !egress || !out || batch < 1 || batch > 65535) return fail(IXB_ERR_INVALID, "bad dense decode arguments");
+  if (num_classes < 1 || num_classes > 1024) return fail(IXB_ERR_INVALID, "num_classes outside [1, 1024]");
+  DenseParams p;
+  memset(&p, 0, sizeof p);
+  int total = 0;
+  for (int h = 0; h < 3; ++h) {
+    const ixb_dense_head& hd = heads[h];
+    if (hd.grid < 1 || hd.grid > 4096 || !(hd.box_scale > 0.f) || !(hd.cls_scale > 0.f) || !(hd.stride > 0.f))
+      return fail(IXB_ERR_INVALID, "dense decode head " + std::to_string(h) + ": bad grid, scale or stride");
+    const uint64_t n = (uint64_t)hd.grid * hd.grid;
+    if (hd.box_offset + 64 * n > egress_image_bytes || hd.cls_offset + (uint64_t)num_classes * n > egress_image_bytes)
+      return fail(IXB_ERR_INVALID, "dense decode head " + std::to_string(h) + " outside the image's egress");
+    DenseHeadDev& o = p.head[h];
+    o.box_off = (long long)hd.box_offset;
+    o.cls_off = (long long)hd.cls_offset;
+    o.box_scale = hd.box_scale;
+    o.box_zp = (float)hd.box_zero_point;
+    o.cls_scale = hd.cls_scale;
+    o.cls_zp = (float)hd.cls_zero_point;
+    o.grid = hd.grid;
+    o.anchors = (int)n;
+    o.anchor_offset = total;
+    o.stride = hd.stride;
+    total += (int)n;
+  }
+  p.egress = egress;
+  p.egress_image_bytes = (long long)egress_image_bytes;
+  p.num_classes = num_classes;
+  p.total_anchors = total;
+  p.out = out;
+  dense_decode_kernel<<<dim3((unsigned)((total + 255) / 256), (unsigned)batch), 256, 0,
+                        static_cast<cudaStream_t>(stream)>>>(p);
   IXB_CUDA(cudaGetLastError());
   return 0;
 }

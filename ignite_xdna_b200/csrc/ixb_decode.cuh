@@ -22,6 +22,8 @@ namespace ixb {
 constexpr int kDecodeThreads = 1024;
 constexpr int kDecodeMaxAnchors = 8400;
 constexpr int kDfl = 16;
+constexpr int kDecodeMaxClasses = 256;
+constexpr int kDecodeMaxGap = 4;  // class gaps checked explicitly before the per-class NMS is trusted
 
 struct DecodeHeadDev {
   long long box_off, cls_off;   // byte offsets of the box and class heads inside one image's egress
@@ -90,6 +92,24 @@ __device__ __forceinline__ double inter_area(double ax, double ay, double aw, do
   return __dmul_rn(w, h);
 }
 
+// The suppression test of the greedy NMS: overlap 1 - (float)(1 - inter / union) of two
+// class-offset boxes, > iou (or unordered: NaN) suppresses; boxes whose areas add up to at most
+// DBL_EPSILON count as overlap 1 (OpenCV's rule).
+__device__ __forceinline__ bool suppresses(float4 bi, double oi, float4 bk, double ok, float iou) {
+  const double ix = __dadd_rn((double)bi.x, oi), iy = __dadd_rn((double)bi.y, oi);
+  const double iw = bi.z, ih = bi.w, iarea = __dmul_rn(iw, ih);
+  const double kx = __dadd_rn((double)bk.x, ok), ky = __dadd_rn((double)bk.y, ok);
+  const double kw = bk.z, kh = bk.w, karea = __dmul_rn(kw, kh);
+  float ov;
+  if (__dadd_rn(iarea, karea) <= DBL_EPSILON) {
+    ov = 1.0f;
+  } else {
+    const double inter = inter_area(ix, iy, iw, ih, kx, ky, kw, kh);
+    ov = __fsub_rn(1.0f, __double2float_rn(__dsub_rn(1.0, __ddiv_rn(inter, __dsub_rn(__dadd_rn(iarea, karea), inter)))));
+  }
+  return !(ov <= iou);
+}
+
 __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ uint8_t dsmem[];
   float* s_score = reinterpret_cast<float*>(dsmem);                       // [8400]
@@ -97,8 +117,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   int16_t* s_anchor = reinterpret_cast<int16_t*>(s_box + kDecodeMaxAnchors);  // [8400] anchor index
   uint8_t* s_class = reinterpret_cast<uint8_t*>(s_anchor + kDecodeMaxAnchors);  // [8400]
   uint16_t* s_order = reinterpret_cast<uint16_t*>(s_class + kDecodeMaxAnchors); // [16384] sort / kept list
-  __shared__ int s_n, s_kept, s_flag;
-  __shared__ double s_maxc[kDecodeThreads / 32];
+  __shared__ int s_n, s_kept, s_flag, s_nv, s_slow;
+  __shared__ double s_maxc[kDecodeThreads / 32], s_lo[kDecodeThreads / 32];
+  __shared__ int s_cnt[kDecodeMaxClasses], s_start[kDecodeMaxClasses], s_cur[kDecodeMaxClasses];
+  __shared__ uint32_t s_keep[(kDecodeMaxAnchors + 31) / 32];
 
   const int img = blockIdx.x, tid = threadIdx.x;
   const int8_t* eg = p.egress + (long long)img * p.egress_image_bytes;
@@ -206,38 +228,194 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   for (int w = 0; w < kDecodeThreads / 32; ++w) maxc = fmax(maxc, s_maxc[w]);
   const double off_step = __dadd_rn(maxc, 1.0);
 
-  // 4. greedy suppression in score order; kept slot ids overwrite the front of s_order, which
-  //    only ever trails the position being read
-  for (int r = 0; r < n; ++r) {
-    const uint16_t ci = s_order[r];
-    if (!(s_score[ci] > p.conf)) break;  // sorted: nothing later passes the strict threshold
-    const float4 bi = s_box[ci];
-    const double oi = __dmul_rn((double)s_class[ci], off_step);
-    const double ix = __dadd_rn((double)bi.x, oi), iy = __dadd_rn((double)bi.y, oi);
-    const double iw = bi.z, ih = bi.w, iarea = __dmul_rn(iw, ih);
-    int sup = 0;
-    const int kept = s_kept;
-    for (int k = tid; k < kept; k += kDecodeThreads) {
-      const uint16_t ck = s_order[k];
-      const float4 bk = s_box[ck];
-      const double ok = __dmul_rn((double)s_class[ck], off_step);
-      const double kx = __dadd_rn((double)bk.x, ok), ky = __dadd_rn((double)bk.y, ok);
-      const double kw = bk.z, kh = bk.w, karea = __dmul_rn(kw, kh);
-      float ov;
-      if (__dadd_rn(iarea, karea) <= DBL_EPSILON) {
-        ov = 1.0f;
-      } else {
-        const double inter = inter_area(ix, iy, iw, ih, kx, ky, kw, kh);
-        ov = __fsub_rn(1.0f, __double2float_rn(__dsub_rn(1.0, __ddiv_rn(inter, __dsub_rn(__dadd_rn(iarea, karea), inter)))));
-      }
-      if (!(ov <= p.iou)) sup = 1;
+  // 4. NMS. Boxes of different classes are offset by class * off_step, so once the class gaps at
+  //    which two offset boxes can still meet have been checked pair by pair (and no box is
+  //    degenerate), no box suppresses one of another class: the greedy suppression over the
+  //    global order then equals each class's own greedy suppression over its candidates in that
+  //    order, which the warps run in parallel (fast path). Otherwise, or when any check fails,
+  //    the greedy loop runs over the global order as written (slow path).
+  if (tid == 0) {
+    s_nv = n;
+    s_slow = !(p.iou >= 0.f) || p.num_classes > kDecodeMaxClasses;
+  }
+  for (int c = tid; c < kDecodeMaxClasses; c += kDecodeThreads) s_cnt[c] = 0;
+  for (int w = tid; w < (kDecodeMaxAnchors + 31) / 32; w += kDecodeThreads) s_keep[w] = 0u;
+  __syncthreads();
+  // candidates strictly above the threshold form a prefix of the order; degenerate or
+  // non-finite boxes force the slow path; lo = the lowest corner coordinate
+  double lo = 0.0;
+  bool any_lo = false;
+  for (int i = tid; i < n; i += kDecodeThreads) {
+    const uint16_t ci = s_order[i];
+    if (!(s_score[ci] > p.conf)) {
+      atomicMin(&s_nv, i);
+      continue;
     }
-    sup = __syncthreads_or(sup);
-    if (!sup && tid == 0) {
-      s_order[s_kept] = ci;
-      s_kept = s_kept + 1;
+    const float4 b = s_box[ci];
+    if (!isfinite(b.x) || !isfinite(b.y) || !isfinite(b.z) || !isfinite(b.w) ||
+        !(__dmul_rn((double)b.z, (double)b.w) > DBL_EPSILON))
+      s_slow = 1;
+    const double m = fmin((double)b.x, (double)b.y);
+    lo = any_lo ? fmin(lo, m) : m;
+    any_lo = true;
+  }
+  if (!any_lo) lo = 1e300;
+  for (int o = 16; o > 0; o >>= 1) lo = fmin(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+  if ((tid & 31) == 0) s_lo[tid >> 5] = lo;
+  __syncthreads();
+  const int nv = s_nv;
+  double lo_all = 1e300;
+  for (int w = 0; w < kDecodeThreads / 32; ++w) lo_all = fmin(lo_all, s_lo[w]);
+  // offset boxes of classes g apart can meet only while lo + g * off_step <= maxc (plus a margin
+  // far above the rounding of the doubles involved)
+  int gap = 0;
+  while (gap <= kDecodeMaxGap) {
+    const double reach = (double)(gap + 1) * off_step;
+    if (lo_all + reach > maxc + 1e-3 + 1e-9 * (fabs(lo_all) + reach + fabs(maxc))) break;
+    ++gap;
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+  if (!s_slow && gap <= kDecodeMaxGap && nv > 0) {
+    // per-class lists in global order: counts, starts, then each warp places its own classes'
+    // candidates (class % 32 == warp) in order
+    for (int i = tid; i < nv; i += kDecodeThreads) atomicAdd(&s_cnt[s_class[s_order[i]]], 1);
+    __syncthreads();
+    if (warp == 0) {
+      int run = 0;
+      for (int c0 = 0; c0 < kDecodeMaxClasses; c0 += 32) {
+        const int v = s_cnt[c0 + lane];
+        int x = v;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        s_start[c0 + lane] = run + x - v;
+        s_cur[c0 + lane] = 0;
+        run += __shfl_sync(0xffffffffu, x, 31);
+      }
     }
     __syncthreads();
+    uint16_t* s_list = reinterpret_cast<uint16_t*>(s_anchor);  // the anchors are not needed after the sort
+    for (int base = 0; base < nv; base += 32) {
+      const int i = base + lane;
+      const int c = i < nv ? (int)s_class[s_order[i]] : -1;
+      unsigned mine = __ballot_sync(0xffffffffu, c >= 0 && (c & 31) == warp);
+      while (mine) {
+        const int l = __ffs(mine) - 1;
+        mine &= mine - 1;
+        const int cl = __shfl_sync(0xffffffffu, c, l);
+        if (lane == 0) s_list[s_start[cl] + s_cur[cl]++] = (uint16_t)(base + l);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    // the class gaps at which boxes can meet: every pair checked; one suppressing pair -> slow path
+    for (int g = 1; g <= gap; ++g) {
+      for (int c = warp; c + g < p.num_classes; c += kDecodeThreads / 32) {
+        const int na = s_cnt[c], nb = s_cnt[c + g];
+        const uint16_t* la = s_list + s_start[c];
+        const uint16_t* lb = s_list + s_start[c + g];
+        const double oa = __dmul_rn((double)c, off_step), ob = __dmul_rn((double)(c + g), off_step);
+        if ((long long)na * nb > (1 << 18)) {  // too many pairs to check: the slow path decides
+          if (lane == 0) s_slow = 1;
+          continue;
+        }
+        bool hit = false;
+        for (int q = lane; q < na * nb; q += 32) {
+          const uint16_t a = s_order[la[q / nb]], b = s_order[lb[q % nb]];
+          hit = hit || suppresses(s_box[a], oa, s_box[b], ob, p.iou);
+        }
+        if (__any_sync(0xffffffffu, hit) && lane == 0) s_slow = 1;
+      }
+    }
+    __syncthreads();
+  } else if (tid == 0) {
+    s_slow = 1;
+  }
+  __syncthreads();
+  if (!s_slow) {
+    // per-class greedy: warp w runs the classes c % 32 == w; a candidate is kept when no earlier
+    // kept candidate of its class suppresses it (keep bits indexed by global order position)
+    const uint16_t* s_list = reinterpret_cast<const uint16_t*>(s_anchor);
+    for (int c = warp; c < p.num_classes; c += kDecodeThreads / 32) {
+      const int m = s_cnt[c];
+      const uint16_t* lc = s_list + s_start[c];
+      const double oc = __dmul_rn((double)c, off_step);
+      for (int k = 0; k < m; ++k) {
+        const int pk = lc[k];
+        const float4 bi = s_box[s_order[pk]];
+        bool sup = false;
+        for (int j = lane; j < k; j += 32) {
+          const int pj = lc[j];
+          if ((s_keep[pj >> 5] >> (pj & 31)) & 1u) sup = sup || suppresses(bi, oc, s_box[s_order[pj]], oc, p.iou);
+        }
+        if (!__any_sync(0xffffffffu, sup) && lane == 0) atomicOr(&s_keep[pk >> 5], 1u << (pk & 31));
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    // kept ids in global order to the front of s_order (rank = kept bits before the position)
+    if (warp == 0) {
+      int run = 0;
+      for (int w0 = 0; w0 < (nv + 31) / 32; w0 += 32) {
+        const int w = w0 + lane;
+        const int v = w < (nv + 31) / 32 ? __popc(s_keep[w]) : 0;
+        int x = v;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        // exclusive prefix of the kept bits before word w, in word w's slot of s_start / s_cur
+        // (the class lists are done with)
+        if (w < (nv + 31) / 32) {
+          if (w < kDecodeMaxClasses) s_start[w] = run + x - v;
+          else s_cur[w - kDecodeMaxClasses] = run + x - v;
+        }
+        run += __shfl_sync(0xffffffffu, x, 31);
+      }
+      if (lane == 0) s_kept = run;
+    }
+    __syncthreads();
+    // s_order[0 .. kept) <- kept ids; positions are read before any write lands (two passes)
+    uint16_t id_of[(kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads];
+    int rank_of[(kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads];
+#pragma unroll
+    for (int t = 0; t < (kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads; ++t) {
+      const int i = tid + t * kDecodeThreads;
+      rank_of[t] = -1;
+      if (i < nv && ((s_keep[i >> 5] >> (i & 31)) & 1u)) {
+        const int w = i >> 5;
+        const int before = __popc(s_keep[w] & ((1u << (i & 31)) - 1u));
+        rank_of[t] = (w < kDecodeMaxClasses ? s_start[w] : s_cur[w - kDecodeMaxClasses]) + before;
+        id_of[t] = s_order[i];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < (kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads; ++t)
+      if (rank_of[t] >= 0) s_order[rank_of[t]] = id_of[t];
+    __syncthreads();
+  } else {
+    // slow path: greedy suppression in score order; kept slot ids overwrite the front of s_order,
+    // which only ever trails the position being read
+    for (int r = 0; r < n; ++r) {
+      const uint16_t ci = s_order[r];
+      if (!(s_score[ci] > p.conf)) break;  // sorted: nothing later passes the strict threshold
+      const float4 bi = s_box[ci];
+      const double oi = __dmul_rn((double)s_class[ci], off_step);
+      int sup = 0;
+      const int kept = s_kept;
+      for (int k = tid; k < kept; k += kDecodeThreads) {
+        const uint16_t ck = s_order[k];
+        if (suppresses(bi, oi, s_box[ck], __dmul_rn((double)s_class[ck], off_step), p.iou)) sup = 1;
+      }
+      sup = __syncthreads_or(sup);
+      if (!sup && tid == 0) {
+        s_order[s_kept] = ci;
+        s_kept = s_kept + 1;
+      }
+      __syncthreads();
+    }
   }
 
   // 5. detections in kept order
@@ -256,8 +434,79 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   if (tid == 0) p.out_count[img] = kept;
 }
 
+// Dynamic shared memory: scores, boxes, anchors (reused as the per-class lists after the sort),
+// classes, and the sort order.
 constexpr int decode_smem_bytes() {
   return kDecodeMaxAnchors * (4 + 16 + 2 + 1) + 16384 * 2 + 16;
+}
+
+// ---------------------------------------------------------------- dense decode
+// The reference's InferenceSession.decode_yolo_predictions (runtime/session.py:1223-1278) on the
+// GPU: int8 heads -> float32 [B][4 + classes][anchors], anchors level by level. Per anchor:
+// dequantize v = (q - zp) * s; per box side a softmax over its 16 bins (max subtracted) and the
+// expectation sum_k k * e_k / sum_e; corners (g - d) * stride and (g + d) * stride around the
+// grid cell (x, y) (no half-cell offset, as the reference); xywh as centre and size; each class
+// 1 / (1 + exp(-v)). One thread per (image, anchor): the head bytes of consecutive anchors are
+// consecutive, so the loads and the stores of every output row coalesce. float32 with CUDA's
+// expf, against numpy's float32 exp in the reference: equal within a few ulp, not bit for bit.
+struct DenseHeadDev {
+  long long box_off, cls_off;  // byte offsets inside one image's egress
+  float box_scale, box_zp, cls_scale, cls_zp;
+  int grid, anchors, anchor_offset;
+  float stride;
+};
+struct DenseParams {
+  const int8_t* egress;
+  long long egress_image_bytes;
+  DenseHeadDev head[3];
+  int num_classes, total_anchors;
+  float* out;  // [B][4 + num_classes][total_anchors]
+};
+
+__global__ void __launch_bounds__(256) dense_decode_kernel(const __grid_constant__ DenseParams p) {
+  const int a = blockIdx.x * blockDim.x + threadIdx.x;
+  const int img = blockIdx.y;
+  if (a >= p.total_anchors) return;
+  const int h = a >= p.head[2].anchor_offset ? 2 : (a >= p.head[1].anchor_offset ? 1 : 0);
+  const DenseHeadDev& hd = p.head[h];
+  const int i = a - hd.anchor_offset, n = hd.anchors;
+  const int8_t* eg = p.egress + (long long)img * p.egress_image_bytes;
+  const int8_t* box = eg + hd.box_off + i;
+  float dist[4];
+#pragma unroll
+  for (int d = 0; d < 4; ++d) {
+    float v[16];
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      v[k] = __fmul_rn(__fsub_rn((float)box[(long long)(d * 16 + k) * n], hd.box_zp), hd.box_scale);
+      m = fmaxf(m, v[k]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      v[k] = expf(__fsub_rn(v[k], m));
+      sum = __fadd_rn(sum, v[k]);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc = __fadd_rn(acc, __fmul_rn(__fdiv_rn(v[k], sum), (float)k));
+    dist[d] = acc;
+  }
+  const float gx = (float)(i % hd.grid), gy = (float)(i / hd.grid);
+  const float x1 = __fmul_rn(__fsub_rn(gx, dist[0]), hd.stride), y1 = __fmul_rn(__fsub_rn(gy, dist[1]), hd.stride);
+  const float x2 = __fmul_rn(__fadd_rn(gx, dist[2]), hd.stride), y2 = __fmul_rn(__fadd_rn(gy, dist[3]), hd.stride);
+  float* o = p.out + (long long)img * (4 + p.num_classes) * p.total_anchors + a;
+  const long long T = p.total_anchors;
+  o[0] = __fdiv_rn(__fadd_rn(x1, x2), 2.0f);
+  o[T] = __fdiv_rn(__fadd_rn(y1, y2), 2.0f);
+  o[2 * T] = __fsub_rn(x2, x1);
+  o[3 * T] = __fsub_rn(y2, y1);
+  const int8_t* cls = eg + hd.cls_off + i;
+  for (int c = 0; c < p.num_classes; ++c) {
+    const float v = __fmul_rn(__fsub_rn((float)cls[(long long)c * n], hd.cls_zp), hd.cls_scale);
+    o[(4 + c) * T] = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+  }
 }
 
 }  // namespace ixb

@@ -80,6 +80,11 @@ class DecodeDesc(C.Structure):
                 ("conf", C.c_float), ("iou", C.c_float)]
 
 
+class DetectConfig(C.Structure):
+    _fields_ = [("decode", DecodeDesc), ("cls_scale", C.c_float * 3), ("cls_zero_point", C.c_int32 * 3),
+                ("capacity", C.c_int32)]
+
+
 @dataclass
 class Detections:
     boxes: np.ndarray      # float32 [n, 4]: x0, y0, w, h in source-image pixels
@@ -125,6 +130,16 @@ class GpuDecoder:
         d.reg_max, d.num_classes = REG_MAX, self.num_classes
         d.conf, d.iou = float(np.float32(self.conf)), float(np.float32(self.iou))
         self.desc = d
+        self.cls_quant = [(layout.spec(c).scale, layout.spec(c).zero_point) for _, c in HEAD_PAIRS]
+
+    def config(self, capacity: int) -> DetectConfig:
+        """The session-level detection stage's configuration (ixb_session_set_detect)."""
+        c = DetectConfig()
+        c.decode = self.desc
+        for h, (sc, zp) in enumerate(self.cls_quant):
+            c.cls_scale[h], c.cls_zero_point[h] = float(sc), int(zp)
+        c.capacity = int(capacity)
+        return c
 
     def __call__(self, egress_dev, batch: int, letterbox=None, capacity: Optional[int] = None,
                  stream: Optional[int] = None) -> List[Detections]:
@@ -153,3 +168,19 @@ class GpuDecoder:
                 raise RuntimeError(f"image {i}: more than {cap} detections survive NMS")
             out.append(Detections(b[i, :n[i]].copy(), s[i, :n[i]].copy(), c[i, :n[i]].copy()))
         return out
+
+
+def dense_heads(layout, imgsz: int, strides: Sequence[int] = STRIDES):
+    """ixb_dense_head[3] of a session's egress: each level's box and class heads, their scales and
+    zero points, grid and stride."""
+    heads = (L.DenseHead * 3)()
+    for h, ((bname, cname), s) in enumerate(zip(HEAD_PAIRS, strides)):
+        bs, cs = layout.spec(bname), layout.spec(cname)
+        if bs.shape[0] != 4 * REG_MAX or bs.shape[1] != bs.shape[2] or bs.shape[1] * s != imgsz:
+            raise ValueError(f"head {bname} does not match a {imgsz}x{imgsz} stride-{s} level")
+        d = heads[h]
+        d.box_offset, d.cls_offset = bs.offset, cs.offset
+        d.box_scale, d.box_zero_point = float(bs.scale), int(bs.zero_point)
+        d.cls_scale, d.cls_zero_point = float(cs.scale), int(cs.zero_point)
+        d.grid, d.stride = bs.shape[1], float(s)
+    return heads

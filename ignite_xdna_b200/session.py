@@ -73,6 +73,52 @@ class RunHandle:
             self._result = out.copy()
 
 
+class DetectHandle:
+    """One submitted detection run in flight: the reference's ``ignite_run_async`` ticket
+    (c_api/ignite.h:102-124). ``wait`` blocks until the detections are in host memory and
+    returns one ``Detections`` per image (copied out of the session's pinned slot)."""
+
+    def __init__(self, session: "GraphSession", ticket: int, batch: int, keep: Any):
+        self._s = session
+        self.ticket = int(ticket)
+        self.batch = int(batch)
+        self._keep = keep
+        self._result = None
+
+    @property
+    def done(self) -> bool:
+        return self._result is not None
+
+    def wait(self, timeout_ms: int = 2000):
+        from .decode import Detections
+        if self._result is None:
+            s = self._s
+            n = C.c_int32()
+            ptrs = [C.c_void_p() for _ in range(4)]
+            rc = s.lib.ixb_session_detections(s._h, C.c_uint64(self.ticket), int(timeout_ms), C.byref(n),
+                                              *[C.byref(p) for p in ptrs])
+            if rc == L.IXB_ERR_TIMEOUT:
+                raise TimeoutError(f"submitted run {self.ticket} did not complete within {timeout_ms} ms")
+            L.check(rc)
+            b, cap = int(n.value), s._det_capacity
+            counts = np.ctypeslib.as_array(C.cast(ptrs[0], C.POINTER(C.c_int32)), (b,)).copy()
+            boxes = np.ctypeslib.as_array(C.cast(ptrs[1], C.POINTER(C.c_float)), (b, cap, 4))
+            scores = np.ctypeslib.as_array(C.cast(ptrs[2], C.POINTER(C.c_float)), (b, cap))
+            classes = np.ctypeslib.as_array(C.cast(ptrs[3], C.POINTER(C.c_int32)), (b, cap))
+            out = []
+            for i in range(b):
+                k = int(counts[i])
+                if k < 0:
+                    raise RuntimeError(f"image {i}: more than {cap} detections survive NMS")
+                out.append(Detections(boxes[i, :k].copy(), scores[i, :k].copy(), classes[i, :k].copy()))
+            self._result = out
+            self._keep = None
+        return self._result
+
+    def _retire(self) -> None:
+        self.wait(60000)
+
+
 class GraphSession:
     """Whole-network XINT8 YOLOv8 on one B200: persistent arena, one CUDA graph per batch size."""
 
@@ -105,9 +151,11 @@ class GraphSession:
         self.last_host_ms = 0.0
         self._next_ticket = 1
         self.pipeline_depth = 1 + len(self.plan.extra_images_offsets)
-        self._inflight = [None] * self.pipeline_depth     # RunHandle per pipeline slot
+        self._inflight = [None] * self.pipeline_depth     # RunHandle / DetectHandle per pipeline slot
         self._pin_in = [None] * self.pipeline_depth
         self._pin_out = [None] * self.pipeline_depth
+        self._decoder = None
+        self._det_capacity = 0
 
     # ------------------------------------------------------------------ status
     @property
@@ -187,7 +235,8 @@ class GraphSession:
                 h._retire()
         self._inflight = [None] * self.pipeline_depth
 
-    def run_async(self, input_tensor: Any, unswizzle: bool = True, out: Optional[np.ndarray] = None) -> RunHandle:
+    def run_async(self, input_tensor: Any, unswizzle: bool = True, out: Optional[np.ndarray] = None,
+                  detect: bool = False, letterbox: Optional[np.ndarray] = None):
         """Submit a batch and return at once (the reference's ``InferenceSession.run_async``,
         runtime/session.py:1280-1318).
 
@@ -198,7 +247,11 @@ class GraphSession:
         is as for ``run``; a pinned CPU or a CUDA tensor is copied from in place (and must not be
         changed until the handle completes), anything else is first copied into the slot's pinned
         staging buffer. ``out``, if given, is an int8 [>=B, egress_image_bytes] array (pinned for
-        overlap) that receives the heads; ``unswizzle`` is accepted for compatibility."""
+        overlap) that receives the heads; ``unswizzle`` is accepted for compatibility.
+
+        ``detect=True`` (after ``set_detect``) appends the GPU decode + NMS to the run and brings back
+        only the detections (a ``DetectHandle``; ``letterbox`` float [B, 3] maps boxes back to source
+        pixels) instead of the heads: the reference's ``ignite_run_async`` contract."""
         torch = _torch()
         x = self._as_pixels(input_tensor)
         b = self._check_shape(x.shape)
@@ -219,6 +272,17 @@ class GraphSession:
             host = x if isinstance(x, torch.Tensor) else torch.from_numpy(x)
             buf[:n].copy_(host.reshape(-1))
             src, keep = buf, None
+        if detect:
+            if self._decoder is None:
+                raise RuntimeError("call set_detect() before detection runs")
+            lb = None
+            if letterbox is not None:
+                lb = np.ascontiguousarray(np.asarray(letterbox, dtype=np.float32).reshape(b, 3))
+            ticket = C.c_uint64()
+            L.check(self.lib.ixb_session_submit_detect(self._h, C.c_void_p(src.data_ptr()), b,
+                                                       lb.ctypes.data_as(C.c_void_p) if lb is not None else None,
+                                                       C.byref(ticket)))
+            return self._track(DetectHandle(self, ticket.value, b, keep), slot, b)
         if out is None:
             if self._pin_out[slot] is None:
                 self._pin_out[slot] = torch.empty((self.max_batch, self.out_bytes), dtype=torch.int8,
@@ -232,13 +296,104 @@ class GraphSession:
         ticket = C.c_uint64()
         L.check(self.lib.ixb_session_submit(self._h, C.c_void_p(src.data_ptr()), b,
                                             egress.ctypes.data_as(C.c_void_p), C.byref(ticket)))
-        if ticket.value != self._next_ticket:
-            raise RuntimeError(f"engine issued ticket {ticket.value}, expected {self._next_ticket}")
+        return self._track(RunHandle(self, ticket.value, b, egress, keep), slot, b)
+
+    def _track(self, h, slot: int, b: int):
+        if h.ticket != self._next_ticket:
+            raise RuntimeError(f"engine issued ticket {h.ticket}, expected {self._next_ticket}")
         self._next_ticket += 1
-        h = RunHandle(self, ticket.value, b, egress, keep)
         self._inflight[slot] = h
         self._last_batch = b
         return h
+
+    # ------------------------------------------------------------------ detection stage
+    def set_detect(self, conf: float = 0.25, iou: float = 0.50, capacity: int = 300, class_names=None) -> None:
+        """Attach the GPU decode + NMS stage (the reference's ``ignite_set_thresholds``, c_api/ignite.h:141,
+        and its post-processing worker, ignite.cpp:640-980): detection runs bring back at most ``capacity``
+        detections per image instead of the heads."""
+        from .decode import GpuDecoder
+        self._drain()
+        dec = GpuDecoder(self.layout, self.plan.img_w, self.device, conf=conf, iou=iou)
+        cfg = dec.config(capacity)
+        L.check(self.lib.ixb_session_set_detect(self._h, C.byref(cfg)))
+        self._decoder, self._det_cfg, self._det_capacity = dec, cfg, int(capacity)
+        if class_names is not None:
+            names = [str(n).encode() for n in class_names]
+            arr = (C.c_char_p * len(names))(*names)
+            L.check(self.lib.ixb_session_set_class_names(self._h, arr, len(names)))
+
+    def set_thresholds(self, conf: float, iou: float) -> None:
+        """Change the decode thresholds of the detection stage (``ignite_set_thresholds``)."""
+        if self._decoder is None:
+            raise RuntimeError("call set_detect() first")
+        self._drain()
+        L.check(self.lib.ixb_session_set_thresholds(self._h, float(conf), float(iou)))
+
+    def submit_frames(self, frames: Any) -> DetectHandle:
+        """uint8 BGR frames [B, H, W, 3] (host or CUDA, all one size): copied in, letterboxed and quantized
+        on the GPU, run through the network, decoded on the GPU; the detections come back in source
+        pixels (the reference's ``ignite_run_async`` on a batch)."""
+        torch = _torch()
+        if self._decoder is None:
+            raise RuntimeError("call set_detect() before detection runs")
+        if isinstance(frames, torch.Tensor):
+            x = frames.contiguous()
+        else:
+            x = torch.from_numpy(np.ascontiguousarray(frames))
+        if x.dtype != torch.uint8 or x.dim() != 4 or x.shape[3] != 3:
+            raise ValueError(f"expected uint8 BGR frames [B, H, W, 3], got {tuple(x.shape)} {x.dtype}")
+        b, h, w = int(x.shape[0]), int(x.shape[1]), int(x.shape[2])
+        if not 1 <= b <= self.max_batch:
+            raise ValueError(f"batch {b} outside [1, {self.max_batch}]")
+        slot = (self._next_ticket - 1) % self.pipeline_depth
+        prev = self._inflight[slot]
+        if prev is not None and not prev.done:
+            prev._retire()
+        if x.is_cuda:
+            torch.cuda.current_stream(x.device).synchronize()
+        ticket = C.c_uint64()
+        L.check(self.lib.ixb_session_submit_frames(self._h, C.c_void_p(x.data_ptr()), b, w, h, 3 * w, 3 * w * h,
+                                                   C.byref(ticket)))
+        return self._track(DetectHandle(self, ticket.value, b, x), slot, b)
+
+    def run_frame(self, img_bgr: Any, max_detections: int = 300):
+        """One BGR frame [H, W, 3] to detections, synchronously: the reference's ``ignite_run``
+        (c_api/ignite.h:80-88) through the C ABI's ``ixb_run_frame``. Returns a list of
+        (x0, y0, w, h, score, class_id, class_name)."""
+        if self._decoder is None:
+            raise RuntimeError("call set_detect() before detection runs")
+        self._drain()
+        a = np.ascontiguousarray(img_bgr, dtype=np.uint8)
+        if a.ndim != 3 or a.shape[2] != 3:
+            raise ValueError(f"expected a BGR frame [H, W, 3], got {a.shape}")
+        out = (L.Detection * max(1, int(max_detections)))()
+        n = L.check(self.lib.ixb_run_frame(self._h, a.ctypes.data_as(C.c_void_p), a.shape[1], a.shape[0],
+                                           3 * a.shape[1], out, int(max_detections)))
+        self._next_ticket += 1          # the engine's ticket of that run
+        return [(d.x0, d.y0, d.w, d.h, d.score, d.class_id, d.class_name.decode()) for d in out[:n]]
+
+    @property
+    def last_timings(self) -> Dict[str, float]:
+        """Stages of the last completed detection run (the reference's ``ignite_get_last_timings``)."""
+        t = L.Timings()
+        L.check(self.lib.ixb_session_last_timings(self._h, C.byref(t)))
+        return {k: float(getattr(t, k)) for k, _ in L.Timings._fields_}
+
+    def decode_predictions(self, batch: Optional[int] = None):
+        """The dense decode of the heads in the device egress, on the GPU: float32 CUDA tensor
+        [B, 84, anchors] (the reference's ``decode_yolo_predictions``, runtime/session.py:1223-1278)."""
+        from .decode import dense_heads
+        torch = _torch()
+        b = int(batch or getattr(self, "_last_batch", self._staged) or 1)
+        heads = dense_heads(self.layout, self.plan.img_w)
+        total = sum(int(h.grid) ** 2 for h in heads)
+        out = torch.empty((b, 4 + 80, total), dtype=torch.float32, device=self.device)
+        eg = self.arena[self.plan.egress_offset:self.plan.egress_offset + b * self.out_bytes]
+        L.check(self.lib.ixb_decode_dense(heads, 80, C.c_void_p(eg.data_ptr()), b, self.out_bytes,
+                                          C.c_void_p(out.data_ptr()), C.c_void_p(self.stream_handle)))
+        torch.cuda.synchronize(self.device)
+        return out
+
 
     def stage_image(self, img_bgr: Any):
         """Letterbox, resize and quantize one BGR frame into the stem's input on the device (the

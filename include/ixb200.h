@@ -43,6 +43,7 @@ extern "C" {
 #define IXB_ERR_TIMEOUT -3    /* the host wait ran out */
 #define IXB_ERR_DEVICE -4     /* a kernel's bounded wait gave up (device error flag set) */
 #define IXB_ERR_UNSUPPORTED -5
+#define IXB_ERR_CAPACITY -6   /* more detections survive NMS than the session's capacity */
 
 #define IXB_MAX_SEGS 4
 #define IXB_API_VERSION 9
@@ -317,6 +318,79 @@ typedef struct ixb_decode_desc {
 int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
                     const float* letterbox, int32_t capacity, float* boxes, float* scores, int32_t* classes,
                     int32_t* counts, void* stream);
+
+/* Dense detect decode on the GPU: the reference's InferenceSession.decode_yolo_predictions
+ * (runtime/session.py:1223-1278), float32 [batch][4 + num_classes][sum of grid^2] (device memory)
+ * from `batch` images of int8 heads (device memory, image i at egress + i * egress_image_bytes).
+ * Per level: dequantize v = (q - zero_point) * scale, DFL softmax over 16 bins per box side and
+ * its expectation, corners (cell - d) * stride and (cell + d) * stride around the grid cell,
+ * centre-size xywh, and the class sigmoid. float32 with CUDA's expf: within a few ulp of the
+ * reference's numpy float32, not bit for bit. Enqueued on `stream`. */
+typedef struct ixb_dense_head {
+  uint64_t box_offset, cls_offset;   /* byte offsets of the 64-channel box and the class head in an image's egress */
+  float box_scale;
+  int32_t box_zero_point;
+  float cls_scale;
+  int32_t cls_zero_point;
+  int32_t grid;                      /* the level's grid is grid x grid anchors */
+  float stride;                      /* pixels per grid cell (8, 16, 32) */
+} ixb_dense_head;
+int ixb_decode_dense(const ixb_dense_head* heads, int32_t num_classes, const int8_t* egress, int batch,
+                     uint64_t egress_image_bytes, float* out, void* stream);
+
+/* Detection stage of a session: the reference's ignite_run / ignite_run_async / ignite_wait
+ * contract (c_api/ignite.h:80-125, ignite.cpp:640-980): frames or images in, detections out.
+ * After the network, the GPU decode + NMS of ixb_decode_yolo runs on the compute stream and only
+ * the detections (counts, boxes, scores, classes) travel back to the host, instead of the heads.
+ * ixb_session_set_detect configures it once: the decode descriptor (tables and anchors in device
+ * memory owned by the caller, valid while the session uses them), the class heads' scales and zero
+ * points (for ixb_session_set_thresholds, the reference's ignite_set_thresholds, ignite.h:141) and
+ * the capacity per image (1 .. 8400). */
+typedef struct ixb_detection {     /* the reference's ignite_detection_t (c_api/ignite.h:40-48) */
+  float x0, y0, w, h;              /* top-left corner and size in source-image pixels */
+  float score;
+  int32_t class_id;
+  char class_name[32];             /* from ixb_session_set_class_names, else empty */
+} ixb_detection;
+typedef struct ixb_timings {       /* the reference's ignite_timings_t (c_api/ignite.h:53-58) */
+  double preprocess_ms;            /* letterbox + quantize on the GPU (frames runs; 0 for images runs) */
+  double gpu_exec_ms;              /* the network (CUDA events around the graph) */
+  double postprocess_ms;           /* decode + NMS on the GPU */
+  double glass_to_glass_ms;        /* host clock from the submit to the completed wait */
+} ixb_timings;
+typedef struct ixb_detect_config {
+  ixb_decode_desc decode;
+  float cls_scale[3];
+  int32_t cls_zero_point[3];
+  int32_t capacity;
+} ixb_detect_config;
+int ixb_session_set_detect(ixb_session* s, const ixb_detect_config* cfg);
+int ixb_session_set_thresholds(ixb_session* s, float conf, float iou);
+int ixb_session_set_class_names(ixb_session* s, const char* const* names, int n);
+/* Pipelined detection runs, ticketed like ixb_session_submit (same ring, same slots):
+ * submit_detect takes `batch` uint8 [3][H][W] images at the model size (host or device memory)
+ * and optional letterbox rows float [batch][3] (pad_top, pad_left, scale; NULL: none);
+ * submit_frames takes `batch` BGR uint8 frames of src_w x src_h (row stride src_stride, frame_bytes
+ * apart, host or device memory), copies them in, letterboxes and quantizes them on the GPU
+ * (ixb_letterbox_frames) and runs the network on them. Both end with decode + NMS on the GPU and
+ * one copy of the detections back. ixb_session_detections waits for the ticket and points into
+ * the session's pinned host copy of its detections (valid until the slot is reused, depth submits
+ * later): counts [batch] (-3 where more than capacity survive), boxes [batch][capacity][4],
+ * scores and classes [batch][capacity]. ixb_session_wait_detections is the reference's ignite_wait:
+ * it fills up to max_detections entries for one image and returns how many (IXB_ERR_CAPACITY when
+ * more than the capacity survived). ixb_run_frame is the reference's ignite_run: one frame,
+ * synchronous. ixb_session_last_timings gives the stages of the last completed detection run. */
+int ixb_session_submit_detect(ixb_session* s, const uint8_t* images, int batch, const float* letterbox,
+                              uint64_t* ticket);
+int ixb_session_submit_frames(ixb_session* s, const uint8_t* frames, int batch, int src_w, int src_h, int src_stride,
+                              uint64_t frame_bytes, uint64_t* ticket);
+int ixb_session_detections(ixb_session* s, uint64_t ticket, int timeout_ms, int32_t* batch, const int32_t** counts,
+                           const float** boxes, const float** scores, const int32_t** classes);
+int ixb_session_wait_detections(ixb_session* s, uint64_t ticket, int timeout_ms, int image, ixb_detection* out,
+                                int max_detections);
+int ixb_run_frame(ixb_session* s, const uint8_t* bgr, int width, int height, int stride, ixb_detection* out,
+                  int max_detections);
+int ixb_session_last_timings(ixb_session* s, ixb_timings* t);
 
 /* Letterbox ingress, the reference's pipelines/preprocess_simd.c fused_preprocess_bgr_to_c8_plane
  * (:331-590; graph_session.py stage_image :866-889) on the GPU, byte for byte: `batch` BGR uint8

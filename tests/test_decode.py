@@ -63,3 +63,18 @@ def test_reference_decode_reproduces_golden(golden):
             assert np.array_equal(b.view(np.uint32), g[f"c{ci}_i{i}_boxes"].view(np.uint32))
             assert np.array_equal(s.view(np.uint32), g[f"c{ci}_i{i}_scores"].view(np.uint32))
             assert np.array_equal(c, g[f"c{ci}_i{i}_classes"])
+
+
+def test_dense_decode_restatement_equals_the_reference(golden_dir):
+    """InferenceSession.decode_yolo_predictions (numpy) against the reference's own
+    runtime/session.py decode_yolo_predictions on the same int8 heads (tests/golden/make_dense_golden.py)."""
+    from ignite_xdna_b200.session import InferenceSession
+    g = np.load(golden_dir / "dense_golden.npz")
+    names = [str(n) for n in g["names"]]
+    heads = {}
+    for n, off, shp in zip(names, g["offsets"], g["shapes"]):
+        size = int(np.prod(shp))
+        heads[n] = g["egress"][:, off:off + size].reshape((2,) + tuple(int(x) for x in shp))
+    heads["scales"] = {n: (float(s), 0) for n, s in zip(names, g["scales"])}
+    out = InferenceSession.decode_yolo_predictions(heads)
+    np.testing.assert_array_equal(out, g["out"])
