@@ -264,23 +264,19 @@ def per_layer_rows(sess, batch, trace, int8_peak_tops):
     return rows
 
 
-def copy_ceiling(sess, pinned_in, pinned_out, world, local, iters=5):
-    """Pure-copy calibration on every rank at once, no compute: the images' pinned H2D and the heads'
-    pinned D2H of one step, alone and together, on the session's copy streams. Returns aggregate
-    GB/s over all ranks (bytes of all ranks / the slowest rank's time) and the e2e images/s these
-    copies alone allow."""
+def copy_ceiling(B, in_bytes, out_bytes, world, local, iters=5):
+    """Pure-copy calibration on every rank at once, no compute: one step's images (pinned host ->
+    HBM) and heads (HBM -> pinned host), alone and together, each direction on its own stream.
+    Returns aggregate GB/s over all ranks (bytes of all ranks / the slowest rank's time) and the
+    e2e images/s these copies alone allow."""
     import torch
     dev = torch.device("cuda", local)
-    h_compute, h_h2d, h_d2h = sess.streams()
-    s_h2d = torch.cuda.ExternalStream(h_h2d, device=dev)
-    s_d2h = torch.cuda.ExternalStream(h_d2h, device=dev)
-    B = pinned_in.shape[0]
-    n_in = pinned_in.numel()
-    n_out = B * sess.out_bytes
-    dst_in = sess.arena[sess.plan.images_offset:sess.plan.images_offset + n_in]
-    src_out = sess.arena[sess.plan.egress_offset:sess.plan.egress_offset + n_out]
-    host_in = pinned_in.reshape(-1)
-    host_out = torch.from_numpy(pinned_out.reshape(-1)[:n_out]).view(torch.uint8)
+    s_h2d, s_d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    n_in, n_out = B * in_bytes, B * out_bytes
+    host_in = torch.empty(n_in, dtype=torch.uint8, pin_memory=True)
+    host_out = torch.empty(n_out, dtype=torch.uint8, pin_memory=True)
+    dst_in = torch.empty(n_in, dtype=torch.uint8, device=dev)
+    src_out = torch.zeros(n_out, dtype=torch.uint8, device=dev)
 
     def timed(h2d, d2h):
         barrier(world)
@@ -304,11 +300,12 @@ def copy_ceiling(sess, pinned_in, pinned_out, world, local, iters=5):
 
     timed(True, True)                                     # warm-up
     t_in, t_out, t_both = timed(True, False), timed(False, True), timed(True, True)
+    torch.cuda.synchronize(local)
     gbs = lambda nb, ms: round(world * nb / (ms * 1e-3) / 1e9, 1)  # noqa: E731
     return {"h2d_gbs": gbs(n_in, t_in), "d2h_gbs": gbs(n_out, t_out),
             "both_ms_per_step": round(t_both, 4), "h2d_bytes_per_rank": int(n_in), "d2h_bytes_per_rank": int(n_out),
             "images_s_ceiling": round(world * B / (t_both * 1e-3), 1),
-            "note": "pinned host <-> HBM copies only, every rank at once, the session's copy streams; "
+            "note": "pinned host <-> HBM copies only, every rank at once, one stream per direction; "
                     "images_s_ceiling = what the images-in + heads-out copies alone allow"}
 
 
@@ -441,7 +438,7 @@ def run_gpu(args):
     ms_e2e = max_over_ranks(ms_e2e, world, local)
     ms_e2e_heads = max_over_ranks(ms_e2e_heads, world, local)
     det_d2h = (B * 4 + 15) // 16 * 16 + B * DET_CAPACITY * 24
-    ceiling = copy_ceiling(sess, pinned_in, pinned_out[0], world, local)
+    ceiling = copy_ceiling(B, sess.in_image_bytes, sess.out_bytes, world, local)
     # per-layer device times inside the step's own CUDA graph (programmatic dependent launch on):
     # each conv from the moment its inputs were ready to its last CTA's end
     hbm_peak, bf16_peak, peak_kind = load_peaks()

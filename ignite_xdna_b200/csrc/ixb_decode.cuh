@@ -22,8 +22,6 @@ namespace ixb {
 constexpr int kDecodeThreads = 1024;
 constexpr int kDecodeMaxAnchors = 8400;
 constexpr int kDfl = 16;
-constexpr int kDecodeMaxClasses = 256;
-constexpr int kDecodeMaxGap = 4;  // class gaps checked explicitly before the per-class NMS is trusted
 
 struct DecodeHeadDev {
   long long box_off, cls_off;   // byte offsets of the box and class heads inside one image's egress
@@ -117,10 +115,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   int16_t* s_anchor = reinterpret_cast<int16_t*>(s_box + kDecodeMaxAnchors);  // [8400] anchor index
   uint8_t* s_class = reinterpret_cast<uint8_t*>(s_anchor + kDecodeMaxAnchors);  // [8400]
   uint16_t* s_order = reinterpret_cast<uint16_t*>(s_class + kDecodeMaxAnchors); // [16384] sort / kept list
-  __shared__ int s_n, s_kept, s_flag, s_nv, s_slow;
-  __shared__ double s_maxc[kDecodeThreads / 32], s_lo[kDecodeThreads / 32];
-  __shared__ int s_cnt[kDecodeMaxClasses], s_start[kDecodeMaxClasses], s_cur[kDecodeMaxClasses];
-  __shared__ uint32_t s_keep[(kDecodeMaxAnchors + 31) / 32];
+  __shared__ int s_n, s_kept, s_nv;
+  __shared__ double s_maxc[kDecodeThreads / 32];
+  __shared__ uint16_t s_chunk[32];
+  __shared__ unsigned s_mask[32];
+  __shared__ int s_sup[32];
 
   const int img = blockIdx.x, tid = threadIdx.x;
   const int8_t* eg = p.egress + (long long)img * p.egress_image_bytes;
@@ -228,194 +227,58 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   for (int w = 0; w < kDecodeThreads / 32; ++w) maxc = fmax(maxc, s_maxc[w]);
   const double off_step = __dadd_rn(maxc, 1.0);
 
-  // 4. NMS. Boxes of different classes are offset by class * off_step, so once the class gaps at
-  //    which two offset boxes can still meet have been checked pair by pair (and no box is
-  //    degenerate), no box suppresses one of another class: the greedy suppression over the
-  //    global order then equals each class's own greedy suppression over its candidates in that
-  //    order, which the warps run in parallel (fast path). Otherwise, or when any check fails,
-  //    the greedy loop runs over the global order as written (slow path).
-  if (tid == 0) {
-    s_nv = n;
-    s_slow = !(p.iou >= 0.f) || p.num_classes > kDecodeMaxClasses;
-  }
-  for (int c = tid; c < kDecodeMaxClasses; c += kDecodeThreads) s_cnt[c] = 0;
-  for (int w = tid; w < (kDecodeMaxAnchors + 31) / 32; w += kDecodeThreads) s_keep[w] = 0u;
+  // 4. Greedy NMS over the global order, 32 candidates at a time. A candidate is kept when no
+  //    earlier kept candidate suppresses it. For a chunk of 32 (in order): every warp takes one
+  //    candidate and its lanes test it against all candidates kept before the chunk; then the
+  //    chunk's own 32 x 32 pairs are tested (thread (a, b): does earlier b suppress later a);
+  //    then one warp resolves the chunk in order (a candidate survives if nothing kept before the
+  //    chunk and no kept earlier member of the chunk suppresses it) and appends the kept ones.
+  //    Exactly the sequential greedy loop, with a block barrier per 32 candidates instead of per
+  //    candidate. Kept ids overwrite the front of s_order, behind the chunk being read.
+  if (tid == 0) s_nv = n;
   __syncthreads();
-  // candidates strictly above the threshold form a prefix of the order; degenerate or
-  // non-finite boxes force the slow path; lo = the lowest corner coordinate
-  double lo = 0.0;
-  bool any_lo = false;
-  for (int i = tid; i < n; i += kDecodeThreads) {
-    const uint16_t ci = s_order[i];
-    if (!(s_score[ci] > p.conf)) {
-      atomicMin(&s_nv, i);
-      continue;
-    }
-    const float4 b = s_box[ci];
-    if (!isfinite(b.x) || !isfinite(b.y) || !isfinite(b.z) || !isfinite(b.w) ||
-        !(__dmul_rn((double)b.z, (double)b.w) > DBL_EPSILON))
-      s_slow = 1;
-    const double m = fmin((double)b.x, (double)b.y);
-    lo = any_lo ? fmin(lo, m) : m;
-    any_lo = true;
-  }
-  if (!any_lo) lo = 1e300;
-  for (int o = 16; o > 0; o >>= 1) lo = fmin(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-  if ((tid & 31) == 0) s_lo[tid >> 5] = lo;
+  for (int i = tid; i < n; i += kDecodeThreads)
+    if (!(s_score[s_order[i]] > p.conf)) atomicMin(&s_nv, i);  // the rest: a prefix of the order
   __syncthreads();
   const int nv = s_nv;
-  double lo_all = 1e300;
-  for (int w = 0; w < kDecodeThreads / 32; ++w) lo_all = fmin(lo_all, s_lo[w]);
-  // offset boxes of classes g apart can meet only while lo + g * off_step <= maxc (plus a margin
-  // far above the rounding of the doubles involved)
-  int gap = 0;
-  while (gap <= kDecodeMaxGap) {
-    const double reach = (double)(gap + 1) * off_step;
-    if (lo_all + reach > maxc + 1e-3 + 1e-9 * (fabs(lo_all) + reach + fabs(maxc))) break;
-    ++gap;
-  }
   const int warp = tid >> 5, lane = tid & 31;
-  if (!s_slow && gap <= kDecodeMaxGap && nv > 0) {
-    // per-class lists in global order: counts, starts, then each warp places its own classes'
-    // candidates (class % 32 == warp) in order
-    for (int i = tid; i < nv; i += kDecodeThreads) atomicAdd(&s_cnt[s_class[s_order[i]]], 1);
+  for (int r0 = 0; r0 < nv; r0 += 32) {
+    const int cn = min(32, nv - r0);
+    if (tid < 32) s_chunk[tid] = tid < cn ? s_order[r0 + tid] : (uint16_t)0;
     __syncthreads();
-    if (warp == 0) {
-      int run = 0;
-      for (int c0 = 0; c0 < kDecodeMaxClasses; c0 += 32) {
-        const int v = s_cnt[c0 + lane];
-        int x = v;
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, x, o);
-          if (lane >= o) x += y;
-        }
-        s_start[c0 + lane] = run + x - v;
-        s_cur[c0 + lane] = 0;
-        run += __shfl_sync(0xffffffffu, x, 31);
-      }
-    }
-    __syncthreads();
-    uint16_t* s_list = reinterpret_cast<uint16_t*>(s_anchor);  // the anchors are not needed after the sort
-    for (int base = 0; base < nv; base += 32) {
-      const int i = base + lane;
-      const int c = i < nv ? (int)s_class[s_order[i]] : -1;
-      unsigned mine = __ballot_sync(0xffffffffu, c >= 0 && (c & 31) == warp);
-      while (mine) {
-        const int l = __ffs(mine) - 1;
-        mine &= mine - 1;
-        const int cl = __shfl_sync(0xffffffffu, c, l);
-        if (lane == 0) s_list[s_start[cl] + s_cur[cl]++] = (uint16_t)(base + l);
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-    // the class gaps at which boxes can meet: every pair checked; one suppressing pair -> slow path
-    for (int g = 1; g <= gap; ++g) {
-      for (int c = warp; c + g < p.num_classes; c += kDecodeThreads / 32) {
-        const int na = s_cnt[c], nb = s_cnt[c + g];
-        const uint16_t* la = s_list + s_start[c];
-        const uint16_t* lb = s_list + s_start[c + g];
-        const double oa = __dmul_rn((double)c, off_step), ob = __dmul_rn((double)(c + g), off_step);
-        if ((long long)na * nb > (1 << 18)) {  // too many pairs to check: the slow path decides
-          if (lane == 0) s_slow = 1;
-          continue;
-        }
-        bool hit = false;
-        for (int q = lane; q < na * nb; q += 32) {
-          const uint16_t a = s_order[la[q / nb]], b = s_order[lb[q % nb]];
-          hit = hit || suppresses(s_box[a], oa, s_box[b], ob, p.iou);
-        }
-        if (__any_sync(0xffffffffu, hit) && lane == 0) s_slow = 1;
-      }
-    }
-    __syncthreads();
-  } else if (tid == 0) {
-    s_slow = 1;
-  }
-  __syncthreads();
-  if (!s_slow) {
-    // per-class greedy: warp w runs the classes c % 32 == w; a candidate is kept when no earlier
-    // kept candidate of its class suppresses it (keep bits indexed by global order position)
-    const uint16_t* s_list = reinterpret_cast<const uint16_t*>(s_anchor);
-    for (int c = warp; c < p.num_classes; c += kDecodeThreads / 32) {
-      const int m = s_cnt[c];
-      const uint16_t* lc = s_list + s_start[c];
-      const double oc = __dmul_rn((double)c, off_step);
-      for (int k = 0; k < m; ++k) {
-        const int pk = lc[k];
-        const float4 bi = s_box[s_order[pk]];
-        bool sup = false;
-        for (int j = lane; j < k; j += 32) {
-          const int pj = lc[j];
-          if ((s_keep[pj >> 5] >> (pj & 31)) & 1u) sup = sup || suppresses(bi, oc, s_box[s_order[pj]], oc, p.iou);
-        }
-        if (!__any_sync(0xffffffffu, sup) && lane == 0) atomicOr(&s_keep[pk >> 5], 1u << (pk & 31));
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-    // kept ids in global order to the front of s_order (rank = kept bits before the position)
-    if (warp == 0) {
-      int run = 0;
-      for (int w0 = 0; w0 < (nv + 31) / 32; w0 += 32) {
-        const int w = w0 + lane;
-        const int v = w < (nv + 31) / 32 ? __popc(s_keep[w]) : 0;
-        int x = v;
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, x, o);
-          if (lane >= o) x += y;
-        }
-        // exclusive prefix of the kept bits before word w, in word w's slot of s_start / s_cur
-        // (the class lists are done with)
-        if (w < (nv + 31) / 32) {
-          if (w < kDecodeMaxClasses) s_start[w] = run + x - v;
-          else s_cur[w - kDecodeMaxClasses] = run + x - v;
-        }
-        run += __shfl_sync(0xffffffffu, x, 31);
-      }
-      if (lane == 0) s_kept = run;
-    }
-    __syncthreads();
-    // s_order[0 .. kept) <- kept ids; positions are read before any write lands (two passes)
-    uint16_t id_of[(kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads];
-    int rank_of[(kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads];
-#pragma unroll
-    for (int t = 0; t < (kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads; ++t) {
-      const int i = tid + t * kDecodeThreads;
-      rank_of[t] = -1;
-      if (i < nv && ((s_keep[i >> 5] >> (i & 31)) & 1u)) {
-        const int w = i >> 5;
-        const int before = __popc(s_keep[w] & ((1u << (i & 31)) - 1u));
-        rank_of[t] = (w < kDecodeMaxClasses ? s_start[w] : s_cur[w - kDecodeMaxClasses]) + before;
-        id_of[t] = s_order[i];
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < (kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads; ++t)
-      if (rank_of[t] >= 0) s_order[rank_of[t]] = id_of[t];
-    __syncthreads();
-  } else {
-    // slow path: greedy suppression in score order; kept slot ids overwrite the front of s_order,
-    // which only ever trails the position being read
-    for (int r = 0; r < n; ++r) {
-      const uint16_t ci = s_order[r];
-      if (!(s_score[ci] > p.conf)) break;  // sorted: nothing later passes the strict threshold
+    const int kept = s_kept;
+    if (warp < cn) {
+      const uint16_t ci = s_chunk[warp];
       const float4 bi = s_box[ci];
       const double oi = __dmul_rn((double)s_class[ci], off_step);
-      int sup = 0;
-      const int kept = s_kept;
-      for (int k = tid; k < kept; k += kDecodeThreads) {
+      bool sup = false;
+      for (int k = lane; k < kept; k += 32) {
         const uint16_t ck = s_order[k];
-        if (suppresses(bi, oi, s_box[ck], __dmul_rn((double)s_class[ck], off_step), p.iou)) sup = 1;
+        sup = sup || suppresses(bi, oi, s_box[ck], __dmul_rn((double)s_class[ck], off_step), p.iou);
       }
-      sup = __syncthreads_or(sup);
-      if (!sup && tid == 0) {
-        s_order[s_kept] = ci;
-        s_kept = s_kept + 1;
+      const bool by_kept = __any_sync(0xffffffffu, sup);
+      // earlier chunk members b < warp that would suppress this one if kept
+      bool m = false;
+      if (lane < warp) {
+        const uint16_t cb = s_chunk[lane];
+        m = suppresses(bi, oi, s_box[cb], __dmul_rn((double)s_class[cb], off_step), p.iou);
       }
-      __syncthreads();
+      const unsigned mask = __ballot_sync(0xffffffffu, m);
+      if (lane == 0) {
+        s_mask[warp] = mask;
+        s_sup[warp] = by_kept ? 1 : 0;
+      }
     }
+    __syncthreads();
+    if (warp == 0) {
+      // in order: a survives unless suppressed by an earlier kept candidate
+      unsigned keep = 0u;
+      for (int a = 0; a < cn; ++a)
+        if (!s_sup[a] && !(s_mask[a] & keep)) keep |= 1u << a;
+      if ((keep >> lane) & 1u) s_order[kept + __popc(keep & ((1u << lane) - 1u))] = s_chunk[lane];
+      if (lane == 0) s_kept = kept + __popc(keep);
+    }
+    __syncthreads();
   }
 
   // 5. detections in kept order
@@ -434,8 +297,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   if (tid == 0) p.out_count[img] = kept;
 }
 
-// Dynamic shared memory: scores, boxes, anchors (reused as the per-class lists after the sort),
-// classes, and the sort order.
+// Dynamic shared memory: scores, boxes, anchors, classes, and the sort order.
 constexpr int decode_smem_bytes() {
   return kDecodeMaxAnchors * (4 + 16 + 2 + 1) + 16384 * 2 + 16;
 }

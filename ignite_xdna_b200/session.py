@@ -84,13 +84,23 @@ class DetectHandle:
         self.batch = int(batch)
         self._keep = keep
         self._result = None
+        self._error: Optional[Exception] = None
 
     @property
     def done(self) -> bool:
-        return self._result is not None
+        return self._result is not None or self._error is not None
+
+    @staticmethod
+    def _view(ptr: int, dtype, shape):
+        """A numpy view of the session's pinned detections (no copy)."""
+        n = int(np.prod(shape))
+        ct = {np.float32: C.c_float, np.int32: C.c_int32}[dtype]
+        return np.frombuffer((ct * max(n, 1)).from_address(ptr), dtype=dtype, count=n).reshape(shape)
 
     def wait(self, timeout_ms: int = 2000):
         from .decode import Detections
+        if self._error is not None:
+            raise self._error
         if self._result is None:
             s = self._s
             n = C.c_int32()
@@ -101,22 +111,27 @@ class DetectHandle:
                 raise TimeoutError(f"submitted run {self.ticket} did not complete within {timeout_ms} ms")
             L.check(rc)
             b, cap = int(n.value), s._det_capacity
-            counts = np.ctypeslib.as_array(C.cast(ptrs[0], C.POINTER(C.c_int32)), (b,)).copy()
-            boxes = np.ctypeslib.as_array(C.cast(ptrs[1], C.POINTER(C.c_float)), (b, cap, 4))
-            scores = np.ctypeslib.as_array(C.cast(ptrs[2], C.POINTER(C.c_float)), (b, cap))
-            classes = np.ctypeslib.as_array(C.cast(ptrs[3], C.POINTER(C.c_int32)), (b, cap))
-            out = []
-            for i in range(b):
-                k = int(counts[i])
-                if k < 0:
-                    raise RuntimeError(f"image {i}: more than {cap} detections survive NMS")
-                out.append(Detections(boxes[i, :k].copy(), scores[i, :k].copy(), classes[i, :k].copy()))
-            self._result = out
+            counts = self._view(ptrs[0].value, np.int32, (b,)).copy()
+            boxes = self._view(ptrs[1].value, np.float32, (b, cap, 4))
+            scores = self._view(ptrs[2].value, np.float32, (b, cap))
+            classes = self._view(ptrs[3].value, np.int32, (b, cap))
             self._keep = None
+            over = [i for i in range(b) if counts[i] < 0]
+            if over:
+                self._error = RuntimeError(f"image {over[0]}: more than {cap} detections survive NMS")
+                raise self._error
+            self._result = [Detections(boxes[i, :k].copy(), scores[i, :k].copy(), classes[i, :k].copy())
+                            for i, k in enumerate(int(c) for c in counts)]
         return self._result
 
     def _retire(self) -> None:
-        self.wait(60000)
+        """Complete the run and copy its detections out of the slot about to be reused; a failed
+        run keeps its error for its own wait."""
+        try:
+            self.wait(60000)
+        except RuntimeError:
+            if self._error is None:
+                raise
 
 
 class GraphSession:
@@ -611,9 +626,16 @@ class InferenceSession:
 
     @classmethod
     def from_file(cls, path: Union[str, Path], device_index: int = 0, max_batch: int = 64, **kwargs) -> GraphSession:
-        """Open a pickled ``GraphIR`` (as ``save_graph`` writes) or a ``yolov8{n,s,m}[_<imgsz>]`` spec name."""
+        """Open an ``.ignite`` container holding a quantized graph (``container.save_container``), a
+        pickled ``GraphIR`` (as ``save_graph`` writes), or a ``yolov8{n,s,m}[_<imgsz>]`` spec name
+        (the reference's ``InferenceSession.from_file``, runtime/session.py:1496)."""
         p = Path(path)
         if p.exists():
+            with open(p, "rb") as f:
+                magic = f.read(4)
+            if magic == b"IGNT":
+                from .container import load_container
+                return GraphSession(load_container(p), device_index=device_index, max_batch=max_batch)
             import pickle
             with open(p, "rb") as f:
                 ir = pickle.load(f)
@@ -667,6 +689,11 @@ class InferenceSession:
 
 
 def save_graph(ir: GraphIR, path: Union[str, Path]) -> None:
+    """Write ``ir`` as an ``.ignite`` container (a path ending in .ignite) or a pickle."""
+    if str(path).endswith(".ignite"):
+        from .container import save_container
+        save_container(ir, path, model_name=Path(path).stem)
+        return
     import pickle
     with open(path, "wb") as f:
         pickle.dump(ir, f)

@@ -247,3 +247,33 @@ def test_submitted_runs_match_synchronous_runs(depth):
     assert np.array_equal(np.array(sess.run(batches[3])), ref[3])
     assert np.array_equal(h.wait(), ref[1])
     sess.close()
+
+
+def test_container_opens_and_matches_reference_hashes(hashes, tmp_path):
+    """InferenceSession.from_file on an .ignite container (written by the engine's container writer,
+    which reproduces the reference's IgniteModelWriter byte for byte): the heads at 640x640 equal the
+    reference's own run_direct hashes."""
+    from ignite_xdna_b200 import save_graph
+    h = hashes["yolov8n"]
+    p = tmp_path / "yolov8n.ignite"
+    save_graph(build_yolov8("n", imgsz=640), p)
+    sess = InferenceSession.from_file(p, max_batch=1)
+    out = sess.run_yolo_monolithic(random_images(1, 640, seed=h["image_seed"]))
+    for name, v in h["heads"].items():
+        assert sha(out[name][0]) == v, name
+    sess.close()
+
+
+@pytest.mark.parametrize("variant", ["s", "m"])
+def test_yolov8sm_batch32_rows_are_independent_and_exact(variant):
+    """YOLOv8s / YOLOv8m at the batch of their benchmark configuration (32 per GPU, 640x640): rows of
+    the batch equal separate runs of those images, and one row equals the oracle."""
+    sess = InferenceSession.from_spec(f"yolov8{variant}", imgsz=640, max_batch=32)
+    imgs = random_images(32, 640, seed=50)
+    full = np.array(sess.run_yolo_monolithic(imgs)["raw_output"])
+    for j in (0, 31):
+        assert np.array_equal(full[j], np.array(sess.run_yolo_monolithic(imgs[j:j + 1])["raw_output"])[0]), j
+    part = np.array(sess.run_yolo_monolithic(imgs[9:14])["raw_output"])
+    assert np.array_equal(full[9:14], part)
+    assert np.array_equal(full[31:32], O.run_batch_egress(sess.ir, imgs[31:32]))
+    sess.close()
