@@ -863,11 +863,24 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
   p.K = K;
   const int sms = sm_count();
   if (bsrc == GEMM_B_W4) {
-    // every B element is unpacked once per tile: as many 128-row blocks per tile as M needs
-    // (up to 4), and BN = 256 / MT, so the unpack work per MMA stays small
-    p.mt = (int)std::min<long long>(4, (M + 127) / 128);
-    if (p.mt == 3) p.mt = 4;
-    p.bn = std::min(256 / p.mt, N);
+    // The tile (MT blocks of 128 rows x BN columns) minimising (waves of tiles over the SMs) x
+    // (the tile's MMA time per K step: MT MMAs of ~max(BN / 2, 32 + BN / 4) cycles, the
+    // operands' shared-memory reads bounding narrow ones); two accumulators must fit TMEM.
+    double best = 1e300;
+    const int mt_max = (int)std::min<long long>(4, (M + 127) / 128);
+    for (int mt : {1, 2, 4}) {
+      if (mt > mt_max && mt != 1) continue;
+      for (int bn = 16; bn <= std::min(256 / mt, round_up(N, 16)); bn += 16) {
+        const long long tiles = ((M + 128LL * mt - 1) / (128LL * mt)) * ((N + bn - 1) / bn);
+        const long long waves = (tiles + sms - 1) / sms;
+        const double cost = (double)waves * mt * std::max(bn / 2.0, 32.0 + bn / 4.0);
+        if (cost < best - 1e-9) {
+          best = cost;
+          p.mt = mt;
+          p.bn = bn;
+        }
+      }
+    }
   } else {
     p.bn = N <= 256 ? N : (N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 256));
     p.mt = 1;
@@ -884,7 +897,12 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
   p.m_tiles = (int)((M + 128LL * p.mt - 1) / (128LL * p.mt));
   p.kblocks = (K + kGemmBK - 1) / kGemmBK;
   p.stage_bytes = p.mt * kGemmABlock + p.bn * kGemmBK;
-  p.stage_tx = bsrc == GEMM_B_W4 ? p.mt * kGemmABlock : p.stage_bytes;
+  p.stage_tx = p.stage_bytes;
+  if (bsrc == GEMM_B_W4) {  // the packed int4 tile lands after the unpacked B operand
+    p.raw_off = p.stage_bytes;
+    p.stage_bytes = round_up(p.stage_bytes + p.bn * (kGemmBK / 2), 1024);
+    p.stage_tx = p.mt * kGemmABlock + p.bn * (kGemmBK / 2);
+  }
   const int budget = kSmemLimit - 1024 - 256;
   p.stages = std::min(kGemmMaxStages, budget / p.stage_bytes);
   if (p.stages < 2) {
@@ -904,6 +922,25 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
   }
   L.grid = (int)std::min<long long>(tiles, sms);
   L.smem = 1024 + p.bar_off + 256;
+  return 0;
+}
+
+// Tensor map of the W4A8 weight image's packed part: uint8 [N][K/2], boxes of 64 bytes (128
+// values, one group) by BN rows, no swizzle; rows past N read as zero.
+int encode_w4(CUtensorMap* map, const void* base, int N, int K, int box_rows, std::string& err) {
+  auto enc = tiled_encoder(err);
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)(K / 2), (cuuint64_t)N};
+  cuuint64_t strides[1] = {(cuuint64_t)(K / 2)};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    err = "cuTensorMapEncodeTiled failed for the W4A8 weights (" + std::to_string((int)r) + ")";
+    return -1;
+  }
   return 0;
 }
 
@@ -2066,6 +2103,7 @@ int ixb_w4a8_gemm(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   L.p.wq = image;
   L.p.eg = image + (uint64_t)N * (K / 2);
   if (encode_kmajor(&L.p.ta, a, M, K, 128, err)) return fail(IXB_ERR_CUDA, err);
+  if (encode_w4(&L.p.tb, image, N, K, L.p.bn, err)) return fail(IXB_ERR_CUDA, err);
   return launch_gemm<GEMM_B_W4>(L, static_cast<cudaStream_t>(stream));
 }
 
@@ -2084,6 +2122,7 @@ int ixb_u8i4_gemm_i32(const uint8_t* a, const uint8_t* image, int32_t* out, int 
   L.p.wq = image;
   L.p.eg = image + (uint64_t)N * (K / 2);
   if (encode_kmajor(&L.p.ta, a, M, K, 128, err)) return fail(IXB_ERR_CUDA, err);
+  if (encode_w4(&L.p.tb, image, N, K, L.p.bn, err)) return fail(IXB_ERR_CUDA, err);
   return launch_gemm<GEMM_B_W4>(L, static_cast<cudaStream_t>(stream));
 }
 
@@ -2092,9 +2131,12 @@ int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   if (!a || !image || !shift || !out) return fail(IXB_ERR_INVALID, "null argument");
   if (int r = check_w4a8_shape(N, K)) return r;
   if (!aligned16(a) || !aligned16(image)) return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
-  const int warps = 8;
-  w4a8_gemv_kernel<<<(N + warps - 1) / warps, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(
-      a, image, image + (uint64_t)N * (K / 2), shift, out, N, K);
+  const GemvPlan g = plan_gemv(N, K, sm_count());
+  if (g.stages < 2) return fail(IXB_ERR_INVALID, "two GEMV stages do not fit shared memory");
+  if (int r = ensure_smem_limit(w4a8_gemv_kernel, g.smem)) return r;
+  w4a8_gemv_kernel<<<g.grid, kGemvThreads, g.smem, static_cast<cudaStream_t>(stream)>>>(
+      a, image, image + (uint64_t)N * (K / 2), shift, out, N, K, g.cols_per_stage, g.warps_per_col, g.stages,
+      g.stage_bytes);
   IXB_CUDA(cudaGetLastError());
   return 0;
 }

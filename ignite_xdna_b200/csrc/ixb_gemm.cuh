@@ -33,10 +33,12 @@ enum : int { GEMM_OUT_SRS = 0, GEMM_OUT_I32 = 1 };
 
 struct GemmParams {
   alignas(64) CUtensorMap ta;  // A [M][K], box {128 B, 128 rows}, SWIZZLE_128B
-  alignas(64) CUtensorMap tb;  // B [N][K], box {128 B, BN rows}, SWIZZLE_128B
+  alignas(64) CUtensorMap tb;  // B [N][K], box {128 B, BN rows}, SWIZZLE_128B; W4A8: the packed
+                               // weights [N][K/2], box {64 B, BN rows}, no swizzle
   int M, N, K;
   int bn, mt, m_tiles, n_tiles, kblocks, stages;
   int stage_bytes, stage_tx, bar_off;
+  int raw_off;               // W4A8: offset of the packed int4 B tile inside a stage
   int acc_cols, tmem_cols;
   uint32_t idesc;
   int out_kind;
@@ -74,10 +76,12 @@ enum : int { GEMM_B_TMA = 0, GEMM_B_W4 = 1 };
 constexpr int kW4Warps = 4;  // warps unpacking int4 weights into the B stage (GEMM_B_W4)
 constexpr int gemm_threads(int epi, int bsrc) { return 32 * (epi + 2 + (bsrc == GEMM_B_W4 ? kW4Warps : 0)); }
 
-// B warps of the W4A8 GEMM: per stage, BN rows x 128 values of K (one group) from the packed
-// image, 16 values (8 bytes) per item, 8 items per row so a row's 64 bytes load coalesced; each
-// item becomes one 16-byte chunk of the 128-byte swizzled row (chunk c at c ^ (row % 8)).
-__device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty,
+// B warps of the W4A8 GEMM: per stage the TMA has brought the packed int4 tile (BN rows x 64
+// bytes = 128 values of K, one group) into shared memory with the A boxes; the warps turn it
+// into the int8 B operand, 16 values (8 packed bytes) per item into one 16-byte chunk of the
+// 128-byte swizzled row (chunk c at c ^ (row % 8)), scaled by the group's 2^-e. Reading the packed
+// tile from shared memory keeps global-memory latency out of the unpack loop.
+__device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* bfull,
                                            int ut) {
   constexpr int UT = kW4Warps * 32;
   const int S = p.stages, G = p.K / 128;
@@ -89,29 +93,28 @@ __device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, u
     const int ntile = t % p.n_tiles;
     const int n0 = ntile * p.bn;
     for (int kb = 0; kb < p.kblocks; ++kb) {
-      if (!mbar_wait(&empty[s], ph ^ 1)) return;
-      uint8_t* bst = smem + s * p.stage_bytes + p.mt * kGemmABlock;
+      if (!mbar_wait(&full[s], ph)) return;
+      uint8_t* st = smem + s * p.stage_bytes;
+      uint8_t* bst = st + p.mt * kGemmABlock;
+      const uint8_t* raw = st + p.raw_off;
       for (int i = ut; i < items; i += UT) {
         const int r = i >> 3, c = i & 7;
         const int n = n0 + r;
-        uint4 o = make_uint4(0, 0, 0, 0);
-        if (n < p.N) {
-          const uint2 w = __ldg(reinterpret_cast<const uint2*>(p.wq + (long long)n * (p.K / 2) + kb * 64 + c * 8));
-          const uint32_t e = __ldg(p.eg + (long long)n * G + kb);
-          o = make_uint4(w4_lo16(w.x), w4_hi16(w.x), w4_lo16(w.y), w4_hi16(w.y));
-          if (e) {
-            const uint32_t keep = (0xFFu >> e) * 0x01010101u;
-            const uint32_t fill = ((0xFFu << (8 - e)) & 0xFFu);
-            o.x = sra8_lanes(o.x, e, keep, fill);
-            o.y = sra8_lanes(o.y, e, keep, fill);
-            o.z = sra8_lanes(o.z, e, keep, fill);
-            o.w = sra8_lanes(o.w, e, keep, fill);
-          }
+        const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);  // zero past N (TMA fill)
+        const uint32_t e = n < p.N ? __ldg(p.eg + (long long)n * G + kb) : 0u;
+        uint4 o = make_uint4(w4_lo16(w.x), w4_hi16(w.x), w4_lo16(w.y), w4_hi16(w.y));
+        if (e) {
+          const uint32_t keep = (0xFFu >> e) * 0x01010101u;
+          const uint32_t fill = ((0xFFu << (8 - e)) & 0xFFu);
+          o.x = sra8_lanes(o.x, e, keep, fill);
+          o.y = sra8_lanes(o.y, e, keep, fill);
+          o.z = sra8_lanes(o.z, e, keep, fill);
+          o.w = sra8_lanes(o.w, e, keep, fill);
         }
         *reinterpret_cast<uint4*>(bst + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = o;
       }
       fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
-      mbar_arrive(&full[s]);
+      mbar_arrive(&bfull[s]);
       if (++s == S) {
         s = 0;
         ph ^= 1;
@@ -132,7 +135,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* done = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* bfull = done + 1;  // W4A8: the stage's B operand is unpacked
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bfull + kGemmMaxStages);
   const int tiles = p.m_tiles * p.n_tiles;
 
   if (warp == MW) {
@@ -141,8 +145,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
   }
   if (tid == PW * 32) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], BSRC == GEMM_B_W4 ? 1 + kW4Warps * 32 : 1);
+      mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&bfull[s], kW4Warps * 32);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -151,7 +156,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     mbar_init(done, 1);
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.ta) : "memory");
-    if (BSRC == GEMM_B_TMA) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tb) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tb) : "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -176,6 +181,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
           for (int b = 0; b < p.mt; ++b)
             tma_load_2d(st + b * kGemmABlock, &p.ta, kb * kGemmBK, (mtile * p.mt + b) * 128, &full[s]);
           if (BSRC == GEMM_B_TMA) tma_load_2d(st + p.mt * kGemmABlock, &p.tb, kb * kGemmBK, ntile * p.bn, &full[s]);
+          else tma_load_2d(st + p.raw_off, &p.tb, kb * (kGemmBK / 2), ntile * p.bn, &full[s]);
           if (++s == S) {
             s = 0;
             ph ^= 1;
@@ -185,7 +191,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     }
   } else if (BSRC == GEMM_B_W4 && warp >= UW0) {
     // ------------------------------------------------------------ int4 -> int8 B producers
-    produce_w4(p, smem, full, empty, tid - UW0 * 32);
+    produce_w4(p, smem, full, bfull, tid - UW0 * 32);
   } else if (warp == MW) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -198,7 +204,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
         tc_fence_after();
         const uint32_t d0 = tmem + acc * p.acc_cols;
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(&full[s], ph)) {
+          if (!mbar_wait(&full[s], ph) || (BSRC == GEMM_B_W4 && !mbar_wait(&bfull[s], ph))) {
             ok = false;
             break;
           }

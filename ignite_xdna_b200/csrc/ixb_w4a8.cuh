@@ -20,6 +20,7 @@
 //   eg  uint8 [N][K/128]: e = 4 - d per (column, group); 16 * w >> e = w << d.
 #pragma once
 #include <cstdint>
+#include <algorithm>
 #include "ixb_ptx.cuh"
 
 namespace ixb {
@@ -72,54 +73,137 @@ __device__ __forceinline__ uint32_t sra8_lanes(uint32_t v, uint32_t e, uint32_t 
 }
 
 // ---------------------------------------------------------------- GEMV (M = 1)
-// One warp per output column; the lanes split K (32 values per lane per step, a step covers 1024)
-// and the column's partial sums meet in a warp reduction. Weights stream once from HBM; the
-// activation vector stays in L1.
-__global__ void __launch_bounds__(256) w4a8_gemv_kernel(const int8_t* __restrict__ a, const uint8_t* __restrict__ wq,
-                                                        const uint8_t* __restrict__ eg,
-                                                        const int32_t* __restrict__ shift, int8_t* __restrict__ out,
-                                                        int N, int K) {
-  const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (n >= N) return;
-  const uint8_t* row = wq + (long long)n * (K / 2);
-  const uint8_t* erow = eg + (long long)n * (K / kW4Group);
-  int acc = 0;
-  // all of a lane's weight loads (up to 8 x 16 bytes) are in flight before the first is used
-  constexpr int kBatch = 8;
-  for (int kb = lane * 32; kb < K; kb += 1024 * kBatch) {
-    uint4 w[kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int k0 = kb + j * 1024;
-      if (k0 < K)
-        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(w[j].x), "=r"(w[j].y), "=r"(w[j].z), "=r"(w[j].w)
-                     : "l"(row + k0 / 2));
-      else
-        w[j] = make_uint4(0, 0, 0, 0);
+// Weight-streaming GEMV: one CTA per SM owns a contiguous range of output columns, whose packed
+// weights are one contiguous byte range of the image ([N][K/2]). A producer thread streams that
+// range through a ring of shared-memory stages with bulk copies (the TMA engine keeps up to
+// ~200 KB per SM in flight, enough to cover DRAM latency at full bandwidth), while 16 consumer
+// warps take the columns of each stage: a column's K words (16 bytes = 32 values) are split over
+// the lanes (and, for large K, over several warps), each word is 8 dp4a on 16 * w and the
+// activations (staged in shared memory once per CTA), shifted per group, and the partial sums
+// meet in a warp (then a shared-memory) reduction before the per-column SRS.
+constexpr int kGemvWarps = 16;                 // consumer warps
+constexpr int kGemvThreads = 32 * (kGemvWarps + 1);
+constexpr int kGemvSmemBudget = 200 * 1024;    // stages + activations
+
+struct GemvPlan {
+  int grid, cols_per_stage, warps_per_col, stages, stage_bytes, smem;
+};
+
+__host__ inline GemvPlan plan_gemv(int N, int K, int sms) {
+  GemvPlan g;
+  const int col_bytes = K / 2;
+  int ch = kGemvWarps;
+  while (ch > 1 && (ch * col_bytes > 96 * 1024)) ch >>= 1;
+  g.cols_per_stage = ch;
+  g.warps_per_col = kGemvWarps / ch;
+  g.stage_bytes = ch * col_bytes;
+  g.stages = std::min(4, (kGemvSmemBudget - K) / g.stage_bytes);
+  g.grid = std::min(sms, N);
+  g.smem = g.stages * g.stage_bytes + K + 2 * 8 * 4 + 1024;
+  return g;
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    w4a8_gemv_kernel(const int8_t* __restrict__ a, const uint8_t* __restrict__ wq, const uint8_t* __restrict__ eg,
+                     const int32_t* __restrict__ shift, int8_t* __restrict__ out, int N, int K, int CH, int WPC,
+                     int S, int stage_bytes) {
+  extern __shared__ uint8_t gsm_raw[];
+  uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(gsm + S * stage_bytes + K);
+  uint64_t* empty = full + 4;
+  __shared__ int colsum[4][kGemvWarps], colcnt[4][kGemvWarps];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = (int)((long long)blockIdx.x * N / gridDim.x), n1 = (int)((long long)(blockIdx.x + 1) * N / gridDim.x);
+  const int chunks = (n1 - n0 + CH - 1) / CH;
+  const int col_bytes = K / 2, words = K / 32;
+  int8_t* a_s = reinterpret_cast<int8_t*>(gsm + S * stage_bytes);
+  if (tid == kGemvWarps * 32) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvWarps);
     }
+    fence_mbar_init();
+  }
+  for (int i = tid; i < K / 16; i += kGemvThreads)
+    reinterpret_cast<int4*>(a_s)[i] = __ldg(reinterpret_cast<const int4*>(a) + i);
+  if (tid < 4 * kGemvWarps) {
+    (&colsum[0][0])[tid] = 0;
+    (&colcnt[0][0])[tid] = 0;
+  }
+  __syncthreads();
+  if (warp == kGemvWarps) {
+    // producer: chunk c (CH columns, the last one ragged) into stage c % S
+    if (lane == 0) {
+      uint32_t ph = 0;
+      for (int c = 0, s = 0; c < chunks; ++c) {
+        if (!mbar_wait(&empty[s], ph ^ 1)) break;
+        const int cols = min(CH, n1 - n0 - c * CH);
+        const uint32_t bytes = (uint32_t)cols * col_bytes;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        const uint8_t* src = wq + ((long long)n0 + (long long)c * CH) * col_bytes;
+        for (uint32_t off = 0; off < bytes; off += 32768u)
+          bulk_g2s(gsm + s * stage_bytes + off, src + off, min(32768u, bytes - off), &full[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+    return;
+  }
+  uint32_t ph = 0;
+  const int G = K / kW4Group;
+  for (int c = 0, s = 0; c < chunks; ++c) {
+    const int cols = min(CH, n1 - n0 - c * CH);
+    if (!mbar_wait(&full[s], ph)) break;
+    const int ci = warp / WPC, part_i = warp % WPC;   // column of the chunk, share of its K words
+    int acc = 0;
+    if (ci < cols) {
+      const int n = n0 + c * CH + ci;
+      const uint8_t* col = gsm + s * stage_bytes + ci * col_bytes;
+      const uint8_t* erow = eg + (long long)n * G;
+      for (int wd = part_i * 32 + lane; wd < words; wd += 32 * WPC) {
+        const uint4 w = *reinterpret_cast<const uint4*>(col + wd * 16);
+        const int4 a0 = reinterpret_cast<const int4*>(a_s)[2 * wd];
+        const int4 a1 = reinterpret_cast<const int4*>(a_s)[2 * wd + 1];
+        int pr = 0;
+        pr = __dp4a((int)w4_lo16(w.x), a0.x, pr);
+        pr = __dp4a((int)w4_hi16(w.x), a0.y, pr);
+        pr = __dp4a((int)w4_lo16(w.y), a0.z, pr);
+        pr = __dp4a((int)w4_hi16(w.y), a0.w, pr);
+        pr = __dp4a((int)w4_lo16(w.z), a1.x, pr);
+        pr = __dp4a((int)w4_hi16(w.z), a1.y, pr);
+        pr = __dp4a((int)w4_lo16(w.w), a1.z, pr);
+        pr = __dp4a((int)w4_hi16(w.w), a1.w, pr);
+        acc += pr >> __ldg(erow + (wd >> 2));   // pr = 16 * sum a * w, a multiple of 16: exact
+      }
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int k0 = kb + j * 1024;
-      if (k0 >= K) break;
-      const int4 a0 = __ldg(reinterpret_cast<const int4*>(a + k0));
-      const int4 a1 = __ldg(reinterpret_cast<const int4*>(a + k0) + 1);
-      int p = 0;
-      p = __dp4a((int)w4_lo16(w[j].x), a0.x, p);
-      p = __dp4a((int)w4_hi16(w[j].x), a0.y, p);
-      p = __dp4a((int)w4_lo16(w[j].y), a0.z, p);
-      p = __dp4a((int)w4_hi16(w[j].y), a0.w, p);
-      p = __dp4a((int)w4_lo16(w[j].z), a1.x, p);
-      p = __dp4a((int)w4_hi16(w[j].z), a1.y, p);
-      p = __dp4a((int)w4_lo16(w[j].w), a1.z, p);
-      p = __dp4a((int)w4_hi16(w[j].w), a1.w, p);
-      acc += p >> __ldg(erow + (k0 >> 7));  // p = 16 * sum a * w, a multiple of 16: exact
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    }
+    if (lane == 0 && ci < cols) {
+      const int n = n0 + c * CH + ci;
+      if (WPC == 1) {
+        out[n] = (int8_t)clamp_i8(rne_shift(acc, __ldg(shift + n)));
+      } else {
+        // the column's warps meet in shared memory: the last to arrive writes the output and
+        // clears the slot, before its release of the stage lets the slot be used again
+        atomicAdd(&colsum[s][ci], acc);
+        __threadfence_block();
+        if (atomicAdd(&colcnt[s][ci], 1) == WPC - 1) {
+          __threadfence_block();
+          const int sum = atomicExch(&colsum[s][ci], 0);
+          colcnt[s][ci] = 0;
+          out[n] = (int8_t)clamp_i8(rne_shift(sum, __ldg(shift + n)));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);   // this warp is done with the stage
+    if (++s == S) {
+      s = 0;
+      ph ^= 1;
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) out[n] = (int8_t)clamp_i8(rne_shift(acc, __ldg(shift + n)));
 }
 
 }  // namespace ixb

@@ -65,7 +65,8 @@ def test_w4a8_gemm_matches_oracle(M, N, K):
     assert np.array_equal(run(a, w, gpos, shift), O.w4a8_srs(a, w, gpos, shift))
 
 
-@pytest.mark.parametrize("N,K", [(4096, 11008), (11008, 4096), (16, 128), (48, 1152), (272, 640)])
+@pytest.mark.parametrize("N,K", [(4096, 11008), (11008, 4096), (16, 128), (48, 1152), (272, 640), (160, 256),
+                                 (400, 16384), (32, 65536)])
 def test_w4a8_gemv_matches_oracle(N, K):
     a, w, gpos, shift = make_case(1, N, K, seed=N + K)
     assert np.array_equal(run(a, w, gpos, shift, gemv=True), O.w4a8_srs(a, w, gpos, shift))
