@@ -457,10 +457,9 @@ int build_conv(const ixb_conv_desc& d, uint8_t* arena, uint64_t arena_bytes, int
   p.bias_off = p.bar_off + 512;
   if ((d.mode == IXB_MODE_IM2COL || d.mode == IXB_MODE_STEM) && p.rowsA > 1024)
     return bad("an im2col load carries at most 1024 pixels");
-  // Warps: 12 epilogue + 1 producer + 3 MMA warps (GATHER: 8 + 4 producer warps + 4); the issuers
-  // split each K-block's MMAs between them. (8 epilogue + 4 MMA warps for MMA-heavy tiles measured
-  // no faster on any YOLOv8n layer and slower on some.)
-  p.ew = d.mode == IXB_MODE_GATHER ? 8 : 12;
+  // Warps: 16 epilogue + 1 producer + 3 MMA warps (GATHER: 8 + 4 producer warps + 4); the issuers
+  // split each K-block's MMAs between them.
+  p.ew = d.mode == IXB_MODE_GATHER ? 8 : 16;
   p.issuers = mma_warps(p.ew);
   p.w_ntile_stride = (long long)b_total;
   p.wpack = arena + d.w_offset;
@@ -701,10 +700,10 @@ int launch_conv_m(const ConvLaunch& L, cudaStream_t st) {
 
 int launch_conv(const ConvLaunch& L, cudaStream_t st) {
   switch (L.mode) {
-    case IXB_MODE_WINDOW: return launch_conv_m<IXB_MODE_WINDOW, 12>(L, st);
+    case IXB_MODE_WINDOW: return launch_conv_m<IXB_MODE_WINDOW, 16>(L, st);
     case IXB_MODE_GATHER: return launch_conv_m<IXB_MODE_GATHER, 8>(L, st);
-    case IXB_MODE_IM2COL: return launch_conv_m<IXB_MODE_IM2COL, 12>(L, st);
-    default: return launch_conv_m<IXB_MODE_STEM, 12>(L, st);
+    case IXB_MODE_IM2COL: return launch_conv_m<IXB_MODE_IM2COL, 16>(L, st);
+    default: return launch_conv_m<IXB_MODE_STEM, 16>(L, st);
   }
 }
 
@@ -2133,7 +2132,8 @@ int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   if (!aligned16(a) || !aligned16(image)) return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
   const GemvPlan g = plan_gemv(N, K, sm_count());
   if (g.stages < 2) return fail(IXB_ERR_INVALID, "two GEMV stages do not fit shared memory");
-  if (int r = ensure_smem_limit(w4a8_gemv_kernel, g.smem)) return r;
+  // the limit is raised once per device to what any plan may take (the first call's plan can be smaller)
+  if (int r = ensure_smem_limit(w4a8_gemv_kernel, kSmemLimit - 1024)) return r;
   w4a8_gemv_kernel<<<g.grid, kGemvThreads, g.smem, static_cast<cudaStream_t>(stream)>>>(
       a, image, image + (uint64_t)N * (K / 2), shift, out, N, K, g.cols_per_stage, g.warps_per_col, g.stages,
       g.stage_bytes);

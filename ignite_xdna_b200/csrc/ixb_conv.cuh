@@ -39,7 +39,7 @@
 // are two A slots (two chunks of one tap, or one chunk at two taps).
 //
 // The kernel is persistent and warp-specialised:
-//   epilogue warps (12, or 8 for GATHER): TMEM -> registers -> epilogue -> global; warp w reads
+//   epilogue warps (16, or 8 for GATHER): TMEM -> registers -> epilogue -> global; warp w reads
 //            TMEM lane quarter w % 4, the warpgroups take shares of the tile's (block, 16-column)
 //            units
 //   producer: one thread issuing bulk / TMA copies (4 warps of cp.async for GATHER)
@@ -96,7 +96,7 @@ struct ConvParams {
   int ctab_off;  // per input chunk: WINDOW its plane's address, GATHER its GatherChunk (shared memory)
   int n_tile, acc_cols, tmem_cols, issuers;  // MMA issuing warps
   int nacc;                                  // TMEM accumulators (2 .. kMaxAcc) of acc_cols columns
-  int ew;                                           // epilogue warps (8 or 12)
+  int ew;                                           // epilogue warps (8 or 16)
   uint32_t idesc;
   int nseg;
   SegDev seg[IXB_MAX_SEGS];
@@ -143,12 +143,14 @@ enum : int {
 constexpr int kBlockM = 128;
 // Warp layout per (mode, epilogue warps EW): EW epilogue warps, the producer warps, then the MMA
 // warps (a warp issues an MMA only every ~95 cycles, so several issue).
-// At most 16 warps: four per SM sub-partition keeps 128 registers per thread.
-//   EW = 12: 12 epilogue + 1 producer + 3 MMA (WINDOW, IM2COL, STEM)
-//   EW = 8:   8 epilogue + 4 producer + 4 MMA (GATHER)
+//   EW = 16: 16 epilogue + 1 producer + 3 MMA (WINDOW, IM2COL, STEM): 20 warps at 96 registers.
+//            The drain is latency-bound (dependent conversions, TMEM and table loads), so four
+//            epilogue warps per SM sub-partition instead of three took the v8n step from 1.158 to
+//            1.127 ms with no spills.
+//   EW = 8:   8 epilogue + 4 producer + 4 MMA (GATHER): 16 warps at 128 registers.
 __host__ __device__ constexpr int prod_warps(int mode) { return mode == IXB_MODE_GATHER ? 4 : 1; }
 __host__ __device__ constexpr int mma_warp0(int mode, int ew) { return ew + prod_warps(mode); }
-__host__ __device__ constexpr int mma_warps(int ew) { return ew == 12 ? 3 : 4; }
+__host__ __device__ constexpr int mma_warps(int ew) { return ew == 8 ? 4 : 3; }
 __host__ __device__ constexpr int conv_threads(int mode, int ew) { return 32 * (mma_warp0(mode, ew) + mma_warps(ew)); }
 constexpr int kGatherThreads = 128;
 

@@ -251,12 +251,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
       const uint16_t ci = s_chunk[warp];
       const float4 bi = s_box[ci];
       const double oi = __dmul_rn((double)s_class[ci], off_step);
-      bool sup = false;
-      for (int k = lane; k < kept; k += 32) {
-        const uint16_t ck = s_order[k];
-        sup = sup || suppresses(bi, oi, s_box[ck], __dmul_rn((double)s_class[ck], off_step), p.iou);
+      // kept candidates 32 at a time, stopping at the first group that suppresses this one (most
+      // suppressed candidates meet their suppressor among the first, highest-scoring kept boxes)
+      bool by_kept = false;
+      for (int k0 = 0; k0 < kept && !by_kept; k0 += 32) {
+        const int k = k0 + lane;
+        bool sup = false;
+        if (k < kept) {
+          const uint16_t ck = s_order[k];
+          sup = suppresses(bi, oi, s_box[ck], __dmul_rn((double)s_class[ck], off_step), p.iou);
+        }
+        by_kept = __any_sync(0xffffffffu, sup);
       }
-      const bool by_kept = __any_sync(0xffffffffu, sup);
       // earlier chunk members b < warp that would suppress this one if kept
       bool m = false;
       if (lane < warp) {
