@@ -910,8 +910,9 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
   }
   p.bar_off = p.stages * p.stage_bytes;
   p.acc_cols = p.mt * p.bn;
+  p.nacc = 2 * p.acc_cols <= 512 ? 2 : 1;  // one accumulator only for a 512-column tile
   int cols = 32;
-  while (cols < 2 * p.acc_cols) cols *= 2;
+  while (cols < p.nacc * p.acc_cols) cols *= 2;
   p.tmem_cols = cols;
   p.idesc = umma_idesc_s8(128, p.bn);
   const long long tiles = (long long)p.m_tiles * p.n_tiles;

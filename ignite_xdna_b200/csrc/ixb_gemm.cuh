@@ -39,7 +39,7 @@ struct GemmParams {
   int bn, mt, m_tiles, n_tiles, kblocks, stages;
   int stage_bytes, stage_tx, bar_off;
   int raw_off;               // W4A8: offset of the packed int4 B tile inside a stage
-  int acc_cols, tmem_cols;
+  int acc_cols, tmem_cols, nacc;  // TMEM accumulators of acc_cols columns (1 or 2)
   uint32_t idesc;
   int out_kind;
   const int32_t* bias;
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
       mbar_init(&empty[s], 1);
       mbar_init(&bfull[s], kW4Warps * 32);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < p.nacc; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], EPI * 32);
     }
@@ -226,8 +226,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
         }
         if (!ok) break;
         umma_commit(&acc_full[acc]);
-        acc ^= 1;
-        if (acc == 0) aph ^= 1;
+        if (++acc == p.nacc) {
+          acc = 0;
+          aph ^= 1;
+        }
       }
       if (issued) {
         umma_commit(done);  // every MMA this CTA issued has finished before TMEM is released
@@ -305,8 +307,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
-      acc ^= 1;
-      if (acc == 0) aph ^= 1;
+      if (++acc == p.nacc) {
+        acc = 0;
+        aph ^= 1;
+      }
     }
   }
   tc_fence_before();

@@ -94,3 +94,14 @@ def test_i8gemm_extremes_saturate_and_round_to_even():
     bias = np.full(N, 2**31 - 1000, dtype=np.int32)
     bias[1::2] = -(2**31)
     assert np.array_equal(run_srs(a, b, bias, 23), O.i8gemm_srs(a, b, bias, 23))
+
+
+@pytest.mark.parametrize("sms", ["4", "16"])
+def test_i8gemm_many_tiles_per_cta(sms, monkeypatch):
+    """A planner SM count below the tile count: each CTA runs several tiles through its TMEM
+    accumulators (the persistent loop's accumulator rotation and phases), SRS and int32 forms."""
+    monkeypatch.setenv("IXB_SM_COUNT", sms)
+    M, N, K = 2048, 1024, 512
+    a, b, bias = _operands(M, N, K, seed=31)
+    assert np.array_equal(run_srs(a, b, bias, 9), O.i8gemm_srs(a, b, bias, 9))
+    assert np.array_equal(run_i32(a, b).astype(np.int64), a.astype(np.int64) @ b.astype(np.int64).T)
