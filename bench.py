@@ -192,6 +192,30 @@ def dist_setup(args):
     return world, rank, local
 
 
+def bind_to_gpu_numa(local):
+    """Run this rank's host threads, and so place its pinned buffers (first touch), on the NUMA node
+    its GPU hangs off (sysfs: the PCI device's numa_node and that node's cpulist), so that host <->
+    device copies do not cross the socket link. Returns the node, or None where sysfs does not say."""
+    try:
+        import torch
+        pr = torch.cuda.get_device_properties(local)
+        pci = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{pci}/numa_node").read_text().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return node
+    except (OSError, ValueError, AttributeError):
+        return None
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -367,6 +391,7 @@ def run_gpu(args):
     from ignite_xdna_b200 import InferenceSession, random_images
     from ignite_xdna_b200 import _lib as L
     torch.cuda.set_device(local)
+    numa = bind_to_gpu_numa(local)
     sess = InferenceSession.from_spec(args.model, imgsz=args.imgsz, device_index=local, max_batch=args.batch)
     lib = sess.lib
     B = args.batch
@@ -502,6 +527,7 @@ def run_gpu(args):
                              "(+ the decode kernel) and the e2e heads steps",
         "clocks": clocks.summary(),
         "copy_ceiling": ceiling,
+        "host_numa_node": numa,
         "per_layer": rows,
     }
     if cpu is not None:

@@ -886,7 +886,9 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
     const int nt = (N + p.bn - 1) / p.bn;
     for (int cand : {4, 2}) {
       const long long tiles = ((M + 128LL * cand - 1) / (128LL * cand)) * nt;
-      if (cand * p.bn <= 256 && tiles >= sms) {
+      // two accumulators of MT x BN columns, or (BN = 256) one 256 x 256 tile filling TMEM: twice
+      // the MMA work per operand byte, which the large square GEMMs need (L2 -> shared traffic)
+      if ((cand * p.bn <= 256 || (p.bn == 256 && cand == 2)) && tiles >= sms) {
         p.mt = cand;
         break;
       }
@@ -902,13 +904,17 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
     p.stage_bytes = round_up(p.stage_bytes + p.bn * (kGemmBK / 2), 1024);
     p.stage_tx = p.mt * kGemmABlock + p.bn * (kGemmBK / 2);
   }
-  const int budget = kSmemLimit - 1024 - 256;
+  // W4A8: a tile's group exponents in shared memory when they take at most 32 KB
+  const int eg_tile = bsrc == GEMM_B_W4 ? round_up(p.bn * (K / kW4Group), 128) : 0;
+  const int eg_bytes = (eg_tile > 0 && eg_tile <= 32 * 1024) ? eg_tile : 0;
+  const int budget = kSmemLimit - 1024 - 256 - eg_bytes;
   p.stages = std::min(kGemmMaxStages, budget / p.stage_bytes);
   if (p.stages < 2) {
     err = "two GEMM pipeline stages do not fit shared memory";
     return -1;
   }
-  p.bar_off = p.stages * p.stage_bytes;
+  p.eg_off = eg_bytes ? p.stages * p.stage_bytes : -1;
+  p.bar_off = p.stages * p.stage_bytes + eg_bytes;
   p.acc_cols = p.mt * p.bn;
   p.nacc = 2 * p.acc_cols <= 512 ? 2 : 1;  // one accumulator only for a 512-column tile
   int cols = 32;
@@ -2137,7 +2143,7 @@ int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   if (int r = ensure_smem_limit(w4a8_gemv_kernel, kSmemLimit - 1024)) return r;
   w4a8_gemv_kernel<<<g.grid, kGemvThreads, g.smem, static_cast<cudaStream_t>(stream)>>>(
       a, image, image + (uint64_t)N * (K / 2), shift, out, N, K, g.cols_per_stage, g.warps_per_col, g.stages,
-      g.stage_bytes);
+      g.stage_bytes, g.eg_bytes);
   IXB_CUDA(cudaGetLastError());
   return 0;
 }

@@ -103,7 +103,16 @@ __device__ __forceinline__ bool suppresses(float4 bi, double oi, float4 bk, doub
     ov = 1.0f;
   } else {
     const double inter = inter_area(ix, iy, iw, ih, kx, ky, kw, kh);
-    ov = __fsub_rn(1.0f, __double2float_rn(__dsub_rn(1.0, __ddiv_rn(inter, __dsub_rn(__dadd_rn(iarea, karea), inter)))));
+    const double uni = __dsub_rn(__dadd_rn(iarea, karea), inter);
+    // Most pairs are decided without the division: inter <= union, so inter - iou * union is
+    // computed to ~1e-16 * union, and a margin of 1e-6 * union puts inter / union on one side of
+    // iou by far more than the double division and the float conversions round (~1e-7).
+    if (iou >= 0.f && iou <= 1.f) {
+      const double dlt = __dsub_rn(inter, __dmul_rn((double)iou, uni)), margin = __dmul_rn(1e-6, uni);
+      if (dlt > margin) return true;
+      if (dlt < -margin) return false;
+    }
+    ov = __fsub_rn(1.0f, __double2float_rn(__dsub_rn(1.0, __ddiv_rn(inter, uni))));
   }
   return !(ov <= iou);
 }

@@ -39,6 +39,8 @@ struct GemmParams {
   int bn, mt, m_tiles, n_tiles, kblocks, stages;
   int stage_bytes, stage_tx, bar_off;
   int raw_off;               // W4A8: offset of the packed int4 B tile inside a stage
+  int eg_off;                // W4A8: the tile's group exponents [BN][K/128] in shared memory, or -1
+                             // (read from global memory) when they would not fit
   int acc_cols, tmem_cols, nacc;  // TMEM accumulators of acc_cols columns (1 or 2)
   uint32_t idesc;
   int out_kind;
@@ -87,21 +89,30 @@ __device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, u
   const int S = p.stages, G = p.K / 128;
   const int tiles = p.m_tiles * p.n_tiles;
   const int items = 8 * p.bn;
+  uint8_t* eg_s = p.eg_off >= 0 ? smem + p.eg_off : nullptr;
   int s = 0;
   uint32_t ph = 0;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int ntile = t % p.n_tiles;
     const int n0 = ntile * p.bn;
+    if (eg_s) {
+      // the tile's group exponents, one contiguous run of [N][K/128], once per tile (the 128 B-warp
+      // threads meet on named barrier 2 around the refill; no thread leaves this loop early)
+      asm volatile("bar.sync 2, %0;" ::"n"(UT) : "memory");
+      const long long e0 = (long long)n0 * G, e1 = (long long)min(n0 + p.bn, p.N) * G;
+      for (long long i = e0 + ut; i < e1; i += UT) eg_s[i - e0] = __ldg(p.eg + i);
+      asm volatile("bar.sync 2, %0;" ::"n"(UT) : "memory");
+    }
     for (int kb = 0; kb < p.kblocks; ++kb) {
-      if (!mbar_wait(&full[s], ph)) return;
+      const bool ok = mbar_wait(&full[s], ph);  // a timeout raised the device flag; the loop runs on
       uint8_t* st = smem + s * p.stage_bytes;
       uint8_t* bst = st + p.mt * kGemmABlock;
       const uint8_t* raw = st + p.raw_off;
-      for (int i = ut; i < items; i += UT) {
+      for (int i = ut; ok && i < items; i += UT) {
         const int r = i >> 3, c = i & 7;
         const int n = n0 + r;
         const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);  // zero past N (TMA fill)
-        const uint32_t e = n < p.N ? __ldg(p.eg + (long long)n * G + kb) : 0u;
+        const uint32_t e = n >= p.N ? 0u : (eg_s ? (uint32_t)eg_s[r * G + kb] : (uint32_t)__ldg(p.eg + (long long)n * G + kb));
         uint4 o = make_uint4(w4_lo16(w.x), w4_hi16(w.x), w4_lo16(w.y), w4_hi16(w.y));
         if (e) {
           const uint32_t keep = (0xFFu >> e) * 0x01010101u;

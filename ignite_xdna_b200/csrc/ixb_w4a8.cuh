@@ -86,30 +86,35 @@ constexpr int kGemvThreads = 32 * (kGemvWarps + 1);
 constexpr int kGemvSmemBudget = 200 * 1024;    // stages + activations
 
 struct GemvPlan {
-  int grid, cols_per_stage, warps_per_col, stages, stage_bytes, smem;
+  int grid, cols_per_stage, warps_per_col, stages, stage_bytes, eg_bytes, smem;
 };
 
 __host__ inline GemvPlan plan_gemv(int N, int K, int sms) {
   GemvPlan g;
   const int col_bytes = K / 2;
-  int ch = kGemvWarps;
-  while (ch > 1 && (ch * col_bytes > 96 * 1024)) ch >>= 1;
-  g.cols_per_stage = ch;
-  g.warps_per_col = kGemvWarps / ch;
-  g.stage_bytes = ch * col_bytes;
-  g.stages = std::min(4, (kGemvSmemBudget - K) / g.stage_bytes);
   g.grid = std::min(sms, N);
-  g.smem = g.stages * g.stage_bytes + K + 2 * 8 * 4 + 1024;
+  // the group exponents of a CTA's columns (at most ceil(N / grid) of them), staged once
+  g.eg_bytes = ((N + g.grid - 1) / g.grid * (K / kW4Group) + 15) / 16 * 16;
+  // columns per stage: 16 (one per warp) unless a stage would pass 96 KB or fewer than two fit
+  for (int ch = kGemvWarps;; ch >>= 1) {
+    g.cols_per_stage = ch;
+    g.warps_per_col = kGemvWarps / ch;
+    g.stage_bytes = ch * col_bytes;
+    g.stages = std::min(4, (kGemvSmemBudget - K - g.eg_bytes) / g.stage_bytes);
+    if (ch == 1 || (g.stage_bytes <= 96 * 1024 && g.stages >= 2)) break;
+  }
+  g.smem = g.stages * g.stage_bytes + K + g.eg_bytes + 2 * 8 * 4 + 1024;
   return g;
 }
 
 __global__ void __launch_bounds__(kGemvThreads, 1)
     w4a8_gemv_kernel(const int8_t* __restrict__ a, const uint8_t* __restrict__ wq, const uint8_t* __restrict__ eg,
                      const int32_t* __restrict__ shift, int8_t* __restrict__ out, int N, int K, int CH, int WPC,
-                     int S, int stage_bytes) {
+                     int S, int stage_bytes, int eg_bytes) {
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 127) & ~uintptr_t(127));
-  uint64_t* full = reinterpret_cast<uint64_t*>(gsm + S * stage_bytes + K);
+  uint8_t* eg_s = gsm + S * stage_bytes + K;   // [columns of this CTA][K / 128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(eg_s + eg_bytes);
   uint64_t* empty = full + 4;
   __shared__ int colsum[4][kGemvWarps], colcnt[4][kGemvWarps];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -126,6 +131,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   }
   for (int i = tid; i < K / 16; i += kGemvThreads)
     reinterpret_cast<int4*>(a_s)[i] = __ldg(reinterpret_cast<const int4*>(a) + i);
+  {
+    const int G = K / kW4Group;
+    const long long e0 = (long long)n0 * G, e1 = (long long)n1 * G;  // contiguous: [N][K / 128]
+    for (long long i = e0 + tid; i < e1; i += kGemvThreads) eg_s[i - e0] = __ldg(eg + i);
+  }
   if (tid < 4 * kGemvWarps) {
     (&colsum[0][0])[tid] = 0;
     (&colcnt[0][0])[tid] = 0;
@@ -161,7 +171,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     if (ci < cols) {
       const int n = n0 + c * CH + ci;
       const uint8_t* col = gsm + s * stage_bytes + ci * col_bytes;
-      const uint8_t* erow = eg + (long long)n * G;
+      const uint8_t* erow = eg_s + (n - n0) * G;
       for (int wd = part_i * 32 + lane; wd < words; wd += 32 * WPC) {
         const uint4 w = *reinterpret_cast<const uint4*>(col + wd * 16);
         const int4 a0 = reinterpret_cast<const int4*>(a_s)[2 * wd];
@@ -175,7 +185,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         pr = __dp4a((int)w4_hi16(w.z), a1.y, pr);
         pr = __dp4a((int)w4_lo16(w.w), a1.z, pr);
         pr = __dp4a((int)w4_hi16(w.w), a1.w, pr);
-        acc += pr >> __ldg(erow + (wd >> 2));   // pr = 16 * sum a * w, a multiple of 16: exact
+        acc += pr >> erow[wd >> 2];   // pr = 16 * sum a * w, a multiple of 16: exact
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);

@@ -121,7 +121,9 @@ def test_gemm_plan_fits_the_hardware():
         bn, mt, mtiles, ntiles, kblocks, stages, grid, smem, tcols, stage_bytes = list(info)
         assert bn % 16 == 0 and 16 <= bn <= 256 and N % 16 == 0
         assert mt * 128 * mtiles >= M and bn * ntiles >= N and kblocks * 128 >= K
-        assert 2 * mt * bn <= tcols <= 512 and tcols & (tcols - 1) == 0
+        # two accumulators of MT x BN columns, or one 256 x 256 tile filling TMEM
+        assert (2 * mt * bn <= tcols or (mt, bn) == (2, 256) and tcols == 512) and tcols <= 512
+        assert tcols & (tcols - 1) == 0
         assert stages >= 2 and smem <= 227 * 1024 and stage_bytes * stages + 1024 + 256 <= smem
         assert 1 <= grid <= 148
 
