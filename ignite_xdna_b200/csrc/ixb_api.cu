@@ -863,8 +863,10 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
   const int sms = sm_count();
   if (bsrc == GEMM_B_W4) {
     // The tile (MT blocks of 128 rows x BN columns) minimising (waves of tiles over the SMs) x
-    // (the tile's MMA time per K step: MT MMAs of ~max(BN / 2, 32 + BN / 4) cycles, the
-    // operands' shared-memory reads bounding narrow ones); two accumulators must fit TMEM.
+    // (a K-block's time: the slower of its MMAs, 4 x MT of ~max(BN / 2, 32 + BN / 4) cycles with the
+    // operands' shared-memory reads bounding narrow ones, and the unpack of BN x 128 int4 values,
+    // ~2.5 BN instructions per unpacking warp at ~0.5 per cycle with 4 warps, halved with 8);
+    // two accumulators must fit TMEM.
     double best = 1e300;
     const int mt_max = (int)std::min<long long>(4, (M + 127) / 128);
     for (int mt : {1, 2, 4}) {
@@ -872,7 +874,9 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
       for (int bn = 16; bn <= std::min(256 / mt, round_up(N, 16)); bn += 16) {
         const long long tiles = ((M + 128LL * mt - 1) / (128LL * mt)) * ((N + bn - 1) / bn);
         const long long waves = (tiles + sms - 1) / sms;
-        const double cost = (double)waves * mt * std::max(bn / 2.0, 32.0 + bn / 4.0);
+        const double mma = 4.0 * mt * std::max(bn / 2.0, 32.0 + bn / 4.0);
+        const double unpack = 5.0 * bn * 4.0 / kW4Warps;
+        const double cost = (double)waves * std::max(mma, unpack);
         if (cost < best - 1e-9) {
           best = cost;
           p.mt = mt;

@@ -75,7 +75,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
 }
 
 enum : int { GEMM_B_TMA = 0, GEMM_B_W4 = 1 };
-constexpr int kW4Warps = 4;  // warps unpacking int4 weights into the B stage (GEMM_B_W4)
+constexpr int kW4Warps = 8;  // warps unpacking int4 weights into the B stage (GEMM_B_W4): two per SM sub-partition
 constexpr int gemm_threads(int epi, int bsrc) { return 32 * (epi + 2 + (bsrc == GEMM_B_W4 ? kW4Warps : 0)); }
 
 // B warps of the W4A8 GEMM: per stage the TMA has brought the packed int4 tile (BN rows x 64
