@@ -865,19 +865,22 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
     // The tile (MT blocks of 128 rows x BN columns) minimising (waves of tiles over the SMs) x
     // (a K-block's time: the slower of its MMAs, 4 x MT of ~max(BN / 2, 32 + BN / 4) cycles with the
     // operands' shared-memory reads bounding narrow ones, and the unpack of BN x 128 int4 values,
-    // ~2.5 BN instructions per unpacking warp at ~0.5 per cycle with 4 warps, halved with 8);
-    // two accumulators must fit TMEM.
+    // ~2.5 BN instructions per unpacking warp at ~0.5 per cycle with 4 warps, halved with 8).
+    // Two accumulators must fit TMEM, or, when every CTA has at most one tile, one of up to 512
+    // columns (MT x BN: the unpacked B tile then serves four 128-row blocks). On a tie the larger
+    // tile wins: fewer tiles unpack each weight tile fewer times.
     double best = 1e300;
     const int mt_max = (int)std::min<long long>(4, (M + 127) / 128);
     for (int mt : {1, 2, 4}) {
       if (mt > mt_max && mt != 1) continue;
-      for (int bn = 16; bn <= std::min(256 / mt, round_up(N, 16)); bn += 16) {
+      for (int bn = 16; bn <= std::min(std::min(512 / mt, 256), round_up(N, 16)); bn += 16) {
         const long long tiles = ((M + 128LL * mt - 1) / (128LL * mt)) * ((N + bn - 1) / bn);
         const long long waves = (tiles + sms - 1) / sms;
+        if (mt * bn > 256 && waves > 1) continue;
         const double mma = 4.0 * mt * std::max(bn / 2.0, 32.0 + bn / 4.0);
         const double unpack = 5.0 * bn * 4.0 / kW4Warps;
         const double cost = (double)waves * std::max(mma, unpack);
-        if (cost < best - 1e-9) {
+        if (cost < best - 1e-9 || (cost < best + 1e-9 && mt * bn > p.mt * p.bn)) {
           best = cost;
           p.mt = mt;
           p.bn = bn;
@@ -908,16 +911,18 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
     p.stage_bytes = round_up(p.stage_bytes + p.bn * (kGemmBK / 2), 1024);
     p.stage_tx = p.mt * kGemmABlock + p.bn * (kGemmBK / 2);
   }
-  // W4A8: a tile's group exponents in shared memory when they take at most 32 KB
+  // W4A8: two tiles' group exponents in shared memory (the producer copies the next tile's while
+  // the current one unpacks) when one takes at most 16 KB
   const int eg_tile = bsrc == GEMM_B_W4 ? round_up(p.bn * (K / kW4Group), 128) : 0;
-  const int eg_bytes = (eg_tile > 0 && eg_tile <= 32 * 1024) ? eg_tile : 0;
-  const int budget = kSmemLimit - 1024 - 256 - eg_bytes;
+  const int eg_bytes = (eg_tile > 0 && eg_tile <= 16 * 1024) ? 2 * eg_tile : 0;
+  const int budget = kSmemLimit - 1024 - kGemmBarBytes - eg_bytes;
   p.stages = std::min(kGemmMaxStages, budget / p.stage_bytes);
   if (p.stages < 2) {
     err = "two GEMM pipeline stages do not fit shared memory";
     return -1;
   }
   p.eg_off = eg_bytes ? p.stages * p.stage_bytes : -1;
+  p.eg_stride = eg_tile;
   p.bar_off = p.stages * p.stage_bytes + eg_bytes;
   p.acc_cols = p.mt * p.bn;
   p.nacc = 2 * p.acc_cols <= 512 ? 2 : 1;  // one accumulator only for a 512-column tile
@@ -931,7 +936,18 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
     return -1;
   }
   L.grid = (int)std::min<long long>(tiles, sms);
-  L.smem = 1024 + p.bar_off + 256;
+  L.smem = 1024 + p.bar_off + kGemmBarBytes;
+  return 0;
+}
+
+// The GEMV with WPL 16-byte loads per lane per column batch (the limit is raised once per device
+// to what any plan may take: the first call's plan can be smaller).
+template <int WPL>
+int launch_gemv(const GemvPlan& g, const int8_t* a, const uint8_t* wq, const uint8_t* eg, const int32_t* shift,
+                int8_t* out, int N, int K, cudaStream_t st) {
+  if (int r = ensure_smem_limit(w4a8_gemv_kernel<WPL>, kSmemLimit / kGemvCtasPerSm - 1024)) return r;
+  w4a8_gemv_kernel<WPL><<<g.grid, kGemvThreads, g.smem, st>>>(a, wq, eg, shift, out, N, K);
+  IXB_CUDA(cudaGetLastError());
   return 0;
 }
 
@@ -1058,6 +1074,8 @@ int prepare_decode(const ixb_decode_desc& d, uint64_t egress_image_bytes, Decode
     const ixb_decode_head& hd = d.head[h];
     if (!hd.dfl_exp || !hd.sigmoid || hd.anchors < 1 || hd.anchor_offset != total)
       return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + ": missing tables or anchors out of order");
+    if (!aligned16(hd.dfl_exp))
+      return fail(IXB_ERR_INVALID, "decode head " + std::to_string(h) + ": dfl_exp must be 16-byte aligned");
     const uint64_t box_end = hd.box_offset + (uint64_t)4 * kDfl * hd.anchors;
     const uint64_t cls_end = hd.cls_offset + (uint64_t)d.num_classes * hd.anchors;
     if (box_end > egress_image_bytes || cls_end > egress_image_bytes)
@@ -2142,14 +2160,20 @@ int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   if (int r = check_w4a8_shape(N, K)) return r;
   if (!aligned16(a) || !aligned16(image)) return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
   const GemvPlan g = plan_gemv(N, K, sm_count());
-  if (g.stages < 2) return fail(IXB_ERR_INVALID, "two GEMV stages do not fit shared memory");
-  // the limit is raised once per device to what any plan may take (the first call's plan can be smaller)
-  if (int r = ensure_smem_limit(w4a8_gemv_kernel, kSmemLimit - 1024)) return r;
-  w4a8_gemv_kernel<<<g.grid, kGemvThreads, g.smem, static_cast<cudaStream_t>(stream)>>>(
-      a, image, image + (uint64_t)N * (K / 2), shift, out, N, K, g.cols_per_stage, g.warps_per_col, g.stages,
-      g.stage_bytes, g.eg_bytes);
-  IXB_CUDA(cudaGetLastError());
-  return 0;
+  if (g.smem > kSmemLimit / kGemvCtasPerSm - 1024)
+    return fail(IXB_ERR_INVALID, "GEMV activations and exponents do not fit shared memory");
+  const uint8_t* eg = image + (uint64_t)N * (K / 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (g.wpl) {
+    case 1: return launch_gemv<1>(g, a, image, eg, shift, out, N, K, st);
+    case 2: return launch_gemv<2>(g, a, image, eg, shift, out, N, K, st);
+    case 3: return launch_gemv<3>(g, a, image, eg, shift, out, N, K, st);
+    case 4: return launch_gemv<4>(g, a, image, eg, shift, out, N, K, st);
+    case 5: return launch_gemv<5>(g, a, image, eg, shift, out, N, K, st);
+    case 6: return launch_gemv<6>(g, a, image, eg, shift, out, N, K, st);
+    case 7: return launch_gemv<7>(g, a, image, eg, shift, out, N, K, st);
+    default: return launch_gemv<8>(g, a, image, eg, shift, out, N, K, st);
+  }
 }
 
 int ixb_gemm_plan_info(int M, int N, int K, int w4a8, int32_t* info, int n) {

@@ -11,7 +11,19 @@
 //   * NMS as OpenCV's NMSBoxesBatched: boxes offset by class * (max coordinate + 1) in double,
 //     scores strictly above the threshold stably sorted in descending order, a box kept when its
 //     overlap 1 - (float)(1 - inter / union) with every kept box is at most the IoU threshold.
-// One CTA decodes one image; its candidates live in shared memory (no scratch in global memory).
+// One CTA decodes one image; its candidates live in shared memory (no scratch in global memory):
+//   1. candidates, compacted in anchor order (a block-wide prefix count per 1024 anchors), with the
+//      sigmoid tables and, when the DFL exp table depends on q - q_max alone (power-of-two box
+//      scales: checked here), its 256-entry diagonal staged in shared memory;
+//   2. a stable two-pass radix sort (5-bit digits) of the candidates by score rank, the rank of a
+//      score being how many of the three heads' 768 table values exceed it (equal scores, equal
+//      ranks): score descending, then anchor ascending, the reference's stable order;
+//   3. exact greedy NMS as alternating steps: the next 32 still-alive candidates in order are
+//      resolved among themselves (any kept box before them has already been applied), then every
+//      later alive candidate is tested against the step's kept boxes by the whole block and dropped
+//      if one suppresses it. A candidate is dropped only by a kept box ahead of it, and one that
+//      reaches a step has survived every kept box ahead of it: the greedy result, in order, with a
+//      block barrier per ~32 kept boxes instead of per 32 candidates.
 #pragma once
 #include <cfloat>
 #include <cstdint>
@@ -48,30 +60,6 @@ struct DecodeParams {
   int32_t* out_class;           // [B][capacity]
   int32_t* out_count;           // [B]: detections, or -3 when more than `capacity` survive NMS
 };
-
-__device__ __forceinline__ float dfl_side(const int8_t* box, int n, int a, int side, const float* dfl_exp) {
-  int q[kDfl];
-  int q_max = -128;
-#pragma unroll
-  for (int k = 0; k < kDfl; ++k) {
-    q[k] = box[(long long)(side * kDfl + k) * n + a];
-    q_max = max(q_max, q[k]);
-  }
-  const float* row = dfl_exp + (q_max + 128) * 256;
-  float e[kDfl];
-#pragma unroll
-  for (int k = 0; k < kDfl; ++k) e[k] = __ldg(row + q[k] + 128);
-  float sum = e[0];
-#pragma unroll
-  for (int k = 1; k < kDfl; ++k) sum = __fadd_rn(sum, e[k]);
-  float acc = 0.f;
-#pragma unroll
-  for (int k = 0; k < kDfl; ++k) {
-    const float w = __fmul_rn(__fdiv_rn(e[k], sum), (float)k);
-    acc = k == 0 ? w : __fadd_rn(acc, w);
-  }
-  return acc;
-}
 
 // Area of the intersection of two class-offset boxes, as OpenCV's Rect2d operator& computes it.
 __device__ __forceinline__ double inter_area(double ax, double ay, double aw, double ah, double bx, double by,
@@ -117,205 +105,454 @@ __device__ __forceinline__ bool suppresses(float4 bi, double oi, float4 bk, doub
   return !(ov <= iou);
 }
 
-__global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __grid_constant__ DecodeParams p) {
-  extern __shared__ uint8_t dsmem[];
-  float* s_score = reinterpret_cast<float*>(dsmem);                       // [8400]
-  float4* s_box = reinterpret_cast<float4*>(s_score + kDecodeMaxAnchors);  // [8400] x0, y0, w, h
-  int16_t* s_anchor = reinterpret_cast<int16_t*>(s_box + kDecodeMaxAnchors);  // [8400] anchor index
-  uint8_t* s_class = reinterpret_cast<uint8_t*>(s_anchor + kDecodeMaxAnchors);  // [8400]
-  uint16_t* s_order = reinterpret_cast<uint16_t*>(s_class + kDecodeMaxAnchors); // [16384] sort / kept list
-  __shared__ int s_n, s_kept, s_nv;
-  __shared__ double s_maxc[kDecodeThreads / 32];
-  __shared__ uint16_t s_chunk[32];
-  __shared__ unsigned s_mask[32];
-  __shared__ int s_sup[32];
+// Expectation over the 16 bins of one box side, float32 in the reference's order. `diag` (shared
+// memory) holds exp(v(q) - v(q_max)) by q - q_max + 255 when the head's table depends on that
+// difference alone; otherwise the table's row q_max is read from global memory.
+__device__ __forceinline__ float dfl_side(const int8_t* box, int n, int a, int side, const float* dfl_exp,
+                                          const float* diag) {
+  int q[kDfl];
+  int q_max = -128;
+#pragma unroll
+  for (int k = 0; k < kDfl; ++k) {
+    q[k] = box[(long long)(side * kDfl + k) * n + a];
+    q_max = max(q_max, q[k]);
+  }
+  float e[kDfl];
+  if (diag) {
+#pragma unroll
+    for (int k = 0; k < kDfl; ++k) e[k] = diag[q[k] - q_max + 255];
+  } else {
+    const float* row = dfl_exp + (q_max + 128) * 256;
+#pragma unroll
+    for (int k = 0; k < kDfl; ++k) e[k] = __ldg(row + q[k] + 128);
+  }
+  float sum = e[0];
+#pragma unroll
+  for (int k = 1; k < kDfl; ++k) sum = __fadd_rn(sum, e[k]);
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < kDfl; ++k) {
+    const float w = __fmul_rn(__fdiv_rn(e[k], sum), (float)k);
+    acc = k == 0 ? w : __fadd_rn(acc, w);
+  }
+  return acc;
+}
 
-  const int img = blockIdx.x, tid = threadIdx.x;
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+constexpr int kDecodeWarps = kDecodeThreads / 32;
+constexpr int kScoreVals = 3 * 256;   // every score is one of the three heads' sigmoid values
+constexpr int kSidxTiny = 0x8000;     // candidate flag: its box area (double) is at most DBL_EPSILON
+
+// Dynamic shared memory of the decode kernel (byte offsets).
+constexpr int kDsBox = 0;                                   // float4 [8400]: x0, y0, w, h
+constexpr int kDsSidx = kDsBox + 16 * kDecodeMaxAnchors;    // uint16 [8400]: head * 256 + q + 128 | tiny
+constexpr int kDsCls = kDsSidx + 2 * kDecodeMaxAnchors;     // uint8 [8400]: class
+constexpr int kDsOrdA = kDsCls + kDecodeMaxAnchors;         // uint16 [8400]: sort buffers; A ends sorted,
+constexpr int kDsOrdB = kDsOrdA + 2 * kDecodeMaxAnchors;    //   B then holds the kept list
+constexpr int kDsSig = kDsOrdB + 2 * kDecodeMaxAnchors;     // float [768]: sigmoid tables
+constexpr int kDsDiag = kDsSig + 4 * kScoreVals;            // float [768]: DFL exp diagonals
+constexpr int kDsLow = kDsDiag + 4 * kScoreVals;            // int32 [768]: sigmoid_low tables
+constexpr int kDsRank = kDsLow + 4 * kScoreVals;            // uint16 [768]: score ranks
+constexpr int kDsAlive = kDsRank + 2 * kScoreVals;          // uint32 [264]: NMS alive bits
+constexpr int kDsWc = kDsAlive + 4 * 264;                   // int [32][33]: per-warp counts
+constexpr int kDsBytes = kDsWc + 4 * 32 * 33;
+
+// One stable counting pass over 32 buckets: dst[start(d) + earlier entries of digit d] = src[i].
+// Entries go 1024 at a time; a warp's entries of one digit find each other with match.any, and
+// a transposed warp scan (warp d over the 32 warps' counts of digit d) places the warps in order.
+// s_wc must be zero on entry and is zero again on exit.
+template <typename Digit>
+__device__ __forceinline__ void radix_pass(const uint16_t* src, uint16_t* dst, int n, Digit digit, int* s_cnt,
+                                           int (*s_wc)[33], int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
+  if (tid < 32) s_cnt[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kDecodeThreads) atomicAdd(&s_cnt[digit(src[i])], 1);
+  __syncthreads();
+  if (warp == 0) {
+    const int v = s_cnt[lane];
+    s_cnt[lane] = warp_incl_scan(v, lane) - v;  // where each digit's run starts
+  }
+  __syncthreads();
+  for (int base = 0; base < n; base += kDecodeThreads) {
+    const int i = base + tid;
+    const bool valid = i < n;
+    const uint16_t key = valid ? src[i] : (uint16_t)0;
+    const int d = valid ? digit(key) : 32;
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const int below = __popc(peers & ((1u << lane) - 1u));
+    if (valid && below == 0) s_wc[warp][d] = __popc(peers);
+    __syncthreads();
+    {  // warp `warp` places digit `warp`: the 32 warps' counts in warp order after the digit's run so far
+      const int v = s_wc[lane][warp];
+      const int run = s_cnt[warp];
+      const int incl = warp_incl_scan(v, lane);
+      s_wc[lane][warp] = run + incl - v;
+      __syncwarp();
+      if (lane == 31) s_cnt[warp] = run + incl;
+    }
+    __syncthreads();
+    if (valid) dst[s_wc[warp][d] + below] = key;
+    __syncwarp();
+    s_wc[warp][lane] = 0;
+    __syncthreads();
+  }
+}
+
+// Whether the cross-class pair (i, k) cannot overlap after the class offsets: the box of the
+// higher class lies right of the other's by at least a pixel whenever its x0 >= 0 (classes one
+// apart) or x0 >= -(gap - 1) * max_coord (further apart), every box ending at or before max_coord.
+// Then the intersection is 0 and, unless both areas are at most DBL_EPSILON, the overlap is 0,
+// which suppresses nothing for an IoU threshold >= 0 (the caller checks).
+__device__ __forceinline__ bool classes_apart(float4 bi, int ci, float4 bk, int ck, double maxc) {
+  if (ci == ck) return false;
+  const float x_hi = ci < ck ? bk.x : bi.x;
+  const int gap = ci < ck ? ck - ci : ci - ck;
+  return x_hi >= 0.f || (double)x_hi >= -(double)(gap - 1) * maxc;
+}
+
+// The suppression test of two boxes of one class decided in float, when the float overlap
+// measure d = inter - iou * union is farther from 0 than its rounding can move it: 1 (suppresses),
+// 0 (does not), -1 (too close: the exact test decides). Same class, same offset: the exact test's
+// double arithmetic on offset coordinates is the exact arithmetic of the raw float coordinates
+// (to ~1e-16). Each float rounding moves a result by at most 2^-24 of its magnitude; with M the
+// largest coordinate magnitude of the pair, the side lengths of the intersection are off by at
+// most delta = 2^-22 M, the intersection by delta * P + delta^2 + 2^-24 inter (P the sum of the
+// four sides), and d by at most err = 2 delta P + 2 delta^2 + 2^-21 (areas + union + inter). The
+// exact test suppresses when d / union > 1e-6 and keeps when d / union < -1e-6 (its float
+// roundings of the overlap are ~1e-7), so |d| > err + 2e-6 union decides. iou in [0, 1].
+__device__ __forceinline__ int screen_same_class(float4 a, float4 b, float iou) {
+  const float ax2 = a.x + a.z, ay2 = a.y + a.w, bx2 = b.x + b.z, by2 = b.y + b.w;
+  const float iw = fminf(ax2, bx2) - fmaxf(a.x, b.x);
+  const float ih = fminf(ay2, by2) - fmaxf(a.y, b.y);
+  const float inter = (iw > 0.f && ih > 0.f) ? iw * ih : 0.f;
+  const float aa = a.z * a.w, ab = b.z * b.w;
+  const float uni = (aa + ab) - inter;
+  const float m = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(ax2)), fmaxf(fabsf(a.y), fabsf(ay2))),
+                        fmaxf(fmaxf(fabsf(b.x), fabsf(bx2)), fmaxf(fabsf(b.y), fabsf(by2))));
+  const float delta = m * 2.384185791015625e-7f;  // 2^-22
+  const float per = (a.z + a.w) + (b.z + b.w);
+  const float err = 2.f * delta * (per + delta) + 4.76837158203125e-7f * (aa + ab + uni + inter);  // 2^-21
+  const float margin = err + 2e-6f * uni;
+  const float d = inter - iou * uni;
+  if (d > margin) return 1;
+  if (d < -margin) return 0;
+  return -1;  // near the threshold, or not finite
+}
+
+// Whether kept box k suppresses candidate i: classes that cannot meet after the offsets and clear
+// same-class cases are decided without the exact double test.
+__device__ __forceinline__ bool pair_suppresses(float4 bi, int cli, bool tiny_i, float4 bk, int clk, bool tiny_k,
+                                                double off_step, double maxc, float iou, bool iou_nonneg,
+                                                bool iou_unit) {
+  if (iou_nonneg && !(tiny_i && tiny_k)) {
+    if (cli != clk) {
+      if (classes_apart(bi, cli, bk, clk, maxc)) return false;
+    } else if (iou_unit) {
+      const int r = screen_same_class(bi, bk, iou);
+      if (r >= 0) return r != 0;
+    }
+  }
+  return suppresses(bi, __dmul_rn((double)cli, off_step), bk, __dmul_rn((double)clk, off_step), iou);
+}
+
+__global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __grid_constant__ DecodeParams p) {
+  extern __shared__ __align__(16) uint8_t dsmem[];
+  float4* s_box = reinterpret_cast<float4*>(dsmem + kDsBox);
+  uint16_t* s_sidx = reinterpret_cast<uint16_t*>(dsmem + kDsSidx);
+  uint8_t* s_class = dsmem + kDsCls;
+  uint16_t* s_ordA = reinterpret_cast<uint16_t*>(dsmem + kDsOrdA);
+  uint16_t* s_ordB = reinterpret_cast<uint16_t*>(dsmem + kDsOrdB);
+  float* s_sig = reinterpret_cast<float*>(dsmem + kDsSig);
+  float* s_diag = reinterpret_cast<float*>(dsmem + kDsDiag);
+  int32_t* s_low = reinterpret_cast<int32_t*>(dsmem + kDsLow);
+  uint16_t* s_rank = reinterpret_cast<uint16_t*>(dsmem + kDsRank);
+  uint32_t* s_alive = reinterpret_cast<uint32_t*>(dsmem + kDsAlive);
+  int(*s_wc)[33] = reinterpret_cast<int(*)[33]>(dsmem + kDsWc);
+  __shared__ int s_n, s_ntot, s_kept, s_nv, s_cn, s_nk, s_f;
+  __shared__ int s_cnt[32], s_wcnt[kDecodeWarps];
+  __shared__ int s_toe[3];
+  __shared__ double s_maxc[kDecodeWarps];
+  __shared__ uint16_t s_chunk[32], s_newk[32];
+  __shared__ unsigned s_mask[32];
+
+  const int img = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int8_t* eg = p.egress + (long long)img * p.egress_image_bytes;
   const float pad_top = p.letterbox[3 * img], pad_left = p.letterbox[3 * img + 1], lscale = p.letterbox[3 * img + 2];
+  const int total = p.head[0].anchors + p.head[1].anchors + p.head[2].anchors;
+
+  // 0. tables: sigmoid values (and the first index of each value's run), the DFL diagonals
+  for (int i = tid; i < kScoreVals; i += kDecodeThreads) {
+    const DecodeHeadDev& hd = p.head[i >> 8];
+    s_sig[i] = __ldg(hd.sigmoid + (i & 255));
+    s_low[i] = hd.sigmoid_low ? __ldg(hd.sigmoid_low + (i & 255)) : 0;
+    s_diag[i] = __ldg(hd.dfl_exp + 255 * 256 + (i & 255));  // row q_max = 127
+  }
   if (tid == 0) {
     s_n = 0;
     s_kept = 0;
   }
   __syncthreads();
-
-  // 1. candidates: prune, class score, DFL, box (shared-memory slots in any order; the sort below
-  //    orders them by score and anchor, which is the reference's order after its stable sort)
   for (int h = 0; h < 3; ++h) {
-    const DecodeHeadDev& hd = p.head[h];
-    const int n = hd.anchors;
-    const int8_t* box = eg + hd.box_off;
-    const int8_t* cls = eg + hd.cls_off;
-    for (int a = tid; a < n; a += kDecodeThreads) {
-      int q_max = -128;
-      for (int c = 0; c < p.num_classes; ++c) q_max = max(q_max, (int)cls[(long long)c * n + a]);
-      if (q_max <= hd.qi) continue;
-      float best;
-      int best_c = 0;
-      if (hd.sigmoid_low) {
-        best = __ldg(hd.sigmoid + q_max + 128);
-        if (!(best >= p.conf)) continue;
-        const int lo = __ldg(hd.sigmoid_low + q_max + 128);
-        while (best_c < p.num_classes - 1 && (int)cls[(long long)best_c * n + a] < lo) ++best_c;
-      } else {
-        best = __ldg(hd.sigmoid + (int)cls[a] + 128);
-        for (int c = 1; c < p.num_classes; ++c) {
-          const float pr = __ldg(hd.sigmoid + (int)cls[(long long)c * n + a] + 128);
-          if (pr > best) {
-            best = pr;
-            best_c = c;
-          }
-        }
-        if (!(best >= p.conf)) continue;
+    // the table is used at (q_max, q) with q <= q_max only: there it must equal the diagonal
+    // (16-byte loads of four columns; the caller's tables are 16-byte aligned)
+    const float4* t4 = reinterpret_cast<const float4*>(p.head[h].dfl_exp);
+    const float* dg = s_diag + h * 256 + 255;
+    bool same = true;
+#pragma unroll 4
+    for (int e = tid; e < 256 * 64; e += kDecodeThreads) {
+      const int r = e >> 6, c = (e & 63) * 4;
+      if (c <= r) {
+        const float4 v = __ldg(t4 + e);
+        same &= __float_as_uint(v.x) == __float_as_uint(dg[c - r]);
+        same &= c + 1 > r || __float_as_uint(v.y) == __float_as_uint(dg[c + 1 - r]);
+        same &= c + 2 > r || __float_as_uint(v.z) == __float_as_uint(dg[c + 2 - r]);
+        same &= c + 3 > r || __float_as_uint(v.w) == __float_as_uint(dg[c + 3 - r]);
       }
-      const float l = dfl_side(box, n, a, 0, hd.dfl_exp);
-      const float t = dfl_side(box, n, a, 1, hd.dfl_exp);
-      const float r = dfl_side(box, n, a, 2, hd.dfl_exp);
-      const float b = dfl_side(box, n, a, 3, hd.dfl_exp);
-      const int ai = hd.anchor_offset + a;
-      const float ax = __ldg(p.anchor_x + ai), ay = __ldg(p.anchor_y + ai), st = __ldg(p.strides + ai);
-      const float x1 = __fsub_rn(ax, l), y1 = __fsub_rn(ay, t), x2 = __fadd_rn(ax, r), y2 = __fadd_rn(ay, b);
-      const float cx = __fmul_rn(__fmul_rn(__fadd_rn(x1, x2), 0.5f), st);
-      const float cy = __fmul_rn(__fmul_rn(__fadd_rn(y1, y2), 0.5f), st);
-      const float bw = __fmul_rn(__fsub_rn(x2, x1), st);
-      const float bh = __fmul_rn(__fsub_rn(y2, y1), st);
-      const int slot = atomicAdd(&s_n, 1);
-      s_score[slot] = best;
-      s_box[slot] = make_float4(__fdiv_rn(__fsub_rn(__fsub_rn(cx, __fdiv_rn(bw, 2.0f)), pad_left), lscale),
-                                __fdiv_rn(__fsub_rn(__fsub_rn(cy, __fdiv_rn(bh, 2.0f)), pad_top), lscale),
-                                __fdiv_rn(bw, lscale), __fdiv_rn(bh, lscale));
-      s_anchor[slot] = (int16_t)ai;
-      s_class[slot] = (uint8_t)best_c;
     }
+    same = __syncthreads_and(same) != 0;
+    if (tid == 0) s_toe[h] = same ? 1 : 0;
+  }
+  for (int i = tid; i < kScoreVals; i += kDecodeThreads) {
+    const float v = s_sig[i];
+    int r = 0;
+    for (int j = 0; j < kScoreVals; ++j) r += s_sig[j] > v ? 1 : 0;
+    s_rank[i] = (uint16_t)r;
   }
   __syncthreads();
+
+  // 1. candidates in anchor order: prune, class score, DFL, box
+  for (int base = 0; base < total; base += kDecodeThreads) {
+    const int A = base + tid;
+    bool pass = false;
+    float4 bx = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sidx = 0, best_c = 0;
+    if (A < total) {
+      const int h = (A >= p.head[1].anchor_offset) + (A >= p.head[2].anchor_offset);
+      const DecodeHeadDev& hd = p.head[h];
+      const int n = hd.anchors, a = A - hd.anchor_offset;
+      const int8_t* box = eg + hd.box_off;
+      const int8_t* cls = eg + hd.cls_off;
+      int q_max = -128;
+#pragma unroll 16
+      for (int c = 0; c < p.num_classes; ++c) q_max = max(q_max, (int)cls[(long long)c * n + a]);
+      if (q_max > hd.qi) {
+        const float* sig = s_sig + h * 256 + 128;
+        float best;
+        int q_best = q_max;
+        if (hd.sigmoid_low) {
+          best = sig[q_max];
+          pass = best >= p.conf;
+          if (pass) {
+            const int lo = s_low[h * 256 + q_max + 128];
+            while (best_c < p.num_classes - 1 && (int)cls[(long long)best_c * n + a] < lo) ++best_c;
+          }
+        } else {
+          q_best = cls[a];
+          best = sig[q_best];
+          for (int c = 1; c < p.num_classes; ++c) {
+            const int q = cls[(long long)c * n + a];
+            const float pr = sig[q];
+            if (pr > best) {
+              best = pr;
+              best_c = c;
+              q_best = q;
+            }
+          }
+          pass = best >= p.conf;
+        }
+        if (pass) {
+          const float* diag = s_toe[h] ? s_diag + h * 256 : nullptr;
+          const float l = dfl_side(box, n, a, 0, hd.dfl_exp, diag);
+          const float t = dfl_side(box, n, a, 1, hd.dfl_exp, diag);
+          const float r = dfl_side(box, n, a, 2, hd.dfl_exp, diag);
+          const float b = dfl_side(box, n, a, 3, hd.dfl_exp, diag);
+          const float ax = __ldg(p.anchor_x + A), ay = __ldg(p.anchor_y + A), st = __ldg(p.strides + A);
+          const float x1 = __fsub_rn(ax, l), y1 = __fsub_rn(ay, t), x2 = __fadd_rn(ax, r), y2 = __fadd_rn(ay, b);
+          const float cx = __fmul_rn(__fmul_rn(__fadd_rn(x1, x2), 0.5f), st);
+          const float cy = __fmul_rn(__fmul_rn(__fadd_rn(y1, y2), 0.5f), st);
+          const float bw = __fmul_rn(__fsub_rn(x2, x1), st);
+          const float bh = __fmul_rn(__fsub_rn(y2, y1), st);
+          bx = make_float4(__fdiv_rn(__fsub_rn(__fsub_rn(cx, __fdiv_rn(bw, 2.0f)), pad_left), lscale),
+                           __fdiv_rn(__fsub_rn(__fsub_rn(cy, __fdiv_rn(bh, 2.0f)), pad_top), lscale),
+                           __fdiv_rn(bw, lscale), __fdiv_rn(bh, lscale));
+          sidx = h * 256 + q_best + 128;
+          if (__dmul_rn((double)bx.z, (double)bx.w) <= DBL_EPSILON) sidx |= kSidxTiny;
+        }
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, pass);
+    if (lane == 0) s_wcnt[warp] = __popc(bal);
+    __syncthreads();
+    if (warp == 0) {
+      const int v = s_wcnt[lane];
+      const int incl = warp_incl_scan(v, lane);
+      s_wcnt[lane] = s_n + incl - v;
+      if (lane == 31) s_ntot = s_n + incl;
+    }
+    __syncthreads();
+    if (pass) {
+      const int slot = s_wcnt[warp] + __popc(bal & ((1u << lane) - 1u));
+      s_box[slot] = bx;
+      s_sidx[slot] = (uint16_t)sidx;
+      s_class[slot] = (uint8_t)best_c;
+    }
+    __syncthreads();
+    if (tid == 0) s_n = s_ntot;
+    __syncthreads();
+  }
   const int n = s_n;
   if (n == 0) {
     if (tid == 0) p.out_count[img] = 0;
     return;
   }
 
-  // 2. the class offset of NMSBoxesBatched: max over every candidate's corners, starting at 0
+  // 2. the class offset of NMSBoxesBatched (max over every candidate's corners, starting at 0), and
+  //    the order: score descending (rank ascending), then anchor ascending (slot order)
   double mc = 0.0;
   for (int i = tid; i < n; i += kDecodeThreads) {
-    const float4 bx = s_box[i];
-    const double x1 = bx.x, y1 = bx.y, x2 = __dadd_rn(x1, (double)bx.z), y2 = __dadd_rn(y1, (double)bx.w);
+    const float4 b = s_box[i];
+    const double x1 = b.x, y1 = b.y, x2 = __dadd_rn(x1, (double)b.z), y2 = __dadd_rn(y1, (double)b.w);
     mc = fmax(mc, fmax(fmax(x1, y1), fmax(x2, y2)));
+    s_ordA[i] = (uint16_t)i;
   }
   for (int o = 16; o > 0; o >>= 1) mc = fmax(mc, __shfl_xor_sync(0xffffffffu, mc, o));
-  if ((tid & 31) == 0) s_maxc[tid >> 5] = mc;
-
-  // 3. order: score descending, then anchor ascending (bitonic sort of slot ids, padded to 2^k)
-  int np2 = 1;
-  while (np2 < n) np2 <<= 1;
-  for (int i = tid; i < np2; i += kDecodeThreads) s_order[i] = (uint16_t)(i < n ? i : 0xFFFF);
+  if (lane == 0) s_maxc[warp] = mc;
+  s_wc[warp][lane] = 0;
+  if (lane == 0) s_wc[warp][32] = 0;
   __syncthreads();
-  auto before = [&](uint16_t x, uint16_t y) -> bool {  // x strictly precedes y
-    if (y == 0xFFFF) return x != 0xFFFF;
-    if (x == 0xFFFF) return false;
-    const float sx = s_score[x], sy = s_score[y];
-    return sx > sy || (sx == sy && s_anchor[x] < s_anchor[y]);
-  };
-  for (int k = 2; k <= np2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < np2; i += kDecodeThreads) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint16_t x = s_order[i], y = s_order[ixj];
-          const bool up = (i & k) == 0;
-          if (up ? before(y, x) : before(x, y)) {
-            s_order[i] = y;
-            s_order[ixj] = x;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
+  radix_pass(s_ordA, s_ordB, n, [&](uint16_t k) { return (int)(s_rank[s_sidx[k] & 0x3FF] & 31); }, s_cnt, s_wc, tid);
+  radix_pass(s_ordB, s_ordA, n, [&](uint16_t k) { return (int)(s_rank[s_sidx[k] & 0x3FF] >> 5); }, s_cnt, s_wc, tid);
   double maxc = 0.0;
-  for (int w = 0; w < kDecodeThreads / 32; ++w) maxc = fmax(maxc, s_maxc[w]);
+  for (int w = 0; w < kDecodeWarps; ++w) maxc = fmax(maxc, s_maxc[w]);
   const double off_step = __dadd_rn(maxc, 1.0);
+  const bool iou_nonneg = p.iou >= 0.f;  // false for NaN too
+  const bool iou_unit = iou_nonneg && p.iou <= 1.f;
 
-  // 4. Greedy NMS over the global order, 32 candidates at a time. A candidate is kept when no
-  //    earlier kept candidate suppresses it. For a chunk of 32 (in order): every warp takes one
-  //    candidate and its lanes test it against all candidates kept before the chunk; then the
-  //    chunk's own 32 x 32 pairs are tested (thread (a, b): does earlier b suppress later a);
-  //    then one warp resolves the chunk in order (a candidate survives if nothing kept before the
-  //    chunk and no kept earlier member of the chunk suppresses it) and appends the kept ones.
-  //    Exactly the sequential greedy loop, with a block barrier per 32 candidates instead of per
-  //    candidate. Kept ids overwrite the front of s_order, behind the chunk being read.
+  // 3. NMS. Scores strictly above conf are a prefix of the order.
   if (tid == 0) s_nv = n;
   __syncthreads();
   for (int i = tid; i < n; i += kDecodeThreads)
-    if (!(s_score[s_order[i]] > p.conf)) atomicMin(&s_nv, i);  // the rest: a prefix of the order
+    if (!(s_sig[s_sidx[s_ordA[i]] & 0x3FF] > p.conf)) atomicMin(&s_nv, i);
   __syncthreads();
   const int nv = s_nv;
-  const int warp = tid >> 5, lane = tid & 31;
-  for (int r0 = 0; r0 < nv; r0 += 32) {
-    const int cn = min(32, nv - r0);
-    if (tid < 32) s_chunk[tid] = tid < cn ? s_order[r0 + tid] : (uint16_t)0;
-    __syncthreads();
-    const int kept = s_kept;
-    if (warp < cn) {
-      const uint16_t ci = s_chunk[warp];
-      const float4 bi = s_box[ci];
-      const double oi = __dmul_rn((double)s_class[ci], off_step);
-      // kept candidates 32 at a time, stopping at the first group that suppresses this one (most
-      // suppressed candidates meet their suppressor among the first, highest-scoring kept boxes)
-      bool by_kept = false;
-      for (int k0 = 0; k0 < kept && !by_kept; k0 += 32) {
-        const int k = k0 + lane;
-        bool sup = false;
-        if (k < kept) {
-          const uint16_t ck = s_order[k];
-          sup = suppresses(bi, oi, s_box[ck], __dmul_rn((double)s_class[ck], off_step), p.iou);
+  const int nwords = (nv + 31) >> 5;
+  for (int w = tid; w < nwords; w += kDecodeThreads)
+    s_alive[w] = (w + 1) * 32 <= nv ? 0xffffffffu : ((1u << (nv & 31)) - 1u);
+  if (tid == 0) s_f = 0;
+  __syncthreads();
+  for (int step = 0; step < nv; ++step) {  // each step takes at least one alive candidate
+    // a. the next (up to) 32 alive positions at or after f, gathered by warp 0
+    if (warp == 0) {
+      const int f = s_f;
+      int got = 0, last = -1;
+      for (int w0 = f >> 5; got < 32 && w0 < nwords; w0 += 32) {
+        const int wi = w0 + lane;
+        uint32_t bits = wi < nwords ? s_alive[wi] : 0u;
+        if (wi == (f >> 5)) bits &= ~0u << (f & 31);
+        const int cnt = __popc(bits);
+        const int incl = warp_incl_scan(cnt, lane);
+        int idx = got + incl - cnt;
+        while (bits && idx < 32) {
+          const int b = __ffs(bits) - 1;
+          bits &= bits - 1;
+          s_chunk[idx] = (uint16_t)(wi * 32 + b);
+          last = max(last, wi * 32 + b);
+          ++idx;
         }
-        by_kept = __any_sync(0xffffffffu, sup);
+        got = min(32, got + __shfl_sync(0xffffffffu, incl, 31));
       }
-      // earlier chunk members b < warp that would suppress this one if kept
-      bool m = false;
-      if (lane < warp) {
-        const uint16_t cb = s_chunk[lane];
-        m = suppresses(bi, oi, s_box[cb], __dmul_rn((double)s_class[cb], off_step), p.iou);
-      }
-      const unsigned mask = __ballot_sync(0xffffffffu, m);
+      for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
       if (lane == 0) {
-        s_mask[warp] = mask;
-        s_sup[warp] = by_kept ? 1 : 0;
+        s_cn = got;
+        s_f = last + 1;
       }
     }
     __syncthreads();
+    const int cn = s_cn;
+    if (cn == 0) break;
+    // b. the chunk among itself: does earlier member b suppress member a (warp a, lane b)
+    if (warp < cn) {
+      const uint16_t ca = s_ordA[s_chunk[warp]];
+      const float4 ba = s_box[ca];
+      const int cla = s_class[ca];
+      const bool tiny_a = (s_sidx[ca] & kSidxTiny) != 0;
+      bool m = false;
+      if (lane < warp) {
+        const uint16_t cb = s_ordA[s_chunk[lane]];
+        m = pair_suppresses(ba, cla, tiny_a, s_box[cb], s_class[cb], (s_sidx[cb] & kSidxTiny) != 0, off_step, maxc,
+                            p.iou, iou_nonneg, iou_unit);
+      }
+      const unsigned mask = __ballot_sync(0xffffffffu, m);
+      if (lane == 0) s_mask[warp] = mask;
+    }
+    __syncthreads();
     if (warp == 0) {
-      // in order: a survives unless suppressed by an earlier kept candidate
       unsigned keep = 0u;
       for (int a = 0; a < cn; ++a)
-        if (!s_sup[a] && !(s_mask[a] & keep)) keep |= 1u << a;
-      if ((keep >> lane) & 1u) s_order[kept + __popc(keep & ((1u << lane) - 1u))] = s_chunk[lane];
-      if (lane == 0) s_kept = kept + __popc(keep);
+        if (!(s_mask[a] & keep)) keep |= 1u << a;
+      const int kept = s_kept;
+      if ((keep >> lane) & 1u) {
+        const int r = __popc(keep & ((1u << lane) - 1u));
+        const uint16_t c = s_ordA[s_chunk[lane]];
+        s_ordB[kept + r] = c;
+        s_newk[r] = c;
+      }
+      if (lane == 0) {
+        s_kept = kept + __popc(keep);
+        s_nk = __popc(keep);
+      }
+    }
+    __syncthreads();
+    // c. every alive position after the chunk against the chunk's kept boxes; warps take whole
+    //    words of the alive bits
+    const int nk = s_nk, f2 = s_f;
+    for (int w = (f2 >> 5) + warp; w < nwords; w += kDecodeWarps) {
+      const int pos = w * 32 + lane;
+      bool alive = pos >= f2 && ((s_alive[w] >> lane) & 1u);
+      if (alive) {
+        const uint16_t ci = s_ordA[pos];
+        const float4 bi = s_box[ci];
+        const int cli = s_class[ci];
+        const bool tiny_i = (s_sidx[ci] & kSidxTiny) != 0;
+        for (int j = 0; j < nk && alive; ++j) {
+          const uint16_t ck = s_newk[j];
+          if (pair_suppresses(bi, cli, tiny_i, s_box[ck], s_class[ck], (s_sidx[ck] & kSidxTiny) != 0, off_step, maxc,
+                              p.iou, iou_nonneg, iou_unit))
+            alive = false;
+        }
+      }
+      const unsigned keepw = __ballot_sync(0xffffffffu, alive);
+      if (lane == 0) s_alive[w] = keepw;  // positions before f2 are behind every later gather
     }
     __syncthreads();
   }
 
-  // 5. detections in kept order
+  // 4. detections in kept order
   const int kept = s_kept;
   if (kept > p.capacity) {
     if (tid == 0) p.out_count[img] = -3;
     return;
   }
   for (int k = tid; k < kept; k += kDecodeThreads) {
-    const uint16_t c = s_order[k];
+    const uint16_t c = s_ordB[k];
     const long long o = (long long)img * p.capacity + k;
     reinterpret_cast<float4*>(p.out_box)[o] = s_box[c];
-    p.out_score[o] = s_score[c];
+    p.out_score[o] = s_sig[s_sidx[c] & 0x3FF];
     p.out_class[o] = s_class[c];
   }
   if (tid == 0) p.out_count[img] = kept;
 }
 
-// Dynamic shared memory: scores, boxes, anchors, classes, and the sort order.
-constexpr int decode_smem_bytes() {
-  return kDecodeMaxAnchors * (4 + 16 + 2 + 1) + 16384 * 2 + 16;
-}
+constexpr int decode_smem_bytes() { return kDsBytes; }
 
 // ---------------------------------------------------------------- dense decode
 // The reference's InferenceSession.decode_yolo_predictions (runtime/session.py:1223-1278) on the

@@ -29,6 +29,7 @@ namespace ixb {
 constexpr int kGemmBK = 128;                 // K bytes per stage: one 128-byte swizzle row
 constexpr int kGemmABlock = 128 * kGemmBK;   // one 128-row A box
 constexpr int kGemmMaxStages = 8;
+constexpr int kGemmBarBytes = 512;           // mbarriers and the TMEM address after the stages
 enum : int { GEMM_OUT_SRS = 0, GEMM_OUT_I32 = 1 };
 
 struct GemmParams {
@@ -39,8 +40,9 @@ struct GemmParams {
   int bn, mt, m_tiles, n_tiles, kblocks, stages;
   int stage_bytes, stage_tx, bar_off;
   int raw_off;               // W4A8: offset of the packed int4 B tile inside a stage
-  int eg_off;                // W4A8: the tile's group exponents [BN][K/128] in shared memory, or -1
-                             // (read from global memory) when they would not fit
+  int eg_off;                // W4A8: two buffers of a tile's group exponents [BN][K/128] in shared
+                             // memory, or -1 (read from global memory) when they would not fit
+  int eg_stride;             // W4A8: bytes per exponent buffer
   int acc_cols, tmem_cols, nacc;  // TMEM accumulators of acc_cols columns (1 or 2)
   uint32_t idesc;
   int out_kind;
@@ -78,65 +80,90 @@ enum : int { GEMM_B_TMA = 0, GEMM_B_W4 = 1 };
 constexpr int kW4Warps = 8;  // warps unpacking int4 weights into the B stage (GEMM_B_W4): two per SM sub-partition
 constexpr int gemm_threads(int epi, int bsrc) { return 32 * (epi + 2 + (bsrc == GEMM_B_W4 ? kW4Warps : 0)); }
 
+// Per-byte arithmetic shift right by e in [0, 4] of int8 lanes whose low nibbles are zero: the
+// logical shift moves only zero bits across lanes, and the sign (prmt's sign-replicate selectors
+// give 0xFF per negative byte) fills the top e bits `hm` of each byte.
+__device__ __forceinline__ uint32_t sra8_nib(uint32_t v, uint32_t e, uint32_t hm) {
+  uint32_t sgn;
+  asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(sgn) : "r"(v));
+  return (v >> e) | (sgn & hm);
+}
+
 // B warps of the W4A8 GEMM: per stage the TMA has brought the packed int4 tile (BN rows x 64
 // bytes = 128 values of K, one group) into shared memory with the A boxes; the warps turn it
 // into the int8 B operand, 16 values (8 packed bytes) per item into one 16-byte chunk of the
-// 128-byte swizzled row (chunk c at c ^ (row % 8)), scaled by the group's 2^-e. Reading the packed
-// tile from shared memory keeps global-memory latency out of the unpack loop.
+// 128-byte swizzled row (chunk c at c ^ (row % 8)), scaled by the group's 2^-e. A thread first
+// loads all its items of the stage (at most 8) and their exponents, then converts and stores
+// them, so the shared-memory latencies overlap instead of adding up item by item. The tile's
+// exponents come by bulk copy from the TMA producer into one of two buffers (eg_full / eg_empty).
+// UT threads unpack: the B warps, joined by the epilogue warps when every CTA has one tile (their
+// drain then waits for the whole K loop anyway).
+constexpr int kW4MaxItems = 8;  // 8 * BN items per stage over at least kW4Warps * 32 threads, BN <= 256
 __device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* bfull,
-                                           int ut) {
-  constexpr int UT = kW4Warps * 32;
+                                           uint64_t* eg_full, uint64_t* eg_empty, int ut, int UT) {
   const int S = p.stages, G = p.K / 128;
   const int tiles = p.m_tiles * p.n_tiles;
-  const int items = 8 * p.bn;
-  uint8_t* eg_s = p.eg_off >= 0 ? smem + p.eg_off : nullptr;
-  int s = 0;
+  // item j of this thread: row rb + j * rstep, 8-byte chunk c of it. UT is a multiple of 64, so a
+  // thread's rows keep their place in the 8-row swizzle atom: one swizzled chunk offset per thread
+  const int c = ut & 7, rb = ut >> 3, rstep = UT >> 3;
+  const int raw0 = rb * 64 + c * 8, raw_step = rstep * 64;
+  const int bst0 = (rb >> 3) * 1024 + (rb & 7) * 128 + ((c ^ (rb & 7)) << 4), bst_step = (rstep >> 3) * 1024;
+  int s = 0, li = 0;
   uint32_t ph = 0;
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {
     const int ntile = t % p.n_tiles;
     const int n0 = ntile * p.bn;
-    if (eg_s) {
-      // the tile's group exponents, one contiguous run of [N][K/128], once per tile (the 128 B-warp
-      // threads meet on named barrier 2 around the refill; no thread leaves this loop early)
-      asm volatile("bar.sync 2, %0;" ::"n"(UT) : "memory");
-      const long long e0 = (long long)n0 * G, e1 = (long long)min(n0 + p.bn, p.N) * G;
-      for (long long i = e0 + ut; i < e1; i += UT) eg_s[i - e0] = __ldg(p.eg + i);
-      asm volatile("bar.sync 2, %0;" ::"n"(UT) : "memory");
+    const uint8_t* eg_s = nullptr;
+    bool eg_ok = true;
+    if (p.eg_off >= 0) {
+      eg_ok = mbar_wait(&eg_full[li & 1], (li >> 1) & 1);
+      eg_s = smem + p.eg_off + (li & 1) * p.eg_stride;
     }
     for (int kb = 0; kb < p.kblocks; ++kb) {
-      const bool ok = mbar_wait(&full[s], ph);  // a timeout raised the device flag; the loop runs on
+      const bool ok = mbar_wait(&full[s], ph) && eg_ok;  // a timeout raised the device flag; the loop runs on
       uint8_t* st = smem + s * p.stage_bytes;
       uint8_t* bst = st + p.mt * kGemmABlock;
       const uint8_t* raw = st + p.raw_off;
-      for (int i = ut; ok && i < items; i += UT) {
-        const int r = i >> 3, c = i & 7;
-        const int n = n0 + r;
-        const uint2 w = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);  // zero past N (TMA fill)
-        const uint32_t e = n >= p.N ? 0u : (eg_s ? (uint32_t)eg_s[r * G + kb] : (uint32_t)__ldg(p.eg + (long long)n * G + kb));
-        uint4 o = make_uint4(w4_lo16(w.x), w4_hi16(w.x), w4_lo16(w.y), w4_hi16(w.y));
-        if (e) {
-          const uint32_t keep = (0xFFu >> e) * 0x01010101u;
-          const uint32_t fill = ((0xFFu << (8 - e)) & 0xFFu);
-          o.x = sra8_lanes(o.x, e, keep, fill);
-          o.y = sra8_lanes(o.y, e, keep, fill);
-          o.z = sra8_lanes(o.z, e, keep, fill);
-          o.w = sra8_lanes(o.w, e, keep, fill);
+      uint2 w[kW4MaxItems];
+      uint32_t e[kW4MaxItems];
+#pragma unroll
+      for (int j = 0; j < kW4MaxItems; ++j) {
+        const int r = rb + j * rstep;
+        if (ok && r < p.bn) {
+          const int n = n0 + r;
+          w[j] = *reinterpret_cast<const uint2*>(raw + raw0 + j * raw_step);  // zero past N (TMA fill)
+          e[j] = n >= p.N ? 0u : (eg_s ? (uint32_t)eg_s[r * G + kb] : (uint32_t)__ldg(p.eg + (long long)n * G + kb));
         }
-        *reinterpret_cast<uint4*>(bst + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = o;
+      }
+#pragma unroll
+      for (int j = 0; j < kW4MaxItems; ++j) {
+        const int r = rb + j * rstep;
+        if (ok && r < p.bn) {
+          const uint32_t hm = ((0xFF00u >> e[j]) & 0xFFu) * 0x01010101u;
+          const uint4 o = make_uint4(sra8_nib(w4_lo16(w[j].x), e[j], hm), sra8_nib(w4_hi16(w[j].x), e[j], hm),
+                                     sra8_nib(w4_lo16(w[j].y), e[j], hm), sra8_nib(w4_hi16(w[j].y), e[j], hm));
+          *reinterpret_cast<uint4*>(bst + bst0 + j * bst_step) = o;
+        }
       }
       fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
-      mbar_arrive(&bfull[s]);
+      __syncwarp();
+      if ((ut & 31) == 0) mbar_arrive(&bfull[s]);  // one arrival per warp: 256 on one barrier serialise
       if (++s == S) {
         s = 0;
         ph ^= 1;
       }
     }
+    __syncwarp();
+    if (p.eg_off >= 0 && (ut & 31) == 0) mbar_arrive(&eg_empty[li & 1]);  // this tile's exponent buffer is free
   }
 }
 
 template <int EPI, int BSRC>
 __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
   constexpr int PW = EPI, MW = EPI + 1, UW0 = EPI + 2;
+  // W4A8 with one tile per CTA: the epilogue warps unpack too until the K loop ends
+  const bool helpers = BSRC == GEMM_B_W4 && p.m_tiles * p.n_tiles <= (int)gridDim.x;
+  const int unpack_warps = kW4Warps + (helpers ? EPI : 0);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -147,7 +174,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* done = acc_empty + 2;
   uint64_t* bfull = done + 1;  // W4A8: the stage's B operand is unpacked
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bfull + kGemmMaxStages);
+  uint64_t* eg_full = bfull + kGemmMaxStages;  // W4A8: a tile's exponents have landed / are free
+  uint64_t* eg_empty = eg_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(eg_empty + 2);
   const int tiles = p.m_tiles * p.n_tiles;
 
   if (warp == MW) {
@@ -158,13 +187,17 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&bfull[s], kW4Warps * 32);
+      mbar_init(&bfull[s], unpack_warps);
     }
     for (int b = 0; b < p.nacc; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], EPI * 32);
     }
     mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&eg_full[b], 1);
+      mbar_init(&eg_empty[b], unpack_warps);
+    }
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.ta) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tb) : "memory");
@@ -177,11 +210,23 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
   if (warp == PW) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int s = 0;
+      int s = 0, li = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+      const int G = p.K / 128;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++li) {
         const int mtile = t / p.n_tiles, ntile = t - mtile * p.n_tiles;
+        if (BSRC == GEMM_B_W4 && p.eg_off >= 0) {
+          // the tile's exponents: rows [n0, min(n0 + BN, N)) x G, contiguous in [N][K/128] (BN and N
+          // are multiples of 16, so the run starts and ends on 16-byte boundaries)
+          if (!mbar_wait(&eg_empty[li & 1], ((li >> 1) & 1) ^ 1)) break;
+          const int n0 = ntile * p.bn, rows = min(p.bn, p.N - n0);
+          const uint32_t bytes = (uint32_t)rows * G;
+          mbar_arrive_expect_tx(&eg_full[li & 1], bytes);
+          uint8_t* dst = smem + p.eg_off + (li & 1) * p.eg_stride;
+          for (uint32_t off = 0; off < bytes; off += 16384u)
+            bulk_g2s(dst + off, p.eg + (long long)n0 * G + off, min(16384u, bytes - off), &eg_full[li & 1]);
+        }
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1)) {
             ok = false;
@@ -202,7 +247,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     }
   } else if (BSRC == GEMM_B_W4 && warp >= UW0) {
     // ------------------------------------------------------------ int4 -> int8 B producers
-    produce_w4(p, smem, full, bfull, tid - UW0 * 32);
+    produce_w4(p, smem, full, bfull, eg_full, eg_empty, tid - UW0 * 32, unpack_warps * 32);
   } else if (warp == MW) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -249,6 +294,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    if (helpers) produce_w4(p, smem, full, bfull, eg_full, eg_empty, kW4Warps * 32 + tid, unpack_warps * 32);
     constexpr int NG = EPI / 4;
     const int q = warp & 3, g = warp >> 2;
     const int nch = p.bn / 16;

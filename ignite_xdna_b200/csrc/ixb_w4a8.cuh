@@ -64,156 +64,141 @@ __global__ void w4a8_groups_kernel(const int8_t* __restrict__ gpos, int G, int N
 __device__ __forceinline__ uint32_t w4_lo16(uint32_t x) { return (x << 4) & 0xF0F0F0F0u; }
 __device__ __forceinline__ uint32_t w4_hi16(uint32_t x) { return x & 0xF0F0F0F0u; }
 
-// Per-byte arithmetic shift right by e in [0, 4] of int8 lanes that are multiples of 16 (exact).
-__device__ __forceinline__ uint32_t sra8_lanes(uint32_t v, uint32_t e, uint32_t keep, uint32_t fill) {
-  // logical shift (low nibbles are zero, so no bits cross lanes), then the sign into the top e bits
-  const uint32_t t = (v >> e) & keep;
-  const uint32_t neg = (v >> 7) & 0x01010101u;
-  return t + neg * fill;
-}
-
 // ---------------------------------------------------------------- GEMV (M = 1)
 // Weight-streaming GEMV: one CTA per SM owns a contiguous range of output columns, whose packed
-// weights are one contiguous byte range of the image ([N][K/2]). A producer thread streams that
-// range through a ring of shared-memory stages with bulk copies (the TMA engine keeps up to
-// ~200 KB per SM in flight, enough to cover DRAM latency at full bandwidth), while 16 consumer
-// warps take the columns of each stage: a column's K words (16 bytes = 32 values) are split over
-// the lanes (and, for large K, over several warps), each word is 8 dp4a on 16 * w and the
-// activations (staged in shared memory once per CTA), shifted per group, and the partial sums
-// meet in a warp (then a shared-memory) reduction before the per-column SRS.
-constexpr int kGemvWarps = 16;                 // consumer warps
-constexpr int kGemvThreads = 32 * (kGemvWarps + 1);
-constexpr int kGemvSmemBudget = 200 * 1024;    // stages + activations
+// weights are one contiguous byte range of the image ([N][K/2]). Each of 16 warps takes every 16th
+// column of the range; a column's K words (16 bytes = 32 values) are spread over the lanes, each
+// word is 8 dp4a on 16 * w and the activations, shifted by the group's exponent, and a warp
+// reduction ends the column with its SRS. The weights are read straight from global memory with
+// 16-byte streaming loads, all of a batch's loads (CPB columns x WPL words per lane, up to 8)
+// issued before any is used; two CTAs per SM, so one computes while the other's loads are in
+// flight and each SM keeps ~128 KB requested -- what the DRAM latency asks for at this GPU's
+// bandwidth per SM. The first batch is issued before the activations and the CTA's group
+// exponents are staged in shared memory, so their latency hides behind it.
+constexpr int kGemvWarps = 16;
+constexpr int kGemvThreads = 32 * kGemvWarps;
+constexpr int kGemvMaxWpl = 8;           // 16-byte loads per lane in flight per batch
+constexpr int kGemvCtasPerSm = 2;
 
 struct GemvPlan {
-  int grid, cols_per_stage, warps_per_col, stages, stage_bytes, eg_bytes, smem;
+  int grid, wpl, eg_bytes, smem;
 };
 
 __host__ inline GemvPlan plan_gemv(int N, int K, int sms) {
   GemvPlan g;
-  const int col_bytes = K / 2;
-  g.grid = std::min(sms, N);
-  // the group exponents of a CTA's columns (at most ceil(N / grid) of them), staged once
-  g.eg_bytes = ((N + g.grid - 1) / g.grid * (K / kW4Group) + 15) / 16 * 16;
-  // columns per stage: 16 (one per warp) unless a stage would pass 96 KB or fewer than two fit
-  for (int ch = kGemvWarps;; ch >>= 1) {
-    g.cols_per_stage = ch;
-    g.warps_per_col = kGemvWarps / ch;
-    g.stage_bytes = ch * col_bytes;
-    g.stages = std::min(4, (kGemvSmemBudget - K - g.eg_bytes) / g.stage_bytes);
-    if (ch == 1 || (g.stage_bytes <= 96 * 1024 && g.stages >= 2)) break;
-  }
-  g.smem = g.stages * g.stage_bytes + K + g.eg_bytes + 2 * 8 * 4 + 1024;
+  g.grid = std::min(kGemvCtasPerSm * sms, N);
+  const int words = K / 32;
+  g.wpl = std::min(kGemvMaxWpl, (words + 31) / 32);  // columns of more words are taken in segments
+  // the group exponents of a CTA's columns (at most ceil(N / grid) of them), from the 16-byte
+  // boundary at or below the first to the one at or above the last (up to 15 more on each side)
+  g.eg_bytes = ((N + g.grid - 1) / g.grid * (K / kW4Group) + 32 + 15) / 16 * 16;
+  g.smem = K + g.eg_bytes;
   return g;
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 1)
-    w4a8_gemv_kernel(const int8_t* __restrict__ a, const uint8_t* __restrict__ wq, const uint8_t* __restrict__ eg,
-                     const int32_t* __restrict__ shift, int8_t* __restrict__ out, int N, int K, int CH, int WPC,
-                     int S, int stage_bytes, int eg_bytes) {
-  extern __shared__ uint8_t gsm_raw[];
-  uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 127) & ~uintptr_t(127));
-  uint8_t* eg_s = gsm + S * stage_bytes + K;   // [columns of this CTA][K / 128]
-  uint64_t* full = reinterpret_cast<uint64_t*>(eg_s + eg_bytes);
-  uint64_t* empty = full + 4;
-  __shared__ int colsum[4][kGemvWarps], colcnt[4][kGemvWarps];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = (int)((long long)blockIdx.x * N / gridDim.x), n1 = (int)((long long)(blockIdx.x + 1) * N / gridDim.x);
-  const int chunks = (n1 - n0 + CH - 1) / CH;
-  const int col_bytes = K / 2, words = K / 32;
-  int8_t* a_s = reinterpret_cast<int8_t*>(gsm + S * stage_bytes);
-  if (tid == kGemvWarps * 32) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kGemvWarps);
+__device__ __forceinline__ uint4 ld_stream16(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// 16 * sum over one 16-byte word (32 values) of a * w, shifted down by the group exponent e:
+// exact, the dp4a sum being a multiple of 16.
+__device__ __forceinline__ int gemv_word(uint4 w, const int8_t* a_s, int wd, uint32_t e) {
+  const int4 a0 = reinterpret_cast<const int4*>(a_s)[2 * wd];
+  const int4 a1 = reinterpret_cast<const int4*>(a_s)[2 * wd + 1];
+  int pr = 0;
+  pr = __dp4a((int)w4_lo16(w.x), a0.x, pr);
+  pr = __dp4a((int)w4_hi16(w.x), a0.y, pr);
+  pr = __dp4a((int)w4_lo16(w.y), a0.z, pr);
+  pr = __dp4a((int)w4_hi16(w.y), a0.w, pr);
+  pr = __dp4a((int)w4_lo16(w.z), a1.x, pr);
+  pr = __dp4a((int)w4_hi16(w.z), a1.y, pr);
+  pr = __dp4a((int)w4_lo16(w.w), a1.z, pr);
+  pr = __dp4a((int)w4_hi16(w.w), a1.w, pr);
+  return pr >> e;
+}
+
+// One warp's columns, CPB at a time, WPL words per lane per column (the column's words wd = lane +
+// 32 i); columns of more than 32 * WPL words (WPL = 8) go in segments of 256 words.
+template <int WPL>
+__device__ __forceinline__ void gemv_warp(const uint8_t* __restrict__ wq, const int32_t* __restrict__ shift,
+                                          int8_t* __restrict__ out, const int8_t* a_s, const uint8_t* eg_s,
+                                          long long e_lo, int n0, int n1, int K, int warp, int lane, bool& staged,
+                                          const int8_t* __restrict__ a, const uint8_t* __restrict__ eg, long long e_hi,
+                                          uint8_t* eg_w, int8_t* a_w) {
+  constexpr int CPB = kGemvMaxWpl / WPL > 4 ? 4 : kGemvMaxWpl / WPL;
+  const int words = K / 32, G = K / kW4Group, col_bytes = K / 2;
+  for (int t0 = 0;; t0 += CPB) {
+    int col[CPB];
+    bool any = false;
+#pragma unroll
+    for (int j = 0; j < CPB; ++j) {
+      col[j] = n0 + warp + kGemvWarps * (t0 + j);
+      any |= col[j] < n1;
     }
-    fence_mbar_init();
-  }
-  for (int i = tid; i < K / 16; i += kGemvThreads)
-    reinterpret_cast<int4*>(a_s)[i] = __ldg(reinterpret_cast<const int4*>(a) + i);
-  {
-    const int G = K / kW4Group;
-    const long long e0 = (long long)n0 * G, e1 = (long long)n1 * G;  // contiguous: [N][K / 128]
-    for (long long i = e0 + tid; i < e1; i += kGemvThreads) eg_s[i - e0] = __ldg(eg + i);
-  }
-  if (tid < 4 * kGemvWarps) {
-    (&colsum[0][0])[tid] = 0;
-    (&colcnt[0][0])[tid] = 0;
-  }
-  __syncthreads();
-  if (warp == kGemvWarps) {
-    // producer: chunk c (CH columns, the last one ragged) into stage c % S
-    if (lane == 0) {
-      uint32_t ph = 0;
-      for (int c = 0, s = 0; c < chunks; ++c) {
-        if (!mbar_wait(&empty[s], ph ^ 1)) break;
-        const int cols = min(CH, n1 - n0 - c * CH);
-        const uint32_t bytes = (uint32_t)cols * col_bytes;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        const uint8_t* src = wq + ((long long)n0 + (long long)c * CH) * col_bytes;
-        for (uint32_t off = 0; off < bytes; off += 32768u)
-          bulk_g2s(gsm + s * stage_bytes + off, src + off, min(32768u, bytes - off), &full[s]);
-        if (++s == S) {
-          s = 0;
-          ph ^= 1;
+    if (!any && staged) break;
+    int acc[CPB];
+#pragma unroll
+    for (int j = 0; j < CPB; ++j) acc[j] = 0;
+    for (int seg = 0; seg < words; seg += 32 * WPL) {
+      uint4 w[CPB][WPL];
+#pragma unroll
+      for (int j = 0; j < CPB; ++j)
+#pragma unroll
+        for (int i = 0; i < WPL; ++i) {
+          const int wd = seg + i * 32 + lane;
+          if (col[j] < n1 && wd < words) w[j][i] = ld_stream16(wq + (long long)col[j] * col_bytes + wd * 16);
         }
-      }
-    }
-    return;
-  }
-  uint32_t ph = 0;
-  const int G = K / kW4Group;
-  for (int c = 0, s = 0; c < chunks; ++c) {
-    const int cols = min(CH, n1 - n0 - c * CH);
-    if (!mbar_wait(&full[s], ph)) break;
-    const int ci = warp / WPC, part_i = warp % WPC;   // column of the chunk, share of its K words
-    int acc = 0;
-    if (ci < cols) {
-      const int n = n0 + c * CH + ci;
-      const uint8_t* col = gsm + s * stage_bytes + ci * col_bytes;
-      const uint8_t* erow = eg_s + (n - n0) * G;
-      for (int wd = part_i * 32 + lane; wd < words; wd += 32 * WPC) {
-        const uint4 w = *reinterpret_cast<const uint4*>(col + wd * 16);
-        const int4 a0 = reinterpret_cast<const int4*>(a_s)[2 * wd];
-        const int4 a1 = reinterpret_cast<const int4*>(a_s)[2 * wd + 1];
-        int pr = 0;
-        pr = __dp4a((int)w4_lo16(w.x), a0.x, pr);
-        pr = __dp4a((int)w4_hi16(w.x), a0.y, pr);
-        pr = __dp4a((int)w4_lo16(w.y), a0.z, pr);
-        pr = __dp4a((int)w4_hi16(w.y), a0.w, pr);
-        pr = __dp4a((int)w4_lo16(w.z), a1.x, pr);
-        pr = __dp4a((int)w4_hi16(w.z), a1.y, pr);
-        pr = __dp4a((int)w4_lo16(w.w), a1.z, pr);
-        pr = __dp4a((int)w4_hi16(w.w), a1.w, pr);
-        acc += pr >> erow[wd >> 2];   // pr = 16 * sum a * w, a multiple of 16: exact
+      if (!staged) {
+        // the CTA's activations and exponents, behind the first weight loads; every thread of the
+        // CTA comes here exactly once (its first batch), then meets the others at the barrier
+        const int tid = warp * 32 + lane;
+        for (int i = tid; i < K / 16; i += kGemvThreads)
+          reinterpret_cast<int4*>(a_w)[i] = __ldg(reinterpret_cast<const int4*>(a) + i);
+        for (long long i = e_lo / 16 + tid; i < e_hi / 16; i += kGemvThreads)
+          reinterpret_cast<uint4*>(eg_w)[i - e_lo / 16] = __ldg(reinterpret_cast<const uint4*>(eg) + i);
+        __syncthreads();
+        staged = true;
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    }
-    if (lane == 0 && ci < cols) {
-      const int n = n0 + c * CH + ci;
-      if (WPC == 1) {
-        out[n] = (int8_t)clamp_i8(rne_shift(acc, __ldg(shift + n)));
-      } else {
-        // the column's warps meet in shared memory: the last to arrive writes the output and
-        // clears the slot, before its release of the stage lets the slot be used again
-        atomicAdd(&colsum[s][ci], acc);
-        __threadfence_block();
-        if (atomicAdd(&colcnt[s][ci], 1) == WPC - 1) {
-          __threadfence_block();
-          const int sum = atomicExch(&colsum[s][ci], 0);
-          colcnt[s][ci] = 0;
-          out[n] = (int8_t)clamp_i8(rne_shift(sum, __ldg(shift + n)));
+      for (int j = 0; j < CPB; ++j) {
+        const uint8_t* erow = eg_s + ((long long)col[j] * G - e_lo);
+#pragma unroll
+        for (int i = 0; i < WPL; ++i) {
+          const int wd = seg + i * 32 + lane;
+          if (col[j] < n1 && wd < words) acc[j] += gemv_word(w[j][i], a_s, wd, erow[wd >> 2]);
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);   // this warp is done with the stage
-    if (++s == S) {
-      s = 0;
-      ph ^= 1;
+    if (!any) break;
+#pragma unroll
+    for (int j = 0; j < CPB; ++j) {
+      int v = acc[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && col[j] < n1) out[col[j]] = (int8_t)clamp_i8(rne_shift(v, __ldg(shift + col[j])));
     }
   }
+}
+
+template <int WPL>
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm)
+    w4a8_gemv_kernel(const int8_t* __restrict__ a, const uint8_t* __restrict__ wq, const uint8_t* __restrict__ eg,
+                     const int32_t* __restrict__ shift, int8_t* __restrict__ out, int N, int K) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  int8_t* a_s = reinterpret_cast<int8_t*>(gsm);  // [K]
+  uint8_t* eg_s = gsm + K;                        // exponents [e_lo, e_hi) of [N][K / 128]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = (int)((long long)blockIdx.x * N / gridDim.x), n1 = (int)((long long)(blockIdx.x + 1) * N / gridDim.x);
+  const int G = K / kW4Group;
+  // the CTA's exponents [n0, n1) x G are one contiguous run of [N][K / 128]; the staged range starts
+  // at the 16-byte boundary below it and ends at the one above (N * G is a multiple of 16: N is)
+  const long long e_lo = ((long long)n0 * G) & ~15LL, e_hi = ((long long)n1 * G + 15) & ~15LL;
+  bool staged = false;
+  gemv_warp<WPL>(wq, shift, out, a_s, eg_s, e_lo, n0, n1, K, warp, lane, staged, a, eg, e_hi, eg_s, a_s);
 }
 
 }  // namespace ixb

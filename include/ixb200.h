@@ -291,7 +291,7 @@ int ixb_u8i4_gemm_i32(const uint8_t* a, const uint8_t* image, int32_t* out, int 
  * heads in the engine's egress layout (device memory, image i at egress + i * egress_image_bytes).
  * Per head: the box and class heads' byte offsets inside an image's egress (int8 NCHW, 4 * 16 and
  * num_classes channels over `anchors`), the tables the reference builds with numpy
- * (dfl_exp float [256][256], sigmoid float [256], sigmoid_low int32 [256] or NULL;
+ * (dfl_exp float [256][256] 16-byte aligned, sigmoid float [256], sigmoid_low int32 [256] or NULL;
  * pipelines/decode_native.py:125-153) and the prune threshold q_threshold; anchor_x / anchor_y /
  * strides float [sum of anchors] (yolo_pipeline.py:191-203). letterbox float [batch][3] holds
  * pad_top, pad_left, scale per image. Writes per image up to `capacity` detections in NMS order:

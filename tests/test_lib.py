@@ -147,8 +147,12 @@ def test_w4a8_plan_and_refusals():
     for M, N, K in [(512, 11008, 4096), (512, 4096, 11008), (1, 4096, 128), (200, 64, 256)]:
         assert lib.ixb_gemm_plan_info(M, N, K, 1, info, 10) == 0
         bn, mt, mtiles, ntiles, kblocks, stages, grid, smem, tcols, stage_bytes = list(info)
-        assert mt * bn <= 256 and bn % 16 == 0 and kblocks * 128 == K and mt * 128 * mtiles >= M
-        assert stages >= 2 and smem <= 227 * 1024 and 2 * mt * bn <= tcols <= 512
+        # two accumulators of MT x BN columns, or one of up to 512 when every CTA has one tile
+        one_wave = mtiles * ntiles <= grid
+        assert (mt * bn <= 256 or (one_wave and mt * bn <= 512)) and bn % 16 == 0 and bn <= 256
+        assert kblocks * 128 == K and mt * 128 * mtiles >= M
+        nacc = 2 if 2 * mt * bn <= 512 else 1
+        assert stages >= 2 and smem <= 227 * 1024 and nacc * mt * bn <= tcols <= 512
     assert lib.ixb_gemm_plan_info(512, 64, 200, 1, info, 10) == L.IXB_ERR_INVALID   # K not a whole group
     nbytes = C.c_uint64()
     assert lib.ixb_w4a8_image_bytes(4096, 11008, C.byref(nbytes)) == 0
