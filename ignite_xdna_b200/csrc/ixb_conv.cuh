@@ -446,6 +446,18 @@ __device__ __forceinline__ uint4 epilogue16_linear(const uint32_t (&v)[16], floa
                     pack_sat_s8(r[8], r[9], r[10], r[11]), pack_sat_s8(r[12], r[13], r[14], r[15]));
 }
 
+// The table index t1 + 128 of t1 = clamp(rne(c * 2^-s), -128, 127) in one conversion: rne(x) + 128 =
+// rne(x + 128) (128 is even). For s <= 16 the fma computing x + 128 = float(c) * 2^-s + 128 is
+// exact whenever |x + 128| < 256 (x's fraction is a multiple of 2^-16; a left shift gives an
+// integer), and beyond that both forms saturate (as in srs_s8, float(c) is exact below 2^24); the
+// unsigned saturating conversion clamps to [0, 255]. It saves the s8 form's sign extension (1.4 %
+// of a step).
+__device__ __forceinline__ uint32_t srs_index(int c, float scale) {
+  uint32_t r;
+  asm("cvt.rni.sat.u8.f32 %0, %1;" : "=r"(r) : "f"(fmaf(__int2float_rn(c), scale, 128.f)));
+  return r;
+}
+
 template <bool RES>
 __device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8_t* lut, float scale,
                                             const ConvParams& p, float rscale, uint4 r4) {
@@ -454,7 +466,7 @@ __device__ __forceinline__ uint4 epilogue16(const uint32_t (&v)[16], const uint8
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     // the accumulator started at the bias: t1 = clamp(rne(acc >> shift)), then the table
-    uint32_t u = lut[srs_s8((int)v[i], scale)];
+    uint32_t u = (lut - 128)[srs_index((int)v[i], scale)];
     if (RES) {
       const int y = ((int)(int8_t)u << p.res_lsh_m) + ((int)rv[i] << p.res_lsh_r);  // |y| < 2^24
       u = (uint32_t)(uint8_t)srs_s8(y, rscale);
