@@ -946,8 +946,8 @@ template <int WPL>
 int launch_gemv(const GemvPlan& g, const int8_t* a, const uint8_t* wq, const uint8_t* eg, const int32_t* shift,
                 int8_t* out, int N, int K, cudaStream_t st) {
   if (int r = ensure_smem_limit(w4a8_gemv_kernel<WPL>, kSmemLimit / kGemvCtasPerSm - 1024)) return r;
-  w4a8_gemv_kernel<WPL><<<g.grid, kGemvThreads, g.smem, st>>>(a, wq, eg, shift, out, N, K);
-  IXB_CUDA(cudaGetLastError());
+  IXB_CUDA(launch_dependent(w4a8_gemv_kernel<WPL>, dim3(g.grid), dim3(kGemvThreads), g.smem, st, true, a, wq, eg,
+                            shift, out, N, K));
   return 0;
 }
 

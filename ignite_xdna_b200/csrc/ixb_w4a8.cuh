@@ -66,19 +66,21 @@ __device__ __forceinline__ uint32_t w4_hi16(uint32_t x) { return x & 0xF0F0F0F0u
 
 // ---------------------------------------------------------------- GEMV (M = 1)
 // Weight-streaming GEMV: one CTA per SM owns a contiguous range of output columns, whose packed
-// weights are one contiguous byte range of the image ([N][K/2]). Each of 16 warps takes every 16th
+// weights are one contiguous byte range of the image ([N][K/2]). Each of 12 warps takes every 12th
 // column of the range; a column's K words (16 bytes = 32 values) are spread over the lanes, each
 // word is 8 dp4a on 16 * w and the activations, shifted by the group's exponent, and a warp
 // reduction ends the column with its SRS. The weights are read straight from global memory with
 // 16-byte streaming loads, all of a batch's loads (CPB columns x WPL words per lane, up to 8)
-// issued before any is used; two CTAs per SM, so one computes while the other's loads are in
-// flight and each SM keeps ~128 KB requested -- what the DRAM latency asks for at this GPU's
-// bandwidth per SM. The first batch is issued before the activations and the CTA's group
-// exponents are staged in shared memory, so their latency hides behind it.
-constexpr int kGemvWarps = 16;
+// issued before any is used. One CTA per SM at half the SM's registers, launched with
+// programmatic dependent launch: it lets the next kernel on the stream launch at once, and the
+// next GEMV of a chain (a decode step's layers) then sits beside it on the same SM and asks for
+// its own weight range in the L2 (a bulk prefetch, a hint that reads nothing it depends on) while
+// this one streams; it waits for the previous kernel (griddepcontrol.wait) before any load whose
+// value it uses, then stages the activations and the CTA's group exponents in shared memory.
+constexpr int kGemvWarps = 12;
 constexpr int kGemvThreads = 32 * kGemvWarps;
 constexpr int kGemvMaxWpl = 8;           // 16-byte loads per lane in flight per batch
-constexpr int kGemvCtasPerSm = 2;
+constexpr int kGemvCtasPerSm = 2;        // for the registers: this GEMV and the next
 
 struct GemvPlan {
   int grid, wpl, eg_bytes, smem;
@@ -86,7 +88,7 @@ struct GemvPlan {
 
 __host__ inline GemvPlan plan_gemv(int N, int K, int sms) {
   GemvPlan g;
-  g.grid = std::min(kGemvCtasPerSm * sms, N);
+  g.grid = std::min(sms, N);
   const int words = K / 32;
   g.wpl = std::min(kGemvMaxWpl, (words + 31) / 32);  // columns of more words are taken in segments
   // the group exponents of a CTA's columns (at most ceil(N / grid) of them), from the 16-byte
@@ -122,13 +124,11 @@ __device__ __forceinline__ int gemv_word(uint4 w, const int8_t* a_s, int wd, uin
 }
 
 // One warp's columns, CPB at a time, WPL words per lane per column (the column's words wd = lane +
-// 32 i); columns of more than 32 * WPL words (WPL = 8) go in segments of 256 words.
+// 32 i); columns of more than 32 * WPL words go in segments of 32 * WPL words.
 template <int WPL>
 __device__ __forceinline__ void gemv_warp(const uint8_t* __restrict__ wq, const int32_t* __restrict__ shift,
                                           int8_t* __restrict__ out, const int8_t* a_s, const uint8_t* eg_s,
-                                          long long e_lo, int n0, int n1, int K, int warp, int lane, bool& staged,
-                                          const int8_t* __restrict__ a, const uint8_t* __restrict__ eg, long long e_hi,
-                                          uint8_t* eg_w, int8_t* a_w) {
+                                          long long e_lo, int n0, int n1, int K, int warp, int lane) {
   constexpr int CPB = kGemvMaxWpl / WPL > 4 ? 4 : kGemvMaxWpl / WPL;
   const int words = K / 32, G = K / kW4Group, col_bytes = K / 2;
   for (int t0 = 0;; t0 += CPB) {
@@ -139,29 +139,18 @@ __device__ __forceinline__ void gemv_warp(const uint8_t* __restrict__ wq, const 
       col[j] = n0 + warp + kGemvWarps * (t0 + j);
       any |= col[j] < n1;
     }
-    if (!any && staged) break;
+    if (!any) break;
     int acc[CPB];
 #pragma unroll
     for (int j = 0; j < CPB; ++j) acc[j] = 0;
     for (int seg = 0; seg < words; seg += 32 * WPL) {
       uint4 w[CPB][WPL];
 #pragma unroll
-      for (int j = 0; j < CPB; ++j)
+      for (int j = 0; j < CPB; ++j) {
+        const uint8_t* cw = wq + (long long)col[j] * col_bytes + (seg + lane) * 16;  // word seg + lane of column j
 #pragma unroll
-        for (int i = 0; i < WPL; ++i) {
-          const int wd = seg + i * 32 + lane;
-          if (col[j] < n1 && wd < words) w[j][i] = ld_stream16(wq + (long long)col[j] * col_bytes + wd * 16);
-        }
-      if (!staged) {
-        // the CTA's activations and exponents, behind the first weight loads; every thread of the
-        // CTA comes here exactly once (its first batch), then meets the others at the barrier
-        const int tid = warp * 32 + lane;
-        for (int i = tid; i < K / 16; i += kGemvThreads)
-          reinterpret_cast<int4*>(a_w)[i] = __ldg(reinterpret_cast<const int4*>(a) + i);
-        for (long long i = e_lo / 16 + tid; i < e_hi / 16; i += kGemvThreads)
-          reinterpret_cast<uint4*>(eg_w)[i - e_lo / 16] = __ldg(reinterpret_cast<const uint4*>(eg) + i);
-        __syncthreads();
-        staged = true;
+        for (int i = 0; i < WPL; ++i)
+          if (col[j] < n1 && seg + i * 32 + lane < words) w[j][i] = ld_stream16(cw + i * 512);
       }
 #pragma unroll
       for (int j = 0; j < CPB; ++j) {
@@ -173,7 +162,6 @@ __device__ __forceinline__ void gemv_warp(const uint8_t* __restrict__ wq, const 
         }
       }
     }
-    if (!any) break;
 #pragma unroll
     for (int j = 0; j < CPB; ++j) {
       int v = acc[j];
@@ -197,8 +185,20 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm)
   // the CTA's exponents [n0, n1) x G are one contiguous run of [N][K / 128]; the staged range starts
   // at the 16-byte boundary below it and ends at the one above (N * G is a multiple of 16: N is)
   const long long e_lo = ((long long)n0 * G) & ~15LL, e_hi = ((long long)n1 * G + 15) & ~15LL;
-  bool staged = false;
-  gemv_warp<WPL>(wq, shift, out, a_s, eg_s, e_lo, n0, n1, K, warp, lane, staged, a, eg, e_hi, eg_s, a_s);
+  grid_dep_launch();  // the next kernel may launch; it waits for this one before using any result
+  if (tid == 0) {
+    const long long w0 = (long long)n0 * (K / 2), w1 = (long long)n1 * (K / 2);  // 16-byte multiples
+    for (long long off = w0; off < w1; off += 65536)
+      bulk_prefetch_l2(wq + off, (uint32_t)(w1 - off < 65536 ? w1 - off : 65536));
+    bulk_prefetch_l2(eg + e_lo, (uint32_t)(e_hi - e_lo));
+  }
+  grid_dep_wait();  // the activations, and anything the previous kernel wrote, from here on
+  for (int i = tid; i < K / 16; i += kGemvThreads)
+    reinterpret_cast<int4*>(a_s)[i] = __ldg(reinterpret_cast<const int4*>(a) + i);
+  for (long long i = e_lo / 16 + tid; i < e_hi / 16; i += kGemvThreads)
+    reinterpret_cast<uint4*>(eg_s)[i - e_lo / 16] = __ldg(reinterpret_cast<const uint4*>(eg) + i);
+  __syncthreads();
+  gemv_warp<WPL>(wq, shift, out, a_s, eg_s, e_lo, n0, n1, K, warp, lane);
 }
 
 }  // namespace ixb
