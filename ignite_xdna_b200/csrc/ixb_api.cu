@@ -940,17 +940,6 @@ int plan_gemm(GemmLaunch& L, int M, int N, int K, std::string& err, int bsrc = G
   return 0;
 }
 
-// The GEMV with WPL 16-byte loads per lane per column batch (the limit is raised once per device
-// to what any plan may take: the first call's plan can be smaller).
-template <int WPL>
-int launch_gemv(const GemvPlan& g, const int8_t* a, const uint8_t* wq, const uint8_t* eg, const int32_t* shift,
-                int8_t* out, int N, int K, cudaStream_t st) {
-  if (int r = ensure_smem_limit(w4a8_gemv_kernel<WPL>, kSmemLimit / kGemvCtasPerSm - 1024)) return r;
-  IXB_CUDA(launch_dependent(w4a8_gemv_kernel<WPL>, dim3(g.grid), dim3(kGemvThreads), g.smem, st, true, a, wq, eg,
-                            shift, out, N, K));
-  return 0;
-}
-
 // Tensor map of the W4A8 weight image's packed part: uint8 [N][K/2], boxes of 64 bytes (128
 // values, one group) by BN rows, no swizzle; rows past N read as zero.
 int encode_w4(CUtensorMap* map, const void* base, int N, int K, int box_rows, std::string& err) {
@@ -2159,21 +2148,10 @@ int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   if (!a || !image || !shift || !out) return fail(IXB_ERR_INVALID, "null argument");
   if (int r = check_w4a8_shape(N, K)) return r;
   if (!aligned16(a) || !aligned16(image)) return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
-  const GemvPlan g = plan_gemv(N, K, sm_count());
-  if (g.smem > kSmemLimit / kGemvCtasPerSm - 1024)
-    return fail(IXB_ERR_INVALID, "GEMV activations and exponents do not fit shared memory");
-  const uint8_t* eg = image + (uint64_t)N * (K / 2);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (g.wpl) {
-    case 1: return launch_gemv<1>(g, a, image, eg, shift, out, N, K, st);
-    case 2: return launch_gemv<2>(g, a, image, eg, shift, out, N, K, st);
-    case 3: return launch_gemv<3>(g, a, image, eg, shift, out, N, K, st);
-    case 4: return launch_gemv<4>(g, a, image, eg, shift, out, N, K, st);
-    case 5: return launch_gemv<5>(g, a, image, eg, shift, out, N, K, st);
-    case 6: return launch_gemv<6>(g, a, image, eg, shift, out, N, K, st);
-    case 7: return launch_gemv<7>(g, a, image, eg, shift, out, N, K, st);
-    default: return launch_gemv<8>(g, a, image, eg, shift, out, N, K, st);
-  }
+  IXB_CUDA(launch_dependent(w4a8_gemv_kernel, dim3((unsigned)((N + kGemvWarps - 1) / kGemvWarps)), dim3(kGemvThreads), 0,
+                            static_cast<cudaStream_t>(stream), true, a, image, image + (uint64_t)N * (K / 2), shift, out, N,
+                            K));
+  return 0;
 }
 
 int ixb_gemm_plan_info(int M, int N, int K, int w4a8, int32_t* info, int n) {
