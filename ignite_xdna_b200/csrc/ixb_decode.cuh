@@ -18,12 +18,13 @@
 //   2. a stable two-pass radix sort (5-bit digits) of the candidates by score rank, the rank of a
 //      score being how many of the three heads' 768 table values exceed it (equal scores, equal
 //      ranks): score descending, then anchor ascending, the reference's stable order;
-//   3. exact greedy NMS as alternating steps: the next 32 still-alive candidates in order are
-//      resolved among themselves (any kept box before them has already been applied), then every
-//      later alive candidate is tested against the step's kept boxes by the whole block and dropped
-//      if one suppresses it. A candidate is dropped only by a kept box ahead of it, and one that
+//   3. exact greedy NMS as alternating steps over the list of still-alive candidates (in order,
+//      compacted in place after each step): its first 32 are resolved among themselves (any kept
+//      box before them has already been applied), then the rest are tested against the step's
+//      kept boxes by the whole block, each thread taking a run of consecutive entries, and dropped
+//      if one suppresses them. A candidate is dropped only by a kept box ahead of it, and one that
 //      reaches a step has survived every kept box ahead of it: the greedy result, in order, with a
-//      block barrier per ~32 kept boxes instead of per 32 candidates.
+//      few block barriers per ~32 kept boxes instead of per 32 candidates.
 #pragma once
 #include <cfloat>
 #include <cstdint>
@@ -150,6 +151,7 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
 constexpr int kDecodeWarps = kDecodeThreads / 32;
 constexpr int kScoreVals = 3 * 256;   // every score is one of the three heads' sigmoid values
 constexpr int kSidxTiny = 0x8000;     // candidate flag: its box area (double) is at most DBL_EPSILON
+constexpr int kDecodeMaxPer = (kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads;  // NMS entries per thread
 
 // Dynamic shared memory of the decode kernel (byte offsets).
 constexpr int kDsBox = 0;                                   // float4 [8400]: x0, y0, w, h
@@ -161,8 +163,7 @@ constexpr int kDsSig = kDsOrdB + 2 * kDecodeMaxAnchors;     // float [768]: sigm
 constexpr int kDsDiag = kDsSig + 4 * kScoreVals;            // float [768]: DFL exp diagonals
 constexpr int kDsLow = kDsDiag + 4 * kScoreVals;            // int32 [768]: sigmoid_low tables
 constexpr int kDsRank = kDsLow + 4 * kScoreVals;            // uint16 [768]: score ranks
-constexpr int kDsAlive = kDsRank + 2 * kScoreVals;          // uint32 [264]: NMS alive bits
-constexpr int kDsWc = kDsAlive + 4 * 264;                   // int [32][33]: per-warp counts
+constexpr int kDsWc = kDsRank + 2 * kScoreVals;             // int [32][33]: per-warp counts
 constexpr int kDsBytes = kDsWc + 4 * 32 * 33;
 
 // One stable counting pass over 32 buckets: dst[start(d) + earlier entries of digit d] = src[i].
@@ -275,13 +276,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   float* s_diag = reinterpret_cast<float*>(dsmem + kDsDiag);
   int32_t* s_low = reinterpret_cast<int32_t*>(dsmem + kDsLow);
   uint16_t* s_rank = reinterpret_cast<uint16_t*>(dsmem + kDsRank);
-  uint32_t* s_alive = reinterpret_cast<uint32_t*>(dsmem + kDsAlive);
   int(*s_wc)[33] = reinterpret_cast<int(*)[33]>(dsmem + kDsWc);
-  __shared__ int s_n, s_ntot, s_kept, s_nv, s_cn, s_nk, s_f;
+  __shared__ int s_n, s_ntot, s_kept, s_nv, s_nk, s_L;
+  __shared__ float4 s_nkbox[32];  // the current step's kept boxes, their classes and tiny flags
+  __shared__ int s_nkcls[32], s_nktiny[32];
   __shared__ int s_cnt[32], s_wcnt[kDecodeWarps];
   __shared__ int s_toe[3];
   __shared__ double s_maxc[kDecodeWarps];
-  __shared__ uint16_t s_chunk[32], s_newk[32];
+
   __shared__ unsigned s_mask[32];
 
   const int img = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -437,57 +439,29 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   const bool iou_nonneg = p.iou >= 0.f;  // false for NaN too
   const bool iou_unit = iou_nonneg && p.iou <= 1.f;
 
-  // 3. NMS. Scores strictly above conf are a prefix of the order.
+  // 3. NMS. Scores strictly above conf are a prefix of the order; s_ordA[0, L) then holds the
+  //    alive candidates in order, compacted in place after every step.
   if (tid == 0) s_nv = n;
   __syncthreads();
   for (int i = tid; i < n; i += kDecodeThreads)
     if (!(s_sig[s_sidx[s_ordA[i]] & 0x3FF] > p.conf)) atomicMin(&s_nv, i);
   __syncthreads();
   const int nv = s_nv;
-  const int nwords = (nv + 31) >> 5;
-  for (int w = tid; w < nwords; w += kDecodeThreads)
-    s_alive[w] = (w + 1) * 32 <= nv ? 0xffffffffu : ((1u << (nv & 31)) - 1u);
-  if (tid == 0) s_f = 0;
+  if (tid == 0) s_L = nv;
   __syncthreads();
   for (int step = 0; step < nv; ++step) {  // each step takes at least one alive candidate
-    // a. the next (up to) 32 alive positions at or after f, gathered by warp 0
-    if (warp == 0) {
-      const int f = s_f;
-      int got = 0, last = -1;
-      for (int w0 = f >> 5; got < 32 && w0 < nwords; w0 += 32) {
-        const int wi = w0 + lane;
-        uint32_t bits = wi < nwords ? s_alive[wi] : 0u;
-        if (wi == (f >> 5)) bits &= ~0u << (f & 31);
-        const int cnt = __popc(bits);
-        const int incl = warp_incl_scan(cnt, lane);
-        int idx = got + incl - cnt;
-        while (bits && idx < 32) {
-          const int b = __ffs(bits) - 1;
-          bits &= bits - 1;
-          s_chunk[idx] = (uint16_t)(wi * 32 + b);
-          last = max(last, wi * 32 + b);
-          ++idx;
-        }
-        got = min(32, got + __shfl_sync(0xffffffffu, incl, 31));
-      }
-      for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
-      if (lane == 0) {
-        s_cn = got;
-        s_f = last + 1;
-      }
-    }
-    __syncthreads();
-    const int cn = s_cn;
+    const int L = s_L;
+    const int cn = min(32, L);
     if (cn == 0) break;
-    // b. the chunk among itself: does earlier member b suppress member a (warp a, lane b)
+    // a. the chunk s_ordA[0, cn) among itself: does earlier member b suppress member a (warp a, lane b)
     if (warp < cn) {
-      const uint16_t ca = s_ordA[s_chunk[warp]];
+      const uint16_t ca = s_ordA[warp];
       const float4 ba = s_box[ca];
       const int cla = s_class[ca];
       const bool tiny_a = (s_sidx[ca] & kSidxTiny) != 0;
       bool m = false;
       if (lane < warp) {
-        const uint16_t cb = s_ordA[s_chunk[lane]];
+        const uint16_t cb = s_ordA[lane];
         m = pair_suppresses(ba, cla, tiny_a, s_box[cb], s_class[cb], (s_sidx[cb] & kSidxTiny) != 0, off_step, maxc,
                             p.iou, iou_nonneg, iou_unit);
       }
@@ -502,9 +476,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
       const int kept = s_kept;
       if ((keep >> lane) & 1u) {
         const int r = __popc(keep & ((1u << lane) - 1u));
-        const uint16_t c = s_ordA[s_chunk[lane]];
+        const uint16_t c = s_ordA[lane];
         s_ordB[kept + r] = c;
-        s_newk[r] = c;
+        s_nkbox[r] = s_box[c];
+        s_nkcls[r] = s_class[c];
+        s_nktiny[r] = (s_sidx[c] & kSidxTiny) != 0 ? 1 : 0;
       }
       if (lane == 0) {
         s_kept = kept + __popc(keep);
@@ -512,27 +488,44 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
       }
     }
     __syncthreads();
-    // c. every alive position after the chunk against the chunk's kept boxes; warps take whole
-    //    words of the alive bits
-    const int nk = s_nk, f2 = s_f;
-    for (int w = (f2 >> 5) + warp; w < nwords; w += kDecodeWarps) {
-      const int pos = w * 32 + lane;
-      bool alive = pos >= f2 && ((s_alive[w] >> lane) & 1u);
-      if (alive) {
-        const uint16_t ci = s_ordA[pos];
+    // b. the rest, s_ordA[cn, L), against the chunk's kept boxes: thread t takes E consecutive
+    //    entries (E <= 9), holds them in registers, and the survivors are written back in order
+    const int nk = s_nk, rest = L - cn;
+    const int E = (rest + kDecodeThreads - 1) / kDecodeThreads, i0 = cn + tid * E;
+    uint32_t cid[kDecodeMaxPer];
+    unsigned live = 0u;
+#pragma unroll
+    for (int e = 0; e < kDecodeMaxPer; ++e) {
+      cid[e] = 0u;
+      if (e < E && i0 + e < L) {
+        const uint16_t ci = s_ordA[i0 + e];
+        cid[e] = ci;
         const float4 bi = s_box[ci];
         const int cli = s_class[ci];
         const bool tiny_i = (s_sidx[ci] & kSidxTiny) != 0;
-        for (int j = 0; j < nk && alive; ++j) {
-          const uint16_t ck = s_newk[j];
-          if (pair_suppresses(bi, cli, tiny_i, s_box[ck], s_class[ck], (s_sidx[ck] & kSidxTiny) != 0, off_step, maxc,
-                              p.iou, iou_nonneg, iou_unit))
+        bool alive = true;
+        for (int j = 0; j < nk && alive; ++j)
+          if (pair_suppresses(bi, cli, tiny_i, s_nkbox[j], s_nkcls[j], s_nktiny[j] != 0, off_step, maxc, p.iou,
+                              iou_nonneg, iou_unit))
             alive = false;
-        }
+        if (alive) live |= 1u << e;
       }
-      const unsigned keepw = __ballot_sync(0xffffffffu, alive);
-      if (lane == 0) s_alive[w] = keepw;  // positions before f2 are behind every later gather
     }
+    const int cnt = __popc(live);
+    int incl = warp_incl_scan(cnt, lane);
+    if (lane == 31) s_wcnt[warp] = incl;
+    __syncthreads();  // every entry is read before any is overwritten
+    if (warp == 0) {
+      const int v = s_wcnt[lane];
+      const int wi = warp_incl_scan(v, lane);
+      s_wcnt[lane] = wi - v;
+      if (lane == 31) s_L = wi;
+    }
+    __syncthreads();
+    int dst = s_wcnt[warp] + incl - cnt;
+#pragma unroll
+    for (int e = 0; e < kDecodeMaxPer; ++e)
+      if ((live >> e) & 1u) s_ordA[dst++] = (uint16_t)cid[e];
     __syncthreads();
   }
 
