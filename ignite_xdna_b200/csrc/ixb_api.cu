@@ -1093,10 +1093,22 @@ int prepare_decode(const ixb_decode_desc& d, uint64_t egress_image_bytes, Decode
   return 0;
 }
 
+// One cluster of kDecodeCluster CTAs per image.
 int launch_decode(const DecodeParams& p, int batch, cudaStream_t st) {
   if (int r = ensure_smem_limit(yolo_decode_kernel, decode_smem_bytes())) return r;
-  yolo_decode_kernel<<<batch, kDecodeThreads, decode_smem_bytes(), st>>>(p);
-  IXB_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(batch * kDecodeCluster));
+  cfg.blockDim = dim3(kDecodeThreads);
+  cfg.dynamicSmemBytes = (size_t)decode_smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kDecodeCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  IXB_CUDA(cudaLaunchKernelEx(&cfg, yolo_decode_kernel, p));
   return 0;
 }
 

@@ -33,6 +33,7 @@
 namespace ixb {
 
 constexpr int kDecodeThreads = 1024;
+constexpr int kDecodeCluster = 2;  // CTAs per image (a thread-block cluster)
 constexpr int kDecodeMaxAnchors = 8400;
 constexpr int kDfl = 16;
 
@@ -151,7 +152,7 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
 constexpr int kDecodeWarps = kDecodeThreads / 32;
 constexpr int kScoreVals = 3 * 256;   // every score is one of the three heads' sigmoid values
 constexpr int kSidxTiny = 0x8000;     // candidate flag: its box area (double) is at most DBL_EPSILON
-constexpr int kDecodeMaxPer = (kDecodeMaxAnchors + kDecodeThreads - 1) / kDecodeThreads;  // NMS entries per thread
+constexpr int kDecodeMaxPer = (kDecodeMaxAnchors / kDecodeCluster + kDecodeThreads) / kDecodeThreads;  // NMS entries per thread
 
 // Dynamic shared memory of the decode kernel (byte offsets).
 constexpr int kDsBox = 0;                                   // float4 [8400]: x0, y0, w, h
@@ -277,7 +278,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   int32_t* s_low = reinterpret_cast<int32_t*>(dsmem + kDsLow);
   uint16_t* s_rank = reinterpret_cast<uint16_t*>(dsmem + kDsRank);
   int(*s_wc)[33] = reinterpret_cast<int(*)[33]>(dsmem + kDsWc);
-  __shared__ int s_n, s_ntot, s_kept, s_nv, s_nk, s_L;
+  __shared__ int s_n, s_kept, s_nv, s_nk, s_L;
+  __shared__ int s_pc[2][kDecodeCluster];  // per-rank counts traded each round (double-buffered by parity)
   __shared__ float4 s_nkbox[32];  // the current step's kept boxes, their classes and tiny flags
   __shared__ int s_nkcls[32], s_nktiny[32];
   __shared__ int s_cnt[32], s_wcnt[kDecodeWarps];
@@ -286,7 +288,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
 
   __shared__ unsigned s_mask[32];
 
-  const int img = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int img = blockIdx.x / kDecodeCluster, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t crank = cluster_rank(), cpeer = crank ^ 1u;
   const int8_t* eg = p.egress + (long long)img * p.egress_image_bytes;
   const float pad_top = p.letterbox[3 * img], pad_left = p.letterbox[3 * img + 1], lscale = p.letterbox[3 * img + 2];
   const int total = p.head[0].anchors + p.head[1].anchors + p.head[2].anchors;
@@ -331,9 +334,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   }
   __syncthreads();
 
-  // 1. candidates in anchor order: prune, class score, DFL, box
-  for (int base = 0; base < total; base += kDecodeThreads) {
-    const int A = base + tid;
+  // 1. candidates in anchor order: prune, class score, DFL, box. The image's two CTAs take
+  //    alternate 1024-anchor tiles; after each pair they trade counts, and each writes its
+  //    candidates into both CTAs' arrays at their places in anchor order.
+  int it = 0;
+  for (int base = 0; base < total; base += kDecodeThreads * kDecodeCluster, ++it) {
+    const int A = base + (int)crank * kDecodeThreads + tid;
     bool pass = false;
     float4 bx = make_float4(0.f, 0.f, 0.f, 0.f);
     int sidx = 0, best_c = 0;
@@ -397,23 +403,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
     if (warp == 0) {
       const int v = s_wcnt[lane];
       const int incl = warp_incl_scan(v, lane);
-      s_wcnt[lane] = s_n + incl - v;
-      if (lane == 31) s_ntot = s_n + incl;
+      s_wcnt[lane] = incl - v;
+      if (lane == 31) {
+        s_pc[it & 1][crank] = incl;
+        st_cluster_u32(cluster_addr(&s_pc[it & 1][crank], cpeer), (uint32_t)incl);
+      }
     }
-    __syncthreads();
+    cluster_sync();  // both tiles' counts in both CTAs
+    const int c0 = s_pc[it & 1][0], c1 = s_pc[it & 1][1];
     if (pass) {
-      const int slot = s_wcnt[warp] + __popc(bal & ((1u << lane) - 1u));
+      const int slot = s_n + (crank ? c0 : 0) + s_wcnt[warp] + __popc(bal & ((1u << lane) - 1u));
       s_box[slot] = bx;
       s_sidx[slot] = (uint16_t)sidx;
       s_class[slot] = (uint8_t)best_c;
+      st_cluster_f4(cluster_addr(&s_box[slot], cpeer), bx);
+      st_cluster_u16(cluster_addr(&s_sidx[slot], cpeer), (uint32_t)sidx);
+      st_cluster_u8(cluster_addr(&s_class[slot], cpeer), (uint32_t)best_c);
     }
     __syncthreads();
-    if (tid == 0) s_n = s_ntot;
+    if (tid == 0) s_n += c0 + c1;
     __syncthreads();
   }
+  cluster_sync();  // every candidate, written by either CTA, is in both
   const int n = s_n;
   if (n == 0) {
-    if (tid == 0) p.out_count[img] = 0;
+    if (tid == 0 && crank == 0) p.out_count[img] = 0;
     return;
   }
 
@@ -488,16 +502,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
       }
     }
     __syncthreads();
-    // b. the rest, s_ordA[cn, L), against the chunk's kept boxes: thread t takes E consecutive
-    //    entries (E <= 9), holds them in registers, and the survivors are written back in order
-    const int nk = s_nk, rest = L - cn;
-    const int E = (rest + kDecodeThreads - 1) / kDecodeThreads, i0 = cn + tid * E;
+    // b. the rest, s_ordA[cn, L), against the chunk's kept boxes: the image's two CTAs take one
+    //    half each, thread t a run of E consecutive entries of it (E <= 5) held in registers; the
+    //    survivors are written back in order into both CTAs' lists
+    const int nk = s_nk, rest = L - cn, half = (rest + 1) / 2;
+    const int lo = cn + (crank ? half : 0), hi = crank ? L : cn + half;
+    const int E = (hi - lo + kDecodeThreads - 1) / kDecodeThreads, i0 = lo + tid * E;
     uint32_t cid[kDecodeMaxPer];
     unsigned live = 0u;
 #pragma unroll
     for (int e = 0; e < kDecodeMaxPer; ++e) {
       cid[e] = 0u;
-      if (e < E && i0 + e < L) {
+      if (e < E && i0 + e < hi) {
         const uint16_t ci = s_ordA[i0 + e];
         cid[e] = ci;
         const float4 bi = s_box[ci];
@@ -514,23 +530,33 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
     const int cnt = __popc(live);
     int incl = warp_incl_scan(cnt, lane);
     if (lane == 31) s_wcnt[warp] = incl;
-    __syncthreads();  // every entry is read before any is overwritten
+    __syncthreads();
     if (warp == 0) {
       const int v = s_wcnt[lane];
       const int wi = warp_incl_scan(v, lane);
       s_wcnt[lane] = wi - v;
-      if (lane == 31) s_L = wi;
+      if (lane == 31) {
+        s_pc[step & 1][crank] = wi;
+        st_cluster_u32(cluster_addr(&s_pc[step & 1][crank], cpeer), (uint32_t)wi);
+      }
     }
-    __syncthreads();
-    int dst = s_wcnt[warp] + incl - cnt;
+    cluster_sync();  // both halves' counts here, and every entry of both CTAs read before any is overwritten
+    const int t0 = s_pc[step & 1][0], t1 = s_pc[step & 1][1];
+    int dst = (crank ? t0 : 0) + s_wcnt[warp] + incl - cnt;
 #pragma unroll
     for (int e = 0; e < kDecodeMaxPer; ++e)
-      if ((live >> e) & 1u) s_ordA[dst++] = (uint16_t)cid[e];
-    __syncthreads();
+      if ((live >> e) & 1u) {
+        s_ordA[dst] = (uint16_t)cid[e];
+        st_cluster_u16(cluster_addr(&s_ordA[dst], cpeer), cid[e]);
+        ++dst;
+      }
+    if (tid == 0) s_L = t0 + t1;
+    cluster_sync();  // the new list in both CTAs
   }
 
   // 4. detections in kept order
   const int kept = s_kept;
+  if (crank != 0) return;  // both CTAs hold the same result
   if (kept > p.capacity) {
     if (tid == 0) p.out_count[img] = -3;
     return;
