@@ -686,6 +686,63 @@ def run_gemm_workloads(args):
     return 0
 
 
+def run_decode_workload(args):
+    """The detection stage alone: decode + NMS (ixb_decode_yolo) of `batch` images' int8 heads, the
+    network's egress for seeded uniform images, resident on the device (77 MB at batch 64, in L2
+    between launches), at two threshold settings. One JSON line: ms per batch and images/s, with a
+    SHA-256 of every image's detections so builds can be compared."""
+    import ctypes as C
+    import hashlib
+    import numpy as np
+    import torch
+    from ignite_xdna_b200 import InferenceSession, random_images
+    from ignite_xdna_b200 import _lib as L
+    from ignite_xdna_b200.decode import GpuDecoder
+    B = args.batch
+    sess = InferenceSession.from_spec(args.model, imgsz=args.imgsz, max_batch=B)
+    sess.stage_input(random_images(B, args.imgsz, seed=100))
+    lib = sess.lib
+    L.check(lib.ixb_session_run(sess._h, None, B, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
+    L.check(lib.ixb_session_wait(sess._h, 60000))
+    eg = sess.arena[sess.plan.egress_offset:sess.plan.egress_offset + B * sess.out_bytes]
+    rows = []
+    for conf, iou in ((0.25, 0.5), (0.5, 0.7)):
+        dec = GpuDecoder(sess.layout, args.imgsz, sess.device, conf=conf, iou=iou)
+        cap = dec.total_anchors
+        lb = torch.zeros((B, 3), dtype=torch.float32, device=sess.device)
+        lb[:, 2] = 1.0
+        boxes = torch.empty((B, cap, 4), dtype=torch.float32, device=sess.device)
+        scores = torch.empty((B, cap), dtype=torch.float32, device=sess.device)
+        classes = torch.empty((B, cap), dtype=torch.int32, device=sess.device)
+        counts = torch.empty(B, dtype=torch.int32, device=sess.device)
+        fn = lambda: L.check(lib.ixb_decode_yolo(  # noqa: E731
+            C.byref(dec.desc), C.c_void_p(eg.data_ptr()), B, dec.layout.image_bytes, C.c_void_p(lb.data_ptr()), cap,
+            C.c_void_p(boxes.data_ptr()), C.c_void_p(scores.data_ptr()), C.c_void_p(classes.data_ptr()),
+            C.c_void_p(counts.data_ptr()), None))
+        ms = _time_events(fn, args.steps, args.warmup)
+        n = counts.cpu().numpy()
+        h = hashlib.sha256()
+        for i in range(B):
+            k = int(n[i])
+            h.update(np.int32(k).tobytes())
+            if k > 0:
+                for t in (boxes[i, :k], scores[i, :k], classes[i, :k]):
+                    h.update(t.cpu().numpy().tobytes())
+        rows.append({"conf": conf, "iou": iou, "ms_per_batch": round(ms, 4), "images_s": round(B / (ms * 1e-3), 1),
+                     "kept_mean": round(float(n.mean()), 1), "candidates_per_image": cap,
+                     "detections_sha256": h.hexdigest()[:16]})
+    sess.close()
+    line = {"metric": "YOLOv8 detect decode + NMS images/s (GPU, heads resident)", "value": rows[0]["images_s"],
+            "unit": "images/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 heads -> float32 (reference order)",
+            "data": "synthetic (the network's heads for seeded uniform images)",
+            "config": {"workload": f"decode {args.model} {args.imgsz} batch {B}",
+                       "l2": "the 77 MB of heads stay in L2 between launches (the decode reads each byte once)"},
+            "rows": rows, "gpu_launches": 2 * args.steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -698,13 +755,15 @@ def main():
     ap.add_argument("--depth", type=int, default=4,
                     help="batches in flight in the e2e legs (the session's staging/egress slots, 1..4)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", default="yolo", choices=["yolo", "i8gemm", "w4a8"],
-                    help="yolo: the whole-network benchmark; i8gemm / w4a8: the kernel microbenchmarks")
+    ap.add_argument("--workload", default="yolo", choices=["yolo", "i8gemm", "w4a8", "decode"],
+                    help="yolo: the whole-network benchmark; i8gemm / w4a8 / decode: the kernel microbenchmarks")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "decode":
+        return run_decode_workload(args)
     if args.workload != "yolo":
         return run_gemm_workloads(args)
     return run_gpu(args)
