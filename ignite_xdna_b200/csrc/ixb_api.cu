@@ -1581,7 +1581,7 @@ int ixb_session_launches(ixb_session* s, int batch) {
 int ixb_session_run(ixb_session* s, const uint8_t* images, int batch, int8_t* egress, int flags) {
   if (!s) return fail(IXB_ERR_INVALID, "null session");
   if (batch < 1 || batch > s->plan.max_batch) return fail(IXB_ERR_INVALID, "batch outside [1, max_batch]");
-  if (s->pending) return fail(IXB_ERR_INVALID, "the previous asynchronous run was not waited for");
+  // a run while an asynchronous one is pending queues behind it on the same stream; the wait covers both
   if (s->any_busy()) return fail(IXB_ERR_INVALID, "submitted runs are still in flight");
   const bool in_store = (flags & IXB_IN_STORE) != 0;
   if (!(flags & IXB_IN_DEVICE) && !in_store && !images) return fail(IXB_ERR_INVALID, "null images");

@@ -96,9 +96,9 @@ __device__ __forceinline__ uint32_t sra8_nib(uint32_t v, uint32_t e, uint32_t hm
 // loads all its items of the stage (at most 8) and their exponents, then converts and stores
 // them, so the shared-memory latencies overlap instead of adding up item by item. The tile's
 // exponents come by bulk copy from the TMA producer into one of two buffers (eg_full / eg_empty).
-// UT threads unpack: the B warps, joined by the epilogue warps when every CTA has one tile (their
-// drain then waits for the whole K loop anyway).
-constexpr int kW4MaxItems = 8;  // 8 * BN items per stage over at least kW4Warps * 32 threads, BN <= 256
+// UT = kW4Warps * 32 threads unpack. (Letting the idle epilogue warps of a one-tile-per-CTA run
+// join them measured 3-7 % slower: the stage pipeline, not the unpack rate, bounds the kernel.)
+constexpr int kW4MaxItems = 8;  // 8 * BN items per stage over kW4Warps * 32 threads, BN <= 256
 __device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, uint64_t* full, uint64_t* bfull,
                                            uint64_t* eg_full, uint64_t* eg_empty, int ut, int UT) {
   const int S = p.stages, G = p.K / 128;
@@ -161,9 +161,6 @@ __device__ __forceinline__ void produce_w4(const GemmParams& p, uint8_t* smem, u
 template <int EPI, int BSRC>
 __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const __grid_constant__ GemmParams p) {
   constexpr int PW = EPI, MW = EPI + 1, UW0 = EPI + 2;
-  // W4A8 with one tile per CTA: the epilogue warps unpack too until the K loop ends
-  const bool helpers = BSRC == GEMM_B_W4 && p.m_tiles * p.n_tiles <= (int)gridDim.x;
-  const int unpack_warps = kW4Warps + (helpers ? EPI : 0);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -187,7 +184,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&bfull[s], unpack_warps);
+      mbar_init(&bfull[s], kW4Warps);
     }
     for (int b = 0; b < p.nacc; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -196,7 +193,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     mbar_init(done, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&eg_full[b], 1);
-      mbar_init(&eg_empty[b], unpack_warps);
+      mbar_init(&eg_empty[b], kW4Warps);
     }
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&p.ta) : "memory");
@@ -247,7 +244,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     }
   } else if (BSRC == GEMM_B_W4 && warp >= UW0) {
     // ------------------------------------------------------------ int4 -> int8 B producers
-    produce_w4(p, smem, full, bfull, eg_full, eg_empty, tid - UW0 * 32, unpack_warps * 32);
+    produce_w4(p, smem, full, bfull, eg_full, eg_empty, tid - UW0 * 32, kW4Warps * 32);
   } else if (warp == MW) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -294,7 +291,6 @@ __global__ void __launch_bounds__(gemm_threads(EPI, BSRC), 1) gemm_kernel(const 
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    if (helpers) produce_w4(p, smem, full, bfull, eg_full, eg_empty, kW4Warps * 32 + tid, unpack_warps * 32);
     constexpr int NG = EPI / 4;
     const int q = warp & 3, g = warp >> 2;
     const int nch = p.bn / 16;

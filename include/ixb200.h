@@ -57,7 +57,9 @@ extern "C" {
 /* ixb_session_run flags */
 #define IXB_IN_DEVICE 1     /* images is a device pointer; NULL: the images already sit in the staging buffer */
 #define IXB_OUT_DEVICE 2    /* egress is a device pointer; NULL: leave the heads in the session's egress buffer */
-#define IXB_ASYNC 4         /* return after enqueueing; ixb_session_wait completes the call */
+#define IXB_ASYNC 4         /* return after enqueueing; ixb_session_wait completes the call. Runs
+                               stack: a run while one is pending queues behind it on the session's
+                               stream, and the wait completes them all (the time is the last run's) */
 #define IXB_NO_GRAPH 8      /* launch layer by layer instead of replaying the captured graph */
 #define IXB_IN_STORE 16     /* the stem's input already holds the images (ixb_session_letterbox): no ingress */
 

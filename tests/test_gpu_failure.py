@@ -34,6 +34,19 @@ def test_host_wait_times_out_then_drains(big):
     assert np.array_equal(heads[5], big.run(imgs[5:6])[0])
 
 
+def test_async_runs_stack(big):
+    """Asynchronous runs queue behind a pending one on the session's stream; one wait completes
+    them all, and the heads are a plain run's (the session's loop the bench times)."""
+    imgs = random_images(64, 640, seed=13)
+    big.stage_input(imgs)
+    lib = big.lib
+    for _ in range(3):
+        L.check(lib.ixb_session_run(big._h, None, 64, None, L.IN_DEVICE | L.OUT_DEVICE | L.ASYNC))
+    assert lib.ixb_session_wait(big._h, 60000) == 0
+    heads = big.read_heads(batch=64).copy()
+    assert np.array_equal(heads[17], big.run(imgs[17:18])[0])
+
+
 def test_ticket_wait_times_out_then_drains(big):
     imgs = random_images(64, 640, seed=12)
     h = big.run_async(imgs)
