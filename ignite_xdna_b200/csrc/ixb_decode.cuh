@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
   __shared__ float4 s_nkbox[32];  // the current step's kept boxes, their classes and tiny flags
   __shared__ int s_nkcls[32], s_nktiny[32];
   __shared__ int s_cnt[32], s_wcnt[kDecodeWarps];
-  __shared__ int s_toe[3];
+  __shared__ int s_toe[3], s_toe_half[kDecodeCluster][3];
   __shared__ double s_maxc[kDecodeWarps];
 
   __shared__ unsigned s_mask[32];
@@ -305,7 +305,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
     s_n = 0;
     s_kept = 0;
   }
-  __syncthreads();
+  cluster_sync();  // both CTAs of the cluster are running before either touches the other's shared memory
+  // The image's two CTAs split the checks and the ranks (rows and values of their own parity) and
+  // trade the results.
   for (int h = 0; h < 3; ++h) {
     // the table is used at (q_max, q) with q <= q_max only: there it must equal the diagonal
     // (16-byte loads of four columns; the caller's tables are 16-byte aligned)
@@ -313,10 +315,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
     const float* dg = s_diag + h * 256 + 255;
     bool same = true;
 #pragma unroll 4
-    for (int e = tid; e < 256 * 64; e += kDecodeThreads) {
-      const int r = e >> 6, c = (e & 63) * 4;
+    for (int e = tid; e < 128 * 64; e += kDecodeThreads) {
+      const int r = 2 * (e >> 6) + (int)crank, c = (e & 63) * 4;
       if (c <= r) {
-        const float4 v = __ldg(t4 + e);
+        const float4 v = __ldg(t4 + r * 64 + (e & 63));
         same &= __float_as_uint(v.x) == __float_as_uint(dg[c - r]);
         same &= c + 1 > r || __float_as_uint(v.y) == __float_as_uint(dg[c + 1 - r]);
         same &= c + 2 > r || __float_as_uint(v.z) == __float_as_uint(dg[c + 2 - r]);
@@ -324,14 +326,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
       }
     }
     same = __syncthreads_and(same) != 0;
-    if (tid == 0) s_toe[h] = same ? 1 : 0;
+    if (tid == 0) {
+      s_toe_half[crank][h] = same ? 1 : 0;
+      st_cluster_u32(cluster_addr(&s_toe_half[crank][h], cpeer), same ? 1u : 0u);
+    }
   }
-  for (int i = tid; i < kScoreVals; i += kDecodeThreads) {
+  for (int i = 2 * tid + (int)crank; i < kScoreVals; i += 2 * kDecodeThreads) {
     const float v = s_sig[i];
     int r = 0;
     for (int j = 0; j < kScoreVals; ++j) r += s_sig[j] > v ? 1 : 0;
     s_rank[i] = (uint16_t)r;
+    st_cluster_u16(cluster_addr(&s_rank[i], cpeer), (uint32_t)r);
   }
+  cluster_sync();  // both halves of the checks and of the ranks in both CTAs
+  if (tid < 3) s_toe[tid] = s_toe_half[0][tid] & s_toe_half[1][tid];
   __syncthreads();
 
   // 1. candidates in anchor order: prune, class score, DFL, box. The image's two CTAs take
