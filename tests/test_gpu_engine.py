@@ -213,9 +213,17 @@ def test_profile_reports_every_op():
     conv = [t for t in tr if t is not None]
     assert len(conv) == len(sess.plan.convs)
     assert all(0 <= s <= r <= e for s, r, e in conv)
-    ends = [e for _, _, e in conv]
-    assert all(b >= a for a, b in zip(ends, ends[1:]))   # serial order: each op ends after the last
-    assert ends[-1] < 10_000                               # the whole run within 10 ms
+    groups = []   # an op flagged OP_WITH_PREV runs beside the ops before it (a branch group)
+    for (kind, _), t in zip(sess.plan.ops, tr):
+        if not (kind & L.OP_WITH_PREV) or not groups:
+            groups.append([])
+        if t is not None:
+            groups[-1].append(t)
+    last = 0
+    for g in filter(None, groups):   # a group starts after the whole group before it has ended
+        assert min(e for _, _, e in g) >= last
+        last = max(e for _, _, e in g)
+    assert last < 10_000                                   # the whole run within 10 ms
     a = sess.run(random_images(2, 128, seed=5))            # the session's own graph is untouched
     assert np.array_equal(a, O.run_batch_egress(sess.ir, random_images(2, 128, seed=5)))
     sess.close()
