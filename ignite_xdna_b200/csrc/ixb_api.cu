@@ -2160,9 +2160,14 @@ int ixb_w4a8_gemv(const int8_t* a, const uint8_t* image, const int32_t* shift, i
   if (!a || !image || !shift || !out) return fail(IXB_ERR_INVALID, "null argument");
   if (int r = check_w4a8_shape(N, K)) return r;
   if (!aligned16(a) || !aligned16(image)) return fail(IXB_ERR_INVALID, "W4A8 operands must be 16-byte aligned");
-  IXB_CUDA(launch_dependent(w4a8_gemv_kernel, dim3((unsigned)((N + kGemvWarps - 1) / kGemvWarps)), dim3(kGemvThreads), 0,
-                            static_cast<cudaStream_t>(stream), true, a, image, image + (uint64_t)N * (K / 2), shift, out, N,
-                            K));
+  const uint8_t* eg = image + (uint64_t)N * (K / 2);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K <= 4 * 1024)  // at most four 16-byte loads per lane and column: two columns per warp
+    IXB_CUDA(launch_dependent(w4a8_gemv_kernel<2>, dim3((unsigned)((N + 2 * kGemvWarps - 1) / (2 * kGemvWarps))),
+                              dim3(kGemvThreads), 0, st, true, a, image, eg, shift, out, N, K));
+  else
+    IXB_CUDA(launch_dependent(w4a8_gemv_kernel<1>, dim3((unsigned)((N + kGemvWarps - 1) / kGemvWarps)), dim3(kGemvThreads),
+                              0, st, true, a, image, eg, shift, out, N, K));
   return 0;
 }
 

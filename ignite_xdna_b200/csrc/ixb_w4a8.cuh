@@ -65,8 +65,8 @@ __device__ __forceinline__ uint32_t w4_lo16(uint32_t x) { return (x << 4) & 0xF0
 __device__ __forceinline__ uint32_t w4_hi16(uint32_t x) { return x & 0xF0F0F0F0u; }
 
 // ---------------------------------------------------------------- GEMV (M = 1)
-// Weight-streaming GEMV: one warp per output column, eight columns per CTA (many small CTAs, up
-// to eight resident per SM, so DRAM latency hides behind other CTAs' loads); a column's K words
+// Weight-streaming GEMV: a warp per output column (or two short columns), eight warps per CTA
+// (many small CTAs, four resident per SM, so DRAM latency hides behind other CTAs' loads); a column's K words
 // (16 bytes = 32 values) are spread over the lanes, and all of a lane's loads of a batch (up to 8)
 // are in flight before the first is used. Each word is 8 dp4a on 16 * w and the activations (read
 // through L1), shifted by the group's exponent, and a warp reduction ends the column with its SRS.
@@ -87,51 +87,71 @@ __device__ __forceinline__ uint4 ld_stream16(const uint8_t* p) {
   return v;
 }
 
+// CPW columns per warp: with K <= 4096 a column is at most four 16-byte loads per lane, so a warp
+// takes two columns (kGemvWarps apart) and keeps eight loads in flight; the activations it reads
+// once serve both. Longer columns take one column per warp and batches of eight loads.
+template <int CPW>
 __global__ void __launch_bounds__(kGemvThreads, 4)
     w4a8_gemv_kernel(const int8_t* __restrict__ a, const uint8_t* __restrict__ wq, const uint8_t* __restrict__ eg,
                      const int32_t* __restrict__ shift, int8_t* __restrict__ out, int N, int K) {
-  const int n0 = blockIdx.x * kGemvWarps, n = n0 + (threadIdx.x >> 5);
+  constexpr int B = kGemvBatch / CPW;  // loads per column per batch
+  const int n0 = blockIdx.x * kGemvWarps * CPW, warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int col_bytes = K / 2, G = K / kW4Group;
   grid_dep_launch();  // the next kernel may launch; it waits for this one before using any result
   if (threadIdx.x == 0) {
-    const int cols = min(kGemvWarps, N - n0);  // the CTA's columns: one contiguous run of each table
+    const int cols = min(kGemvWarps * CPW, N - n0);  // the CTA's columns: one contiguous run of each table
     bulk_prefetch_l2(wq + (long long)n0 * col_bytes, (uint32_t)(cols * col_bytes));
     const long long e_lo = ((long long)n0 * G) & ~15LL, e_hi = ((long long)(n0 + cols) * G + 15) & ~15LL;
     bulk_prefetch_l2(eg + e_lo, (uint32_t)(e_hi - e_lo));
   }
   grid_dep_wait();  // the activations, and anything the previous kernel wrote, from here on
-  if (n >= N) return;
-  const uint8_t* row = wq + (long long)n * col_bytes;
-  const uint8_t* erow = eg + (long long)n * G;
-  int acc = 0;
-  for (int k0 = lane * 32; k0 < K; k0 += 1024 * kGemvBatch) {
-    uint4 w[kGemvBatch];
+  int nc[CPW], acc[CPW];
+  bool ok[CPW];
 #pragma unroll
-    for (int j = 0; j < kGemvBatch; ++j)
-      if (k0 + j * 1024 < K) w[j] = ld_stream16(row + (k0 + j * 1024) / 2);
+  for (int c = 0; c < CPW; ++c) {
+    nc[c] = n0 + c * kGemvWarps + warp;
+    ok[c] = nc[c] < N;  // warp-uniform
+    acc[c] = 0;
+  }
+  if (!ok[0]) return;
+  for (int k0 = lane * 32; k0 < K; k0 += 1024 * B) {
+    uint4 w[CPW][B];
 #pragma unroll
-    for (int j = 0; j < kGemvBatch; ++j) {
+    for (int c = 0; c < CPW; ++c)
+#pragma unroll
+      for (int j = 0; j < B; ++j)
+        if (ok[c] && k0 + j * 1024 < K) w[c][j] = ld_stream16(wq + (long long)nc[c] * col_bytes + (k0 + j * 1024) / 2);
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
       const int k = k0 + j * 1024;
       if (k < K) {
         const int4 a0 = __ldg(reinterpret_cast<const int4*>(a + k));
         const int4 a1 = __ldg(reinterpret_cast<const int4*>(a + k) + 1);
-        int pr = 0;
-        pr = __dp4a((int)w4_lo16(w[j].x), a0.x, pr);
-        pr = __dp4a((int)w4_hi16(w[j].x), a0.y, pr);
-        pr = __dp4a((int)w4_lo16(w[j].y), a0.z, pr);
-        pr = __dp4a((int)w4_hi16(w[j].y), a0.w, pr);
-        pr = __dp4a((int)w4_lo16(w[j].z), a1.x, pr);
-        pr = __dp4a((int)w4_hi16(w[j].z), a1.y, pr);
-        pr = __dp4a((int)w4_lo16(w[j].w), a1.z, pr);
-        pr = __dp4a((int)w4_hi16(w[j].w), a1.w, pr);
-        acc += pr >> __ldg(erow + (k >> 7));  // pr = 16 * sum a * w, a multiple of 16: exact
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          if (!ok[c]) continue;
+          int pr = 0;
+          pr = __dp4a((int)w4_lo16(w[c][j].x), a0.x, pr);
+          pr = __dp4a((int)w4_hi16(w[c][j].x), a0.y, pr);
+          pr = __dp4a((int)w4_lo16(w[c][j].y), a0.z, pr);
+          pr = __dp4a((int)w4_hi16(w[c][j].y), a0.w, pr);
+          pr = __dp4a((int)w4_lo16(w[c][j].z), a1.x, pr);
+          pr = __dp4a((int)w4_hi16(w[c][j].z), a1.y, pr);
+          pr = __dp4a((int)w4_lo16(w[c][j].w), a1.z, pr);
+          pr = __dp4a((int)w4_hi16(w[c][j].w), a1.w, pr);
+          acc[c] += pr >> __ldg(eg + (long long)nc[c] * G + (k >> 7));  // pr = 16 * sum a * w: exact
+        }
       }
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) out[n] = (int8_t)clamp_i8(rne_shift(acc, __ldg(shift + n)));
+  for (int c = 0; c < CPW; ++c) {
+    int v = acc[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && ok[c]) out[nc[c]] = (int8_t)clamp_i8(rne_shift(v, __ldg(shift + nc[c])));
+  }
 }
 
 }  // namespace ixb
