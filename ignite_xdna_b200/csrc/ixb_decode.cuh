@@ -357,9 +357,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
       const int n = hd.anchors, a = A - hd.anchor_offset;
       const int8_t* box = eg + hd.box_off;
       const int8_t* cls = eg + hd.cls_off;
-      int q_max = -128;
+      int q_max = -128, c_max = 0;  // the maximum byte and the first class holding it
 #pragma unroll 16
-      for (int c = 0; c < p.num_classes; ++c) q_max = max(q_max, (int)cls[(long long)c * n + a]);
+      for (int c = 0; c < p.num_classes; ++c) {
+        const int q = cls[(long long)c * n + a];
+        if (q > q_max) {
+          q_max = q;
+          c_max = c;
+        }
+      }
       if (q_max > hd.qi) {
         const float* sig = s_sig + h * 256 + 128;
         float best;
@@ -368,8 +374,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
           best = sig[q_max];
           pass = best >= p.conf;
           if (pass) {
+            // the first class whose byte reaches lo, the lowest byte with q_max's sigmoid value:
+            // c_max when no smaller byte shares that value (the usual case, without a walk
+            // through the class bytes)
             const int lo = s_low[h * 256 + q_max + 128];
-            while (best_c < p.num_classes - 1 && (int)cls[(long long)best_c * n + a] < lo) ++best_c;
+            if (lo == q_max) {
+              best_c = c_max;
+            } else {
+              while (best_c < p.num_classes - 1 && (int)cls[(long long)best_c * n + a] < lo) ++best_c;
+            }
           }
         } else {
           q_best = cls[a];
