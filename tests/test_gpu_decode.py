@@ -58,3 +58,51 @@ def test_gpu_decode_matches_reference_at_640(conf, iou):
         assert np.array_equal(_bits(det[i].boxes), _bits(b)) and np.array_equal(_bits(det[i].scores), _bits(s))
         assert np.array_equal(det[i].classes, c)
     sess.close()
+
+
+def test_gpu_decode_class_pick_with_saturated_sigmoid():
+    """Class heads read at scale 0.5: the float32 sigmoid is 1.0 from q = 34 up, so many anchors
+    have an earlier class whose byte is below the maximum but shares its score. The numpy argmax
+    of the reference picks that earlier class; the kernel's walk through the class bytes must
+    too (the maximum's first class alone would differ)."""
+    import dataclasses
+    import ref_decode
+    lib = ref_decode.load()
+    if lib is None:
+        pytest.skip("oracle/_ref/decode_native.so is not built")
+    import torch
+    sess = InferenceSession.from_spec("yolov8n", imgsz=640, max_batch=2)
+    imgs = random_images(2, 640, seed=21)
+    raw = np.array(sess.run(imgs))
+    cls_names = {c for _, c in D.HEAD_PAIRS}
+    layout = dataclasses.replace(sess.layout, heads=tuple(
+        dataclasses.replace(h, scale=0.5) if h.name in cls_names else h for h in sess.layout.heads))
+    conf, iou = 0.9, 0.6
+    # the case this test exists for occurs: an anchor whose first class reaching the saturated
+    # score comes before the first class holding the maximum byte
+    views = layout.unpack(raw)
+    sig = D.sigmoid_table(0.5, 0)
+    low = D.sigmoid_low_table(sig)
+    ties = 0
+    for _, cname in D.HEAD_PAIRS:
+        q = views[cname][0].reshape(views[cname].shape[1], -1).astype(np.int32)
+        qmax = q.max(axis=0)
+        lo = low[qmax + 128]
+        ties += int(np.sum((q >= lo).argmax(axis=0) != q.argmax(axis=0)))
+    assert ties > 0
+    dec = D.GpuDecoder(layout, 640, torch.device("cuda"), conf=conf, iou=iou)
+    egress = sess.arena[sess.plan.egress_offset:sess.plan.egress_offset + 2 * sess.out_bytes]
+    lb = np.array([[0, 0, 1], [0, 0, 1]], dtype=np.float32)
+    det = dec(egress, 2, letterbox=lb)
+    anchors = D.anchor_grid(640)
+    tables = []
+    for bname, cname in D.HEAD_PAIRS:
+        bs, cs = layout.spec(bname), layout.spec(cname)
+        s = D.sigmoid_table(cs.scale, 0)
+        tables.append((D.dfl_exp_table(bs.scale, 0), s, D.sigmoid_low_table(s), D.q_threshold(conf, cs.scale, 0)))
+    for i in range(2):
+        b, s, c = ref_decode.decode(lib, raw[i], layout, tables, anchors, conf, iou, tuple(lb[i]))
+        assert len(s) == len(det[i].scores) and len(s) > 0
+        assert np.array_equal(_bits(det[i].boxes), _bits(b)) and np.array_equal(_bits(det[i].scores), _bits(s))
+        assert np.array_equal(det[i].classes, c)
+    sess.close()
