@@ -1158,6 +1158,7 @@ struct ixb_session {
   ixb_detect_config dcfg{};
   DecodeParams dparams{};
   uint8_t* det_mem = nullptr;   // device memory of every slot's detections and letterbox rows
+  uint8_t* det_tables = nullptr;  // the decode tables' score ranks and DFL checks (decode_tables_kernel)
   uint8_t* det_pinned = nullptr;
   std::vector<std::string> class_names;
   ixb_timings last_timings{};
@@ -1550,6 +1551,7 @@ int ixb_session_destroy(ixb_session* s) {
       if (ev) cudaEventDestroy(ev);
     if (sl.frames_dev) cudaFree(sl.frames_dev);
   }
+  if (s->det_tables) cudaFree(s->det_tables);
   if (s->det_mem) cudaFree(s->det_mem);
   if (s->det_pinned) cudaFreeHost(s->det_pinned);
   if (s->h2d) cudaStreamDestroy(s->h2d);
@@ -1699,6 +1701,15 @@ int ixb_session_set_detect(ixb_session* s, const ixb_detect_config* cfg) {
   IXB_CUDA(cudaSetDevice(s->device));
   DecodeParams p;
   if (int r = prepare_decode(cfg->decode, s->plan.egress_image_bytes, p)) return r;
+  // the tables' ranks and DFL checks once, here, instead of in every decode launch (the session
+  // reads the caller's tables from here on; a change to them goes through set_detect again)
+  if (!s->det_tables) IXB_CUDA(cudaMalloc(&s->det_tables, 2 * kScoreVals + 16));
+  p.ranks = reinterpret_cast<const uint16_t*>(s->det_tables);
+  p.toe = reinterpret_cast<const int32_t*>(s->det_tables + 2 * kScoreVals);
+  decode_tables_kernel<<<1, kDecodeThreads, 0, s->stream>>>(p, reinterpret_cast<uint16_t*>(s->det_tables),
+                                                            reinterpret_cast<int32_t*>(s->det_tables + 2 * kScoreVals));
+  IXB_CUDA(cudaGetLastError());
+  IXB_CUDA(cudaStreamSynchronize(s->stream));
   const bool grow = !s->detect || cfg->capacity != s->dcfg.capacity;
   s->dcfg = *cfg;
   s->dparams = p;

@@ -61,6 +61,11 @@ struct DecodeParams {
   float* out_score;             // [B][capacity]
   int32_t* out_class;           // [B][capacity]
   int32_t* out_count;           // [B]: detections, or -3 when more than `capacity` survive NMS
+  // Optional, from decode_tables_kernel over the same tables (a session computes them once): the
+  // 768 score ranks and, per head, whether the DFL table depends on q - q_max alone. Null: every
+  // launch derives them itself.
+  const uint16_t* ranks;
+  const int32_t* toe;
 };
 
 // Area of the intersection of two class-offset boxes, as OpenCV's Rect2d operator& computes it.
@@ -305,42 +310,48 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
     s_n = 0;
     s_kept = 0;
   }
-  cluster_sync();  // both CTAs of the cluster are running before either touches the other's shared memory
-  // The image's two CTAs split the checks and the ranks (rows and values of their own parity) and
-  // trade the results.
-  for (int h = 0; h < 3; ++h) {
-    // the table is used at (q_max, q) with q <= q_max only: there it must equal the diagonal
-    // (16-byte loads of four columns; the caller's tables are 16-byte aligned)
-    const float4* t4 = reinterpret_cast<const float4*>(p.head[h].dfl_exp);
-    const float* dg = s_diag + h * 256 + 255;
-    bool same = true;
+  if (p.ranks) {
+    for (int i = tid; i < kScoreVals; i += kDecodeThreads) s_rank[i] = __ldg(p.ranks + i);
+    if (tid < 3) s_toe[tid] = __ldg(p.toe + tid);
+    cluster_sync();  // both CTAs of the cluster are running before either touches the other's shared memory
+  } else {
+    cluster_sync();  // both CTAs of the cluster are running before either touches the other's shared memory
+    // The image's two CTAs split the checks and the ranks (rows and values of their own parity) and
+    // trade the results.
+    for (int h = 0; h < 3; ++h) {
+      // the table is used at (q_max, q) with q <= q_max only: there it must equal the diagonal
+      // (16-byte loads of four columns; the caller's tables are 16-byte aligned)
+      const float4* t4 = reinterpret_cast<const float4*>(p.head[h].dfl_exp);
+      const float* dg = s_diag + h * 256 + 255;
+      bool same = true;
 #pragma unroll 4
-    for (int e = tid; e < 128 * 64; e += kDecodeThreads) {
-      const int r = 2 * (e >> 6) + (int)crank, c = (e & 63) * 4;
-      if (c <= r) {
-        const float4 v = __ldg(t4 + r * 64 + (e & 63));
-        same &= __float_as_uint(v.x) == __float_as_uint(dg[c - r]);
-        same &= c + 1 > r || __float_as_uint(v.y) == __float_as_uint(dg[c + 1 - r]);
-        same &= c + 2 > r || __float_as_uint(v.z) == __float_as_uint(dg[c + 2 - r]);
-        same &= c + 3 > r || __float_as_uint(v.w) == __float_as_uint(dg[c + 3 - r]);
+      for (int e = tid; e < 128 * 64; e += kDecodeThreads) {
+        const int r = 2 * (e >> 6) + (int)crank, c = (e & 63) * 4;
+        if (c <= r) {
+          const float4 v = __ldg(t4 + r * 64 + (e & 63));
+          same &= __float_as_uint(v.x) == __float_as_uint(dg[c - r]);
+          same &= c + 1 > r || __float_as_uint(v.y) == __float_as_uint(dg[c + 1 - r]);
+          same &= c + 2 > r || __float_as_uint(v.z) == __float_as_uint(dg[c + 2 - r]);
+          same &= c + 3 > r || __float_as_uint(v.w) == __float_as_uint(dg[c + 3 - r]);
+        }
+      }
+      same = __syncthreads_and(same) != 0;
+      if (tid == 0) {
+        s_toe_half[crank][h] = same ? 1 : 0;
+        st_cluster_u32(cluster_addr(&s_toe_half[crank][h], cpeer), same ? 1u : 0u);
       }
     }
-    same = __syncthreads_and(same) != 0;
-    if (tid == 0) {
-      s_toe_half[crank][h] = same ? 1 : 0;
-      st_cluster_u32(cluster_addr(&s_toe_half[crank][h], cpeer), same ? 1u : 0u);
+    for (int i = 2 * tid + (int)crank; i < kScoreVals; i += 2 * kDecodeThreads) {
+      const float v = s_sig[i];
+      int r = 0;
+      for (int j = 0; j < kScoreVals; ++j) r += s_sig[j] > v ? 1 : 0;
+      s_rank[i] = (uint16_t)r;
+      st_cluster_u16(cluster_addr(&s_rank[i], cpeer), (uint32_t)r);
     }
+    cluster_sync();  // both halves of the checks and of the ranks in both CTAs
+    if (tid < 3) s_toe[tid] = s_toe_half[0][tid] & s_toe_half[1][tid];
+    __syncthreads();
   }
-  for (int i = 2 * tid + (int)crank; i < kScoreVals; i += 2 * kDecodeThreads) {
-    const float v = s_sig[i];
-    int r = 0;
-    for (int j = 0; j < kScoreVals; ++j) r += s_sig[j] > v ? 1 : 0;
-    s_rank[i] = (uint16_t)r;
-    st_cluster_u16(cluster_addr(&s_rank[i], cpeer), (uint32_t)r);
-  }
-  cluster_sync();  // both halves of the checks and of the ranks in both CTAs
-  if (tid < 3) s_toe[tid] = s_toe_half[0][tid] & s_toe_half[1][tid];
-  __syncthreads();
 
   // 1. candidates in anchor order: prune, class score, DFL, box. The image's two CTAs take
   //    alternate 1024-anchor tiles; after each pair they trade counts, and each writes its
@@ -593,6 +604,45 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) yolo_decode_kernel(const __
 }
 
 constexpr int decode_smem_bytes() { return kDsBytes; }
+
+// The per-table part of the decode, once for a set of tables (one CTA of kDecodeThreads): each
+// score value's rank (how many of the three heads' 768 sigmoid values exceed it) and, per head,
+// whether the DFL exp table equals its q_max = 127 row's diagonal wherever the decode reads it
+// (q <= q_max). The same tests as the decode kernel's own, over every row.
+__global__ void __launch_bounds__(kDecodeThreads, 1) decode_tables_kernel(const __grid_constant__ DecodeParams p,
+                                                                          uint16_t* ranks, int32_t* toe) {
+  __shared__ float s_sig[kScoreVals], s_diag[kScoreVals];
+  const int tid = threadIdx.x;
+  for (int i = tid; i < kScoreVals; i += kDecodeThreads) {
+    const DecodeHeadDev& hd = p.head[i >> 8];
+    s_sig[i] = __ldg(hd.sigmoid + (i & 255));
+    s_diag[i] = __ldg(hd.dfl_exp + 255 * 256 + (i & 255));
+  }
+  __syncthreads();
+  for (int h = 0; h < 3; ++h) {
+    const float4* t4 = reinterpret_cast<const float4*>(p.head[h].dfl_exp);
+    const float* dg = s_diag + h * 256 + 255;
+    bool same = true;
+    for (int e = tid; e < 256 * 64; e += kDecodeThreads) {
+      const int r = e >> 6, c = (e & 63) * 4;
+      if (c <= r) {
+        const float4 v = __ldg(t4 + r * 64 + (e & 63));
+        same &= __float_as_uint(v.x) == __float_as_uint(dg[c - r]);
+        same &= c + 1 > r || __float_as_uint(v.y) == __float_as_uint(dg[c + 1 - r]);
+        same &= c + 2 > r || __float_as_uint(v.z) == __float_as_uint(dg[c + 2 - r]);
+        same &= c + 3 > r || __float_as_uint(v.w) == __float_as_uint(dg[c + 3 - r]);
+      }
+    }
+    same = __syncthreads_and(same) != 0;
+    if (tid == 0) toe[h] = same ? 1 : 0;
+  }
+  for (int i = tid; i < kScoreVals; i += kDecodeThreads) {
+    const float v = s_sig[i];
+    int r = 0;
+    for (int j = 0; j < kScoreVals; ++j) r += s_sig[j] > v ? 1 : 0;
+    ranks[i] = (uint16_t)r;
+  }
+}
 
 // ---------------------------------------------------------------- dense decode
 // The reference's InferenceSession.decode_yolo_predictions (runtime/session.py:1223-1278) on the

@@ -347,7 +347,9 @@ int ixb_decode_dense(const ixb_dense_head* heads, int32_t num_classes, const int
  * ixb_session_set_detect configures it once: the decode descriptor (tables and anchors in device
  * memory owned by the caller, valid while the session uses them), the class heads' scales and zero
  * points (for ixb_session_set_thresholds, the reference's ignite_set_thresholds, ignite.h:141) and
- * the capacity per image (1 .. 8400). */
+ * the capacity per image (1 .. 8400). It also ranks the score tables and checks the DFL tables
+ * once, for every later decode of the session: tables whose contents change afterwards need
+ * ixb_session_set_detect again (ixb_decode_yolo derives both in every launch). */
 typedef struct ixb_detection {     /* the reference's ignite_detection_t (c_api/ignite.h:40-48) */
   float x0, y0, w, h;              /* top-left corner and size in source-image pixels */
   float score;
