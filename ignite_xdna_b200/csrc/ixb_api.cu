@@ -2211,6 +2211,72 @@ int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, u
   return launch_decode(p, batch, static_cast<cudaStream_t>(stream));
 }
 
+// ixb_decode_yolo_noalloc: the decode with its table ranks and DFL checks in the library's own
+// device array instead of memory the caller or a session allocates. For callers that may not
+// allocate device memory at all: a plugin inside a host application that owns the CUDA context and
+// its memory pool, or a loop whose timing cannot take cudaMalloc's implicit synchronisation.
+}  // extern "C"
+
+// 2 KB per GPU that loads the library, held until the process exits: the score ranks (uint16
+// [768]) and the three DFL checks (int32 [3]) of one decode's tables. Host code must not hand this
+// name to a kernel: on the host it is only the runtime's handle for the array, not its device
+// address (noalloc_scratch looks that up).
+constexpr int kNoAllocScratchBytes = 2048;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static_assert(2 * kScoreVals + 3 * sizeof(int32_t) <= kNoAllocScratchBytes,
+              "one table set's ranks and checks must fit the no-allocation scratch");
+
+namespace {
+// The scratch array's device address on the current device: looked up the first time a device
+// asks, with that device current, then kept.
+int noalloc_scratch(uint8_t** out) {
+  static std::mutex mu;
+  static uint8_t* addr[64] = {};
+  int dev = 0;
+  IXB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(IXB_ERR_UNSUPPORTED, "device index above 63");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* ptr = nullptr;
+    IXB_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    addr[dev] = static_cast<uint8_t*>(ptr);
+  }
+  *out = addr[dev];
+  return 0;
+}
+}  // namespace
+
+extern "C" {
+
+int ixb_decode_yolo_noalloc(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
+                            const float* letterbox, int32_t capacity, float* boxes, float* scores, int32_t* classes,
+                            int32_t* counts, void* stream) {
+  if (!d || !egress || !letterbox || !boxes || !scores || !classes || !counts || batch < 1 || capacity < 0)
+    return fail(IXB_ERR_INVALID, "bad decode arguments");
+  if (reinterpret_cast<uintptr_t>(boxes) & 15) return fail(IXB_ERR_INVALID, "boxes must be 16-byte aligned");
+  DecodeParams p;
+  if (int r = prepare_decode(*d, egress_image_bytes, p)) return r;
+  uint8_t* scratch = nullptr;
+  if (int r = noalloc_scratch(&scratch)) return r;
+  p.egress = egress;
+  p.letterbox = letterbox;
+  p.capacity = capacity;
+  p.out_box = boxes;
+  p.out_score = scores;
+  p.out_class = classes;
+  p.out_count = counts;
+  // the tables kernel rewrites all 768 ranks and the three checks before the decode reads them, so
+  // nothing from an earlier call carries over and nothing needs clearing
+  uint16_t* ranks = reinterpret_cast<uint16_t*>(scratch);
+  int32_t* toe = reinterpret_cast<int32_t*>(scratch + 2 * kScoreVals);
+  p.ranks = ranks;
+  p.toe = toe;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  decode_tables_kernel<<<1, kDecodeThreads, 0, st>>>(p, ranks, toe);
+  IXB_CUDA(cudaGetLastError());
+  return launch_decode(p, batch, st);
+}
+
 int ixb_decode_dense(const ixb_dense_head* heads, int32_t num_classes, const int8_t* egress, int batch,
                      uint64_t egress_image_bytes, float* out, void* stream) {
   if (!heads || !egress || !out || batch < 1 || batch > 65535) return fail(IXB_ERR_INVALID, "bad dense decode arguments");

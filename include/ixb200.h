@@ -320,6 +320,20 @@ typedef struct ixb_decode_desc {
 int ixb_decode_yolo(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
                     const float* letterbox, int32_t capacity, float* boxes, float* scores, int32_t* classes,
                     int32_t* counts, void* stream);
+/* ixb_decode_yolo for callers that may not allocate device memory. No counterpart in the
+ * reference. Some callers cannot call cudaMalloc: a plugin running inside a host application that
+ * owns the CUDA context and its memory pool, or a loop whose timing cannot take cudaMalloc's
+ * implicit synchronisation. Same arguments and detections as ixb_decode_yolo (the caller still
+ * passes every input and output); it first ranks the score tables and checks the DFL tables, as a
+ * session's detection stage does once, into a 2 KB array of device memory that the library holds
+ * on every GPU that loads it until the process exits, and allocates nothing. That scratch holds one
+ * table set, so no argument can ask for more. The first call on a device looks up the array's
+ * device address: make that first call before any stream capture. Every call uses the same array
+ * and rewrites it whole before reading it; calls whose work overlaps on the GPU (on other streams
+ * or from other host threads) race on it, so serialise them. Enqueued on `stream`. */
+int ixb_decode_yolo_noalloc(const ixb_decode_desc* d, const int8_t* egress, int batch, uint64_t egress_image_bytes,
+                            const float* letterbox, int32_t capacity, float* boxes, float* scores,
+                            int32_t* classes, int32_t* counts, void* stream);
 
 /* Dense detect decode on the GPU: the reference's InferenceSession.decode_yolo_predictions
  * (runtime/session.py:1223-1278), float32 [batch][4 + num_classes][sum of grid^2] (device memory)
